@@ -1,0 +1,140 @@
+"""Pins the CPU oracle before it is trusted as the checker of the CUDA path.
+
+1. The reference's own known-answer tests (tests/kat_cases.py) pass on the oracle, and on
+   the compiled reference when it is present.
+2. The oracle reproduces the committed golden fixtures, which the compiled reference
+   produced (tests/golden/make_golden.py): generator draws bit-exact, op and small-model
+   outputs to a few ulps, scheduler trajectories.
+3. Where the reference build is present, the oracle and the reference agree on fresh
+   seeded cases too.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import kat_cases as K
+from conftest import GOLDEN
+
+import importlib.util
+
+_spec = importlib.util.spec_from_file_location("make_golden", os.path.join(GOLDEN, "make_golden.py"))
+MG = importlib.util.module_from_spec(_spec)
+_spec.loader.exec_module(MG)
+syn = MG.syn
+
+
+def rel_err(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.mark.parametrize("case", K.ALL_KATS, ids=lambda f: f.__name__)
+def test_reference_kats_on_oracle(oracle, case):
+    K.check(case(oracle))
+
+
+@pytest.mark.parametrize("case", K.ALL_KATS, ids=lambda f: f.__name__)
+def test_reference_kats_on_reference_build(reference, case):
+    K.check(case(reference))
+
+
+def test_rng_matches_golden(oracle):
+    g = np.load(os.path.join(GOLDEN, "rng.npz"))
+    assert np.array_equal(oracle.randn(17, 3).view(np.uint32), g["r17_3"].view(np.uint32))
+    assert np.array_equal(oracle.randn(1000, 42).view(np.uint32), g["r1000_42"].view(np.uint32))
+    assert np.array_equal(oracle.randn(100003, 9)[-64:].view(np.uint32), g["r100003_9"].view(np.uint32))
+    with pytest.raises(ValueError):
+        oracle.randn(15, 0)
+
+
+def test_ops_match_golden(oracle):
+    g = np.load(os.path.join(GOLDEN, "ops_small.npz"))
+    for name, meth, args in MG.ops_cases(oracle.randn):
+        out = getattr(oracle, meth)(*args)
+        assert out.shape == g[name].shape, name
+        assert rel_err(out, g[name]) < 1e-6, (name, rel_err(out, g[name]))
+
+
+def test_small_model_matches_golden(oracle):
+    g = np.load(os.path.join(GOLDEN, "model_small.npz"))
+    tensors = syn.generate_model(MG.SMALL, oracle.randn, base_seed=5, bias_std=0.02)
+    got = MG.small_model_run(oracle.model(tensors, *MG.SMALL.as_args()), oracle.randn)
+    for k, v in got.items():
+        assert rel_err(v, g[k]) < 1e-5, (k, rel_err(v, g[k]))
+
+
+def test_scheduler_matches_golden(oracle):
+    g = np.load(os.path.join(GOLDEN, "scheduler_20.npz"))
+    ts, sg = oracle.scheduler_schedule(20, 3.0)
+    assert np.array_equal(ts, g["timesteps"]) and np.array_equal(sg, g["sigmas"])
+    assert ts[0] == 999 and ts[-1] == 136 and sg[-1] == 0.0
+    mo = syn._draw(oracle.randn, 20 * 64, 300).reshape(20, 64)
+    x0 = syn._draw(oracle.randn, 64, 301)
+    assert rel_err(oracle.scheduler_run(mo, x0, 3.0), g["samples"]) < 1e-6
+
+
+def test_scheduler_step_state_machine(oracle):
+    """The explicit-state step reproduces the whole-run trajectory: first order at step 0
+    and at the last step, second order between, a history of two."""
+    ts, sg = oracle.scheduler_schedule(6, 3.0)
+    rng = np.random.default_rng(0)
+    mo = rng.standard_normal((6, 10)).astype(np.float32)
+    x = rng.standard_normal(10).astype(np.float32)
+    traj = oracle.scheduler_run(mo, x, 3.0)
+    hist, lower = [], 0
+    for s in range(6):
+        x, hist, lower = oracle.scheduler_step(sg, s, lower, hist, mo[s], x)
+        assert len(hist) == min(s + 1, 2) and lower == min(s + 1, 2)
+        np.testing.assert_array_equal(x, traj[s])
+
+
+def test_invalid_arguments_raise(oracle):
+    with pytest.raises(ValueError):
+        oracle.scheduler_schedule(0)
+    with pytest.raises(ValueError):
+        oracle.scheduler_update(2, np.array([0.5, 0.2, 0.0], np.float32), 0, np.ones(1, np.float32),
+                                np.ones(1, np.float32), np.ones(1, np.float32))
+    with pytest.raises(ValueError):
+        oracle.attention_block(np.ones((1, 2, 3), np.float32), *[np.eye(3, dtype=np.float32), None] * 4, 2)
+
+
+def test_oracle_agrees_with_reference_on_fresh_cases(oracle, reference):
+    rng = np.random.default_rng(11)
+    q, k, v = (rng.standard_normal((2, 4, 9, 12)).astype(np.float32) for _ in range(3))
+    assert rel_err(oracle.linear_attention(q, k, v), reference.linear_attention(q, k, v)) < 1e-6
+    kk, vv = (rng.standard_normal((2, 4, 5, 12)).astype(np.float32) for _ in range(2))
+    bias = syn.attention_bias([1, 5], 5)
+    assert rel_err(oracle.attention(q, kk, vv, bias), reference.attention(q, kk, vv, bias)) < 1e-6
+    img = rng.standard_normal((1, 8, 6, 6)).astype(np.float32)
+    w = rng.standard_normal((8, 1, 3, 3)).astype(np.float32)
+    b = rng.standard_normal(8).astype(np.float32)
+    assert rel_err(oracle.depthwise3x3(img, w, b), reference.depthwise3x3(img, w, b)) < 1e-6
+    for n, s in ((16, 0), (1152 * 3 + 5, 77)):
+        assert np.array_equal(oracle.randn(n, s), reference.randn(n, s))
+
+
+def test_full_block_signature(oracle):
+    """Block 0 of the full-size synthetic model at config-0 shapes against the compiled
+    reference's signature (first 4096 values, per-row sums and sums of squares)."""
+    path = os.path.join(GOLDEN, "block0_full.npz")
+    if not os.path.exists(path):
+        pytest.skip("block0_full.npz not generated")
+    g = np.load(path)
+    d1 = syn.ModelDims(n_blocks=1)
+    tensors = syn.generate_model(d1, oracle.randn, base_seed=0)
+    m = oracle.model(tensors, *d1.as_args())
+    enc = syn.encoder_states(oracle.randn, 2, 300, d1.caption_dim, 7)
+    bias = syn.attention_bias([8, 24], 300)
+    ctx = m.project_caption(enc)
+    emb, tmod = m.time_embed([999.0, 999.0])
+    np.testing.assert_allclose(ctx.reshape(-1)[:4096], g["ctx_head"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(tmod, g["tmod"], rtol=1e-5, atol=1e-6)
+    x = syn._draw(oracle.randn, 2 * 1024 * d1.hidden, 400).reshape(2, 1024, d1.hidden)
+    st = m.block_forward(0, x, ctx, tmod, bias)
+    for name, a in zip(("after_self", "after_cross", "after_ff"), st):
+        sig = MG._signature(a)
+        assert rel_err(sig["head"], g[f"{name}_head"]) < 1e-5
+        assert rel_err(sig["row_sq"], g[f"{name}_row_sq"]) < 1e-5
+        assert rel_err(sig["row_sum"], g[f"{name}_row_sum"]) < 1e-4
