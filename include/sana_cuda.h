@@ -1,0 +1,226 @@
+/*
+ * sana_cuda.h — C ABI of the B200 (sm_100a) implementation of the Sana-0.6B denoiser path
+ * of cconthekeyboard/sana.cpp: the linear-attention DiT blocks, their step and the
+ * DPM-Solver++ classifier-free-guidance loop.
+ *
+ * Plain C: opaque handle, raw pointers and sizes, int status codes. Every call that takes
+ * host buffers copies them to the device, runs, copies results back and synchronises; the
+ * *_device variants take device pointers and run asynchronously on the handle's stream
+ * (sana_cuda_stream) until sana_cuda_synchronize.
+ *
+ * Layouts are the reference's unless stated otherwise: fp32, row-major; activations
+ * [batch, tokens, hidden]; images / latents NCHW; linear weights [in, out]
+ * (SanaDenoiserWeights as load_linear_weight_tensor leaves them, weights_io.cpp:367-377)
+ * or [out, in] with SANA_LAYOUT_TORCH; conv weights [out, in, kh, kw].
+ *
+ * Errors: every function returns SANA_OK or an error code; the message of the last
+ * failure on a handle is sana_cuda_last_error(handle). SANA_ERR_INVALID corresponds to the
+ * reference's std::invalid_argument, SANA_ERR_CUDA / SANA_ERR_TIMEOUT / SANA_ERR_STATE to
+ * std::runtime_error. A handle is not thread-safe (the reference is single-threaded).
+ */
+#ifndef SANA_CUDA_H
+#define SANA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct sana_cuda_ctx sana_cuda_ctx;
+
+enum {
+    SANA_OK = 0,
+    SANA_ERR_INVALID = 1, /* argument / shape error */
+    SANA_ERR_CUDA = 2,    /* CUDA runtime error */
+    SANA_ERR_TIMEOUT = 3, /* a bounded device-side wait gave up; the kernel returned early */
+    SANA_ERR_STATE = 4,   /* call order (e.g. no weights uploaded) */
+    SANA_ERR_NOMEM = 5
+};
+
+enum { SANA_MODE_BF16 = 0, SANA_MODE_F32 = 1 };
+enum { SANA_LAYOUT_REFERENCE = 0, SANA_LAYOUT_TORCH = 1 };
+
+/* Model dimensions (SanaDenoiserWeights / SanaBlockWeights shapes, transformer.h:26-79). */
+typedef struct {
+    int n_blocks;        /* 28 for Sana-0.6B */
+    int hidden;          /* 1152 */
+    int latent_channels; /* 32 */
+    int caption_dim;     /* 2304 */
+    int ff_expanded;     /* 5760 (GLUMBConv inverted width; the point conv reads half) */
+    int self_heads;      /* 36 in the reference's callers (infer_main.cpp:366) */
+    int cross_heads;     /* 16 */
+} sana_dims;
+
+/* --- lifetime ------------------------------------------------------------------------ */
+
+/* Creates a handle on CUDA device `device`. mode: SANA_MODE_BF16 (bf16 operands, fp32
+ * accumulation and residual stream, tcgen05 tensor cores) or SANA_MODE_F32 (fp32
+ * everywhere, CUDA-core GEMMs; the parity check mode). No reference counterpart: the
+ * reference has no device state. */
+int sana_cuda_create(int device, int mode, sana_cuda_ctx **out);
+void sana_cuda_destroy(sana_cuda_ctx *ctx);
+const char *sana_cuda_last_error(const sana_cuda_ctx *ctx);
+/* The cudaStream_t all work of the handle runs on (as void*). */
+void *sana_cuda_stream(sana_cuda_ctx *ctx);
+/* Runs later work on `stream` (a cudaStream_t; NULL restores the handle's own stream). */
+int sana_cuda_set_stream(sana_cuda_ctx *ctx, void *stream);
+/* Waits for the handle's stream and reports device-side timeouts. */
+int sana_cuda_synchronize(sana_cuda_ctx *ctx);
+/* Kernel launches in the last captured denoising loop replay (0 before the first replay). */
+int sana_cuda_last_launch_count(const sana_cuda_ctx *ctx);
+/* Process-wide number of dense projections dispatched to the tcgen05 tensor-core kernel
+ * and to the CUDA-core kernel (fp32 check mode, tiny or unaligned shapes). */
+void sana_cuda_gemm_counts(long long *tensor_core, long long *cuda_core);
+
+/* Diagnostics: copies `bytes` at `offset` of a named workspace buffer of the last call
+ * (a, qkv, ao, cq, xb, ffh, glu, x, x1, x2, x3, mods, tmod, emb, ckv1, ctx, kvlen, noise,
+ * lat, part) to `host`; *size_out receives the buffer's size. No reference counterpart. */
+int sana_cuda_debug_read(sana_cuda_ctx *ctx, const char *name, size_t offset, size_t bytes, void *host,
+                         size_t *size_out);
+
+/* --- weights --------------------------------------------------------------------------- */
+
+/* Uploads the denoiser weights into the handle's device cache (bf16 or fp32 by mode).
+ * Replaces holding SanaDenoiserWeights (transformer.h:64-79) as built by
+ * load_denoiser_weights (transformer.cpp:453-488).
+ *   model[16]: caption.linear_1_weight, caption.linear_1_bias, caption.linear_2_weight,
+ *     caption.linear_2_bias, patch_embed_weight, patch_embed_bias,
+ *     time_embed_linear_1_weight, _bias, time_embed_linear_2_weight, _bias,
+ *     time_projection_weight, _bias, caption_norm_weight, final_scale_shift_table,
+ *     proj_out_weight, proj_out_bias                (the struct's field order)
+ *   blocks[26 * n_blocks]: per block the SanaBlockWeights fields in order
+ *     (scale_shift_table, attn_norm_gamma, attn_norm_beta, q_weight, q_bias, k_weight,
+ *      k_bias, v_weight, v_bias, out_weight, out_bias, cross_q_weight, cross_q_bias,
+ *      cross_k_weight, cross_k_bias, cross_v_weight, cross_v_bias, cross_out_weight,
+ *      cross_out_bias, mlp_norm_gamma, mlp_norm_beta, ff_inverted_weight,
+ *      ff_inverted_bias, ff_depth_weight, ff_depth_bias, ff_point_weight).
+ * Bias pointers may be NULL (zero), norm gamma/beta NULL (identity), as the loader's
+ * defaults (transformer.cpp:361-398). Weight pointers must not be NULL. */
+int sana_cuda_upload_weights(sana_cuda_ctx *ctx, const sana_dims *dims, const float *const *model,
+                             const float *const *blocks, int layout);
+
+/* --- the denoiser path (host buffers) --------------------------------------------------- */
+
+/* run_full_denoising_loop_with_cfg (transformer.h:140-148, transformer.cpp:692-724) with a
+ * fresh scheduler state of `num_steps` steps (init_sana_scheduler_state, scheduler.h:40):
+ * caption projection, then the 20-step (or num_steps) DPM-Solver++ loop.
+ *   latents [B, Cl, H, W]; enc [2B, L, caption_dim] (uncond block first); bias [2B, 1, L]
+ *   additive mask or NULL; out [B, Cl, H, W]. The whole loop runs as one CUDA graph from
+ *   the second call with the same shapes on. */
+int sana_cuda_denoise_loop(sana_cuda_ctx *ctx, const float *latents, int B, int H, int W, const float *enc, int L,
+                           int enc_dim, const float *bias, float guidance, int num_steps, float flow_shift,
+                           float *out);
+
+/* The same with device pointers (fp32), asynchronous on the handle's stream. */
+int sana_cuda_denoise_loop_device(sana_cuda_ctx *ctx, const float *latents, int B, int H, int W, const float *enc,
+                                  int L, int enc_dim, const float *bias, float guidance, int num_steps,
+                                  float flow_shift, float *out);
+
+/* run_full_denoising_step_with_cfg (transformer.h:131-139, transformer.cpp:604-690): one
+ * step on latents [B, Cl, H, W] (updated in place) with the projected context
+ * [2B, L, hidden], at timestep value `timestep`, with an explicit scheduler state
+ * (SanaSchedulerState, scheduler.h:27-32): sigmas[n_sigmas], *step_index,
+ * *lower_order_count, history[*n_history x numel] (converted outputs, oldest first,
+ * capacity 2 x numel), all updated as step_sana_scheduler does (scheduler.cpp:272-318). */
+int sana_cuda_denoise_step(sana_cuda_ctx *ctx, float *latents, int B, int H, int W, const float *context, int L,
+                           const float *bias, float guidance, float timestep, const float *sigmas, int n_sigmas,
+                           int *step_index, int *lower_order_count, float *history, int *n_history);
+
+/* One denoiser forward without CFG or scheduler for S independent sequences at timestep t:
+ * patch embed, time embedding, all blocks, final layer (transformer.cpp:631-681).
+ *   latents [S, Cl, H, W]; context [S, L, hidden] (projected); bias [S, 1, L] or NULL;
+ *   noise_pred out [S, Cl, H, W]. */
+int sana_cuda_forward(sana_cuda_ctx *ctx, const float *latents, int S, int H, int W, float t, const float *context,
+                      int L, const float *bias, float *noise_pred);
+
+/* block_forward (transformer.h:149-155, transformer.cpp:726-778) of block `block`.
+ *   x [S, T, hidden] (T a square), context [S, L, hidden], timestep modulation
+ *   tmod [S, 6 * hidden], bias [S, 1, L] or NULL; any stage output may be NULL
+ *   (SanaBlockStageOutputs, transformer.h:20-24). */
+int sana_cuda_block_forward(sana_cuda_ctx *ctx, int block, const float *x, int S, int T, const float *context, int L,
+                            const float *tmod, const float *bias, float *after_self, float *after_cross,
+                            float *after_ff);
+
+/* run_model_blocks (transformer.h:118-126, transformer.cpp:544-568): blocks [begin, end). */
+int sana_cuda_run_model_blocks(sana_cuda_ctx *ctx, const float *x, int S, int T, const float *context, int L,
+                               const float *tmod, const float *bias, int begin, int end, float *out);
+
+/* project_caption_context with the uploaded caption weights (transformer.cpp:701-708;
+ * transformer_ops.cpp:64-76): enc [S, L, caption_dim] -> out [S, L, hidden]. */
+int sana_cuda_project_caption(sana_cuda_ctx *ctx, const float *enc, int S, int L, int enc_dim, float *out);
+
+/* --- single operations (host buffers, reference semantics and layouts) ------------------ */
+
+/* linear_3d_lastdim / linear_2d (common_ops.cpp:114-209): x [rows, K], w [K, N], bias [N]. */
+int sana_op_linear(sana_cuda_ctx *ctx, const float *x, int rows, int K, const float *w, const float *bias, int N,
+                   float *out);
+/* Tensor::layer_norm_3d_lastdim (tensor.cpp:188-271): x [rows, C]. */
+int sana_op_layer_norm(sana_cuda_ctx *ctx, const float *x, int rows, int C, float eps, const float *gamma,
+                       const float *beta, float *out);
+/* Tensor::rms_norm_3d_lastdim (tensor.cpp:276-316). */
+int sana_op_rms_norm(sana_cuda_ctx *ctx, const float *x, int rows, int C, float eps, const float *weight, float *out);
+/* Tensor::modulate_3d_lastdim (tensor.cpp:323-376): x [B, T, C], shift/scale [B, 1, C]. */
+int sana_op_modulate(sana_cuda_ctx *ctx, const float *x, int B, int T, int C, const float *shift, const float *scale,
+                     float *out);
+/* linear_attention_4d (transformer_ops.cpp:402-543): q [B, H, Tq, D], k/v [B, H, Tk, D]. */
+int sana_op_linear_attention(sana_cuda_ctx *ctx, const float *q, const float *k, const float *v, int B, int H, int Tq,
+                             int Tk, int D, float *out);
+/* attention_4d (transformer_ops.cpp:348-392): softmax(q k^T / sqrt(D) + bias) v, bias [B, 1, Tk]. */
+int sana_op_attention(sana_cuda_ctx *ctx, const float *q, const float *k, const float *v, int B, int H, int Tq,
+                      int Tk, int D, const float *bias, float *out);
+/* conv2d_1x1 (common_ops.cpp:322-405): x [B, Cin, H, W], w [Cout, Cin, 1, 1]. */
+int sana_op_conv1x1(sana_cuda_ctx *ctx, const float *x, int B, int Cin, int H, int W, const float *w,
+                    const float *bias, int Cout, float *out);
+/* depthwise_conv2d_3x3 (common_ops.cpp:510-572): x [B, C, H, W], w [C, 1, 3, 3]. */
+int sana_op_depthwise3x3(sana_cuda_ctx *ctx, const float *x, int B, int C, int H, int W, const float *w,
+                         const float *bias, float *out);
+/* glumb_conv (common_ops.cpp:733-761): x [B, Cin, H, W] -> [B, Cout, H, W]. */
+int sana_op_glumb_conv(sana_cuda_ctx *ctx, const float *x, int B, int Cin, int H, int W, const float *w_inv,
+                       const float *b_inv, int E, const float *w_dw, const float *b_dw, const float *w_pt, int Cout,
+                       float *out);
+/* project_caption_context (transformer_ops.cpp:64-76) with explicit weights ([in, out]). */
+int sana_op_project_caption(sana_cuda_ctx *ctx, const float *enc, int B, int L, int Din, const float *w1,
+                            const float *b1, int C, const float *w2, const float *b2, const float *norm_w, float *out);
+/* attention_block_3d (transformer_ops.cpp:545-570): weights [C, C] ([in, out]), biases may be NULL. */
+int sana_op_attention_block(sana_cuda_ctx *ctx, const float *x, int B, int T, int C, const float *wq, const float *bq,
+                            const float *wk, const float *bk, const float *wv, const float *bv, const float *wo,
+                            const float *bo, int heads, float *out);
+/* cross_attention_block_3d (transformer_ops.cpp:572-608): context [B, L, C], bias [B, 1, L] or NULL. */
+int sana_op_cross_attention_block(sana_cuda_ctx *ctx, const float *x, int B, int T, int C, const float *context,
+                                  int L, const float *bias, const float *wq, const float *bq, const float *wk,
+                                  const float *bk, const float *wv, const float *bv, const float *wo, const float *bo,
+                                  int heads, float *out);
+/* apply_classifier_free_guidance (transformer.cpp:570-602): noise [2B, Cl, H, W] -> [B, Cl, H, W]. */
+int sana_op_cfg(sana_cuda_ctx *ctx, const float *noise, int B, int Cl, int H, int W, float guidance, float *out);
+
+/* --- scheduler (scheduler.h:34-65) ----------------------------------------------------- */
+
+/* build_sana_scheduler_timesteps (scheduler.cpp:89-141), default config with flow_shift;
+ * host only: timesteps[n], sigmas[n + 1]. */
+int sana_scheduler_schedule(int n, float flow_shift, float *timesteps, float *sigmas);
+/* convert_sana_scheduler_model_output (scheduler.cpp:155-173) on the device. */
+int sana_scheduler_convert(sana_cuda_ctx *ctx, const float *sigmas, int n_sigmas, int step_index,
+                           const float *model_output, const float *sample, int numel, float *out);
+/* sana_scheduler_first_order_update (order 1, m0 = converted output) or
+ * sana_scheduler_second_order_update (order 2, history [m1, m0]) (scheduler.cpp:175-270). */
+int sana_scheduler_update(sana_cuda_ctx *ctx, int order, const float *sigmas, int n_sigmas, int step_index,
+                          const float *m0, const float *m1, const float *sample, int numel, float *out);
+/* step_sana_scheduler (scheduler.cpp:272-318) with an explicit state: history
+ * [n_history x numel] oldest first (n_history <= 2, capacity 2 x numel), updated in place
+ * together with *step_index, *lower_order_count and *n_history. */
+int sana_scheduler_step(sana_cuda_ctx *ctx, const float *sigmas, int n_sigmas, int *step_index,
+                        int *lower_order_count, float *history, int *n_history, const float *model_output,
+                        const float *sample, int numel, float *out);
+
+/* --- synthetic inputs -------------------------------------------------------------------- */
+
+/* randn_torch_cpu (torch_rng.cpp:35-68): torch.randn of n >= 16 float32 values on a CPU
+ * generator seeded with `seed`, bit-identical to the reference's restatement. Host only. */
+int sana_randn_torch_cpu(float *out, size_t n, uint64_t seed);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SANA_CUDA_H */

@@ -1,0 +1,834 @@
+// The C ABI of include/sana_cuda.h over the Engine and the kernels.
+#include <cstring>
+#include <memory>
+#include <new>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+#include "sana_cuda.h"
+
+struct sana_cuda_ctx {
+    std::unique_ptr<sana::Engine> eng;
+    std::string err;
+};
+
+namespace {
+
+using sana::bf16;
+using sana::DevBuf;
+
+// The stream of the handle the current entry point works on: every transfer of the
+// single-op entry points is ordered on it (set by engine()).
+thread_local cudaStream_t tl_stream = nullptr;
+
+template <class F>
+int guard(sana_cuda_ctx* ctx, F&& f) {
+    if (!ctx) return SANA_ERR_INVALID;
+    try {
+        f();
+        return SANA_OK;
+    } catch (const std::invalid_argument& e) {
+        ctx->err = e.what();
+        return SANA_ERR_INVALID;
+    } catch (const sana::TimeoutError& e) {
+        ctx->err = e.what();
+        return SANA_ERR_TIMEOUT;
+    } catch (const sana::CudaError& e) {
+        ctx->err = e.what();
+        return SANA_ERR_CUDA;
+    } catch (const std::bad_alloc&) {
+        ctx->err = "out of host memory";
+        return SANA_ERR_NOMEM;
+    } catch (const std::exception& e) {
+        ctx->err = e.what();
+        return SANA_ERR_STATE;
+    }
+}
+
+// --- host-side layout / precision helpers for the single-op entry points ----------------
+uint16_t f32_to_bf16_bits(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return static_cast<uint16_t>((u >> 16) | 0x40);  // NaN
+    const uint32_t rounding = 0x7fffu + ((u >> 16) & 1u);
+    return static_cast<uint16_t>((u + rounding) >> 16);
+}
+float bf16_bits_to_f32(uint16_t h) {
+    const uint32_t u = static_cast<uint32_t>(h) << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+// A device copy of host fp32 data in the activation type of the handle's mode.
+struct ActBuf {
+    DevBuf buf;
+    bool bf = false;
+    size_t n = 0;
+    void upload(const float* host, size_t count, bool as_bf16) {
+        bf = as_bf16;
+        n = count;
+        buf.ensure(std::max<size_t>(count, 1) * (bf ? 2 : 4));
+        if (count == 0) return;
+        if (bf) {
+            std::vector<uint16_t> h(count);
+            for (size_t i = 0; i < count; ++i) h[i] = f32_to_bf16_bits(host[i]);
+            SANA_CUDA(cudaMemcpyAsync(buf.get(), h.data(), count * 2, cudaMemcpyHostToDevice, tl_stream));
+        } else {
+            SANA_CUDA(cudaMemcpyAsync(buf.get(), host, count * 4, cudaMemcpyHostToDevice, tl_stream));
+        }
+    }
+    void alloc(size_t count, bool as_bf16) {
+        bf = as_bf16;
+        n = count;
+        buf.ensure(std::max<size_t>(count, 1) * (bf ? 2 : 4));
+    }
+    void download(float* host) const {
+        if (n == 0) return;
+        if (bf) {
+            std::vector<uint16_t> h(n);
+            SANA_CUDA(cudaMemcpyAsync(h.data(), buf.get(), n * 2, cudaMemcpyDeviceToHost, tl_stream));
+            SANA_CUDA(cudaStreamSynchronize(tl_stream));
+            for (size_t i = 0; i < n; ++i) host[i] = bf16_bits_to_f32(h[i]);
+        } else {
+            SANA_CUDA(cudaMemcpyAsync(host, buf.get(), n * 4, cudaMemcpyDeviceToHost, tl_stream));
+            SANA_CUDA(cudaStreamSynchronize(tl_stream));
+        }
+    }
+    void* get() const { return buf.get(); }
+};
+
+DevBuf f32_upload(const float* host, size_t n) {
+    DevBuf b;
+    b.ensure(std::max<size_t>(n, 1) * 4);
+    if (n) SANA_CUDA(cudaMemcpyAsync(b.get(), host, n * 4, cudaMemcpyHostToDevice, tl_stream));
+    return b;
+}
+
+// [rows, cols] -> [cols, rows]
+std::vector<float> transpose(const float* src, size_t rows, size_t cols) {
+    std::vector<float> out(rows * cols);
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t c = 0; c < cols; ++c) out[c * rows + r] = src[r * cols + c];
+    return out;
+}
+
+// [B, H, T, D] -> token rows [B*T, H*D] (split_heads_3d inverse, transformer_ops.cpp:133)
+std::vector<float> heads_to_tokens(const float* x, int B, int H, int T, int D) {
+    std::vector<float> out(static_cast<size_t>(B) * T * H * D);
+    for (int b = 0; b < B; ++b)
+        for (int h = 0; h < H; ++h)
+            for (int t = 0; t < T; ++t)
+                std::memcpy(&out[(static_cast<size_t>(b) * T + t) * H * D + static_cast<size_t>(h) * D],
+                            x + ((static_cast<size_t>(b) * H + h) * T + t) * D, D * sizeof(float));
+    return out;
+}
+
+void tokens_to_heads(const float* x, int B, int H, int T, int D, float* out) {
+    for (int b = 0; b < B; ++b)
+        for (int h = 0; h < H; ++h)
+            for (int t = 0; t < T; ++t)
+                std::memcpy(out + ((static_cast<size_t>(b) * H + h) * T + t) * D,
+                            &x[(static_cast<size_t>(b) * T + t) * H * D + static_cast<size_t>(h) * D],
+                            D * sizeof(float));
+}
+
+// NCHW [B, C, HW] <-> NHWC token rows [B*HW, C]
+std::vector<float> nchw_to_tokens(const float* x, int B, int C, int HW) {
+    std::vector<float> out(static_cast<size_t>(B) * C * HW);
+    for (int b = 0; b < B; ++b)
+        for (int c = 0; c < C; ++c)
+            for (int t = 0; t < HW; ++t)
+                out[(static_cast<size_t>(b) * HW + t) * C + c] = x[(static_cast<size_t>(b) * C + c) * HW + t];
+    return out;
+}
+
+void tokens_to_nchw(const float* x, int B, int C, int HW, float* out) {
+    for (int b = 0; b < B; ++b)
+        for (int c = 0; c < C; ++c)
+            for (int t = 0; t < HW; ++t)
+                out[(static_cast<size_t>(b) * C + c) * HW + t] = x[(static_cast<size_t>(b) * HW + t) * C + c];
+}
+
+sana::Epilogue epi(void* out, bool bf, long long ldo, const float* bias = nullptr, int act = sana::kActNone) {
+    sana::Epilogue e;
+    e.out = out;
+    e.out_bf16 = bf ? 1 : 0;
+    e.ldo = ldo;
+    e.bias = bias;
+    e.act = act;
+    return e;
+}
+
+void run_gemm(sana::Engine& eng, const ActBuf& A, long long lda, const ActBuf& B, long long ldb, int M, int N, int K,
+              const sana::Epilogue& e) {
+    sana::GemmProblem p;
+    p.A = A.get();
+    p.a_bf16 = A.bf;
+    p.lda = lda;
+    p.B = B.get();
+    p.b_bf16 = B.bf;
+    p.ldb = ldb;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.ep = e;
+    sana::gemm(p, eng.err(), eng.stream(), eng.num_sms());
+}
+
+void finish(sana::Engine& eng) {
+    SANA_CUDA(cudaStreamSynchronize(eng.stream()));
+    eng.check_device_error();
+}
+
+sana::Engine& engine(sana_cuda_ctx* ctx) {
+    if (!ctx->eng) throw std::runtime_error("handle has no engine");
+    tl_stream = ctx->eng->stream();
+    return *ctx->eng;
+}
+
+// Device -> host copy ordered after the handle's work.
+void d2h(void* host, const void* dev, size_t bytes) {
+    if (!bytes) return;
+    SANA_CUDA(cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, tl_stream));
+    SANA_CUDA(cudaStreamSynchronize(tl_stream));
+}
+
+}  // namespace
+
+extern "C" {
+
+int sana_cuda_create(int device, int mode, sana_cuda_ctx** out) {
+    if (!out) return SANA_ERR_INVALID;
+    *out = nullptr;
+    auto* ctx = new (std::nothrow) sana_cuda_ctx();
+    if (!ctx) return SANA_ERR_NOMEM;
+    int rc = guard(ctx, [&] { ctx->eng = std::make_unique<sana::Engine>(device, mode); });
+    if (rc != SANA_OK) {
+        // keep the handle so the caller can read the message; it has no engine
+        *out = ctx;
+        return rc;
+    }
+    *out = ctx;
+    return SANA_OK;
+}
+
+void sana_cuda_destroy(sana_cuda_ctx* ctx) { delete ctx; }
+
+const char* sana_cuda_last_error(const sana_cuda_ctx* ctx) { return ctx ? ctx->err.c_str() : "null handle"; }
+
+void* sana_cuda_stream(sana_cuda_ctx* ctx) { return (ctx && ctx->eng) ? ctx->eng->stream() : nullptr; }
+
+int sana_cuda_set_stream(sana_cuda_ctx* ctx, void* stream) {
+    return guard(ctx, [&] { engine(ctx).set_stream(static_cast<cudaStream_t>(stream)); });
+}
+
+int sana_cuda_synchronize(sana_cuda_ctx* ctx) { return guard(ctx, [&] { finish(engine(ctx)); }); }
+
+int sana_cuda_last_launch_count(const sana_cuda_ctx* ctx) {
+    return (ctx && ctx->eng) ? ctx->eng->last_launches() : 0;
+}
+
+void sana_cuda_gemm_counts(long long* tensor_core, long long* cuda_core) { sana::gemm_counts(tensor_core, cuda_core); }
+
+int sana_cuda_upload_weights(sana_cuda_ctx* ctx, const sana_dims* dims, const float* const* model,
+                             const float* const* blocks, int layout) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(dims != nullptr, "dims must not be null");
+        sana::Dims d;
+        d.n_blocks = dims->n_blocks;
+        d.C = dims->hidden;
+        d.Cl = dims->latent_channels;
+        d.Din = dims->caption_dim;
+        d.E = dims->ff_expanded;
+        d.Hs = dims->self_heads;
+        d.Hc = dims->cross_heads;
+        engine(ctx).upload(d, model, blocks, layout);
+    });
+}
+
+int sana_cuda_denoise_loop(sana_cuda_ctx* ctx, const float* latents, int B, int H, int W, const float* enc, int L,
+                           int enc_dim, const float* bias, float guidance, int num_steps, float flow_shift,
+                           float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(latents && enc && out, "latents, encoder states and output must not be null");
+        engine(ctx).denoise_loop(latents, B, H, W, enc, L, enc_dim, bias, guidance, num_steps, flow_shift, out);
+    });
+}
+
+int sana_cuda_denoise_loop_device(sana_cuda_ctx* ctx, const float* latents, int B, int H, int W, const float* enc,
+                                  int L, int enc_dim, const float* bias, float guidance, int num_steps,
+                                  float flow_shift, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(latents && enc && out, "latents, encoder states and output must not be null");
+        engine(ctx).denoise_loop_device(latents, B, H, W, enc, L, enc_dim, bias, guidance, num_steps, flow_shift,
+                                        out);
+    });
+}
+
+int sana_cuda_denoise_step(sana_cuda_ctx* ctx, float* latents, int B, int H, int W, const float* context, int L,
+                           const float* bias, float guidance, float timestep, const float* sigmas, int n_sigmas,
+                           int* step_index, int* lower_order_count, float* history, int* n_history) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(latents && context && sigmas && step_index && lower_order_count && n_history,
+                     "null argument to denoise_step");
+        SANA_REQUIRE(*n_history >= 0 && *n_history <= 2, "history holds at most two converted outputs");
+        SANA_REQUIRE(*n_history == 0 || history, "history buffer missing");
+        sana::Engine& eng = engine(ctx);
+        const size_t numel = static_cast<size_t>(B) * eng.dims().Cl * H * W;
+        sana::SchedulerHostState st;
+        st.sigmas.assign(sigmas, sigmas + n_sigmas);
+        st.step_index = *step_index;
+        st.lower_order_count = *lower_order_count;
+        for (int i = 0; i < *n_history; ++i) st.history.emplace_back(history + i * numel, history + (i + 1) * numel);
+        eng.denoise_step(latents, B, H, W, context, L, bias, guidance, st, timestep);
+        *step_index = st.step_index;
+        *lower_order_count = st.lower_order_count;
+        *n_history = static_cast<int>(st.history.size());
+        SANA_REQUIRE(history != nullptr, "history buffer missing");
+        for (size_t i = 0; i < st.history.size(); ++i) std::memcpy(history + i * numel, st.history[i].data(), numel * 4);
+    });
+}
+
+int sana_cuda_forward(sana_cuda_ctx* ctx, const float* latents, int S, int H, int W, float t, const float* context,
+                      int L, const float* bias, float* noise_pred) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(latents && context && noise_pred, "null argument to forward");
+        engine(ctx).forward_nocfg(latents, S, H, W, t, context, L, bias, noise_pred);
+    });
+}
+
+int sana_cuda_block_forward(sana_cuda_ctx* ctx, int block, const float* x, int S, int T, const float* context, int L,
+                            const float* tmod, const float* bias, float* after_self, float* after_cross,
+                            float* after_ff) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(x && context && tmod, "null argument to block_forward");
+        engine(ctx).block_forward(block, x, S, T, context, L, tmod, bias, after_self, after_cross, after_ff);
+    });
+}
+
+int sana_cuda_run_model_blocks(sana_cuda_ctx* ctx, const float* x, int S, int T, const float* context, int L,
+                               const float* tmod, const float* bias, int begin, int end, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(x && context && tmod && out, "null argument to run_model_blocks");
+        engine(ctx).run_blocks(x, S, T, context, L, tmod, bias, begin, end, out);
+    });
+}
+
+int sana_cuda_project_caption(sana_cuda_ctx* ctx, const float* enc, int S, int L, int enc_dim, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(enc && out, "null argument to project_caption");
+        engine(ctx).project_caption(enc, S, L, enc_dim, out);
+    });
+}
+
+int sana_cuda_debug_read(sana_cuda_ctx* ctx, const char* name, size_t offset, size_t bytes, void* host,
+                         size_t* size_out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(name != nullptr, "buffer name must not be null");
+        const size_t n = engine(ctx).debug_read(name, offset, bytes, host);
+        if (size_out) *size_out = n;
+    });
+}
+
+// --- single operations -------------------------------------------------------------------
+
+int sana_op_linear(sana_cuda_ctx* ctx, const float* x, int rows, int K, const float* w, const float* bias, int N,
+                   float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(x && w && out && rows >= 0 && K >= 1 && N >= 1, "invalid linear arguments");
+        sana::Engine& eng = engine(ctx);
+        const bool bf = eng.mode() == sana::kModeBf16;
+        ActBuf A, Bw;
+        A.upload(x, static_cast<size_t>(rows) * K, bf);
+        std::vector<float> wt = transpose(w, K, N);
+        Bw.upload(wt.data(), wt.size(), bf);
+        DevBuf bd = bias ? f32_upload(bias, N) : DevBuf();
+        DevBuf o;
+        o.ensure(std::max<size_t>(static_cast<size_t>(rows) * N, 1) * 4);
+        run_gemm(eng, A, K, Bw, K, rows, N, K, epi(o.get(), false, N, bias ? bd.as<float>() : nullptr));
+        finish(eng);
+        if (rows) d2h(out, o.get(), static_cast<size_t>(rows) * N * 4);
+    });
+}
+
+int sana_op_layer_norm(sana_cuda_ctx* ctx, const float* x, int rows, int C, float eps, const float* gamma,
+                       const float* beta, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(x && out && rows >= 0 && C >= 1, "invalid layer_norm arguments");
+        sana::Engine& eng = engine(ctx);
+        const size_t n = static_cast<size_t>(rows) * C;
+        DevBuf xd = f32_upload(x, n), o, g, b;
+        o.ensure(std::max<size_t>(n, 1) * 4);
+        if (gamma) g = f32_upload(gamma, C);
+        if (beta) b = f32_upload(beta, C);
+        sana::ln_modulate<float>(xd.as<float>(), rows, C, std::max(rows, 1), g.as<float>(), b.as<float>(), nullptr, 0, 0,
+                                 0, eps, o.as<float>(), eng.stream());
+        finish(eng);
+        if (n) d2h(out, o.get(), n * 4);
+    });
+}
+
+int sana_op_rms_norm(sana_cuda_ctx* ctx, const float* x, int rows, int C, float eps, const float* weight, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(x && out && rows >= 0 && C >= 1, "invalid rms_norm arguments");
+        sana::Engine& eng = engine(ctx);
+        const size_t n = static_cast<size_t>(rows) * C;
+        DevBuf xd = f32_upload(x, n), o, w;
+        o.ensure(std::max<size_t>(n, 1) * 4);
+        if (weight) w = f32_upload(weight, C);
+        sana::rms_norm<float>(xd.as<float>(), rows, C, eps, w.as<float>(), o.as<float>(), eng.stream());
+        finish(eng);
+        if (n) d2h(out, o.get(), n * 4);
+    });
+}
+
+int sana_op_modulate(sana_cuda_ctx* ctx, const float* x, int B, int T, int C, const float* shift, const float* scale,
+                     float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(x && shift && scale && out && B >= 1 && T >= 1 && C >= 1, "invalid modulate arguments");
+        sana::Engine& eng = engine(ctx);
+        const size_t n = static_cast<size_t>(B) * T * C;
+        std::vector<float> mod(static_cast<size_t>(B) * 2 * C);
+        for (int b = 0; b < B; ++b) {
+            std::memcpy(&mod[static_cast<size_t>(b) * 2 * C], shift + static_cast<size_t>(b) * C, C * 4);
+            std::memcpy(&mod[static_cast<size_t>(b) * 2 * C + C], scale + static_cast<size_t>(b) * C, C * 4);
+        }
+        DevBuf xd = f32_upload(x, n), md = f32_upload(mod.data(), mod.size()), o;
+        o.ensure(n * 4);
+        sana::modulate(xd.as<float>(), static_cast<long long>(B) * T, C, T, md.as<float>(), 2LL * C, 0, 1,
+                       o.as<float>(), eng.stream());
+        finish(eng);
+        d2h(out, o.get(), n * 4);
+    });
+}
+
+int sana_op_linear_attention(sana_cuda_ctx* ctx, const float* q, const float* k, const float* v, int B, int H, int Tq,
+                             int Tk, int D, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(q && k && v && out && B >= 1 && H >= 1 && Tq >= 1 && Tk >= 1 && D >= 1,
+                     "invalid linear attention arguments");
+        sana::Engine& eng = engine(ctx);
+        const bool bf = eng.mode() == sana::kModeBf16;
+        const int HD = H * D;
+        std::vector<float> qt = heads_to_tokens(q, B, H, Tq, D);
+        std::vector<float> kt = heads_to_tokens(k, B, H, Tk, D), vt = heads_to_tokens(v, B, H, Tk, D);
+        std::vector<float> kv(static_cast<size_t>(B) * Tk * 2 * HD);
+        for (size_t r = 0; r < static_cast<size_t>(B) * Tk; ++r) {
+            std::memcpy(&kv[r * 2 * HD], &kt[r * HD], HD * 4);
+            std::memcpy(&kv[r * 2 * HD + HD], &vt[r * HD], HD * 4);
+        }
+        ActBuf Q, KV, O;
+        Q.upload(qt.data(), qt.size(), bf);
+        KV.upload(kv.data(), kv.size(), bf);
+        O.alloc(qt.size(), bf);
+        DevBuf part;
+        part.ensure(static_cast<size_t>(B) * H * (sana::linattn_chunks(Tk) + 1) * (D + 1) * D * 4);
+        if (bf) {
+            sana::linear_attention<bf16>(static_cast<const bf16*>(Q.get()), HD, 0, static_cast<const bf16*>(KV.get()),
+                                         2LL * HD, 0, HD, B, Tq, Tk, H, D, part.as<float>(),
+                                         static_cast<bf16*>(O.get()), HD, eng.stream());
+        } else {
+            sana::linear_attention<float>(static_cast<const float*>(Q.get()), HD, 0,
+                                          static_cast<const float*>(KV.get()), 2LL * HD, 0, HD, B, Tq, Tk, H, D,
+                                          part.as<float>(), static_cast<float*>(O.get()), HD, eng.stream());
+        }
+        finish(eng);
+        std::vector<float> ot(qt.size());
+        O.download(ot.data());
+        tokens_to_heads(ot.data(), B, H, Tq, D, out);
+    });
+}
+
+int sana_op_attention(sana_cuda_ctx* ctx, const float* q, const float* k, const float* v, int B, int H, int Tq,
+                      int Tk, int D, const float* bias, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(q && k && v && out && B >= 1 && H >= 1 && Tq >= 1 && Tk >= 1 && D >= 1,
+                     "invalid attention arguments");
+        sana::Engine& eng = engine(ctx);
+        const bool bf = eng.mode() == sana::kModeBf16;
+        const int HD = H * D;
+        std::vector<float> qt = heads_to_tokens(q, B, H, Tq, D);
+        std::vector<float> kt = heads_to_tokens(k, B, H, Tk, D), vt = heads_to_tokens(v, B, H, Tk, D);
+        std::vector<float> kv(static_cast<size_t>(B) * Tk * 2 * HD);
+        for (size_t r = 0; r < static_cast<size_t>(B) * Tk; ++r) {
+            std::memcpy(&kv[r * 2 * HD], &kt[r * HD], HD * 4);
+            std::memcpy(&kv[r * 2 * HD + HD], &vt[r * HD], HD * 4);
+        }
+        ActBuf Q, KV, O;
+        Q.upload(qt.data(), qt.size(), bf);
+        KV.upload(kv.data(), kv.size(), bf);
+        O.alloc(qt.size(), bf);
+        DevBuf bd, kl;
+        if (bias) {
+            bd = f32_upload(bias, static_cast<size_t>(B) * Tk);
+            kl.ensure(static_cast<size_t>(B) * 4);
+            sana::caption_kv_len(bd.as<float>(), B, Tk, kl.as<int>(), eng.stream());
+        }
+        const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)));
+        if (bf) {
+            sana::cross_attention<bf16>(static_cast<const bf16*>(Q.get()), HD, static_cast<const bf16*>(KV.get()),
+                                        2LL * HD, 0, HD, bd.as<float>(), kl.as<int>(), B, Tq, Tk, H, D, scale,
+                                        static_cast<bf16*>(O.get()), HD, eng.stream());
+        } else {
+            sana::cross_attention<float>(static_cast<const float*>(Q.get()), HD, static_cast<const float*>(KV.get()),
+                                         2LL * HD, 0, HD, bd.as<float>(), kl.as<int>(), B, Tq, Tk, H, D, scale,
+                                         static_cast<float*>(O.get()), HD, eng.stream());
+        }
+        finish(eng);
+        std::vector<float> ot(qt.size());
+        O.download(ot.data());
+        tokens_to_heads(ot.data(), B, H, Tq, D, out);
+    });
+}
+
+int sana_op_conv1x1(sana_cuda_ctx* ctx, const float* x, int B, int Cin, int H, int W, const float* w,
+                    const float* bias, int Cout, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(x && w && out && B >= 1 && Cin >= 1 && H >= 1 && W >= 1 && Cout >= 1, "invalid conv1x1 arguments");
+        sana::Engine& eng = engine(ctx);
+        const bool bf = eng.mode() == sana::kModeBf16;
+        const int HW = H * W;
+        std::vector<float> xt = nchw_to_tokens(x, B, Cin, HW);
+        ActBuf A, Wt;
+        A.upload(xt.data(), xt.size(), bf);
+        Wt.upload(w, static_cast<size_t>(Cout) * Cin, bf);
+        DevBuf bd = bias ? f32_upload(bias, Cout) : DevBuf(), o;
+        o.ensure(static_cast<size_t>(B) * HW * Cout * 4);
+        run_gemm(eng, A, Cin, Wt, Cin, B * HW, Cout, Cin, epi(o.get(), false, Cout, bd.as<float>()));
+        finish(eng);
+        std::vector<float> ot(static_cast<size_t>(B) * HW * Cout);
+        d2h(ot.data(), o.get(), ot.size() * 4);
+        tokens_to_nchw(ot.data(), B, Cout, HW, out);
+    });
+}
+
+int sana_op_depthwise3x3(sana_cuda_ctx* ctx, const float* x, int B, int C, int H, int W, const float* w,
+                         const float* bias, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(x && w && out && B >= 1 && C >= 1 && H >= 1 && W >= 1, "invalid depthwise arguments");
+        sana::Engine& eng = engine(ctx);
+        const int HW = H * W;
+        std::vector<float> xt = nchw_to_tokens(x, B, C, HW);
+        DevBuf xd = f32_upload(xt.data(), xt.size()), wd = f32_upload(w, static_cast<size_t>(C) * 9), bd, o;
+        if (bias) bd = f32_upload(bias, C);
+        o.ensure(xt.size() * 4);
+        sana::depthwise3x3(xd.as<float>(), B, H, W, C, wd.as<float>(), bd.as<float>(), o.as<float>(), eng.stream());
+        finish(eng);
+        std::vector<float> ot(xt.size());
+        d2h(ot.data(), o.get(), ot.size() * 4);
+        tokens_to_nchw(ot.data(), B, C, HW, out);
+    });
+}
+
+int sana_op_glumb_conv(sana_cuda_ctx* ctx, const float* x, int B, int Cin, int H, int W, const float* w_inv,
+                       const float* b_inv, int E, const float* w_dw, const float* b_dw, const float* w_pt, int Cout,
+                       float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(x && w_inv && w_dw && w_pt && out && E >= 2 && E % 2 == 0, "invalid glumb_conv arguments");
+        sana::Engine& eng = engine(ctx);
+        const bool bf = eng.mode() == sana::kModeBf16;
+        const int HW = H * W, M = B * HW;
+        std::vector<float> xt = nchw_to_tokens(x, B, Cin, HW);
+        ActBuf A, Wi, Wp, Hb, G;
+        A.upload(xt.data(), xt.size(), bf);
+        Wi.upload(w_inv, static_cast<size_t>(E) * Cin, bf);
+        Wp.upload(w_pt, static_cast<size_t>(Cout) * (E / 2), bf);
+        Hb.alloc(static_cast<size_t>(M) * E, bf);
+        G.alloc(static_cast<size_t>(M) * (E / 2), bf);
+        DevBuf bi, bd, wd = f32_upload(w_dw, static_cast<size_t>(E) * 9), o;
+        if (b_inv) bi = f32_upload(b_inv, E);
+        std::vector<float> zeros(E, 0.f);
+        bd = f32_upload(b_dw ? b_dw : zeros.data(), E);
+        o.ensure(static_cast<size_t>(M) * Cout * 4);
+        run_gemm(eng, A, Cin, Wi, Cin, M, E, Cin, epi(Hb.get(), bf, E, bi.as<float>(), sana::kActSilu));
+        if (bf) {
+            sana::depthwise_glu<bf16>(static_cast<const bf16*>(Hb.get()), E, B, H, W, E, wd.as<float>(),
+                                      bd.as<float>(), static_cast<bf16*>(G.get()), E / 2, eng.stream());
+        } else {
+            sana::depthwise_glu<float>(static_cast<const float*>(Hb.get()), E, B, H, W, E, wd.as<float>(),
+                                       bd.as<float>(), static_cast<float*>(G.get()), E / 2, eng.stream());
+        }
+        run_gemm(eng, G, E / 2, Wp, E / 2, M, Cout, E / 2, epi(o.get(), false, Cout));
+        finish(eng);
+        std::vector<float> ot(static_cast<size_t>(M) * Cout);
+        d2h(ot.data(), o.get(), ot.size() * 4);
+        tokens_to_nchw(ot.data(), B, Cout, HW, out);
+    });
+}
+
+int sana_op_project_caption(sana_cuda_ctx* ctx, const float* enc, int B, int L, int Din, const float* w1,
+                            const float* b1, int C, const float* w2, const float* b2, const float* norm_w, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(enc && w1 && w2 && norm_w && out && B >= 1 && L >= 1 && Din >= 1 && C >= 1,
+                     "invalid project_caption arguments");
+        sana::Engine& eng = engine(ctx);
+        const bool bf = eng.mode() == sana::kModeBf16;
+        const int M = B * L;
+        ActBuf A, W1, W2, Hh;
+        A.upload(enc, static_cast<size_t>(M) * Din, bf);
+        std::vector<float> w1t = transpose(w1, Din, C), w2t = transpose(w2, C, C);
+        W1.upload(w1t.data(), w1t.size(), bf);
+        W2.upload(w2t.data(), w2t.size(), bf);
+        Hh.alloc(static_cast<size_t>(M) * C, bf);
+        DevBuf bd1, bd2, nd = f32_upload(norm_w, C), p, o;
+        if (b1) bd1 = f32_upload(b1, C);
+        if (b2) bd2 = f32_upload(b2, C);
+        p.ensure(static_cast<size_t>(M) * C * 4);
+        o.ensure(static_cast<size_t>(M) * C * 4);
+        run_gemm(eng, A, Din, W1, Din, M, C, Din, epi(Hh.get(), bf, C, bd1.as<float>(), sana::kActGelu));
+        run_gemm(eng, Hh, C, W2, C, M, C, C, epi(p.get(), false, C, bd2.as<float>()));
+        sana::rms_norm<float>(p.as<float>(), M, C, 1e-5f, nd.as<float>(), o.as<float>(), eng.stream());
+        finish(eng);
+        d2h(out, o.get(), static_cast<size_t>(M) * C * 4);
+    });
+}
+
+int sana_op_attention_block(sana_cuda_ctx* ctx, const float* x, int B, int T, int C, const float* wq, const float* bq,
+                            const float* wk, const float* bk, const float* wv, const float* bv, const float* wo,
+                            const float* bo, int heads, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(x && wq && wk && wv && wo && out && B >= 1 && T >= 1 && C >= 1, "invalid attention_block arguments");
+        SANA_REQUIRE(heads >= 1 && C % heads == 0, "hidden size must be divisible by num_heads");
+        sana::Engine& eng = engine(ctx);
+        const bool bf = eng.mode() == sana::kModeBf16;
+        const int M = B * T, D = C / heads;
+        std::vector<float> wqkv(static_cast<size_t>(3) * C * C), bqkv(3 * static_cast<size_t>(C), 0.f);
+        const float* ws[3] = {wq, wk, wv};
+        const float* bs[3] = {bq, bk, bv};
+        for (int j = 0; j < 3; ++j) {
+            std::vector<float> t = transpose(ws[j], C, C);
+            std::memcpy(&wqkv[static_cast<size_t>(j) * C * C], t.data(), t.size() * 4);
+            if (bs[j]) std::memcpy(&bqkv[static_cast<size_t>(j) * C], bs[j], C * 4);
+        }
+        std::vector<float> wot = transpose(wo, C, C);
+        ActBuf X, Wqkv, Wo, QKV, AO;
+        X.upload(x, static_cast<size_t>(M) * C, bf);
+        Wqkv.upload(wqkv.data(), wqkv.size(), bf);
+        Wo.upload(wot.data(), wot.size(), bf);
+        QKV.alloc(static_cast<size_t>(M) * 3 * C, bf);
+        AO.alloc(static_cast<size_t>(M) * C, bf);
+        DevBuf bqd = f32_upload(bqkv.data(), bqkv.size()), bod, part, o;
+        if (bo) bod = f32_upload(bo, C);
+        part.ensure(static_cast<size_t>(B) * heads * (sana::linattn_chunks(T) + 1) * (D + 1) * D * 4);
+        o.ensure(static_cast<size_t>(M) * C * 4);
+        run_gemm(eng, X, C, Wqkv, C, M, 3 * C, C, epi(QKV.get(), bf, 3 * C, bqd.as<float>()));
+        if (bf) {
+            const bf16* qkv = static_cast<const bf16*>(QKV.get());
+            sana::linear_attention<bf16>(qkv, 3LL * C, 0, qkv, 3LL * C, C, 2 * C, B, T, T, heads, D, part.as<float>(),
+                                         static_cast<bf16*>(AO.get()), C, eng.stream());
+        } else {
+            const float* qkv = static_cast<const float*>(QKV.get());
+            sana::linear_attention<float>(qkv, 3LL * C, 0, qkv, 3LL * C, C, 2 * C, B, T, T, heads, D,
+                                          part.as<float>(), static_cast<float*>(AO.get()), C, eng.stream());
+        }
+        run_gemm(eng, AO, C, Wo, C, M, C, C, epi(o.get(), false, C, bod.as<float>()));
+        finish(eng);
+        d2h(out, o.get(), static_cast<size_t>(M) * C * 4);
+    });
+}
+
+int sana_op_cross_attention_block(sana_cuda_ctx* ctx, const float* x, int B, int T, int C, const float* context,
+                                  int L, const float* bias, const float* wq, const float* bq, const float* wk,
+                                  const float* bk, const float* wv, const float* bv, const float* wo, const float* bo,
+                                  int heads, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(x && context && wq && wk && wv && wo && out && B >= 1 && T >= 1 && C >= 1 && L >= 1,
+                     "invalid cross_attention_block arguments");
+        SANA_REQUIRE(heads >= 1 && C % heads == 0, "hidden size must be divisible by num_heads");
+        sana::Engine& eng = engine(ctx);
+        const bool bf = eng.mode() == sana::kModeBf16;
+        const int M = B * T, D = C / heads;
+        std::vector<float> wkv(static_cast<size_t>(2) * C * C), bkv(2 * static_cast<size_t>(C), 0.f);
+        {
+            std::vector<float> tk = transpose(wk, C, C), tv = transpose(wv, C, C);
+            std::memcpy(wkv.data(), tk.data(), tk.size() * 4);
+            std::memcpy(wkv.data() + static_cast<size_t>(C) * C, tv.data(), tv.size() * 4);
+            if (bk) std::memcpy(bkv.data(), bk, C * 4);
+            if (bv) std::memcpy(bkv.data() + C, bv, C * 4);
+        }
+        std::vector<float> wqt = transpose(wq, C, C), wot = transpose(wo, C, C);
+        ActBuf X, Cx, Wq, Wkv, Wo, Q, KV, AO;
+        X.upload(x, static_cast<size_t>(M) * C, bf);
+        Cx.upload(context, static_cast<size_t>(B) * L * C, bf);
+        Wq.upload(wqt.data(), wqt.size(), bf);
+        Wkv.upload(wkv.data(), wkv.size(), bf);
+        Wo.upload(wot.data(), wot.size(), bf);
+        Q.alloc(static_cast<size_t>(M) * C, bf);
+        KV.alloc(static_cast<size_t>(B) * L * 2 * C, bf);
+        AO.alloc(static_cast<size_t>(M) * C, bf);
+        DevBuf bqd, bkvd = f32_upload(bkv.data(), bkv.size()), bod, bd, kl, o;
+        if (bq) bqd = f32_upload(bq, C);
+        if (bo) bod = f32_upload(bo, C);
+        if (bias) {
+            bd = f32_upload(bias, static_cast<size_t>(B) * L);
+            kl.ensure(static_cast<size_t>(B) * 4);
+            sana::caption_kv_len(bd.as<float>(), B, L, kl.as<int>(), eng.stream());
+        }
+        o.ensure(static_cast<size_t>(M) * C * 4);
+        run_gemm(eng, X, C, Wq, C, M, C, C, epi(Q.get(), bf, C, bqd.as<float>()));
+        run_gemm(eng, Cx, C, Wkv, C, B * L, 2 * C, C, epi(KV.get(), bf, 2 * C, bkvd.as<float>()));
+        const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)));
+        if (bf) {
+            sana::cross_attention<bf16>(static_cast<const bf16*>(Q.get()), C, static_cast<const bf16*>(KV.get()), 2LL * C,
+                                        0, C, bd.as<float>(), kl.as<int>(), B, T, L, heads, D, scale,
+                                        static_cast<bf16*>(AO.get()), C, eng.stream());
+        } else {
+            sana::cross_attention<float>(static_cast<const float*>(Q.get()), C, static_cast<const float*>(KV.get()),
+                                         2LL * C, 0, C, bd.as<float>(), kl.as<int>(), B, T, L, heads, D, scale,
+                                         static_cast<float*>(AO.get()), C, eng.stream());
+        }
+        run_gemm(eng, AO, C, Wo, C, M, C, C, epi(o.get(), false, C, bod.as<float>()));
+        finish(eng);
+        d2h(out, o.get(), static_cast<size_t>(M) * C * 4);
+    });
+}
+
+int sana_op_cfg(sana_cuda_ctx* ctx, const float* noise, int B, int Cl, int H, int W, float guidance, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(noise && out && B >= 1 && Cl >= 1 && H >= 1 && W >= 1, "invalid cfg arguments");
+        sana::Engine& eng = engine(ctx);
+        const int HW = H * W;
+        const size_t n = static_cast<size_t>(B) * Cl * HW;
+        std::vector<float> rows = nchw_to_tokens(noise, 2 * B, Cl, HW);
+        DevBuf nd = f32_upload(rows.data(), rows.size()), lat, h0, h1;
+        lat.ensure(n * 4);
+        h0.ensure(n * 4);
+        h1.ensure(n * 4);
+        SANA_CUDA(cudaMemsetAsync(lat.get(), 0, n * 4, eng.stream()));
+        sana::SchedCoef k{};
+        k.guidance = guidance;
+        k.sigma_s = -1.0f;  // x0 = 0 - (-1) * guided = guided
+        k.a = 0.0f;
+        k.b = 1.0f;
+        sana::cfg_scheduler_step(nd.as<float>(), B, Cl, HW, lat.as<float>(), h0.as<float>(), h1.as<float>(), k,
+                                 eng.stream());
+        finish(eng);
+        d2h(out, lat.get(), n * 4);
+    });
+}
+
+// --- scheduler -------------------------------------------------------------------------------
+
+int sana_scheduler_schedule(int n, float flow_shift, float* timesteps, float* sigmas) {
+    if (n <= 0 || !timesteps || !sigmas) return SANA_ERR_INVALID;
+    try {
+        std::vector<float> ts, sg;
+        sana::scheduler_schedule(n, flow_shift, ts, sg);
+        std::memcpy(timesteps, ts.data(), ts.size() * 4);
+        std::memcpy(sigmas, sg.data(), sg.size() * 4);
+        return SANA_OK;
+    } catch (...) {
+        return SANA_ERR_INVALID;
+    }
+}
+
+int sana_scheduler_convert(sana_cuda_ctx* ctx, const float* sigmas, int n_sigmas, int step_index,
+                           const float* model_output, const float* sample, int numel, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(sigmas && model_output && sample && out && numel >= 1, "invalid convert arguments");
+        SANA_REQUIRE(n_sigmas >= 2 && step_index >= 0 && step_index < n_sigmas - 1,
+                     "scheduler step_index is out of range");
+        sana::Engine& eng = engine(ctx);
+        std::vector<float> rows(2 * static_cast<size_t>(numel));
+        std::memcpy(rows.data(), model_output, numel * 4);
+        std::memcpy(rows.data() + numel, model_output, numel * 4);
+        DevBuf nd = f32_upload(rows.data(), rows.size()), lat = f32_upload(sample, numel), h0, h1;
+        h0.ensure(numel * 4);
+        h1.ensure(numel * 4);
+        sana::SchedCoef k{};
+        k.guidance = 1.0f;
+        k.sigma_s = sigmas[step_index];
+        sana::cfg_scheduler_step(nd.as<float>(), 1, 1, numel, lat.as<float>(), h0.as<float>(), h1.as<float>(), k,
+                                 eng.stream());
+        finish(eng);
+        d2h(out, h0.get(), numel * 4);
+    });
+}
+
+int sana_scheduler_update(sana_cuda_ctx* ctx, int order, const float* sigmas, int n_sigmas, int step_index,
+                          const float* m0, const float* m1, const float* sample, int numel, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(sigmas && m0 && sample && out && numel >= 1, "invalid update arguments");
+        SANA_REQUIRE(order == 1 || order == 2, "order must be 1 or 2");
+        SANA_REQUIRE(order == 1 || m1, "second-order update requires two model outputs");
+        sana::Engine& eng = engine(ctx);
+        std::vector<float> sg(sigmas, sigmas + n_sigmas);
+        const sana::SchedCoef k = sana::scheduler_coefficients_order(sg, step_index, order, 1.0f);
+        DevBuf a = f32_upload(m0, numel), b = f32_upload(m1 ? m1 : m0, numel), x = f32_upload(sample, numel), o;
+        o.ensure(numel * 4);
+        sana::scheduler_update(a.as<float>(), b.as<float>(), x.as<float>(), numel, k, o.as<float>(), eng.stream());
+        finish(eng);
+        d2h(out, o.get(), numel * 4);
+    });
+}
+
+int sana_scheduler_step(sana_cuda_ctx* ctx, const float* sigmas, int n_sigmas, int* step_index,
+                        int* lower_order_count, float* history, int* n_history, const float* model_output,
+                        const float* sample, int numel, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(sigmas && step_index && lower_order_count && n_history && model_output && sample && out &&
+                         numel >= 1,
+                     "invalid step arguments");
+        SANA_REQUIRE(*n_history >= 0 && *n_history <= 2 && (*n_history == 0 || history), "invalid history");
+        SANA_REQUIRE(history != nullptr, "history buffer (2 x numel) required");
+        sana::Engine& eng = engine(ctx);
+        std::vector<float> sg(sigmas, sigmas + n_sigmas);
+        const sana::SchedCoef k = sana::scheduler_coefficients(sg, *step_index, *lower_order_count, 1.0f);
+        if (k.second_order) {
+            SANA_REQUIRE(*n_history >= 1, "second-order update requires two model outputs");
+        }
+        std::vector<float> rows(2 * static_cast<size_t>(numel));
+        std::memcpy(rows.data(), model_output, numel * 4);
+        std::memcpy(rows.data() + numel, model_output, numel * 4);
+        DevBuf nd = f32_upload(rows.data(), rows.size()), lat = f32_upload(sample, numel), h0, h1;
+        h0.ensure(numel * 4);
+        if (*n_history >= 1) h1 = f32_upload(history + static_cast<size_t>(*n_history - 1) * numel, numel);
+        else h1.ensure(numel * 4);
+        sana::cfg_scheduler_step(nd.as<float>(), 1, 1, numel, lat.as<float>(), h0.as<float>(), h1.as<float>(), k,
+                                 eng.stream());
+        finish(eng);
+        d2h(out, lat.get(), numel * 4);
+        std::vector<float> conv(numel);
+        d2h(conv.data(), h0.get(), numel * 4);
+        if (*n_history == 2) std::memmove(history, history + numel, static_cast<size_t>(numel) * 4);
+        const int slot = *n_history == 2 ? 1 : *n_history;
+        std::memcpy(history + static_cast<size_t>(slot) * numel, conv.data(), numel * 4);
+        *n_history = slot + 1;
+        if (*lower_order_count < 2) ++*lower_order_count;
+        ++*step_index;
+    });
+}
+
+// --- synthetic inputs ---------------------------------------------------------------------
+
+// torch.randn on a CPU generator for n >= 16 (the algorithm restated by torch_rng.cpp:9-68):
+// MT19937 draws, uniforms u = (draw & (2^24 - 1)) / 2^24, Box-Muller on complete blocks of
+// 16 (radius from the first 8, angle from the last 8), and a final re-drawn block of 16
+// over the last 16 elements when n is not a multiple of 16.
+int sana_randn_torch_cpu(float* out, size_t n, uint64_t seed) {
+    if (!out || n < 16) return SANA_ERR_INVALID;
+    std::mt19937 gen(static_cast<std::mt19937::result_type>(seed & 0xffffffffULL));
+    auto uniform = [&gen]() { return static_cast<float>(gen() & 0xffffffu) * (1.0f / 16777216.0f); };
+    auto block16 = [](float* d) {
+        const double two_pi = 2.0 * 3.14159265358979323846;
+        for (int j = 0; j < 8; ++j) {
+            const float radius = std::sqrt(-2.0f * std::log(1.0f - d[j]));
+            const float angle = static_cast<float>(two_pi * static_cast<double>(d[j + 8]));
+            d[j] = radius * std::cos(angle);
+            d[j + 8] = radius * std::sin(angle);
+        }
+    };
+    for (size_t i = 0; i < n; ++i) out[i] = uniform();
+    for (size_t i = 0; i + 16 <= n; i += 16) block16(out + i);
+    if (n % 16 != 0) {
+        float* tail = out + n - 16;
+        for (int j = 0; j < 16; ++j) tail[j] = uniform();
+        block16(tail);
+    }
+    return SANA_OK;
+}
+
+}  // extern "C"

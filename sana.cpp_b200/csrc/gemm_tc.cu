@@ -1,0 +1,458 @@
+// Tensor-core GEMM for sm_100a: tcgen05.mma (kind::f16, bf16 x bf16 -> fp32 in TMEM),
+// operands staged by TMA (cp.async.bulk.tensor, 128-byte swizzle, no multicast), a
+// persistent warp-specialised pipeline and the fused epilogue of gemm.h.
+//
+//   warp 0      TMA producer (one lane): A tile [128 x 64] and B tile [BN x 64] per stage
+//   warp 1      TMEM allocator + MMA issuer (one lane): 4 x (128 x BN x 16) MMAs per stage
+//   warps 2..5  epilogue: tcgen05.ld of their 32-lane TMEM quarter, bias/act/gate/residual,
+//               stores to global
+// Two TMEM accumulators (2 x BN fp32 columns) let the epilogue of one tile overlap the
+// MMAs of the next. Every mbarrier wait is bounded (common.cuh); on expiry the kernel
+// records kTimeout in the device error word, drains its own TMA copies and MMAs with
+// bounded waits, frees TMEM and returns.
+#include <cuda.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "gemm.h"
+
+namespace sana {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+
+template <int BN>
+struct Cfg {
+    static constexpr int kStages = BN == 128 ? 6 : 4;
+    static constexpr int kABytes = BM * BK * 2;
+    static constexpr int kBBytes = BN * BK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kTmemCols = 2 * BN;
+    // layout: [A stages][B stages][barriers][tmem slot]
+    static constexpr int kBarOffset = kStages * kStageBytes;
+    static constexpr int kSmemBytes = kBarOffset + (2 * kStages + 5) * 8 + 16 + 1024;
+};
+
+// --- tcgen05 / TMA primitives -----------------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint32_t dst, uint32_t bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major operand in the canonical 128-byte-swizzle
+// layout that TMA writes: 8-row x 128-byte atoms stacked every 1024 bytes (SBO = 1024),
+// leading offset unused for swizzled K-major (encoded 1), descriptor version 1 (sm_100),
+// base offset 0 (tiles are 1024-byte aligned), layout type 2 = SWIZZLE_128B.
+__device__ __forceinline__ uint64_t kmajor_sw128_desc(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(1u) << 16;
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(2u) << 61;
+    return d;
+}
+
+// Instruction descriptor for kind::f16: D fp32 (bits 4-5 = 1), A and B bf16 (bits 7-9,
+// 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// --- epilogue -------------------------------------------------------------------------
+__device__ __forceinline__ void store_val(void* out, int is_bf16, long long idx, float v) {
+    if (is_bf16) {
+        static_cast<bf16*>(out)[idx] = __float2bfloat16_rn(v);
+    } else {
+        static_cast<float*>(out)[idx] = v;
+    }
+}
+
+// Applies the epilogue to 16 consecutive columns [n0, n0+16) of one row.
+__device__ __forceinline__ void epilogue16(const Epilogue& ep, int row, int n0, int N, float (&v)[16],
+                                           bool vec) {
+    if (vec && n0 + 16 <= N) {
+        if (ep.bias) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+                const float4 b = *reinterpret_cast<const float4*>(ep.bias + n0 + j);
+                v[j] += b.x;
+                v[j + 1] += b.y;
+                v[j + 2] += b.z;
+                v[j + 3] += b.w;
+            }
+        }
+        if (ep.act == kActSilu) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = silu(v[j]);
+        } else if (ep.act == kActGelu) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = gelu_tanh(v[j]);
+        }
+        if (ep.resid) {
+            const float* r = ep.resid + static_cast<long long>(row) * ep.ldr + n0;
+            const float* g = ep.gate ? ep.gate + static_cast<long long>(row / ep.rows_per_gate) * ep.gate_ld + n0
+                                     : nullptr;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+                const float4 rv = *reinterpret_cast<const float4*>(r + j);
+                float4 gv = make_float4(1.f, 1.f, 1.f, 1.f);
+                if (g) gv = *reinterpret_cast<const float4*>(g + j);
+                v[j] = rv.x + gv.x * v[j];
+                v[j + 1] = rv.y + gv.y * v[j + 1];
+                v[j + 2] = rv.z + gv.z * v[j + 2];
+                v[j + 3] = rv.w + gv.w * v[j + 3];
+            }
+        }
+        void* outs[2] = {ep.out, ep.out2};
+        const int bfs[2] = {ep.out_bf16, ep.out2_bf16};
+        const long long lds[2] = {ep.ldo, ep.ldo2};
+#pragma unroll
+        for (int o = 0; o < 2; ++o) {
+            if (!outs[o]) continue;
+            if (o == 1 && ep.act2 == kActSilu) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = silu(v[j]);
+            }
+            const long long base = static_cast<long long>(row) * lds[o] + n0;
+            if (bfs[o]) {
+                uint4 pk[2];
+                uint32_t* w = reinterpret_cast<uint32_t*>(pk);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+                    w[j] = *reinterpret_cast<uint32_t*>(&h);
+                }
+                uint4* dst = reinterpret_cast<uint4*>(static_cast<bf16*>(outs[o]) + base);
+                dst[0] = pk[0];
+                dst[1] = pk[1];
+            } else {
+                float4* dst = reinterpret_cast<float4*>(static_cast<float*>(outs[o]) + base);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            }
+        }
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const int n = n0 + j;
+        if (n >= N) break;
+        float x = v[j];
+        if (ep.bias) x += ep.bias[n];
+        if (ep.act == kActSilu) x = silu(x);
+        else if (ep.act == kActGelu) x = gelu_tanh(x);
+        if (ep.resid) {
+            const float g = ep.gate ? ep.gate[static_cast<long long>(row / ep.rows_per_gate) * ep.gate_ld + n] : 1.0f;
+            x = ep.resid[static_cast<long long>(row) * ep.ldr + n] + g * x;
+        }
+        if (ep.out) store_val(ep.out, ep.out_bf16, static_cast<long long>(row) * ep.ldo + n, x);
+        if (ep.out2) store_val(ep.out2, ep.out2_bf16, static_cast<long long>(row) * ep.ldo2 + n,
+                               ep.act2 == kActSilu ? silu(x) : x);
+    }
+}
+
+// --- the kernel ------------------------------------------------------------------------
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
+                   int N, int K, Epilogue ep, int vec, int* err) {
+    using C = Cfg<BN>;
+    constexpr int S = C::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* gbase = smem_raw + (base - raw);
+    const uint32_t a_smem = base;                       // S x kABytes
+    const uint32_t b_smem = base + S * C::kABytes;      // S x kBBytes
+    const uint32_t bars = base + C::kBarOffset;
+    auto full = [&](int s) { return bars + 8u * s; };
+    auto empty = [&](int s) { return bars + 8u * (S + s); };
+    auto tfull = [&](int a) { return bars + 8u * (2 * S + a); };
+    auto tempty = [&](int a) { return bars + 8u * (2 * S + 2 + a); };
+    const uint32_t done_bar = bars + 8u * (2 * S + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kBarOffset + (2 * S + 5) * 8);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int num_m = (M + BM - 1) / BM;
+    const int num_n = (N + BN - 1) / BN;
+    const int num_tiles = num_m * num_n;
+    const int num_kb = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull(a), 1);
+            mbar_init(tempty(a), 4);
+        }
+        mbar_init(done_bar, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+            int stage = 0;
+            uint32_t phase = 0;
+            long long issued = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+                const int m_blk = tile % num_m;
+                const int n_blk = tile / num_m;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(empty(stage), phase ^ 1u, err, kTimeout)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full(stage), C::kStageBytes);
+                    tma_load_2d(&tmA, a_smem + stage * C::kABytes, full(stage), kb * BK, m_blk * BM);
+                    tma_load_2d(&tmB, b_smem + stage * C::kBBytes, full(stage), kb * BK, n_blk * BN);
+                    ++issued;
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok || *(volatile int*)err != 0) {
+                // Drain: wait (bounded) until each of the last issued copies has landed.
+                const long long first = issued > S ? issued - S : 0;
+                for (long long i = first; i < issued; ++i) {
+                    mbar_wait_quiet(full(static_cast<int>(i % S)), static_cast<uint32_t>((i / S) & 1));
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int local = 0;
+            for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++local) {
+                const int acc = local & 1;
+                const uint32_t use = static_cast<uint32_t>(local >> 1);
+                if (!mbar_wait(tempty(acc), (use & 1u) ^ 1u, err, kTimeout)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(full(stage), phase, err, kTimeout)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = a_smem + stage * C::kABytes;
+                    const uint32_t b_addr = b_smem + stage * C::kBBytes;
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        umma_bf16(d_tmem, kmajor_sw128_desc(a_addr + k * 32), kmajor_sw128_desc(b_addr + k * 32),
+                                  idesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    umma_commit(empty(stage));
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(tfull(acc));
+            }
+            // All MMAs issued by this thread are complete once done_bar fires.
+            umma_commit(done_bar);
+            mbar_wait_quiet(done_bar, 0u);
+        }
+    } else {
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        int local = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const uint32_t use = static_cast<uint32_t>(local >> 1);
+            if (!mbar_wait(tfull(acc), use & 1u, err, kTimeout)) break;
+            tc_fence_after();
+            const int m_blk = tile % num_m;
+            const int n_blk = tile / num_m;
+            const int row = m_blk * BM + q * 32 + lane;
+            const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 16) {
+                uint32_t r[16];
+                tmem_ld16(t_row + static_cast<uint32_t>(c), r);
+                tmem_wait_ld();
+                const int n0 = n_blk * BN + c;
+                if (row < M && n0 < N) {
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+                    epilogue16(ep, row, n0, N, v, vec != 0);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty(acc));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::kTmemCols);
+    }
+}
+
+// --- host side ---------------------------------------------------------------------------
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiled encoder() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<EncodeTiled>(p);
+        }
+    });
+    if (!fn) throw CudaError("cuTensorMapEncodeTiled is not available from the driver");
+    return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with row stride ld elements;
+// box = [box_rows, 64 columns], 128-byte swizzle, out-of-bounds elements read as zero.
+static CUtensorMap make_map(const void* ptr, int rows, int cols, long long ld, int box_rows) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
+    return m;
+}
+
+template <int BN>
+static void launch(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
+    using C = Cfg<BN>;
+    static bool attr_done = false;
+    if (!attr_done) {
+        SANA_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::kSmemBytes));
+        attr_done = true;
+    }
+    const CUtensorMap ma = make_map(p.A, p.M, p.K, p.lda, BM);
+    const CUtensorMap mb = make_map(p.B, p.N, p.K, p.ldb, BN);
+    const Epilogue& e = p.ep;
+    auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    bool vec = (p.N % 16 == 0);
+    if (e.bias) vec = vec && a16(e.bias);
+    if (e.resid) vec = vec && a16(e.resid) && (e.ldr % 4 == 0);
+    if (e.gate) vec = vec && a16(e.gate) && (e.gate_ld % 4 == 0);
+    if (e.out) vec = vec && a16(e.out) && (e.ldo % 8 == 0);
+    if (e.out2) vec = vec && a16(e.out2) && (e.ldo2 % 8 == 0);
+    const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+    const int grid = tiles < num_sms ? tiles : num_sms;
+    gemm_tc_kernel<BN><<<grid, 192, C::kSmemBytes, stream>>>(ma, mb, p.M, p.N, p.K, e, vec ? 1 : 0, err);
+    SANA_CUDA(cudaGetLastError());
+}
+
+}  // namespace tc
+
+bool gemm_tc_supported(const GemmProblem& p) {
+    auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    return p.a_bf16 && p.b_bf16 && p.M > 0 && p.N > 0 && p.K > 0 && (p.K % 8 == 0) && (p.lda % 8 == 0) &&
+           (p.ldb % 8 == 0) && a16(p.A) && a16(p.B) && p.N >= 16;
+}
+
+void gemm_tc(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
+    SANA_REQUIRE(gemm_tc_supported(p), "gemm_tc: unsupported problem");
+    tc::launch<128>(p, err, stream, num_sms);
+}
+
+static std::atomic<long long> g_tc_launches{0}, g_simt_launches{0};
+
+void gemm(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms, bool allow_tc) {
+    if (p.M == 0 || p.N == 0) return;
+    if (allow_tc && gemm_tc_supported(p)) {
+        gemm_tc(p, err, stream, num_sms);
+        ++g_tc_launches;
+    } else {
+        gemm_simt(p, stream);
+        ++g_simt_launches;
+    }
+}
+
+void gemm_counts(long long* tc, long long* simt) {
+    if (tc) *tc = g_tc_launches.load();
+    if (simt) *simt = g_simt_launches.load();
+}
+
+}  // namespace sana

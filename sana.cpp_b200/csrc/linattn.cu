@@ -1,0 +1,144 @@
+// ReLU linear self-attention (linear_attention_4d, transformer_ops.cpp:402-543), three
+// launches over token-major q/k/v columns of the fused QKV projection output:
+//   1. state:  per (sequence, head, 128-token chunk) the partial relu(K)^T V [D x D] and
+//              relu(K) column sum [D], fp32, written to partial[s][h][chunk];
+//   2. reduce: sum of the chunk partials (fixed order, deterministic) -> state[s][h];
+//   3. apply:  per 128-token tile, out[t, r] = sum_d S[r][d] relu(q[t, d]) /
+//              (sum_d z[d] relu(q[t, d]) + 1e-15), staged through shared memory so loads
+//              and stores are row-coalesced.
+// Memory-bound: q, k, v are read once, the output written once; states are tiny.
+#include "kernels.h"
+
+namespace sana {
+namespace {
+
+constexpr int kChunk = 128;
+constexpr int kTile = 128;
+
+template <class T>
+__global__ void __launch_bounds__(256) linattn_state_kernel(const T* __restrict__ kv, long long ld, int k_off,
+                                                            int v_off, int Tk, int heads, int D, int chunks,
+                                                            float* __restrict__ partial) {
+    extern __shared__ float sm[];
+    float* Ks = sm;                 // [kChunk][D], relu applied
+    float* Vs = sm + kChunk * D;    // [kChunk][D]
+    const int s = blockIdx.z, h = blockIdx.y, c = blockIdx.x;
+    const int t0 = c * kChunk;
+    const int n = min(Tk - t0, kChunk);
+    for (int i = threadIdx.x; i < n * D; i += blockDim.x) {
+        const int t = i / D, d = i % D;
+        const long long row = static_cast<long long>(s) * Tk + t0 + t;
+        const float kval = to_f(kv[row * ld + k_off + h * D + d]);
+        Ks[i] = kval > 0.f ? kval : 0.f;
+        Vs[i] = to_f(kv[row * ld + v_off + h * D + d]);
+    }
+    __syncthreads();
+    float* out = partial + ((static_cast<long long>(s) * heads + h) * chunks + c) * (D + 1) * D;
+    for (int e = threadIdx.x; e < (D + 1) * D; e += blockDim.x) {
+        float acc = 0.f;
+        if (e < D * D) {
+            const int r = e / D, d = e % D;
+            for (int t = 0; t < n; ++t) acc = fmaf(Vs[t * D + r], Ks[t * D + d], acc);
+        } else {
+            const int d = e - D * D;
+            for (int t = 0; t < n; ++t) acc += Ks[t * D + d];
+        }
+        out[e] = acc;
+    }
+}
+
+__global__ void linattn_reduce_kernel(const float* __restrict__ partial, int chunks, int width,
+                                      float* __restrict__ state) {
+    const long long sh = blockIdx.y;
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < width; e += gridDim.x * blockDim.x) {
+        float acc = 0.f;
+        for (int c = 0; c < chunks; ++c) acc += partial[(sh * chunks + c) * width + e];
+        state[sh * width + e] = acc;
+    }
+}
+
+template <class T>
+__global__ void __launch_bounds__(kTile) linattn_apply_kernel(const T* __restrict__ q, long long ld, int q_off,
+                                                              int Tq, int heads, int D,
+                                                              const float* __restrict__ state, T* __restrict__ out,
+                                                              long long ldo) {
+    extern __shared__ float sm[];
+    float* Ss = sm;                          // [(D+1) * D]
+    float* qs = Ss + (D + 1) * D;            // [D][kTile]
+    float* os = qs + D * kTile;              // [kTile][D + 1]
+    const int s = blockIdx.z, h = blockIdx.y;
+    const int t0 = blockIdx.x * kTile;
+    const int n = min(Tq - t0, kTile);
+    const float* st = state + (static_cast<long long>(s) * heads + h) * (D + 1) * D;
+    for (int e = threadIdx.x; e < (D + 1) * D; e += blockDim.x) Ss[e] = st[e];
+    for (int i = threadIdx.x; i < kTile * D; i += blockDim.x) {
+        const int t = i / D, d = i % D;
+        float v = 0.f;
+        if (t < n) {
+            v = to_f(q[(static_cast<long long>(s) * Tq + t0 + t) * ld + q_off + h * D + d]);
+            v = v > 0.f ? v : 0.f;
+        }
+        qs[d * kTile + t] = v;
+    }
+    __syncthreads();
+    const int t = threadIdx.x;
+    float den = 0.f;
+    for (int d = 0; d < D; ++d) den = fmaf(Ss[D * D + d], qs[d * kTile + t], den);
+    den += 1e-15f;
+    for (int r = 0; r < D; ++r) {
+        float num = 0.f;
+        const float* srow = Ss + r * D;
+        for (int d = 0; d < D; ++d) num = fmaf(srow[d], qs[d * kTile + t], num);
+        os[t * (D + 1) + r] = num / den;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n * D; i += blockDim.x) {
+        const int tt = i / D, r = i % D;
+        out[(static_cast<long long>(s) * Tq + t0 + tt) * ldo + h * D + r] = from_f<T>(os[tt * (D + 1) + r]);
+    }
+}
+
+}  // namespace
+
+int linattn_chunks(int T) { return (T + kChunk - 1) / kChunk; }
+
+template <class T>
+void linear_attention(const T* q, long long ldq, int q_off, const T* kv, long long ldkv, int k_off, int v_off,
+                      int S, int Tq, int Tk, int heads, int D, float* partial, T* out, long long ldo,
+                      cudaStream_t st) {
+    SANA_REQUIRE(D >= 1 && D <= 128, "linear attention supports head_dim 1..128");
+    if (S == 0 || Tq == 0) return;
+    const int chunks = linattn_chunks(Tk);
+    const int width = (D + 1) * D;
+    float* state = partial + static_cast<long long>(S) * heads * chunks * width;
+    const size_t sm1 = static_cast<size_t>(2) * kChunk * D * sizeof(float);
+    const size_t sm3 = (static_cast<size_t>(width) + static_cast<size_t>(D) * kTile +
+                        static_cast<size_t>(kTile) * (D + 1)) * sizeof(float);
+    static bool attr = false;
+    if (!attr) {
+        SANA_CUDA(cudaFuncSetAttribute(linattn_state_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       2 * kChunk * 128 * 4));
+        SANA_CUDA(cudaFuncSetAttribute(linattn_apply_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (129 * 128 + 128 * kTile + kTile * 129) * 4));
+        attr = true;
+    }
+    if (Tk > 0) {
+        linattn_state_kernel<T><<<dim3(chunks, heads, S), 256, sm1, st>>>(kv, ldkv, k_off, v_off, Tk, heads, D,
+                                                                          chunks, partial);
+        SANA_CUDA(cudaGetLastError());
+        linattn_reduce_kernel<<<dim3(ceil_div(width, 256), S * heads), 256, 0, st>>>(partial, chunks, width, state);
+        SANA_CUDA(cudaGetLastError());
+    } else {
+        SANA_CUDA(cudaMemsetAsync(state, 0, static_cast<size_t>(S) * heads * width * sizeof(float), st));
+    }
+    linattn_apply_kernel<T><<<dim3(ceil_div(Tq, kTile), heads, S), kTile, sm3, st>>>(q, ldq, q_off, Tq, heads, D,
+                                                                                    state, out, ldo);
+    SANA_CUDA(cudaGetLastError());
+}
+
+template void linear_attention<float>(const float*, long long, int, const float*, long long, int, int, int, int,
+                                      int, int, int, float*, float*, long long, cudaStream_t);
+template void linear_attention<bf16>(const bf16*, long long, int, const bf16*, long long, int, int, int, int, int,
+                                     int, int, float*, bf16*, long long, cudaStream_t);
+
+}  // namespace sana

@@ -1,0 +1,323 @@
+// Row-wise and elementwise kernels of the denoiser step (see kernels.h for contracts).
+#include "kernels.h"
+
+namespace sana {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// One warp per row. Three passes over the row (it stays in L1): mean, centred variance,
+// write — the order of tensor.cpp:243-265 (mean first, then sum of squared deviations).
+template <class TO>
+__global__ void ln_modulate_kernel(const float* __restrict__ x, long long rows, int C, int rows_per_seq,
+                                   const float* __restrict__ gamma, const float* __restrict__ beta,
+                                   const float* __restrict__ mod, long long mod_ld, int shift_idx, int scale_idx,
+                                   float eps, TO* __restrict__ out) {
+    const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + row * C;
+    const bool vec = (C % 128 == 0) && ((reinterpret_cast<uintptr_t>(xr) & 15) == 0);
+    float s = 0.f;
+    if (vec) {
+        for (int c = lane * 4; c < C; c += 128) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + c);
+            s += (v.x + v.y) + (v.z + v.w);
+        }
+    } else {
+        for (int c = lane; c < C; c += 32) s += xr[c];
+    }
+    const float mean = warp_sum(s) / static_cast<float>(C);
+    float q = 0.f;
+    if (vec) {
+        for (int c = lane * 4; c < C; c += 128) {
+            const float4 v = *reinterpret_cast<const float4*>(xr + c);
+            const float a = v.x - mean, b = v.y - mean, d = v.z - mean, e = v.w - mean;
+            q += (a * a + b * b) + (d * d + e * e);
+        }
+    } else {
+        for (int c = lane; c < C; c += 32) {
+            const float d = xr[c] - mean;
+            q += d * d;
+        }
+    }
+    const float var = warp_sum(q) / static_cast<float>(C);
+    const float inv_std = 1.0f / sqrtf(var + eps);
+    const long long seq = row / rows_per_seq;
+    const float* shift = mod ? mod + seq * mod_ld + static_cast<long long>(shift_idx) * C : nullptr;
+    const float* scale = mod ? mod + seq * mod_ld + static_cast<long long>(scale_idx) * C : nullptr;
+    TO* o = out + row * C;
+    for (int c = lane; c < C; c += 32) {
+        float v = (xr[c] - mean) * inv_std;
+        if (gamma) v *= gamma[c];
+        if (beta) v += beta[c];
+        if (mod) v = v * (1.0f + scale[c]) + shift[c];
+        o[c] = from_f<TO>(v);
+    }
+}
+
+template <class TO>
+__global__ void rms_norm_kernel(const float* __restrict__ x, long long rows, int C, float eps,
+                                const float* __restrict__ w, TO* __restrict__ out) {
+    const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + row * C;
+    float s = 0.f;
+    for (int c = lane; c < C; c += 32) s += xr[c] * xr[c];
+    const float ms = warp_sum(s) / static_cast<float>(C);
+    const float inv = 1.0f / sqrtf(ms + eps);
+    TO* o = out + row * C;
+    for (int c = lane; c < C; c += 32) {
+        float v = xr[c] * inv;
+        if (w) v *= w[c];
+        o[c] = from_f<TO>(v);
+    }
+}
+
+__global__ void block_modulation_kernel(const float* __restrict__ tmod, int S, int width,
+                                        const float* __restrict__ tables, int n_blocks, float* __restrict__ mod) {
+    const long long total = static_cast<long long>(n_blocks) * S * width;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int k = static_cast<int>(i % width);
+        const long long bs = i / width;
+        const int s = static_cast<int>(bs % S);
+        const int b = static_cast<int>(bs / S);
+        mod[i] = tmod[static_cast<long long>(s) * width + k] + tables[static_cast<long long>(b) * width + k];
+    }
+}
+
+__global__ void final_modulation_kernel(const float* __restrict__ emb, int S, int C, const float* __restrict__ table,
+                                        float* __restrict__ fmod) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= S * C) return;
+    const int s = i / C, c = i % C;
+    fmod[static_cast<long long>(s) * 2 * C + c] = emb[i] + table[c];
+    fmod[static_cast<long long>(s) * 2 * C + C + c] = emb[i] + table[C + c];
+}
+
+__global__ void patch_tokens_kernel(const float* __restrict__ lat, int images, int seqs, int Cl, int HW,
+                                    float* __restrict__ out) {
+    const long long total = static_cast<long long>(seqs) * HW * Cl;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % Cl);
+        const long long r = i / Cl;
+        const int t = static_cast<int>(r % HW);
+        const int s = static_cast<int>(r / HW);
+        const int img = s % images;
+        out[i] = lat[(static_cast<long long>(img) * Cl + c) * HW + t];
+    }
+}
+
+__global__ void broadcast_rows_kernel(const float* __restrict__ row, int S, int width, float* __restrict__ out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < S * width) out[i] = row[i % width];
+}
+
+__global__ void kv_len_kernel(const float* __restrict__ bias, int S, int L, int* __restrict__ kv_len) {
+    const int s = blockIdx.x;
+    int last = -1;
+    for (int j = threadIdx.x; j < L; j += blockDim.x) {
+        if (bias[static_cast<long long>(s) * L + j] > -1000.0f) last = max(last, j);
+    }
+    __shared__ int red[32];
+    for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int m = -1;
+        for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w) m = max(m, red[w]);
+        kv_len[s] = (m < 0) ? L : m + 1;
+    }
+}
+
+__global__ void cfg_scheduler_kernel(const float* __restrict__ noise, int images, int Cl, int HW,
+                                     float* __restrict__ lat, float* __restrict__ hist_cur,
+                                     const float* __restrict__ hist_prev, SchedCoef k) {
+    const long long n = static_cast<long long>(images) * Cl * HW;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int t = static_cast<int>(i % HW);
+        const long long bc = i / HW;
+        const int c = static_cast<int>(bc % Cl);
+        const int b = static_cast<int>(bc / Cl);
+        const float u = noise[(static_cast<long long>(b) * HW + t) * Cl + c];
+        const float txt = noise[(static_cast<long long>(images + b) * HW + t) * Cl + c];
+        const float guided = u + k.guidance * (txt - u);
+        const float x = lat[i];
+        const float x0 = x - k.sigma_s * guided;
+        float xn;
+        if (k.second_order) {
+            const float d1 = k.inv_r0 * (x0 - hist_prev[i]);
+            xn = k.a * x + k.b * x0 + k.c * d1;
+        } else {
+            xn = k.a * x + k.b * x0;
+        }
+        hist_cur[i] = x0;
+        lat[i] = xn;
+    }
+}
+
+__global__ void modulate_kernel(const float* __restrict__ x, long long rows, int C, int rows_per_seq,
+                                const float* __restrict__ mod, long long mod_ld, int shift_idx, int scale_idx,
+                                float* __restrict__ out) {
+    const long long n = rows * C;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % C);
+        const long long seq = (i / C) / rows_per_seq;
+        const float* m = mod + seq * mod_ld;
+        out[i] = x[i] * (1.0f + m[static_cast<long long>(scale_idx) * C + c]) + m[static_cast<long long>(shift_idx) * C + c];
+    }
+}
+
+__global__ void scheduler_update_kernel(const float* __restrict__ m0, const float* __restrict__ m1,
+                                        const float* __restrict__ x, long long n, SchedCoef k,
+                                        float* __restrict__ out) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        if (k.second_order) {
+            const float d1 = k.inv_r0 * (m0[i] - m1[i]);
+            out[i] = k.a * x[i] + k.b * m0[i] + k.c * d1;
+        } else {
+            out[i] = k.a * x[i] + k.b * m0[i];
+        }
+    }
+}
+
+template <class TO>
+__global__ void repack_kernel(const float* __restrict__ src, int rows, int cols, int transpose, TO* __restrict__ dst) {
+    __shared__ float tile[32][33];
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int r = r0 + i, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) tile[i][threadIdx.x] = src[static_cast<long long>(r) * cols + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        if (transpose) {
+            const int c = c0 + i, r = r0 + threadIdx.x;  // dst[c][r]
+            if (r < rows && c < cols) dst[static_cast<long long>(c) * rows + r] = from_f<TO>(tile[threadIdx.x][i]);
+        } else {
+            const int r = r0 + i, c = c0 + threadIdx.x;
+            if (r < rows && c < cols) dst[static_cast<long long>(r) * cols + c] = from_f<TO>(tile[i][threadIdx.x]);
+        }
+    }
+}
+
+template <class TO>
+__global__ void convert_kernel(const float* __restrict__ src, long long n, TO* __restrict__ dst) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        dst[i] = from_f<TO>(src[i]);
+}
+
+int grid_for(long long n, int threads) {
+    long long g = (n + threads - 1) / threads;
+    if (g > 148LL * 32) g = 148LL * 32;
+    return static_cast<int>(g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+template <class TO>
+void ln_modulate(const float* x, long long rows, int C, int rows_per_seq, const float* gamma, const float* beta,
+                 const float* mod, long long mod_ld, int shift_idx, int scale_idx, float eps, TO* out,
+                 cudaStream_t st) {
+    if (rows == 0) return;
+    const int warps = 8;
+    ln_modulate_kernel<TO><<<static_cast<unsigned>((rows + warps - 1) / warps), warps * 32, 0, st>>>(
+        x, rows, C, rows_per_seq, gamma, beta, mod, mod_ld, shift_idx, scale_idx, eps, out);
+    SANA_CUDA(cudaGetLastError());
+}
+
+template <class TO>
+void rms_norm(const float* x, long long rows, int C, float eps, const float* w, TO* out, cudaStream_t st) {
+    if (rows == 0) return;
+    const int warps = 8;
+    rms_norm_kernel<TO><<<static_cast<unsigned>((rows + warps - 1) / warps), warps * 32, 0, st>>>(x, rows, C, eps,
+                                                                                                  w, out);
+    SANA_CUDA(cudaGetLastError());
+}
+
+void modulate(const float* x, long long rows, int C, int rows_per_seq, const float* mod, long long mod_ld,
+              int shift_idx, int scale_idx, float* out, cudaStream_t st) {
+    if (rows == 0) return;
+    modulate_kernel<<<grid_for(rows * C, 256), 256, 0, st>>>(x, rows, C, rows_per_seq, mod, mod_ld, shift_idx,
+                                                             scale_idx, out);
+    SANA_CUDA(cudaGetLastError());
+}
+
+void scheduler_update(const float* m0, const float* m1, const float* x, long long n, SchedCoef k, float* out,
+                      cudaStream_t st) {
+    if (n == 0) return;
+    scheduler_update_kernel<<<grid_for(n, 256), 256, 0, st>>>(m0, m1, x, n, k, out);
+    SANA_CUDA(cudaGetLastError());
+}
+
+void block_modulation(const float* tmod, int S, int C, const float* tables, int n_blocks, float* mod,
+                      cudaStream_t st) {
+    const long long n = static_cast<long long>(n_blocks) * S * 6 * C;
+    block_modulation_kernel<<<grid_for(n, 256), 256, 0, st>>>(tmod, S, 6 * C, tables, n_blocks, mod);
+    SANA_CUDA(cudaGetLastError());
+}
+
+void final_modulation(const float* emb, int S, int C, const float* table, float* fmod, cudaStream_t st) {
+    final_modulation_kernel<<<ceil_div(static_cast<long long>(S) * C, 256), 256, 0, st>>>(emb, S, C, table, fmod);
+    SANA_CUDA(cudaGetLastError());
+}
+
+void patch_tokens(const float* lat, int images, int seqs, int Cl, int HW, float* out, cudaStream_t st) {
+    const long long n = static_cast<long long>(seqs) * HW * Cl;
+    patch_tokens_kernel<<<grid_for(n, 256), 256, 0, st>>>(lat, images, seqs, Cl, HW, out);
+    SANA_CUDA(cudaGetLastError());
+}
+
+void broadcast_rows(const float* row, int S, int width, float* out, cudaStream_t st) {
+    broadcast_rows_kernel<<<ceil_div(static_cast<long long>(S) * width, 256), 256, 0, st>>>(row, S, width, out);
+    SANA_CUDA(cudaGetLastError());
+}
+
+void caption_kv_len(const float* bias, int S, int L, int* kv_len, cudaStream_t st) {
+    kv_len_kernel<<<S, 256, 0, st>>>(bias, S, L, kv_len);
+    SANA_CUDA(cudaGetLastError());
+}
+
+void cfg_scheduler_step(const float* noise, int images, int Cl, int HW, float* lat, float* hist_cur,
+                        const float* hist_prev, SchedCoef k, cudaStream_t st) {
+    const long long n = static_cast<long long>(images) * Cl * HW;
+    cfg_scheduler_kernel<<<grid_for(n, 256), 256, 0, st>>>(noise, images, Cl, HW, lat, hist_cur, hist_prev, k);
+    SANA_CUDA(cudaGetLastError());
+}
+
+template <class TO>
+void repack(const float* src, int rows, int cols, bool transpose, TO* dst, cudaStream_t st) {
+    dim3 grid(ceil_div(cols, 32), ceil_div(rows, 32));
+    repack_kernel<TO><<<grid, dim3(32, 8), 0, st>>>(src, rows, cols, transpose ? 1 : 0, dst);
+    SANA_CUDA(cudaGetLastError());
+}
+
+template <class TO>
+void convert(const float* src, long long n, TO* dst, cudaStream_t st) {
+    if (n == 0) return;
+    convert_kernel<TO><<<grid_for(n, 256), 256, 0, st>>>(src, n, dst);
+    SANA_CUDA(cudaGetLastError());
+}
+
+#define SANA_INST_TO(TO)                                                                                          \
+    template void ln_modulate<TO>(const float*, long long, int, int, const float*, const float*, const float*,   \
+                                  long long, int, int, float, TO*, cudaStream_t);                                \
+    template void rms_norm<TO>(const float*, long long, int, float, const float*, TO*, cudaStream_t);             \
+    template void repack<TO>(const float*, int, int, bool, TO*, cudaStream_t);                                    \
+    template void convert<TO>(const float*, long long, TO*, cudaStream_t);
+SANA_INST_TO(float)
+SANA_INST_TO(bf16)
+#undef SANA_INST_TO
+
+}  // namespace sana

@@ -1,0 +1,220 @@
+"""CUDA path, whole model pieces, through the C ABI.
+
+* small model (hidden 64, 2 blocks): caption projection, block stages, the no-CFG forward
+  and a 4-step CFG loop against the compiled reference's golden outputs;
+* full-size Sana-0.6B block 0 at config-0 shapes ([2, 1024, 1152], 36x32 and 16x72 self
+  heads) against the oracle: per-stage relative L2 <= 1e-2 in bf16 mode, <= 1e-4 in the
+  fp32 check mode;
+* the config-1 20-step image against the reference's golden latents (cosine >= 0.999), and
+  properties at config-3 size (4096 tokens).
+"""
+import concurrent.futures as cf
+import importlib.util
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+_spec = importlib.util.spec_from_file_location("make_golden", os.path.join(GOLDEN, "make_golden.py"))
+MG = importlib.util.module_from_spec(_spec)
+_spec.loader.exec_module(MG)
+syn = MG.syn
+
+BLOCK_BF16 = 1e-2  # per-block relative L2, bf16 mode
+BLOCK_F32 = 1e-4   # per-block relative L2, fp32 check mode
+
+
+def rel_err(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def cosine(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def product_model(d, base_seed=0, bias_std=0.0):
+    """The synthetic checkpoint drawn with the product's generator, tensors in parallel."""
+    from sana_b200 import randn_torch_cpu
+    specs = syn.model_tensor_specs(d)
+    with cf.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as ex:
+        return list(ex.map(lambda j: syn.generate_tensor(specs[j], j, d, randn_torch_cpu, base_seed, 0.02, bias_std),
+                           range(len(specs))))
+
+
+@pytest.fixture(scope="module", params=["f32", "bf16"])
+def small(request):
+    from sana_b200 import SANA_MODE_BF16, SANA_MODE_F32, SanaCuda, randn_torch_cpu
+    g = SanaCuda(0, SANA_MODE_F32 if request.param == "f32" else SANA_MODE_BF16)
+    tensors = syn.generate_model(MG.SMALL, randn_torch_cpu, base_seed=5, bias_std=0.02)
+    return request.param, g.model(tensors, *MG.SMALL.as_args())
+
+
+def test_small_model_matches_golden(small):
+    from sana_b200 import randn_torch_cpu
+    mode, m = small
+    gold = np.load(os.path.join(GOLDEN, "model_small.npz"))
+    got = MG.small_model_run(_WithTimeEmbed(m), randn_torch_cpu)
+    tol = {"f32": 1e-4, "bf16": 3e-2}[mode]
+    for k in ("ctx", "after_self", "after_cross", "after_ff", "noise_pred", "loop4"):
+        e = rel_err(got[k], gold[k])
+        assert e < tol, (mode, k, e)
+
+
+class _WithTimeEmbed:
+    """The small-model recipe asks for time_embed(); the GPU path has no standalone entry
+    for it (it runs inside the step), so use the golden values for that input only."""
+
+    def __init__(self, m):
+        self.m = m
+        self.gold = np.load(os.path.join(GOLDEN, "model_small.npz"))
+
+    def __getattr__(self, k):
+        return getattr(self.m, k)
+
+    def time_embed(self, tvals):
+        return self.gold["emb"], self.gold["tmod"]
+
+
+# --- full size --------------------------------------------------------------------------------
+@pytest.fixture(scope="module")
+def block0_inputs(oracle):
+    d1 = syn.ModelDims(n_blocks=1)
+    tensors = product_model(d1, base_seed=0)
+    m = oracle.model(tensors, *d1.as_args())
+    from sana_b200 import randn_torch_cpu
+    enc = syn.encoder_states(randn_torch_cpu, 2, 300, d1.caption_dim, 7)
+    bias = syn.attention_bias([8, 24], 300)
+    ctx = m.project_caption(enc)
+    emb, tmod = m.time_embed([999.0, 999.0])
+    x = syn._draw(randn_torch_cpu, 2 * 1024 * d1.hidden, 400).reshape(2, 1024, d1.hidden)
+    ref = m.block_forward(0, x, ctx, tmod, bias)
+    return d1, tensors, x, ctx, tmod, bias, ref
+
+
+def test_oracle_full_block_matches_reference_signature(block0_inputs):
+    path = os.path.join(GOLDEN, "block0_full.npz")
+    if not os.path.exists(path):
+        pytest.skip("block0_full.npz not generated")
+    g = np.load(path)
+    for name, a in zip(("after_self", "after_cross", "after_ff"), block0_inputs[-1]):
+        sig = MG._signature(a)
+        assert rel_err(sig["row_sq"], g[f"{name}_row_sq"]) < 1e-5
+
+
+@pytest.mark.parametrize("mode", ["bf16", "f32"])
+def test_full_block_parity(block0_inputs, mode):
+    from sana_b200 import SANA_MODE_BF16, SANA_MODE_F32, SanaCuda
+    d1, tensors, x, ctx, tmod, bias, ref = block0_inputs
+    g = SanaCuda(0, SANA_MODE_BF16 if mode == "bf16" else SANA_MODE_F32)
+    g.upload_checkpoint(d1.as_args(), tensors)
+    got = g.block_forward(0, x, ctx, tmod, bias)
+    tol = BLOCK_BF16 if mode == "bf16" else BLOCK_F32
+    for name, a, b in zip(("after_self", "after_cross", "after_ff"), got, ref):
+        # the residual stream dominates the stage outputs; also check the branch deltas
+        e = rel_err(a, b)
+        assert e < tol, (mode, name, e)
+    e_branch = rel_err(got[2] - x, ref[2] - x)
+    assert e_branch < (5 * tol if mode == "bf16" else 10 * tol), e_branch
+
+
+def test_full_block_baseline_heads(oracle):
+    """BASELINE.json's literal 16 x 72 self-attention heads (the reference's callers use 36 x 32)."""
+    from sana_b200 import SANA_MODE_BF16, SanaCuda, randn_torch_cpu
+    d1 = syn.ModelDims(n_blocks=1, self_heads=16)
+    tensors = product_model(d1, base_seed=1, bias_std=0.02)
+    m = oracle.model(tensors, *d1.as_args())
+    enc = syn.encoder_states(randn_torch_cpu, 2, 300, d1.caption_dim, 8)
+    bias = syn.attention_bias([24, 8], 300)
+    ctx = m.project_caption(enc)
+    _, tmod = m.time_embed([500.0, 500.0])
+    x = syn._draw(randn_torch_cpu, 2 * 1024 * d1.hidden, 401).reshape(2, 1024, d1.hidden)
+    ref = m.block_forward(0, x, ctx, tmod, bias)
+    g = SanaCuda(0, SANA_MODE_BF16)
+    g.upload_checkpoint(d1.as_args(), tensors)
+    got = g.block_forward(0, x, ctx, tmod, bias)
+    for a, b in zip(got, ref):
+        assert rel_err(a, b) < BLOCK_BF16
+
+
+@pytest.fixture(scope="module")
+def full_gpu():
+    from sana_b200 import SANA_MODE_BF16, SanaCuda
+    d = syn.ModelDims()
+    tensors = product_model(d, base_seed=0)
+    g = SanaCuda(0, SANA_MODE_BF16)
+    g.upload_checkpoint(d.as_args(), tensors)
+    del tensors
+    return g
+
+
+def test_loop20_matches_reference_golden(full_gpu):
+    path = os.path.join(GOLDEN, "loop20_full.npz")
+    if not os.path.exists(path):
+        pytest.skip("loop20_full.npz not generated")
+    from sana_b200 import randn_torch_cpu
+    gold = np.load(path)["latents"]
+    enc = syn.encoder_states(randn_torch_cpu, 2, 300, 2304, 7)
+    bias = syn.attention_bias([8, 24], 300)
+    lat = syn.latents(randn_torch_cpu, 1, 32, 32, 32, 42)
+    out = full_gpu.denoise_loop(lat, enc, bias, 4.5, 20)
+    assert np.isfinite(out).all()
+    c = cosine(out, gold)
+    assert c >= 0.999, c
+    # the captured-graph replay gives the same result as the first (eager) call
+    out2 = full_gpu.denoise_loop(lat, enc, bias, 4.5, 20)
+    assert np.array_equal(out, out2)
+
+
+def test_forward_config0_matches_reference_golden(full_gpu):
+    path = os.path.join(GOLDEN, "forward_full.npz")
+    if not os.path.exists(path):
+        pytest.skip("forward_full.npz not generated")
+    from sana_b200 import randn_torch_cpu
+    gold = np.load(path)["noise_pred"]
+    enc = syn.encoder_states(randn_torch_cpu, 2, 300, 2304, 7)
+    bias = syn.attention_bias([8, 24], 300)
+    lat = syn.latents(randn_torch_cpu, 2, 32, 32, 32, 42)
+    ctx = full_gpu.project_caption_model(enc)
+    out = full_gpu.forward(lat, 999.0, ctx, bias)
+    assert cosine(out, gold) >= 0.999
+    assert rel_err(out, gold) < 5e-2
+
+
+def test_batched_loop_images_are_independent(full_gpu):
+    """Config-2 style batch: each image of a batch gets the latents it would get alone."""
+    from sana_b200 import randn_torch_cpu
+    B, L = 3, 300
+    lens = syn.batch_valid_lengths(B, 11)
+    enc = syn.encoder_states(randn_torch_cpu, 2 * B, L, 2304, 21)
+    bias = syn.attention_bias(lens, L)
+    lat = syn.latents(randn_torch_cpu, B, 32, 32, 32, 22)
+    batch = full_gpu.denoise_loop(lat, enc, bias, 4.5, 4)
+    for i in range(B):
+        idx = [i, B + i]
+        one = full_gpu.denoise_loop(lat[i:i + 1], enc[idx], bias[idx], 4.5, 4)
+        assert cosine(batch[i], one[0]) > 0.9999
+
+
+def test_highres_step_is_finite_and_consistent(full_gpu):
+    """Config 3 (64 x 64 latent, 4096 tokens): one step through the loop API and through
+    the single-step API agree."""
+    from sana_b200 import randn_torch_cpu
+    enc = syn.encoder_states(randn_torch_cpu, 2, 300, 2304, 7)
+    bias = syn.attention_bias([8, 24], 300)
+    lat = syn.latents(randn_torch_cpu, 1, 32, 64, 64, 43)
+    one_step = full_gpu.denoise_loop(lat, enc, bias, 4.5, 1)
+    assert np.isfinite(one_step).all()
+    ctx = full_gpu.project_caption_model(enc)
+    from sana_b200 import scheduler_schedule
+    ts, sg = scheduler_schedule(1)
+    lat2, si, lo, hist = full_gpu.denoise_step(lat, ctx, bias, 4.5, float(ts[0]), sg, 0, 0, [])
+    assert si == 1 and lo == 1 and len(hist) == 1
+    assert cosine(lat2, one_step) > 0.9999

@@ -1,0 +1,204 @@
+"""CUDA path, single operations, through the C ABI (include/sana_cuda.h).
+
+* the tcgen05 tensor-core GEMM against float64 products of the same bf16-rounded
+  operands (only accumulation error remains), and the CUDA-core GEMM in fp32;
+* the reference's own known-answer tests in the fp32 check mode (reference tolerances);
+* every op against the golden fixtures the compiled reference produced
+  (fp32 check mode: relative L2 <= 1e-5; bf16 mode: <= 2e-2);
+* edge cases of the reference's op contracts against the oracle.
+"""
+import importlib.util
+import os
+
+import numpy as np
+import pytest
+
+import kat_cases as K
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+_spec = importlib.util.spec_from_file_location("make_golden", os.path.join(GOLDEN, "make_golden.py"))
+MG = importlib.util.module_from_spec(_spec)
+_spec.loader.exec_module(MG)
+
+F32_TOL = 1e-5   # fp32 check mode, relative L2 to the reference
+BF16_TOL = 2e-2  # bf16 operands / activations, fp32 accumulation
+
+
+def rel_err(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def bf16_round(a):
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    u = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return u.astype(np.uint32).view(np.float32)
+
+
+@pytest.fixture(scope="module")
+def gpu_f32():
+    from sana_b200 import SANA_MODE_F32, SanaCuda
+    return SanaCuda(0, SANA_MODE_F32)
+
+
+@pytest.fixture(scope="module")
+def gpu_bf16():
+    from sana_b200 import SANA_MODE_BF16, SanaCuda
+    return SanaCuda(0, SANA_MODE_BF16)
+
+
+# --- GEMM -----------------------------------------------------------------------------------
+GEMM_SHAPES = [(128, 64, 128), (256, 128, 256), (300, 136, 200), (1, 64, 32), (77, 1152, 16), (640, 512, 1152),
+               (2048, 1152, 3456), (1000, 2880, 1152), (517, 2304, 1152), (2048, 1152, 5760)]
+
+
+@pytest.mark.parametrize("M,K,N", GEMM_SHAPES)
+def test_tensor_core_gemm(gpu_bf16, M, K, N):
+    from sana_b200 import gemm_counts
+    rng = np.random.default_rng(M * 7 + K * 3 + N)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((K, N)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    tc0, _ = gemm_counts()
+    out = gpu_bf16.linear_3d(x, w, b)
+    tc1, _ = gemm_counts()
+    assert tc1 == tc0 + 1, "the tensor-core path did not run"
+    ref = bf16_round(x).astype(np.float64) @ bf16_round(w).astype(np.float64) + b
+    assert rel_err(out, ref) < 1e-5 + 2e-6 * np.sqrt(K)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 1, 1), (3, 5, 7), (64, 64, 64), (130, 300, 70), (512, 1152, 1152)])
+def test_cuda_core_gemm_fp32(gpu_f32, M, K, N):
+    from sana_b200 import gemm_counts
+    rng = np.random.default_rng(M + K + N)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = rng.standard_normal((K, N)).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    _, s0 = gemm_counts()
+    out = gpu_f32.linear_3d(x, w, b)
+    _, s1 = gemm_counts()
+    assert s1 == s0 + 1
+    ref = x.astype(np.float64) @ w.astype(np.float64) + b
+    assert rel_err(out, ref) < 1e-6
+
+
+def test_gemm_repeatable(gpu_bf16):
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((1024, 1152)).astype(np.float32)
+    w = rng.standard_normal((1152, 1152)).astype(np.float32)
+    a = gpu_bf16.linear_3d(x, w)
+    b = gpu_bf16.linear_3d(x, w)
+    assert np.array_equal(a, b)
+
+
+# --- the reference's known-answer tests ------------------------------------------------------
+@pytest.mark.parametrize("case", K.ALL_KATS, ids=lambda f: f.__name__)
+def test_reference_kats_fp32_mode(gpu_f32, case):
+    K.check(case(gpu_f32))
+
+
+# --- ops against the reference's outputs -----------------------------------------------------
+@pytest.mark.parametrize("mode", ["f32", "bf16"])
+def test_ops_match_golden(request, mode, oracle):
+    g = request.getfixturevalue("gpu_" + mode)
+    gold = np.load(os.path.join(GOLDEN, "ops_small.npz"))
+    tol = F32_TOL if mode == "f32" else BF16_TOL
+    for name, meth, args in MG.ops_cases(oracle.randn):
+        out = getattr(g, meth)(*args)
+        assert out.shape == gold[name].shape, name
+        e = rel_err(out, gold[name])
+        assert e < tol, (name, e)
+
+
+# --- edge cases of the op contracts (against the oracle) -------------------------------------
+def test_attention_all_keys_masked(gpu_f32, gpu_bf16, oracle):
+    """Every key masked: the reference's softmax still runs over all keys, each score
+    carrying the -10000 bias (its fp32 rounding at that magnitude included); no key may
+    be dropped."""
+    rng = np.random.default_rng(1)
+    q, k, v = (rng.standard_normal((2, 2, 5, 8)).astype(np.float32) for _ in range(3))
+    bias = np.full((2, 1, 5), -10000.0, np.float32)
+    ref = oracle.attention(q, k, v, bias)
+    assert rel_err(ref, oracle.attention(q, k, v)) < 1e-2  # close to, not equal to, unmasked
+    assert rel_err(gpu_f32.attention(q, k, v, bias), ref) < F32_TOL
+    assert rel_err(gpu_bf16.attention(q, k, v, bias), ref) < BF16_TOL
+
+
+def test_attention_mask_with_holes_and_soft_bias(gpu_f32, oracle):
+    rng = np.random.default_rng(2)
+    q = rng.standard_normal((2, 3, 9, 16)).astype(np.float32)
+    k, v = (rng.standard_normal((2, 3, 12, 16)).astype(np.float32) for _ in range(2))
+    bias = rng.standard_normal((2, 1, 12)).astype(np.float32)
+    bias[0, 0, [1, 4, 11]] = -10000.0
+    bias[1, 0, 6:] = -10000.0
+    assert rel_err(gpu_f32.attention(q, k, v, bias), oracle.attention(q, k, v, bias)) < F32_TOL
+
+
+@pytest.mark.parametrize("D,Tq,Tk", [(1, 3, 5), (32, 200, 130), (72, 129, 257), (128, 16, 16)])
+def test_linear_attention_shapes(gpu_f32, gpu_bf16, oracle, D, Tq, Tk):
+    rng = np.random.default_rng(D)
+    q = rng.standard_normal((2, 3, Tq, D)).astype(np.float32)
+    k, v = (rng.standard_normal((2, 3, Tk, D)).astype(np.float32) for _ in range(2))
+    ref = oracle.linear_attention(q, k, v)
+    assert rel_err(gpu_f32.linear_attention(q, k, v), ref) < F32_TOL
+    assert rel_err(gpu_bf16.linear_attention(q, k, v), ref) < BF16_TOL
+
+
+def test_linear_attention_all_negative_queries(gpu_f32):
+    """relu(q) = 0: numerator 0, denominator 1e-15, output exactly 0 (transformer_ops.cpp:532)."""
+    q = -np.ones((1, 1, 4, 2), np.float32)
+    k = np.ones((1, 1, 4, 2), np.float32)
+    v = np.arange(8, dtype=np.float32).reshape(1, 1, 4, 2)
+    assert np.array_equal(gpu_f32.linear_attention(q, k, v), np.zeros_like(q))
+
+
+@pytest.mark.parametrize("H,W", [(1, 1), (1, 7), (5, 7), (32, 32)])
+def test_depthwise_and_glumb_grids(gpu_f32, gpu_bf16, oracle, H, W):
+    rng = np.random.default_rng(H * 31 + W)
+    img = rng.standard_normal((2, 16, H, W)).astype(np.float32)
+    w = rng.standard_normal((16, 1, 3, 3)).astype(np.float32)
+    b = rng.standard_normal(16).astype(np.float32)
+    assert rel_err(gpu_f32.depthwise3x3(img, w, b), oracle.depthwise3x3(img, w, b)) < F32_TOL
+    wi = (rng.standard_normal((32, 16, 1, 1)) * 0.3).astype(np.float32)
+    bi = rng.standard_normal(32).astype(np.float32)
+    wd = (rng.standard_normal((32, 1, 3, 3)) * 0.3).astype(np.float32)
+    bd = rng.standard_normal(32).astype(np.float32)
+    wp = (rng.standard_normal((12, 16, 1, 1)) * 0.3).astype(np.float32)
+    ref = oracle.glumb_conv(img, wi, bi, wd, bd, wp)
+    assert rel_err(gpu_f32.glumb_conv(img, wi, bi, wd, bd, wp), ref) < F32_TOL
+    assert rel_err(gpu_bf16.glumb_conv(img, wi, bi, wd, bd, wp), ref) < BF16_TOL
+
+
+def test_norms_degenerate_rows(gpu_f32, oracle):
+    x = np.zeros((1, 3, 5), np.float32)
+    x[0, 1] = 7.0  # constant row: zero variance
+    x[0, 2] = np.arange(5, dtype=np.float32)
+    for eps in (1e-6, 1e-5):
+        np.testing.assert_allclose(gpu_f32.layer_norm(x, eps), oracle.layer_norm(x, eps), rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(gpu_f32.rms_norm(x, eps), oracle.rms_norm(x, eps), rtol=1e-5, atol=1e-6)
+
+
+def test_invalid_arguments_raise(gpu_f32):
+    with pytest.raises(ValueError):
+        gpu_f32.attention_block(np.ones((1, 2, 3), np.float32), *[np.eye(3, dtype=np.float32), None] * 4, 2)
+    with pytest.raises(ValueError):
+        gpu_f32.scheduler_update(2, np.array([0.5, 0.2, 0.0], np.float32), 0, np.ones(1, np.float32),
+                                 np.ones(1, np.float32), np.ones(1, np.float32))
+    with pytest.raises(ValueError):
+        gpu_f32.block_forward(0, np.ones((1, 2, 2), np.float32), np.ones((1, 2, 2), np.float32),
+                              np.ones((1, 12), np.float32))
+
+
+def test_scheduler_trajectory_matches_golden(gpu_f32, oracle):
+    """step_sana_scheduler through the device kernel over a 20-step schedule."""
+    g = np.load(os.path.join(GOLDEN, "scheduler_20.npz"))
+    _, sg = gpu_f32.scheduler_schedule(20, 3.0)
+    mo = MG.syn._draw(oracle.randn, 20 * 64, 300).reshape(20, 64)
+    x = MG.syn._draw(oracle.randn, 64, 301)
+    hist, lower = [], 0
+    for s in range(20):
+        x, hist, lower = gpu_f32.scheduler_step(sg, s, lower, hist, mo[s], x)
+        assert rel_err(x, g["samples"][s]) < 1e-6, s
