@@ -1,0 +1,400 @@
+"""Throughput benchmark of the B200 Sana-0.6B denoiser (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU, NCCL)
+
+Workload (per GPU): 16 images x CFG (32 sequences of 1024 tokens),
+20-step DPM-Solver++ loop with guidance 4.5, caption states [300, 2304] with valid lengths
+drawn from 8..120; seeded random-init weights of the real architecture (synthetic: there
+are no checkpoints or datasets here). Each rank denoises its own 16 images, weights
+replicated; the final latents of all ranks are NCCL-gathered each step (the path's only
+collective), so per-GPU work is fixed as N grows ("weak" scaling).
+
+One bench step = one full denoising loop over the rank's batch (caption projection,
+cross-K/V for all blocks, 20 denoiser steps, CFG + scheduler), replayed from a CUDA graph.
+`value` is images/s over all ranks with inputs resident in HBM, timed with CUDA events on
+the launching stream (L2 flushed between iterations, untimed), max over ranks; `e2e` is the
+same through the reference-facing C ABI call with pinned host buffers (host<->device
+copies inside the timed region). Rank 0 prints one JSON line.
+
+--impl reference times the reference's own CPU implementation (oracle/_ref, compiled from
+the reference's sources; the CPU oracle when that build is absent) on this host's cores:
+one block_forward of one sequence per thread, extrapolated to images/s.
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "sana.cpp_b200")]
+
+METRIC = "denoiser steps/sec & images/sec (Sana-0.6B 1024px, 20 steps, CFG) at 1/2/4/8 B200"
+NUM_STEPS = 20
+GUIDANCE = 4.5
+CAPTION_LEN = 300
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ------------------------------------------------------------------------------------------
+# Synthetic workload
+# ------------------------------------------------------------------------------------------
+def make_weights(dims, seed=0):
+    from sana_b200 import randn_torch_cpu
+    from sana_b200 import synthetic as syn
+    specs = syn.model_tensor_specs(dims)
+    workers = min(32, len(os.sched_getaffinity(0)))
+    with cf.ThreadPoolExecutor(max_workers=workers) as ex:
+        return list(ex.map(lambda j: syn.generate_tensor(specs[j], j, dims, randn_torch_cpu, seed), range(len(specs))))
+
+
+def make_inputs(images, rank):
+    from sana_b200 import randn_torch_cpu
+    from sana_b200 import synthetic as syn
+    lens = syn.batch_valid_lengths(images, 1000 + rank)
+    lat = syn.latents(randn_torch_cpu, images, 32, 32, 32, 42 + 97 * rank)
+    enc = syn.encoder_states(randn_torch_cpu, 2 * images, CAPTION_LEN, 2304, 7 + 97 * rank)
+    bias = syn.attention_bias(lens, CAPTION_LEN)
+    return lat, enc, bias, lens
+
+
+def loop_flops(images, lens, C=1152, E=5760, T=1024, n_blocks=28, Hs=36, steps=NUM_STEPS, Din=2304, Cl=32):
+    """Algorithmic FLOPs of one denoising loop (multiply-add = 2): per step and sequence the
+    block GEMMs, linear attention, cross-attention at each sequence's valid key count and the
+    depthwise conv; once per loop the caption projection and cross-K/V (hoisted)."""
+    D = C // Hs
+    S = 2 * images
+    gemm_block = 2 * T * C * (3 * C + C + C + C + E) + 2 * T * (E // 2) * C
+    lin = 2 * T * D * D * 2 * Hs + 2 * T * D * Hs
+    dw = 2 * 9 * T * E
+    xattn = sum(4 * T * L * C for L in lens)  # q k^T and p v over the valid keys of each sequence
+    per_step = S * n_blocks * (gemm_block + lin + dw) + n_blocks * xattn + S * (2 * T * Cl * C * 2)
+    once = S * CAPTION_LEN * (2 * Din * C + 2 * C * C) + n_blocks * S * CAPTION_LEN * 2 * C * 2 * C
+    gemm_only = steps * S * n_blocks * gemm_block
+    return steps * per_step + once, gemm_only
+
+
+# ------------------------------------------------------------------------------------------
+# Clock sampling during the timed region
+# ------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = str(gpu_index)
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.p:
+            self.p.terminate()
+            self.p.wait(timeout=10)
+
+    def summary(self):
+        self.f.flush()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines()]
+        rows = [[c.strip() for c in r] for r in rows if len(r) >= 9 and r[0].strip() == self.gpu]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+
+
+# ------------------------------------------------------------------------------------------
+# CPU baseline (the reference's own code) — a bounded sample on this host's cores
+# ------------------------------------------------------------------------------------------
+def cpu_sample(threads=None):
+    """One reference block_forward of one 1024-token sequence per thread, all threads at
+    once; returns (images_per_s, seconds, threads, kind)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Oracle, Reference
+    from sana_b200 import randn_torch_cpu
+    from sana_b200 import synthetic as syn
+    impl, kind = (Reference(), "reference") if Reference.available() else (Oracle(), "port")
+    d1 = syn.ModelDims(n_blocks=1)
+    tensors = make_weights(d1)
+    model = impl.model(tensors, *d1.as_args())
+    del tensors
+    threads = threads or min(64, len(os.sched_getaffinity(0)))
+    if kind == "port":
+        threads = 1  # the oracle parallelises internally
+    enc = syn.encoder_states(randn_torch_cpu, 1, CAPTION_LEN, 2304, 7)
+    ctx = model.project_caption(enc)
+    _, tmod = model.time_embed([999.0])
+    bias = syn.attention_bias([24], CAPTION_LEN)
+    xs = [syn._draw(randn_torch_cpu, 1024 * 1152, 500 + i).reshape(1, 1024, 1152) for i in range(threads)]
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(lambda x: model.block_forward(0, x, ctx, tmod, bias), xs))
+    dt = time.perf_counter() - t0
+    seq_blocks_per_s = threads / dt
+    images_per_s = seq_blocks_per_s / (2 * 28 * NUM_STEPS)
+    return images_per_s, dt, threads, kind
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    W, K = args.warmup, args.steps
+    vals, secs = [], []
+    kind, threads = "reference", 0
+    for i in range(W + K):
+        v, dt, threads, kind = cpu_sample()
+        if i >= W:
+            vals.append(v)
+            secs.append(dt)
+    value = statistics.mean(vals)
+    sample = (f"one reference block_forward of one 1024-token sequence per thread ({threads} threads at once), "
+              f"extrapolated x2 sequences x28 blocks x{NUM_STEPS} steps per image")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
+        "steps": K, "warmup": W, "ms_per_step": 1000 * statistics.mean(secs), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(args),
+        "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def config_dict(args):
+    return {"workload": f"config2: {args.images} images x CFG per GPU (2x{args.images} sequences x 1024 tokens), "
+                        f"{NUM_STEPS}-step DPM-Solver++ loop, guidance {GUIDANCE}",
+            "images_per_gpu": args.images, "global_batch": args.images * args.gpus, "seq_len": 1024,
+            "caption_tokens": CAPTION_LEN, "caption_valid_lengths": "uniform 8..120 (seeded)",
+            "self_attention": "36 heads x 32 (linear)", "cross_attention": "16 heads x 72 (softmax)",
+            "parallelism": f"images sharded over {args.gpus} GPU(s), weights replicated, final latents gathered",
+            "l2": "flushed between timed iterations (256 MiB write, untimed)"}
+
+
+# ------------------------------------------------------------------------------------------
+# GPU arm
+# ------------------------------------------------------------------------------------------
+def gemm_roofline(g, torch, stream, M, peak_tflops):
+    """The dominant kernel (tcgen05 GEMM) alone at the step's shapes: algorithmic FLOPs per
+    launch / CUDA-event launch time, FLOP-weighted over the block's six projections."""
+    shapes = [(M, 3456, 1152), (M, 1152, 1152), (M, 1152, 1152), (M, 1152, 1152), (M, 5760, 1152), (M, 1152, 2880)]
+    tot_f, tot_ms, per = 0.0, 0.0, []
+    dev = torch.device("cuda")
+    for (m, n, k) in shapes:
+        A = torch.randn(m, k, device=dev, dtype=torch.bfloat16)
+        B = torch.randn(n, k, device=dev, dtype=torch.bfloat16) * 0.02
+        C = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        for _ in range(3):
+            g.gemm_device(A.data_ptr(), B.data_ptr(), m, n, k, C.data_ptr())
+        reps = 10
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            g.gemm_device(A.data_ptr(), B.data_ptr(), m, n, k, C.data_ptr())
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        f = 2.0 * m * n * k
+        per.append({"shape": [m, n, k], "ms": round(ms, 4), "tflops": round(f / ms / 1e9, 1)})
+        tot_f += f
+        tot_ms += ms
+        del A, B, C
+    achieved = tot_f / tot_ms / 1e9
+    return achieved, per
+
+
+def run_cuda(args):
+    import torch
+    import torch.distributed as dist
+    from sana_b200 import SANA_MODE_BF16, SanaCuda
+    from sana_b200 import synthetic as syn
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    dims = syn.ModelDims()
+    t0 = time.time()
+    tensors = make_weights(dims)
+    g = SanaCuda(local, SANA_MODE_BF16)
+    g.upload_checkpoint(dims.as_args(), tensors)
+    del tensors
+    log(f"[rank {rank}] weights ready in {time.time() - t0:.1f}s")
+
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    g.set_stream(stream.cuda_stream)
+    B = args.images
+    lat, enc, bias, lens = make_inputs(B, rank)
+    d_lat = torch.from_numpy(lat).cuda()
+    d_enc = torch.from_numpy(enc).cuda()
+    d_bias = torch.from_numpy(bias).cuda()
+    d_out = torch.empty_like(d_lat)
+    gathered = [torch.empty_like(d_lat) for _ in range(world)] if world > 1 else None
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+
+    def step():
+        g.denoise_loop_device(d_lat.data_ptr(), B, 32, 32, d_enc.data_ptr(), CAPTION_LEN, 2304,
+                              d_bias.data_ptr(), d_out.data_ptr(), GUIDANCE, NUM_STEPS)
+        if world > 1:
+            dist.all_gather(gathered, d_out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    # ---- timed: K steps, CUDA events on the launching stream, L2 flushed between ----
+    gpu_index = os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local] if os.environ.get(
+        "CUDA_VISIBLE_DEVICES") else str(local)
+    events = []
+    with ClockSampler(gpu_index) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        wall0 = time.perf_counter()
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+            events.append((e0, e1))
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        wall = time.perf_counter() - wall0
+    ms = sum(a.elapsed_time(b) for a, b in events)
+    launches = g.last_launch_count()
+    if world > 1:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    images_per_s = world * B / (ms_per_step / 1000.0)
+    flops, gemm_flops = loop_flops(B, lens)
+    pk, pk_kind = peaks()
+
+    # ---- e2e: the reference-facing C ABI call with pinned host buffers ----
+    h_lat = torch.from_numpy(lat).pin_memory()
+    h_enc = torch.from_numpy(enc).pin_memory()
+    h_bias = torch.from_numpy(bias).pin_memory()
+    h_out = torch.empty_like(h_lat).pin_memory()
+
+    def e2e_step():
+        g.denoise_loop_ptrs(h_lat.data_ptr(), B, 32, 32, h_enc.data_ptr(), CAPTION_LEN, 2304, h_bias.data_ptr(),
+                            h_out.data_ptr(), GUIDANCE, NUM_STEPS)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t1 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    h2d = h_lat.numel() * 4 + h_enc.numel() * 4 + h_bias.numel() * 4
+    d2h = h_out.numel() * 4
+
+    # ---- roofline of the dominant kernel, measured live ----
+    achieved, per_shape = gemm_roofline(g, torch, stream, 2 * B * 1024, pk["bf16_tflops"])
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, dt, threads, kind = cpu_sample()
+        cpu = {"value": v, "unit": "images/s", "cores": threads, "kind": kind,
+               "sample": f"one reference block_forward of one 1024-token sequence per thread ({threads} threads, "
+                         f"{dt:.1f} s), extrapolated x2 sequences x28 blocks x{NUM_STEPS} steps per image"}
+
+    if rank == 0:
+        clocks = clk.summary()
+        out = {
+            "metric": METRIC, "value": images_per_s, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded random-init Sana-0.6B weights, N(0,1) latents and caption states",
+            "config": config_dict(args),
+            "denoiser_steps_per_s": images_per_s * NUM_STEPS,
+            "wall_s_timed_region": wall,
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel<128> (tcgen05.mma kind::f16, TMA, TMEM)",
+                         "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": achieved / pk["bf16_tflops"], "peak_source": f"{pk_kind} bf16_tflops (burst)",
+                         "traffic": None, "per_shape": per_shape},
+            "model_flops": {"per_loop_tflop": flops / 1e12, "achieved_tflops": flops / (ms_per_step / 1e3) / 1e12,
+                            "frac_of_sustained_peak": flops / (ms_per_step / 1e3) / 1e12 / pk["bf16_tflops_sustained"],
+                            "gemm_share_of_flops": gemm_flops / flops},
+            "cpu_baseline": cpu,
+            "e2e": {"value": world * B / e2e_s, "unit": "images/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--images", type=int, default=16, help="images (x2 CFG sequences) per GPU")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_cuda(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -195,6 +195,26 @@ int sana_op_cross_attention_block(sana_cuda_ctx *ctx, const float *x, int B, int
 /* apply_classifier_free_guidance (transformer.cpp:570-602): noise [2B, Cl, H, W] -> [B, Cl, H, W]. */
 int sana_op_cfg(sana_cuda_ctx *ctx, const float *noise, int B, int Cl, int H, int W, float guidance, float *out);
 
+/* --- device-pointer kernels (microbenchmarks; bf16 activations, token-major, asynchronous
+ *     on the handle's stream) ------------------------------------------------------------ */
+
+/* out[M, N] (bf16) = act(A[M, K] . B[N, K]^T + bias): the dense projections of
+ * linear_3d_lastdim / conv2d_1x1 (common_ops.cpp:177, :322). act: 0 none, 1 SiLU, 2 GELU-tanh. */
+int sana_op_gemm_device(sana_cuda_ctx *ctx, const void *A, const void *B, int M, int N, int K, const float *bias,
+                        int act, void *out);
+/* linear_attention_4d on the fused QKV rows [S*T, 3*heads*D] -> [S*T, heads*D]; partial is
+ * fp32 scratch of sana_op_linear_attention_workspace() bytes. */
+int sana_op_linear_attention_device(sana_cuda_ctx *ctx, const void *qkv, int S, int T, int heads, int D,
+                                    float *partial, void *out);
+size_t sana_op_linear_attention_workspace(int S, int T, int heads, int D);
+/* depthwise_conv2d_3x3 + GLU gate on NHWC rows [S*H*W, E] -> [S*H*W, E/2]; w [E, 9], b [E] fp32. */
+int sana_op_depthwise_glu_device(sana_cuda_ctx *ctx, const void *in, int S, int H, int W, int E, const float *w,
+                                 const float *b, void *out);
+/* attention_4d for cross-attention: q [S*T, heads*D], kv [S*L, 2*heads*D] (k | v), bias
+ * [S, L] fp32 or NULL, kv_len int[S] scratch (filled from bias), out [S*T, heads*D]. */
+int sana_op_cross_attention_device(sana_cuda_ctx *ctx, const void *q, const void *kv, const float *bias,
+                                   int *kv_len, int S, int T, int L, int heads, int D, void *out);
+
 /* --- scheduler (scheduler.h:34-65) ----------------------------------------------------- */
 
 /* build_sana_scheduler_timesteps (scheduler.cpp:89-141), default config with flow_shift;

@@ -710,6 +710,67 @@ int sana_op_cfg(sana_cuda_ctx* ctx, const float* noise, int B, int Cl, int H, in
     });
 }
 
+
+// --- device-pointer kernels (microbenchmarks) ---------------------------------------------
+
+int sana_op_gemm_device(sana_cuda_ctx* ctx, const void* A, const void* B, int M, int N, int K, const float* bias,
+                        int act, void* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(A && B && out && M >= 1 && N >= 1 && K >= 1, "invalid gemm arguments");
+        sana::Engine& eng = engine(ctx);
+        sana::GemmProblem p;
+        p.A = A;
+        p.lda = K;
+        p.B = B;
+        p.ldb = K;
+        p.M = M;
+        p.N = N;
+        p.K = K;
+        p.ep = epi(out, true, N, bias, act);
+        sana::gemm(p, eng.err(), eng.stream(), eng.num_sms());
+    });
+}
+
+int sana_op_linear_attention_device(sana_cuda_ctx* ctx, const void* qkv, int S, int T, int heads, int D,
+                                    float* partial, void* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(qkv && partial && out && S >= 1 && T >= 1 && heads >= 1 && D >= 1, "invalid arguments");
+        sana::Engine& eng = engine(ctx);
+        const int C = heads * D;
+        const bf16* q = static_cast<const bf16*>(qkv);
+        sana::linear_attention<bf16>(q, 3LL * C, 0, q, 3LL * C, C, 2 * C, S, T, T, heads, D, partial,
+                                     static_cast<bf16*>(out), C, eng.stream());
+    });
+}
+
+size_t sana_op_linear_attention_workspace(int S, int T, int heads, int D) {
+    return static_cast<size_t>(S) * heads * (sana::linattn_chunks(T) + 1) * (D + 1) * D * sizeof(float);
+}
+
+int sana_op_depthwise_glu_device(sana_cuda_ctx* ctx, const void* in, int S, int H, int W, int E, const float* w,
+                                 const float* b, void* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(in && w && b && out && S >= 1 && H >= 1 && W >= 1 && E >= 2, "invalid arguments");
+        sana::Engine& eng = engine(ctx);
+        sana::depthwise_glu<bf16>(static_cast<const bf16*>(in), E, S, H, W, E, w, b, static_cast<bf16*>(out), E / 2,
+                                  eng.stream());
+    });
+}
+
+int sana_op_cross_attention_device(sana_cuda_ctx* ctx, const void* q, const void* kv, const float* bias,
+                                   int* kv_len, int S, int T, int L, int heads, int D, void* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(q && kv && out && S >= 1 && T >= 1 && L >= 1 && heads >= 1 && D >= 1, "invalid arguments");
+        sana::Engine& eng = engine(ctx);
+        const int C = heads * D;
+        if (bias && kv_len) sana::caption_kv_len(bias, S, L, kv_len, eng.stream());
+        const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)));
+        sana::cross_attention<bf16>(static_cast<const bf16*>(q), C, static_cast<const bf16*>(kv), 2LL * C, 0, C, bias,
+                                    bias ? kv_len : nullptr, S, T, L, heads, D, scale, static_cast<bf16*>(out), C,
+                                    eng.stream());
+    });
+}
+
 // --- scheduler -------------------------------------------------------------------------------
 
 int sana_scheduler_schedule(int n, float flow_shift, float* timesteps, float* sigmas) {

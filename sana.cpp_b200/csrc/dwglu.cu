@@ -23,21 +23,45 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
     }
 }
 
-// bf16, 8 channels per thread (half % 8 == 0, 16-byte aligned rows).
-__global__ void __launch_bounds__(256) dwglu_vec8_kernel(const bf16* __restrict__ in, long long ldi, int S, int H,
-                                                         int W, int half, const float* __restrict__ w,
-                                                         const float* __restrict__ b, bf16* __restrict__ out,
-                                                         long long ldo) {
+// bf16, 8 channels per thread (half % 8 == 0, 16-byte aligned rows). A block owns a tile
+// of kGroups x 8 channels of both halves; their 3x3 taps and biases are staged once in
+// shared memory, tap-major, so every weight read is a conflict-free 16-byte load. Lane i of
+// a warp handles channel group i of one pixel: input loads and output stores are 512-byte
+// contiguous runs. Threads stride over pixels.
+constexpr int kGroups = 32;  // channel groups (of 8) per block
+constexpr int kPixLanes = 8; // pixels in flight per block (blockDim = kGroups * kPixLanes)
+
+__global__ void __launch_bounds__(kGroups * kPixLanes) dwglu_vec8_kernel(const bf16* __restrict__ in, long long ldi,
+                                                                         int S, int H, int W, int half,
+                                                                         const float* __restrict__ w,
+                                                                         const float* __restrict__ b,
+                                                                         bf16* __restrict__ out, long long ldo) {
+    __shared__ __align__(16) float ws[2][9][kGroups * 8];  // [half][tap][channel in tile]
+    __shared__ __align__(16) float bs[2][kGroups * 8];
     const int groups = half / 8;
-    const long long total = static_cast<long long>(S) * H * W * groups;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int g = static_cast<int>(i % groups);
-        const long long pix = i / groups;
+    const int g0 = blockIdx.y * kGroups;
+    const int ng = min(kGroups, groups - g0);
+    for (int i = threadIdx.x; i < 2 * 9 * kGroups * 8; i += blockDim.x) {
+        const int hf = i / (9 * kGroups * 8);
+        const int rem = i % (9 * kGroups * 8);
+        const int c = rem / 9, tap = rem % 9;  // coalesced read of w[(ch)*9 + tap]
+        const int ch = g0 * 8 + c;
+        ws[hf][tap][c] = (c < ng * 8) ? w[(static_cast<long long>(hf) * half + ch) * 9 + tap] : 0.f;
+    }
+    for (int i = threadIdx.x; i < 2 * kGroups * 8; i += blockDim.x) {
+        const int hf = i / (kGroups * 8), c = i % (kGroups * 8);
+        bs[hf][c] = (c < ng * 8) ? b[static_cast<long long>(hf) * half + g0 * 8 + c] : 0.f;
+    }
+    __syncthreads();
+    const int gl = threadIdx.x % kGroups;
+    if (gl >= ng) return;
+    const int c0 = (g0 + gl) * 8;
+    const long long pixels = static_cast<long long>(S) * H * W;
+    for (long long pix = blockIdx.x * static_cast<long long>(kPixLanes) + threadIdx.x / kGroups; pix < pixels;
+         pix += static_cast<long long>(gridDim.x) * kPixLanes) {
         const int x = static_cast<int>(pix % W);
         const int y = static_cast<int>((pix / W) % H);
-        const long long s = pix / (static_cast<long long>(W) * H);
-        const int c0 = g * 8;
+        const long long sH = pix / (static_cast<long long>(W) * H) * H;
         float dv[8], gv[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -52,15 +76,21 @@ __global__ void __launch_bounds__(256) dwglu_vec8_kernel(const bf16* __restrict_
             for (int kx = 0; kx < 3; ++kx) {
                 const int ix = x + kx - 1;
                 if (ix < 0 || ix >= W) continue;
-                const bf16* src = in + ((s * H + iy) * W + ix) * ldi;
+                const bf16* src = in + ((sH + iy) * W + ix) * ldi;
                 float fd[8], fg[8];
                 unpack8(*reinterpret_cast<const uint4*>(src + c0), fd);
                 unpack8(*reinterpret_cast<const uint4*>(src + half + c0), fg);
                 const int tap = ky * 3 + kx;
+                const float4 wd0 = *reinterpret_cast<const float4*>(&ws[0][tap][gl * 8]);
+                const float4 wd1 = *reinterpret_cast<const float4*>(&ws[0][tap][gl * 8 + 4]);
+                const float4 wg0 = *reinterpret_cast<const float4*>(&ws[1][tap][gl * 8]);
+                const float4 wg1 = *reinterpret_cast<const float4*>(&ws[1][tap][gl * 8 + 4]);
+                const float wdv[8] = {wd0.x, wd0.y, wd0.z, wd0.w, wd1.x, wd1.y, wd1.z, wd1.w};
+                const float wgv[8] = {wg0.x, wg0.y, wg0.z, wg0.w, wg1.x, wg1.y, wg1.z, wg1.w};
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    dv[j] = fmaf(fd[j], w[(c0 + j) * 9 + tap], dv[j]);
-                    gv[j] = fmaf(fg[j], w[(half + c0 + j) * 9 + tap], gv[j]);
+                    dv[j] = fmaf(fd[j], wdv[j], dv[j]);
+                    gv[j] = fmaf(fg[j], wgv[j], gv[j]);
                 }
             }
         }
@@ -68,8 +98,8 @@ __global__ void __launch_bounds__(256) dwglu_vec8_kernel(const bf16* __restrict_
         uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
         for (int j = 0; j < 8; j += 2) {
-            const float o0 = (dv[j] + b[c0 + j]) * silu(gv[j] + b[half + c0 + j]);
-            const float o1 = (dv[j + 1] + b[c0 + j + 1]) * silu(gv[j + 1] + b[half + c0 + j + 1]);
+            const float o0 = (dv[j] + bs[0][gl * 8 + j]) * silu(gv[j] + bs[1][gl * 8 + j]);
+            const float o1 = (dv[j + 1] + bs[0][gl * 8 + j + 1]) * silu(gv[j + 1] + bs[1][gl * 8 + j + 1]);
             __nv_bfloat162 h2 = __floats2bfloat162_rn(o0, o1);
             pw[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
         }
@@ -152,7 +182,11 @@ void depthwise_glu(const T* in, long long ldi, int S, int H, int W, int E, const
     bool vec = sizeof(T) == 2 && half % 8 == 0 && ldi % 8 == 0 && ldo % 8 == 0 &&
                (reinterpret_cast<uintptr_t>(in) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
     if (vec) {
-        dwglu_vec8_kernel<<<grid_for(pixels * (half / 8)), 256, 0, st>>>(
+        const int tiles = ceil_div(half / 8, kGroups);
+        long long px_blocks = (pixels + kPixLanes - 1) / kPixLanes;
+        const long long cap = (148LL * 8 + tiles - 1) / tiles * 4;  // ~32 resident blocks per SM in total
+        if (px_blocks > cap) px_blocks = cap;
+        dwglu_vec8_kernel<<<dim3(static_cast<unsigned>(px_blocks), tiles), kGroups * kPixLanes, 0, st>>>(
             reinterpret_cast<const bf16*>(in), ldi, S, H, W, half, w, b, reinterpret_cast<bf16*>(out), ldo);
     } else {
         dwglu_scalar_kernel<T><<<grid_for(pixels * half), 256, 0, st>>>(in, ldi, S, H, W, half, w, b, out, ldo);

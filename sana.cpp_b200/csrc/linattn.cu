@@ -98,6 +98,149 @@ __global__ void __launch_bounds__(kTile) linattn_apply_kernel(const T* __restric
     }
 }
 
+
+// Register-blocked state (head_dim a multiple of 4): each thread accumulates a 4 x 4 tile of
+// S = relu(K)^T V (two 16-byte shared loads per 16 FMAs); when the (D/4)^2 tiles do not
+// fill the block, tokens are split across thread groups and the group sums added in a
+// fixed order.
+template <class T>
+__global__ void __launch_bounds__(256) linattn_state4_kernel(const T* __restrict__ kv, long long ld, int k_off,
+                                                             int v_off, int Tk, int heads, int D, int chunks,
+                                                             float* __restrict__ partial) {
+    extern __shared__ __align__(16) float sm4[];
+    float* Ks = sm4;               // [kChunk][D]
+    float* Vs = Ks + kChunk * D;   // [kChunk][D]
+    float* red = Vs + kChunk * D;  // [splits][(D + 1) * D]
+    const int s = blockIdx.z, h = blockIdx.y, c = blockIdx.x;
+    const int t0 = c * kChunk;
+    const int n = min(Tk - t0, kChunk);
+    for (int i = threadIdx.x; i < n * D; i += blockDim.x) {
+        const int t = i / D, d = i % D;
+        const long long row = static_cast<long long>(s) * Tk + t0 + t;
+        const float kval = to_f(kv[row * ld + k_off + h * D + d]);
+        Ks[i] = kval > 0.f ? kval : 0.f;
+        Vs[i] = to_f(kv[row * ld + v_off + h * D + d]);
+    }
+    __syncthreads();
+    const int nb = D / 4, nblk = nb * nb;
+    int splits = 1;
+    while (splits * 2 * nblk <= static_cast<int>(blockDim.x) && splits < 8) splits *= 2;
+    const int per = blockDim.x / splits;
+    const int split = threadIdx.x / per;
+    const int ta = (n * split) / splits, tb = (n * (split + 1)) / splits;
+    const int width = (D + 1) * D;
+    for (int blk = threadIdx.x % per; blk < nblk && split < splits; blk += per) {
+        const int r0 = (blk / nb) * 4, d0 = (blk % nb) * 4;
+        float acc[4][4] = {};
+        float z[4] = {};
+        for (int t = ta; t < tb; ++t) {
+            const float4 v = *reinterpret_cast<const float4*>(Vs + t * D + r0);
+            const float4 k = *reinterpret_cast<const float4*>(Ks + t * D + d0);
+            const float vv[4] = {v.x, v.y, v.z, v.w};
+            const float kk[4] = {k.x, k.y, k.z, k.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(vv[i], kk[j], acc[i][j]);
+            if (r0 == 0) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) z[j] += kk[j];
+            }
+        }
+        float* rd = red + split * width;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) rd[(r0 + i) * D + d0 + j] = acc[i][j];
+        if (r0 == 0) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) rd[D * D + d0 + j] = z[j];
+        }
+    }
+    __syncthreads();
+    float* out = partial + ((static_cast<long long>(s) * heads + h) * chunks + c) * width;
+    for (int e = threadIdx.x; e < width; e += blockDim.x) {
+        float a = 0.f;
+        for (int sp = 0; sp < splits; ++sp) a += red[sp * width + e];
+        out[e] = a;
+    }
+}
+
+// Apply with relu(q) in registers (compile-time head dim): one thread per token, the state
+// rows read as 16-byte broadcasts from shared memory.
+template <class T, int D>
+__global__ void __launch_bounds__(kTile) linattn_apply_reg_kernel(const T* __restrict__ q, long long ld, int q_off,
+                                                                  int Tq, int heads, const float* __restrict__ state,
+                                                                  T* __restrict__ out, long long ldo) {
+    extern __shared__ __align__(16) float sm5[];
+    float* Ss = sm5;                    // [(D+1) * D]
+    float* qs = Ss + (D + 1) * D;       // [D][kTile]; reused as the output tile [kTile][D + 1]
+    const int s = blockIdx.z, h = blockIdx.y;
+    const int t0 = blockIdx.x * kTile;
+    const int n = min(Tq - t0, kTile);
+    const float* st = state + (static_cast<long long>(s) * heads + h) * (D + 1) * D;
+    for (int e = threadIdx.x; e < (D + 1) * D; e += blockDim.x) Ss[e] = st[e];
+    for (int i = threadIdx.x; i < kTile * D; i += blockDim.x) {
+        const int t = i / D, d = i % D;
+        float v = 0.f;
+        if (t < n) {
+            v = to_f(q[(static_cast<long long>(s) * Tq + t0 + t) * ld + q_off + h * D + d]);
+            v = v > 0.f ? v : 0.f;
+        }
+        qs[d * kTile + t] = v;
+    }
+    __syncthreads();
+    const int t = threadIdx.x;
+    float qv[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) qv[d] = qs[d * kTile + t];
+    float den = 0.f;
+#pragma unroll
+    for (int d = 0; d < D; d += 4) {
+        const float4 zz = *reinterpret_cast<const float4*>(Ss + D * D + d);
+        den = fmaf(zz.x, qv[d], den);
+        den = fmaf(zz.y, qv[d + 1], den);
+        den = fmaf(zz.z, qv[d + 2], den);
+        den = fmaf(zz.w, qv[d + 3], den);
+    }
+    den += 1e-15f;
+    __syncthreads();  // qs is overwritten by the output tile below
+    float* os = qs;
+    for (int r = 0; r < D; ++r) {
+        const float* srow = Ss + r * D;
+        float num = 0.f;
+#pragma unroll
+        for (int d = 0; d < D; d += 4) {
+            const float4 w4 = *reinterpret_cast<const float4*>(srow + d);
+            num = fmaf(w4.x, qv[d], num);
+            num = fmaf(w4.y, qv[d + 1], num);
+            num = fmaf(w4.z, qv[d + 2], num);
+            num = fmaf(w4.w, qv[d + 3], num);
+        }
+        os[t * (D + 1) + r] = num / den;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n * D; i += blockDim.x) {
+        const int tt = i / D, r = i % D;
+        out[(static_cast<long long>(s) * Tq + t0 + tt) * ldo + h * D + r] = from_f<T>(os[tt * (D + 1) + r]);
+    }
+}
+
+template <class T, int D>
+void launch_apply_reg(const T* q, long long ldq, int q_off, int Tq, int heads, int S, const float* state, T* out,
+                      long long ldo, cudaStream_t st) {
+    const size_t smem = (static_cast<size_t>(D + 1) * D + static_cast<size_t>(kTile) * (D + 1)) * sizeof(float);
+    static bool attr = false;
+    if (!attr) {
+        SANA_CUDA(cudaFuncSetAttribute(linattn_apply_reg_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem)));
+        attr = true;
+    }
+    linattn_apply_reg_kernel<T, D><<<dim3(ceil_div(Tq, kTile), heads, S), kTile, smem, st>>>(q, ldq, q_off, Tq, heads,
+                                                                                          state, out, ldo);
+    SANA_CUDA(cudaGetLastError());
+}
+
 }  // namespace
 
 int linattn_chunks(int T) { return (T + kChunk - 1) / kChunk; }
@@ -123,13 +266,34 @@ void linear_attention(const T* q, long long ldq, int q_off, const T* kv, long lo
         attr = true;
     }
     if (Tk > 0) {
-        linattn_state_kernel<T><<<dim3(chunks, heads, S), 256, sm1, st>>>(kv, ldkv, k_off, v_off, Tk, heads, D,
-                                                                          chunks, partial);
+        if (D % 4 == 0) {
+            const int nblk = (D / 4) * (D / 4);
+            int splits = 1;
+            while (splits * 2 * nblk <= 256 && splits < 8) splits *= 2;
+            const size_t sm4 = (static_cast<size_t>(2) * kChunk * D + static_cast<size_t>(splits) * width) * 4;
+            static bool attr4 = false;
+            if (!attr4) {
+                SANA_CUDA(cudaFuncSetAttribute(linattn_state4_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               227 * 1024));
+                attr4 = true;
+            }
+            linattn_state4_kernel<T><<<dim3(chunks, heads, S), 256, sm4, st>>>(kv, ldkv, k_off, v_off, Tk, heads, D,
+                                                                               chunks, partial);
+        } else {
+            linattn_state_kernel<T><<<dim3(chunks, heads, S), 256, sm1, st>>>(kv, ldkv, k_off, v_off, Tk, heads, D,
+                                                                              chunks, partial);
+        }
         SANA_CUDA(cudaGetLastError());
         linattn_reduce_kernel<<<dim3(ceil_div(width, 256), S * heads), 256, 0, st>>>(partial, chunks, width, state);
         SANA_CUDA(cudaGetLastError());
     } else {
         SANA_CUDA(cudaMemsetAsync(state, 0, static_cast<size_t>(S) * heads * width * sizeof(float), st));
+    }
+    switch (D) {
+        case 32: launch_apply_reg<T, 32>(q, ldq, q_off, Tq, heads, S, state, out, ldo, st); return;
+        case 64: launch_apply_reg<T, 64>(q, ldq, q_off, Tq, heads, S, state, out, ldo, st); return;
+        case 72: launch_apply_reg<T, 72>(q, ldq, q_off, Tq, heads, S, state, out, ldo, st); return;
+        default: break;
     }
     linattn_apply_kernel<T><<<dim3(ceil_div(Tq, kTile), heads, S), kTile, sm3, st>>>(q, ldq, q_off, Tq, heads, D,
                                                                                     state, out, ldo);

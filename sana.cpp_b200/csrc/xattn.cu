@@ -4,6 +4,8 @@
 // query: the maximum of the scaled, biased scores, then exp(s - max) weighted sums,
 // divided once by their total (the softmax of :318-334 followed by probs @ v).
 //
+// bf16 mode runs the tensor-core variant below (xattn_mma_kernel) for head dims 32/64/72/128.
+//
 // Keys at index >= kv_len[s] are skipped: their bias is <= -1000 (caption_kv_len), so
 // exp(score - max) underflows to exactly 0 in fp32 and the reference's sum is unchanged.
 #include "kernels.h"
@@ -93,6 +95,209 @@ void launch(const T* q, long long ldq, const T* kv, long long ldkv, int k_off, i
     SANA_CUDA(cudaGetLastError());
 }
 
+
+// ---------------------------------------------------------------------------------------
+// bf16 path on tensor cores (mma.sync m16n8k16, fp32 accumulation), flash-style: each warp
+// owns 16 query rows; keys stream through shared memory in chunks of 64 with an online
+// softmax (running max / sum per row, rescaled accumulators). Scores are rounded as the
+// reference rounds them (scale, then bias); P is rounded to bf16 for the P.V product.
+// Shared tiles are padded (K rows DP + 8, V^T rows 64 + 8 elements) so that every fragment
+// load is bank-conflict free.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+constexpr int kMmaWarps = 4;   // 64 queries per block
+constexpr int kChunkKeys = 64;
+
+template <int D>
+__global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* __restrict__ q, long long ldq,
+                                                                   const bf16* __restrict__ kv, long long ldkv,
+                                                                   int k_off, int v_off,
+                                                                   const float* __restrict__ bias,
+                                                                   const int* __restrict__ kv_len, int Tq, int L,
+                                                                   float scale, bf16* __restrict__ out,
+                                                                   long long ldo) {
+    constexpr int KS = (D + 15) / 16;     // k-steps over the head dim
+    constexpr int DP = KS * 16;           // padded head dim
+    constexpr int NT = D / 8;             // 8-wide output tiles
+    constexpr int KSTR = DP + 8;          // K tile row stride (elements)
+    constexpr int VSTR = kChunkKeys + 8;  // V^T tile row stride (elements)
+    __shared__ __align__(16) bf16 Ks[kChunkKeys * KSTR];
+    __shared__ __align__(16) bf16 Vt[D * VSTR];
+    __shared__ float bsh[kChunkKeys];
+
+    const int s = blockIdx.z, h = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, tig = lane & 3;
+    const int q0 = blockIdx.x * (16 * kMmaWarps) + warp * 16;
+    const int n_kv = kv_len ? kv_len[s] : L;
+    const bool active = q0 < Tq;
+
+    uint32_t qa[KS][4];
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int row = q0 + g + ((r & 1) ? 8 : 0);
+            const int col = kk * 16 + tig * 2 + ((r & 2) ? 8 : 0);
+            uint32_t v = 0;
+            if (row < Tq && col < D)
+                v = *reinterpret_cast<const uint32_t*>(q + (static_cast<long long>(s) * Tq + row) * ldq + h * D + col);
+            qa[kk][r] = v;
+        }
+    }
+    float o[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+    for (int c0 = 0; c0 < n_kv; c0 += kChunkKeys) {
+        const int nk = min(kChunkKeys, n_kv - c0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < kChunkKeys * (DP / 2); i += blockDim.x) {
+            const int j = i / (DP / 2), dp = (i % (DP / 2)) * 2;
+            uint32_t v = 0;
+            if (j < nk && dp < D)
+                v = *reinterpret_cast<const uint32_t*>(kv + (static_cast<long long>(s) * L + c0 + j) * ldkv + k_off +
+                                                       h * D + dp);
+            *reinterpret_cast<uint32_t*>(&Ks[j * KSTR + dp]) = v;
+        }
+        for (int i = threadIdx.x; i < kChunkKeys * D; i += blockDim.x) {
+            const int j = i / D, d = i % D;
+            Vt[d * VSTR + j] = (j < nk) ? kv[(static_cast<long long>(s) * L + c0 + j) * ldkv + v_off + h * D + d]
+                                        : __float2bfloat16_rn(0.f);
+        }
+        for (int j = threadIdx.x; j < kChunkKeys; j += blockDim.x)
+            bsh[j] = (j < nk && bias) ? bias[static_cast<long long>(s) * L + c0 + j] : 0.f;
+        __syncthreads();
+        if (!active) continue;
+
+        float sc[kChunkKeys / 8][4];
+#pragma unroll
+        for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
+            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+            for (int kk = 0; kk < KS; ++kk) {
+                const bf16* kr = Ks + (nt * 8 + g) * KSTR + kk * 16 + tig * 2;
+                mma_bf16_16816(sc[nt], qa[kk], *reinterpret_cast<const uint32_t*>(kr),
+                               *reinterpret_cast<const uint32_t*>(kr + 8));
+            }
+        }
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = nt * 8 + tig * 2 + (e & 1);
+                const float v = key < nk ? __fadd_rn(__fmul_rn(sc[nt][e], scale), bsh[key]) : -INFINITY;
+                sc[nt][e] = v;
+            }
+            mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
+            mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float corr0 = expf(m0 - mn0), corr1 = expf(m1 - mn1);  // m = -inf on the first chunk: 0
+        m0 = mn0;
+        m1 = mn1;
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
+            sc[nt][0] = expf(sc[nt][0] - mn0);
+            sc[nt][1] = expf(sc[nt][1] - mn0);
+            sc[nt][2] = expf(sc[nt][2] - mn1);
+            sc[nt][3] = expf(sc[nt][3] - mn1);
+            sum0 += sc[nt][0] + sc[nt][1];
+            sum1 += sc[nt][2] + sc[nt][3];
+        }
+        l0 = l0 * corr0 + sum0;
+        l1 = l1 * corr1 + sum1;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            o[nt][0] *= corr0;
+            o[nt][1] *= corr0;
+            o[nt][2] *= corr1;
+            o[nt][3] *= corr1;
+        }
+#pragma unroll
+        for (int kk = 0; kk < kChunkKeys / 16; ++kk) {
+            const uint32_t pa[4] = {pack_bf16(sc[2 * kk][0], sc[2 * kk][1]), pack_bf16(sc[2 * kk][2], sc[2 * kk][3]),
+                                    pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]),
+                                    pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3])};
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const bf16* vr = Vt + (nt * 8 + g) * VSTR + kk * 16 + tig * 2;
+                mma_bf16_16816(o[nt], pa, *reinterpret_cast<const uint32_t*>(vr),
+                               *reinterpret_cast<const uint32_t*>(vr + 8));
+            }
+        }
+    }
+    if (!active) return;
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
+    const int r0 = q0 + g, r1 = q0 + g + 8;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int col = h * D + nt * 8 + tig * 2;
+        if (r0 < Tq)
+            *reinterpret_cast<uint32_t*>(out + (static_cast<long long>(s) * Tq + r0) * ldo + col) =
+                pack_bf16(o[nt][0] * inv0, o[nt][1] * inv0);
+        if (r1 < Tq)
+            *reinterpret_cast<uint32_t*>(out + (static_cast<long long>(s) * Tq + r1) * ldo + col) =
+                pack_bf16(o[nt][2] * inv1, o[nt][3] * inv1);
+    }
+}
+
+template <int D>
+bool launch_mma(const bf16* q, long long ldq, const bf16* kv, long long ldkv, int k_off, int v_off, const float* bias,
+                const int* kv_len, int S, int Tq, int L, int heads, float scale, bf16* out, long long ldo,
+                cudaStream_t st) {
+    xattn_mma_kernel<D><<<dim3(ceil_div(Tq, 16 * kMmaWarps), heads, S), 32 * kMmaWarps, 0, st>>>(
+        q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, Tq, L, scale, out, ldo);
+    SANA_CUDA(cudaGetLastError());
+    return true;
+}
+
+// Tensor-core path when the operands allow 32-bit fragment loads.
+template <class T>
+bool try_mma(const T*, long long, const T*, long long, int, int, const float*, const int*, int, int, int, int, int,
+             float, T*, long long, cudaStream_t) {
+    return false;
+}
+template <>
+bool try_mma<bf16>(const bf16* q, long long ldq, const bf16* kv, long long ldkv, int k_off, int v_off,
+                   const float* bias, const int* kv_len, int S, int Tq, int L, int heads, int D, float scale, bf16* out,
+                   long long ldo, cudaStream_t st) {
+    const bool aligned = ldq % 2 == 0 && ldkv % 2 == 0 && ldo % 2 == 0 && k_off % 2 == 0 && v_off % 2 == 0 &&
+                         (reinterpret_cast<uintptr_t>(q) & 3) == 0 && (reinterpret_cast<uintptr_t>(kv) & 3) == 0 &&
+                         (reinterpret_cast<uintptr_t>(out) & 3) == 0;
+    if (!aligned) return false;
+    switch (D) {
+        case 32: return launch_mma<32>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, scale, out, ldo, st);
+        case 64: return launch_mma<64>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, scale, out, ldo, st);
+        case 72: return launch_mma<72>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, scale, out, ldo, st);
+        case 128: return launch_mma<128>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, scale, out, ldo, st);
+        default: return false;
+    }
+}
+
 }  // namespace
 
 template <class T>
@@ -104,6 +309,7 @@ void cross_attention(const T* q, long long ldq, const T* kv, long long ldkv, int
     const size_t smem = 2 * static_cast<size_t>(L) * D * sizeof(T) + static_cast<size_t>(L) * 4 + 8;
     SANA_REQUIRE(smem <= 227 * 1024, "caption too long for the shared-memory key/value tile");
     if (S == 0 || Tq == 0) return;
+    if (try_mma<T>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, D, scale, out, ldo, st)) return;
     if (D <= 8) launch<T, 8>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, D, scale, out, ldo, st);
     else if (D <= 32) launch<T, 32>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, D, scale, out, ldo, st);
     else if (D <= 72) launch<T, 72>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, D, scale, out, ldo, st);

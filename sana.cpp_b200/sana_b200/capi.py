@@ -151,6 +151,22 @@ class SanaCuda:
     def synchronize(self):
         self._call("sana_cuda_synchronize")
 
+    def set_stream(self, stream_ptr: int):
+        """Runs later work on the given cudaStream_t (0 restores the handle's own stream)."""
+        self._call("sana_cuda_set_stream", ctypes.c_void_p(stream_ptr or None))
+
+    def gemm_device(self, A: int, B: int, M: int, N: int, K: int, out: int, bias: int = 0, act: int = 0):
+        vp = ctypes.c_void_p
+        self._call("sana_op_gemm_device", vp(A), vp(B), _i(M), _i(N), _i(K), vp(bias) if bias else None, _i(act),
+                   vp(out))
+
+    def denoise_loop_ptrs(self, lat: int, B: int, H: int, W: int, enc: int, L: int, Din: int, bias: int, out: int,
+                          guidance: float = 4.5, num_steps: int = 20, flow_shift: float = 3.0):
+        """sana_cuda_denoise_loop on raw host pointers (e.g. pinned buffers)."""
+        vp = ctypes.c_void_p
+        self._call("sana_cuda_denoise_loop", vp(lat), _i(B), _i(H), _i(W), vp(enc), _i(L), _i(Din),
+                   vp(bias) if bias else None, _f(guidance), _i(num_steps), _f(flow_shift), vp(out))
+
     def last_launch_count(self) -> int:
         return self.lib.sana_cuda_last_launch_count(self.h)
 

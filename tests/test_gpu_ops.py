@@ -202,3 +202,17 @@ def test_scheduler_trajectory_matches_golden(gpu_f32, oracle):
     for s in range(20):
         x, hist, lower = gpu_f32.scheduler_step(sg, s, lower, hist, mo[s], x)
         assert rel_err(x, g["samples"][s]) < 1e-6, s
+
+
+@pytest.mark.parametrize("D,Tq,L,lens", [(72, 1024, 300, (8, 24)), (72, 100, 300, (300, 1)), (32, 77, 70, (70, 65)),
+                                        (64, 130, 129, (64, 129)), (128, 40, 20, (20, 3))])
+def test_cross_attention_tensor_core_shapes(gpu_bf16, oracle, D, Tq, L, lens):
+    """The bf16 tensor-core cross-attention at the model's shape (16 heads x 72, 300 caption
+    tokens, short valid prefixes) and at chunk-boundary key counts."""
+    from sana_b200 import synthetic as syn
+    rng = np.random.default_rng(D * 3 + L)
+    q = rng.standard_normal((2, 4, Tq, D)).astype(np.float32)
+    k, v = (rng.standard_normal((2, 4, L, D)).astype(np.float32) for _ in range(2))
+    bias = syn.attention_bias(lens, L)
+    ref = oracle.attention(q, k, v, bias)
+    assert rel_err(gpu_bf16.attention(q, k, v, bias), ref) < BF16_TOL
