@@ -23,88 +23,115 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
     }
 }
 
-// bf16, 8 channels per thread (half % 8 == 0, 16-byte aligned rows). A block owns a tile
-// of kGroups x 8 channels of both halves; their 3x3 taps and biases are staged once in
-// shared memory, tap-major, so every weight read is a conflict-free 16-byte load. Lane i of
-// a warp handles channel group i of one pixel: input loads and output stores are 512-byte
-// contiguous runs. Threads stride over pixels.
-constexpr int kGroups = 32;  // channel groups (of 8) per block
-constexpr int kPixLanes = 8; // pixels in flight per block (blockDim = kGroups * kPixLanes)
+// bf16 tiled path (half % 8 == 0, 16-byte aligned rows, W <= kTileW). A block owns 64
+// channels of both halves and kTileRows full image rows of one sequence. The tile's input
+// rows plus a one-pixel halo are copied to shared memory with asynchronous 16-byte copies
+// (cp.async, zero-filled outside the image = the conv's zero padding), all issued before
+// the first wait, so the block streams its ~87 KB at full bandwidth. Thread (channel quad,
+// column) keeps its 4 data + 4 gate channels' 3x3 weights in registers and reads the 9 taps
+// of each output from shared memory as 8-byte loads.
+constexpr int kTileCh = 64;     // channels per half in a tile
+constexpr int kTileRows = 8;
+constexpr int kTileW = 64;      // widest image row handled by the tiled path
+constexpr int kQuads = kTileCh / 4;
 
-__global__ void __launch_bounds__(kGroups * kPixLanes) dwglu_vec8_kernel(const bf16* __restrict__ in, long long ldi,
-                                                                         int S, int H, int W, int half,
-                                                                         const float* __restrict__ w,
-                                                                         const float* __restrict__ b,
-                                                                         bf16* __restrict__ out, long long ldo) {
-    __shared__ __align__(16) float ws[2][9][kGroups * 8];  // [half][tap][channel in tile]
-    __shared__ __align__(16) float bs[2][kGroups * 8];
-    const int groups = half / 8;
-    const int g0 = blockIdx.y * kGroups;
-    const int ng = min(kGroups, groups - g0);
-    for (int i = threadIdx.x; i < 2 * 9 * kGroups * 8; i += blockDim.x) {
-        const int hf = i / (9 * kGroups * 8);
-        const int rem = i % (9 * kGroups * 8);
-        const int c = rem / 9, tap = rem % 9;  // coalesced read of w[(ch)*9 + tap]
-        const int ch = g0 * 8 + c;
-        ws[hf][tap][c] = (c < ng * 8) ? w[(static_cast<long long>(hf) * half + ch) * 9 + tap] : 0.f;
-    }
-    for (int i = threadIdx.x; i < 2 * kGroups * 8; i += blockDim.x) {
-        const int hf = i / (kGroups * 8), c = i % (kGroups * 8);
-        bs[hf][c] = (c < ng * 8) ? b[static_cast<long long>(hf) * half + g0 * 8 + c] : 0.f;
-    }
-    __syncthreads();
-    const int gl = threadIdx.x % kGroups;
-    if (gl >= ng) return;
-    const int c0 = (g0 + gl) * 8;
-    const long long pixels = static_cast<long long>(S) * H * W;
-    for (long long pix = blockIdx.x * static_cast<long long>(kPixLanes) + threadIdx.x / kGroups; pix < pixels;
-         pix += static_cast<long long>(gridDim.x) * kPixLanes) {
-        const int x = static_cast<int>(pix % W);
-        const int y = static_cast<int>((pix / W) % H);
-        const long long sH = pix / (static_cast<long long>(W) * H) * H;
-        float dv[8], gv[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            dv[j] = 0.f;
-            gv[j] = 0.f;
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void unpack4(const uint2& u, float (&f)[4]) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+    f[0] = a.x;
+    f[1] = a.y;
+    f[2] = b.x;
+    f[3] = b.y;
+}
+
+template <int WMAX>
+__global__ void __launch_bounds__(256) dwglu_tile_kernel(const bf16* __restrict__ in, long long ldi, int S, int H,
+                                                         int W, int half, const float* __restrict__ w,
+                                                         const float* __restrict__ b, bf16* __restrict__ out,
+                                                         long long ldo) {
+    constexpr int PW = WMAX + 2;  // staged pixels per row (with halo)
+    extern __shared__ __align__(16) bf16 tile[];  // [kTileRows+2][PW][2][kTileCh]
+    const int c0 = blockIdx.y * kTileCh;          // first channel of the tile in each half
+    const int nch = min(kTileCh, half - c0);      // a multiple of 8
+    const int row_tiles = (H + kTileRows - 1) / kTileRows;
+    const int s = blockIdx.x / row_tiles;
+    const int y0 = (blockIdx.x % row_tiles) * kTileRows;
+    {
+        constexpr int kChunks = kTileCh / 8;  // 16-byte chunks per half-pixel
+        const int total = (kTileRows + 2) * PW * 2 * kChunks;
+        const uint32_t base = smem_u32(tile);
+        for (int i = threadIdx.x; i < total; i += blockDim.x) {
+            const int ck = i % kChunks;
+            const int hf = (i / kChunks) % 2;
+            const int px = (i / (2 * kChunks)) % PW;
+            const int r = i / (2 * kChunks * PW);
+            const int iy = y0 + r - 1, ix = px - 1;
+            const bool ok = iy >= 0 && iy < H && ix >= 0 && ix < W && ck * 8 < nch;
+            const bf16* src = ok ? in + ((static_cast<long long>(s) * H + iy) * W + ix) * ldi + hf * half + c0 + ck * 8
+                                 : in;
+            cp_async16(base + static_cast<uint32_t>(i) * 16u, src, ok ? 16u : 0u);
         }
+    }
+    const int q = threadIdx.x % kQuads;  // channel quad within the tile
+    const int ch = c0 + q * 4;
+    const bool qok = q * 4 < nch;
+    float wd[4][9], wg[4][9], bd[4], bg[4];
 #pragma unroll
-        for (int ky = 0; ky < 3; ++ky) {
-            const int iy = y + ky - 1;
-            if (iy < 0 || iy >= H) continue;
+    for (int j = 0; j < 4; ++j) {
 #pragma unroll
-            for (int kx = 0; kx < 3; ++kx) {
-                const int ix = x + kx - 1;
-                if (ix < 0 || ix >= W) continue;
-                const bf16* src = in + ((sH + iy) * W + ix) * ldi;
-                float fd[8], fg[8];
-                unpack8(*reinterpret_cast<const uint4*>(src + c0), fd);
-                unpack8(*reinterpret_cast<const uint4*>(src + half + c0), fg);
-                const int tap = ky * 3 + kx;
-                const float4 wd0 = *reinterpret_cast<const float4*>(&ws[0][tap][gl * 8]);
-                const float4 wd1 = *reinterpret_cast<const float4*>(&ws[0][tap][gl * 8 + 4]);
-                const float4 wg0 = *reinterpret_cast<const float4*>(&ws[1][tap][gl * 8]);
-                const float4 wg1 = *reinterpret_cast<const float4*>(&ws[1][tap][gl * 8 + 4]);
-                const float wdv[8] = {wd0.x, wd0.y, wd0.z, wd0.w, wd1.x, wd1.y, wd1.z, wd1.w};
-                const float wgv[8] = {wg0.x, wg0.y, wg0.z, wg0.w, wg1.x, wg1.y, wg1.z, wg1.w};
+        for (int t = 0; t < 9; ++t) {
+            wd[j][t] = qok ? w[static_cast<long long>(ch + j) * 9 + t] : 0.f;
+            wg[j][t] = qok ? w[static_cast<long long>(half + ch + j) * 9 + t] : 0.f;
+        }
+        bd[j] = qok ? b[ch + j] : 0.f;
+        bg[j] = qok ? b[half + ch + j] : 0.f;
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    if (!qok) return;
+    const int rows = min(kTileRows, H - y0);
+    for (int x = threadIdx.x / kQuads; x < W; x += blockDim.x / kQuads) {
+        for (int ry = 0; ry < rows; ++ry) {
+            float dv[4] = {0.f, 0.f, 0.f, 0.f}, gv[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    dv[j] = fmaf(fd[j], wdv[j], dv[j]);
-                    gv[j] = fmaf(fg[j], wgv[j], gv[j]);
+            for (int ky = 0; ky < 3; ++ky) {
+#pragma unroll
+                for (int kx = 0; kx < 3; ++kx) {
+                    const bf16* t = tile + (((ry + ky) * PW + (x + kx)) * 2) * kTileCh + q * 4;
+                    float fd[4], fg[4];
+                    unpack4(*reinterpret_cast<const uint2*>(t), fd);
+                    unpack4(*reinterpret_cast<const uint2*>(t + kTileCh), fg);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        dv[j] = fmaf(fd[j], wd[j][ky * 3 + kx], dv[j]);
+                        gv[j] = fmaf(fg[j], wg[j][ky * 3 + kx], gv[j]);
+                    }
                 }
             }
+            const float o0 = (dv[0] + bd[0]) * silu(gv[0] + bg[0]);
+            const float o1 = (dv[1] + bd[1]) * silu(gv[1] + bg[1]);
+            const float o2 = (dv[2] + bd[2]) * silu(gv[2] + bg[2]);
+            const float o3 = (dv[3] + bd[3]) * silu(gv[3] + bg[3]);
+            uint2 pk;
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(o0, o1), h1 = __floats2bfloat162_rn(o2, o3);
+            pk.x = *reinterpret_cast<uint32_t*>(&h0);
+            pk.y = *reinterpret_cast<uint32_t*>(&h1);
+            const long long pix = (static_cast<long long>(s) * H + y0 + ry) * W + x;
+            *reinterpret_cast<uint2*>(out + pix * ldo + ch) = pk;
         }
-        uint4 pk;
-        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-        for (int j = 0; j < 8; j += 2) {
-            const float o0 = (dv[j] + bs[0][gl * 8 + j]) * silu(gv[j] + bs[1][gl * 8 + j]);
-            const float o1 = (dv[j + 1] + bs[0][gl * 8 + j + 1]) * silu(gv[j + 1] + bs[1][gl * 8 + j + 1]);
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(o0, o1);
-            pw[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
-        }
-        *reinterpret_cast<uint4*>(out + pix * ldo + c0) = pk;
     }
+}
+
+template <int WMAX>
+size_t dwglu_tile_smem() {
+    return sizeof(bf16) * (kTileRows + 2) * (WMAX + 2) * 2 * kTileCh;
 }
 
 // Any type / channel count: one output channel per thread.
@@ -181,13 +208,29 @@ void depthwise_glu(const T* in, long long ldi, int S, int H, int W, int E, const
     if (pixels == 0 || half == 0) return;
     bool vec = sizeof(T) == 2 && half % 8 == 0 && ldi % 8 == 0 && ldo % 8 == 0 &&
                (reinterpret_cast<uintptr_t>(in) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
-    if (vec) {
-        const int tiles = ceil_div(half / 8, kGroups);
-        long long px_blocks = (pixels + kPixLanes - 1) / kPixLanes;
-        const long long cap = (148LL * 8 + tiles - 1) / tiles * 4;  // ~32 resident blocks per SM in total
-        if (px_blocks > cap) px_blocks = cap;
-        dwglu_vec8_kernel<<<dim3(static_cast<unsigned>(px_blocks), tiles), kGroups * kPixLanes, 0, st>>>(
-            reinterpret_cast<const bf16*>(in), ldi, S, H, W, half, w, b, reinterpret_cast<bf16*>(out), ldo);
+    if (vec && W <= kTileW) {
+        const int tiles = ceil_div(half, kTileCh);
+        const int row_tiles = ceil_div(H, kTileRows);
+        const dim3 grid(static_cast<unsigned>(S * row_tiles), tiles);
+        if (W <= 32) {
+            static bool a32 = false;
+            if (!a32) {
+                SANA_CUDA(cudaFuncSetAttribute(dwglu_tile_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(dwglu_tile_smem<32>())));
+                a32 = true;
+            }
+            dwglu_tile_kernel<32><<<grid, 256, dwglu_tile_smem<32>(), st>>>(
+                reinterpret_cast<const bf16*>(in), ldi, S, H, W, half, w, b, reinterpret_cast<bf16*>(out), ldo);
+        } else {
+            static bool a64 = false;
+            if (!a64) {
+                SANA_CUDA(cudaFuncSetAttribute(dwglu_tile_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(dwglu_tile_smem<64>())));
+                a64 = true;
+            }
+            dwglu_tile_kernel<64><<<grid, 256, dwglu_tile_smem<64>(), st>>>(
+                reinterpret_cast<const bf16*>(in), ldi, S, H, W, half, w, b, reinterpret_cast<bf16*>(out), ldo);
+        }
     } else {
         dwglu_scalar_kernel<T><<<grid_for(pixels * half), 256, 0, st>>>(in, ldi, S, H, W, half, w, b, out, ldo);
     }

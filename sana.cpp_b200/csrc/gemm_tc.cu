@@ -25,11 +25,11 @@ constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 
 template <int BN>
 struct Cfg {
-    static constexpr int kStages = BN == 128 ? 6 : 4;
+    static constexpr int kStages = BN == 128 ? 6 : (BN == 192 ? 5 : 4);
     static constexpr int kABytes = BM * BK * 2;
     static constexpr int kBBytes = BN * BK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;  // power of two >= two accumulators
     // layout: [A stages][B stages][barriers][tmem slot]
     static constexpr int kBarOffset = kStages * kStageBytes;
     static constexpr int kSmemBytes = kBarOffset + (2 * kStages + 5) * 8 + 16 + 1024;
@@ -434,7 +434,10 @@ bool gemm_tc_supported(const GemmProblem& p) {
 
 void gemm_tc(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
     SANA_REQUIRE(gemm_tc_supported(p), "gemm_tc: unsupported problem");
-    tc::launch<128>(p, err, stream, num_sms);
+    // 128 x 192 tiles when they divide N (every projection width of the model: 1152, 2304,
+    // 3456, 5760), 128 x 128 otherwise.
+    if (p.N % 192 == 0) tc::launch<192>(p, err, stream, num_sms);
+    else tc::launch<128>(p, err, stream, num_sms);
 }
 
 static std::atomic<long long> g_tc_launches{0}, g_simt_launches{0};

@@ -117,8 +117,24 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-constexpr int kMmaWarps = 4;   // 64 queries per block
+constexpr int kMmaWarps = 8;   // 128 queries per block
 constexpr int kChunkKeys = 64;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void ldmatrix_x2_trans(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+
+// Row strides (elements) whose 4-byte-word stride is 4 mod 8: every 8-row fragment load
+// then touches 32 distinct banks.
+__host__ __device__ constexpr int conflict_free_stride(int min_elems) {
+    return ((min_elems / 2) % 8 == 4) ? min_elems : ((min_elems + 7) / 8 * 8 + ((((min_elems + 7) / 8 * 8) / 2) % 8 == 4 ? 0 : 8));
+}
 
 template <int D>
 __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* __restrict__ q, long long ldq,
@@ -128,13 +144,14 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
                                                                    const int* __restrict__ kv_len, int Tq, int L,
                                                                    float scale, bf16* __restrict__ out,
                                                                    long long ldo) {
-    constexpr int KS = (D + 15) / 16;     // k-steps over the head dim
-    constexpr int DP = KS * 16;           // padded head dim
-    constexpr int NT = D / 8;             // 8-wide output tiles
-    constexpr int KSTR = DP + 8;          // K tile row stride (elements)
-    constexpr int VSTR = kChunkKeys + 8;  // V^T tile row stride (elements)
+    constexpr int KS = (D + 15) / 16;                       // k-steps over the head dim
+    constexpr int DP = KS * 16;                             // padded head dim
+    constexpr int NT = D / 8;                               // 8-wide output tiles
+    constexpr int KSTR = conflict_free_stride(DP);          // K tile row stride
+    constexpr int VSTR = conflict_free_stride(D);           // V tile row stride
+    static_assert((KSTR / 2) % 8 == 4 && (VSTR / 2) % 8 == 4 && KSTR % 8 == 0 && VSTR % 8 == 0, "strides");
     __shared__ __align__(16) bf16 Ks[kChunkKeys * KSTR];
-    __shared__ __align__(16) bf16 Vt[D * VSTR];
+    __shared__ __align__(16) bf16 Vs[kChunkKeys * VSTR];
     __shared__ float bsh[kChunkKeys];
 
     const int s = blockIdx.z, h = blockIdx.y;
@@ -143,6 +160,10 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
     const int q0 = blockIdx.x * (16 * kMmaWarps) + warp * 16;
     const int n_kv = kv_len ? kv_len[s] : L;
     const bool active = q0 < Tq;
+    if (DP > D) {  // zero the K padding columns once; the copies below never touch them
+        for (int i = threadIdx.x; i < kChunkKeys * (DP - D); i += blockDim.x)
+            Ks[(i / (DP - D)) * KSTR + D + i % (DP - D)] = __float2bfloat16_rn(0.f);
+    }
 
     uint32_t qa[KS][4];
 #pragma unroll
@@ -161,25 +182,28 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    const uint32_t kbase = smem_u32(Ks), vbase = smem_u32(Vs);
 
     for (int c0 = 0; c0 < n_kv; c0 += kChunkKeys) {
         const int nk = min(kChunkKeys, n_kv - c0);
         __syncthreads();
-        for (int i = threadIdx.x; i < kChunkKeys * (DP / 2); i += blockDim.x) {
-            const int j = i / (DP / 2), dp = (i % (DP / 2)) * 2;
-            uint32_t v = 0;
-            if (j < nk && dp < D)
-                v = *reinterpret_cast<const uint32_t*>(kv + (static_cast<long long>(s) * L + c0 + j) * ldkv + k_off +
-                                                       h * D + dp);
-            *reinterpret_cast<uint32_t*>(&Ks[j * KSTR + dp]) = v;
-        }
-        for (int i = threadIdx.x; i < kChunkKeys * D; i += blockDim.x) {
-            const int j = i / D, d = i % D;
-            Vt[d * VSTR + j] = (j < nk) ? kv[(static_cast<long long>(s) * L + c0 + j) * ldkv + v_off + h * D + d]
-                                        : __float2bfloat16_rn(0.f);
+        for (int i = threadIdx.x; i < kChunkKeys * (D / 8) * 2; i += blockDim.x) {
+            const int which = i / (kChunkKeys * (D / 8)), rem = i % (kChunkKeys * (D / 8));
+            const int j = rem / (D / 8), ck = rem % (D / 8);
+            if (j < nk) {
+                const bf16* src = kv + (static_cast<long long>(s) * L + c0 + j) * ldkv + (which ? v_off : k_off) + h * D +
+                                  ck * 8;
+                cp_async16((which ? vbase + static_cast<uint32_t>(j * VSTR + ck * 8) * 2u
+                                  : kbase + static_cast<uint32_t>(j * KSTR + ck * 8) * 2u),
+                           src);
+            } else {  // keys past the chunk end: zeros (their scores are masked to -inf)
+                bf16* dst = which ? Vs + j * VSTR + ck * 8 : Ks + j * KSTR + ck * 8;
+                *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+            }
         }
         for (int j = threadIdx.x; j < kChunkKeys; j += blockDim.x)
             bsh[j] = (j < nk && bias) ? bias[static_cast<long long>(s) * L + c0 + j] : 0.f;
+        cp_async_wait_all();
         __syncthreads();
         if (!active) continue;
 
@@ -200,8 +224,7 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int key = nt * 8 + tig * 2 + (e & 1);
-                const float v = key < nk ? __fadd_rn(__fmul_rn(sc[nt][e], scale), bsh[key]) : -INFINITY;
-                sc[nt][e] = v;
+                sc[nt][e] = key < nk ? __fadd_rn(__fmul_rn(sc[nt][e], scale), bsh[key]) : -INFINITY;
             }
             mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
             mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
@@ -233,16 +256,19 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
             o[nt][2] *= corr1;
             o[nt][3] *= corr1;
         }
+        const int kmax = (nk + 15) / 16;  // k-steps holding live keys
 #pragma unroll
         for (int kk = 0; kk < kChunkKeys / 16; ++kk) {
+            if (kk >= kmax) break;
             const uint32_t pa[4] = {pack_bf16(sc[2 * kk][0], sc[2 * kk][1]), pack_bf16(sc[2 * kk][2], sc[2 * kk][3]),
                                     pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]),
                                     pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3])};
+            const uint32_t vrow = vbase + static_cast<uint32_t>((kk * 16 + (lane & 15)) * VSTR) * 2u;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                const bf16* vr = Vt + (nt * 8 + g) * VSTR + kk * 16 + tig * 2;
-                mma_bf16_16816(o[nt], pa, *reinterpret_cast<const uint32_t*>(vr),
-                               *reinterpret_cast<const uint32_t*>(vr + 8));
+                uint32_t b0, b1;
+                ldmatrix_x2_trans(vrow + static_cast<uint32_t>(nt * 16), b0, b1);
+                mma_bf16_16816(o[nt], pa, b0, b1);
             }
         }
     }
@@ -285,9 +311,10 @@ template <>
 bool try_mma<bf16>(const bf16* q, long long ldq, const bf16* kv, long long ldkv, int k_off, int v_off,
                    const float* bias, const int* kv_len, int S, int Tq, int L, int heads, int D, float scale, bf16* out,
                    long long ldo, cudaStream_t st) {
-    const bool aligned = ldq % 2 == 0 && ldkv % 2 == 0 && ldo % 2 == 0 && k_off % 2 == 0 && v_off % 2 == 0 &&
-                         (reinterpret_cast<uintptr_t>(q) & 3) == 0 && (reinterpret_cast<uintptr_t>(kv) & 3) == 0 &&
-                         (reinterpret_cast<uintptr_t>(out) & 3) == 0;
+    // 16-byte copies of K / V rows: row starts, offsets and the head stride 8-element aligned
+    const bool aligned = ldq % 2 == 0 && ldkv % 8 == 0 && ldo % 2 == 0 && k_off % 8 == 0 && v_off % 8 == 0 &&
+                         D % 8 == 0 && (reinterpret_cast<uintptr_t>(q) & 3) == 0 &&
+                         (reinterpret_cast<uintptr_t>(kv) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 3) == 0;
     if (!aligned) return false;
     switch (D) {
         case 32: return launch_mma<32>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, scale, out, ldo, st);
