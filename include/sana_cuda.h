@@ -74,6 +74,13 @@ int sana_cuda_last_launch_count(const sana_cuda_ctx *ctx);
  * and to the CUDA-core kernel (fp32 check mode, tiny or unaligned shapes). */
 void sana_cuda_gemm_counts(long long *tensor_core, long long *cuda_core);
 
+/* Profiling: runs the denoising loop of sana_cuda_denoise_loop_device once without graph
+ * capture, with CUDA events around every kernel launch on the handle's stream, and writes a
+ * JSON object {"kernel class": [launches, total milliseconds], ...} to `report`. */
+int sana_cuda_profile_loop(sana_cuda_ctx *ctx, const float *latents, int B, int H, int W, const float *enc, int L,
+                           int enc_dim, const float *bias, float guidance, int num_steps, float flow_shift, float *out,
+                           char *report, size_t report_len);
+
 /* Diagnostics: copies `bytes` at `offset` of a named workspace buffer of the last call
  * (a, qkv, ao, cq, xb, ffh, glu, x, x1, x2, x3, mods, tmod, emb, ckv1, ctx, kvlen, noise,
  * lat, part) to `host`; *size_out receives the buffer's size. No reference counterpart. */

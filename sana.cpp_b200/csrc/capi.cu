@@ -1,4 +1,5 @@
 // The C ABI of include/sana_cuda.h over the Engine and the kernels.
+#include <cstdio>
 #include <cstring>
 #include <memory>
 #include <new>
@@ -321,6 +322,19 @@ int sana_cuda_project_caption(sana_cuda_ctx* ctx, const float* enc, int S, int L
     return guard(ctx, [&] {
         SANA_REQUIRE(enc && out, "null argument to project_caption");
         engine(ctx).project_caption(enc, S, L, enc_dim, out);
+    });
+}
+
+int sana_cuda_profile_loop(sana_cuda_ctx* ctx, const float* latents, int B, int H, int W, const float* enc, int L,
+                           int enc_dim, const float* bias, float guidance, int num_steps, float flow_shift, float* out,
+                           char* report, size_t report_len) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(latents && enc && out && report && report_len > 0, "null argument to profile_loop");
+        sana::Engine& eng = engine(ctx);
+        eng.profile_loop_device(latents, B, H, W, enc, L, enc_dim, bias, guidance, num_steps, flow_shift, out);
+        const std::string r = eng.profile_report();
+        eng.profile_enable(false);
+        std::snprintf(report, report_len, "%s", r.c_str());
     });
 }
 

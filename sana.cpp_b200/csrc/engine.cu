@@ -424,10 +424,20 @@ void Engine::block_impl(int b, const float* x_in, float* x_self, float* x_cross,
     T* ao = ao_.as<T>();
 
     // self attention: LN(eps 1e-6) + modulate(shift_msa, scale_msa) -> QKV -> linear attention
-    ln_modulate<T>(x_in, M, C, Tn, w.ln1g.as<float>(), w.ln1b.as<float>(), mod_b, C6, 0, 1, 1e-6f, a, st_);
-    gemm_act(a, C, w.wqkv.get(), C, M, 3 * C, C, epi_out(qkv, bf, 3 * C, w.bqkv.as<float>()));
+    {
+        ProfScope p(this, "ln_modulate");
+        ln_modulate<T>(x_in, M, C, Tn, w.ln1g.as<float>(), w.ln1b.as<float>(), mod_b, C6, 0, 1, 1e-6f, a, st_);
+    }
+    {
+        ProfScope p(this, "gemm_qkv");
+        gemm_act(a, C, w.wqkv.get(), C, M, 3 * C, C, epi_out(qkv, bf, 3 * C, w.bqkv.as<float>()));
+    }
     const int Ds = C / d_.Hs;
-    linear_attention<T>(qkv, 3LL * C, 0, qkv, 3LL * C, C, 2 * C, S, Tn, Tn, d_.Hs, Ds, part_.as<float>(), ao, C, st_);
+    {
+        ProfScope p(this, "linear_attention");
+        linear_attention<T>(qkv, 3LL * C, 0, qkv, 3LL * C, C, 2 * C, S, Tn, Tn, d_.Hs, Ds, part_.as<float>(), ao, C,
+                            st_);
+    }
     // out projection + gate_msa + residual (after_self); bf16 mode also keeps a bf16 copy
     {
         Epilogue e = epi_out(x_self, false, C, w.bo.as<float>());
@@ -441,28 +451,45 @@ void Engine::block_impl(int b, const float* x_in, float* x_self, float* x_cross,
             e.out2_bf16 = 1;
             e.ldo2 = C;
         }
+        ProfScope p(this, "gemm_out");
         gemm_act(ao, C, w.wo.get(), C, M, C, C, e);
     }
     // cross attention (no norm, no gate): q from the residual stream
     const void* xq = bf ? static_cast<const void*>(xb_.get()) : static_cast<const void*>(x_self);
-    gemm_act(xq, C, w.wcq.get(), C, M, C, C, epi_out(cq_.get(), bf, C, w.bcq.as<float>()));
+    {
+        ProfScope p(this, "gemm_cross_q");
+        gemm_act(xq, C, w.wcq.get(), C, M, C, C, epi_out(cq_.get(), bf, C, w.bcq.as<float>()));
+    }
     const int Dc = C / d_.Hc;
     const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(Dc)));
-    cross_attention<T>(cq_.as<T>(), C, static_cast<const T*>(ckv_b), 2LL * C, 0, C, bias_d, kvlen_d, S, Tn, L, d_.Hc,
-                       Dc, scale, ao, C, st_);
+    {
+        ProfScope p(this, "cross_attention");
+        cross_attention<T>(cq_.as<T>(), C, static_cast<const T*>(ckv_b), 2LL * C, 0, C, bias_d, kvlen_d, S, Tn, L,
+                           d_.Hc, Dc, scale, ao, C, st_);
+    }
     {
         Epilogue e = epi_out(x_cross, false, C, w.bco.as<float>());
         e.resid = x_self;
         e.ldr = C;
+        ProfScope p(this, "gemm_cross_out");
         gemm_act(ao, C, w.wco.get(), C, M, C, C, e);
     }
     // Mix-FFN: LN + modulate(shift_mlp, scale_mlp) -> inverted 1x1 + SiLU -> depthwise + GLU
     // -> point 1x1 + gate_mlp + residual (after_ff)
-    ln_modulate<T>(x_cross, M, C, Tn, w.ln2g.as<float>(), w.ln2b.as<float>(), mod_b, C6, 3, 4, 1e-6f, a, st_);
-    gemm_act(a, C, w.winv.get(), C, M, E, C, epi_out(ffh_.get(), bf, E, w.binv.as<float>(), kActSilu));
+    {
+        ProfScope p(this, "ln_modulate");
+        ln_modulate<T>(x_cross, M, C, Tn, w.ln2g.as<float>(), w.ln2b.as<float>(), mod_b, C6, 3, 4, 1e-6f, a, st_);
+    }
+    {
+        ProfScope p(this, "gemm_ff_inverted");
+        gemm_act(a, C, w.winv.get(), C, M, E, C, epi_out(ffh_.get(), bf, E, w.binv.as<float>(), kActSilu));
+    }
     const int side = static_cast<int>(std::lround(std::sqrt(static_cast<double>(Tn))));
-    depthwise_glu<T>(ffh_.as<T>(), E, S, side, side, E, w.wdw.as<float>(), w.bdw.as<float>(), glu_.as<T>(), E / 2,
-                     st_);
+    {
+        ProfScope p(this, "depthwise_glu");
+        depthwise_glu<T>(ffh_.as<T>(), E, S, side, side, E, w.wdw.as<float>(), w.bdw.as<float>(), glu_.as<T>(), E / 2,
+                         st_);
+    }
     {
         Epilogue e = epi_out(x_ff, false, C);
         e.resid = x_cross;
@@ -470,6 +497,7 @@ void Engine::block_impl(int b, const float* x_in, float* x_self, float* x_cross,
         e.gate = mod_b + 5 * C;
         e.gate_ld = C6;
         e.rows_per_gate = Tn;
+        ProfScope p(this, "gemm_ff_point");
         gemm_act(glu_.get(), E / 2, w.wpt.get(), E / 2, M, C, E / 2, e);
     }
 }
@@ -515,24 +543,40 @@ void Engine::loop_body(const float* lat_in, int B, int H, int W, const float* en
     (void)Din;
     const int S = 2 * B, Tn = H * W, C = d_.C, Cl = d_.Cl, nb = d_.n_blocks;
     const size_t n_lat = static_cast<size_t>(B) * Cl * Tn;
-    caption_impl<T>(enc_d, S, L);
-    kv_all_impl<T>(S, L);
+    {
+        ProfScope p(this, "caption_projection");
+        caption_impl<T>(enc_d, S, L);
+    }
+    {
+        ProfScope p(this, "gemm_cross_kv");
+        kv_all_impl<T>(S, L);
+    }
     if (bias_d) caption_kv_len(bias_d, S, L, kvlen_.as<int>(), st_);
     SANA_CUDA(cudaMemcpyAsync(lat_.get(), lat_in, n_lat * 4, cudaMemcpyDeviceToDevice, st_));
     const size_t ckv_stride = static_cast<size_t>(S) * L * 2 * C;
     for (size_t step = 0; step < coefs.size(); ++step) {
-        broadcast_rows(tproj_table_.as<float>() + step * 256, S, 256, tproj_.as<float>(), st_);
-        time_embed_impl<T>(tproj_.as<float>(), S);
-        block_modulation(tmod_.as<float>(), S, C, tables_.as<float>(), nb, mods_.as<float>(), st_);
-        prologue_impl<T>(lat_.as<float>(), B, S, H, W);
+        {
+            ProfScope p(this, "timestep_embedding");
+            broadcast_rows(tproj_table_.as<float>() + step * 256, S, 256, tproj_.as<float>(), st_);
+            time_embed_impl<T>(tproj_.as<float>(), S);
+            block_modulation(tmod_.as<float>(), S, C, tables_.as<float>(), nb, mods_.as<float>(), st_);
+        }
+        {
+            ProfScope p(this, "patch_embed");
+            prologue_impl<T>(lat_.as<float>(), B, S, H, W);
+        }
         for (int b = 0; b < nb; ++b) {
             block_impl<T>(b, x_.as<float>(), x_.as<float>(), x_.as<float>(), x_.as<float>(), S, Tn, L,
                           mods_.as<float>() + static_cast<size_t>(b) * S * 6 * C, ckv_.as<T>() + b * ckv_stride, bias_d,
                           bias_d ? kvlen_.as<int>() : nullptr);
         }
-        epilogue_impl<T>(S, Tn);
+        {
+            ProfScope p(this, "final_layer");
+            epilogue_impl<T>(S, Tn);
+        }
         float* cur = hist_.as<float>() + (step % 2) * n_lat;
         const float* prev = hist_.as<float>() + ((step + 1) % 2) * n_lat;
+        ProfScope p(this, "cfg_scheduler");
         cfg_scheduler_step(noise_.as<float>(), B, Cl, Tn, lat_.as<float>(), cur, prev, coefs[step], st_);
     }
     SANA_CUDA(cudaMemcpyAsync(out_d, lat_.get(), n_lat * 4, cudaMemcpyDeviceToDevice, st_));
@@ -838,6 +882,64 @@ size_t Engine::debug_read(const std::string& name, size_t offset, size_t bytes, 
         SANA_CUDA(cudaStreamSynchronize(st_));
     }
     return b.bytes();
+}
+
+cudaEvent_t Engine::prof_event() {
+    cudaEvent_t e;
+    SANA_CUDA(cudaEventCreate(&e));
+    ev_pool_.push_back(e);
+    return e;
+}
+
+void Engine::profile_enable(bool on) {
+    SANA_CUDA(cudaStreamSynchronize(st_));
+    for (auto e : ev_pool_) cudaEventDestroy(e);
+    ev_pool_.clear();
+    prof_.clear();
+    prof_on_ = on;
+}
+
+std::string Engine::profile_report() {
+    SANA_CUDA(cudaStreamSynchronize(st_));
+    std::map<std::string, std::pair<int, double>> agg;
+    for (const auto& r : prof_) {
+        float ms = 0.f;
+        SANA_CUDA(cudaEventElapsedTime(&ms, r.a, r.b));
+        auto& a = agg[r.name];
+        a.first += 1;
+        a.second += ms;
+    }
+    std::ostringstream o;
+    o << "{";
+    bool first = true;
+    for (const auto& kv : agg) {
+        o << (first ? "" : ", ") << '"' << kv.first << "\": [" << kv.second.first << ", " << kv.second.second << "]";
+        first = false;
+    }
+    o << "}";
+    return o.str();
+}
+
+void Engine::profile_loop_device(const float* lat, int B, int H, int W, const float* enc, int L, int Din,
+                                 const float* bias, float guidance, int num_steps, float flow_shift, float* out) {
+    SANA_REQUIRE(have_w_, "weights have not been uploaded");
+    ensure_workspace(2 * B, H * W, L);
+    std::vector<float> ts, sg;
+    scheduler_schedule(num_steps, flow_shift, ts, sg);
+    std::vector<SchedCoef> coefs;
+    int lower = 0;
+    for (int i = 0; i < num_steps; ++i) {
+        coefs.push_back(scheduler_coefficients(sg, i, lower, guidance));
+        if (lower < 2) ++lower;
+    }
+    std::vector<float> table(static_cast<size_t>(num_steps) * 256);
+    for (int i = 0; i < num_steps; ++i) timestep_features(ts[i], table.data() + static_cast<size_t>(i) * 256);
+    SANA_CUDA(cudaMemcpyAsync(tproj_table_.get(), table.data(), table.size() * 4, cudaMemcpyHostToDevice, st_));
+    profile_enable(true);
+    if (mode_ == kModeBf16) loop_body<bf16>(lat, B, H, W, enc, L, Din, bias, coefs, out);
+    else loop_body<float>(lat, B, H, W, enc, L, Din, bias, coefs, out);
+    SANA_CUDA(cudaStreamSynchronize(st_));
+    prof_on_ = false;
 }
 
 }  // namespace sana

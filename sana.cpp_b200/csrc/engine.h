@@ -115,6 +115,14 @@ class Engine {
     void denoise_loop_device(const float* lat, int B, int H, int W, const float* enc, int L, int Din,
                              const float* bias, float guidance, int num_steps, float flow_shift, float* out);
 
+    // Per-kernel profiling of eager (uncaptured) work: CUDA events around every launch of the
+    // loop, summed per kernel class. enable() clears previous records.
+    void profile_enable(bool on);
+    std::string profile_report();  // JSON: {"kernel": [launches, total_ms], ...}
+    // Runs the denoising loop once eagerly with profiling on (device pointers).
+    void profile_loop_device(const float* lat, int B, int H, int W, const float* enc, int L, int Din,
+                             const float* bias, float guidance, int num_steps, float flow_shift, float* out);
+
     // Read-back of a named workspace buffer (diagnostics): a, qkv, ao, cq, xb, ffh, glu,
     // x, x1, x2, x3, mods, tmod, emb, ckv1, ctx, kvlen, noise, lat. Returns its size.
     size_t debug_read(const std::string& name, size_t offset, size_t bytes, void* host);
@@ -174,6 +182,40 @@ class Engine {
         int calls = 0;
     };
     std::map<std::string, GraphEntry> graphs_;
+
+    // profiling
+    friend class ProfScope;
+    bool prof_on_ = false;
+    struct ProfRec {
+        std::string name;
+        cudaEvent_t a, b;
+    };
+    std::vector<ProfRec> prof_;
+    std::vector<cudaEvent_t> ev_pool_;
+    cudaEvent_t prof_event();
+};
+
+// Records CUDA events around the launches in its scope when the engine profiles.
+class ProfScope {
+   public:
+    ProfScope(Engine* e, const char* name) : e_(e) {
+        if (e_->prof_on_) {
+            rec_.name = name;
+            rec_.a = e_->prof_event();
+            rec_.b = e_->prof_event();
+            cudaEventRecord(rec_.a, e_->st_);
+        }
+    }
+    ~ProfScope() {
+        if (e_->prof_on_) {
+            cudaEventRecord(rec_.b, e_->st_);
+            e_->prof_.push_back(rec_);
+        }
+    }
+
+   private:
+    Engine* e_;
+    Engine::ProfRec rec_{};
 };
 
 }  // namespace sana

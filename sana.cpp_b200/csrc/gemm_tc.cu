@@ -4,8 +4,9 @@
 //
 //   warp 0      TMA producer (one lane): A tile [128 x 64] and B tile [BN x 64] per stage
 //   warp 1      TMEM allocator + MMA issuer (one lane): 4 x (128 x BN x 16) MMAs per stage
-//   warps 2..5  epilogue: tcgen05.ld of their 32-lane TMEM quarter, bias/act/gate/residual,
-//               stores to global
+//   warps 2..9  epilogue: two warps per 32-lane TMEM quarter, each taking half of the tile's
+//               columns; tcgen05.ld, bias/act/gate/residual, stores to global, with the
+//               residual / gate of the next 16 columns fetched while the current ones finish
 // Two TMEM accumulators (2 x BN fp32 columns) let the epilogue of one tile overlap the
 // MMAs of the next. Every mbarrier wait is bounded (common.cuh); on expiry the kernel
 // records kTimeout in the device error word, drains its own TMA copies and MMAs with
@@ -116,11 +117,60 @@ __device__ __forceinline__ void store_val(void* out, int is_bf16, long long idx,
     }
 }
 
-// Applies the epilogue to 16 consecutive columns [n0, n0+16) of one row.
-__device__ __forceinline__ void epilogue16(const Epilogue& ep, int row, int n0, int N, float (&v)[16],
-                                           bool vec) {
+// SiLU for the tensor-core path's epilogue (bf16 outputs only): CUDA's fast exponential and
+// a correctly rounded reciprocal.
+__device__ __forceinline__ float silu_fast(float x) { return x * __frcp_rn(1.0f + __expf(-x)); }
+
+// Residual and gate values of 16 consecutive columns [n0, n0+16) of one row, fetched one
+// chunk ahead of their use so the epilogue does not wait on global-memory latency.
+struct Side16 {
+    float r[16];
+    float g[16];
+};
+
+__device__ __forceinline__ void fetch16(const Epilogue& ep, int row, int n0, int N, bool vec, Side16& sd) {
+    if (!ep.resid) return;
     if (vec && n0 + 16 <= N) {
-        if (ep.bias) {
+        const float* r = ep.resid + static_cast<long long>(row) * ep.ldr + n0;
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(r + j);
+            sd.r[j] = v.x;
+            sd.r[j + 1] = v.y;
+            sd.r[j + 2] = v.z;
+            sd.r[j + 3] = v.w;
+        }
+        if (ep.gate) {
+            const float* g = ep.gate + static_cast<long long>(row / ep.rows_per_gate) * ep.gate_ld + n0;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+                const float4 v = *reinterpret_cast<const float4*>(g + j);
+                sd.g[j] = v.x;
+                sd.g[j + 1] = v.y;
+                sd.g[j + 2] = v.z;
+                sd.g[j + 3] = v.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) sd.g[j] = 1.f;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int n = n0 + j;
+            sd.r[j] = n < N ? ep.resid[static_cast<long long>(row) * ep.ldr + n] : 0.f;
+            sd.g[j] = (n < N && ep.gate) ? ep.gate[static_cast<long long>(row / ep.rows_per_gate) * ep.gate_ld + n]
+                                         : 1.f;
+        }
+    }
+}
+
+// Applies the epilogue to 16 consecutive columns [n0, n0+16) of one row.
+__device__ __forceinline__ void epilogue16(const Epilogue& ep, int row, int n0, int N, float (&v)[16], bool vec,
+                                           const Side16& sd) {
+    const bool full = vec && n0 + 16 <= N;
+    if (ep.bias) {
+        if (full) {
 #pragma unroll
             for (int j = 0; j < 16; j += 4) {
                 const float4 b = *reinterpret_cast<const float4*>(ep.bias + n0 + j);
@@ -129,29 +179,24 @@ __device__ __forceinline__ void epilogue16(const Epilogue& ep, int row, int n0, 
                 v[j + 2] += b.z;
                 v[j + 3] += b.w;
             }
-        }
-        if (ep.act == kActSilu) {
+        } else {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = silu(v[j]);
-        } else if (ep.act == kActGelu) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = gelu_tanh(v[j]);
+            for (int j = 0; j < 16; ++j)
+                if (n0 + j < N) v[j] += ep.bias[n0 + j];
         }
-        if (ep.resid) {
-            const float* r = ep.resid + static_cast<long long>(row) * ep.ldr + n0;
-            const float* g = ep.gate ? ep.gate + static_cast<long long>(row / ep.rows_per_gate) * ep.gate_ld + n0
-                                     : nullptr;
+    }
+    if (ep.act == kActSilu) {
 #pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-                const float4 rv = *reinterpret_cast<const float4*>(r + j);
-                float4 gv = make_float4(1.f, 1.f, 1.f, 1.f);
-                if (g) gv = *reinterpret_cast<const float4*>(g + j);
-                v[j] = rv.x + gv.x * v[j];
-                v[j + 1] = rv.y + gv.y * v[j + 1];
-                v[j + 2] = rv.z + gv.z * v[j + 2];
-                v[j + 3] = rv.w + gv.w * v[j + 3];
-            }
-        }
+        for (int j = 0; j < 16; ++j) v[j] = silu_fast(v[j]);
+    } else if (ep.act == kActGelu) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = gelu_tanh(v[j]);
+    }
+    if (ep.resid) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = sd.r[j] + sd.g[j] * v[j];
+    }
+    if (full) {
         void* outs[2] = {ep.out, ep.out2};
         const int bfs[2] = {ep.out_bf16, ep.out2_bf16};
         const long long lds[2] = {ep.ldo, ep.ldo2};
@@ -186,14 +231,7 @@ __device__ __forceinline__ void epilogue16(const Epilogue& ep, int row, int n0, 
     for (int j = 0; j < 16; ++j) {
         const int n = n0 + j;
         if (n >= N) break;
-        float x = v[j];
-        if (ep.bias) x += ep.bias[n];
-        if (ep.act == kActSilu) x = silu(x);
-        else if (ep.act == kActGelu) x = gelu_tanh(x);
-        if (ep.resid) {
-            const float g = ep.gate ? ep.gate[static_cast<long long>(row / ep.rows_per_gate) * ep.gate_ld + n] : 1.0f;
-            x = ep.resid[static_cast<long long>(row) * ep.ldr + n] + g * x;
-        }
+        const float x = v[j];
         if (ep.out) store_val(ep.out, ep.out_bf16, static_cast<long long>(row) * ep.ldo + n, x);
         if (ep.out2) store_val(ep.out2, ep.out2_bf16, static_cast<long long>(row) * ep.ldo2 + n,
                                ep.act2 == kActSilu ? silu(x) : x);
@@ -201,8 +239,11 @@ __device__ __forceinline__ void epilogue16(const Epilogue& ep, int row, int n0, 
 }
 
 // --- the kernel ------------------------------------------------------------------------
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 32 * (2 + kEpiWarps);
+
 template <int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
                    int N, int K, Epilogue ep, int vec, int* err) {
     using C = Cfg<BN>;
@@ -235,7 +276,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull(a), 1);
-            mbar_init(tempty(a), 4);
+            mbar_init(tempty(a), kEpiWarps);
         }
         mbar_init(done_bar, 1);
         fence_barrier_init();
@@ -326,7 +367,9 @@ __global__ void __launch_bounds__(192, 1)
             mbar_wait_quiet(done_bar, 0u);
         }
     } else {
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int q = warp & 3;                   // TMEM lane quarter this warp may access
+        const int chalf = (warp - 2) / 4;         // which half of the tile's columns
+        constexpr int kChunks = BN / 2 / 16;      // 16-column chunks per warp
         int local = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const int acc = local & 1;
@@ -336,18 +379,24 @@ __global__ void __launch_bounds__(192, 1)
             const int m_blk = tile % num_m;
             const int n_blk = tile / num_m;
             const int row = m_blk * BM + q * 32 + lane;
-            const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-#pragma unroll 1
-            for (int c = 0; c < BN; c += 16) {
+            const bool row_ok = row < M;
+            const int col0 = chalf * (BN / 2);
+            const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN + col0);
+            Side16 sd[2];
+            if (row_ok && n_blk * BN + col0 < N) fetch16(ep, row, n_blk * BN + col0, N, vec != 0, sd[0]);
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c) {
+                const int n0 = n_blk * BN + col0 + c * 16;
+                if (c + 1 < kChunks && row_ok && n0 + 16 < N) fetch16(ep, row, n0 + 16, N, vec != 0, sd[(c + 1) & 1]);
                 uint32_t r[16];
-                tmem_ld16(t_row + static_cast<uint32_t>(c), r);
+                tmem_ld16(t_row + static_cast<uint32_t>(c * 16), r);
                 tmem_wait_ld();
-                const int n0 = n_blk * BN + c;
-                if (row < M && n0 < N) {
+                if (row_ok && n0 < N) {
                     float v[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-                    epilogue16(ep, row, n0, N, v, vec != 0);
+                    epilogue16(ep, row, n0, N, v, vec != 0, sd[c & 1]);
                 }
             }
             tc_fence_before();
@@ -420,7 +469,7 @@ static void launch(const GemmProblem& p, int* err, cudaStream_t stream, int num_
     if (e.out2) vec = vec && a16(e.out2) && (e.ldo2 % 8 == 0);
     const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    gemm_tc_kernel<BN><<<grid, 192, C::kSmemBytes, stream>>>(ma, mb, p.M, p.N, p.K, e, vec ? 1 : 0, err);
+    gemm_tc_kernel<BN><<<grid, kThreads, C::kSmemBytes, stream>>>(ma, mb, p.M, p.N, p.K, e, vec ? 1 : 0, err);
     SANA_CUDA(cudaGetLastError());
 }
 

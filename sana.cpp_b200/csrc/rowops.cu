@@ -60,6 +60,70 @@ __global__ void ln_modulate_kernel(const float* __restrict__ x, long long rows, 
     }
 }
 
+// Row in registers (C = 128 * NV): one warp per row, each lane holding NV float4 of the
+// row; mean, then the centred variance from the registers, then the normalised, modulated
+// row written with 8-byte (bf16) or 16-byte (fp32) stores.
+template <class TO, int NV>
+__global__ void ln_modulate_reg_kernel(const float* __restrict__ x, long long rows, int rows_per_seq,
+                                       const float* __restrict__ gamma, const float* __restrict__ beta,
+                                       const float* __restrict__ mod, long long mod_ld, int shift_idx, int scale_idx,
+                                       float eps, TO* __restrict__ out) {
+    constexpr int C = 128 * NV;
+    const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float4* xr = reinterpret_cast<const float4*>(x + row * C);
+    float4 v[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = xr[lane + 32 * i];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    const float mean = warp_sum(s) / static_cast<float>(C);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+        q += (a * a + b * b) + (c * c + d * d);
+    }
+    const float var = warp_sum(q) / static_cast<float>(C);
+    const float inv_std = 1.0f / sqrtf(var + eps);
+    const long long seq = row / rows_per_seq;
+    const float* shift = mod ? mod + seq * mod_ld + static_cast<long long>(shift_idx) * C : nullptr;
+    const float* scale = mod ? mod + seq * mod_ld + static_cast<long long>(scale_idx) * C : nullptr;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int c = 4 * (lane + 32 * i);
+        float o[4] = {(v[i].x - mean) * inv_std, (v[i].y - mean) * inv_std, (v[i].z - mean) * inv_std,
+                      (v[i].w - mean) * inv_std};
+        if (gamma) {
+            const float4 g = *reinterpret_cast<const float4*>(gamma + c);
+            o[0] *= g.x; o[1] *= g.y; o[2] *= g.z; o[3] *= g.w;
+        }
+        if (beta) {
+            const float4 bb = *reinterpret_cast<const float4*>(beta + c);
+            o[0] += bb.x; o[1] += bb.y; o[2] += bb.z; o[3] += bb.w;
+        }
+        if (mod) {
+            const float4 sc = *reinterpret_cast<const float4*>(scale + c);
+            const float4 sh = *reinterpret_cast<const float4*>(shift + c);
+            o[0] = o[0] * (1.0f + sc.x) + sh.x;
+            o[1] = o[1] * (1.0f + sc.y) + sh.y;
+            o[2] = o[2] * (1.0f + sc.z) + sh.z;
+            o[3] = o[3] * (1.0f + sc.w) + sh.w;
+        }
+        if constexpr (sizeof(TO) == 2) {
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(o[0], o[1]), h1 = __floats2bfloat162_rn(o[2], o[3]);
+            uint2 pk;
+            pk.x = *reinterpret_cast<uint32_t*>(&h0);
+            pk.y = *reinterpret_cast<uint32_t*>(&h1);
+            *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(out) + row * C + c) = pk;
+        } else {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + row * C + c) = make_float4(o[0], o[1], o[2], o[3]);
+        }
+    }
+}
+
 template <class TO>
 __global__ void rms_norm_kernel(const float* __restrict__ x, long long rows, int C, float eps,
                                 const float* __restrict__ w, TO* __restrict__ out) {
@@ -232,8 +296,26 @@ void ln_modulate(const float* x, long long rows, int C, int rows_per_seq, const 
                  cudaStream_t st) {
     if (rows == 0) return;
     const int warps = 8;
-    ln_modulate_kernel<TO><<<static_cast<unsigned>((rows + warps - 1) / warps), warps * 32, 0, st>>>(
-        x, rows, C, rows_per_seq, gamma, beta, mod, mod_ld, shift_idx, scale_idx, eps, out);
+    const unsigned grid = static_cast<unsigned>((rows + warps - 1) / warps);
+    auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const bool reg = C % 128 == 0 && C / 128 <= 12 && a16(x) && a16(out) && (!gamma || a16(gamma)) &&
+                     (!beta || a16(beta)) && (!mod || (a16(mod) && mod_ld % 4 == 0));
+    if (reg) {
+        switch (C / 128) {
+#define SANA_LN_CASE(NV)                                                                                        \
+    case NV:                                                                                                    \
+        ln_modulate_reg_kernel<TO, NV><<<grid, warps * 32, 0, st>>>(x, rows, rows_per_seq, gamma, beta, mod, mod_ld, \
+                                                                    shift_idx, scale_idx, eps, out);           \
+        SANA_CUDA(cudaGetLastError());                                                                          \
+        return;
+            SANA_LN_CASE(1) SANA_LN_CASE(2) SANA_LN_CASE(3) SANA_LN_CASE(4) SANA_LN_CASE(5) SANA_LN_CASE(6)
+            SANA_LN_CASE(7) SANA_LN_CASE(8) SANA_LN_CASE(9) SANA_LN_CASE(10) SANA_LN_CASE(11) SANA_LN_CASE(12)
+#undef SANA_LN_CASE
+            default: break;
+        }
+    }
+    ln_modulate_kernel<TO><<<grid, warps * 32, 0, st>>>(x, rows, C, rows_per_seq, gamma, beta, mod, mod_ld, shift_idx,
+                                                        scale_idx, eps, out);
     SANA_CUDA(cudaGetLastError());
 }
 

@@ -214,6 +214,18 @@ class SanaCuda:
         self._call("sana_cuda_denoise_loop_device", vp(lat_ptr), _i(B), _i(H), _i(W), vp(enc_ptr), _i(L), _i(Din),
                    vp(bias_ptr) if bias_ptr else None, _f(guidance), _i(num_steps), _f(flow_shift), vp(out_ptr))
 
+    def profile_loop_device(self, lat_ptr: int, B: int, H: int, W: int, enc_ptr: int, L: int, Din: int,
+                            bias_ptr: Optional[int], out_ptr: int, guidance: float = 4.5, num_steps: int = 20,
+                            flow_shift: float = 3.0) -> dict:
+        """One eager loop with CUDA events around every launch: {kernel class: (launches, ms)}."""
+        import json
+        vp = ctypes.c_void_p
+        buf = ctypes.create_string_buffer(1 << 16)
+        self._call("sana_cuda_profile_loop", vp(lat_ptr), _i(B), _i(H), _i(W), vp(enc_ptr), _i(L), _i(Din),
+                   vp(bias_ptr) if bias_ptr else None, _f(guidance), _i(num_steps), _f(flow_shift), vp(out_ptr), buf,
+                   ctypes.c_size_t(len(buf)))
+        return {k: tuple(v) for k, v in json.loads(buf.value.decode()).items()}
+
     def denoise_step(self, latents, context, bias, guidance, timestep, sigmas, step_index, lower, history):
         """Returns (latents, step_index, lower, history list)."""
         lat = _f32(latents).copy()
