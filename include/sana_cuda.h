@@ -214,6 +214,33 @@ int sana_op_gemm_device(sana_cuda_ctx *ctx, const void *A, const void *B, int M,
 int sana_op_linear_attention_device(sana_cuda_ctx *ctx, const void *qkv, int S, int T, int heads, int D,
                                     float *partial, void *out);
 size_t sana_op_linear_attention_workspace(int S, int T, int heads, int D);
+
+/* Size of the fixed scratch behind sana_op_linear_attention_noalloc (8 MiB). */
+#define SANA_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+
+/* sana_op_linear_attention_device without the workspace argument, and without any device
+ * allocation: the fp32 scratch comes from one fixed array of SANA_NOALLOC_SCRATCH_BYTES
+ * built into this library's device image. There is no counterpart in the reference (its
+ * linear_attention_4d allocates its intermediates on the host); it is an addition for
+ * callers that cannot allocate device memory at the point of the call and have no
+ * workspace of their own to lend: a host that has already handed its device memory to its
+ * own pool allocator, or a tight loop where cudaMalloc/cudaFree would stall it (cudaFree
+ * synchronises the whole device). Inputs, output and results are those of
+ * sana_op_linear_attention_device; the work is queued on the handle's stream.
+ *  - Limit: sana_op_linear_attention_workspace(S, T, heads, D) must not exceed
+ *    SANA_NOALLOC_SCRATCH_BYTES (two 1024-token sequences fit, at 36 x 32 or 16 x 72 heads).
+ *    Larger shapes return SANA_ERR_INVALID, with the sizes in sana_cuda_last_error(), and
+ *    launch nothing.
+ *  - First call on each device: it looks up the scratch's device address, with the handle's
+ *    device made current for the call, and the CUDA runtime may load this library's device
+ *    code there at that moment. Make that first call before any stream capture begins.
+ *  - Nothing in the scratch has to start at zero: every call writes each scratch word
+ *    before reading it.
+ *  - All handles, streams and host threads on one device share the one scratch. Two calls
+ *    whose GPU work can overlap (different streams or handles with no ordering between
+ *    them) race on it and give wrong results: keep such calls on one stream, or order them
+ *    with events. */
+int sana_op_linear_attention_noalloc(sana_cuda_ctx *ctx, const void *qkv, int S, int T, int heads, int D, void *out);
 /* depthwise_conv2d_3x3 + GLU gate on NHWC rows [S*H*W, E] -> [S*H*W, E/2]; w [E, 9], b [E] fp32. */
 int sana_op_depthwise_glu_device(sana_cuda_ctx *ctx, const void *in, int S, int H, int W, int E, const float *w,
                                  const float *b, void *out);

@@ -2,6 +2,7 @@
 #include <cstdio>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <new>
 #include <random>
 #include <string>
@@ -196,6 +197,46 @@ void d2h(void* host, const void* dev, size_t bytes) {
     SANA_CUDA(cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, tl_stream));
     SANA_CUDA(cudaStreamSynchronize(tl_stream));
 }
+
+}  // namespace
+
+// --- fixed scratch of sana_op_linear_attention_noalloc ----------------------------------
+// One array per device, part of this library's device image: it holds 8 MiB of a device's
+// memory from the time the CUDA runtime loads this library's device code there. Every
+// handle, stream and host thread on a device shares it.
+static __device__ __align__(256) float g_linattn_scratch[SANA_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+namespace {
+
+constexpr int kScratchMaxDevices = 64;
+std::mutex g_scratch_mu;
+float* g_scratch_addr[kScratchMaxDevices] = {};
+
+// The device address of g_linattn_scratch on `device`, which the caller has made current.
+// Looked up on the first call per device and remembered.
+float* linattn_scratch(int device) {
+    SANA_REQUIRE(device >= 0 && device < kScratchMaxDevices, "device ordinal out of range for the fixed scratch");
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_addr[device]) {
+        void* p = nullptr;
+        SANA_CUDA(cudaGetSymbolAddress(&p, g_linattn_scratch));
+        g_scratch_addr[device] = static_cast<float*>(p);
+    }
+    return g_scratch_addr[device];
+}
+
+// Makes `device` current for the lifetime of the guard and restores the previous one.
+struct CurrentDevice {
+    int prev = -1;
+    explicit CurrentDevice(int device) {
+        SANA_CUDA(cudaGetDevice(&prev));
+        if (prev != device) SANA_CUDA(cudaSetDevice(device));
+    }
+    ~CurrentDevice() {
+        int now = -1;
+        if (cudaGetDevice(&now) == cudaSuccess && now != prev) cudaSetDevice(prev);
+    }
+};
 
 }  // namespace
 
@@ -759,6 +800,27 @@ int sana_op_linear_attention_device(sana_cuda_ctx* ctx, const void* qkv, int S, 
 
 size_t sana_op_linear_attention_workspace(int S, int T, int heads, int D) {
     return static_cast<size_t>(S) * heads * (sana::linattn_chunks(T) + 1) * (D + 1) * D * sizeof(float);
+}
+
+int sana_op_linear_attention_noalloc(sana_cuda_ctx* ctx, const void* qkv, int S, int T, int heads, int D,
+                                     void* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(qkv && out && S >= 1 && T >= 1 && heads >= 1 && D >= 1 && D <= 128, "invalid arguments");
+        // in double: the product of the four factors can overflow size_t for absurd inputs
+        const double need = static_cast<double>(S) * heads * (sana::linattn_chunks(T) + 1) * (D + 1) * D * 4.0;
+        if (need > static_cast<double>(SANA_NOALLOC_SCRATCH_BYTES))
+            throw sana::InvalidArg("linear attention scratch of " + std::to_string(static_cast<long long>(need)) +
+                                   " bytes exceeds the fixed " + std::to_string(SANA_NOALLOC_SCRATCH_BYTES) +
+                                   "-byte scratch of sana_op_linear_attention_noalloc; pass a workspace to "
+                                   "sana_op_linear_attention_device instead");
+        sana::Engine& eng = engine(ctx);
+        CurrentDevice on(eng.device());
+        float* scratch = linattn_scratch(eng.device());
+        const int C = heads * D;
+        const bf16* q = static_cast<const bf16*>(qkv);
+        sana::linear_attention<bf16>(q, 3LL * C, 0, q, 3LL * C, C, 2 * C, S, T, T, heads, D, scratch,
+                                     static_cast<bf16*>(out), C, eng.stream());
+    });
 }
 
 int sana_op_depthwise_glu_device(sana_cuda_ctx* ctx, const void* in, int S, int H, int W, int E, const float* w,

@@ -131,6 +131,7 @@ class Engine {
     void check_device_error();
     int* err() const { return err_.as<int>(); }
     int num_sms() const { return num_sms_; }
+    int device() const { return device_; }
 
    private:
     template <class T> void upload_impl(const float* const* model, const float* const* blocks, int layout);
