@@ -7,8 +7,10 @@ Workload (per GPU): 16 images x CFG (32 sequences of 1024 t
 20-step DPM-Solver++ loop with guidance 4.5, caption states [300, 2304] with valid lengths
 drawn from 8..120; seeded random-init weights of the real architecture (synthetic: there
 are no checkpoints or datasets here). Each rank denoises its own 16 images, weights
-replicated; the final latents of all ranks are NCCL-gathered each step (the path's only
-collective), so per-GPU work is fixed as N grows ("weak" scaling).
+replicated; the final latents of all ranks are NCCL-gathered after each loop (the path's
+only collective), so per-GPU work is fixed as N grows ("weak" scaling).
+
+    python bench.py --microbench [--op NAME,...]     (one GPU)
 
 One bench step = one full denoising loop over the rank's batch (caption projection,
 cross-K/V for all blocks, 20 denoiser steps, CFG + scheduler), replayed from a CUDA graph.
@@ -264,6 +266,108 @@ def gemm_roofline(g, torch, stream, M, peak_tflops):
     return achieved, per
 
 
+MICRO_OPS = ("qkv_gemm", "linear_attention_16x72", "linear_attention_36x32", "depthwise_glu", "cross_attention",
+             "ff_inverted_config2")
+
+
+def run_microbench(args):
+    """BASELINE configs[4], the op-level microbenchmark: 4096 tokens, batch 2, hidden 1152,
+    bf16 activations N(0,1), each op through its device entry point of the C ABI and against
+    its roofline: (a) ReLU linear attention 16 x 72 (and the model's 36 x 32), (b) depthwise
+    3x3 + SiLU-GLU on 5760 -> 2880 channels, (c) the QKV projection M=8192, K=1152, N=3456,
+    (d) cross-attention to 300 unmasked caption tokens. Also the step's largest kernel at
+    config-2 size: the FF-inverted projection M=32768, K=1152, N=5760 with bias and SiLU.
+    L2 is flushed (256 MiB write, untimed) before every timed launch; the median of --steps
+    launches is reported. One JSON line per op."""
+    import ctypes
+    import torch
+    from sana_b200 import SANA_MODE_BF16, SanaCuda
+    pk, pk_kind = peaks()
+    ops = MICRO_OPS if not args.op else tuple(args.op.split(","))
+    bad = [o for o in ops if o not in MICRO_OPS]
+    if bad:
+        raise SystemExit(f"unknown --op {bad}; choose from {MICRO_OPS}")
+    torch.cuda.set_device(0)
+    g = SanaCuda(0, SANA_MODE_BF16)
+    g.lib.sana_op_linear_attention_workspace.restype = ctypes.c_size_t
+    st = torch.cuda.Stream()
+    g.set_stream(st.cuda_stream)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    vp, I = ctypes.c_void_p, ctypes.c_int
+    S, T, C, E, L = 2, 4096, 1152, 5760, CAPTION_LEN
+    gen = torch.Generator(device="cpu").manual_seed(4)
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, generator=gen) * scale).to(device="cuda", dtype=torch.bfloat16)
+
+    def timed(fn):
+        times = []
+        with torch.cuda.stream(st):
+            for _ in range(args.warmup):
+                fn()
+            for _ in range(args.steps):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                fn()
+                e1.record(st)
+                e1.synchronize()
+                times.append(e0.elapsed_time(e1))
+        return statistics.median(times)
+
+    def report(name, what, ms, work, bound):
+        if bound == "hbm":
+            ach, peak, unit = work / ms / 1e6, pk["hbm_gbs"], "GB/s"
+        else:
+            ach, peak, unit = work / ms / 1e9, pk["bf16_tflops"], "TFLOP/s"
+        print(json.dumps({"microbench": name, "workload": what, "ms": round(ms, 4), "bound": bound,
+                          "algorithmic": work, "achieved": round(ach, 1), "peak": peak, "unit": unit,
+                          "frac": round(ach / peak, 3), "peak_source": f"{pk_kind} (burst: op timed alone)",
+                          "steps": args.steps, "warmup": args.warmup, "l2": "flushed before every launch"}),
+              flush=True)
+
+    for name in ops:
+        if name.startswith("linear_attention"):
+            heads, D = (16, 72) if name.endswith("16x72") else (36, 32)
+            qkv = rnd(S * T, 3 * C)
+            part = torch.empty(g.lib.sana_op_linear_attention_workspace(I(S), I(T), I(heads), I(D)) // 4,
+                               device="cuda", dtype=torch.float32)
+            out = torch.empty(S * T, C, device="cuda", dtype=torch.bfloat16)
+            ms = timed(lambda: g._call("sana_op_linear_attention_device", vp(qkv.data_ptr()), I(S), I(T), I(heads),
+                                       I(D), vp(part.data_ptr()), vp(out.data_ptr())))
+            report(name, f"q,k,v [{S},{heads},{T},{D}] bf16 -> o", ms, 2.0 * S * T * 4 * C, "hbm")
+        elif name == "depthwise_glu":
+            h = rnd(S * T, E)
+            w = (torch.randn(E * 9, generator=gen) * 0.02).cuda()
+            b = torch.zeros(E, device="cuda")
+            out = torch.empty(S * T, E // 2, device="cuda", dtype=torch.bfloat16)
+            ms = timed(lambda: g._call("sana_op_depthwise_glu_device", vp(h.data_ptr()), I(S), I(64), I(64), I(E),
+                                       vp(w.data_ptr()), vp(b.data_ptr()), vp(out.data_ptr())))
+            report(name, f"[{S},64,64,{E}] -> [{S},64,64,{E // 2}] bf16", ms, 2.0 * S * T * (E + E // 2), "hbm")
+        elif name == "qkv_gemm":
+            M, N, K = S * T, 3 * C, C
+            A, B = rnd(M, K), rnd(N, K, scale=0.02)
+            out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            ms = timed(lambda: g.gemm_device(A.data_ptr(), B.data_ptr(), M, N, K, out.data_ptr()))
+            report(name, f"M={M} K={K} N={N} bf16 -> bf16", ms, 2.0 * M * N * K, "tensor")
+        elif name == "ff_inverted_config2":
+            M, N, K = 32 * 1024, E, C
+            A, B = rnd(M, K), rnd(N, K, scale=0.02)
+            bias = torch.zeros(N, device="cuda")
+            out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            ms = timed(lambda: g.gemm_device(A.data_ptr(), B.data_ptr(), M, N, K, out.data_ptr(), bias.data_ptr(), 1))
+            report(name, f"M={M} K={K} N={N} +bias, SiLU, bf16 out", ms, 2.0 * M * N * K, "tensor")
+        elif name == "cross_attention":
+            heads, D = 16, 72
+            q, kv = rnd(S * T, C), rnd(S * L, 2 * C)
+            kvl = torch.empty(S, device="cuda", dtype=torch.int32)
+            out = torch.empty(S * T, C, device="cuda", dtype=torch.bfloat16)
+            ms = timed(lambda: g._call("sana_op_cross_attention_device", vp(q.data_ptr()), vp(kv.data_ptr()), None,
+                                       vp(kvl.data_ptr()), I(S), I(T), I(L), I(heads), I(D), vp(out.data_ptr())))
+            report(name, f"q [{S},{heads},{T},{D}], k/v {L} keys, no mask", ms, 4.0 * S * T * L * C, "tensor")
+    g.close()
+
+
 def run_cuda(args):
     import torch
     import torch.distributed as dist
@@ -439,8 +543,13 @@ def main():
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--images", type=int, default=16, help="images (x2 CFG sequences) per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--microbench", action="store_true",
+                    help="op-level microbenchmark (BASELINE configs[4]) instead of the loop; one GPU")
+    ap.add_argument("--op", default="", help="with --microbench: comma-separated subset of " + ",".join(MICRO_OPS))
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.microbench:
+        run_microbench(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_cuda(args)

@@ -85,6 +85,35 @@ def test_cuda_core_gemm_fp32(gpu_f32, M, K, N):
     assert rel_err(out, ref) < 1e-6
 
 
+@pytest.mark.parametrize("act", [1, 2], ids=["silu", "gelu_tanh"])
+def test_gemm_activation_epilogue(gpu_bf16, act):
+    """Bias + SiLU / GELU-tanh fused into the tensor-core epilogue (the FF-inverted and
+    caption projections), over pre-activations from -120 to 120: every bf16 output within
+    its own rounding (2^-8 relative) of the float64 activation of the same bf16 product."""
+    import torch
+    M, K, N = 256, 64, 384
+    rng = np.random.default_rng(act)
+    x = bf16_round(rng.standard_normal((M, K)).astype(np.float32))
+    w = bf16_round((rng.standard_normal((N, K)) * 0.3).astype(np.float32))
+    b = np.linspace(-120, 120, N).astype(np.float32)
+    pre = x.astype(np.float64) @ w.astype(np.float64).T + b
+    if act == 1:
+        ref = pre / (1 + np.exp(-pre))
+    else:
+        ref = 0.5 * pre * (1 + np.tanh(np.sqrt(2 / np.pi) * (pre + 0.044715 * pre ** 3)))
+    A = torch.from_numpy(x).to("cuda", torch.bfloat16)
+    B = torch.from_numpy(w).to("cuda", torch.bfloat16)
+    bias = torch.from_numpy(b).cuda()
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    gpu_bf16.gemm_device(A.data_ptr(), B.data_ptr(), M, N, K, out.data_ptr(), bias.data_ptr(), act)
+    gpu_bf16.synchronize()
+    got = out.float().cpu().numpy().astype(np.float64)
+    err = np.abs(got - ref)
+    bound = 2.0 ** -8 * np.abs(ref) + 1e-6
+    assert (err <= bound).all(), float((err / bound).max())
+
+
 def test_gemm_repeatable(gpu_bf16):
     rng = np.random.default_rng(5)
     x = rng.standard_normal((1024, 1152)).astype(np.float32)
