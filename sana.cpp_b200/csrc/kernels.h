@@ -92,6 +92,11 @@ void convert(const float* src, long long n, TO* dst, cudaStream_t st);
 // q rows at column q_off + h*D of `q` (stride ldq); k and v rows of `kv` (stride ldkv).
 // partial must hold S * heads * (linattn_chunks(Tk) + 1) * (D + 1) * D floats.
 int linattn_chunks(int T);
+// bf16 tensor-core path of linear_attention (head_dim 32, 64 or 72, 16-byte aligned rows);
+// returns false, launching nothing, when the shape or alignment does not fit it.
+bool linattn_mma(const bf16* q, long long ldq, int q_off, const bf16* kv, long long ldkv, int k_off, int v_off,
+                 int S, int Tq, int Tk, int heads, int D, float* partial, bf16* out, long long ldo,
+                 cudaStream_t st);
 template <class T>
 void linear_attention(const T* q, long long ldq, int q_off, const T* kv, long long ldkv, int k_off, int v_off,
                       int S, int Tq, int Tk, int heads, int D, float* partial, T* out, long long ldo,

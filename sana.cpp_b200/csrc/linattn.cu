@@ -410,6 +410,7 @@ template <>
 bool linattn_bf16_path<bf16>(const bf16* q, long long ldq, int q_off, const bf16* kv, long long ldkv, int k_off,
                              int v_off, int S, int Tq, int Tk, int heads, int D, float* partial, bf16* out,
                              long long ldo, int chunks, int width, cudaStream_t st) {
+    if (linattn_mma(q, ldq, q_off, kv, ldkv, k_off, v_off, S, Tq, Tk, heads, D, partial, out, ldo, st)) return true;
     auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     if (D % 8 != 0 || (D != 32 && D != 64 && D != 72) || ldq % 8 || ldkv % 8 || ldo % 8 || q_off % 8 || k_off % 8 ||
         v_off % 8 || !a16(q) || !a16(kv) || !a16(out) || Tk <= 0)
