@@ -65,6 +65,23 @@ template <> __device__ __forceinline__ bf16 from_f<bf16>(float v) { return __flo
 // Elementwise activations. SiLU is x / (1 + e^-x) as tensor.cpp:551-555; GELU is the tanh
 // form of transformer_ops.cpp:15-18. Both call CUDA's own expf / tanhf.
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+// 1/y for finite y >= 1 without the special-function unit: the integer-subtraction estimate
+// (subtracting the float's bit pattern from a constant near twice the exponent bias negates
+// the exponent and linearly approximates the mantissa's reciprocal, within 5.1 %), refined
+// by two Newton-Raphson steps r <- r (2 - y r), each squaring the relative error
+// (5.1e-2 -> 2.6e-3 -> 6.6e-6: far below the rounding of the bf16 output it feeds).
+__device__ __forceinline__ float rcp_newton(float y) {
+    float r = __int_as_float(0x7EF311C3 - __float_as_int(y));
+    r = r * fmaf(-y, r, 2.0f);
+    return r * fmaf(-y, r, 2.0f);
+}
+
+// SiLU with one special-function operation per element (the exponential): the FF-inverted
+// projection's epilogue and the depthwise GLU gate are otherwise limited by that unit.
+// Inputs below -80 are clamped: e^80 keeps 1 + e^-x finite, and silu(x) there is below
+// 1e-33 either way.
+__device__ __forceinline__ float silu_fast(float x) { return x * rcp_newton(1.0f + __expf(-fmaxf(x, -80.0f))); }
+
 __device__ __forceinline__ float gelu_tanh(float x) {
     const float alpha = sqrtf(2.0f / 3.14159265358979323846f);  // as transformer_ops.cpp:16
     return 0.5f * x * (1.0f + tanhf(alpha * (x + 0.044715f * x * x * x)));

@@ -4,36 +4,20 @@
 // bias last; glumb_conv's split and gate, common_ops.cpp:745-758).
 //
 // The input is the SiLU-ed output of the inverted 1x1 conv, already token-major, so the
-// reference's NCHW round trips (tokens_to_grid_4d / grid_to_tokens_3d) disappear. Each
-// thread produces 8 consecutive output channels of one pixel with 128-bit loads of the 9
-// taps of the data and gate halves; neighbouring pixels' re-reads are served by L1/L2,
-// so DRAM traffic stays at one read of the input and one write of the output.
+// reference's NCHW round trips (tokens_to_grid_4d / grid_to_tokens_3d) disappear.
 #include "kernels.h"
 
 namespace sana {
 namespace {
 
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 v = __bfloat1622float2(h[i]);
-        f[2 * i] = v.x;
-        f[2 * i + 1] = v.y;
-    }
-}
-
 // bf16 tiled path (half % 8 == 0, 16-byte aligned rows, W <= kTileW). A block owns 64
 // channels of both halves and kTileRows full image rows of one sequence. The tile's input
 // rows plus a one-pixel halo are copied to shared memory with asynchronous 16-byte copies
 // (cp.async, zero-filled outside the image = the conv's zero padding), all issued before
-// the first wait, so the block streams its ~87 KB at full bandwidth. Thread (channel quad,
-// column) keeps its 4 data + 4 gate channels' 3x3 weights in registers and reads the 9 taps
-// of each output from shared memory as 8-byte loads.
+// the first wait, so the block streams its ~87 KB at full bandwidth.
 constexpr int kTileCh = 64;     // channels per half in a tile
 constexpr int kTileRows = 8;
 constexpr int kTileW = 64;      // widest image row handled by the tiled path
-constexpr int kQuads = kTileCh / 4;
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
@@ -42,21 +26,40 @@ __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
-__device__ __forceinline__ void unpack4(const uint2& u, float (&f)[4]) {
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-    const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
-    f[0] = a.x;
-    f[1] = a.y;
-    f[2] = b.x;
-    f[3] = b.y;
+// Packed fp32 pair arithmetic (sm_100 f32x2): one instruction for two channels.
+__device__ __forceinline__ uint64_t pk2(float2 v) {
+    return (static_cast<uint64_t>(__float_as_uint(v.y)) << 32) | __float_as_uint(v.x);
 }
+__device__ __forceinline__ float2 upk2(uint64_t u) {
+    return make_float2(__uint_as_float(static_cast<uint32_t>(u)), __uint_as_float(static_cast<uint32_t>(u >> 32)));
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)), "l"(pk2(c)));
+    return upk2(d);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)));
+    return upk2(d);
+}
+// bf16 pair -> fp32 pair (exact: bf16 is the top half of an fp32)
+__device__ __forceinline__ float2 bf2(uint32_t u) { return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u)); }
 
+// Thread = (channel pair p of the tile = lane, column pair): it keeps its pair's 3x3 taps of
+// both halves in registers and walks the tile's input rows top to bottom, loading the four
+// pixels x0-1 .. x0+2 of each row once (4-byte shared loads, conflict-free across the warp)
+// and adding row iy's taps into the three output rows iy-1, iy, iy+1 held in a rolling set
+// of accumulators. Each output therefore receives its taps in the reference's order (ky
+// major, then kx, from zero; bias last) with fp32 fused multiply-adds issued two channels
+// at a time.
 template <int WMAX>
-__global__ void __launch_bounds__(256) dwglu_tile_kernel(const bf16* __restrict__ in, long long ldi, int S, int H,
-                                                         int W, int half, const float* __restrict__ w,
-                                                         const float* __restrict__ b, bf16* __restrict__ out,
-                                                         long long ldo) {
+__global__ void __launch_bounds__(256, 2) dwglu_tile_kernel(const bf16* __restrict__ in, long long ldi, int S, int H,
+                                                            int W, int half, const float* __restrict__ w,
+                                                            const float* __restrict__ b, bf16* __restrict__ out,
+                                                            long long ldo) {
     constexpr int PW = WMAX + 2;  // staged pixels per row (with halo)
+    constexpr int kPairs = kTileCh / 2;
     extern __shared__ __align__(16) bf16 tile[];  // [kTileRows+2][PW][2][kTileCh]
     const int c0 = blockIdx.y * kTileCh;          // first channel of the tile in each half
     const int nch = min(kTileCh, half - c0);      // a multiple of 8
@@ -79,52 +82,68 @@ __global__ void __launch_bounds__(256) dwglu_tile_kernel(const bf16* __restrict_
             cp_async16(base + static_cast<uint32_t>(i) * 16u, src, ok ? 16u : 0u);
         }
     }
-    const int q = threadIdx.x % kQuads;  // channel quad within the tile
-    const int ch = c0 + q * 4;
-    const bool qok = q * 4 < nch;
-    float wd[4][9], wg[4][9], bd[4], bg[4];
+    const int p = threadIdx.x % 32;  // channel pair within the tile
+    const int ch = c0 + 2 * p;
+    const bool pok = 2 * p < nch;
+    float2 wv[9], wg[9], bv = make_float2(0.f, 0.f), bg = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-#pragma unroll
-        for (int t = 0; t < 9; ++t) {
-            wd[j][t] = qok ? w[static_cast<long long>(ch + j) * 9 + t] : 0.f;
-            wg[j][t] = qok ? w[static_cast<long long>(half + ch + j) * 9 + t] : 0.f;
-        }
-        bd[j] = qok ? b[ch + j] : 0.f;
-        bg[j] = qok ? b[half + ch + j] : 0.f;
+    for (int t = 0; t < 9; ++t) {
+        wv[t] = pok ? make_float2(w[static_cast<long long>(ch) * 9 + t], w[static_cast<long long>(ch + 1) * 9 + t])
+                    : make_float2(0.f, 0.f);
+        wg[t] = pok ? make_float2(w[static_cast<long long>(half + ch) * 9 + t],
+                                  w[static_cast<long long>(half + ch + 1) * 9 + t])
+                    : make_float2(0.f, 0.f);
+    }
+    if (pok) {
+        bv = make_float2(b[ch], b[ch + 1]);
+        bg = make_float2(b[half + ch], b[half + ch + 1]);
     }
     cp_async_wait_all();
     __syncthreads();
-    if (!qok) return;
+    if (!pok) return;
     const int rows = min(kTileRows, H - y0);
-    for (int x = threadIdx.x / kQuads; x < W; x += blockDim.x / kQuads) {
-        for (int ry = 0; ry < rows; ++ry) {
-            float dv[4] = {0.f, 0.f, 0.f, 0.f}, gv[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t* t32 = reinterpret_cast<const uint32_t*>(tile);
+    for (int x0 = 2 * (threadIdx.x / 32); x0 < W; x0 += 2 * (blockDim.x / 32)) {
+        float2 acc[3][2][2];  // [output row slot][column][value, gate]
+#pragma unroll
+        for (int a = 0; a < 3; ++a)
+#pragma unroll
+            for (int c = 0; c < 2; ++c) acc[a][c][0] = acc[a][c][1] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < kTileRows + 2; ++r) {
+            if (r >= rows + 2) break;
+            float2 fv[4], fg[4];
+            const uint32_t* rp = t32 + ((r * PW + x0) * 2) * kPairs + p;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                fv[j] = bf2(rp[(2 * j) * kPairs]);
+                fg[j] = bf2(rp[(2 * j + 1) * kPairs]);
+            }
 #pragma unroll
             for (int ky = 0; ky < 3; ++ky) {
+                const int o = r - ky;  // the output row this input row feeds through tap row ky
+                if (o < 0 || o >= kTileRows) continue;
 #pragma unroll
-                for (int kx = 0; kx < 3; ++kx) {
-                    const bf16* t = tile + (((ry + ky) * PW + (x + kx)) * 2) * kTileCh + q * 4;
-                    float fd[4], fg[4];
-                    unpack4(*reinterpret_cast<const uint2*>(t), fd);
-                    unpack4(*reinterpret_cast<const uint2*>(t + kTileCh), fg);
+                for (int c = 0; c < 2; ++c)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        dv[j] = fmaf(fd[j], wd[j][ky * 3 + kx], dv[j]);
-                        gv[j] = fmaf(fg[j], wg[j][ky * 3 + kx], gv[j]);
+                    for (int kx = 0; kx < 3; ++kx) {
+                        acc[o % 3][c][0] = fma2(fv[c + kx], wv[ky * 3 + kx], acc[o % 3][c][0]);
+                        acc[o % 3][c][1] = fma2(fg[c + kx], wg[ky * 3 + kx], acc[o % 3][c][1]);
+                    }
+            }
+            if (r >= 2) {  // output row r - 2 has all nine taps
+                const int o = r - 2;
+                const long long pix = (static_cast<long long>(s) * H + y0 + o) * W + x0;
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const float2 v = add2(acc[o % 3][c][0], bv), g = add2(acc[o % 3][c][1], bg);
+                    acc[o % 3][c][0] = acc[o % 3][c][1] = make_float2(0.f, 0.f);
+                    if (x0 + c < W) {
+                        const __nv_bfloat162 h = __floats2bfloat162_rn(v.x * silu_fast(g.x), v.y * silu_fast(g.y));
+                        *reinterpret_cast<__nv_bfloat162*>(out + (pix + c) * ldo + ch) = h;
                     }
                 }
             }
-            const float o0 = (dv[0] + bd[0]) * silu(gv[0] + bg[0]);
-            const float o1 = (dv[1] + bd[1]) * silu(gv[1] + bg[1]);
-            const float o2 = (dv[2] + bd[2]) * silu(gv[2] + bg[2]);
-            const float o3 = (dv[3] + bd[3]) * silu(gv[3] + bg[3]);
-            uint2 pk;
-            __nv_bfloat162 h0 = __floats2bfloat162_rn(o0, o1), h1 = __floats2bfloat162_rn(o2, o3);
-            pk.x = *reinterpret_cast<uint32_t*>(&h0);
-            pk.y = *reinterpret_cast<uint32_t*>(&h1);
-            const long long pix = (static_cast<long long>(s) * H + y0 + ry) * W + x;
-            *reinterpret_cast<uint2*>(out + pix * ldo + ch) = pk;
         }
     }
 }

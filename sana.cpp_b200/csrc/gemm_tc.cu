@@ -119,21 +119,6 @@ __device__ __forceinline__ void store_val(void* out, int is_bf16, long long idx,
 
 // SiLU for the tensor-core path's epilogue (bf16 outputs only): CUDA's fast exponential and
 // a correctly rounded reciprocal.
-// 1/y for finite y >= 1 without the special-function unit: the integer-subtraction estimate
-// (subtracting the float's bit pattern from a constant near twice the exponent bias negates
-// the exponent and linearly approximates the mantissa's reciprocal, within 5.1 %), refined
-// by two Newton-Raphson steps r <- r (2 - y r), each squaring the relative error
-// (5.1e-2 -> 2.6e-3 -> 6.6e-6: far below the rounding of the bf16 output it feeds).
-__device__ __forceinline__ float rcp_newton(float y) {
-    float r = __int_as_float(0x7EF311C3 - __float_as_int(y));
-    r = r * fmaf(-y, r, 2.0f);
-    return r * fmaf(-y, r, 2.0f);
-}
-
-// SiLU with one special-function operation per element (the exponential); the epilogue of
-// the FF-inverted projection is otherwise limited by that unit. Inputs below -80 are
-// clamped: e^80 keeps 1 + e^-x finite, and silu(x) there is below 1e-33 either way.
-__device__ __forceinline__ float silu_fast(float x) { return x * rcp_newton(1.0f + __expf(-fmaxf(x, -80.0f))); }
 
 // Residual and gate values of 16 consecutive columns [n0, n0+16) of one row, fetched one
 // chunk ahead of their use so the epilogue does not wait on global-memory latency.
