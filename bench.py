@@ -267,7 +267,7 @@ def gemm_roofline(g, torch, stream, M, peak_tflops):
 
 
 MICRO_OPS = ("qkv_gemm", "linear_attention_16x72", "linear_attention_36x32", "depthwise_glu", "cross_attention",
-             "ff_inverted_config2")
+             "ff_inverted_config2", "linear_attention_config2", "depthwise_glu_config2")
 
 
 def run_microbench(args):
@@ -275,8 +275,9 @@ def run_microbench(args):
     bf16 activations N(0,1), each op through its device entry point of the C ABI and against
     its roofline: (a) ReLU linear attention 16 x 72 (and the model's 36 x 32), (b) depthwise
     3x3 + SiLU-GLU on 5760 -> 2880 channels, (c) the QKV projection M=8192, K=1152, N=3456,
-    (d) cross-attention to 300 unmasked caption tokens. Also the step's largest kernel at
-    config-2 size: the FF-inverted projection M=32768, K=1152, N=5760 with bias and SiLU.
+    (d) cross-attention to 300 unmasked caption tokens. Also three kernels at the loop's
+    config-2 size (32 sequences x 1024 tokens): the FF-inverted projection M=32768, K=1152,
+    N=5760 with bias and SiLU, linear attention 36 x 32 and depthwise+GLU on 32 x 32 images.
     L2 is flushed (256 MiB write, untimed) before every timed launch; the median of --steps
     launches is reported. One JSON line per op."""
     import ctypes
@@ -327,6 +328,8 @@ def run_microbench(args):
               flush=True)
 
     for name in ops:
+        S, T = (32, 1024) if name.endswith("config2") else (2, 4096)
+        side = int(round(T ** 0.5))
         if name.startswith("linear_attention"):
             heads, D = (16, 72) if name.endswith("16x72") else (36, 32)
             qkv = rnd(S * T, 3 * C)
@@ -336,14 +339,15 @@ def run_microbench(args):
             ms = timed(lambda: g._call("sana_op_linear_attention_device", vp(qkv.data_ptr()), I(S), I(T), I(heads),
                                        I(D), vp(part.data_ptr()), vp(out.data_ptr())))
             report(name, f"q,k,v [{S},{heads},{T},{D}] bf16 -> o", ms, 2.0 * S * T * 4 * C, "hbm")
-        elif name == "depthwise_glu":
+        elif name.startswith("depthwise_glu"):
             h = rnd(S * T, E)
             w = (torch.randn(E * 9, generator=gen) * 0.02).cuda()
             b = torch.zeros(E, device="cuda")
             out = torch.empty(S * T, E // 2, device="cuda", dtype=torch.bfloat16)
-            ms = timed(lambda: g._call("sana_op_depthwise_glu_device", vp(h.data_ptr()), I(S), I(64), I(64), I(E),
+            ms = timed(lambda: g._call("sana_op_depthwise_glu_device", vp(h.data_ptr()), I(S), I(side), I(side), I(E),
                                        vp(w.data_ptr()), vp(b.data_ptr()), vp(out.data_ptr())))
-            report(name, f"[{S},64,64,{E}] -> [{S},64,64,{E // 2}] bf16", ms, 2.0 * S * T * (E + E // 2), "hbm")
+            report(name, f"[{S},{side},{side},{E}] -> [{S},{side},{side},{E // 2}] bf16", ms,
+                   2.0 * S * T * (E + E // 2), "hbm")
         elif name == "qkv_gemm":
             M, N, K = S * T, 3 * C, C
             A, B = rnd(M, K), rnd(N, K, scale=0.02)
@@ -351,7 +355,7 @@ def run_microbench(args):
             ms = timed(lambda: g.gemm_device(A.data_ptr(), B.data_ptr(), M, N, K, out.data_ptr()))
             report(name, f"M={M} K={K} N={N} bf16 -> bf16", ms, 2.0 * M * N * K, "tensor")
         elif name == "ff_inverted_config2":
-            M, N, K = 32 * 1024, E, C
+            M, N, K = S * T, E, C
             A, B = rnd(M, K), rnd(N, K, scale=0.02)
             bias = torch.zeros(N, device="cuda")
             out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)

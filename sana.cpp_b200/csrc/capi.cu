@@ -601,10 +601,10 @@ int sana_op_glumb_conv(sana_cuda_ctx* ctx, const float* x, int B, int Cin, int H
         run_gemm(eng, A, Cin, Wi, Cin, M, E, Cin, epi(Hb.get(), bf, E, bi.as<float>(), sana::kActSilu));
         if (bf) {
             sana::depthwise_glu<bf16>(static_cast<const bf16*>(Hb.get()), E, B, H, W, E, wd.as<float>(),
-                                      bd.as<float>(), static_cast<bf16*>(G.get()), E / 2, eng.stream());
+                                      bd.as<float>(), static_cast<bf16*>(G.get()), E / 2, eng.err(), eng.stream());
         } else {
             sana::depthwise_glu<float>(static_cast<const float*>(Hb.get()), E, B, H, W, E, wd.as<float>(),
-                                       bd.as<float>(), static_cast<float*>(G.get()), E / 2, eng.stream());
+                                       bd.as<float>(), static_cast<float*>(G.get()), E / 2, eng.err(), eng.stream());
         }
         run_gemm(eng, G, E / 2, Wp, E / 2, M, Cout, E / 2, epi(o.get(), false, Cout));
         finish(eng);
@@ -829,7 +829,7 @@ int sana_op_depthwise_glu_device(sana_cuda_ctx* ctx, const void* in, int S, int 
         SANA_REQUIRE(in && w && b && out && S >= 1 && H >= 1 && W >= 1 && E >= 2, "invalid arguments");
         sana::Engine& eng = engine(ctx);
         sana::depthwise_glu<bf16>(static_cast<const bf16*>(in), E, S, H, W, E, w, b, static_cast<bf16*>(out), E / 2,
-                                  eng.stream());
+                                  eng.err(), eng.stream());
     });
 }
 

@@ -6,45 +6,77 @@
 // The input is the SiLU-ed output of the inverted 1x1 conv, already token-major, so the
 // reference's NCHW round trips (tokens_to_grid_4d / grid_to_tokens_3d) disappear.
 #include "kernels.h"
+#include "tma.h"
 
 namespace sana {
 namespace {
 
 // bf16 tiled path (half % 8 == 0, 16-byte aligned rows, W <= kTileW). A block owns 64
-// channels of both halves and kTileRows full image rows of one sequence. The tile's input
-// rows plus a one-pixel halo are copied to shared memory with asynchronous 16-byte copies
-// (cp.async, zero-filled outside the image = the conv's zero padding), all issued before
-// the first wait, so the block streams its ~87 KB at full bandwidth.
+// channels of both halves and kTileRows full image rows of one sequence. One thread loads
+// the tile's input rows plus a one-pixel halo with two TMA copies (a 4-D box of
+// [1 sequence, kTileRows + 2 rows, W + 2 pixels, 64 channels] per half); TMA reads the
+// halo outside the image as zeros, which is the conv's zero padding.
 constexpr int kTileCh = 64;     // channels per half in a tile
 constexpr int kTileRows = 8;
 constexpr int kTileW = 64;      // widest image row handled by the tiled path
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
+// Staged pixels per image row: the row plus its halo, plus one more for odd widths so the
+// last column pair's four-pixel window stays inside the row.
+__host__ __device__ __forceinline__ int tile_pixels(int W) { return W + 2 + (W & 1); }
 
-// Packed fp32 pair arithmetic (sm_100 f32x2): one instruction for two channels.
-__device__ __forceinline__ uint64_t pk2(float2 v) {
-    return (static_cast<uint64_t>(__float_as_uint(v.y)) << 32) | __float_as_uint(v.x);
-}
-__device__ __forceinline__ float2 upk2(uint64_t u) {
-    return make_float2(__uint_as_float(static_cast<uint32_t>(u)), __uint_as_float(static_cast<uint32_t>(u >> 32)));
-}
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+// Packed fp32 pairs (sm_100 f32x2): a 64-bit register holds two channels' fp32 values and
+// one instruction does the arithmetic of both. Values stay in that form from the bf16 load
+// to the final GLU, so no pack / unpack sits between the multiply-adds.
+__device__ __forceinline__ uint64_t f2_from_bf2(uint32_t u) {  // bf16 pair -> fp32 pair (exact)
     uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)), "l"(pk2(c)));
-    return upk2(d);
+    asm("{\n\t.reg .b32 lo, hi;\n\tshl.b32 lo, %1, 16;\n\tand.b32 hi, %1, 0xffff0000;\n\tmov.b64 %0, {lo, hi};\n\t}"
+        : "=l"(d)
+        : "r"(u));
+    return d;
 }
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+__device__ __forceinline__ uint64_t f2_make(float lo, float hi) {
     uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)));
-    return upk2(d);
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
 }
-// bf16 pair -> fp32 pair (exact: bf16 is the top half of an fp32)
-__device__ __forceinline__ float2 bf2(uint32_t u) { return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u)); }
+__device__ __forceinline__ float2 f2_split(uint64_t u) {
+    float lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(u));
+    return make_float2(lo, hi);
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// silu_fast (common.cuh) on a pair: the exponentials per lane, the rest pairwise.
+__device__ __forceinline__ uint64_t silu2(uint64_t g) {
+    const float2 x = f2_split(g);
+    const uint64_t e = f2_make(__expf(-fmaxf(x.x, -80.0f)), __expf(-fmaxf(x.y, -80.0f)));
+    const uint64_t ny = sub2(f2_make(-1.0f, -1.0f), e);  // -(1 + e)
+    const float2 y = f2_split(ny);
+    uint64_t r = f2_make(__int_as_float(0x7EF311C3 - __float_as_int(-y.x)),
+                         __int_as_float(0x7EF311C3 - __float_as_int(-y.y)));
+    const uint64_t two = f2_make(2.0f, 2.0f);
+    r = mul2(r, fma2(ny, r, two));
+    r = mul2(r, fma2(ny, r, two));
+    return mul2(g, r);
+}
 
 // Thread = (channel pair p of the tile = lane, column pair): it keeps its pair's 3x3 taps of
 // both halves in registers and walks the tile's input rows top to bottom, loading the four
@@ -53,71 +85,67 @@ __device__ __forceinline__ float2 bf2(uint32_t u) { return make_float2(__uint_as
 // of accumulators. Each output therefore receives its taps in the reference's order (ky
 // major, then kx, from zero; bias last) with fp32 fused multiply-adds issued two channels
 // at a time.
-template <int WMAX>
-__global__ void __launch_bounds__(256, 2) dwglu_tile_kernel(const bf16* __restrict__ in, long long ldi, int S, int H,
+__global__ void __launch_bounds__(256, 2) dwglu_tile_kernel(const __grid_constant__ CUtensorMap map, int S, int H,
                                                             int W, int half, const float* __restrict__ w,
                                                             const float* __restrict__ b, bf16* __restrict__ out,
-                                                            long long ldo) {
-    constexpr int PW = WMAX + 2;  // staged pixels per row (with halo)
+                                                            long long ldo, int* err) {
     constexpr int kPairs = kTileCh / 2;
-    extern __shared__ __align__(16) bf16 tile[];  // [kTileRows+2][PW][2][kTileCh]
+    extern __shared__ __align__(16) unsigned char dyn[];
+    __shared__ __align__(8) uint64_t bar_storage;
+    // two boxes [kTileRows + 2][W + 2][kTileCh] (value half, gate half), 128-byte aligned
+    bf16* tile = reinterpret_cast<bf16*>((reinterpret_cast<uintptr_t>(dyn) + 127) & ~uintptr_t(127));
+    const int PW = tile_pixels(W);
+    const int box = (kTileRows + 2) * PW * kTileCh;  // elements per half
     const int c0 = blockIdx.y * kTileCh;          // first channel of the tile in each half
     const int nch = min(kTileCh, half - c0);      // a multiple of 8
     const int row_tiles = (H + kTileRows - 1) / kTileRows;
     const int s = blockIdx.x / row_tiles;
     const int y0 = (blockIdx.x % row_tiles) * kTileRows;
-    {
-        constexpr int kChunks = kTileCh / 8;  // 16-byte chunks per half-pixel
-        const int total = (kTileRows + 2) * PW * 2 * kChunks;
-        const uint32_t base = smem_u32(tile);
-        for (int i = threadIdx.x; i < total; i += blockDim.x) {
-            const int ck = i % kChunks;
-            const int hf = (i / kChunks) % 2;
-            const int px = (i / (2 * kChunks)) % PW;
-            const int r = i / (2 * kChunks * PW);
-            const int iy = y0 + r - 1, ix = px - 1;
-            const bool ok = iy >= 0 && iy < H && ix >= 0 && ix < W && ck * 8 < nch;
-            const bf16* src = ok ? in + ((static_cast<long long>(s) * H + iy) * W + ix) * ldi + hf * half + c0 + ck * 8
-                                 : in;
-            cp_async16(base + static_cast<uint32_t>(i) * 16u, src, ok ? 16u : 0u);
-        }
+    const uint32_t bar = smem_u32(&bar_storage);
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(2 * box * 2));
+        tma_load_4d(&map, smem_u32(tile), bar, c0, -1, y0 - 1, s);
+        tma_load_4d(&map, smem_u32(tile + box), bar, half + c0, -1, y0 - 1, s);
     }
     const int p = threadIdx.x % 32;  // channel pair within the tile
     const int ch = c0 + 2 * p;
     const bool pok = 2 * p < nch;
-    float2 wv[9], wg[9], bv = make_float2(0.f, 0.f), bg = make_float2(0.f, 0.f);
+    uint64_t wv[9], wg[9], bv = 0, bg = 0;
 #pragma unroll
     for (int t = 0; t < 9; ++t) {
-        wv[t] = pok ? make_float2(w[static_cast<long long>(ch) * 9 + t], w[static_cast<long long>(ch + 1) * 9 + t])
-                    : make_float2(0.f, 0.f);
-        wg[t] = pok ? make_float2(w[static_cast<long long>(half + ch) * 9 + t],
-                                  w[static_cast<long long>(half + ch + 1) * 9 + t])
-                    : make_float2(0.f, 0.f);
+        wv[t] = pok ? f2_make(w[static_cast<long long>(ch) * 9 + t], w[static_cast<long long>(ch + 1) * 9 + t]) : 0;
+        wg[t] = pok ? f2_make(w[static_cast<long long>(half + ch) * 9 + t], w[static_cast<long long>(half + ch + 1) * 9 + t])
+                    : 0;
     }
     if (pok) {
-        bv = make_float2(b[ch], b[ch + 1]);
-        bg = make_float2(b[half + ch], b[half + ch + 1]);
+        bv = f2_make(b[ch], b[ch + 1]);
+        bg = f2_make(b[half + ch], b[half + ch + 1]);
     }
-    cp_async_wait_all();
-    __syncthreads();
+    __syncthreads();  // the barrier is initialised before anyone waits on it
+    if (!mbar_wait(bar, 0, err, kTimeout)) {
+        if (threadIdx.x == 0) mbar_wait_quiet(bar, 0);  // let the copies land before the block exits
+        return;
+    }
     if (!pok) return;
     const int rows = min(kTileRows, H - y0);
     const uint32_t* t32 = reinterpret_cast<const uint32_t*>(tile);
     for (int x0 = 2 * (threadIdx.x / 32); x0 < W; x0 += 2 * (blockDim.x / 32)) {
-        float2 acc[3][2][2];  // [output row slot][column][value, gate]
+        uint64_t acc[3][2][2];  // [output row slot][column][value, gate]; +0.0 pairs
 #pragma unroll
         for (int a = 0; a < 3; ++a)
 #pragma unroll
-            for (int c = 0; c < 2; ++c) acc[a][c][0] = acc[a][c][1] = make_float2(0.f, 0.f);
+            for (int c = 0; c < 2; ++c) acc[a][c][0] = acc[a][c][1] = 0;
 #pragma unroll
         for (int r = 0; r < kTileRows + 2; ++r) {
             if (r >= rows + 2) break;
-            float2 fv[4], fg[4];
-            const uint32_t* rp = t32 + ((r * PW + x0) * 2) * kPairs + p;
+            uint64_t fv[4], fg[4];
+            const uint32_t* rp = t32 + (r * PW + x0) * kPairs + p;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                fv[j] = bf2(rp[(2 * j) * kPairs]);
-                fg[j] = bf2(rp[(2 * j + 1) * kPairs]);
+                fv[j] = f2_from_bf2(rp[j * kPairs]);
+                fg[j] = f2_from_bf2(rp[box / 2 + j * kPairs]);
             }
 #pragma unroll
             for (int ky = 0; ky < 3; ++ky) {
@@ -136,11 +164,12 @@ __global__ void __launch_bounds__(256, 2) dwglu_tile_kernel(const bf16* __restri
                 const long long pix = (static_cast<long long>(s) * H + y0 + o) * W + x0;
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
-                    const float2 v = add2(acc[o % 3][c][0], bv), g = add2(acc[o % 3][c][1], bg);
-                    acc[o % 3][c][0] = acc[o % 3][c][1] = make_float2(0.f, 0.f);
+                    const uint64_t v = add2(acc[o % 3][c][0], bv);
+                    const uint64_t g = add2(acc[o % 3][c][1], bg);
+                    acc[o % 3][c][0] = acc[o % 3][c][1] = 0;
                     if (x0 + c < W) {
-                        const __nv_bfloat162 h = __floats2bfloat162_rn(v.x * silu_fast(g.x), v.y * silu_fast(g.y));
-                        *reinterpret_cast<__nv_bfloat162*>(out + (pix + c) * ldo + ch) = h;
+                        const float2 y = f2_split(mul2(v, silu2(g)));
+                        *reinterpret_cast<__nv_bfloat162*>(out + (pix + c) * ldo + ch) = __floats2bfloat162_rn(y.x, y.y);
                     }
                 }
             }
@@ -148,9 +177,8 @@ __global__ void __launch_bounds__(256, 2) dwglu_tile_kernel(const bf16* __restri
     }
 }
 
-template <int WMAX>
-size_t dwglu_tile_smem() {
-    return sizeof(bf16) * (kTileRows + 2) * (WMAX + 2) * 2 * kTileCh;
+size_t dwglu_tile_smem(int W) {
+    return sizeof(bf16) * (kTileRows + 2) * tile_pixels(W) * 2 * kTileCh + 128;
 }
 
 // Any type / channel count: one output channel per thread.
@@ -220,7 +248,7 @@ int grid_for(long long n) {
 
 template <class T>
 void depthwise_glu(const T* in, long long ldi, int S, int H, int W, int E, const float* w, const float* b, T* out,
-                   long long ldo, cudaStream_t st) {
+                   long long ldo, int* err, cudaStream_t st) {
     SANA_REQUIRE(E % 2 == 0, "channel count must be even");
     const int half = E / 2;
     const long long pixels = static_cast<long long>(S) * H * W;
@@ -231,25 +259,25 @@ void depthwise_glu(const T* in, long long ldi, int S, int H, int W, int E, const
         const int tiles = ceil_div(half, kTileCh);
         const int row_tiles = ceil_div(H, kTileRows);
         const dim3 grid(static_cast<unsigned>(S * row_tiles), tiles);
-        if (W <= 32) {
-            static bool a32 = false;
-            if (!a32) {
-                SANA_CUDA(cudaFuncSetAttribute(dwglu_tile_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(dwglu_tile_smem<32>())));
-                a32 = true;
-            }
-            dwglu_tile_kernel<32><<<grid, 256, dwglu_tile_smem<32>(), st>>>(
-                reinterpret_cast<const bf16*>(in), ldi, S, H, W, half, w, b, reinterpret_cast<bf16*>(out), ldo);
-        } else {
-            static bool a64 = false;
-            if (!a64) {
-                SANA_CUDA(cudaFuncSetAttribute(dwglu_tile_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(dwglu_tile_smem<64>())));
-                a64 = true;
-            }
-            dwglu_tile_kernel<64><<<grid, 256, dwglu_tile_smem<64>(), st>>>(
-                reinterpret_cast<const bf16*>(in), ldi, S, H, W, half, w, b, reinterpret_cast<bf16*>(out), ldo);
+        static bool attr = false;
+        if (!attr) {
+            SANA_CUDA(cudaFuncSetAttribute(dwglu_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(dwglu_tile_smem(kTileW))));
+            attr = true;
         }
+        // [S, H, W, channels] with the channel rows ldi apart; box = 64 channels x tile pixels
+        // x (kTileRows + 2) rows x 1 sequence
+        CUtensorMap map;
+        const cuuint64_t dims[4] = {static_cast<cuuint64_t>(2 * half), static_cast<cuuint64_t>(W),
+                                    static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(S)};
+        const cuuint64_t strides[3] = {static_cast<cuuint64_t>(ldi) * 2, static_cast<cuuint64_t>(ldi) * 2 * W,
+                                       static_cast<cuuint64_t>(ldi) * 2 * W * H};
+        const cuuint32_t box[4] = {static_cast<cuuint32_t>(kTileCh), static_cast<cuuint32_t>(tile_pixels(W)),
+                                   static_cast<cuuint32_t>(kTileRows + 2), 1};
+        tma_encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, in, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+        dwglu_tile_kernel<<<grid, 256, dwglu_tile_smem(W), st>>>(map, S, H, W, half, w, b,
+                                                                  reinterpret_cast<bf16*>(out), ldo, err);
     } else {
         dwglu_scalar_kernel<T><<<grid_for(pixels * half), 256, 0, st>>>(in, ldi, S, H, W, half, w, b, out, ldo);
     }
@@ -265,8 +293,8 @@ void depthwise3x3(const float* in, int S, int H, int W, int C, const float* w, c
 }
 
 template void depthwise_glu<float>(const float*, long long, int, int, int, int, const float*, const float*, float*,
-                                   long long, cudaStream_t);
+                                   long long, int*, cudaStream_t);
 template void depthwise_glu<bf16>(const bf16*, long long, int, int, int, int, const float*, const float*, bf16*,
-                                  long long, cudaStream_t);
+                                  long long, int*, cudaStream_t);
 
 }  // namespace sana

@@ -488,7 +488,7 @@ void Engine::block_impl(int b, const float* x_in, float* x_self, float* x_cross,
     {
         ProfScope p(this, "depthwise_glu");
         depthwise_glu<T>(ffh_.as<T>(), E, S, side, side, E, w.wdw.as<float>(), w.bdw.as<float>(), glu_.as<T>(), E / 2,
-                         st_);
+                         err(), st_);
     }
     {
         Epilogue e = epi_out(x_ff, false, C);

@@ -17,6 +17,7 @@
 #include <mutex>
 
 #include "gemm.h"
+#include "tma.h"
 
 namespace sana {
 namespace tc {
@@ -413,25 +414,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // --- host side ---------------------------------------------------------------------------
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiled encoder() {
-    static EncodeTiled fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess) {
-            fn = reinterpret_cast<EncodeTiled>(p);
-        }
-    });
-    if (!fn) throw CudaError("cuTensorMapEncodeTiled is not available from the driver");
-    return fn;
-}
-
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix with row stride ld elements;
 // box = [box_rows, 64 columns], 128-byte swizzle, out-of-bounds elements read as zero.
 static CUtensorMap make_map(const void* ptr, int rows, int cols, long long ld, int box_rows) {
@@ -439,11 +421,7 @@ static CUtensorMap make_map(const void* ptr, int rows, int cols, long long ld, i
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
     const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
-    const cuuint32_t estr[2] = {1, 1};
-    CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
-                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
+    tma_encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     return m;
 }
 

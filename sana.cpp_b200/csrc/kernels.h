@@ -119,8 +119,9 @@ void cross_attention(const T* q, long long ldq, const T* kv, long long ldkv, int
 // the GLU gate data * silu(gate) (depthwise_conv2d_3x3, common_ops.cpp:510-572, then
 // glumb_conv's split and gate, :745-758). in [S*H*W, E] (stride ldi), out [S*H*W, E/2].
 template <class T>
+// err: the device error word (a bounded wait records kTimeout there).
 void depthwise_glu(const T* in, long long ldi, int S, int H, int W, int E, const float* w, const float* b, T* out,
-                   long long ldo, cudaStream_t st);
+                   long long ldo, int* err, cudaStream_t st);
 
 // The depthwise 3x3 conv alone (depthwise_conv2d_3x3), all C channels, NHWC fp32.
 void depthwise3x3(const float* in, int S, int H, int W, int C, const float* w, const float* b, float* out,

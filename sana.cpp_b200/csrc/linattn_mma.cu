@@ -11,13 +11,14 @@
 // accumulation order differs from the reference's sequential loop. The state is split into
 // bf16 hi + lo parts for the apply product (two MMAs), which keeps it to ~2^-16 relative.
 //
-// Kernel 1 (state): one CTA per (token split, head, sequence); K and V chunks of 64 tokens
-// stream through a 3-stage cp.async ring; warp (m-tile, token slice) accumulates a 16-row
-// slab of S' over its slice of each chunk; slices are summed through shared memory and the
-// split's D x (D+1) partial state is written to global memory.
+// Kernel 1 (state): one CTA per (token split, head, sequence); K and V chunks of 128 (head
+// dim 32) or 64 tokens stream through a 3-stage cp.async ring; warp (m-tile, token slice)
+// accumulates a 16-row slab of S' over its slice of each chunk; slices are summed through
+// shared memory and the split's D x (D+1) partial state is written to global memory.
 // Kernel 2 (apply): one CTA per (token split, head, sequence) sums the partial states,
 // converts them to hi/lo bf16 in shared memory, then streams Q chunks of 64 tokens; each
-// warp computes 16 tokens' outputs, divides by the last column and writes bf16 rows.
+// warp computes 16 tokens' outputs, scales them by the reciprocal of the last column and
+// writes bf16 rows.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -70,35 +71,41 @@ __device__ __forceinline__ uint32_t relu2(uint32_t x) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Copies a [kChunk, D] bf16 tile (rows t0.., columns col of a row-major matrix with row
+// Copies a [CH, D] bf16 tile (rows t0.., columns from `src` of a row-major matrix with row
 // stride ld) into shared memory rows of `stride` elements; rows at or past t_end are zero.
+template <int D, int CH, int NT>
 __device__ __forceinline__ void load_tile(uint32_t dst, const bf16* src, long long ld, int row0, int t0, int t_end,
-                                          int D, int stride) {
-    const int cpr = D / 8;
-    for (int i = threadIdx.x; i < kChunk * cpr; i += blockDim.x) {
-        const int r = i / cpr, c = i % cpr;
-        const bool ok = t0 + r < t_end;
-        const bf16* p = src + static_cast<long long>(row0 + (ok ? t0 + r : t_end - 1)) * ld + c * 8;
-        cp_async16z(dst + static_cast<uint32_t>(r * stride + c * 8) * 2u, p, ok);
+                                          int stride) {
+    constexpr int cpr = D / 8;
+#pragma unroll
+    for (int k = 0; k < (CH * cpr + NT - 1) / NT; ++k) {
+        const int i = threadIdx.x + k * NT;
+        if (CH * cpr % NT == 0 || i < CH * cpr) {
+            const int r = i / cpr, c = i % cpr;
+            const bool ok = t0 + r < t_end;
+            const bf16* p = src + static_cast<long long>(row0 + (ok ? t0 + r : t_end - 1)) * ld + c * 8;
+            cp_async16z(dst + static_cast<uint32_t>(r * stride + c * 8) * 2u, p, ok);
+        }
     }
 }
 
-template <int D, int TS>
+template <int D, int TS, int CH>
 __global__ void __launch_bounds__(32 * (dpad(D) / 16) * TS)
     la_state_kernel(const bf16* __restrict__ kv, long long ld, int k_off, int v_off, int Tk, int heads, int splits,
                     int per_split, float* __restrict__ partial) {
     constexpr int DP = dpad(D), NP = npad(D), MT = DP / 16, NT = NP / 8, KS = row_stride(DP);
-    constexpr int kTile = kChunk * KS;  // elements per stage per matrix
+    constexpr int kTile = CH * KS;  // elements per stage per matrix
+    constexpr int kThreads = 32 * MT * TS;
     extern __shared__ __align__(16) unsigned char smem[];
     bf16* Ks = reinterpret_cast<bf16*>(smem);
     bf16* Vs = Ks + kStages * kTile;
     const int split = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
     const int t_begin = split * per_split, t_end = min(Tk, t_begin + per_split);
-    const int nchunks = t_end > t_begin ? (t_end - t_begin + kChunk - 1) / kChunk : 0;
+    const int nchunks = t_end > t_begin ? (t_end - t_begin + CH - 1) / CH : 0;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int mt = warp % MT, ts = warp / MT;
     if (DP > D) {  // pad columns of every stage stay zero
-        for (int i = threadIdx.x; i < 2 * kStages * kChunk; i += blockDim.x)
+        for (int i = threadIdx.x; i < 2 * kStages * CH; i += blockDim.x)
             for (int c = D; c < DP; ++c) Ks[i * KS + c] = __float2bfloat16_rn(0.f);
     }
     const bf16* kbase = kv + k_off + h * D;
@@ -107,9 +114,9 @@ __global__ void __launch_bounds__(32 * (dpad(D) / 16) * TS)
     auto issue = [&](int c) {
         if (c < nchunks) {
             const int stg = c % kStages;
-            const int t0 = t_begin + c * kChunk;
-            load_tile(ks0 + static_cast<uint32_t>(stg * kTile) * 2u, kbase, ld, s * Tk, t0, t_end, D, KS);
-            load_tile(vs0 + static_cast<uint32_t>(stg * kTile) * 2u, vbase, ld, s * Tk, t0, t_end, D, KS);
+            const int t0 = t_begin + c * CH;
+            load_tile<D, CH, kThreads>(ks0 + static_cast<uint32_t>(stg * kTile) * 2u, kbase, ld, s * Tk, t0, t_end, KS);
+            load_tile<D, CH, kThreads>(vs0 + static_cast<uint32_t>(stg * kTile) * 2u, vbase, ld, s * Tk, t0, t_end, KS);
         }
         cp_async_commit();
     };
@@ -120,7 +127,7 @@ __global__ void __launch_bounds__(32 * (dpad(D) / 16) * TS)
     for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
     __syncthreads();
     for (int c = 0; c < kStages - 1; ++c) issue(c);
-    constexpr int kSlice = kChunk / TS;
+    constexpr int kSlice = CH / TS;
     for (int c = 0; c < nchunks; ++c) {
         cp_async_wait<kStages - 2>();
         __syncthreads();
@@ -192,8 +199,8 @@ __global__ void __launch_bounds__(128)
     const uint32_t qs0 = smem_u32(Qs);
     auto issue = [&](int c) {
         if (c < nchunks)
-            load_tile(qs0 + static_cast<uint32_t>((c % kStages) * kTile) * 2u, qbase, ldq, s * Tq,
-                      t_begin + c * kChunk, t_end, D, QS);
+            load_tile<D, kChunk, 128>(qs0 + static_cast<uint32_t>((c % kStages) * kTile) * 2u, qbase, ldq, s * Tq,
+                                      t_begin + c * kChunk, t_end, QS);
         cp_async_commit();
     };
     for (int c = 0; c < kStages - 1; ++c) issue(c);
@@ -220,9 +227,12 @@ __global__ void __launch_bounds__(128)
         issue(c + kStages - 1);
         const int stg = c % kStages;
         const uint32_t qc = qs0 + static_cast<uint32_t>(stg * kTile) * 2u;
-        float acc[NT][4];
+        // hi and lo parts accumulate separately (independent MMA chains), summed at the end
+        float acc[NT][4], acl[NT][4];
 #pragma unroll
-        for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[n][r] = acl[n][r] = 0.f;
 #pragma unroll
         for (int k0 = 0; k0 < DP; k0 += 16) {
             uint32_t a[4];
@@ -237,21 +247,26 @@ __global__ void __launch_bounds__(128)
                 ldsm_x2_t(bhi0 + brow + static_cast<uint32_t>(n * 8) * 2u, b0, b1);
                 mma16816(acc[n], a, b0, b1);
                 ldsm_x2_t(blo0 + brow + static_cast<uint32_t>(n * 8) * 2u, b0, b1);
-                mma16816(acc[n], a, b0, b1);
+                mma16816(acl[n], a, b0, b1);
             }
         }
-        // denominators: column D (first column of the last n-tile) of rows g and g + 8
-        const float den0 = __shfl_sync(0xffffffffu, acc[NT - 1][0], lane & ~3) + 1e-15f;
-        const float den1 = __shfl_sync(0xffffffffu, acc[NT - 1][2], lane & ~3) + 1e-15f;
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[n][r] += acl[n][r];
+        // denominators: column D (first column of the last n-tile) of rows g and g + 8; one
+        // reciprocal per row (within an ulp of dividing each element)
+        const float den0 = __frcp_rn(__shfl_sync(0xffffffffu, acc[NT - 1][0], lane & ~3) + 1e-15f);
+        const float den1 = __frcp_rn(__shfl_sync(0xffffffffu, acc[NT - 1][2], lane & ~3) + 1e-15f);
         // stage this warp's 16 output rows in its own (consumed) Q rows, then store them
         __syncwarp();
         bf16* orow = Qs + stg * kTile + (warp * 16) * QS;
 #pragma unroll
         for (int n = 0; n < NT - 1; ++n) {
             *reinterpret_cast<__nv_bfloat162*>(orow + g * QS + n * 8 + q2) =
-                __floats2bfloat162_rn(acc[n][0] / den0, acc[n][1] / den0);
+                __floats2bfloat162_rn(acc[n][0] * den0, acc[n][1] * den0);
             *reinterpret_cast<__nv_bfloat162*>(orow + (g + 8) * QS + n * 8 + q2) =
-                __floats2bfloat162_rn(acc[n][2] / den1, acc[n][3] / den1);
+                __floats2bfloat162_rn(acc[n][2] * den1, acc[n][3] * den1);
         }
         __syncwarp();
         const int t0 = t_begin + c * kChunk + warp * 16;
@@ -266,10 +281,10 @@ __global__ void __launch_bounds__(128)
     cp_async_wait<0>();
 }
 
-template <int D, int TS>
+template <int D, int TS, int CH>
 size_t state_smem() {
     constexpr int DP = dpad(D), NP = npad(D);
-    const size_t ring = static_cast<size_t>(2) * kStages * kChunk * row_stride(DP) * 2;
+    const size_t ring = static_cast<size_t>(2) * kStages * CH * row_stride(DP) * 2;
     const size_t red = static_cast<size_t>(TS) * DP * NP * 4;
     return ring > red ? ring : red;
 }
@@ -302,13 +317,13 @@ int token_splits(int units, int T, int min_tokens, int* per) {
     return (T + *per - 1) / *per;
 }
 
-template <int D, int TS>
+template <int D, int TS, int CH>
 void launch(const bf16* q, long long ldq, int q_off, const bf16* kv, long long ldkv, int k_off, int v_off, int S,
             int Tq, int Tk, int heads, float* partial, bf16* out, long long ldo, cudaStream_t st) {
     static bool attr = false;
-    const size_t sm1 = state_smem<D, TS>(), sm2 = apply_smem<D>();
+    const size_t sm1 = state_smem<D, TS, CH>(), sm2 = apply_smem<D>();
     if (!attr) {
-        SANA_CUDA(cudaFuncSetAttribute(la_state_kernel<D, TS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        SANA_CUDA(cudaFuncSetAttribute(la_state_kernel<D, TS, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(sm1)));
         SANA_CUDA(cudaFuncSetAttribute(la_apply_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(sm2)));
@@ -320,7 +335,7 @@ void launch(const bf16* q, long long ldq, int q_off, const bf16* kv, long long l
     const int splits = token_splits(S * heads, Tk, 128, &per1);
     const int blocks = token_splits(S * heads, Tq, kChunk, &per2);
     constexpr int kWarps = (dpad(D) / 16) * TS;
-    la_state_kernel<D, TS><<<dim3(splits, heads, S), 32 * kWarps, sm1, st>>>(kv, ldkv, k_off, v_off, Tk, heads,
+    la_state_kernel<D, TS, CH><<<dim3(splits, heads, S), 32 * kWarps, sm1, st>>>(kv, ldkv, k_off, v_off, Tk, heads,
                                                                              splits, per1, partial);
     SANA_CUDA(cudaGetLastError());
     la_apply_kernel<D><<<dim3(blocks, heads, S), 128, sm2, st>>>(q, ldq, q_off, Tq, heads, splits, partial, per2,
@@ -338,9 +353,9 @@ bool linattn_mma(const bf16* q, long long ldq, int q_off, const bf16* kv, long l
         !a16(q) || !a16(kv) || !a16(out) || Tk <= 0 || Tq <= 0)
         return false;
     switch (D) {
-        case 32: launch<32, 4>(q, ldq, q_off, kv, ldkv, k_off, v_off, S, Tq, Tk, heads, partial, out, ldo, st); break;
-        case 64: launch<64, 2>(q, ldq, q_off, kv, ldkv, k_off, v_off, S, Tq, Tk, heads, partial, out, ldo, st); break;
-        default: launch<72, 2>(q, ldq, q_off, kv, ldkv, k_off, v_off, S, Tq, Tk, heads, partial, out, ldo, st); break;
+        case 32: launch<32, 4, 128>(q, ldq, q_off, kv, ldkv, k_off, v_off, S, Tq, Tk, heads, partial, out, ldo, st); break;
+        case 64: launch<64, 2, 64>(q, ldq, q_off, kv, ldkv, k_off, v_off, S, Tq, Tk, heads, partial, out, ldo, st); break;
+        default: launch<72, 2, 64>(q, ldq, q_off, kv, ldkv, k_off, v_off, S, Tq, Tk, heads, partial, out, ldo, st); break;
     }
     return true;
 }

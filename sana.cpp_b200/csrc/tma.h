@@ -1,0 +1,26 @@
+// Tensor Memory Accelerator helpers shared by the kernels: the driver's tensor-map encoder
+// (looked up at run time, so the library does not link libcuda) and the bulk tensor loads.
+// No load here uses cluster multicast.
+#pragma once
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace sana {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point; throws CudaError when
+// the driver does not provide it or rejects the arguments.
+void tma_encode_tiled(CUtensorMap* map, CUtensorMapDataType type, cuuint32_t rank, const void* addr,
+                      const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box,
+                      CUtensorMapSwizzle swizzle);
+
+__device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint32_t dst, uint32_t bar, int c0, int c1,
+                                            int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+        "[%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+}  // namespace sana
