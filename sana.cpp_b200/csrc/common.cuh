@@ -82,6 +82,59 @@ __device__ __forceinline__ float rcp_newton(float y) {
 // 1e-33 either way.
 __device__ __forceinline__ float silu_fast(float x) { return x * rcp_newton(1.0f + __expf(-fmaxf(x, -80.0f))); }
 
+// Packed fp32 pairs (sm_100 f32x2): a 64-bit register holds two fp32 values and one
+// instruction does the arithmetic of both.
+__device__ __forceinline__ uint64_t f2_from_bf2(uint32_t u) {  // bf16 pair -> fp32 pair (exact)
+    uint64_t d;
+    asm("{\n\t.reg .b32 lo, hi;\n\tshl.b32 lo, %1, 16;\n\tand.b32 hi, %1, 0xffff0000;\n\tmov.b64 %0, {lo, hi};\n\t}"
+        : "=l"(d)
+        : "r"(u));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_make(float lo, float hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ float2 f2_split(uint64_t u) {
+    float lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(u));
+    return make_float2(lo, hi);
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// silu_fast on a pair: the exponentials per lane, the rest pairwise.
+__device__ __forceinline__ uint64_t silu2(uint64_t g) {
+    const float2 x = f2_split(g);
+    const uint64_t e = f2_make(__expf(-fmaxf(x.x, -80.0f)), __expf(-fmaxf(x.y, -80.0f)));
+    const uint64_t ny = sub2(f2_make(-1.0f, -1.0f), e);  // -(1 + e)
+    const float2 y = f2_split(ny);
+    uint64_t r = f2_make(__int_as_float(0x7EF311C3 - __float_as_int(-y.x)),
+                         __int_as_float(0x7EF311C3 - __float_as_int(-y.y)));
+    const uint64_t two = f2_make(2.0f, 2.0f);
+    r = mul2(r, fma2(ny, r, two));
+    r = mul2(r, fma2(ny, r, two));
+    return mul2(g, r);
+}
+
 __device__ __forceinline__ float gelu_tanh(float x) {
     const float alpha = sqrtf(2.0f / 3.14159265358979323846f);  // as transformer_ops.cpp:16
     return 0.5f * x * (1.0f + tanhf(alpha * (x + 0.044715f * x * x * x)));

@@ -24,60 +24,6 @@ constexpr int kTileW = 64;      // widest image row handled by the tiled path
 // last column pair's four-pixel window stays inside the row.
 __host__ __device__ __forceinline__ int tile_pixels(int W) { return W + 2 + (W & 1); }
 
-// Packed fp32 pairs (sm_100 f32x2): a 64-bit register holds two channels' fp32 values and
-// one instruction does the arithmetic of both. Values stay in that form from the bf16 load
-// to the final GLU, so no pack / unpack sits between the multiply-adds.
-__device__ __forceinline__ uint64_t f2_from_bf2(uint32_t u) {  // bf16 pair -> fp32 pair (exact)
-    uint64_t d;
-    asm("{\n\t.reg .b32 lo, hi;\n\tshl.b32 lo, %1, 16;\n\tand.b32 hi, %1, 0xffff0000;\n\tmov.b64 %0, {lo, hi};\n\t}"
-        : "=l"(d)
-        : "r"(u));
-    return d;
-}
-__device__ __forceinline__ uint64_t f2_make(float lo, float hi) {
-    uint64_t d;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
-    return d;
-}
-__device__ __forceinline__ float2 f2_split(uint64_t u) {
-    float lo, hi;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(u));
-    return make_float2(lo, hi);
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-// silu_fast (common.cuh) on a pair: the exponentials per lane, the rest pairwise.
-__device__ __forceinline__ uint64_t silu2(uint64_t g) {
-    const float2 x = f2_split(g);
-    const uint64_t e = f2_make(__expf(-fmaxf(x.x, -80.0f)), __expf(-fmaxf(x.y, -80.0f)));
-    const uint64_t ny = sub2(f2_make(-1.0f, -1.0f), e);  // -(1 + e)
-    const float2 y = f2_split(ny);
-    uint64_t r = f2_make(__int_as_float(0x7EF311C3 - __float_as_int(-y.x)),
-                         __int_as_float(0x7EF311C3 - __float_as_int(-y.y)));
-    const uint64_t two = f2_make(2.0f, 2.0f);
-    r = mul2(r, fma2(ny, r, two));
-    r = mul2(r, fma2(ny, r, two));
-    return mul2(g, r);
-}
-
 // Thread = (channel pair p of the tile = lane, column pair): it keeps its pair's 3x3 taps of
 // both halves in registers and walks the tile's input rows top to bottom, loading the four
 // pixels x0-1 .. x0+2 of each row once (4-byte shared loads, conflict-free across the warp)

@@ -14,6 +14,7 @@
 #include <cuda.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm.h"
@@ -109,6 +110,69 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
            (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// --- CTA-pair (cta_group::2) primitives ---------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// All threads of both CTAs of the cluster (release / acquire).
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The shared::cluster address of this CTA's shared-memory address `a` in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa(uint32_t a, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tmem_alloc2(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish2() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// M = 256 across the pair: rows 0-127 of A and columns [0, N/2) of B from the issuing CTA's
+// shared memory, rows 128-255 and columns [N/2, N) from the peer's, at the same addresses.
+__device__ __forceinline__ void umma2_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrives on the barrier at the same offset in both CTAs once this thread's MMAs complete.
+__device__ __forceinline__ void umma2_commit_both(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            bar),
+        "h"(static_cast<uint16_t>(3))
+        : "memory");
+}
+__device__ __forceinline__ void umma2_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+// TMA load into this CTA's shared memory that completes its bytes on `bar_cluster`, a
+// barrier of either CTA of the pair (here always the leader's). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t dst, uint32_t bar_cluster, int c0,
+                                                 int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1)
+        : "memory");
+}
+
 // --- epilogue -------------------------------------------------------------------------
 __device__ __forceinline__ void store_val(void* out, int is_bf16, long long idx, float v) {
     if (is_bf16) {
@@ -117,9 +181,6 @@ __device__ __forceinline__ void store_val(void* out, int is_bf16, long long idx,
         static_cast<float*>(out)[idx] = v;
     }
 }
-
-// SiLU for the tensor-core path's epilogue (bf16 outputs only): CUDA's fast exponential and
-// a correctly rounded reciprocal.
 
 // Residual and gate values of 16 consecutive columns [n0, n0+16) of one row, fetched one
 // chunk ahead of their use so the epilogue does not wait on global-memory latency.
@@ -187,7 +248,11 @@ __device__ __forceinline__ void epilogue16(const Epilogue& ep, int row, int n0, 
     }
     if (ep.act == kActSilu) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = silu_fast(v[j]);
+        for (int j = 0; j < 16; j += 2) {
+            const float2 y = f2_split(silu2(f2_make(v[j], v[j + 1])));
+            v[j] = y.x;
+            v[j + 1] = y.y;
+        }
     } else if (ep.act == kActGelu) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = gelu_tanh(v[j]);
@@ -235,6 +300,38 @@ __device__ __forceinline__ void epilogue16(const Epilogue& ep, int row, int n0, 
         if (ep.out) store_val(ep.out, ep.out_bf16, static_cast<long long>(row) * ep.ldo + n, x);
         if (ep.out2) store_val(ep.out2, ep.out2_bf16, static_cast<long long>(row) * ep.ldo2 + n,
                                ep.act2 == kActSilu ? silu(x) : x);
+    }
+}
+
+// One epilogue warp's share of a tile: row `row` (the warp's TMEM lane quarter + lane) and
+// kCols columns from n_start, read from TMEM at t_addr. TMEM loads go out two 16-column
+// chunks at a time, so each wait covers 32 columns; the residual / gate of the next chunk
+// is fetched before the current one is finished.
+template <int kCols>
+__device__ __forceinline__ void epilogue_span(const Epilogue& ep, int row, bool row_ok, int n_start, int N, bool vec,
+                                              uint32_t t_addr) {
+    constexpr int kChunks = kCols / 16;
+    static_assert(kChunks % 2 == 0, "chunks go out in pairs");
+    Side16 sd[2];
+    if (row_ok && n_start < N) fetch16(ep, row, n_start, N, vec, sd[0]);
+#pragma unroll
+    for (int c = 0; c < kChunks; c += 2) {
+        uint32_t r[2][16];
+        tmem_ld16(t_addr + static_cast<uint32_t>(c * 16), r[0]);
+        tmem_ld16(t_addr + static_cast<uint32_t>((c + 1) * 16), r[1]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+            const int cc = c + g;
+            const int n0 = n_start + cc * 16;
+            if (cc + 1 < kChunks && row_ok && n0 + 16 < N) fetch16(ep, row, n0 + 16, N, vec, sd[(cc + 1) & 1]);
+            if (row_ok && n0 < N) {
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[g][j]);
+                epilogue16(ep, row, n0, N, v, vec, sd[cc & 1]);
+            }
+        }
     }
 }
 
@@ -369,7 +466,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         const int q = warp & 3;                   // TMEM lane quarter this warp may access
         const int chalf = (warp - 2) / 4;         // which half of the tile's columns
-        constexpr int kChunks = BN / 2 / 16;      // 16-column chunks per warp
         int local = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const int acc = local & 1;
@@ -383,22 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int col0 = chalf * (BN / 2);
             const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + col0);
-            Side16 sd[2];
-            if (row_ok && n_blk * BN + col0 < N) fetch16(ep, row, n_blk * BN + col0, N, vec != 0, sd[0]);
-#pragma unroll
-            for (int c = 0; c < kChunks; ++c) {
-                const int n0 = n_blk * BN + col0 + c * 16;
-                if (c + 1 < kChunks && row_ok && n0 + 16 < N) fetch16(ep, row, n0 + 16, N, vec != 0, sd[(c + 1) & 1]);
-                uint32_t r[16];
-                tmem_ld16(t_row + static_cast<uint32_t>(c * 16), r);
-                tmem_wait_ld();
-                if (row_ok && n0 < N) {
-                    float v[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-                    epilogue16(ep, row, n0, N, v, vec != 0, sd[c & 1]);
-                }
-            }
+            epilogue_span<BN / 2>(ep, row, row_ok, n_blk * BN + col0, N, vec != 0, t_row);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty(acc));
@@ -410,6 +491,201 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, C::kTmemCols);
+    }
+}
+
+// --- the CTA-pair kernel -------------------------------------------------------------------
+// The same pipeline over a cluster of two CTAs on two SMs computing 256 x BN tiles with
+// tcgen05.mma.cta_group::2: each CTA stages its own 128 rows of A and BN/2 rows of B per
+// k-block (the shared-memory traffic per FLOP drops by a quarter against 128 x BN tiles,
+// and 7-8 stages fit), the leader CTA (rank 0) issues the MMAs, and each CTA's TMEM holds
+// its 128 rows of the accumulator for its own epilogue warps.
+//   full[s]    leader only: armed by the leader's producer with both CTAs' bytes; both
+//              CTAs' TMA loads complete on it
+//   empty[s]   both CTAs: the leader's MMA commit arrives on both
+//   tfull[a]   both CTAs: the leader's commit after a tile's last MMA arrives on both
+//   tempty[a]  leader only: one arrival per epilogue warp of either CTA
+// Every wait is bounded; on expiry each role stops issuing work and every thread still
+// reaches the final cluster barrier, so neither CTA leaves while its peer uses its memory.
+template <int BN>
+struct Cfg2 {
+    static constexpr int kBH = BN / 2;  // B rows per CTA
+    static constexpr int kABytes = 128 * BK * 2;
+    static constexpr int kBBytes = kBH * BK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = BN == 128 ? 8 : (BN == 192 ? 7 : 6);
+    static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
+    static constexpr int kBarOffset = kStages * kStageBytes;
+    static constexpr int kSmemBytes = kBarOffset + (2 * kStages + 5) * 8 + 16 + 1024;
+};
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
+                    int N, int K, Epilogue ep, int vec, int* err) {
+    using C = Cfg2<BN>;
+    constexpr int S = C::kStages;
+    constexpr int BM2 = 2 * BM;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* gbase = smem_raw + (base - raw);
+    const uint32_t a_smem = base;
+    const uint32_t b_smem = base + S * C::kABytes;
+    const uint32_t bars = base + C::kBarOffset;
+    auto full = [&](int s) { return bars + 8u * s; };
+    auto empty = [&](int s) { return bars + 8u * (S + s); };
+    auto tfull = [&](int a) { return bars + 8u * (2 * S + a); };
+    auto tempty = [&](int a) { return bars + 8u * (2 * S + 2 + a); };
+    const uint32_t done_bar = bars + 8u * (2 * S + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kBarOffset + (2 * S + 5) * 8);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1;
+    const int npairs = gridDim.x >> 1;
+    const int num_m = (M + BM2 - 1) / BM2;
+    const int num_n = (N + BN - 1) / BN;
+    const int num_tiles = num_m * num_n;
+    const int num_kb = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull(a), 1);
+            mbar_init(tempty(a), 2 * kEpiWarps);
+        }
+        mbar_init(done_bar, 1);
+        fence_barrier_init();
+    }
+    cluster_sync();  // barriers of both CTAs initialised before any remote arrival
+    if (warp == 1) {
+        tmem_alloc2(smem_u32(tmem_slot), C::kTmemCols);
+        tmem_relinquish2();
+    }
+    tc_fence_before();
+    cluster_sync();  // both CTAs' accumulator columns exist before the leader's first MMA
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t full_leader = mapa(full(0), 0);
+    const uint32_t tempty_leader = mapa(tempty(0), 0);
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+            int stage = 0;
+            uint32_t phase = 0;
+            long long issued = 0;
+            bool ok = true;
+            for (int tile = pair; ok && tile < num_tiles; tile += npairs) {
+                const int m_blk = tile / num_n;
+                const int n_blk = tile % num_n;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(empty(stage), phase ^ 1u, err, kTimeout)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_arrive_expect_tx(full(stage), 2 * C::kStageBytes);
+                    const uint32_t fb = full_leader + 8u * stage;
+                    tma_load_2d_pair(&tmA, a_smem + stage * C::kABytes, fb, kb * BK,
+                                     m_blk * BM2 + static_cast<int>(rank) * BM);
+                    tma_load_2d_pair(&tmB, b_smem + stage * C::kBBytes, fb, kb * BK,
+                                     n_blk * BN + static_cast<int>(rank) * C::kBH);
+                    ++issued;
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok || *(volatile int*)err != 0) {
+                // Drain (bounded): the leader waits for its last armed stages to fill; the
+                // peer for the MMAs that consume its last copies to release them.
+                const long long first = issued > S ? issued - S : 0;
+                for (long long i = first; i < issued; ++i) {
+                    const int st = static_cast<int>(i % S);
+                    const uint32_t ph = static_cast<uint32_t>((i / S) & 1);
+                    if (leader) mbar_wait_quiet(full(st), ph);
+                    else mbar_wait_quiet(empty(st), ph);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_bf16_f32(BM2, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int local = 0;
+            for (int tile = pair; ok && tile < num_tiles; tile += npairs, ++local) {
+                const int acc = local & 1;
+                const uint32_t use = static_cast<uint32_t>(local >> 1);
+                if (!mbar_wait(tempty(acc), (use & 1u) ^ 1u, err, kTimeout)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(full(stage), phase, err, kTimeout)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = a_smem + stage * C::kABytes;
+                    const uint32_t b_addr = b_smem + stage * C::kBBytes;
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        umma2_bf16(d_tmem, kmajor_sw128_desc(a_addr + k * 32), kmajor_sw128_desc(b_addr + k * 32),
+                                   idesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    umma2_commit_both(empty(stage));
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma2_commit_both(tfull(acc));
+            }
+            umma2_commit(done_bar);
+            mbar_wait_quiet(done_bar, 0u);
+        }
+    } else {
+        const int q = warp & 3;
+        const int chalf = (warp - 2) / 4;
+        int local = 0;
+        for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
+            const int acc = local & 1;
+            const uint32_t use = static_cast<uint32_t>(local >> 1);
+            if (!mbar_wait(tfull(acc), use & 1u, err, kTimeout)) break;
+            tc_fence_after();
+            const int m_blk = tile / num_n;
+            const int n_blk = tile % num_n;
+            const int row = m_blk * BM2 + static_cast<int>(rank) * BM + q * 32 + lane;
+            const bool row_ok = row < M;
+            const int col0 = chalf * (BN / 2);
+            const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN + col0);
+            epilogue_span<BN / 2>(ep, row, row_ok, n_blk * BN + col0, N, vec != 0, t_row);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * acc);
+        }
+    }
+
+    tc_fence_before();
+    __syncwarp();
+    cluster_sync();  // no CTA leaves while its peer may still use its memory or TMEM
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc2(tmem, C::kTmemCols);
     }
 }
 
@@ -450,6 +726,43 @@ static void launch(const GemmProblem& p, int* err, cudaStream_t stream, int num_
     SANA_CUDA(cudaGetLastError());
 }
 
+template <int BN>
+static void launch2(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
+    using C = Cfg2<BN>;
+    static bool attr_done = false;
+    if (!attr_done) {
+        SANA_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::kSmemBytes));
+        attr_done = true;
+    }
+    const CUtensorMap ma = make_map(p.A, p.M, p.K, p.lda, BM);
+    const CUtensorMap mb = make_map(p.B, p.N, p.K, p.ldb, C::kBH);
+    const Epilogue& e = p.ep;
+    auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    bool vec = (p.N % 16 == 0);
+    if (e.bias) vec = vec && a16(e.bias);
+    if (e.resid) vec = vec && a16(e.resid) && (e.ldr % 4 == 0);
+    if (e.gate) vec = vec && a16(e.gate) && (e.gate_ld % 4 == 0);
+    if (e.out) vec = vec && a16(e.out) && (e.ldo % 8 == 0);
+    if (e.out2) vec = vec && a16(e.out2) && (e.ldo2 % 8 == 0);
+    const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + BN - 1) / BN);
+    const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
+    gemm_tc2_kernel<BN><<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(ma, mb, p.M, p.N, p.K, e, vec ? 1 : 0,
+                                                                         err);
+    SANA_CUDA(cudaGetLastError());
+}
+
+// CTA-pair tiles for tall problems (the block projections: M = sequences x tokens); the
+// single-CTA kernel otherwise. SANA_GEMM_PAIR=0 in the environment selects the single-CTA
+// kernel for every shape.
+static bool use_pair(const GemmProblem& p, int num_sms) {
+    static const bool enabled = [] {
+        const char* v = std::getenv("SANA_GEMM_PAIR");
+        return !(v && v[0] == '0');
+    }();
+    return enabled && num_sms >= 2 && p.M >= 2048;
+}
+
 }  // namespace tc
 
 bool gemm_tc_supported(const GemmProblem& p) {
@@ -460,10 +773,17 @@ bool gemm_tc_supported(const GemmProblem& p) {
 
 void gemm_tc(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
     SANA_REQUIRE(gemm_tc_supported(p), "gemm_tc: unsupported problem");
-    // 128 x 192 tiles when they divide N (every projection width of the model: 1152, 2304,
-    // 3456, 5760), 128 x 128 otherwise.
-    if (p.N % 192 == 0) tc::launch<192>(p, err, stream, num_sms);
-    else tc::launch<128>(p, err, stream, num_sms);
+    // The MMA costs the same issue time for any N up to 256, so tiles are 256 wide whenever
+    // N allows (the last one ragged: its out-of-range B rows read as zero and its columns
+    // are masked in the epilogue); narrow problems use 128 columns.
+    const bool pair = tc::use_pair(p, num_sms);
+    if (p.N >= 256) {
+        if (pair) tc::launch2<256>(p, err, stream, num_sms);
+        else tc::launch<256>(p, err, stream, num_sms);
+    } else {
+        if (pair) tc::launch2<128>(p, err, stream, num_sms);
+        else tc::launch<128>(p, err, stream, num_sms);
+    }
 }
 
 static std::atomic<long long> g_tc_launches{0}, g_simt_launches{0};
