@@ -33,8 +33,9 @@ struct Cfg {
     static constexpr int kBBytes = BN * BK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;  // power of two >= two accumulators
-    // layout: [A stages][B stages][barriers][tmem slot]
-    static constexpr int kBarOffset = kStages * kStageBytes;
+    // layout: [A stages][B stages][epilogue staging][barriers][tmem slot]
+    static constexpr int kEpiOffset = kStages * kStageBytes;
+    static constexpr int kBarOffset = kEpiOffset + 8 * 32 * 64;
     static constexpr int kSmemBytes = kBarOffset + (2 * kStages + 5) * 8 + 16 + 1024;
 };
 
@@ -226,7 +227,103 @@ __device__ __forceinline__ void fetch16(const Epilogue& ep, int row, int n0, int
     }
 }
 
+// Bias, activation and gated residual on 16 consecutive columns [n0, n0+16) of one row,
+// all of them in range (the fast path); the stores are the caller's.
+template <bool kResid>
+__device__ __forceinline__ void compute16(const Epilogue& ep, int n0, float (&v)[16], const float (&rv)[16],
+                                          const float (&gv)[16]) {
+    if (ep.bias) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+            const float4 b = *reinterpret_cast<const float4*>(ep.bias + n0 + j);
+            v[j] += b.x;
+            v[j + 1] += b.y;
+            v[j + 2] += b.z;
+            v[j + 3] += b.w;
+        }
+    }
+    if (ep.act == kActSilu) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+            const float2 y = f2_split(silu2(f2_make(v[j], v[j + 1])));
+            v[j] = y.x;
+            v[j + 1] = y.y;
+        }
+    } else if (ep.act == kActGelu) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = gelu_tanh(v[j]);
+    }
+    if (kResid) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = rv[j] + gv[j] * v[j];
+    }
+}
+
+// --- coalesced stores through a per-warp staging block ----------------------------------
+// Each lane holds one row of the tile; storing straight from there writes 32 rows x 16 bytes
+// per instruction. Instead a warp writes its 32 rows x 64 bytes into shared memory and
+// stores them back as 8 rows x 64 bytes per instruction (full 32-byte sectors). 16-byte slot
+// k of row r sits at slot 4r + (k ^ ((r >> 1) & 3)): both the row writes and the row-group
+// reads then touch eight distinct bank groups per quarter-warp.
+constexpr int kEpiStageBytes = 32 * 64;  // per epilogue warp
+
+__device__ __forceinline__ uint32_t stage_slot(int r, int k) { return static_cast<uint32_t>(4 * r + (k ^ ((r >> 1) & 3))) * 16u; }
+
+// The lane's 64 bytes (4 x 16) into its staging row.
+__device__ __forceinline__ void stage_put(uint8_t* stg, int lane, const uint4 (&w)[4]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4*>(stg + stage_slot(lane, k)) = w[k];
+}
+// The staged 32 x 64 bytes to global rows row0 .. row0+31 (rows >= M skipped) at byte
+// offset col_bytes of rows ld_bytes apart.
+__device__ __forceinline__ void stage_flush(const uint8_t* stg, int lane, uint8_t* gout, long long ld_bytes,
+                                            long long col_bytes, int row0, int M) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = 8 * i + lane / 4, k = lane % 4;
+        if (row0 + r < M)
+            *reinterpret_cast<uint4*>(gout + static_cast<long long>(row0 + r) * ld_bytes + col_bytes + 16 * k) =
+                *reinterpret_cast<const uint4*>(stg + stage_slot(r, k));
+    }
+}
+__device__ __forceinline__ void pack_bf16x16(const float (&v)[16], uint4 (&w)[2]) {
+    uint32_t* u = reinterpret_cast<uint32_t*>(w);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        u[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+}
+// Stores 32 columns [n0, n0+32) of the warp's 32 rows to one output (bf16 or fp32).
+__device__ __forceinline__ void store32(uint8_t* stg, int lane, void* out, int is_bf16, long long ld, int row0,
+                                        int M, int n0, const float (&v0)[16], const float (&v1)[16]) {
+    uint8_t* g = static_cast<uint8_t*>(out);
+    if (is_bf16) {
+        uint4 w[4];
+        pack_bf16x16(v0, *reinterpret_cast<uint4(*)[2]>(&w[0]));
+        pack_bf16x16(v1, *reinterpret_cast<uint4(*)[2]>(&w[2]));
+        stage_put(stg, lane, w);
+        __syncwarp();
+        stage_flush(stg, lane, g, ld * 2, static_cast<long long>(n0) * 2, row0, M);
+        __syncwarp();
+    } else {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float(&v)[16] = h ? v1 : v0;
+            uint4 w[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) w[k] = make_uint4(__float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]),
+                                                          __float_as_uint(v[4 * k + 2]), __float_as_uint(v[4 * k + 3]));
+            stage_put(stg, lane, w);
+            __syncwarp();
+            stage_flush(stg, lane, g, ld * 4, static_cast<long long>(n0 + 16 * h) * 4, row0, M);
+            __syncwarp();
+        }
+    }
+}
+
 // Applies the epilogue to 16 consecutive columns [n0, n0+16) of one row.
+template <bool kResid>
 __device__ __forceinline__ void epilogue16(const Epilogue& ep, int row, int n0, int N, float (&v)[16], bool vec,
                                            const Side16& sd) {
     const bool full = vec && n0 + 16 <= N;
@@ -257,7 +354,7 @@ __device__ __forceinline__ void epilogue16(const Epilogue& ep, int row, int n0, 
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = gelu_tanh(v[j]);
     }
-    if (ep.resid) {
+    if (kResid) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = sd.r[j] + sd.g[j] * v[j];
     }
@@ -303,33 +400,119 @@ __device__ __forceinline__ void epilogue16(const Epilogue& ep, int row, int n0, 
     }
 }
 
-// One epilogue warp's share of a tile: row `row` (the warp's TMEM lane quarter + lane) and
-// kCols columns from n_start, read from TMEM at t_addr. TMEM loads go out two 16-column
-// chunks at a time, so each wait covers 32 columns; the residual / gate of the next chunk
-// is fetched before the current one is finished.
-template <int kCols>
-__device__ __forceinline__ void epilogue_span(const Epilogue& ep, int row, bool row_ok, int n_start, int N, bool vec,
-                                              uint32_t t_addr) {
+// Residual of one 16-column chunk of the warp's 32 rows, loaded coalesced: lane l holds rows
+// 8i + l/4 (i = 0..3), 16-byte slot l%4. resid_rows() hands every lane its own row back
+// through the staging block.
+struct ResidChunk {
+    uint4 q[4];
+};
+__device__ __forceinline__ void resid_fetch(const Epilogue& ep, int row0, int M, int n0, ResidChunk& rc) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = 8 * i + lane / 4;
+        rc.q[i] = row0 + r < M ? *reinterpret_cast<const uint4*>(ep.resid + static_cast<long long>(row0 + r) * ep.ldr +
+                                                                 n0 + 4 * (lane % 4))
+                               : make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+__device__ __forceinline__ void resid_rows(uint8_t* stg, const ResidChunk& rc, float (&rv)[16]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        *reinterpret_cast<uint4*>(stg + stage_slot(8 * i + lane / 4, lane % 4)) = rc.q[i];
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint4 w = *reinterpret_cast<const uint4*>(stg + stage_slot(lane, k));
+        rv[4 * k] = __uint_as_float(w.x);
+        rv[4 * k + 1] = __uint_as_float(w.y);
+        rv[4 * k + 2] = __uint_as_float(w.z);
+        rv[4 * k + 3] = __uint_as_float(w.w);
+    }
+    __syncwarp();
+}
+// The gate values of one row's 16 columns (1 when the epilogue has no gate).
+__device__ __forceinline__ void gate16(const Epilogue& ep, int row, int n0, float (&gv)[16]) {
+    if (ep.gate) {
+        const float* g = ep.gate + static_cast<long long>(row / ep.rows_per_gate) * ep.gate_ld + n0;
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(g + j);
+            gv[j] = v.x;
+            gv[j + 1] = v.y;
+            gv[j + 2] = v.z;
+            gv[j + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) gv[j] = 1.f;
+    }
+}
+
+// One epilogue warp's share of a tile: rows row0 .. row0+31 (lane = row - row0, the warp's
+// TMEM lane quarter) and kCols columns from n_start, read from TMEM at t_addr. TMEM loads go
+// out two 16-column chunks at a time (one wait per 32 columns). Batches of 32 columns inside
+// N with vector-aligned operands take the coalesced path (residual loaded a chunk ahead,
+// outputs stored through the staging block `stg`); the rest go element by element.
+template <int kCols, bool kResid>
+__device__ __forceinline__ void epilogue_span(const Epilogue& ep, int row0, int M, int n_start, int N, bool vec,
+                                              uint32_t t_addr, uint8_t* stg) {
     constexpr int kChunks = kCols / 16;
     static_assert(kChunks % 2 == 0, "chunks go out in pairs");
-    Side16 sd[2];
-    if (row_ok && n_start < N) fetch16(ep, row, n_start, N, vec, sd[0]);
-#pragma unroll
+    const int lane = threadIdx.x & 31;
+    const int row = row0 + lane;
+    const bool row_ok = row < M;
+    auto fast = [&](int cc) { const int b = n_start + (cc / 2) * 32; return vec && b + 32 <= N; };
+    // rc holds the coalesced residual of the next chunk to use: it is handed out, refilled with
+    // the following chunk, and that load completes while the current chunk is finished
+    ResidChunk rc;
+    if (kResid && fast(0)) resid_fetch(ep, row0, M, n_start, rc);
+#pragma unroll 1
     for (int c = 0; c < kChunks; c += 2) {
         uint32_t r[2][16];
         tmem_ld16(t_addr + static_cast<uint32_t>(c * 16), r[0]);
         tmem_ld16(t_addr + static_cast<uint32_t>((c + 1) * 16), r[1]);
         tmem_wait_ld();
+        const int n0 = n_start + c * 16;
+        if (n0 >= N) continue;  // uniform across the warp
+        if (fast(c)) {
+            float v[2][16];
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[g][j] = __uint_as_float(r[g][j]);
+                float rv[16], gv[16];
+                if (kResid) {
+                    resid_rows(stg, rc, rv);
+                    if (g == 0) resid_fetch(ep, row0, M, n0 + 16, rc);
+                    else if (c + 2 < kChunks && fast(c + 2)) resid_fetch(ep, row0, M, n0 + 32, rc);
+                    if (row_ok) gate16(ep, row, n0 + 16 * g, gv);
+                }
+                compute16<kResid>(ep, n0 + 16 * g, v[g], rv, gv);
+            }
+            if (ep.out) store32(stg, lane, ep.out, ep.out_bf16, ep.ldo, row0, M, n0, v[0], v[1]);
+            if (ep.out2) {
+                if (ep.act2 == kActSilu) {
+#pragma unroll
+                    for (int g = 0; g < 2; ++g)
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[g][j] = silu(v[g][j]);
+                }
+                store32(stg, lane, ep.out2, ep.out2_bf16, ep.ldo2, row0, M, n0, v[0], v[1]);
+            }
+            continue;
+        }
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
-            const int cc = c + g;
-            const int n0 = n_start + cc * 16;
-            if (cc + 1 < kChunks && row_ok && n0 + 16 < N) fetch16(ep, row, n0 + 16, N, vec, sd[(cc + 1) & 1]);
-            if (row_ok && n0 < N) {
+            const int n1 = n0 + g * 16;
+            if (row_ok && n1 < N) {
+                Side16 sd;
+                if (kResid) fetch16(ep, row, n1, N, vec, sd);
                 float v[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[g][j]);
-                epilogue16(ep, row, n0, N, v, vec, sd[cc & 1]);
+                epilogue16<kResid>(ep, row, n1, N, v, vec, sd);
             }
         }
     }
@@ -339,7 +522,7 @@ __device__ __forceinline__ void epilogue_span(const Epilogue& ep, int row, bool 
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 
-template <int BN>
+template <int BN, bool kResid>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
                    int N, int K, Epilogue ep, int vec, int* err) {
@@ -474,12 +657,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int m_blk = tile / num_n;
             const int n_blk = tile % num_n;
-            const int row = m_blk * BM + q * 32 + lane;
-            const bool row_ok = row < M;
             const int col0 = chalf * (BN / 2);
             const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + col0);
-            epilogue_span<BN / 2>(ep, row, row_ok, n_blk * BN + col0, N, vec != 0, t_row);
+            epilogue_span<BN / 2, kResid>(ep, m_blk * BM + q * 32, M, n_blk * BN + col0, N, vec != 0, t_row,
+                                  gbase + C::kEpiOffset + (warp - 2) * kEpiStageBytes);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty(acc));
@@ -515,11 +697,12 @@ struct Cfg2 {
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kStages = BN == 128 ? 8 : (BN == 192 ? 7 : 6);
     static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
-    static constexpr int kBarOffset = kStages * kStageBytes;
+    static constexpr int kEpiOffset = kStages * kStageBytes;
+    static constexpr int kBarOffset = kEpiOffset + 8 * 32 * 64;
     static constexpr int kSmemBytes = kBarOffset + (2 * kStages + 5) * 8 + 16 + 1024;
 };
 
-template <int BN>
+template <int BN, bool kResid>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
                     int N, int K, Epilogue ep, int vec, int* err) {
@@ -668,12 +851,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int m_blk = tile / num_n;
             const int n_blk = tile % num_n;
-            const int row = m_blk * BM2 + static_cast<int>(rank) * BM + q * 32 + lane;
-            const bool row_ok = row < M;
             const int col0 = chalf * (BN / 2);
             const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + col0);
-            epilogue_span<BN / 2>(ep, row, row_ok, n_blk * BN + col0, N, vec != 0, t_row);
+            epilogue_span<BN / 2, kResid>(ep, m_blk * BM2 + static_cast<int>(rank) * BM + q * 32, M, n_blk * BN + col0, N,
+                                  vec != 0, t_row, gbase + C::kEpiOffset + (warp - 2) * kEpiStageBytes);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * acc);
@@ -701,12 +883,12 @@ static CUtensorMap make_map(const void* ptr, int rows, int cols, long long ld, i
     return m;
 }
 
-template <int BN>
+template <int BN, bool kResid>
 static void launch(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
     using C = Cfg<BN>;
     static bool attr_done = false;
     if (!attr_done) {
-        SANA_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        SANA_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, kResid>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::kSmemBytes));
         attr_done = true;
     }
@@ -722,16 +904,16 @@ static void launch(const GemmProblem& p, int* err, cudaStream_t stream, int num_
     if (e.out2) vec = vec && a16(e.out2) && (e.ldo2 % 8 == 0);
     const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    gemm_tc_kernel<BN><<<grid, kThreads, C::kSmemBytes, stream>>>(ma, mb, p.M, p.N, p.K, e, vec ? 1 : 0, err);
+    gemm_tc_kernel<BN, kResid><<<grid, kThreads, C::kSmemBytes, stream>>>(ma, mb, p.M, p.N, p.K, e, vec ? 1 : 0, err);
     SANA_CUDA(cudaGetLastError());
 }
 
-template <int BN>
+template <int BN, bool kResid>
 static void launch2(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
     using C = Cfg2<BN>;
     static bool attr_done = false;
     if (!attr_done) {
-        SANA_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        SANA_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<BN, kResid>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::kSmemBytes));
         attr_done = true;
     }
@@ -747,7 +929,7 @@ static void launch2(const GemmProblem& p, int* err, cudaStream_t stream, int num
     if (e.out2) vec = vec && a16(e.out2) && (e.ldo2 % 8 == 0);
     const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + BN - 1) / BN);
     const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
-    gemm_tc2_kernel<BN><<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(ma, mb, p.M, p.N, p.K, e, vec ? 1 : 0,
+    gemm_tc2_kernel<BN, kResid><<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(ma, mb, p.M, p.N, p.K, e, vec ? 1 : 0,
                                                                          err);
     SANA_CUDA(cudaGetLastError());
 }
@@ -777,12 +959,13 @@ void gemm_tc(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
     // N allows (the last one ragged: its out-of-range B rows read as zero and its columns
     // are masked in the epilogue); narrow problems use 128 columns.
     const bool pair = tc::use_pair(p, num_sms);
+    const bool resid = p.ep.resid != nullptr;
     if (p.N >= 256) {
-        if (pair) tc::launch2<256>(p, err, stream, num_sms);
-        else tc::launch<256>(p, err, stream, num_sms);
+        if (pair) resid ? tc::launch2<256, true>(p, err, stream, num_sms) : tc::launch2<256, false>(p, err, stream, num_sms);
+        else resid ? tc::launch<256, true>(p, err, stream, num_sms) : tc::launch<256, false>(p, err, stream, num_sms);
     } else {
-        if (pair) tc::launch2<128>(p, err, stream, num_sms);
-        else tc::launch<128>(p, err, stream, num_sms);
+        if (pair) resid ? tc::launch2<128, true>(p, err, stream, num_sms) : tc::launch2<128, false>(p, err, stream, num_sms);
+        else resid ? tc::launch<128, true>(p, err, stream, num_sms) : tc::launch<128, false>(p, err, stream, num_sms);
     }
 }
 
