@@ -47,6 +47,9 @@ NUM_STEPS = 20
 GUIDANCE = 4.5
 CAPTION_LEN = 300
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (read + write) of one FF-inverted projection launch at the default workload,
+# from the ncu capture summarised in profiles/gemm_tc2_ff_inverted_config2.md.
+FF_INVERTED_TRAFFIC_BYTES = 88_987_904 + 329_661_952
 
 
 def log(*a):
@@ -484,6 +487,11 @@ def run_cuda(args):
     gemm_ms = sum(prof[k][1] for k in gemm_names if k in prof)
     gemm_fl = sum(classes[k][1] * prof[k][0] for k in gemm_names if k in prof)
     achieved = gemm_fl / (gemm_ms / 1e3) / 1e12
+    # the dominant kernel: the FF-inverted projection (the loop's largest launch)
+    ff_n, ff_total_ms = prof.get("gemm_ff_inverted", (0, 0.0))
+    ff_flops = classes["gemm_ff_inverted"][1]
+    ff_ms_launch = ff_total_ms / max(ff_n, 1)
+    ff_achieved = ff_flops / (ff_ms_launch / 1e3) / 1e12 if ff_n else None
     loop_ms = sum(v[1] for v in prof.values())
     breakdown = {}
     for k, (n, ms_k) in sorted(prof.items(), key=lambda kv: -kv[1][1]):
@@ -517,12 +525,20 @@ def run_cuda(args):
             "denoiser_steps_per_s": images_per_s * NUM_STEPS,
             "wall_s_timed_region": wall,
             "roofline": {"bound": "tensor",
-                         "kernel": "gemm_tc_kernel (tcgen05.mma kind::f16 128x192 tiles, TMA, TMEM accumulators)",
-                         "achieved": achieved, "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                         "frac": achieved / pk["bf16_tflops_sustained"],
+                         "kernel": "gemm_tc2_kernel<256> FF-inverted projection (tcgen05.mma.cta_group::2, "
+                                   "256x256 tiles, TMA, TMEM accumulators, +bias +SiLU epilogue)",
+                         "achieved": ff_achieved, "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                         "frac": ff_achieved / pk["bf16_tflops_sustained"],
+                         "algorithmic_per_launch": ff_flops, "launches": ff_n, "avg_launch_ms": ff_ms_launch,
                          "peak_source": f"{pk_kind} bf16_tflops_sustained (kernel timed inside the loop)",
-                         "measured": "CUDA events around every block projection of one eager loop on the launch stream",
-                         "traffic": None, "isolated_per_shape": per_shape},
+                         "measured": "CUDA events around every launch of one eager loop on the launch stream",
+                         # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel at this
+                         # workload (M=32768, K=1152, N=5760) from the ncu capture summarised in
+                         # profiles/gemm_tc2_ff_inverted_config2.md (algorithmic bytes: 466 MB)
+                         "traffic": FF_INVERTED_TRAFFIC_BYTES if B == 16 else None, "traffic_unit": "bytes",
+                         "all_block_gemms": {"achieved": achieved, "unit": "TFLOP/s",
+                                             "frac": achieved / pk["bf16_tflops_sustained"]},
+                         "isolated_per_shape": per_shape},
             "kernels": breakdown,
             "model_flops": {"per_loop_tflop": flops / 1e12, "achieved_tflops": flops / (ms_per_step / 1e3) / 1e12,
                             "frac_of_sustained_peak": flops / (ms_per_step / 1e3) / 1e12 / pk["bf16_tflops_sustained"],
