@@ -202,6 +202,24 @@ int sana_op_cross_attention_block(sana_cuda_ctx *ctx, const float *x, int B, int
 /* apply_classifier_free_guidance (transformer.cpp:570-602): noise [2B, Cl, H, W] -> [B, Cl, H, W]. */
 int sana_op_cfg(sana_cuda_ctx *ctx, const float *noise, int B, int Cl, int H, int W, float guidance, float *out);
 
+/* split_heads_3d (transformer_ops.cpp:83-122): [B, T, hidden] -> [B, heads, T, hidden/heads]. */
+int sana_op_split_heads(sana_cuda_ctx *ctx, const float *in, int B, int T, int hidden, int heads, float *out);
+/* merge_heads_4d (transformer_ops.cpp:128-171): [B, H, T, D] -> [B, T, H*D]. */
+int sana_op_merge_heads(sana_cuda_ctx *ctx, const float *in, int B, int H, int T, int D, float *out);
+/* attention_scores_4d (transformer_ops.cpp:178-225): unscaled q k^T per (batch, head);
+ * q [B, H, Tq, D], k [B, H, Tk, D] -> [B, H, Tq, Tk]. */
+int sana_op_attention_scores(sana_cuda_ctx *ctx, const float *q, const float *k, int B, int H, int Tq, int Tk, int D,
+                             float *out);
+/* softmax_lastdim_4d (transformer_ops.cpp:278-339) over `rows` rows of n values. */
+int sana_op_softmax_lastdim(sana_cuda_ctx *ctx, const float *in, long long rows, int n, float *out);
+/* attention_values_4d (transformer_ops.cpp:232-273): probs [B, H, Tq, Tk] . v [B, H, Tk, D]. */
+int sana_op_attention_values(sana_cuda_ctx *ctx, const float *probs, const float *v, int B, int H, int Tq, int Tk,
+                             int D, float *out);
+/* compute_sana_block_modulation (transformer.cpp:496-542): t_mod [B, 6C] + table [6, C]
+ * -> [B, 6C]; its six C-wide column blocks are shift_msa, scale_msa, gate_msa, shift_mlp,
+ * scale_mlp, gate_mlp. */
+int sana_op_block_modulation(sana_cuda_ctx *ctx, const float *tmod, const float *table, int B, int C, float *out);
+
 /* --- device-pointer kernels (microbenchmarks; bf16 activations, token-major, asynchronous
  *     on the handle's stream) ------------------------------------------------------------ */
 

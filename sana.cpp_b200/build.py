@@ -4,8 +4,11 @@
 
 Compiles ``csrc/*.cu`` for sm_100a only (``-gencode arch=compute_100a,code=sm_100a``) and
 links ``lib/libsana_cuda.so`` (CUDA runtime linked statically, C ABI of
-``include/sana_cuda.h``). Objects go to ``build/`` (git-ignored); the ``.so`` stays in the
-tree so it travels with the repository snapshot.
+``include/sana_cuda.h``), then the C++17 host layer ``host/*.cpp`` (the reference's
+transformer.h / transformer_ops.h / scheduler.h entry points over that C ABI) into
+``lib/libsana_shim.so``; ``host/tensor.cpp`` is left out of it (a sana.cpp build brings its own
+Tensor). Objects go to ``build/`` (git-ignored); the ``.so`` files stay in the tree so they
+travel with the repository snapshot.
 """
 from __future__ import annotations
 
@@ -22,7 +25,12 @@ CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "build")
 LIB = os.path.join(HERE, "lib")
 SO = os.path.join(LIB, "libsana_cuda.so")
+SHIM_SO = os.path.join(LIB, "libsana_shim.so")
 INCLUDE = os.path.join(ROOT, "include")
+HOST = os.path.join(HERE, "host")
+CXX = os.environ.get("CXX_HOST", "g++")
+HOST_FLAGS = ["-std=c++17", "-O2", "-fPIC", "-Wall", "-Wextra", "-I", INCLUDE, "-I", os.path.join(HOST, "include"),
+              "-I", HOST]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc" if os.path.exists("/usr/local/cuda/bin/nvcc") else "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -65,7 +73,32 @@ def build(force: bool = False, ptxas_v: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    build_shim(force)
     return SO
+
+
+def _host_headers():
+    return glob.glob(os.path.join(HOST, "*.h")) + glob.glob(os.path.join(HOST, "include", "*.h")) + \
+        glob.glob(os.path.join(INCLUDE, "*.h"))
+
+
+def build_shim(force: bool = False) -> str:
+    """lib/libsana_shim.so from host/*.cpp except tensor.cpp, linked against libsana_cuda.so."""
+    srcs = sorted(s for s in glob.glob(os.path.join(HOST, "*.cpp")) if os.path.basename(s) != "tensor.cpp")
+    objs = []
+    for src in srcs:
+        obj = os.path.join(OBJ, "host_" + os.path.basename(src)[:-4] + ".o")
+        if force or _stale(obj, [src] + _host_headers()):
+            r = subprocess.run([CXX] + HOST_FLAGS + ["-c", src, "-o", obj], capture_output=True, text=True)
+            if r.returncode != 0:
+                raise RuntimeError(f"{CXX} failed for {src}:\n{r.stdout}\n{r.stderr}")
+        objs.append(obj)
+    if force or _stale(SHIM_SO, objs + [SO]):
+        cmd = [CXX, "-shared", "-o", SHIM_SO] + objs + ["-L", LIB, "-lsana_cuda", "-Wl,-rpath,$ORIGIN"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"shim link failed:\n{r.stdout}\n{r.stderr}")
+    return SHIM_SO
 
 
 if __name__ == "__main__":

@@ -765,6 +765,132 @@ int sana_op_cfg(sana_cuda_ctx* ctx, const float* noise, int B, int Cl, int H, in
     });
 }
 
+// --- the remaining transformer_ops.h / transformer.h pieces --------------------------------
+
+int sana_op_split_heads(sana_cuda_ctx* ctx, const float* in, int B, int T, int hidden, int heads, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(in && out && B >= 0 && T >= 0 && hidden >= 1, "invalid split_heads arguments");
+        SANA_REQUIRE(heads >= 1, "num_heads must be greater than 0");
+        SANA_REQUIRE(hidden % heads == 0, "hidden size must be divisible by num_heads");
+        sana::Engine& eng = engine(ctx);
+        const size_t n = static_cast<size_t>(B) * T * hidden;
+        DevBuf a = f32_upload(in, n), o;
+        o.ensure(std::max<size_t>(n, 1) * 4);
+        sana::permute_heads(a.as<float>(), o.as<float>(), B, T, heads, hidden / heads, true, eng.stream());
+        finish(eng);
+        d2h(out, o.get(), n * 4);
+    });
+}
+
+int sana_op_merge_heads(sana_cuda_ctx* ctx, const float* in, int B, int H, int T, int D, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(in && out && B >= 0 && H >= 0 && T >= 0 && D >= 0, "invalid merge_heads arguments");
+        sana::Engine& eng = engine(ctx);
+        const size_t n = static_cast<size_t>(B) * H * T * D;
+        DevBuf a = f32_upload(in, n), o;
+        o.ensure(std::max<size_t>(n, 1) * 4);
+        sana::permute_heads(a.as<float>(), o.as<float>(), B, T, H, D, false, eng.stream());
+        finish(eng);
+        d2h(out, o.get(), n * 4);
+    });
+}
+
+namespace {
+// Per (batch, head) products C_bh[M, N] = A_bh[M, K] . B_bh[N, K]^T on the handle's GEMM path
+// (tensor cores in bf16 mode where the shape allows, CUDA cores otherwise), fp32 output.
+void batched_gemm_nt(sana::Engine& eng, const ActBuf& A, const ActBuf& Bm, int batches, int M, int N, int K, float* C) {
+    const size_t es = A.bf ? 2 : 4;
+    for (int i = 0; i < batches; ++i) {
+        sana::GemmProblem p;
+        p.A = static_cast<const uint8_t*>(A.get()) + static_cast<size_t>(i) * M * K * es;
+        p.a_bf16 = A.bf;
+        p.lda = K;
+        p.B = static_cast<const uint8_t*>(Bm.get()) + static_cast<size_t>(i) * N * K * es;
+        p.b_bf16 = Bm.bf;
+        p.ldb = K;
+        p.M = M;
+        p.N = N;
+        p.K = K;
+        p.ep = epi(C + static_cast<size_t>(i) * M * N, false, N);
+        sana::gemm(p, eng.err(), eng.stream(), eng.num_sms());
+    }
+}
+}  // namespace
+
+int sana_op_attention_scores(sana_cuda_ctx* ctx, const float* q, const float* k, int B, int H, int Tq, int Tk, int D,
+                             float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(q && k && out && B >= 1 && H >= 1 && Tq >= 1 && Tk >= 1 && D >= 1,
+                     "invalid attention_scores arguments");
+        sana::Engine& eng = engine(ctx);
+        const bool bf = eng.mode() == sana::kModeBf16;
+        ActBuf Q, K;
+        Q.upload(q, static_cast<size_t>(B) * H * Tq * D, bf);
+        K.upload(k, static_cast<size_t>(B) * H * Tk * D, bf);
+        DevBuf o;
+        o.ensure(static_cast<size_t>(B) * H * Tq * Tk * 4);
+        batched_gemm_nt(eng, Q, K, B * H, Tq, Tk, D, o.as<float>());
+        finish(eng);
+        d2h(out, o.get(), static_cast<size_t>(B) * H * Tq * Tk * 4);
+    });
+}
+
+int sana_op_softmax_lastdim(sana_cuda_ctx* ctx, const float* in, long long rows, int n, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(in && out && rows >= 0 && n >= 1, "invalid softmax arguments");
+        sana::Engine& eng = engine(ctx);
+        const size_t count = static_cast<size_t>(rows) * n;
+        DevBuf a = f32_upload(in, count), o;
+        o.ensure(std::max<size_t>(count, 1) * 4);
+        sana::softmax_rows(a.as<float>(), rows, n, o.as<float>(), eng.stream());
+        finish(eng);
+        d2h(out, o.get(), count * 4);
+    });
+}
+
+int sana_op_attention_values(sana_cuda_ctx* ctx, const float* probs, const float* v, int B, int H, int Tq, int Tk,
+                             int D, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(probs && v && out && B >= 1 && H >= 1 && Tq >= 1 && Tk >= 1 && D >= 1,
+                     "invalid attention_values arguments");
+        sana::Engine& eng = engine(ctx);
+        const bool bf = eng.mode() == sana::kModeBf16;
+        const int BH = B * H;
+        ActBuf P, Vt;
+        P.upload(probs, static_cast<size_t>(BH) * Tq * Tk, bf);
+        DevBuf vd = f32_upload(v, static_cast<size_t>(BH) * Tk * D);
+        Vt.alloc(static_cast<size_t>(BH) * D * Tk, bf);  // per (b, h): v^T [D, Tk]
+        for (int i = 0; i < BH; ++i) {
+            const float* src = vd.as<float>() + static_cast<size_t>(i) * Tk * D;
+            if (bf) {
+                sana::repack<bf16>(src, Tk, D, true, static_cast<bf16*>(Vt.get()) + static_cast<size_t>(i) * D * Tk,
+                                   eng.stream());
+            } else {
+                sana::repack<float>(src, Tk, D, true, static_cast<float*>(Vt.get()) + static_cast<size_t>(i) * D * Tk,
+                                    eng.stream());
+            }
+        }
+        DevBuf o;
+        o.ensure(static_cast<size_t>(BH) * Tq * D * 4);
+        batched_gemm_nt(eng, P, Vt, BH, Tq, D, Tk, o.as<float>());
+        finish(eng);
+        d2h(out, o.get(), static_cast<size_t>(BH) * Tq * D * 4);
+    });
+}
+
+int sana_op_block_modulation(sana_cuda_ctx* ctx, const float* tmod, const float* table, int B, int C, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(tmod && table && out && B >= 1 && C >= 1, "invalid block modulation arguments");
+        sana::Engine& eng = engine(ctx);
+        DevBuf t = f32_upload(tmod, static_cast<size_t>(B) * 6 * C), tb = f32_upload(table, static_cast<size_t>(6) * C),
+               o;
+        o.ensure(static_cast<size_t>(B) * 6 * C * 4);
+        sana::block_modulation(t.as<float>(), B, C, tb.as<float>(), 1, o.as<float>(), eng.stream());
+        finish(eng);
+        d2h(out, o.get(), static_cast<size_t>(B) * 6 * C * 4);
+    });
+}
+
 
 // --- device-pointer kernels (microbenchmarks) ---------------------------------------------
 

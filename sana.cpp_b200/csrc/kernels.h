@@ -45,6 +45,12 @@ void patch_tokens(const float* lat, int images, int seqs, int Cl, int HW, float*
 // host with the reference's arithmetic) broadcast; used only to fill [S, 256].
 void broadcast_rows(const float* row, int S, int width, float* out, cudaStream_t st);
 
+// split_heads_3d ([B, T, H*D] -> [B, H, T, D], to_heads) and merge_heads_4d (the inverse),
+// transformer_ops.cpp:83-171; fp32.
+void permute_heads(const float* in, float* out, int B, int T, int H, int D, bool to_heads, cudaStream_t st);
+// softmax_lastdim_4d (transformer_ops.cpp:278-339) over `rows` rows of n values; fp32.
+void softmax_rows(const float* in, long long rows, int n, float* out, cudaStream_t st);
+
 // Effective key count per caption row: 1 + the last index whose additive bias exceeds
 // -1000 (L when every key is masked, so the softmax runs over all of them as the
 // reference does). Keys past it carry <= -1000 and contribute exactly 0 in fp32.

@@ -378,6 +378,68 @@ void cfg_scheduler_step(const float* noise, int images, int Cl, int HW, float* l
     SANA_CUDA(cudaGetLastError());
 }
 
+// split_heads_3d / merge_heads_4d (transformer_ops.cpp:83-171): one thread per output element.
+__global__ void permute_heads_kernel(const float* __restrict__ in, float* __restrict__ out, int B, int T, int H, int D,
+                                     int to_heads) {
+    const long long n = static_cast<long long>(B) * T * H * D;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int d = static_cast<int>(i % D);
+        if (to_heads) {  // out [B, H, T, D] <- in [B, T, H*D]
+            const long long r = i / D;
+            const int t = static_cast<int>(r % T);
+            const long long bh = r / T;
+            const int h = static_cast<int>(bh % H);
+            const long long b = bh / H;
+            out[i] = in[((b * T + t) * H + h) * D + d];
+        } else {  // out [B, T, H*D] <- in [B, H, T, D]
+            const long long r = i / D;
+            const int h = static_cast<int>(r % H);
+            const long long bt = r / H;
+            const int t = static_cast<int>(bt % T);
+            const long long b = bt / T;
+            out[i] = in[((b * H + h) * T + t) * D + d];
+        }
+    }
+}
+
+// softmax_lastdim_4d (transformer_ops.cpp:278-339): per row, e = exp(x - max), then
+// e * (1 / sum e). One warp per row.
+__global__ void softmax_rows_kernel(const float* __restrict__ in, long long rows, int n, float* __restrict__ out) {
+    const long long row = blockIdx.x * static_cast<long long>(blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* x = in + row * n;
+    float* y = out + row * n;
+    float m = x[0];
+    for (int d = lane; d < n; d += 32) m = fmaxf(m, x[d]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float sum = 0.f;
+    for (int d = lane; d < n; d += 32) {
+        const float e = expf(x[d] - m);
+        y[d] = e;
+        sum += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float recip = 1.0f / sum;
+    for (int d = lane; d < n; d += 32) y[d] *= recip;
+}
+
+void permute_heads(const float* in, float* out, int B, int T, int H, int D, bool to_heads, cudaStream_t st) {
+    const long long n = static_cast<long long>(B) * T * H * D;
+    if (n == 0) return;
+    permute_heads_kernel<<<grid_for(n, 256), 256, 0, st>>>(in, out, B, T, H, D, to_heads ? 1 : 0);
+    SANA_CUDA(cudaGetLastError());
+}
+
+void softmax_rows(const float* in, long long rows, int n, float* out, cudaStream_t st) {
+    if (rows == 0 || n == 0) return;
+    softmax_rows_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(in, rows, n, out);
+    SANA_CUDA(cudaGetLastError());
+}
+
 template <class TO>
 void repack(const float* src, int rows, int cols, bool transpose, TO* dst, cudaStream_t st) {
     dim3 grid(ceil_div(cols, 32), ceil_div(rows, 32));
