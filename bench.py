@@ -3,12 +3,13 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU, NCCL)
 
-Workload (per GPU): 16 images x CFG (32 sequences of 1024 tokens),
-20-step DPM-Solver++ loop with guidance 4.5, caption states [300, 2304] with valid lengths
-drawn from 8..120; seeded random-init weights of the real architecture (synthetic: there
-are no checkpoints or datasets here). Each rank denoises its own 16 images, weights
-replicated; the final latents of all ranks are NCCL-gathered after each loop (the path's
-only collective), so per-GPU work is fixed as N grows ("weak" scaling).
+Workload: 16 images x CFG (32 sequences of 1024 tokens), 20-step
+DPM-Solver++ loop with guidance 4.5, caption states [300, 2304] with valid lengths drawn
+from 8..120; seeded random-init weights of the real architecture (synthetic: there are no
+checkpoints or datasets here). The 16 images are sharded across the ranks in contiguous
+ranges (sana_b200.sharding), weights replicated, every image's inputs drawn from seeds of its
+own index; the final latents are NCCL-gathered into the full batch on every rank after each
+loop (the path's only collective). Total work is fixed as N grows ("strong" scaling).
 
     python bench.py --microbench [--op NAME,...]     (one GPU)
 
@@ -76,14 +77,11 @@ def make_weights(dims, seed=0):
         return list(ex.map(lambda j: syn.generate_tensor(specs[j], j, dims, randn_torch_cpu, seed), range(len(specs))))
 
 
-def make_inputs(images, rank):
+def make_inputs(first, count):
+    """Images [first, first + count) of the synthetic batch (sana_b200.sharding.image_inputs)."""
     from sana_b200 import randn_torch_cpu
-    from sana_b200 import synthetic as syn
-    lens = syn.batch_valid_lengths(images, 1000 + rank)
-    lat = syn.latents(randn_torch_cpu, images, 32, 32, 32, 42 + 97 * rank)
-    enc = syn.encoder_states(randn_torch_cpu, 2 * images, CAPTION_LEN, 2304, 7 + 97 * rank)
-    bias = syn.attention_bias(lens, CAPTION_LEN)
-    return lat, enc, bias, lens
+    from sana_b200.sharding import image_inputs
+    return image_inputs(randn_torch_cpu, first, count, (32, 32, 32), CAPTION_LEN, 2304)
 
 
 def loop_flops(images, lens, C=1152, E=5760, T=1024, n_blocks=28, Hs=36, steps=NUM_STEPS, Din=2304, Cl=32):
@@ -219,7 +217,7 @@ def run_reference(args):
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
         "steps": K, "warmup": W, "ms_per_step": 1000 * statistics.mean(secs), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_dict(args),
         "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -227,10 +225,11 @@ def run_reference(args):
 
 
 def config_dict(args):
-    return {"workload": f"config2: {args.images} images x CFG per GPU (2x{args.images} sequences x 1024 tokens), "
-                        f"{NUM_STEPS}-step DPM-Solver++ loop, guidance {GUIDANCE}",
-            "images_per_gpu": args.images, "global_batch": args.images * args.gpus, "seq_len": 1024,
-            "caption_tokens": CAPTION_LEN, "caption_valid_lengths": "uniform 8..120 (seeded)",
+    per = [f"{(args.images + args.gpus - 1 - r) // args.gpus}" for r in range(args.gpus)]
+    return {"workload": f"config2: {args.images} images x CFG ({2 * args.images} sequences x 1024 tokens) sharded "
+                        f"over {args.gpus} GPU(s), {NUM_STEPS}-step DPM-Solver++ loop, guidance {GUIDANCE}",
+            "global_batch": args.images, "images_per_gpu": "/".join(per), "seq_len": 1024,
+            "caption_tokens": CAPTION_LEN, "caption_valid_lengths": "uniform 8..120 (seeded per image)",
             "self_attention": "36 heads x 32 (linear)", "cross_attention": "16 heads x 72 (softmax)",
             "parallelism": f"images sharded over {args.gpus} GPU(s), weights replicated, final latents gathered",
             "l2": "flushed between timed iterations (256 MiB write, untimed)"}
@@ -399,13 +398,16 @@ def run_cuda(args):
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     g.set_stream(stream.cuda_stream)
-    B = args.images
-    lat, enc, bias, lens = make_inputs(B, rank)
+    from sana_b200.sharding import gather_images, shard_range
+    total = args.images
+    if total < world:
+        raise SystemExit(f"--images {total} is smaller than the number of ranks {world}")
+    first, B = shard_range(total, world, rank)
+    lat, enc, bias, lens = make_inputs(first, B)
     d_lat = torch.from_numpy(lat).cuda()
     d_enc = torch.from_numpy(enc).cuda()
     d_bias = torch.from_numpy(bias).cuda()
     d_out = torch.empty_like(d_lat)
-    gathered = [torch.empty_like(d_lat) for _ in range(world)] if world > 1 else None
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     torch.cuda.synchronize()
 
@@ -413,7 +415,7 @@ def run_cuda(args):
         g.denoise_loop_device(d_lat.data_ptr(), B, 32, 32, d_enc.data_ptr(), CAPTION_LEN, 2304,
                               d_bias.data_ptr(), d_out.data_ptr(), GUIDANCE, NUM_STEPS)
         if world > 1:
-            dist.all_gather(gathered, d_out)
+            gather_images(d_out, total, world)
 
     for _ in range(args.warmup):
         step()
@@ -448,7 +450,7 @@ def run_cuda(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / args.steps
-    images_per_s = world * B / (ms_per_step / 1000.0)
+    images_per_s = total / (ms_per_step / 1000.0)
     flops, gemm_flops = loop_flops(B, lens)
     pk, pk_kind = peaks()
 
@@ -518,7 +520,7 @@ def run_cuda(args):
         clocks = clk.summary()
         out = {
             "metric": METRIC, "value": images_per_s, "unit": "images/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded random-init Sana-0.6B weights, N(0,1) latents and caption states",
             "config": config_dict(args),
@@ -544,7 +546,7 @@ def run_cuda(args):
                             "frac_of_sustained_peak": flops / (ms_per_step / 1e3) / 1e12 / pk["bf16_tflops_sustained"],
                             "gemm_share_of_flops": gemm_flops / flops},
             "cpu_baseline": cpu,
-            "e2e": {"value": world * B / e2e_s, "unit": "images/s", "h2d_bytes_per_step": h2d,
+            "e2e": {"value": total / e2e_s, "unit": "images/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": launches * args.steps,
             "clocks": clocks,
@@ -561,7 +563,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
-    ap.add_argument("--images", type=int, default=16, help="images (x2 CFG sequences) per GPU")
+    ap.add_argument("--images", type=int, default=16, help="images (x2 CFG sequences) in the batch, over all GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--microbench", action="store_true",
                     help="op-level microbenchmark (BASELINE configs[4]) instead of the loop; one GPU")
