@@ -269,7 +269,7 @@ def gemm_roofline(g, torch, stream, M, peak_tflops):
 
 
 MICRO_OPS = ("qkv_gemm", "linear_attention_16x72", "linear_attention_36x32", "depthwise_glu", "cross_attention",
-             "ff_inverted_config2", "linear_attention_config2", "depthwise_glu_config2")
+             "ff_inverted_config2", "linear_attention_config2", "depthwise_glu_config2", "cross_attention_config2")
 
 
 def run_microbench(args):
@@ -363,14 +363,23 @@ def run_microbench(args):
             out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
             ms = timed(lambda: g.gemm_device(A.data_ptr(), B.data_ptr(), M, N, K, out.data_ptr(), bias.data_ptr(), 1))
             report(name, f"M={M} K={K} N={N} +bias, SiLU, bf16 out", ms, 2.0 * M * N * K, "tensor")
-        elif name == "cross_attention":
+        elif name.startswith("cross_attention"):
             heads, D = 16, 72
             q, kv = rnd(S * T, C), rnd(S * L, 2 * C)
             kvl = torch.empty(S, device="cuda", dtype=torch.int32)
             out = torch.empty(S * T, C, device="cuda", dtype=torch.bfloat16)
-            ms = timed(lambda: g._call("sana_op_cross_attention_device", vp(q.data_ptr()), vp(kv.data_ptr()), None,
-                                       vp(kvl.data_ptr()), I(S), I(T), I(L), I(heads), I(D), vp(out.data_ptr())))
-            report(name, f"q [{S},{heads},{T},{D}], k/v {L} keys, no mask", ms, 4.0 * S * T * L * C, "tensor")
+            if name.endswith("config2"):  # the loop's caption masks: valid lengths uniform in 8..120
+                from sana_b200.sharding import image_valid_lengths
+                lens = [v for i in range(S // 2) for v in image_valid_lengths(i)]
+                from sana_b200 import synthetic as syn
+                bias = torch.from_numpy(syn.attention_bias(lens, L).reshape(S, L)).cuda()
+                what = f"q [{S},{heads},{T},{D}], k/v {L} keys, valid lengths 8..120 (mean {sum(lens) / S:.0f})"
+            else:
+                lens, bias, what = [L] * S, None, f"q [{S},{heads},{T},{D}], k/v {L} keys, no mask"
+            ms = timed(lambda: g._call("sana_op_cross_attention_device", vp(q.data_ptr()), vp(kv.data_ptr()),
+                                       vp(bias.data_ptr()) if bias is not None else None, vp(kvl.data_ptr()), I(S),
+                                       I(T), I(L), I(heads), I(D), vp(out.data_ptr())))
+            report(name, what, ms, 4.0 * T * C * sum(lens), "tensor")
     g.close()
 
 

@@ -26,17 +26,33 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 
-template <int BN>
-struct Cfg {
-    static constexpr int kStages = BN == 128 ? 6 : (BN == 192 ? 5 : 4);
-    static constexpr int kABytes = BM * BK * 2;
-    static constexpr int kBBytes = BN * BK * 2;
+// Residual chunks in flight per epilogue warp, and the bytes of one (32 rows x 16 fp32).
+constexpr int kRing = 4;
+constexpr int kRingChunk = 32 * 16 * 4;
+constexpr int kEpiWarpsCfg = 8;
+
+// Shared-memory layout of a CTA: [A stages][B stages][epilogue staging (8 x 2 KB)]
+// [residual ring (8 warps x kRing x 2 KB, residual epilogues only)][barriers][tmem slot].
+// Residual epilogues are HBM-bound, so they trade pipeline stages for the residual ring.
+template <int kStagesV, int kABytesV, int kBBytesV, bool kResid>
+struct Layout {
+    static constexpr int kStages = kStagesV;
+    static constexpr int kABytes = kABytesV;
+    static constexpr int kBBytes = kBBytesV;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;  // power of two >= two accumulators
-    // layout: [A stages][B stages][epilogue staging][barriers][tmem slot]
     static constexpr int kEpiOffset = kStages * kStageBytes;
-    static constexpr int kBarOffset = kEpiOffset + 8 * 32 * 64;
-    static constexpr int kSmemBytes = kBarOffset + (2 * kStages + 5) * 8 + 16 + 1024;
+    static constexpr int kRingOffset = kEpiOffset + kEpiWarpsCfg * 32 * 64;
+    static constexpr int kRingBytes = kResid ? kEpiWarpsCfg * kRing * kRingChunk : 0;
+    static constexpr int kBarOffset = kRingOffset + kRingBytes;
+    static constexpr int kBars = 2 * kStages + 5 + (kResid ? kEpiWarpsCfg * kRing : 0);
+    static constexpr int kSmemBytes = kBarOffset + kBars * 8 + 16 + 1024;
+    static_assert(kSmemBytes <= 232448, "shared memory of one CTA");
+};
+
+template <int BN, bool kResid = false>
+struct Cfg : Layout<kResid ? (BN == 128 ? 4 : 3) : (BN == 128 ? 6 : (BN == 192 ? 5 : 4)), BM * BK * 2, BN * BK * 2,
+                    kResid> {
+    static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;  // power of two >= two accumulators
 };
 
 // --- tcgen05 / TMA primitives -----------------------------------------------------------
@@ -183,49 +199,11 @@ __device__ __forceinline__ void store_val(void* out, int is_bf16, long long idx,
     }
 }
 
-// Residual and gate values of 16 consecutive columns [n0, n0+16) of one row, fetched one
-// chunk ahead of their use so the epilogue does not wait on global-memory latency.
+// Residual and gate values of 16 consecutive columns [n0, n0+16) of one row.
 struct Side16 {
     float r[16];
     float g[16];
 };
-
-__device__ __forceinline__ void fetch16(const Epilogue& ep, int row, int n0, int N, bool vec, Side16& sd) {
-    if (!ep.resid) return;
-    if (vec && n0 + 16 <= N) {
-        const float* r = ep.resid + static_cast<long long>(row) * ep.ldr + n0;
-#pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-            const float4 v = *reinterpret_cast<const float4*>(r + j);
-            sd.r[j] = v.x;
-            sd.r[j + 1] = v.y;
-            sd.r[j + 2] = v.z;
-            sd.r[j + 3] = v.w;
-        }
-        if (ep.gate) {
-            const float* g = ep.gate + static_cast<long long>(row / ep.rows_per_gate) * ep.gate_ld + n0;
-#pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-                const float4 v = *reinterpret_cast<const float4*>(g + j);
-                sd.g[j] = v.x;
-                sd.g[j + 1] = v.y;
-                sd.g[j + 2] = v.z;
-                sd.g[j + 3] = v.w;
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) sd.g[j] = 1.f;
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int n = n0 + j;
-            sd.r[j] = n < N ? ep.resid[static_cast<long long>(row) * ep.ldr + n] : 0.f;
-            sd.g[j] = (n < N && ep.gate) ? ep.gate[static_cast<long long>(row / ep.rows_per_gate) * ep.gate_ld + n]
-                                         : 1.f;
-        }
-    }
-}
 
 // Bias, activation and gated residual on 16 consecutive columns [n0, n0+16) of one row,
 // all of them in range (the fast path); the stores are the caller's.
@@ -400,38 +378,63 @@ __device__ __forceinline__ void epilogue16(const Epilogue& ep, int row, int n0, 
     }
 }
 
-// Residual of one 16-column chunk of the warp's 32 rows, loaded coalesced: lane l holds rows
-// 8i + l/4 (i = 0..3), 16-byte slot l%4. resid_rows() hands every lane its own row back
-// through the staging block.
-struct ResidChunk {
-    uint4 q[4];
+// The residual chunks an epilogue warp will need, in the order it needs them: chunk j is the
+// warp's 32 rows x 16 fp32 columns number j % kchunks of its span of the (j / kchunks)-th
+// tile it processes. Lane 0 keeps kRing chunks in flight with TMA (64-byte swizzle: 16-byte
+// slot k of row r lands at stage_slot(r, k), so each lane reads its own row without bank
+// conflicts); every lane takes the chunks in order. Boxes past M or N read as zeros.
+struct ResidRing {
+    const CUtensorMap* map;
+    const uint8_t* buf;   // slot 0, generic address
+    uint32_t buf_s, bar;  // slot 0 and its barrier, shared-window addresses
+    int first, stride, num_tiles, num_n, bn, tile_rows, row_off, col0, kchunks;
+    int issued, used;
+    int* err;
+
+    __device__ bool coords(int j, int& x, int& y) const {
+        const int tile = first + (j / kchunks) * stride;
+        if (tile >= num_tiles) return false;
+        x = (tile % num_n) * bn + col0 + 16 * (j % kchunks);
+        y = (tile / num_n) * tile_rows + row_off;
+        return true;
+    }
+    // Lane 0: keeps the ring full.
+    __device__ void refill() {
+        while (issued < used + kRing) {
+            int x, y;
+            if (!coords(issued, x, y)) break;
+            const uint32_t s = static_cast<uint32_t>(issued % kRing);
+            mbar_arrive_expect_tx(bar + 8u * s, kRingChunk);
+            tma_load_2d(map, buf_s + s * kRingChunk, bar + 8u * s, x, y);
+            ++issued;
+        }
+    }
+    // Every lane: its row of the next chunk. A wait that gives up has recorded the error.
+    __device__ void take(float (&rv)[16]) {
+        const int lane = threadIdx.x & 31;
+        const uint32_t s = static_cast<uint32_t>(used % kRing);
+        if (mbar_wait(bar + 8u * s, static_cast<uint32_t>((used / kRing) & 1), err, kTimeout)) {
+            const uint8_t* b = buf + s * kRingChunk;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint4 w = *reinterpret_cast<const uint4*>(b + stage_slot(lane, k));
+                rv[4 * k] = __uint_as_float(w.x);
+                rv[4 * k + 1] = __uint_as_float(w.y);
+                rv[4 * k + 2] = __uint_as_float(w.z);
+                rv[4 * k + 3] = __uint_as_float(w.w);
+            }
+        }
+        __syncwarp();  // the slot is free once every lane has read it
+        ++used;
+        if (lane == 0) refill();
+    }
+    // Lane 0: waits (bounded) for chunks issued and never taken, so no copy lands after exit.
+    __device__ void drain() {
+        for (int j = used; j < issued; ++j)
+            mbar_wait_quiet(bar + 8u * static_cast<uint32_t>(j % kRing), static_cast<uint32_t>((j / kRing) & 1));
+    }
 };
-__device__ __forceinline__ void resid_fetch(const Epilogue& ep, int row0, int M, int n0, ResidChunk& rc) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int r = 8 * i + lane / 4;
-        rc.q[i] = row0 + r < M ? *reinterpret_cast<const uint4*>(ep.resid + static_cast<long long>(row0 + r) * ep.ldr +
-                                                                 n0 + 4 * (lane % 4))
-                               : make_uint4(0u, 0u, 0u, 0u);
-    }
-}
-__device__ __forceinline__ void resid_rows(uint8_t* stg, const ResidChunk& rc, float (&rv)[16]) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        *reinterpret_cast<uint4*>(stg + stage_slot(8 * i + lane / 4, lane % 4)) = rc.q[i];
-    __syncwarp();
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const uint4 w = *reinterpret_cast<const uint4*>(stg + stage_slot(lane, k));
-        rv[4 * k] = __uint_as_float(w.x);
-        rv[4 * k + 1] = __uint_as_float(w.y);
-        rv[4 * k + 2] = __uint_as_float(w.z);
-        rv[4 * k + 3] = __uint_as_float(w.w);
-    }
-    __syncwarp();
-}
+
 // The gate values of one row's 16 columns (1 when the epilogue has no gate).
 __device__ __forceinline__ void gate16(const Epilogue& ep, int row, int n0, float (&gv)[16]) {
     if (ep.gate) {
@@ -452,44 +455,39 @@ __device__ __forceinline__ void gate16(const Epilogue& ep, int row, int n0, floa
 
 // One epilogue warp's share of a tile: rows row0 .. row0+31 (lane = row - row0, the warp's
 // TMEM lane quarter) and kCols columns from n_start, read from TMEM at t_addr. TMEM loads go
-// out two 16-column chunks at a time (one wait per 32 columns). Batches of 32 columns inside
-// N with vector-aligned operands take the coalesced path (residual loaded a chunk ahead,
-// outputs stored through the staging block `stg`); the rest go element by element.
+// out two 16-column chunks at a time (one wait per 32 columns). Residual epilogues take each
+// chunk's residual from the warp's TMA ring. Batches of 32 columns inside N with aligned
+// operands store through the staging block `stg`; the rest go element by element.
 template <int kCols, bool kResid>
 __device__ __forceinline__ void epilogue_span(const Epilogue& ep, int row0, int M, int n_start, int N, bool vec,
-                                              uint32_t t_addr, uint8_t* stg) {
+                                              uint32_t t_addr, uint8_t* stg, ResidRing* ring) {
     constexpr int kChunks = kCols / 16;
     static_assert(kChunks % 2 == 0, "chunks go out in pairs");
     const int lane = threadIdx.x & 31;
     const int row = row0 + lane;
     const bool row_ok = row < M;
-    auto fast = [&](int cc) { const int b = n_start + (cc / 2) * 32; return vec && b + 32 <= N; };
-    // rc holds the coalesced residual of the next chunk to use: it is handed out, refilled with
-    // the following chunk, and that load completes while the current chunk is finished
-    ResidChunk rc;
-    if (kResid && fast(0)) resid_fetch(ep, row0, M, n_start, rc);
 #pragma unroll 1
     for (int c = 0; c < kChunks; c += 2) {
         uint32_t r[2][16];
         tmem_ld16(t_addr + static_cast<uint32_t>(c * 16), r[0]);
         tmem_ld16(t_addr + static_cast<uint32_t>((c + 1) * 16), r[1]);
         tmem_wait_ld();
+        float rv[2][16];
+        if (kResid) {  // every chunk is taken, in order, even the ones past N
+            ring->take(rv[0]);
+            ring->take(rv[1]);
+        }
         const int n0 = n_start + c * 16;
         if (n0 >= N) continue;  // uniform across the warp
-        if (fast(c)) {
+        if (vec && n0 + 32 <= N) {
             float v[2][16];
 #pragma unroll
             for (int g = 0; g < 2; ++g) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[g][j] = __uint_as_float(r[g][j]);
-                float rv[16], gv[16];
-                if (kResid) {
-                    resid_rows(stg, rc, rv);
-                    if (g == 0) resid_fetch(ep, row0, M, n0 + 16, rc);
-                    else if (c + 2 < kChunks && fast(c + 2)) resid_fetch(ep, row0, M, n0 + 32, rc);
-                    if (row_ok) gate16(ep, row, n0 + 16 * g, gv);
-                }
-                compute16<kResid>(ep, n0 + 16 * g, v[g], rv, gv);
+                float gv[16];
+                if (kResid && row_ok) gate16(ep, row, n0 + 16 * g, gv);
+                compute16<kResid>(ep, n0 + 16 * g, v[g], rv[g], gv);
             }
             if (ep.out) store32(stg, lane, ep.out, ep.out_bf16, ep.ldo, row0, M, n0, v[0], v[1]);
             if (ep.out2) {
@@ -508,7 +506,15 @@ __device__ __forceinline__ void epilogue_span(const Epilogue& ep, int row0, int 
             const int n1 = n0 + g * 16;
             if (row_ok && n1 < N) {
                 Side16 sd;
-                if (kResid) fetch16(ep, row, n1, N, vec, sd);
+                if (kResid) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        sd.r[j] = rv[g][j];
+                        sd.g[j] = (ep.gate && n1 + j < N)
+                                      ? ep.gate[static_cast<long long>(row / ep.rows_per_gate) * ep.gate_ld + n1 + j]
+                                      : 1.f;
+                    }
+                }
                 float v[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[g][j]);
@@ -524,9 +530,9 @@ constexpr int kThreads = 32 * (2 + kEpiWarps);
 
 template <int BN, bool kResid>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
-                   int N, int K, Epilogue ep, int vec, int* err) {
-    using C = Cfg<BN>;
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmR, int M, int N, int K, Epilogue ep, int vec, int* err) {
+    using C = Cfg<BN, kResid>;
     constexpr int S = C::kStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -540,7 +546,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto tfull = [&](int a) { return bars + 8u * (2 * S + a); };
     auto tempty = [&](int a) { return bars + 8u * (2 * S + 2 + a); };
     const uint32_t done_bar = bars + 8u * (2 * S + 4);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kBarOffset + (2 * S + 5) * 8);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kBarOffset + C::kBars * 8);
+    const uint32_t ring_bars = bars + 8u * (2 * S + 5);  // kEpiWarps x kRing, residual epilogues
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -559,6 +566,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(tempty(a), kEpiWarps);
         }
         mbar_init(done_bar, 1);
+        if (kResid)
+            for (int i = 0; i < kEpiWarps * kRing; ++i) mbar_init(ring_bars + 8u * i, 1);
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -649,6 +658,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         const int q = warp & 3;                   // TMEM lane quarter this warp may access
         const int chalf = (warp - 2) / 4;         // which half of the tile's columns
+        const int ew = warp - 2;
+        ResidRing ring{&tmR, gbase + C::kRingOffset + ew * kRing * kRingChunk,
+                       base + C::kRingOffset + static_cast<uint32_t>(ew * kRing * kRingChunk),
+                       ring_bars + 8u * static_cast<uint32_t>(ew * kRing), static_cast<int>(blockIdx.x),
+                       static_cast<int>(gridDim.x), num_tiles, num_n, BN, BM, q * 32, chalf * (BN / 2), BN / 2 / 16,
+                       0, 0, err};
+        if (kResid && lane == 0) ring.refill();
         int local = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const int acc = local & 1;
@@ -661,11 +677,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + col0);
             epilogue_span<BN / 2, kResid>(ep, m_blk * BM + q * 32, M, n_blk * BN + col0, N, vec != 0, t_row,
-                                  gbase + C::kEpiOffset + (warp - 2) * kEpiStageBytes);
+                                          gbase + C::kEpiOffset + ew * kEpiStageBytes, &ring);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty(acc));
         }
+        if (kResid && lane == 0) ring.drain();
     }
 
     tc_fence_before();
@@ -689,24 +706,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   tempty[a]  leader only: one arrival per epilogue warp of either CTA
 // Every wait is bounded; on expiry each role stops issuing work and every thread still
 // reaches the final cluster barrier, so neither CTA leaves while its peer uses its memory.
-template <int BN>
-struct Cfg2 {
+template <int BN, bool kResid = false>
+struct Cfg2 : Layout<kResid ? (BN == 128 ? 5 : 4) : (BN == 128 ? 8 : (BN == 192 ? 7 : 6)), 128 * BK * 2,
+                     (BN / 2) * BK * 2, kResid> {
     static constexpr int kBH = BN / 2;  // B rows per CTA
-    static constexpr int kABytes = 128 * BK * 2;
-    static constexpr int kBBytes = kBH * BK * 2;
-    static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kStages = BN == 128 ? 8 : (BN == 192 ? 7 : 6);
     static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
-    static constexpr int kEpiOffset = kStages * kStageBytes;
-    static constexpr int kBarOffset = kEpiOffset + 8 * 32 * 64;
-    static constexpr int kSmemBytes = kBarOffset + (2 * kStages + 5) * 8 + 16 + 1024;
 };
 
 template <int BN, bool kResid>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
-                    int N, int K, Epilogue ep, int vec, int* err) {
-    using C = Cfg2<BN>;
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmR, int M, int N, int K, Epilogue ep, int vec, int* err) {
+    using C = Cfg2<BN, kResid>;
     constexpr int S = C::kStages;
     constexpr int BM2 = 2 * BM;
     extern __shared__ uint8_t smem_raw[];
@@ -721,7 +732,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     auto tfull = [&](int a) { return bars + 8u * (2 * S + a); };
     auto tempty = [&](int a) { return bars + 8u * (2 * S + 2 + a); };
     const uint32_t done_bar = bars + 8u * (2 * S + 4);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kBarOffset + (2 * S + 5) * 8);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kBarOffset + C::kBars * 8);
+    const uint32_t ring_bars = bars + 8u * (2 * S + 5);  // kEpiWarps x kRing, residual epilogues
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -744,6 +756,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_init(tempty(a), 2 * kEpiWarps);
         }
         mbar_init(done_bar, 1);
+        if (kResid)
+            for (int i = 0; i < kEpiWarps * kRing; ++i) mbar_init(ring_bars + 8u * i, 1);
         fence_barrier_init();
     }
     cluster_sync();  // barriers of both CTAs initialised before any remote arrival
@@ -843,6 +857,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else {
         const int q = warp & 3;
         const int chalf = (warp - 2) / 4;
+        const int ew = warp - 2;
+        ResidRing ring{&tmR, gbase + C::kRingOffset + ew * kRing * kRingChunk,
+                       base + C::kRingOffset + static_cast<uint32_t>(ew * kRing * kRingChunk),
+                       ring_bars + 8u * static_cast<uint32_t>(ew * kRing), pair, npairs, num_tiles, num_n, BN, BM2,
+                       static_cast<int>(rank) * BM + q * 32, chalf * (BN / 2), BN / 2 / 16, 0, 0, err};
+        if (kResid && lane == 0) ring.refill();
         int local = 0;
         for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
             const int acc = local & 1;
@@ -854,12 +874,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int col0 = chalf * (BN / 2);
             const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + col0);
-            epilogue_span<BN / 2, kResid>(ep, m_blk * BM2 + static_cast<int>(rank) * BM + q * 32, M, n_blk * BN + col0, N,
-                                  vec != 0, t_row, gbase + C::kEpiOffset + (warp - 2) * kEpiStageBytes);
+            epilogue_span<BN / 2, kResid>(ep, m_blk * BM2 + static_cast<int>(rank) * BM + q * 32, M,
+                                          n_blk * BN + col0, N, vec != 0, t_row,
+                                          gbase + C::kEpiOffset + ew * kEpiStageBytes, &ring);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * acc);
         }
+        if (kResid && lane == 0) ring.drain();
     }
 
     tc_fence_before();
@@ -883,9 +905,21 @@ static CUtensorMap make_map(const void* ptr, int rows, int cols, long long ld, i
     return m;
 }
 
+// fp32 residual [M, N] (row stride ldr) in boxes of 32 rows x 16 columns with the 64-byte
+// swizzle the epilogue's staging layout uses; out-of-range rows and columns read as zero.
+static CUtensorMap resid_map(const GemmProblem& p) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.N), static_cast<cuuint64_t>(p.M)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.ep.ldr) * 4};
+    const cuuint32_t box[2] = {16, 32};
+    tma_encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.ep.resid, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_64B);
+    return m;
+}
+
 template <int BN, bool kResid>
 static void launch(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
-    using C = Cfg<BN>;
+    using C = Cfg<BN, kResid>;
     static bool attr_done = false;
     if (!attr_done) {
         SANA_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, kResid>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -894,6 +928,7 @@ static void launch(const GemmProblem& p, int* err, cudaStream_t stream, int num_
     }
     const CUtensorMap ma = make_map(p.A, p.M, p.K, p.lda, BM);
     const CUtensorMap mb = make_map(p.B, p.N, p.K, p.ldb, BN);
+    const CUtensorMap mr = kResid ? resid_map(p) : ma;
     const Epilogue& e = p.ep;
     auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     bool vec = (p.N % 16 == 0);
@@ -904,13 +939,13 @@ static void launch(const GemmProblem& p, int* err, cudaStream_t stream, int num_
     if (e.out2) vec = vec && a16(e.out2) && (e.ldo2 % 8 == 0);
     const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    gemm_tc_kernel<BN, kResid><<<grid, kThreads, C::kSmemBytes, stream>>>(ma, mb, p.M, p.N, p.K, e, vec ? 1 : 0, err);
+    gemm_tc_kernel<BN, kResid><<<grid, kThreads, C::kSmemBytes, stream>>>(ma, mb, mr, p.M, p.N, p.K, e, vec ? 1 : 0, err);
     SANA_CUDA(cudaGetLastError());
 }
 
 template <int BN, bool kResid>
 static void launch2(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
-    using C = Cfg2<BN>;
+    using C = Cfg2<BN, kResid>;
     static bool attr_done = false;
     if (!attr_done) {
         SANA_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<BN, kResid>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -919,6 +954,7 @@ static void launch2(const GemmProblem& p, int* err, cudaStream_t stream, int num
     }
     const CUtensorMap ma = make_map(p.A, p.M, p.K, p.lda, BM);
     const CUtensorMap mb = make_map(p.B, p.N, p.K, p.ldb, C::kBH);
+    const CUtensorMap mr = kResid ? resid_map(p) : ma;
     const Epilogue& e = p.ep;
     auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     bool vec = (p.N % 16 == 0);
@@ -929,8 +965,8 @@ static void launch2(const GemmProblem& p, int* err, cudaStream_t stream, int num
     if (e.out2) vec = vec && a16(e.out2) && (e.ldo2 % 8 == 0);
     const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + BN - 1) / BN);
     const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
-    gemm_tc2_kernel<BN, kResid><<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(ma, mb, p.M, p.N, p.K, e, vec ? 1 : 0,
-                                                                         err);
+    gemm_tc2_kernel<BN, kResid><<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(ma, mb, mr, p.M, p.N, p.K, e,
+                                                                                 vec ? 1 : 0, err);
     SANA_CUDA(cudaGetLastError());
 }
 
@@ -949,8 +985,10 @@ static bool use_pair(const GemmProblem& p, int num_sms) {
 
 bool gemm_tc_supported(const GemmProblem& p) {
     auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    // the residual epilogue reads its fp32 residual with TMA: 16-byte aligned base and rows
+    const bool resid_ok = !p.ep.resid || (a16(p.ep.resid) && p.ep.ldr % 4 == 0);
     return p.a_bf16 && p.b_bf16 && p.M > 0 && p.N > 0 && p.K > 0 && (p.K % 8 == 0) && (p.lda % 8 == 0) &&
-           (p.ldb % 8 == 0) && a16(p.A) && a16(p.B) && p.N >= 16;
+           (p.ldb % 8 == 0) && a16(p.A) && a16(p.B) && p.N >= 16 && resid_ok;
 }
 
 void gemm_tc(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
