@@ -269,7 +269,8 @@ def gemm_roofline(g, torch, stream, M, peak_tflops):
 
 
 MICRO_OPS = ("qkv_gemm", "linear_attention_16x72", "linear_attention_36x32", "depthwise_glu", "cross_attention",
-             "ff_inverted_config2", "linear_attention_config2", "depthwise_glu_config2", "cross_attention_config2")
+             "ff_inverted_config2", "linear_attention_config2", "depthwise_glu_config2", "cross_attention_config2",
+             "out_proj_config2")
 
 
 def run_microbench(args):
@@ -363,6 +364,21 @@ def run_microbench(args):
             out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
             ms = timed(lambda: g.gemm_device(A.data_ptr(), B.data_ptr(), M, N, K, out.data_ptr(), bias.data_ptr(), 1))
             report(name, f"M={M} K={K} N={N} +bias, SiLU, bf16 out", ms, 2.0 * M * N * K, "tensor")
+        elif name == "out_proj_config2":
+            # the self-attention output projection: fp32 residual + gate x (A W^T + b), bf16 copy
+            M, N, K = S * T, C, C
+            A, Bw = rnd(M, K), rnd(N, K, scale=0.02)
+            bias = torch.zeros(N, device="cuda")
+            resid = torch.randn(M, N, generator=gen).cuda()
+            gate = torch.randn(S, N, generator=gen).cuda()
+            out = torch.empty(M, N, device="cuda")
+            out2 = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            ms = timed(lambda: g._call("sana_op_gemm_residual_device", vp(A.data_ptr()), vp(Bw.data_ptr()), I(M),
+                                       I(N), I(K), vp(bias.data_ptr()), vp(resid.data_ptr()), vp(gate.data_ptr()),
+                                       I(T), vp(out.data_ptr()), vp(out2.data_ptr())))
+            byts = 2.0 * M * K + 2.0 * N * K + 4.0 * M * N * 2 + 2.0 * M * N
+            report(name, f"M={M} K={K} N={N}: fp32 residual read + fp32 and bf16 out ({byts / 1e6:.0f} MB)", ms, byts,
+                   "hbm")
         elif name.startswith("cross_attention"):
             heads, D = 16, 72
             q, kv = rnd(S * T, C), rnd(S * L, 2 * C)

@@ -227,6 +227,13 @@ int sana_op_block_modulation(sana_cuda_ctx *ctx, const float *tmod, const float 
  * linear_3d_lastdim / conv2d_1x1 (common_ops.cpp:177, :322). act: 0 none, 1 SiLU, 2 GELU-tanh. */
 int sana_op_gemm_device(sana_cuda_ctx *ctx, const void *A, const void *B, int M, int N, int K, const float *bias,
                         int act, void *out);
+/* The residual projection of a block stage (the attention / cross-attention output and the
+ * Mix-FFN point projection, transformer.cpp:740-777): out[M, N] (fp32) =
+ * resid + gate[row / rows_per_gate] * (A . B^T + bias), gate NULL = 1, bias NULL = 0; out
+ * may alias resid; out_bf16 (may be NULL) receives a bf16 copy of out. */
+int sana_op_gemm_residual_device(sana_cuda_ctx *ctx, const void *A, const void *B, int M, int N, int K,
+                                 const float *bias, const float *resid, const float *gate, int rows_per_gate,
+                                 float *out, void *out_bf16);
 /* linear_attention_4d on the fused QKV rows [S*T, 3*heads*D] -> [S*T, heads*D]; partial is
  * fp32 scratch of sana_op_linear_attention_workspace() bytes. */
 int sana_op_linear_attention_device(sana_cuda_ctx *ctx, const void *qkv, int S, int T, int heads, int D,

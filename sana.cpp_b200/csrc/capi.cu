@@ -912,6 +912,34 @@ int sana_op_gemm_device(sana_cuda_ctx* ctx, const void* A, const void* B, int M,
     });
 }
 
+int sana_op_gemm_residual_device(sana_cuda_ctx* ctx, const void* A, const void* B, int M, int N, int K,
+                                 const float* bias, const float* resid, const float* gate, int rows_per_gate,
+                                 float* out, void* out_bf16) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(A && B && resid && out && M >= 1 && N >= 1 && K >= 1, "invalid gemm arguments");
+        SANA_REQUIRE(!gate || rows_per_gate >= 1, "rows_per_gate must be positive with a gate");
+        sana::Engine& eng = engine(ctx);
+        sana::GemmProblem p;
+        p.A = A;
+        p.lda = K;
+        p.B = B;
+        p.ldb = K;
+        p.M = M;
+        p.N = N;
+        p.K = K;
+        p.ep = epi(out, false, N, bias);
+        p.ep.resid = resid;
+        p.ep.ldr = N;
+        p.ep.gate = gate;
+        p.ep.gate_ld = N;
+        p.ep.rows_per_gate = gate ? rows_per_gate : 1;
+        p.ep.out2 = out_bf16;
+        p.ep.out2_bf16 = 1;
+        p.ep.ldo2 = N;
+        sana::gemm(p, eng.err(), eng.stream(), eng.num_sms());
+    });
+}
+
 int sana_op_linear_attention_device(sana_cuda_ctx* ctx, const void* qkv, int S, int T, int heads, int D,
                                     float* partial, void* out) {
     return guard(ctx, [&] {
