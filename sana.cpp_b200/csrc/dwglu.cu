@@ -1,131 +1,291 @@
 // Mix-FFN middle: depthwise 3x3 conv with zero padding and bias over all E channels of the
 // NHWC token grid, then the GLU gate out[c] = dw[c] * silu(dw[c + E/2])
 // (depthwise_conv2d_3x3, common_ops.cpp:484-505, per-plane taps summed ky-major then kx,
-// bias last; glumb_conv's split and gate, common_ops.cpp:745-758).
+// bias last; glumb_conv's split and gate, common_ops.cpp:745-758). The fp32 path keeps that
+// order and CUDA's expf; the bf16 path starts each sum from the bias and takes the sigmoid
+// from the hardware tanh (both differences sit far below the bf16 rounding of its output).
 //
 // The input is the SiLU-ed output of the inverted 1x1 conv, already token-major, so the
 // reference's NCHW round trips (tokens_to_grid_4d / grid_to_tokens_3d) disappear.
+#include <algorithm>
+
 #include "kernels.h"
 #include "tma.h"
+
+#ifndef DW_SLOT_ROWS
+#define DW_SLOT_ROWS 4
+#endif
+#ifndef DW_RING
+#define DW_RING 4
+#endif
 
 namespace sana {
 namespace {
 
-// bf16 tiled path (half % 8 == 0, 16-byte aligned rows, W <= kTileW). A block owns 64
-// channels of both halves and kTileRows full image rows of one sequence. One thread loads
-// the tile's input rows plus a one-pixel halo with two TMA copies (a 4-D box of
-// [1 sequence, kTileRows + 2 rows, W + 2 pixels, 64 channels] per half); TMA reads the
-// halo outside the image as zeros, which is the conv's zero padding.
-constexpr int kTileCh = 64;     // channels per half in a tile
-constexpr int kTileRows = 8;
-constexpr int kTileW = 64;      // widest image row handled by the tiled path
+// bf16 streaming path (half % 8 == 0, 16-byte aligned rows). A work item is one sequence,
+// 64 channels of each half, a stripe of up to 32 image columns and a band of image rows; a
+// persistent block walks its items in grid stride. The last warp is the producer: one lane
+// streams the item's input rows (the band plus a one-row halo above and below) into a ring
+// of shared-memory slots, one TMA copy of [kSlotRows rows, stripe + 2 pixels, 2 halves,
+// 64 channels] per slot; pixels and rows outside the image read as zeros (the conv's zero
+// padding). Warps 0-7 consume the rows: thread (warp w, lane p) owns channel pair p of both
+// halves and the four columns 4w .. 4w+3 of the stripe, and waits on the ring once per slot.
+constexpr int kSliceCh = 64;                          // channels per half in a work item
+constexpr int kStripe = 32;                           // image columns per work item
+constexpr int kCols = 4;                              // columns per thread
+constexpr int kDwWarps = kStripe / kCols;             // consumer warps
+constexpr int kStripePx = kStripe + 2;                // staged pixels per row
+constexpr int kPxBytes = 2 * kSliceCh * 2;            // one pixel: 64 value + 64 gate channels, bf16
+constexpr int kRowBytes = kStripePx * kPxBytes;       // 8704
+constexpr int kSlotRows = DW_SLOT_ROWS;               // input rows per ring slot
+constexpr int kSlotBytes = kSlotRows * kRowBytes;
+constexpr int kDwRing = DW_RING;                      // slots
+constexpr int kDwThreads = 32 * (kDwWarps + 1);
 
-// Staged pixels per image row: the row plus its halo, plus one more for odd widths so the
-// last column pair's four-pixel window stays inside the row.
-__host__ __device__ __forceinline__ int tile_pixels(int W) { return W + 2 + (W & 1); }
+__device__ __forceinline__ float tanh_approx(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
-// Thread = (channel pair p of the tile = lane, column pair): it keeps its pair's 3x3 taps of
-// both halves in registers and walks the tile's input rows top to bottom, loading the four
-// pixels x0-1 .. x0+2 of each row once (4-byte shared loads, conflict-free across the warp)
-// and adding row iy's taps into the three output rows iy-1, iy, iy+1 held in a rolling set
-// of accumulators. Each output therefore receives its taps in the reference's order (ky
-// major, then kx, from zero; bias last) with fp32 fused multiply-adds issued two channels
-// at a time.
-__global__ void __launch_bounds__(256, 2) dwglu_tile_kernel(const __grid_constant__ CUtensorMap map, int S, int H,
-                                                            int W, int half, const float* __restrict__ w,
-                                                            const float* __restrict__ b, bf16* __restrict__ out,
-                                                            long long ldo, int* err) {
-    constexpr int kPairs = kTileCh / 2;
-    extern __shared__ __align__(16) unsigned char dyn[];
-    __shared__ __align__(8) uint64_t bar_storage;
-    // two boxes [kTileRows + 2][W + 2][kTileCh] (value half, gate half), 128-byte aligned
-    bf16* tile = reinterpret_cast<bf16*>((reinterpret_cast<uintptr_t>(dyn) + 127) & ~uintptr_t(127));
-    const int PW = tile_pixels(W);
-    const int box = (kTileRows + 2) * PW * kTileCh;  // elements per half
-    const int c0 = blockIdx.y * kTileCh;          // first channel of the tile in each half
-    const int nch = min(kTileCh, half - c0);      // a multiple of 8
-    const int row_tiles = (H + kTileRows - 1) / kTileRows;
-    const int s = blockIdx.x / row_tiles;
-    const int y0 = (blockIdx.x % row_tiles) * kTileRows;
-    const uint32_t bar = smem_u32(&bar_storage);
-    if (threadIdx.x == 0) {
-        mbar_init(bar, 1);
-        fence_barrier_init();
-        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(2 * box * 2));
-        tma_load_4d(&map, smem_u32(tile), bar, c0, -1, y0 - 1, s);
-        tma_load_4d(&map, smem_u32(tile + box), bar, half + c0, -1, y0 - 1, s);
+struct DwItem {
+    int s, c0, x0, y0, rows;
+};
+
+__device__ __forceinline__ DwItem dw_item(int it, int H, int band_rows, int bands, int stripes, int slices) {
+    DwItem d;
+    const int slice = it % slices;
+    it /= slices;
+    const int stripe = it % stripes;
+    it /= stripes;
+    const int band = it % bands;
+    d.s = it / bands;
+    d.c0 = slice * kSliceCh;
+    d.x0 = stripe * kStripe;
+    d.y0 = band * band_rows;
+    d.rows = min(band_rows, H - d.y0);
+    return d;
+}
+
+// Slots of an item: its R + 2 input rows (image rows y0 - 1 .. y0 + R).
+__host__ __device__ __forceinline__ int dw_slots(int R) { return (R + 2 + kSlotRows - 1) / kSlotRows; }
+
+// A thread's accumulators of one output row: [column][value, gate] fp32 channel pairs. The
+// gate half's taps and bias are pre-halved (exactly), so it holds h = g / 2 and
+// silu(g) = g (1 + tanh(g / 2)) / 2 = h + h tanh(h).
+struct DwRow {
+    uint64_t a[kCols][2];
+};
+
+template <int KY>
+__device__ __forceinline__ void dw_taps(DwRow& r, const uint64_t (&fv)[kCols + 2], const uint64_t (&fg)[kCols + 2],
+                                        const uint64_t (&wv)[9], const uint64_t (&wg)[9]) {
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+        for (int c = 0; c < kCols; ++c) {
+            r.a[c][0] = fma2(fv[c + kx], wv[KY * 3 + kx], r.a[c][0]);
+            r.a[c][1] = fma2(fg[c + kx], wg[KY * 3 + kx], r.a[c][1]);
+        }
+}
+
+// This thread's staged values of one input row: pixels 4w - 1 .. 4w + 4 of the stripe,
+// value and gate bf16 channel pairs.
+struct DwRaw {
+    uint32_t v[kCols + 2], g[kCols + 2];
+};
+
+// Per-item state of a consumer thread.
+struct DwStep {
+    const unsigned char* px;  // this thread's first staged pixel (column 4w - 1), channel pair p, slot 0, row 0
+    uint64_t* full_bar;
+    uint64_t* empty_bar;
+    int* err;
+    uint32_t slot0;           // ring index of the item's first slot
+    int lane;
+    bool pok;                 // the channel pair exists
+    int ncols;                // columns of the thread inside the image (0..4)
+    int y0, R, H;             // band's first row, its row count; image height
+    bf16* orow;               // output row y0, column 4w, channel pair p
+    long long orow_step, ldo;
+};
+
+// Copies input row i of the item out of its slot, waiting for the slot on its first row
+// and releasing it after its last. A wait that gives up has recorded the error; the thread
+// then goes on with whatever the slot holds (every access stays in bounds, later waits give
+// up at once) and the kernel's result is discarded by the host.
+__device__ __forceinline__ void dw_fetch(const DwStep& st, int i, DwRaw& raw) {
+    const uint32_t n = st.slot0 + i / kSlotRows;
+    const int slot = n % kDwRing;
+    const int rs = i % kSlotRows;
+    if (rs == 0) mbar_wait(smem_u32(&st.full_bar[slot]), (n / kDwRing) & 1, st.err, kTimeout);
+    const uint32_t* px = reinterpret_cast<const uint32_t*>(st.px + slot * kSlotBytes + rs * kRowBytes);
+#pragma unroll
+    for (int j = 0; j < kCols + 2; ++j) {
+        raw.v[j] = px[j * (kPxBytes / 4)];
+        raw.g[j] = px[j * (kPxBytes / 4) + kSliceCh / 2];
     }
-    const int p = threadIdx.x % 32;  // channel pair within the tile
-    const int ch = c0 + 2 * p;
-    const bool pok = 2 * p < nch;
-    uint64_t wv[9], wg[9], bv = 0, bg = 0;
-#pragma unroll
-    for (int t = 0; t < 9; ++t) {
-        wv[t] = pok ? f2_make(w[static_cast<long long>(ch) * 9 + t], w[static_cast<long long>(ch + 1) * 9 + t]) : 0;
-        wg[t] = pok ? f2_make(w[static_cast<long long>(half + ch) * 9 + t], w[static_cast<long long>(half + ch + 1) * 9 + t])
-                    : 0;
+    if (rs == kSlotRows - 1 || i == st.R + 1) {
+        __syncwarp();
+        if (st.lane == 0) mbar_arrive(smem_u32(&st.empty_bar[slot]));
     }
-    if (pok) {
-        bv = f2_make(b[ch], b[ch + 1]);
-        bg = f2_make(b[half + ch], b[half + ch + 1]);
+}
+
+// Step i of the band: input row i (image row y0 - 1 + i, in `raw`) feeds output rows i,
+// i - 1, i - 2 through tap rows 0, 1, 2; output row i - 2 is then complete. The next input
+// row is fetched before the finished row is gated and stored, so its shared-memory latency
+// hides behind the GLU. kInner steps (2 <= i < R) take every tap and need no bounds tests.
+template <bool kInner>
+__device__ __forceinline__ void dw_step(const DwStep& st, int i, DwRow& oi, DwRow& oi1, DwRow& oi2, DwRaw& raw,
+                                        const uint64_t (&wv)[9], const uint64_t (&wg)[9], uint64_t bv,
+                                        uint64_t bg) {
+    if (!kInner && i > st.R + 1) return;
+    const int y = st.y0 - 1 + i;
+    const bool fin = kInner || (i >= 2 && i - 2 < st.R);
+    if (kInner || (y >= 0 && y < st.H)) {
+        uint64_t fv[kCols + 2], fg[kCols + 2];
+#pragma unroll
+        for (int j = 0; j < kCols + 2; ++j) {
+            fv[j] = f2_from_bf2(raw.v[j]);
+            fg[j] = f2_from_bf2(raw.g[j]);
+        }
+        if (fin) dw_taps<2>(oi2, fv, fg, wv, wg);
+        if (kInner || (i >= 1 && i - 1 < st.R)) dw_taps<1>(oi1, fv, fg, wv, wg);
+        if (kInner || i < st.R) dw_taps<0>(oi, fv, fg, wv, wg);
     }
-    __syncthreads();  // the barrier is initialised before anyone waits on it
-    if (!mbar_wait(bar, 0, err, kTimeout)) {
-        if (threadIdx.x == 0) mbar_wait_quiet(bar, 0);  // let the copies land before the block exits
-        return;
+    uint64_t t[kCols];
+    if (fin) {
+#pragma unroll
+        for (int c = 0; c < kCols; ++c) {
+            const float2 hs = f2_split(oi2.a[c][1]);
+            t[c] = f2_make(tanh_approx(hs.x), tanh_approx(hs.y));
+        }
     }
-    if (!pok) return;
-    const int rows = min(kTileRows, H - y0);
-    const uint32_t* t32 = reinterpret_cast<const uint32_t*>(tile);
-    for (int x0 = 2 * (threadIdx.x / 32); x0 < W; x0 += 2 * (blockDim.x / 32)) {
-        uint64_t acc[3][2][2];  // [output row slot][column][value, gate]; +0.0 pairs
+    if (kInner || i + 1 <= st.R + 1) dw_fetch(st, i + 1, raw);
+    if (fin) {
+        bf16* o = st.orow + (i - 2) * st.orow_step;
 #pragma unroll
-        for (int a = 0; a < 3; ++a)
-#pragma unroll
-            for (int c = 0; c < 2; ++c) acc[a][c][0] = acc[a][c][1] = 0;
-#pragma unroll
-        for (int r = 0; r < kTileRows + 2; ++r) {
-            if (r >= rows + 2) break;
-            uint64_t fv[4], fg[4];
-            const uint32_t* rp = t32 + (r * PW + x0) * kPairs + p;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                fv[j] = f2_from_bf2(rp[j * kPairs]);
-                fg[j] = f2_from_bf2(rp[box / 2 + j * kPairs]);
-            }
-#pragma unroll
-            for (int ky = 0; ky < 3; ++ky) {
-                const int o = r - ky;  // the output row this input row feeds through tap row ky
-                if (o < 0 || o >= kTileRows) continue;
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int kx = 0; kx < 3; ++kx) {
-                        acc[o % 3][c][0] = fma2(fv[c + kx], wv[ky * 3 + kx], acc[o % 3][c][0]);
-                        acc[o % 3][c][1] = fma2(fg[c + kx], wg[ky * 3 + kx], acc[o % 3][c][1]);
-                    }
-            }
-            if (r >= 2) {  // output row r - 2 has all nine taps
-                const int o = r - 2;
-                const long long pix = (static_cast<long long>(s) * H + y0 + o) * W + x0;
-#pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    const uint64_t v = add2(acc[o % 3][c][0], bv);
-                    const uint64_t g = add2(acc[o % 3][c][1], bg);
-                    acc[o % 3][c][0] = acc[o % 3][c][1] = 0;
-                    if (x0 + c < W) {
-                        const float2 y = f2_split(mul2(v, silu2(g)));
-                        *reinterpret_cast<__nv_bfloat162*>(out + (pix + c) * ldo + ch) = __floats2bfloat162_rn(y.x, y.y);
-                    }
-                }
-            }
+        for (int c = 0; c < kCols; ++c) {
+            const uint64_t h = oi2.a[c][1];
+            const float2 v = f2_split(mul2(oi2.a[c][0], fma2(h, t[c], h)));
+            if (st.pok && c < st.ncols)
+                *reinterpret_cast<__nv_bfloat162*>(o + c * st.ldo) = __floats2bfloat162_rn(v.x, v.y);
+            oi2.a[c][0] = bv;
+            oi2.a[c][1] = bg;
         }
     }
 }
 
-size_t dwglu_tile_smem(int W) {
-    return sizeof(bf16) * (kTileRows + 2) * tile_pixels(W) * 2 * kTileCh + 128;
+__global__ void __launch_bounds__(kDwThreads, 1)
+    dwglu_stream_kernel(const __grid_constant__ CUtensorMap map, int S, int H, int W, int half, int band_rows,
+                        int bands, int stripes, const float* __restrict__ w, const float* __restrict__ b,
+                        bf16* __restrict__ out, long long ldo, int* err) {
+    extern __shared__ __align__(128) unsigned char dyn[];
+    __shared__ __align__(8) uint64_t full_bar[kDwRing], empty_bar[kDwRing];
+    unsigned char* ring = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(dyn) + 127) & ~uintptr_t(127));
+    const int slices = (half + kSliceCh - 1) / kSliceCh;
+    const int items = S * bands * stripes * slices;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kDwRing; ++i) {
+            mbar_init(smem_u32(&full_bar[i]), 1);
+            mbar_init(smem_u32(&empty_bar[i]), kDwWarps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == kDwWarps) {  // producer
+        if (lane != 0) return;
+        uint32_t n = 0;
+        bool ok = true;
+        for (int it = blockIdx.x; ok && it < items; it += gridDim.x) {
+            const DwItem d = dw_item(it, H, band_rows, bands, stripes, slices);
+            const int nslots = dw_slots(d.rows);
+            for (int k = 0; k < nslots; ++k, ++n) {
+                const int slot = n % kDwRing;
+                if (!mbar_wait(smem_u32(&empty_bar[slot]), ((n / kDwRing) & 1) ^ 1, err, kTimeout)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t fb = smem_u32(&full_bar[slot]);
+                mbar_arrive_expect_tx(fb, kSlotBytes);
+                tma_load_5d(&map, smem_u32(ring + slot * kSlotBytes), fb, d.c0, 0, d.x0 - 1,
+                            d.y0 - 1 + k * kSlotRows, d.s);
+            }
+        }
+        if (!ok) {  // let the copies in flight land before the block exits
+            for (uint32_t k = n > kDwRing ? n - kDwRing : 0; k < n; ++k)
+                mbar_wait_quiet(smem_u32(&full_bar[k % kDwRing]), (k / kDwRing) & 1);
+        }
+        return;
+    }
+
+    // consumer
+    const int p = lane;
+    DwStep st;
+    st.px = ring + kCols * warp * kPxBytes + 4 * p;
+    st.full_bar = full_bar;
+    st.empty_bar = empty_bar;
+    st.err = err;
+    st.slot0 = 0;
+    st.lane = lane;
+    st.H = H;
+    st.ldo = ldo;
+    st.orow_step = static_cast<long long>(W) * ldo;
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+        const DwItem d = dw_item(it, H, band_rows, bands, stripes, slices);
+        const int ch = d.c0 + 2 * p;
+        st.pok = ch < half;  // half is a multiple of 8: both channels of the pair exist
+        uint64_t wv[9], wg[9], bv = 0, bg = 0;
+#pragma unroll
+        for (int t = 0; t < 9; ++t) {
+            wv[t] = st.pok ? f2_make(w[static_cast<long long>(ch) * 9 + t], w[static_cast<long long>(ch + 1) * 9 + t])
+                           : 0;
+            wg[t] = st.pok ? f2_make(0.5f * w[static_cast<long long>(half + ch) * 9 + t],
+                                     0.5f * w[static_cast<long long>(half + ch + 1) * 9 + t])
+                           : 0;
+        }
+        if (st.pok) {
+            bv = f2_make(b[ch], b[ch + 1]);
+            bg = f2_make(0.5f * b[half + ch], 0.5f * b[half + ch + 1]);
+        }
+        const int xw = d.x0 + kCols * warp;  // first column of this thread
+        st.ncols = min(kCols, W - xw);
+        st.y0 = d.y0;
+        st.R = d.rows;
+        st.orow = out + (static_cast<long long>(d.s) * H + d.y0) * st.orow_step + static_cast<long long>(xw) * ldo + ch;
+        DwRow acc[3];  // output row ol of the band accumulates in acc[ol % 3]
+#pragma unroll
+        for (int k = 0; k < 3; ++k)
+#pragma unroll
+            for (int c = 0; c < kCols; ++c) {
+                acc[k].a[c][0] = bv;
+                acc[k].a[c][1] = bg;
+            }
+        // step i passes (output i, output i - 1, output i - 2) =
+        // (acc[i % 3], acc[(i + 2) % 3], acc[(i + 1) % 3])
+        DwRaw raw;
+        dw_fetch(st, 0, raw);
+        dw_step<false>(st, 0, acc[0], acc[2], acc[1], raw, wv, wg, bv, bg);
+        dw_step<false>(st, 1, acc[1], acc[0], acc[2], raw, wv, wg, bv, bg);
+        int i = 2;
+        for (; i + 3 <= d.rows; i += 3) {
+            dw_step<true>(st, i, acc[2], acc[1], acc[0], raw, wv, wg, bv, bg);
+            dw_step<true>(st, i + 1, acc[0], acc[2], acc[1], raw, wv, wg, bv, bg);
+            dw_step<true>(st, i + 2, acc[1], acc[0], acc[2], raw, wv, wg, bv, bg);
+        }
+        // the last two to four steps (through i = R + 1), with bounds tests
+        dw_step<false>(st, i, acc[2], acc[1], acc[0], raw, wv, wg, bv, bg);
+        dw_step<false>(st, i + 1, acc[0], acc[2], acc[1], raw, wv, wg, bv, bg);
+        dw_step<false>(st, i + 2, acc[1], acc[0], acc[2], raw, wv, wg, bv, bg);
+        dw_step<false>(st, i + 3, acc[2], acc[1], acc[0], raw, wv, wg, bv, bg);
+        if (*reinterpret_cast<volatile int*>(err) != 0) return;
+        st.slot0 += dw_slots(d.rows);
+    }
 }
+
+size_t dwglu_stream_smem() { return static_cast<size_t>(kDwRing) * kSlotBytes + 128; }
 
 // Any type / channel count: one output channel per thread.
 template <class T>
@@ -199,31 +359,43 @@ void depthwise_glu(const T* in, long long ldi, int S, int H, int W, int E, const
     const int half = E / 2;
     const long long pixels = static_cast<long long>(S) * H * W;
     if (pixels == 0 || half == 0) return;
-    bool vec = sizeof(T) == 2 && half % 8 == 0 && ldi % 8 == 0 && ldo % 8 == 0 &&
-               (reinterpret_cast<uintptr_t>(in) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
-    if (vec && W <= kTileW) {
-        const int tiles = ceil_div(half, kTileCh);
-        const int row_tiles = ceil_div(H, kTileRows);
-        const dim3 grid(static_cast<unsigned>(S * row_tiles), tiles);
+    bool vec = sizeof(T) == 2 && half % 8 == 0 && ldi % 8 == 0 && ldo % 2 == 0 &&
+               (reinterpret_cast<uintptr_t>(in) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 3) == 0;
+    if (vec) {
+        static int device_sms[64] = {0};
         static bool attr = false;
+        int dev = 0;
+        SANA_CUDA(cudaGetDevice(&dev));
         if (!attr) {
-            SANA_CUDA(cudaFuncSetAttribute(dwglu_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(dwglu_tile_smem(kTileW))));
+            SANA_CUDA(cudaFuncSetAttribute(dwglu_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(dwglu_stream_smem())));
             attr = true;
         }
-        // [S, H, W, channels] with the channel rows ldi apart; box = 64 channels x tile pixels
-        // x (kTileRows + 2) rows x 1 sequence
+        int& sms = device_sms[dev & 63];
+        if (sms == 0) SANA_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        const int slices = ceil_div(half, kSliceCh), stripes = ceil_div(W, kStripe);
+        // Split the image rows into bands (each re-reading a one-row halo) only when the
+        // sequences, stripes and channel slices alone give fewer than two items per SM.
+        const long long base = static_cast<long long>(S) * stripes * slices;
+        int bands = static_cast<int>(std::min<long long>((2LL * sms + base - 1) / base, (H + 7) / 8));
+        if (bands < 1) bands = 1;
+        const int band_rows = ceil_div(H, bands);
+        bands = ceil_div(H, band_rows);
+        const long long items = base * bands;
+        SANA_REQUIRE(items < (1LL << 31), "depthwise_glu: too many work items");
+        // [S, H, W, 2 halves, half channels]; box = 64 channels x 2 halves x (32 + 2) pixels x rows
         CUtensorMap map;
-        const cuuint64_t dims[4] = {static_cast<cuuint64_t>(2 * half), static_cast<cuuint64_t>(W),
+        const cuuint64_t dims[5] = {static_cast<cuuint64_t>(half), 2, static_cast<cuuint64_t>(W),
                                     static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(S)};
-        const cuuint64_t strides[3] = {static_cast<cuuint64_t>(ldi) * 2, static_cast<cuuint64_t>(ldi) * 2 * W,
+        const cuuint64_t strides[4] = {static_cast<cuuint64_t>(half) * 2, static_cast<cuuint64_t>(ldi) * 2,
+                                       static_cast<cuuint64_t>(ldi) * 2 * W,
                                        static_cast<cuuint64_t>(ldi) * 2 * W * H};
-        const cuuint32_t box[4] = {static_cast<cuuint32_t>(kTileCh), static_cast<cuuint32_t>(tile_pixels(W)),
-                                   static_cast<cuuint32_t>(kTileRows + 2), 1};
-        tma_encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, in, dims, strides, box,
+        const cuuint32_t box[5] = {kSliceCh, 2, kStripePx, kSlotRows, 1};
+        tma_encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, in, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_NONE);
-        dwglu_tile_kernel<<<grid, 256, dwglu_tile_smem(W), st>>>(map, S, H, W, half, w, b,
-                                                                  reinterpret_cast<bf16*>(out), ldo, err);
+        const int grid = static_cast<int>(std::min<long long>(items, sms));
+        dwglu_stream_kernel<<<grid, kDwThreads, dwglu_stream_smem(), st>>>(
+            map, S, H, W, half, band_rows, bands, stripes, w, b, reinterpret_cast<bf16*>(out), ldo, err);
     } else {
         dwglu_scalar_kernel<T><<<grid_for(pixels * half), 256, 0, st>>>(in, ldi, S, H, W, half, w, b, out, ldo);
     }

@@ -114,6 +114,54 @@ def test_gemm_activation_epilogue(gpu_bf16, act):
     assert (err <= bound).all(), float((err / bound).max())
 
 
+def _dwglu_f64(x, w, b):
+    """Depthwise 3x3 (zero padding) + bias over [S, H, W, E] tokens, split into the value and
+    gate halves (common_ops.cpp:484-505 and 745-758), in float64."""
+    S, H, W, E = x.shape
+    xp = np.zeros((S, H + 2, W + 2, E))
+    xp[:, 1:-1, 1:-1] = x
+    acc = np.zeros((S, H, W, E))
+    for ky in range(3):
+        for kx in range(3):
+            acc += xp[:, ky:ky + H, kx:kx + W] * w[:, ky * 3 + kx]
+    acc += b
+    return acc[..., :E // 2], acc[..., E // 2:]
+
+
+@pytest.mark.parametrize("S,H,W,E,gscale", [(2, 32, 32, 5760, 1.0), (1, 64, 64, 256, 1.0), (3, 7, 40, 80, 1.0),
+                                            (1, 1, 1, 16, 1.0), (2, 9, 33, 128, 40.0)])
+def test_depthwise_glu_device(gpu_bf16, S, H, W, E, gscale):
+    """The bf16 streaming depthwise+GLU kernel on device buffers (config-2 channel count, two
+    column stripes, a partial channel slice, a single pixel, gates reaching +-100): every bf16
+    output within its own rounding (2^-8) of the float64 result of the same bf16 inputs, plus
+    the hardware tanh's error (2^-10 relative) carried through silu(g) = g (1 + tanh(g/2)) / 2."""
+    import ctypes
+
+    import torch
+    rng = np.random.default_rng(S * 1000 + H * 10 + W + E)
+    x = bf16_round(rng.standard_normal((S, H, W, E)).astype(np.float32))
+    w = (rng.standard_normal((E, 9)) * 0.3).astype(np.float32)
+    b = rng.standard_normal(E).astype(np.float32)
+    w[E // 2:] *= gscale
+    b[E // 2:] *= gscale
+    v, g = _dwglu_f64(x.astype(np.float64), w.astype(np.float64), b.astype(np.float64))
+    sig = 1.0 / (1.0 + np.exp(-g))
+    ref = v * g * sig
+    xt = torch.from_numpy(x).to("cuda", torch.bfloat16)
+    wt, bt = torch.from_numpy(w).cuda(), torch.from_numpy(b).cuda()
+    out = torch.empty(S, H, W, E // 2, device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    vp = ctypes.c_void_p
+    gpu_bf16._call("sana_op_depthwise_glu_device", vp(xt.data_ptr()), ctypes.c_int(S), ctypes.c_int(H),
+                   ctypes.c_int(W), ctypes.c_int(E), vp(wt.data_ptr()), vp(bt.data_ptr()), vp(out.data_ptr()))
+    gpu_bf16.synchronize()
+    got = out.float().cpu().numpy().astype(np.float64)
+    tanh_err = 2.0 ** -10 * np.abs(v * g / 2) * np.abs(2 * sig - 1)
+    bound = 2.0 ** -8 * np.abs(ref) + tanh_err + 1e-5 * np.abs(v) + 1e-6
+    err = np.abs(got - ref)
+    assert (err <= bound).all(), float((err / bound).max())
+
+
 def test_gemm_repeatable(gpu_bf16):
     rng = np.random.default_rng(5)
     x = rng.standard_normal((1024, 1152)).astype(np.float32)
