@@ -270,7 +270,7 @@ def gemm_roofline(g, torch, stream, M, peak_tflops):
 
 MICRO_OPS = ("qkv_gemm", "linear_attention_16x72", "linear_attention_36x32", "depthwise_glu", "cross_attention",
              "ff_inverted_config2", "linear_attention_config2", "depthwise_glu_config2", "cross_attention_config2",
-             "out_proj_config2")
+             "out_proj_config2", "ln_modulate_config2")
 
 
 def run_microbench(args):
@@ -364,6 +364,17 @@ def run_microbench(args):
             out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
             ms = timed(lambda: g.gemm_device(A.data_ptr(), B.data_ptr(), M, N, K, out.data_ptr(), bias.data_ptr(), 1))
             report(name, f"M={M} K={K} N={N} +bias, SiLU, bf16 out", ms, 2.0 * M * N * K, "tensor")
+        elif name == "ln_modulate_config2":
+            # layer_norm + AdaLN modulate of the residual stream (norm1 / norm2 of every block)
+            M = S * T
+            x = torch.randn(M, C, generator=gen).cuda()
+            mod = torch.randn(S, 6 * C, generator=gen).cuda()
+            out = torch.empty(M, C, device="cuda", dtype=torch.bfloat16)
+            ms = timed(lambda: g._call("sana_op_ln_modulate_device", vp(x.data_ptr()), ctypes.c_longlong(M), I(C), I(T),
+                                       vp(mod.data_ptr()), ctypes.c_longlong(6 * C), I(0), I(1), ctypes.c_float(1e-6),
+                                       vp(out.data_ptr())))
+            byts = 4.0 * M * C + 2.0 * M * C
+            report(name, f"[{M},{C}] fp32 -> bf16 ({byts / 1e6:.0f} MB)", ms, byts, "hbm")
         elif name == "out_proj_config2":
             # the self-attention output projection: fp32 residual + gate x (A W^T + b), bf16 copy
             M, N, K = S * T, C, C

@@ -269,6 +269,12 @@ int sana_op_linear_attention_noalloc(sana_cuda_ctx *ctx, const void *qkv, int S,
 /* depthwise_conv2d_3x3 + GLU gate on NHWC rows [S*H*W, E] -> [S*H*W, E/2]; w [E, 9], b [E] fp32. */
 int sana_op_depthwise_glu_device(sana_cuda_ctx *ctx, const void *in, int S, int H, int W, int E, const float *w,
                                  const float *b, void *out);
+/* layer_norm (no affine) followed by modulate_3d_lastdim (tensor.cpp:243-265, 323-376) on
+ * device rows: x [rows, C] fp32, sequence s = row / rows_per_seq takes shift = mod + s*mod_ld
+ * + shift_idx*C and scale = mod + s*mod_ld + scale_idx*C; out [rows, C] bf16. */
+int sana_op_ln_modulate_device(sana_cuda_ctx *ctx, const float *x, long long rows, int C, int rows_per_seq,
+                               const float *mod, long long mod_ld, int shift_idx, int scale_idx, float eps,
+                               void *out);
 /* attention_4d for cross-attention: q [S*T, heads*D], kv [S*L, 2*heads*D] (k | v), bias
  * [S, L] fp32 or NULL, kv_len int[S] scratch (filled from bias), out [S*T, heads*D]. */
 int sana_op_cross_attention_device(sana_cuda_ctx *ctx, const void *q, const void *kv, const float *bias,

@@ -987,6 +987,18 @@ int sana_op_depthwise_glu_device(sana_cuda_ctx* ctx, const void* in, int S, int 
     });
 }
 
+int sana_op_ln_modulate_device(sana_cuda_ctx* ctx, const float* x, long long rows, int C, int rows_per_seq,
+                               const float* mod, long long mod_ld, int shift_idx, int scale_idx, float eps,
+                               void* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(x && out && rows >= 0 && C >= 1 && rows_per_seq >= 1 && eps >= 0.f, "invalid arguments");
+        SANA_REQUIRE(!mod || (shift_idx >= 0 && scale_idx >= 0 && mod_ld >= C), "invalid modulation layout");
+        sana::Engine& eng = engine(ctx);
+        sana::ln_modulate<bf16>(x, rows, C, rows_per_seq, nullptr, nullptr, mod, mod_ld, shift_idx, scale_idx, eps,
+                                static_cast<bf16*>(out), eng.stream());
+    });
+}
+
 int sana_op_cross_attention_device(sana_cuda_ctx* ctx, const void* q, const void* kv, const float* bias,
                                    int* kv_len, int S, int T, int L, int heads, int D, void* out) {
     return guard(ctx, [&] {

@@ -60,66 +60,98 @@ __global__ void ln_modulate_kernel(const float* __restrict__ x, long long rows, 
     }
 }
 
-// Row in registers (C = 128 * NV): one warp per row, each lane holding NV float4 of the
-// row; mean, then the centred variance from the registers, then the normalised, modulated
-// row written with 8-byte (bf16) or 16-byte (fp32) stores.
-template <class TO, int NV>
-__global__ void ln_modulate_reg_kernel(const float* __restrict__ x, long long rows, int rows_per_seq,
-                                       const float* __restrict__ gamma, const float* __restrict__ beta,
-                                       const float* __restrict__ mod, long long mod_ld, int shift_idx, int scale_idx,
-                                       float eps, TO* __restrict__ out) {
+// Rows in registers (C = 128 * NV): a block of 8 warps takes 8 * RW consecutive rows, each
+// warp RW of them (w, w + 8, ...; two when a row is at most 1024 wide, else one, so that the
+// rows fit the registers), and every lane holds NV float4 of each row; the
+// mean, then the centred variance come from the registers (the order of tensor.cpp:243-265),
+// and the normalised, modulated rows are written with 8-byte (bf16) or 16-byte (fp32)
+// stores. All of the block's row loads are in flight before anything else; meanwhile the
+// block stages the shift and scale vectors of its first row's sequence in shared memory
+// once, instead of every warp fetching them after its reductions.
+constexpr int kLnWarps = 8;
+template <int NV> constexpr int ln_rows_per_warp() { return NV <= 8 ? 2 : 1; }
+
+template <class TO, int NV, int RW = ln_rows_per_warp<NV>()>
+__global__ void __launch_bounds__(32 * kLnWarps, RW == 1 ? 4 : 2)
+    ln_modulate_reg_kernel(const float* __restrict__ x, long long rows, int rows_per_seq,
+                           const float* __restrict__ gamma, const float* __restrict__ beta,
+                           const float* __restrict__ mod, long long mod_ld, int shift_idx, int scale_idx, float eps,
+                           TO* __restrict__ out) {
     constexpr int C = 128 * NV;
-    const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
-    const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    const float4* xr = reinterpret_cast<const float4*>(x + row * C);
-    float4 v[NV];
+    __shared__ float4 s_shift[32 * NV], s_scale[32 * NV];
+    const long long row0 = static_cast<long long>(blockIdx.x) * (kLnWarps * RW);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    float4 v[RW][NV];
 #pragma unroll
-    for (int i = 0; i < NV; ++i) v[i] = xr[lane + 32 * i];
-    float s = 0.f;
+    for (int r = 0; r < RW; ++r) {
+        const long long row = row0 + warp + r * kLnWarps;
+        if (row < rows) {
+            const float4* xr = reinterpret_cast<const float4*>(x + row * C);
 #pragma unroll
-    for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-    const float mean = warp_sum(s) / static_cast<float>(C);
-    float q = 0.f;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
-        q += (a * a + b * b) + (c * c + d * d);
+            for (int i = 0; i < NV; ++i) v[r][i] = xr[lane + 32 * i];
+        }
     }
-    const float var = warp_sum(q) / static_cast<float>(C);
-    const float inv_std = 1.0f / sqrtf(var + eps);
-    const long long seq = row / rows_per_seq;
-    const float* shift = mod ? mod + seq * mod_ld + static_cast<long long>(shift_idx) * C : nullptr;
-    const float* scale = mod ? mod + seq * mod_ld + static_cast<long long>(scale_idx) * C : nullptr;
+    const long long seq0 = row0 / rows_per_seq;
+    if (mod) {
+        const float4* sh = reinterpret_cast<const float4*>(mod + seq0 * mod_ld + static_cast<long long>(shift_idx) * C);
+        const float4* sc = reinterpret_cast<const float4*>(mod + seq0 * mod_ld + static_cast<long long>(scale_idx) * C);
+        for (int i = threadIdx.x; i < 32 * NV; i += blockDim.x) {
+            s_shift[i] = sh[i];
+            s_scale[i] = sc[i];
+        }
+    }
+    __syncthreads();
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        const int c = 4 * (lane + 32 * i);
-        float o[4] = {(v[i].x - mean) * inv_std, (v[i].y - mean) * inv_std, (v[i].z - mean) * inv_std,
-                      (v[i].w - mean) * inv_std};
-        if (gamma) {
-            const float4 g = *reinterpret_cast<const float4*>(gamma + c);
-            o[0] *= g.x; o[1] *= g.y; o[2] *= g.z; o[3] *= g.w;
+    for (int r = 0; r < RW; ++r) {
+        const long long row = row0 + warp + r * kLnWarps;
+        if (row >= rows) break;
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) s += (v[r][i].x + v[r][i].y) + (v[r][i].z + v[r][i].w);
+        const float mean = warp_sum(s) / static_cast<float>(C);
+        float q = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const float a = v[r][i].x - mean, b = v[r][i].y - mean, c = v[r][i].z - mean, d = v[r][i].w - mean;
+            q += (a * a + b * b) + (c * c + d * d);
         }
-        if (beta) {
-            const float4 bb = *reinterpret_cast<const float4*>(beta + c);
-            o[0] += bb.x; o[1] += bb.y; o[2] += bb.z; o[3] += bb.w;
-        }
-        if (mod) {
-            const float4 sc = *reinterpret_cast<const float4*>(scale + c);
-            const float4 sh = *reinterpret_cast<const float4*>(shift + c);
-            o[0] = o[0] * (1.0f + sc.x) + sh.x;
-            o[1] = o[1] * (1.0f + sc.y) + sh.y;
-            o[2] = o[2] * (1.0f + sc.z) + sh.z;
-            o[3] = o[3] * (1.0f + sc.w) + sh.w;
-        }
-        if constexpr (sizeof(TO) == 2) {
-            __nv_bfloat162 h0 = __floats2bfloat162_rn(o[0], o[1]), h1 = __floats2bfloat162_rn(o[2], o[3]);
-            uint2 pk;
-            pk.x = *reinterpret_cast<uint32_t*>(&h0);
-            pk.y = *reinterpret_cast<uint32_t*>(&h1);
-            *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(out) + row * C + c) = pk;
-        } else {
-            *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + row * C + c) = make_float4(o[0], o[1], o[2], o[3]);
+        const float var = warp_sum(q) / static_cast<float>(C);
+        const float inv_std = 1.0f / sqrtf(var + eps);
+        const long long seq = row / rows_per_seq;
+        const bool staged = seq == seq0;
+        const float* shift = mod ? mod + seq * mod_ld + static_cast<long long>(shift_idx) * C : nullptr;
+        const float* scale = mod ? mod + seq * mod_ld + static_cast<long long>(scale_idx) * C : nullptr;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int c = 4 * (lane + 32 * i);
+            float o[4] = {(v[r][i].x - mean) * inv_std, (v[r][i].y - mean) * inv_std, (v[r][i].z - mean) * inv_std,
+                          (v[r][i].w - mean) * inv_std};
+            if (gamma) {
+                const float4 g = *reinterpret_cast<const float4*>(gamma + c);
+                o[0] *= g.x; o[1] *= g.y; o[2] *= g.z; o[3] *= g.w;
+            }
+            if (beta) {
+                const float4 bb = *reinterpret_cast<const float4*>(beta + c);
+                o[0] += bb.x; o[1] += bb.y; o[2] += bb.z; o[3] += bb.w;
+            }
+            if (mod) {
+                const float4 sc = staged ? s_scale[lane + 32 * i] : *reinterpret_cast<const float4*>(scale + c);
+                const float4 sh = staged ? s_shift[lane + 32 * i] : *reinterpret_cast<const float4*>(shift + c);
+                o[0] = o[0] * (1.0f + sc.x) + sh.x;
+                o[1] = o[1] * (1.0f + sc.y) + sh.y;
+                o[2] = o[2] * (1.0f + sc.z) + sh.z;
+                o[3] = o[3] * (1.0f + sc.w) + sh.w;
+            }
+            if constexpr (sizeof(TO) == 2) {
+                __nv_bfloat162 h0 = __floats2bfloat162_rn(o[0], o[1]), h1 = __floats2bfloat162_rn(o[2], o[3]);
+                uint2 pk;
+                pk.x = *reinterpret_cast<uint32_t*>(&h0);
+                pk.y = *reinterpret_cast<uint32_t*>(&h1);
+                *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(out) + row * C + c) = pk;
+            } else {
+                *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + row * C + c) =
+                    make_float4(o[0], o[1], o[2], o[3]);
+            }
         }
     }
 }
@@ -304,8 +336,11 @@ void ln_modulate(const float* x, long long rows, int C, int rows_per_seq, const 
         switch (C / 128) {
 #define SANA_LN_CASE(NV)                                                                                        \
     case NV:                                                                                                    \
-        ln_modulate_reg_kernel<TO, NV><<<grid, warps * 32, 0, st>>>(x, rows, rows_per_seq, gamma, beta, mod, mod_ld, \
-                                                                    shift_idx, scale_idx, eps, out);           \
+        ln_modulate_reg_kernel<TO, NV>                                                                          \
+            <<<static_cast<unsigned>((rows + kLnWarps * ln_rows_per_warp<NV>() - 1) /                          \
+                                     (kLnWarps * ln_rows_per_warp<NV>())),                                      \
+               kLnWarps * 32, 0, st>>>(x, rows, rows_per_seq, gamma, beta, mod, mod_ld, shift_idx, scale_idx, eps, \
+                                       out);                                                                    \
         SANA_CUDA(cudaGetLastError());                                                                          \
         return;
             SANA_LN_CASE(1) SANA_LN_CASE(2) SANA_LN_CASE(3) SANA_LN_CASE(4) SANA_LN_CASE(5) SANA_LN_CASE(6)

@@ -162,6 +162,38 @@ def test_depthwise_glu_device(gpu_bf16, S, H, W, E, gscale):
     assert (err <= bound).all(), float((err / bound).max())
 
 
+@pytest.mark.parametrize("rows,C,rps", [(32768 // 8, 1152, 1024), (45, 1152, 7), (33, 256, 5), (19, 384, 19),
+                                         (10, 1000, 3)])
+def test_ln_modulate_device(gpu_bf16, rows, C, rps):
+    """layer_norm + modulate on device rows (the register path for widths of 128 k, blocks whose
+    rows span several sequences, and the generic path for other widths) against float64: every
+    bf16 output within its own rounding of the exact value."""
+    import ctypes
+
+    import torch
+    rng = np.random.default_rng(rows + C + rps)
+    x = (rng.standard_normal((rows, C)) * 3 + 1.5).astype(np.float32)
+    S = -(-rows // rps)
+    mod = (rng.standard_normal((S, 6, C)) * 0.5).astype(np.float32)
+    xd = x.astype(np.float64)
+    mean = xd.mean(axis=1, keepdims=True)
+    var = ((xd - mean) ** 2).mean(axis=1, keepdims=True)
+    seq = np.arange(rows) // rps
+    shift, scale = mod[seq, 3].astype(np.float64), mod[seq, 4].astype(np.float64)
+    ref = (xd - mean) / np.sqrt(var + 1e-6) * (1 + scale) + shift
+    xt, mt = torch.from_numpy(x).cuda(), torch.from_numpy(mod).cuda()
+    out = torch.empty(rows, C, device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    gpu_bf16._call("sana_op_ln_modulate_device", ctypes.c_void_p(xt.data_ptr()), ctypes.c_longlong(rows),
+                   ctypes.c_int(C), ctypes.c_int(rps), ctypes.c_void_p(mt.data_ptr()), ctypes.c_longlong(6 * C),
+                   ctypes.c_int(3), ctypes.c_int(4), ctypes.c_float(1e-6), ctypes.c_void_p(out.data_ptr()))
+    gpu_bf16.synchronize()
+    got = out.float().cpu().numpy().astype(np.float64)
+    err = np.abs(got - ref)
+    bound = 2.0 ** -8 * np.abs(ref) + 1e-5 * (1 + np.abs(ref))
+    assert (err <= bound).all(), float((err / bound).max())
+
+
 def test_gemm_repeatable(gpu_bf16):
     rng = np.random.default_rng(5)
     x = rng.standard_normal((1024, 1152)).astype(np.float32)
