@@ -241,22 +241,22 @@ void Engine::upload_impl(const float* const* model, const float* const* blocks, 
     cap_w2_.ensure(static_cast<size_t>(C) * C * as);
     put(cap_w2_.as<T>(), model[2], C, C, true);
     vec(cap_b2_, model[3], C, 0.f, true);
-    patch_w_.ensure(static_cast<size_t>(C) * Cl * 4);
-    put(patch_w_.as<float>(), model[4], C, Cl, false);
+    patch_w_.ensure(static_cast<size_t>(C) * Cl * as);
+    put(patch_w_.as<T>(), model[4], C, Cl, false);
     vec(patch_b_, model[5], C, 0.f, true);
-    te_w1_.ensure(static_cast<size_t>(C) * 256 * 4);
-    put(te_w1_.as<float>(), model[6], C, 256, true);
+    te_w1_.ensure(static_cast<size_t>(C) * 256 * as);
+    put(te_w1_.as<T>(), model[6], C, 256, true);
     vec(te_b1_, model[7], C, 0.f, true);
-    te_w2_.ensure(static_cast<size_t>(C) * C * 4);
-    put(te_w2_.as<float>(), model[8], C, C, true);
+    te_w2_.ensure(static_cast<size_t>(C) * C * as);
+    put(te_w2_.as<T>(), model[8], C, C, true);
     vec(te_b2_, model[9], C, 0.f, true);
-    tp_w_.ensure(static_cast<size_t>(6) * C * C * 4);
-    put(tp_w_.as<float>(), model[10], 6 * C, C, true);
+    tp_w_.ensure(static_cast<size_t>(6) * C * C * as);
+    put(tp_w_.as<T>(), model[10], 6 * C, C, true);
     vec(tp_b_, model[11], 6 * static_cast<size_t>(C), 0.f, true);
     vec(cap_norm_, model[12], C, 1.f, false);
     vec(ftable_, model[13], 2 * static_cast<size_t>(C), 0.f, false);
-    out_w_.ensure(static_cast<size_t>(Cl) * C * 4);
-    put(out_w_.as<float>(), model[14], Cl, C, true);
+    out_w_.ensure(static_cast<size_t>(Cl) * C * as);
+    put(out_w_.as<T>(), model[14], Cl, C, true);
     vec(out_b_, model[15], Cl, 0.f, true);
 
     // blocks (SanaBlockWeights field order)
@@ -504,17 +504,21 @@ void Engine::block_impl(int b, const float* x_in, float* x_self, float* x_cross,
 
 // t-embedding MLP and t_block (transformer.cpp:638-656), fp32 weights and activations.
 template <class T>
-void Engine::time_embed_impl(const float* tproj_d, int S) {
+void Engine::time_embed_impl(const void* tproj_d, int S) {
+    // timestep embedding MLP and t_block (transformer.cpp:639-652); in bf16 mode the three
+    // projections run on the tensor cores with bf16 operands like every other dense
+    // projection, emb itself (the final layer's modulation input) staying fp32
     const int C = d_.C;
-    gemm_act(tproj_d, 256, te_w1_.get(), 256, S, C, 256, epi_out(teh_.get(), false, C, te_b1_.as<float>(), kActSilu),
-             true);
+    const bool b16 = sizeof(T) == 2;
+    gemm_act(tproj_d, 256, te_w1_.get(), 256, S, C, 256, epi_out(teh_.get(), b16, C, te_b1_.as<float>(), kActSilu),
+             false);
     Epilogue e = epi_out(emb_.get(), false, C, te_b2_.as<float>());
     e.out2 = embs_.get();
-    e.out2_bf16 = 0;
+    e.out2_bf16 = b16 ? 1 : 0;
     e.ldo2 = C;
     e.act2 = kActSilu;
-    gemm_act(teh_.get(), C, te_w2_.get(), C, S, C, C, e, true);
-    gemm_act(embs_.get(), C, tp_w_.get(), C, S, 6 * C, C, epi_out(tmod_.get(), false, 6 * C, tp_b_.as<float>()), true);
+    gemm_act(teh_.get(), C, te_w2_.get(), C, S, C, C, e, false);
+    gemm_act(embs_.get(), C, tp_w_.get(), C, S, 6 * C, C, epi_out(tmod_.get(), false, 6 * C, tp_b_.as<float>()), false);
 }
 
 // repeat_batch_4d_local + patch embed 1x1 conv + grid_to_tokens (transformer.cpp:627-636).
@@ -522,8 +526,8 @@ template <class T>
 void Engine::prologue_impl(const float* lat_d, int images, int S, int H, int W) {
     const int C = d_.C, Cl = d_.Cl;
     const int M = S * H * W;
-    patch_tokens(lat_d, images, S, Cl, H * W, pt_.as<float>(), st_);
-    gemm_act(pt_.get(), Cl, patch_w_.get(), Cl, M, C, Cl, epi_out(x_.get(), false, C, patch_b_.as<float>()), true);
+    patch_tokens<T>(lat_d, images, S, Cl, H * W, pt_.as<T>(), st_);
+    gemm_act(pt_.get(), Cl, patch_w_.get(), Cl, M, C, Cl, epi_out(x_.get(), false, C, patch_b_.as<float>()), false);
 }
 
 // Final layer (transformer.cpp:668-678): LN (no affine) + modulate(emb + table) + proj_out.
@@ -532,9 +536,9 @@ void Engine::epilogue_impl(int S, int Tn) {
     const int C = d_.C, Cl = d_.Cl;
     const int M = S * Tn;
     final_modulation(emb_.as<float>(), S, C, ftable_.as<float>(), fmod_.as<float>(), st_);
-    ln_modulate<float>(x_.as<float>(), M, C, Tn, nullptr, nullptr, fmod_.as<float>(), 2LL * C, 0, 1, 1e-6f,
-                       y_.as<float>(), st_);
-    gemm_act(y_.get(), C, out_w_.get(), C, M, Cl, C, epi_out(noise_.get(), false, Cl, out_b_.as<float>()), true);
+    ln_modulate<T>(x_.as<float>(), M, C, Tn, nullptr, nullptr, fmod_.as<float>(), 2LL * C, 0, 1, 1e-6f, y_.as<T>(),
+                   st_);
+    gemm_act(y_.get(), C, out_w_.get(), C, M, Cl, C, epi_out(noise_.get(), false, Cl, out_b_.as<float>()), false);
 }
 
 template <class T>
@@ -557,8 +561,8 @@ void Engine::loop_body(const float* lat_in, int B, int H, int W, const float* en
     for (size_t step = 0; step < coefs.size(); ++step) {
         {
             ProfScope p(this, "timestep_embedding");
-            broadcast_rows(tproj_table_.as<float>() + step * 256, S, 256, tproj_.as<float>(), st_);
-            time_embed_impl<T>(tproj_.as<float>(), S);
+            broadcast_rows<T>(tproj_table_.as<float>() + step * 256, S, 256, tproj_.as<T>(), st_);
+            time_embed_impl<T>(tproj_.get(), S);
             block_modulation(tmod_.as<float>(), S, C, tables_.as<float>(), nb, mods_.as<float>(), st_);
         }
         {
@@ -787,8 +791,8 @@ void Engine::forward_nocfg(const float* lat, int S, int H, int W, float t, const
         using T = decltype(tag);
         convert<T>(ctx_f32_.as<float>(), static_cast<long long>(S) * L * C, ctx_.as<T>(), st_);
         kv_all_impl<T>(S, L);
-        broadcast_rows(tproj_table_.as<float>(), S, 256, tproj_.as<float>(), st_);
-        time_embed_impl<T>(tproj_.as<float>(), S);
+        broadcast_rows<T>(tproj_table_.as<float>(), S, 256, tproj_.as<T>(), st_);
+        time_embed_impl<T>(tproj_.get(), S);
         block_modulation(tmod_.as<float>(), S, C, tables_.as<float>(), d_.n_blocks, mods_.as<float>(), st_);
         prologue_impl<T>(in_lat_.as<float>(), S, S, H, W);
         const size_t ckv_stride = static_cast<size_t>(S) * L * 2 * C;
@@ -839,8 +843,8 @@ void Engine::denoise_step(float* lat, int B, int H, int W, const float* ctx, int
         using T = decltype(tag);
         convert<T>(ctx_f32_.as<float>(), static_cast<long long>(S) * L * C, ctx_.as<T>(), st_);
         kv_all_impl<T>(S, L);
-        broadcast_rows(tproj_table_.as<float>(), S, 256, tproj_.as<float>(), st_);
-        time_embed_impl<T>(tproj_.as<float>(), S);
+        broadcast_rows<T>(tproj_table_.as<float>(), S, 256, tproj_.as<T>(), st_);
+        time_embed_impl<T>(tproj_.get(), S);
         block_modulation(tmod_.as<float>(), S, C, tables_.as<float>(), d_.n_blocks, mods_.as<float>(), st_);
         prologue_impl<T>(lat_.as<float>(), B, S, H, W);
         const size_t ckv_stride = static_cast<size_t>(S) * L * 2 * C;

@@ -141,7 +141,7 @@ class Engine {
     template <class T>
     void block_impl(int b, const float* x_in, float* x_self, float* x_cross, float* x_ff, int S, int Tn, int L,
                     const float* mod_b, const void* ckv_b, const float* bias_d, const int* kvlen_d);
-    template <class T> void time_embed_impl(const float* tproj_d, int S);
+    template <class T> void time_embed_impl(const void* tproj_d, int S);
     template <class T> void prologue_impl(const float* lat_d, int images, int S, int H, int W);
     template <class T> void epilogue_impl(int S, int Tn);
     template <class T>

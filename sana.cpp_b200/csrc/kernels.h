@@ -39,11 +39,13 @@ void final_modulation(const float* emb, int S, int C, const float* table, float*
 // NCHW latents [images, Cl, HW] -> token rows [seqs * HW, Cl]; sequence s reads image
 // s % images (repeat_batch_4d_local, transformer.cpp:55-75, then the 1x1 conv's input
 // order; grid_to_tokens_3d, tensor.cpp:427).
-void patch_tokens(const float* lat, int images, int seqs, int Cl, int HW, float* out, cudaStream_t st);
+template <class TO>
+void patch_tokens(const float* lat, int images, int seqs, int Cl, int HW, TO* out, cudaStream_t st);
 
 // Sinusoidal timestep features for all sequences: out[s] = table row (precomputed on the
 // host with the reference's arithmetic) broadcast; used only to fill [S, 256].
-void broadcast_rows(const float* row, int S, int width, float* out, cudaStream_t st);
+template <class TO>
+void broadcast_rows(const float* row, int S, int width, TO* out, cudaStream_t st);
 
 // split_heads_3d ([B, T, H*D] -> [B, H, T, D], to_heads) and merge_heads_4d (the inverse),
 // transformer_ops.cpp:83-171; fp32.

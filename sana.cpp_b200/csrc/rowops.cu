@@ -197,8 +197,9 @@ __global__ void final_modulation_kernel(const float* __restrict__ emb, int S, in
     fmod[static_cast<long long>(s) * 2 * C + C + c] = emb[i] + table[C + c];
 }
 
+template <class TO>
 __global__ void patch_tokens_kernel(const float* __restrict__ lat, int images, int seqs, int Cl, int HW,
-                                    float* __restrict__ out) {
+                                    TO* __restrict__ out) {
     const long long total = static_cast<long long>(seqs) * HW * Cl;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -207,13 +208,14 @@ __global__ void patch_tokens_kernel(const float* __restrict__ lat, int images, i
         const int t = static_cast<int>(r % HW);
         const int s = static_cast<int>(r / HW);
         const int img = s % images;
-        out[i] = lat[(static_cast<long long>(img) * Cl + c) * HW + t];
+        out[i] = from_f<TO>(lat[(static_cast<long long>(img) * Cl + c) * HW + t]);
     }
 }
 
-__global__ void broadcast_rows_kernel(const float* __restrict__ row, int S, int width, float* __restrict__ out) {
+template <class TO>
+__global__ void broadcast_rows_kernel(const float* __restrict__ row, int S, int width, TO* __restrict__ out) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < S * width) out[i] = row[i % width];
+    if (i < S * width) out[i] = from_f<TO>(row[i % width]);
 }
 
 __global__ void kv_len_kernel(const float* __restrict__ bias, int S, int L, int* __restrict__ kv_len) {
@@ -390,16 +392,23 @@ void final_modulation(const float* emb, int S, int C, const float* table, float*
     SANA_CUDA(cudaGetLastError());
 }
 
-void patch_tokens(const float* lat, int images, int seqs, int Cl, int HW, float* out, cudaStream_t st) {
+template <class TO>
+void patch_tokens(const float* lat, int images, int seqs, int Cl, int HW, TO* out, cudaStream_t st) {
     const long long n = static_cast<long long>(seqs) * HW * Cl;
-    patch_tokens_kernel<<<grid_for(n, 256), 256, 0, st>>>(lat, images, seqs, Cl, HW, out);
+    patch_tokens_kernel<TO><<<grid_for(n, 256), 256, 0, st>>>(lat, images, seqs, Cl, HW, out);
     SANA_CUDA(cudaGetLastError());
 }
 
-void broadcast_rows(const float* row, int S, int width, float* out, cudaStream_t st) {
-    broadcast_rows_kernel<<<ceil_div(static_cast<long long>(S) * width, 256), 256, 0, st>>>(row, S, width, out);
+template <class TO>
+void broadcast_rows(const float* row, int S, int width, TO* out, cudaStream_t st) {
+    broadcast_rows_kernel<TO><<<ceil_div(static_cast<long long>(S) * width, 256), 256, 0, st>>>(row, S, width, out);
     SANA_CUDA(cudaGetLastError());
 }
+
+template void patch_tokens<float>(const float*, int, int, int, int, float*, cudaStream_t);
+template void patch_tokens<bf16>(const float*, int, int, int, int, bf16*, cudaStream_t);
+template void broadcast_rows<float>(const float*, int, int, float*, cudaStream_t);
+template void broadcast_rows<bf16>(const float*, int, int, bf16*, cudaStream_t);
 
 void caption_kv_len(const float* bias, int S, int L, int* kv_len, cudaStream_t st) {
     kv_len_kernel<<<S, 256, 0, st>>>(bias, S, L, kv_len);
