@@ -27,21 +27,25 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 
 // Residual chunks in flight per epilogue warp, and the bytes of one (32 rows x 16 fp32).
-constexpr int kRing = 4;
+constexpr int kRing = 3;
 constexpr int kRingChunk = 32 * 16 * 4;
 constexpr int kEpiWarpsCfg = 8;
+constexpr int kEpiStageBytes = 32 * 64;  // one staging buffer: 32 rows x 64 bytes
 
-// Shared-memory layout of a CTA: [A stages][B stages][epilogue staging (8 x 2 KB)]
-// [residual ring (8 warps x kRing x 2 KB, residual epilogues only)][barriers][tmem slot].
-// Residual epilogues are HBM-bound, so they trade pipeline stages for the residual ring.
-template <int kStagesV, int kABytesV, int kBBytesV, bool kResid>
+// Shared-memory layout of a CTA: [A stages][B stages][epilogue staging (8 warps x kStoreBufs
+// x 2 KB)][residual ring (8 warps x kRing x 2 KB, residual epilogues only)][barriers][tmem
+// slot]. Residual epilogues are HBM-bound, so they trade pipeline stages for the residual
+// ring and for several staging buffers per warp, which their TMA stores drain
+// asynchronously.
+template <int kStagesV, int kABytesV, int kBBytesV, bool kResid, int kStoreBufsV = 1>
 struct Layout {
     static constexpr int kStages = kStagesV;
     static constexpr int kABytes = kABytesV;
     static constexpr int kBBytes = kBBytesV;
+    static constexpr int kStoreBufs = kStoreBufsV;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kEpiOffset = kStages * kStageBytes;
-    static constexpr int kRingOffset = kEpiOffset + kEpiWarpsCfg * 32 * 64;
+    static constexpr int kRingOffset = kEpiOffset + kEpiWarpsCfg * kStoreBufs * kEpiStageBytes;
     static constexpr int kRingBytes = kResid ? kEpiWarpsCfg * kRing * kRingChunk : 0;
     static constexpr int kBarOffset = kRingOffset + kRingBytes;
     static constexpr int kBars = 2 * kStages + 5 + (kResid ? kEpiWarpsCfg * kRing : 0);
@@ -51,7 +55,7 @@ struct Layout {
 
 template <int BN, bool kResid = false>
 struct Cfg : Layout<kResid ? (BN == 128 ? 4 : 3) : (BN == 128 ? 6 : (BN == 192 ? 5 : 4)), BM * BK * 2, BN * BK * 2,
-                    kResid> {
+                    kResid, kResid ? (BN == 128 ? 3 : 2) : 1> {
     static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;  // power of two >= two accumulators
 };
 
@@ -104,6 +108,25 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint32_t dst
         "[%2];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
         : "memory");
+}
+
+// TMA tensor store of a staged box (bulk-group completion) and its bookkeeping. Coordinates
+// are never negative; boxes reaching past the tensor are clipped by the hardware.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(src), "r"(c0), "r"(c1)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int kPending>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kPending) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor, K-major operand in the canonical 128-byte-swizzle
@@ -243,8 +266,6 @@ __device__ __forceinline__ void compute16(const Epilogue& ep, int n0, float (&v)
 // stores them back as 8 rows x 64 bytes per instruction (full 32-byte sectors). 16-byte slot
 // k of row r sits at slot 4r + (k ^ ((r >> 1) & 3)): both the row writes and the row-group
 // reads then touch eight distinct bank groups per quarter-warp.
-constexpr int kEpiStageBytes = 32 * 64;  // per epilogue warp
-
 __device__ __forceinline__ uint32_t stage_slot(int r, int k) { return static_cast<uint32_t>(4 * r + (k ^ ((r >> 1) & 3))) * 16u; }
 
 // The lane's 64 bytes (4 x 16) into its staging row.
@@ -453,14 +474,68 @@ __device__ __forceinline__ void gate16(const Epilogue& ep, int row, int n0, floa
     }
 }
 
+// A warp's output staging for TMA stores: kBufs buffers of 32 rows x 64 bytes in the layout of
+// stage_slot (the 64-byte swizzle of the output tensor maps), used round robin. Before a
+// buffer is rewritten, lane 0 waits until the store that last read it has finished reading
+// (at most kBufs - 1 younger stores pending); every lane fences its writes to the async
+// proxy, and lane 0 issues the store of the box at (x, y).
+template <int kBufs>
+struct TmaStage {
+    uint8_t* buf;    // buffer 0, generic address
+    uint32_t buf_s;  // buffer 0, shared-window address
+    int issued;
+
+    __device__ __forceinline__ void put(int lane, const uint4 (&w)[4], const CUtensorMap* map, int x, int y) {
+        const int b = issued % kBufs;
+        if (lane == 0 && issued >= kBufs) bulk_wait_read<kBufs - 1>();
+        __syncwarp();
+        stage_put(buf + b * kEpiStageBytes, lane, w);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_2d(map, buf_s + static_cast<uint32_t>(b * kEpiStageBytes), x, y);
+            bulk_commit();
+        }
+        ++issued;
+    }
+    // 32 columns [n0, n0+32) of the warp's rows to an fp32 (two boxes) or bf16 (one) output.
+    __device__ __forceinline__ void put32(int lane, const CUtensorMap* map, int is_bf16, int row0, int n0,
+                                          const float (&v0)[16], const float (&v1)[16]) {
+        if (is_bf16) {
+            uint4 w[4];
+            pack_bf16x16(v0, *reinterpret_cast<uint4(*)[2]>(&w[0]));
+            pack_bf16x16(v1, *reinterpret_cast<uint4(*)[2]>(&w[2]));
+            put(lane, w, map, n0, row0);
+        } else {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float(&v)[16] = h ? v1 : v0;
+                uint4 w[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    w[k] = make_uint4(__float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]),
+                                      __float_as_uint(v[4 * k + 2]), __float_as_uint(v[4 * k + 3]));
+                put(lane, w, map, n0 + 16 * h, row0);
+            }
+        }
+    }
+    // Lane 0: every store issued has completed (before the warp's shared memory goes away).
+    __device__ __forceinline__ void finish(int lane) {
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
+    }
+};
+
 // One epilogue warp's share of a tile: rows row0 .. row0+31 (lane = row - row0, the warp's
 // TMEM lane quarter) and kCols columns from n_start, read from TMEM at t_addr. TMEM loads go
 // out two 16-column chunks at a time (one wait per 32 columns). Residual epilogues take each
 // chunk's residual from the warp's TMA ring. Batches of 32 columns inside N with aligned
-// operands store through the staging block `stg`; the rest go element by element.
-template <int kCols, bool kResid>
+// operands store through the staging block `stg` (residual epilogues: as TMA stores through
+// `ts`, maps mo / mo2); the rest go element by element.
+template <int kCols, bool kResid, int kBufs>
 __device__ __forceinline__ void epilogue_span(const Epilogue& ep, int row0, int M, int n_start, int N, bool vec,
-                                              uint32_t t_addr, uint8_t* stg, ResidRing* ring) {
+                                              uint32_t t_addr, uint8_t* stg, ResidRing* ring, TmaStage<kBufs>* ts,
+                                              const CUtensorMap* mo, const CUtensorMap* mo2) {
     constexpr int kChunks = kCols / 16;
     static_assert(kChunks % 2 == 0, "chunks go out in pairs");
     const int lane = threadIdx.x & 31;
@@ -489,7 +564,10 @@ __device__ __forceinline__ void epilogue_span(const Epilogue& ep, int row0, int 
                 if (kResid && row_ok) gate16(ep, row, n0 + 16 * g, gv);
                 compute16<kResid>(ep, n0 + 16 * g, v[g], rv[g], gv);
             }
-            if (ep.out) store32(stg, lane, ep.out, ep.out_bf16, ep.ldo, row0, M, n0, v[0], v[1]);
+            if (ep.out) {
+                if (kResid) ts->put32(lane, mo, ep.out_bf16, row0, n0, v[0], v[1]);
+                else store32(stg, lane, ep.out, ep.out_bf16, ep.ldo, row0, M, n0, v[0], v[1]);
+            }
             if (ep.out2) {
                 if (ep.act2 == kActSilu) {
 #pragma unroll
@@ -497,7 +575,8 @@ __device__ __forceinline__ void epilogue_span(const Epilogue& ep, int row0, int 
 #pragma unroll
                         for (int j = 0; j < 16; ++j) v[g][j] = silu(v[g][j]);
                 }
-                store32(stg, lane, ep.out2, ep.out2_bf16, ep.ldo2, row0, M, n0, v[0], v[1]);
+                if (kResid) ts->put32(lane, mo2, ep.out2_bf16, row0, n0, v[0], v[1]);
+                else store32(stg, lane, ep.out2, ep.out2_bf16, ep.ldo2, row0, M, n0, v[0], v[1]);
             }
             continue;
         }
@@ -531,7 +610,8 @@ constexpr int kThreads = 32 * (2 + kEpiWarps);
 template <int BN, bool kResid>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmR, int M, int N, int K, Epilogue ep, int vec, int* err) {
+                   const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmO,
+                   const __grid_constant__ CUtensorMap tmO2, int M, int N, int K, Epilogue ep, int vec, int* err) {
     using C = Cfg<BN, kResid>;
     constexpr int S = C::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -665,6 +745,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                        static_cast<int>(gridDim.x), num_tiles, num_n, BN, BM, q * 32, chalf * (BN / 2), BN / 2 / 16,
                        0, 0, err};
         if (kResid && lane == 0) ring.refill();
+        uint8_t* stg = gbase + C::kEpiOffset + ew * C::kStoreBufs * kEpiStageBytes;
+        TmaStage<C::kStoreBufs> ts{stg, base + static_cast<uint32_t>(C::kEpiOffset + ew * C::kStoreBufs * kEpiStageBytes),
+                                   0};
         int local = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const int acc = local & 1;
@@ -676,12 +759,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int col0 = chalf * (BN / 2);
             const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + col0);
-            epilogue_span<BN / 2, kResid>(ep, m_blk * BM + q * 32, M, n_blk * BN + col0, N, vec != 0, t_row,
-                                          gbase + C::kEpiOffset + ew * kEpiStageBytes, &ring);
+            epilogue_span<BN / 2, kResid, C::kStoreBufs>(ep, m_blk * BM + q * 32, M, n_blk * BN + col0, N,
+                                                         vec != 0, t_row, stg, &ring, &ts, &tmO, &tmO2);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty(acc));
         }
+        if (kResid) ts.finish(lane);
         if (kResid && lane == 0) ring.drain();
     }
 
@@ -708,7 +792,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // reaches the final cluster barrier, so neither CTA leaves while its peer uses its memory.
 template <int BN, bool kResid = false>
 struct Cfg2 : Layout<kResid ? (BN == 128 ? 5 : 4) : (BN == 128 ? 8 : (BN == 192 ? 7 : 6)), 128 * BK * 2,
-                     (BN / 2) * BK * 2, kResid> {
+                     (BN / 2) * BK * 2, kResid, kResid ? 3 : 1> {
     static constexpr int kBH = BN / 2;  // B rows per CTA
     static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
 };
@@ -716,7 +800,8 @@ struct Cfg2 : Layout<kResid ? (BN == 128 ? 5 : 4) : (BN == 128 ? 8 : (BN == 192 
 template <int BN, bool kResid>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmR, int M, int N, int K, Epilogue ep, int vec, int* err) {
+                    const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmO,
+                    const __grid_constant__ CUtensorMap tmO2, int M, int N, int K, Epilogue ep, int vec, int* err) {
     using C = Cfg2<BN, kResid>;
     constexpr int S = C::kStages;
     constexpr int BM2 = 2 * BM;
@@ -863,6 +948,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                        ring_bars + 8u * static_cast<uint32_t>(ew * kRing), pair, npairs, num_tiles, num_n, BN, BM2,
                        static_cast<int>(rank) * BM + q * 32, chalf * (BN / 2), BN / 2 / 16, 0, 0, err};
         if (kResid && lane == 0) ring.refill();
+        uint8_t* stg = gbase + C::kEpiOffset + ew * C::kStoreBufs * kEpiStageBytes;
+        TmaStage<C::kStoreBufs> ts{stg, base + static_cast<uint32_t>(C::kEpiOffset + ew * C::kStoreBufs * kEpiStageBytes),
+                                   0};
         int local = 0;
         for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
             const int acc = local & 1;
@@ -874,13 +962,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int col0 = chalf * (BN / 2);
             const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + col0);
-            epilogue_span<BN / 2, kResid>(ep, m_blk * BM2 + static_cast<int>(rank) * BM + q * 32, M,
-                                          n_blk * BN + col0, N, vec != 0, t_row,
-                                          gbase + C::kEpiOffset + ew * kEpiStageBytes, &ring);
+            epilogue_span<BN / 2, kResid, C::kStoreBufs>(ep, m_blk * BM2 + static_cast<int>(rank) * BM + q * 32, M,
+                                                         n_blk * BN + col0, N, vec != 0, t_row, stg, &ring, &ts,
+                                                         &tmO, &tmO2);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * acc);
         }
+        if (kResid) ts.finish(lane);
         if (kResid && lane == 0) ring.drain();
     }
 
@@ -917,6 +1006,18 @@ static CUtensorMap resid_map(const GemmProblem& p) {
     return m;
 }
 
+// Output tensor map for the residual epilogues' TMA stores: [M, N] fp32 or bf16 with row
+// stride ld elements, box = 32 rows x 64 bytes, 64-byte swizzle (the staging layout).
+static CUtensorMap out_map(void* ptr, int is_bf16, long long ld, int M, int N) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * (is_bf16 ? 2 : 4)};
+    const cuuint32_t box[2] = {is_bf16 ? 32u : 16u, 32};
+    tma_encode_tiled(&m, is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims,
+                     strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+    return m;
+}
+
 template <int BN, bool kResid>
 static void launch(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
     using C = Cfg<BN, kResid>;
@@ -937,9 +1038,13 @@ static void launch(const GemmProblem& p, int* err, cudaStream_t stream, int num_
     if (e.gate) vec = vec && a16(e.gate) && (e.gate_ld % 4 == 0);
     if (e.out) vec = vec && a16(e.out) && (e.ldo % 8 == 0);
     if (e.out2) vec = vec && a16(e.out2) && (e.ldo2 % 8 == 0);
+    // the residual epilogue's TMA stores need what `vec` already requires of the outputs
+    const CUtensorMap mo = kResid && vec && e.out ? out_map(e.out, e.out_bf16, e.ldo, p.M, p.N) : ma;
+    const CUtensorMap mo2 = kResid && vec && e.out2 ? out_map(e.out2, e.out2_bf16, e.ldo2, p.M, p.N) : ma;
     const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    gemm_tc_kernel<BN, kResid><<<grid, kThreads, C::kSmemBytes, stream>>>(ma, mb, mr, p.M, p.N, p.K, e, vec ? 1 : 0, err);
+    gemm_tc_kernel<BN, kResid><<<grid, kThreads, C::kSmemBytes, stream>>>(ma, mb, mr, mo, mo2, p.M, p.N, p.K, e,
+                                                                          vec ? 1 : 0, err);
     SANA_CUDA(cudaGetLastError());
 }
 
@@ -963,9 +1068,11 @@ static void launch2(const GemmProblem& p, int* err, cudaStream_t stream, int num
     if (e.gate) vec = vec && a16(e.gate) && (e.gate_ld % 4 == 0);
     if (e.out) vec = vec && a16(e.out) && (e.ldo % 8 == 0);
     if (e.out2) vec = vec && a16(e.out2) && (e.ldo2 % 8 == 0);
+    const CUtensorMap mo = kResid && vec && e.out ? out_map(e.out, e.out_bf16, e.ldo, p.M, p.N) : ma;
+    const CUtensorMap mo2 = kResid && vec && e.out2 ? out_map(e.out2, e.out2_bf16, e.ldo2, p.M, p.N) : ma;
     const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + BN - 1) / BN);
     const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
-    gemm_tc2_kernel<BN, kResid><<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(ma, mb, mr, p.M, p.N, p.K, e,
+    gemm_tc2_kernel<BN, kResid><<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(ma, mb, mr, mo, mo2, p.M, p.N, p.K, e,
                                                                                  vec ? 1 : 0, err);
     SANA_CUDA(cudaGetLastError());
 }

@@ -194,6 +194,41 @@ def test_ln_modulate_device(gpu_bf16, rows, C, rps):
     assert (err <= bound).all(), float((err / bound).max())
 
 
+@pytest.mark.parametrize("M,N,K,rpg,copy", [(4096 + 96, 1152, 1152, 1024, True), (3000, 1152, 2880, 700, False),
+                                             (1000, 384, 128, 300, True), (2304, 200, 64, 2304, True)])
+def test_gemm_residual_epilogue(gpu_bf16, M, N, K, rpg, copy):
+    """out = resid + gate[row / rows_per_gate] * (A B^T + bias) with an optional bf16 copy (the
+    out-projection, cross-out and FF-point epilogues): CTA-pair and single-CTA kernels, ragged
+    row and column tiles, TMA-stored and element-wise column batches, against float64 of the
+    same bf16 operands."""
+    import ctypes
+
+    import torch
+    rng = np.random.default_rng(M + N + K)
+    a = bf16_round(rng.standard_normal((M, K)).astype(np.float32))
+    w = bf16_round((rng.standard_normal((N, K)) * 0.05).astype(np.float32))
+    b = rng.standard_normal(N).astype(np.float32)
+    r = rng.standard_normal((M, N)).astype(np.float32)
+    g = rng.standard_normal((-(-M // rpg), N)).astype(np.float32)
+    ref = r + g[np.arange(M) // rpg] * (a.astype(np.float64) @ w.astype(np.float64).T + b)
+    A, B = torch.from_numpy(a).to("cuda", torch.bfloat16), torch.from_numpy(w).to("cuda", torch.bfloat16)
+    bt, rt, gt = (torch.from_numpy(x).cuda() for x in (b, r, g))
+    out = torch.empty(M, N, device="cuda")
+    out2 = torch.empty(M, N, device="cuda", dtype=torch.bfloat16) if copy else None
+    torch.cuda.synchronize()
+    vp = ctypes.c_void_p
+    gpu_bf16._call("sana_op_gemm_residual_device", vp(A.data_ptr()), vp(B.data_ptr()), ctypes.c_int(M),
+                   ctypes.c_int(N), ctypes.c_int(K), vp(bt.data_ptr()), vp(rt.data_ptr()), vp(gt.data_ptr()),
+                   ctypes.c_int(rpg), vp(out.data_ptr()), vp(out2.data_ptr()) if copy else None)
+    gpu_bf16.synchronize()
+    got = out.cpu().numpy().astype(np.float64)
+    scale = np.abs(g[np.arange(M) // rpg]) * (np.abs(a) @ np.abs(w).T + np.abs(b))
+    assert (np.abs(got - ref) <= 1e-5 * scale + 1e-5 * np.abs(ref) + 1e-6).all()
+    if copy:
+        got2 = out2.float().cpu().numpy().astype(np.float64)
+        assert (np.abs(got2 - got) <= 2.0 ** -8 * np.abs(got) + 1e-30).all()
+
+
 def test_gemm_repeatable(gpu_bf16):
     rng = np.random.default_rng(5)
     x = rng.standard_normal((1024, 1152)).astype(np.float32)
