@@ -31,12 +31,13 @@ constexpr int kRing = 3;
 constexpr int kRingChunk = 32 * 16 * 4;
 constexpr int kEpiWarpsCfg = 8;
 constexpr int kEpiStageBytes = 32 * 64;  // one staging buffer: 32 rows x 64 bytes
+constexpr int kSideWarpBytes = 2 * 128 * 4;  // bias and gate of a warp's (at most 128) columns
 
 // Shared-memory layout of a CTA: [A stages][B stages][epilogue staging (8 warps x kStoreBufs
-// x 2 KB)][residual ring (8 warps x kRing x 2 KB, residual epilogues only)][barriers][tmem
-// slot]. Residual epilogues are HBM-bound, so they trade pipeline stages for the residual
-// ring and for several staging buffers per warp, which their TMA stores drain
-// asynchronously.
+// x 2 KB)][residual ring (8 warps x kRing x 2 KB) and side vectors (8 warps x 1 KB), residual
+// epilogues only][barriers][tmem slot]. Residual epilogues are HBM-bound, so they trade
+// pipeline stages for the residual ring and for staging buffers, which their TMA stores
+// drain asynchronously.
 template <int kStagesV, int kABytesV, int kBBytesV, bool kResid, int kStoreBufsV = 1>
 struct Layout {
     static constexpr int kStages = kStagesV;
@@ -47,7 +48,9 @@ struct Layout {
     static constexpr int kEpiOffset = kStages * kStageBytes;
     static constexpr int kRingOffset = kEpiOffset + kEpiWarpsCfg * kStoreBufs * kEpiStageBytes;
     static constexpr int kRingBytes = kResid ? kEpiWarpsCfg * kRing * kRingChunk : 0;
-    static constexpr int kBarOffset = kRingOffset + kRingBytes;
+    static constexpr int kSideOffset = kRingOffset + kRingBytes;  // per warp: its span's bias and gate row
+    static constexpr int kSideBytes = kResid ? kEpiWarpsCfg * kSideWarpBytes : 0;
+    static constexpr int kBarOffset = kSideOffset + kSideBytes;
     static constexpr int kBars = 2 * kStages + 5 + (kResid ? kEpiWarpsCfg * kRing : 0);
     static constexpr int kSmemBytes = kBarOffset + kBars * 8 + 16 + 1024;
     static_assert(kSmemBytes <= 232448, "shared memory of one CTA");
@@ -55,7 +58,7 @@ struct Layout {
 
 template <int BN, bool kResid = false>
 struct Cfg : Layout<kResid ? (BN == 128 ? 4 : 3) : (BN == 128 ? 6 : (BN == 192 ? 5 : 4)), BM * BK * 2, BN * BK * 2,
-                    kResid, kResid ? (BN == 128 ? 3 : 2) : 1> {
+                    kResid, kResid ? (BN == 128 ? 2 : 1) : 1> {
     static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;  // power of two >= two accumulators
 };
 
@@ -231,17 +234,11 @@ struct Side16 {
 // Bias, activation and gated residual on 16 consecutive columns [n0, n0+16) of one row,
 // all of them in range (the fast path); the stores are the caller's.
 template <bool kResid>
-__device__ __forceinline__ void compute16(const Epilogue& ep, int n0, float (&v)[16], const float (&rv)[16],
-                                          const float (&gv)[16]) {
+__device__ __forceinline__ void compute16(const Epilogue& ep, const float (&bv)[16], float (&v)[16],
+                                          const float (&rv)[16], const float (&gv)[16]) {
     if (ep.bias) {
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-            const float4 b = *reinterpret_cast<const float4*>(ep.bias + n0 + j);
-            v[j] += b.x;
-            v[j + 1] += b.y;
-            v[j + 2] += b.z;
-            v[j + 3] += b.w;
-        }
+        for (int j = 0; j < 16; ++j) v[j] += bv[j];
     }
     if (ep.act == kActSilu) {
 #pragma unroll
@@ -411,23 +408,32 @@ struct ResidRing {
     int first, stride, num_tiles, num_n, bn, tile_rows, row_off, col0, kchunks;
     int issued, used;
     int* err;
+    // the next chunk to issue: its tile, its index in the span, the span's origin in that tile
+    int it_tile = 0, it_chunk = 0, it_x = 0, it_y = 0;
 
-    __device__ bool coords(int j, int& x, int& y) const {
-        const int tile = first + (j / kchunks) * stride;
-        if (tile >= num_tiles) return false;
-        x = (tile % num_n) * bn + col0 + 16 * (j % kchunks);
-        y = (tile / num_n) * tile_rows + row_off;
-        return true;
+    __device__ void set_tile() {
+        it_x = (it_tile % num_n) * bn + col0;
+        it_y = (it_tile / num_n) * tile_rows + row_off;
+    }
+    // Lane 0: positions the cursor on the first chunk and fills the ring.
+    __device__ void start() {
+        it_tile = first;
+        it_chunk = 0;
+        if (it_tile < num_tiles) set_tile();
+        refill();
     }
     // Lane 0: keeps the ring full.
     __device__ void refill() {
-        while (issued < used + kRing) {
-            int x, y;
-            if (!coords(issued, x, y)) break;
+        while (issued < used + kRing && it_tile < num_tiles) {
             const uint32_t s = static_cast<uint32_t>(issued % kRing);
             mbar_arrive_expect_tx(bar + 8u * s, kRingChunk);
-            tma_load_2d(map, buf_s + s * kRingChunk, bar + 8u * s, x, y);
+            tma_load_2d(map, buf_s + s * kRingChunk, bar + 8u * s, it_x + 16 * it_chunk, it_y);
             ++issued;
+            if (++it_chunk == kchunks) {
+                it_chunk = 0;
+                it_tile += stride;
+                if (it_tile < num_tiles) set_tile();
+            }
         }
     }
     // Every lane: its row of the next chunk. A wait that gives up has recorded the error.
@@ -506,6 +512,29 @@ struct TmaStage {
             pack_bf16x16(v0, *reinterpret_cast<uint4(*)[2]>(&w[0]));
             pack_bf16x16(v1, *reinterpret_cast<uint4(*)[2]>(&w[2]));
             put(lane, w, map, n0, row0);
+        } else if (kBufs >= 2) {  // both boxes staged behind one wait and one fence
+            const int b0 = issued % kBufs, b1 = (issued + 1) % kBufs;
+            if (lane == 0 && issued + 2 > kBufs) bulk_wait_read<(kBufs >= 2 ? kBufs - 2 : 0)>();
+            __syncwarp();
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float(&v)[16] = h ? v1 : v0;
+                uint4 w[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    w[k] = make_uint4(__float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]),
+                                      __float_as_uint(v[4 * k + 2]), __float_as_uint(v[4 * k + 3]));
+                stage_put(buf + (h ? b1 : b0) * kEpiStageBytes, lane, w);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(map, buf_s + static_cast<uint32_t>(b0 * kEpiStageBytes), n0, row0);
+                bulk_commit();
+                tma_store_2d(map, buf_s + static_cast<uint32_t>(b1 * kEpiStageBytes), n0 + 16, row0);
+                bulk_commit();
+            }
+            issued += 2;
         } else {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -531,16 +560,33 @@ struct TmaStage {
 // out two 16-column chunks at a time (one wait per 32 columns). Residual epilogues take each
 // chunk's residual from the warp's TMA ring. Batches of 32 columns inside N with aligned
 // operands store through the staging block `stg` (residual epilogues: as TMA stores through
-// `ts`, maps mo / mo2); the rest go element by element.
+// `ts`, maps mo / mo2, reading the span's bias and, when the warp's rows share one, its gate
+// row from `side`, which the warp fills once per tile); the rest go element by element.
 template <int kCols, bool kResid, int kBufs>
 __device__ __forceinline__ void epilogue_span(const Epilogue& ep, int row0, int M, int n_start, int N, bool vec,
                                               uint32_t t_addr, uint8_t* stg, ResidRing* ring, TmaStage<kBufs>* ts,
-                                              const CUtensorMap* mo, const CUtensorMap* mo2) {
+                                              const CUtensorMap* mo, const CUtensorMap* mo2, float* side) {
     constexpr int kChunks = kCols / 16;
     static_assert(kChunks % 2 == 0, "chunks go out in pairs");
+    static_assert(kCols <= 128, "side vectors hold 128 columns");
     const int lane = threadIdx.x & 31;
     const int row = row0 + lane;
     const bool row_ok = row < M;
+    bool side_gate = false;
+    if (kResid && vec) {
+        constexpr int kPer = kCols / 32;
+        const int c0 = n_start + kPer * lane;
+        const int g0 = row0 / ep.rows_per_gate;
+        side_gate = ep.gate != nullptr && g0 == (min(row0 + 31, M - 1) / ep.rows_per_gate);
+        const float* grow = side_gate ? ep.gate + static_cast<long long>(g0) * ep.gate_ld : nullptr;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const bool in = c0 + k < N;
+            side[kPer * lane + k] = ep.bias && in ? ep.bias[c0 + k] : 0.f;
+            side[128 + kPer * lane + k] = grow && in ? grow[c0 + k] : 1.f;
+        }
+        __syncwarp();
+    }
 #pragma unroll 1
     for (int c = 0; c < kChunks; c += 2) {
         uint32_t r[2][16];
@@ -560,9 +606,31 @@ __device__ __forceinline__ void epilogue_span(const Epilogue& ep, int row0, int 
             for (int g = 0; g < 2; ++g) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[g][j] = __uint_as_float(r[g][j]);
-                float gv[16];
-                if (kResid && row_ok) gate16(ep, row, n0 + 16 * g, gv);
-                compute16<kResid>(ep, n0 + 16 * g, v[g], rv[g], gv);
+                float gv[16], bv[16];
+                if (kResid) {
+                    const float* sb = side + (n0 - n_start) + 16 * g;
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4) {
+                        const float4 b4 = *reinterpret_cast<const float4*>(sb + j);
+                        bv[j] = b4.x, bv[j + 1] = b4.y, bv[j + 2] = b4.z, bv[j + 3] = b4.w;
+                    }
+                    if (side_gate) {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4) {
+                            const float4 g4 = *reinterpret_cast<const float4*>(sb + 128 + j);
+                            gv[j] = g4.x, gv[j + 1] = g4.y, gv[j + 2] = g4.z, gv[j + 3] = g4.w;
+                        }
+                    } else if (row_ok) {
+                        gate16(ep, row, n0 + 16 * g, gv);
+                    }
+                } else if (ep.bias) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4) {
+                        const float4 b4 = *reinterpret_cast<const float4*>(ep.bias + n0 + 16 * g + j);
+                        bv[j] = b4.x, bv[j + 1] = b4.y, bv[j + 2] = b4.z, bv[j + 3] = b4.w;
+                    }
+                }
+                compute16<kResid>(ep, bv, v[g], rv[g], gv);
             }
             if (ep.out) {
                 if (kResid) ts->put32(lane, mo, ep.out_bf16, row0, n0, v[0], v[1]);
@@ -744,10 +812,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                        ring_bars + 8u * static_cast<uint32_t>(ew * kRing), static_cast<int>(blockIdx.x),
                        static_cast<int>(gridDim.x), num_tiles, num_n, BN, BM, q * 32, chalf * (BN / 2), BN / 2 / 16,
                        0, 0, err};
-        if (kResid && lane == 0) ring.refill();
+        if (kResid && lane == 0) ring.start();
         uint8_t* stg = gbase + C::kEpiOffset + ew * C::kStoreBufs * kEpiStageBytes;
         TmaStage<C::kStoreBufs> ts{stg, base + static_cast<uint32_t>(C::kEpiOffset + ew * C::kStoreBufs * kEpiStageBytes),
                                    0};
+        float* side = reinterpret_cast<float*>(gbase + C::kSideOffset + ew * kSideWarpBytes);
         int local = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const int acc = local & 1;
@@ -760,7 +829,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + col0);
             epilogue_span<BN / 2, kResid, C::kStoreBufs>(ep, m_blk * BM + q * 32, M, n_blk * BN + col0, N,
-                                                         vec != 0, t_row, stg, &ring, &ts, &tmO, &tmO2);
+                                                         vec != 0, t_row, stg, &ring, &ts, &tmO, &tmO2, side);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty(acc));
@@ -792,7 +861,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // reaches the final cluster barrier, so neither CTA leaves while its peer uses its memory.
 template <int BN, bool kResid = false>
 struct Cfg2 : Layout<kResid ? (BN == 128 ? 5 : 4) : (BN == 128 ? 8 : (BN == 192 ? 7 : 6)), 128 * BK * 2,
-                     (BN / 2) * BK * 2, kResid, kResid ? 3 : 1> {
+                     (BN / 2) * BK * 2, kResid, kResid ? 2 : 1> {
     static constexpr int kBH = BN / 2;  // B rows per CTA
     static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
 };
@@ -947,10 +1016,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                        base + C::kRingOffset + static_cast<uint32_t>(ew * kRing * kRingChunk),
                        ring_bars + 8u * static_cast<uint32_t>(ew * kRing), pair, npairs, num_tiles, num_n, BN, BM2,
                        static_cast<int>(rank) * BM + q * 32, chalf * (BN / 2), BN / 2 / 16, 0, 0, err};
-        if (kResid && lane == 0) ring.refill();
+        if (kResid && lane == 0) ring.start();
         uint8_t* stg = gbase + C::kEpiOffset + ew * C::kStoreBufs * kEpiStageBytes;
         TmaStage<C::kStoreBufs> ts{stg, base + static_cast<uint32_t>(C::kEpiOffset + ew * C::kStoreBufs * kEpiStageBytes),
                                    0};
+        float* side = reinterpret_cast<float*>(gbase + C::kSideOffset + ew * kSideWarpBytes);
         int local = 0;
         for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
             const int acc = local & 1;
@@ -964,7 +1034,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                    static_cast<uint32_t>(acc * BN + col0);
             epilogue_span<BN / 2, kResid, C::kStoreBufs>(ep, m_blk * BM2 + static_cast<int>(rank) * BM + q * 32, M,
                                                          n_blk * BN + col0, N, vec != 0, t_row, stg, &ring, &ts,
-                                                         &tmO, &tmO2);
+                                                         &tmO, &tmO2, side);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * acc);
