@@ -270,7 +270,7 @@ def gemm_roofline(g, torch, stream, M, peak_tflops):
 
 MICRO_OPS = ("qkv_gemm", "linear_attention_16x72", "linear_attention_36x32", "depthwise_glu", "cross_attention",
              "ff_inverted_config2", "linear_attention_config2", "depthwise_glu_config2", "cross_attention_config2",
-             "out_proj_config2", "ln_modulate_config2")
+             "out_proj_config2", "ff_point_config2", "ln_modulate_config2")
 
 
 def run_microbench(args):
@@ -375,21 +375,23 @@ def run_microbench(args):
                                        vp(out.data_ptr())))
             byts = 4.0 * M * C + 2.0 * M * C
             report(name, f"[{M},{C}] fp32 -> bf16 ({byts / 1e6:.0f} MB)", ms, byts, "hbm")
-        elif name == "out_proj_config2":
-            # the self-attention output projection: fp32 residual + gate x (A W^T + b), bf16 copy
-            M, N, K = S * T, C, C
+        elif name in ("out_proj_config2", "ff_point_config2"):
+            # the self-attention output projection: fp32 residual + gate x (A W^T + b), bf16 copy;
+            # the FF point projection: the same from the 2880 GLU channels, no copy
+            copy = name == "out_proj_config2"
+            M, N, K = S * T, C, (C if copy else E // 2)
             A, Bw = rnd(M, K), rnd(N, K, scale=0.02)
             bias = torch.zeros(N, device="cuda")
             resid = torch.randn(M, N, generator=gen).cuda()
             gate = torch.randn(S, N, generator=gen).cuda()
             out = torch.empty(M, N, device="cuda")
-            out2 = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            out2 = torch.empty(M, N, device="cuda", dtype=torch.bfloat16) if copy else None
             ms = timed(lambda: g._call("sana_op_gemm_residual_device", vp(A.data_ptr()), vp(Bw.data_ptr()), I(M),
                                        I(N), I(K), vp(bias.data_ptr()), vp(resid.data_ptr()), vp(gate.data_ptr()),
-                                       I(T), vp(out.data_ptr()), vp(out2.data_ptr())))
-            byts = 2.0 * M * K + 2.0 * N * K + 4.0 * M * N * 2 + 2.0 * M * N
-            report(name, f"M={M} K={K} N={N}: fp32 residual read + fp32 and bf16 out ({byts / 1e6:.0f} MB)", ms, byts,
-                   "hbm")
+                                       I(T), vp(out.data_ptr()), vp(out2.data_ptr()) if copy else None))
+            byts = 2.0 * M * K + 2.0 * N * K + 4.0 * M * N * 2 + (2.0 * M * N if copy else 0.0)
+            report(name, f"M={M} K={K} N={N}: fp32 residual read + fp32{' and bf16' if copy else ''} out "
+                         f"({byts / 1e6:.0f} MB; {2.0 * M * N * K / 1e9:.0f} GFLOP)", ms, byts, "hbm")
         elif name.startswith("cross_attention"):
             heads, D = 16, 72
             q, kv = rnd(S * T, C), rnd(S * L, 2 * C)

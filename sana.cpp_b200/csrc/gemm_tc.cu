@@ -26,8 +26,8 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 
-// Residual chunks in flight per epilogue warp, and the bytes of one (32 rows x 16 fp32).
-constexpr int kRing = 3;
+// Bytes of one residual chunk (32 rows x 16 fp32); a configuration sets how many each
+// epilogue warp keeps in flight.
 constexpr int kRingChunk = 32 * 16 * 4;
 constexpr int kEpiWarpsCfg = 8;
 constexpr int kEpiStageBytes = 32 * 64;  // one staging buffer: 32 rows x 64 bytes
@@ -37,9 +37,11 @@ constexpr int kSideWarpBytes = 2 * 128 * 4;  // bias and gate of a warp's (at mo
 // x 2 KB)][residual ring (8 warps x kRing x 2 KB) and side vectors (8 warps x 1 KB), residual
 // epilogues only][barriers][tmem slot]. Residual epilogues are HBM-bound, so they trade
 // pipeline stages for the residual ring and for staging buffers, which their TMA stores
-// drain asynchronously.
-template <int kStagesV, int kABytesV, int kBBytesV, bool kResid, int kStoreBufsV = 1>
+// drain asynchronously; long-K residual products (the deep variant) keep more stages and a
+// shallower ring instead, their epilogue having time to spare.
+template <int kStagesV, int kABytesV, int kBBytesV, bool kResid, int kStoreBufsV = 1, int kRingV = 3>
 struct Layout {
+    static constexpr int kRing = kRingV;
     static constexpr int kStages = kStagesV;
     static constexpr int kABytes = kABytesV;
     static constexpr int kBBytes = kBBytesV;
@@ -47,11 +49,11 @@ struct Layout {
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kEpiOffset = kStages * kStageBytes;
     static constexpr int kRingOffset = kEpiOffset + kEpiWarpsCfg * kStoreBufs * kEpiStageBytes;
-    static constexpr int kRingBytes = kResid ? kEpiWarpsCfg * kRing * kRingChunk : 0;
+    static constexpr int kRingBytes = kResid ? kEpiWarpsCfg * kRingV * kRingChunk : 0;
     static constexpr int kSideOffset = kRingOffset + kRingBytes;  // per warp: its span's bias and gate row
     static constexpr int kSideBytes = kResid ? kEpiWarpsCfg * kSideWarpBytes : 0;
     static constexpr int kBarOffset = kSideOffset + kSideBytes;
-    static constexpr int kBars = 2 * kStages + 5 + (kResid ? kEpiWarpsCfg * kRing : 0);
+    static constexpr int kBars = 2 * kStages + 5 + (kResid ? kEpiWarpsCfg * kRingV : 0);
     static constexpr int kSmemBytes = kBarOffset + kBars * 8 + 16 + 1024;
     static_assert(kSmemBytes <= 232448, "shared memory of one CTA");
 };
@@ -398,7 +400,7 @@ __device__ __forceinline__ void epilogue16(const Epilogue& ep, int row, int n0, 
 
 // The residual chunks an epilogue warp will need, in the order it needs them: chunk j is the
 // warp's 32 rows x 16 fp32 columns number j % kchunks of its span of the (j / kchunks)-th
-// tile it processes. Lane 0 keeps kRing chunks in flight with TMA (64-byte swizzle: 16-byte
+// tile it processes. Lane 0 keeps `depth` chunks in flight with TMA (64-byte swizzle: 16-byte
 // slot k of row r lands at stage_slot(r, k), so each lane reads its own row without bank
 // conflicts); every lane takes the chunks in order. Boxes past M or N read as zeros.
 struct ResidRing {
@@ -410,6 +412,7 @@ struct ResidRing {
     int* err;
     // the next chunk to issue: its tile, its index in the span, the span's origin in that tile
     int it_tile = 0, it_chunk = 0, it_x = 0, it_y = 0;
+    int depth = 3;  // chunks in flight
 
     __device__ void set_tile() {
         it_x = (it_tile % num_n) * bn + col0;
@@ -424,8 +427,8 @@ struct ResidRing {
     }
     // Lane 0: keeps the ring full.
     __device__ void refill() {
-        while (issued < used + kRing && it_tile < num_tiles) {
-            const uint32_t s = static_cast<uint32_t>(issued % kRing);
+        while (issued < used + depth && it_tile < num_tiles) {
+            const uint32_t s = static_cast<uint32_t>(issued % depth);
             mbar_arrive_expect_tx(bar + 8u * s, kRingChunk);
             tma_load_2d(map, buf_s + s * kRingChunk, bar + 8u * s, it_x + 16 * it_chunk, it_y);
             ++issued;
@@ -439,8 +442,8 @@ struct ResidRing {
     // Every lane: its row of the next chunk. A wait that gives up has recorded the error.
     __device__ void take(float (&rv)[16]) {
         const int lane = threadIdx.x & 31;
-        const uint32_t s = static_cast<uint32_t>(used % kRing);
-        if (mbar_wait(bar + 8u * s, static_cast<uint32_t>((used / kRing) & 1), err, kTimeout)) {
+        const uint32_t s = static_cast<uint32_t>(used % depth);
+        if (mbar_wait(bar + 8u * s, static_cast<uint32_t>((used / depth) & 1), err, kTimeout)) {
             const uint8_t* b = buf + s * kRingChunk;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -458,7 +461,7 @@ struct ResidRing {
     // Lane 0: waits (bounded) for chunks issued and never taken, so no copy lands after exit.
     __device__ void drain() {
         for (int j = used; j < issued; ++j)
-            mbar_wait_quiet(bar + 8u * static_cast<uint32_t>(j % kRing), static_cast<uint32_t>((j / kRing) & 1));
+            mbar_wait_quiet(bar + 8u * static_cast<uint32_t>(j % depth), static_cast<uint32_t>((j / depth) & 1));
     }
 };
 
@@ -695,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto tempty = [&](int a) { return bars + 8u * (2 * S + 2 + a); };
     const uint32_t done_bar = bars + 8u * (2 * S + 4);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kBarOffset + C::kBars * 8);
-    const uint32_t ring_bars = bars + 8u * (2 * S + 5);  // kEpiWarps x kRing, residual epilogues
+    const uint32_t ring_bars = bars + 8u * (2 * S + 5);  // kEpiWarps x C::kRing, residual epilogues
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -715,7 +718,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(done_bar, 1);
         if (kResid)
-            for (int i = 0; i < kEpiWarps * kRing; ++i) mbar_init(ring_bars + 8u * i, 1);
+            for (int i = 0; i < kEpiWarps * C::kRing; ++i) mbar_init(ring_bars + 8u * i, 1);
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -807,11 +810,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3;                   // TMEM lane quarter this warp may access
         const int chalf = (warp - 2) / 4;         // which half of the tile's columns
         const int ew = warp - 2;
-        ResidRing ring{&tmR, gbase + C::kRingOffset + ew * kRing * kRingChunk,
-                       base + C::kRingOffset + static_cast<uint32_t>(ew * kRing * kRingChunk),
-                       ring_bars + 8u * static_cast<uint32_t>(ew * kRing), static_cast<int>(blockIdx.x),
+        ResidRing ring{&tmR, gbase + C::kRingOffset + ew * C::kRing * kRingChunk,
+                       base + C::kRingOffset + static_cast<uint32_t>(ew * C::kRing * kRingChunk),
+                       ring_bars + 8u * static_cast<uint32_t>(ew * C::kRing), static_cast<int>(blockIdx.x),
                        static_cast<int>(gridDim.x), num_tiles, num_n, BN, BM, q * 32, chalf * (BN / 2), BN / 2 / 16,
                        0, 0, err};
+        ring.depth = C::kRing;
         if (kResid && lane == 0) ring.start();
         uint8_t* stg = gbase + C::kEpiOffset + ew * C::kStoreBufs * kEpiStageBytes;
         TmaStage<C::kStoreBufs> ts{stg, base + static_cast<uint32_t>(C::kEpiOffset + ew * C::kStoreBufs * kEpiStageBytes),
@@ -859,19 +863,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   tempty[a]  leader only: one arrival per epilogue warp of either CTA
 // Every wait is bounded; on expiry each role stops issuing work and every thread still
 // reaches the final cluster barrier, so neither CTA leaves while its peer uses its memory.
-template <int BN, bool kResid = false>
-struct Cfg2 : Layout<kResid ? (BN == 128 ? 5 : 4) : (BN == 128 ? 8 : (BN == 192 ? 7 : 6)), 128 * BK * 2,
-                     (BN / 2) * BK * 2, kResid, kResid ? 2 : 1> {
+template <int BN, bool kResid = false, bool kDeep = false>
+struct Cfg2 : Layout<kResid ? (kDeep ? (BN == 128 ? 7 : 5) : (BN == 128 ? 5 : 4))
+                            : (BN == 128 ? 8 : (BN == 192 ? 7 : 6)),
+                     128 * BK * 2, (BN / 2) * BK * 2, kResid, kResid && !kDeep ? 2 : 1, kDeep ? 2 : 3> {
     static constexpr int kBH = BN / 2;  // B rows per CTA
     static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
 };
 
-template <int BN, bool kResid>
+template <int BN, bool kResid, bool kDeep>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmO,
                     const __grid_constant__ CUtensorMap tmO2, int M, int N, int K, Epilogue ep, int vec, int* err) {
-    using C = Cfg2<BN, kResid>;
+    using C = Cfg2<BN, kResid, kDeep>;
     constexpr int S = C::kStages;
     constexpr int BM2 = 2 * BM;
     extern __shared__ uint8_t smem_raw[];
@@ -887,7 +892,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     auto tempty = [&](int a) { return bars + 8u * (2 * S + 2 + a); };
     const uint32_t done_bar = bars + 8u * (2 * S + 4);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::kBarOffset + C::kBars * 8);
-    const uint32_t ring_bars = bars + 8u * (2 * S + 5);  // kEpiWarps x kRing, residual epilogues
+    const uint32_t ring_bars = bars + 8u * (2 * S + 5);  // kEpiWarps x C::kRing, residual epilogues
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -911,7 +916,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         mbar_init(done_bar, 1);
         if (kResid)
-            for (int i = 0; i < kEpiWarps * kRing; ++i) mbar_init(ring_bars + 8u * i, 1);
+            for (int i = 0; i < kEpiWarps * C::kRing; ++i) mbar_init(ring_bars + 8u * i, 1);
         fence_barrier_init();
     }
     cluster_sync();  // barriers of both CTAs initialised before any remote arrival
@@ -1012,10 +1017,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int q = warp & 3;
         const int chalf = (warp - 2) / 4;
         const int ew = warp - 2;
-        ResidRing ring{&tmR, gbase + C::kRingOffset + ew * kRing * kRingChunk,
-                       base + C::kRingOffset + static_cast<uint32_t>(ew * kRing * kRingChunk),
-                       ring_bars + 8u * static_cast<uint32_t>(ew * kRing), pair, npairs, num_tiles, num_n, BN, BM2,
+        ResidRing ring{&tmR, gbase + C::kRingOffset + ew * C::kRing * kRingChunk,
+                       base + C::kRingOffset + static_cast<uint32_t>(ew * C::kRing * kRingChunk),
+                       ring_bars + 8u * static_cast<uint32_t>(ew * C::kRing), pair, npairs, num_tiles, num_n, BN, BM2,
                        static_cast<int>(rank) * BM + q * 32, chalf * (BN / 2), BN / 2 / 16, 0, 0, err};
+        ring.depth = C::kRing;
         if (kResid && lane == 0) ring.start();
         uint8_t* stg = gbase + C::kEpiOffset + ew * C::kStoreBufs * kEpiStageBytes;
         TmaStage<C::kStoreBufs> ts{stg, base + static_cast<uint32_t>(C::kEpiOffset + ew * C::kStoreBufs * kEpiStageBytes),
@@ -1118,12 +1124,12 @@ static void launch(const GemmProblem& p, int* err, cudaStream_t stream, int num_
     SANA_CUDA(cudaGetLastError());
 }
 
-template <int BN, bool kResid>
+template <int BN, bool kResid, bool kDeep = false>
 static void launch2(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
-    using C = Cfg2<BN, kResid>;
+    using C = Cfg2<BN, kResid, kDeep>;
     static bool attr_done = false;
     if (!attr_done) {
-        SANA_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<BN, kResid>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        SANA_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<BN, kResid, kDeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::kSmemBytes));
         attr_done = true;
     }
@@ -1142,8 +1148,8 @@ static void launch2(const GemmProblem& p, int* err, cudaStream_t stream, int num
     const CUtensorMap mo2 = kResid && vec && e.out2 ? out_map(e.out2, e.out2_bf16, e.ldo2, p.M, p.N) : ma;
     const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + BN - 1) / BN);
     const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
-    gemm_tc2_kernel<BN, kResid><<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(ma, mb, mr, mo, mo2, p.M, p.N, p.K, e,
-                                                                                 vec ? 1 : 0, err);
+    gemm_tc2_kernel<BN, kResid, kDeep><<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(ma, mb, mr, mo, mo2, p.M, p.N,
+                                                                                        p.K, e, vec ? 1 : 0, err);
     SANA_CUDA(cudaGetLastError());
 }
 
@@ -1175,11 +1181,15 @@ void gemm_tc(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
     // are masked in the epilogue); narrow problems use 128 columns.
     const bool pair = tc::use_pair(p, num_sms);
     const bool resid = p.ep.resid != nullptr;
+    // long reductions keep the MMA fed with deeper operand pipelines (their epilogue has slack)
+    const bool deep = p.K >= 2048;
     if (p.N >= 256) {
-        if (pair) resid ? tc::launch2<256, true>(p, err, stream, num_sms) : tc::launch2<256, false>(p, err, stream, num_sms);
+        if (pair && resid && deep) tc::launch2<256, true, true>(p, err, stream, num_sms);
+        else if (pair) resid ? tc::launch2<256, true>(p, err, stream, num_sms) : tc::launch2<256, false>(p, err, stream, num_sms);
         else resid ? tc::launch<256, true>(p, err, stream, num_sms) : tc::launch<256, false>(p, err, stream, num_sms);
     } else {
-        if (pair) resid ? tc::launch2<128, true>(p, err, stream, num_sms) : tc::launch2<128, false>(p, err, stream, num_sms);
+        if (pair && resid && deep) tc::launch2<128, true, true>(p, err, stream, num_sms);
+        else if (pair) resid ? tc::launch2<128, true>(p, err, stream, num_sms) : tc::launch2<128, false>(p, err, stream, num_sms);
         else resid ? tc::launch<128, true>(p, err, stream, num_sms) : tc::launch<128, false>(p, err, stream, num_sms);
     }
 }
