@@ -97,12 +97,15 @@ void launch(const T* q, long long ldq, const T* kv, long long ldkv, int k_off, i
 
 
 // ---------------------------------------------------------------------------------------
-// bf16 path on tensor cores (mma.sync m16n8k16, fp32 accumulation), flash-style: each warp
-// owns 16 query rows; keys stream through shared memory in chunks of 64 with an online
-// softmax (running max / sum per row, rescaled accumulators). Scores are rounded as the
-// reference rounds them (scale, then bias); P is rounded to bf16 for the P.V product.
-// Shared tiles are padded (K rows DP + 8, V^T rows 64 + 8 elements) so that every fragment
-// load is bank-conflict free.
+// bf16 path on tensor cores (mma.sync m16n8k16, fp32 accumulation), flash-style: a block
+// takes 128 queries of one head; each warp owns 16 query rows. The query tile arrives with
+// 16-byte async copies and is read into fragments with ldmatrix; keys and values stream
+// through shared memory in chunks of 64 with an online softmax (running max / sum per row,
+// rescaled accumulators), and only the 8-key column tiles holding live keys are multiplied.
+// Scores are rounded as the reference rounds them (scale, then bias); P is rounded to bf16
+// for the P.V product, so the exponentials use the hardware's fast path. The normalised
+// output goes back through the warp's rows of the query tile and leaves as 16-byte stores.
+// Shared tiles are padded to conflict-free row strides.
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -129,12 +132,28 @@ __device__ __forceinline__ void cp_async_wait_all() {
 __device__ __forceinline__ void ldmatrix_x2_trans(uint32_t addr, uint32_t& r0, uint32_t& r1) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
 
 // Row strides (elements) whose 4-byte-word stride is 4 mod 8: every 8-row fragment load
 // then touches 32 distinct banks.
 __host__ __device__ constexpr int conflict_free_stride(int min_elems) {
     return ((min_elems / 2) % 8 == 4) ? min_elems : ((min_elems + 7) / 8 * 8 + ((((min_elems + 7) / 8 * 8) / 2) % 8 == 4 ? 0 : 8));
 }
+
+template <int D>
+struct XattnTiles {
+    static constexpr int KS = (D + 15) / 16;               // k-steps over the head dim
+    static constexpr int DP = KS * 16;                     // padded head dim
+    static constexpr int KSTR = conflict_free_stride(DP);  // Q and K tile row stride
+    static constexpr int VSTR = conflict_free_stride(D);   // V tile row stride
+    static constexpr int kQRows = 16 * kMmaWarps;
+    static constexpr size_t kBytes = (static_cast<size_t>(kQRows) * KSTR + kChunkKeys * KSTR + kChunkKeys * VSTR) * 2 +
+                                     kChunkKeys * 4;
+};
 
 template <int D>
 __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* __restrict__ q, long long ldq,
@@ -144,52 +163,60 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
                                                                    const int* __restrict__ kv_len, int Tq, int L,
                                                                    float scale, bf16* __restrict__ out,
                                                                    long long ldo) {
-    constexpr int KS = (D + 15) / 16;                       // k-steps over the head dim
-    constexpr int DP = KS * 16;                             // padded head dim
-    constexpr int NT = D / 8;                               // 8-wide output tiles
-    constexpr int KSTR = conflict_free_stride(DP);          // K tile row stride
-    constexpr int VSTR = conflict_free_stride(D);           // V tile row stride
+    using X = XattnTiles<D>;
+    constexpr int KS = X::KS, DP = X::DP, KSTR = X::KSTR, VSTR = X::VSTR;
+    constexpr int NT = D / 8;  // 8-wide output tiles
+    constexpr int RC = D / 8;  // 16-byte pieces of a row
     static_assert((KSTR / 2) % 8 == 4 && (VSTR / 2) % 8 == 4 && KSTR % 8 == 0 && VSTR % 8 == 0, "strides");
-    __shared__ __align__(16) bf16 Ks[kChunkKeys * KSTR];
-    __shared__ __align__(16) bf16 Vs[kChunkKeys * VSTR];
-    __shared__ float bsh[kChunkKeys];
+    extern __shared__ __align__(16) unsigned char xsm[];
+    bf16* Qs = reinterpret_cast<bf16*>(xsm);            // [128][KSTR], later the output rows
+    bf16* Ks = Qs + X::kQRows * KSTR;                    // [64][KSTR]
+    bf16* Vs = Ks + kChunkKeys * KSTR;                   // [64][VSTR]
+    float* bsh = reinterpret_cast<float*>(Vs + kChunkKeys * VSTR);
 
     const int s = blockIdx.z, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, tig = lane & 3;
-    const int q0 = blockIdx.x * (16 * kMmaWarps) + warp * 16;
+    const int qb = blockIdx.x * X::kQRows;
+    const int q0 = qb + warp * 16;
     const int n_kv = kv_len ? kv_len[s] : L;
     const bool active = q0 < Tq;
-    if (DP > D) {  // zero the K padding columns once; the copies below never touch them
+    const uint32_t qbase = smem_u32(Qs), kbase = smem_u32(Ks), vbase = smem_u32(Vs);
+
+    // query tile (rows past Tq and the head-dim padding read as zeros)
+    for (int i = threadIdx.x; i < X::kQRows * RC; i += blockDim.x) {
+        const int r = i / RC, ck = i % RC;
+        if (qb + r < Tq)
+            cp_async16(qbase + static_cast<uint32_t>(r * KSTR + ck * 8) * 2u,
+                       q + (static_cast<long long>(s) * Tq + qb + r) * ldq + h * D + ck * 8);
+        else
+            *reinterpret_cast<uint4*>(Qs + r * KSTR + ck * 8) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    if constexpr (DP > D) {
+        for (int i = threadIdx.x; i < X::kQRows * (DP - D); i += blockDim.x)
+            Qs[(i / (DP - D)) * KSTR + D + i % (DP - D)] = __float2bfloat16_rn(0.f);
         for (int i = threadIdx.x; i < kChunkKeys * (DP - D); i += blockDim.x)
             Ks[(i / (DP - D)) * KSTR + D + i % (DP - D)] = __float2bfloat16_rn(0.f);
     }
-
+    cp_async_wait_all();
+    __syncthreads();
     uint32_t qa[KS][4];
 #pragma unroll
-    for (int kk = 0; kk < KS; ++kk) {
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int row = q0 + g + ((r & 1) ? 8 : 0);
-            const int col = kk * 16 + tig * 2 + ((r & 2) ? 8 : 0);
-            uint32_t v = 0;
-            if (row < Tq && col < D)
-                v = *reinterpret_cast<const uint32_t*>(q + (static_cast<long long>(s) * Tq + row) * ldq + h * D + col);
-            qa[kk][r] = v;
-        }
-    }
+    for (int kk = 0; kk < KS; ++kk)
+        ldmatrix_x4(qbase + static_cast<uint32_t>((warp * 16 + (lane & 15)) * KSTR + kk * 16 + (lane >> 4) * 8) * 2u,
+                    qa[kk]);
+
     float o[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    const uint32_t kbase = smem_u32(Ks), vbase = smem_u32(Vs);
 
     for (int c0 = 0; c0 < n_kv; c0 += kChunkKeys) {
         const int nk = min(kChunkKeys, n_kv - c0);
         __syncthreads();
-        for (int i = threadIdx.x; i < kChunkKeys * (D / 8) * 2; i += blockDim.x) {
-            const int which = i / (kChunkKeys * (D / 8)), rem = i % (kChunkKeys * (D / 8));
-            const int j = rem / (D / 8), ck = rem % (D / 8);
+        for (int i = threadIdx.x; i < kChunkKeys * RC * 2; i += blockDim.x) {
+            const int which = i / (kChunkKeys * RC), rem = i % (kChunkKeys * RC);
+            const int j = rem / RC, ck = rem % RC;
             if (j < nk) {
                 const bf16* src = kv + (static_cast<long long>(s) * L + c0 + j) * ldkv + (which ? v_off : k_off) + h * D +
                                   ck * 8;
@@ -207,25 +234,34 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
         __syncthreads();
         if (!active) continue;
 
+        const int ntmax = (nk + 7) / 8;  // 8-key column tiles holding live keys
         float sc[kChunkKeys / 8][4];
 #pragma unroll
         for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
-            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = -INFINITY;
+            if (nt < ntmax) {
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int kk = 0; kk < KS; ++kk) {
-                const bf16* kr = Ks + (nt * 8 + g) * KSTR + kk * 16 + tig * 2;
-                mma_bf16_16816(sc[nt], qa[kk], *reinterpret_cast<const uint32_t*>(kr),
-                               *reinterpret_cast<const uint32_t*>(kr + 8));
+                for (int kk = 0; kk < KS; ++kk) {
+                    const bf16* kr = Ks + (nt * 8 + g) * KSTR + kk * 16 + tig * 2;
+                    mma_bf16_16816(acc, qa[kk], *reinterpret_cast<const uint32_t*>(kr),
+                                   *reinterpret_cast<const uint32_t*>(kr + 8));
+                }
+                const int key = nt * 8 + tig * 2;
+                const float2 b2 = *reinterpret_cast<const float2*>(bsh + key);
+                if (key < nk) {
+                    sc[nt][0] = __fadd_rn(__fmul_rn(acc[0], scale), b2.x);
+                    sc[nt][2] = __fadd_rn(__fmul_rn(acc[2], scale), b2.x);
+                }
+                if (key + 1 < nk) {
+                    sc[nt][1] = __fadd_rn(__fmul_rn(acc[1], scale), b2.y);
+                    sc[nt][3] = __fadd_rn(__fmul_rn(acc[3], scale), b2.y);
+                }
             }
         }
         float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
         for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int key = nt * 8 + tig * 2 + (e & 1);
-                sc[nt][e] = key < nk ? __fadd_rn(__fmul_rn(sc[nt][e], scale), bsh[key]) : -INFINITY;
-            }
             mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
             mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
         }
@@ -234,18 +270,22 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
         const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-        const float corr0 = expf(m0 - mn0), corr1 = expf(m1 - mn1);  // m = -inf on the first chunk: 0
+        const float corr0 = __expf(m0 - mn0), corr1 = __expf(m1 - mn1);  // m = -inf on the first chunk: 0
         m0 = mn0;
         m1 = mn1;
         float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
         for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
-            sc[nt][0] = expf(sc[nt][0] - mn0);
-            sc[nt][1] = expf(sc[nt][1] - mn0);
-            sc[nt][2] = expf(sc[nt][2] - mn1);
-            sc[nt][3] = expf(sc[nt][3] - mn1);
-            sum0 += sc[nt][0] + sc[nt][1];
-            sum1 += sc[nt][2] + sc[nt][3];
+            if (nt < ntmax) {
+                sc[nt][0] = __expf(sc[nt][0] - mn0);
+                sc[nt][1] = __expf(sc[nt][1] - mn0);
+                sc[nt][2] = __expf(sc[nt][2] - mn1);
+                sc[nt][3] = __expf(sc[nt][3] - mn1);
+                sum0 += sc[nt][0] + sc[nt][1];
+                sum1 += sc[nt][2] + sc[nt][3];
+            } else {
+                sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+            }
         }
         l0 = l0 * corr0 + sum0;
         l1 = l1 * corr1 + sum1;
@@ -278,16 +318,20 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
     const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
-    const int r0 = q0 + g, r1 = q0 + g + 8;
+    // the warp's 16 output rows through its own rows of the query tile, then 16-byte stores
+    bf16* orows = Qs + warp * 16 * KSTR;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-        const int col = h * D + nt * 8 + tig * 2;
-        if (r0 < Tq)
-            *reinterpret_cast<uint32_t*>(out + (static_cast<long long>(s) * Tq + r0) * ldo + col) =
-                pack_bf16(o[nt][0] * inv0, o[nt][1] * inv0);
-        if (r1 < Tq)
-            *reinterpret_cast<uint32_t*>(out + (static_cast<long long>(s) * Tq + r1) * ldo + col) =
-                pack_bf16(o[nt][2] * inv1, o[nt][3] * inv1);
+        *reinterpret_cast<uint32_t*>(orows + g * KSTR + nt * 8 + tig * 2) = pack_bf16(o[nt][0] * inv0, o[nt][1] * inv0);
+        *reinterpret_cast<uint32_t*>(orows + (g + 8) * KSTR + nt * 8 + tig * 2) =
+            pack_bf16(o[nt][2] * inv1, o[nt][3] * inv1);
+    }
+    __syncwarp();
+    for (int i = lane; i < 16 * RC; i += 32) {
+        const int r = i / RC, ck = i % RC;
+        if (q0 + r < Tq)
+            *reinterpret_cast<uint4*>(out + (static_cast<long long>(s) * Tq + q0 + r) * ldo + h * D + ck * 8) =
+                *reinterpret_cast<const uint4*>(orows + r * KSTR + ck * 8);
     }
 }
 
@@ -295,7 +339,14 @@ template <int D>
 bool launch_mma(const bf16* q, long long ldq, const bf16* kv, long long ldkv, int k_off, int v_off, const float* bias,
                 const int* kv_len, int S, int Tq, int L, int heads, float scale, bf16* out, long long ldo,
                 cudaStream_t st) {
-    xattn_mma_kernel<D><<<dim3(ceil_div(Tq, 16 * kMmaWarps), heads, S), 32 * kMmaWarps, 0, st>>>(
+    constexpr size_t smem = XattnTiles<D>::kBytes;
+    static bool attr = false;
+    if (!attr) {
+        SANA_CUDA(cudaFuncSetAttribute(xattn_mma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem)));
+        attr = true;
+    }
+    xattn_mma_kernel<D><<<dim3(ceil_div(Tq, 16 * kMmaWarps), heads, S), 32 * kMmaWarps, smem, st>>>(
         q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, Tq, L, scale, out, ldo);
     SANA_CUDA(cudaGetLastError());
     return true;
@@ -311,10 +362,10 @@ template <>
 bool try_mma<bf16>(const bf16* q, long long ldq, const bf16* kv, long long ldkv, int k_off, int v_off,
                    const float* bias, const int* kv_len, int S, int Tq, int L, int heads, int D, float scale, bf16* out,
                    long long ldo, cudaStream_t st) {
-    // 16-byte copies of K / V rows: row starts, offsets and the head stride 8-element aligned
-    const bool aligned = ldq % 2 == 0 && ldkv % 8 == 0 && ldo % 2 == 0 && k_off % 8 == 0 && v_off % 8 == 0 &&
-                         D % 8 == 0 && (reinterpret_cast<uintptr_t>(q) & 3) == 0 &&
-                         (reinterpret_cast<uintptr_t>(kv) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 3) == 0;
+    // 16-byte copies of Q / K / V / O rows: row starts, offsets and the head stride 8-element aligned
+    const bool aligned = ldq % 8 == 0 && ldkv % 8 == 0 && ldo % 8 == 0 && k_off % 8 == 0 && v_off % 8 == 0 &&
+                         D % 8 == 0 && (reinterpret_cast<uintptr_t>(q) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(kv) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
     if (!aligned) return false;
     switch (D) {
         case 32: return launch_mma<32>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, scale, out, ldo, st);
