@@ -108,6 +108,31 @@ int sana_cuda_debug_read(sana_cuda_ctx *ctx, const char *name, size_t offset, si
 int sana_cuda_upload_weights(sana_cuda_ctx *ctx, const sana_dims *dims, const float *const *model,
                              const float *const *blocks, int layout);
 
+/* GGUF weight files, read without ggml: the reference's model_weights.gguf,
+ * caption_weights.gguf and denoiser_weights.gguf (infer_main.cpp:347-365), whose tensors
+ * load_weight_index / load_weight_tensor (weights_io.cpp:134-164, 325-377) read as fp32 and
+ * load_denoiser_weights (transformer.cpp:166-488) assembles by name. sana_gguf_* index one
+ * file (no device needed); sana_cuda_upload_gguf maps the three files, resolves the
+ * reference's names and block prefixes ("<prefix>.scale_shift_table", ordered by trailing
+ * index), checks the shapes as the loaders do and uploads straight from the mapping into the
+ * device cache (linear weights stay in the files' [out, in] layout), filling *dims_out if
+ * not NULL. Errors follow the loaders: a missing tensor is SANA_ERR_INVALID ("weight name not
+ * found in weight index"), an unreadable or malformed file, a non-fp32 tensor or a shape
+ * mismatch SANA_ERR_STATE (std::runtime_error). */
+typedef struct sana_gguf sana_gguf;
+int sana_gguf_open(const char *path, sana_gguf **out, char *err, size_t err_len);
+void sana_gguf_close(sana_gguf *file);
+int sana_gguf_tensor_count(const sana_gguf *file);
+/* index of the named tensor, or -1 */
+int sana_gguf_find(const sana_gguf *file, const char *name);
+/* tensor i: name, element type (0 fp32, 1 fp16, 30 bf16, others as the file says), rank,
+ * the first max_rank extents slowest-first (numpy / PyTorch order), its bytes in the
+ * mapping (valid until sana_gguf_close) and their count (0 for types other than those three). */
+int sana_gguf_tensor_info(const sana_gguf *file, int i, const char **name, int *type, int *rank, int64_t *shape,
+                          int max_rank, const void **data, uint64_t *nbytes);
+int sana_cuda_upload_gguf(sana_cuda_ctx *ctx, const char *model_path, const char *caption_path,
+                          const char *denoiser_path, int self_heads, int cross_heads, sana_dims *dims_out);
+
 /* --- the denoiser path (host buffers) --------------------------------------------------- */
 
 /* run_full_denoising_loop_with_cfg (transformer.h:140-148, transformer.cpp:692-724) with a

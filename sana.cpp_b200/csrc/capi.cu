@@ -8,7 +8,12 @@
 #include <string>
 #include <vector>
 
+#include <algorithm>
+#include <set>
+#include <stdexcept>
+
 #include "engine.h"
+#include "gguf.h"
 #include "sana_cuda.h"
 
 struct sana_cuda_ctx {
@@ -288,6 +293,206 @@ int sana_cuda_upload_weights(sana_cuda_ctx* ctx, const sana_dims* dims, const fl
         d.Hs = dims->self_heads;
         d.Hc = dims->cross_heads;
         engine(ctx).upload(d, model, blocks, layout);
+    });
+}
+
+// --- GGUF weight files ---------------------------------------------------------------------
+namespace {
+
+// The reference's tensor names (load_caption_weights / load_block_weights /
+// load_denoiser_weights, transformer.cpp:166-488); every tensor is required, as there.
+const char* const kCaptionNames[4] = {"caption_projection.linear_1.weight", "caption_projection.linear_1.bias",
+                                      "caption_projection.linear_2.weight", "caption_projection.linear_2.bias"};
+const char* const kDenoiserNames[12] = {
+    "patch_embed.proj.weight", "patch_embed.proj.bias",
+    "time_embed.emb.timestep_embedder.linear_1.weight", "time_embed.emb.timestep_embedder.linear_1.bias",
+    "time_embed.emb.timestep_embedder.linear_2.weight", "time_embed.emb.timestep_embedder.linear_2.bias",
+    "time_embed.linear.weight", "time_embed.linear.bias", "caption_norm.weight", "scale_shift_table",
+    "proj_out.weight", "proj_out.bias"};
+// SanaBlockWeights field -> tensor suffix (nullptr: the loader's default, a zero bias or an
+// identity norm, transformer.cpp:361-398)
+const char* const kBlockNames[26] = {
+    "scale_shift_table", nullptr, nullptr, "attn1.to_q.weight", nullptr, "attn1.to_k.weight", nullptr,
+    "attn1.to_v.weight", nullptr, "attn1.to_out.0.weight", "attn1.to_out.0.bias", "attn2.to_q.weight",
+    "attn2.to_q.bias", "attn2.to_k.weight", "attn2.to_k.bias", "attn2.to_v.weight", "attn2.to_v.bias",
+    "attn2.to_out.0.weight", "attn2.to_out.0.bias", nullptr, nullptr, "ff.conv_inverted.weight",
+    "ff.conv_inverted.bias", "ff.conv_depth.weight", "ff.conv_depth.bias", "ff.conv_point.weight"};
+
+// block_weight_name / parse_trailing_index / find_block_prefixes (transformer.cpp:26-55, 401-430):
+// the prefixes of every "<prefix>.scale_shift_table", numerically ordered on a trailing index.
+bool trailing_index(const std::string& p, std::string* stem, size_t* idx) {
+    const size_t dot = p.rfind('.');
+    if (dot == std::string::npos || dot + 1 >= p.size()) return false;
+    const std::string tail = p.substr(dot + 1);
+    for (char ch : tail)
+        if (ch < '0' || ch > '9') return false;
+    *stem = p.substr(0, dot);
+    *idx = static_cast<size_t>(std::stoull(tail));
+    return true;
+}
+
+std::vector<std::string> block_prefixes(const sana::GgufFile& f) {
+    const std::string suffix = ".scale_shift_table";
+    std::set<std::string> uniq;
+    for (const auto& t : f.tensors())
+        if (t.name.size() > suffix.size() && t.name.compare(t.name.size() - suffix.size(), suffix.size(), suffix) == 0)
+            uniq.insert(t.name.substr(0, t.name.size() - suffix.size()));
+    std::vector<std::string> v(uniq.begin(), uniq.end());
+    std::sort(v.begin(), v.end(), [](const std::string& a, const std::string& b) {
+        std::string sa, sb;
+        size_t ia = 0, ib = 0;
+        if (trailing_index(a, &sa, &ia) && trailing_index(b, &sb, &ib) && sa == sb) return ia < ib;
+        return a < b;
+    });
+    return v;
+}
+
+// An fp32 tensor of the file with the given rank; the reference reads GGUF payloads as
+// float32 only (weights_io.cpp:331-351).
+const float* tensor_f32(const sana::GgufFile& f, const std::string& name, size_t rank,
+                        std::vector<int64_t>* shape_out) {
+    const sana::GgufTensor* t = f.find(name);
+    if (!t) throw std::invalid_argument("weight name not found in weight index: " + name);
+    if (t->type != sana::kGgufF32) throw std::runtime_error("only float32 saved weights are supported: " + name);
+    if (t->shape.size() != rank)
+        throw std::runtime_error(name + " must be rank " + std::to_string(rank) + " in " + f.path());
+    if (shape_out) *shape_out = t->shape;
+    return reinterpret_cast<const float*>(t->data);
+}
+
+void require_shape(const std::string& name, const std::vector<int64_t>& got, const std::vector<int64_t>& want) {
+    if (got != want) {
+        std::string g, w;
+        for (auto v : got) g += std::to_string(v) + ",";
+        for (auto v : want) w += std::to_string(v) + ",";
+        throw std::runtime_error(name + " has shape {" + g + "}, expected {" + w + "}");
+    }
+}
+
+// Expected shape of SanaBlockWeights field i ([out, in] linear weights, conv [out, in, kh, kw]).
+std::vector<int64_t> block_shape(int i, int64_t C, int64_t E) {
+    switch (i) {
+        case 0: return {6, C};
+        case 10: case 12: case 14: case 16: case 18: return {C};
+        case 21: return {E, C, 1, 1};
+        case 22: case 24: return {E};
+        case 23: return {E, 1, 3, 3};
+        case 25: return {C, E / 2, 1, 1};
+        default: return {C, C};  // the eight attention projections
+    }
+}
+
+}  // namespace
+
+struct sana_gguf {
+    std::unique_ptr<sana::GgufFile> file;
+};
+
+int sana_gguf_open(const char* path, sana_gguf** out, char* err, size_t err_len) {
+    if (!path || !out) return SANA_ERR_INVALID;
+    *out = nullptr;
+    try {
+        auto h = std::make_unique<sana_gguf>();
+        h->file = std::make_unique<sana::GgufFile>(path);
+        *out = h.release();
+        return SANA_OK;
+    } catch (const std::exception& e) {
+        if (err && err_len) std::snprintf(err, err_len, "%s", e.what());
+        return SANA_ERR_STATE;
+    }
+}
+
+void sana_gguf_close(sana_gguf* f) { delete f; }
+
+int sana_gguf_tensor_count(const sana_gguf* f) { return f ? static_cast<int>(f->file->tensors().size()) : -1; }
+
+int sana_gguf_find(const sana_gguf* f, const char* name) {
+    if (!f || !name) return -1;
+    const sana::GgufTensor* t = f->file->find(name);
+    return t ? static_cast<int>(t - f->file->tensors().data()) : -1;
+}
+
+int sana_gguf_tensor_info(const sana_gguf* f, int i, const char** name, int* type, int* rank, int64_t* shape,
+                          int max_rank, const void** data, uint64_t* nbytes) {
+    if (!f || i < 0 || i >= static_cast<int>(f->file->tensors().size())) return SANA_ERR_INVALID;
+    const sana::GgufTensor& t = f->file->tensors()[static_cast<size_t>(i)];
+    if (name) *name = t.name.c_str();
+    if (type) *type = static_cast<int>(t.type);
+    if (rank) *rank = static_cast<int>(t.shape.size());
+    if (shape)
+        for (int d = 0; d < max_rank && d < static_cast<int>(t.shape.size()); ++d) shape[d] = t.shape[static_cast<size_t>(d)];
+    if (data) *data = t.data;
+    if (nbytes) *nbytes = t.nbytes;
+    return SANA_OK;
+}
+
+int sana_cuda_upload_gguf(sana_cuda_ctx* ctx, const char* model_path, const char* caption_path,
+                          const char* denoiser_path, int self_heads, int cross_heads, sana_dims* dims_out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(model_path && caption_path && denoiser_path, "weight file paths must not be null");
+        if (self_heads <= 0) throw std::invalid_argument("self_num_heads must be greater than 0");
+        if (cross_heads <= 0) throw std::invalid_argument("cross_num_heads must be greater than 0");
+        const sana::GgufFile mf(model_path), cf(caption_path), df(denoiser_path);
+        std::vector<int64_t> sh;
+        // dimensions from the caption, patch and first block tensors ([out, in] linear weights)
+        const float* model[16];
+        model[0] = tensor_f32(cf, kCaptionNames[0], 2, &sh);
+        const int64_t C = sh[0], Din = sh[1];
+        model[1] = tensor_f32(cf, kCaptionNames[1], 1, &sh);
+        require_shape(kCaptionNames[1], sh, {C});
+        model[2] = tensor_f32(cf, kCaptionNames[2], 2, &sh);
+        require_shape(kCaptionNames[2], sh, {C, C});
+        model[3] = tensor_f32(cf, kCaptionNames[3], 1, &sh);
+        require_shape(kCaptionNames[3], sh, {C});
+        model[4] = tensor_f32(df, kDenoiserNames[0], 4, &sh);
+        const int64_t Cl = sh[1];
+        require_shape(kDenoiserNames[0], sh, {C, Cl, 1, 1});
+        const std::vector<std::vector<int64_t>> dshape = {
+            {C, Cl, 1, 1}, {C}, {C, 256}, {C}, {C, C}, {C}, {6 * C, C}, {6 * C}, {C}, {2, C}, {Cl, C}, {Cl}};
+        for (int i = 1; i < 12; ++i) {
+            model[4 + i] = tensor_f32(df, kDenoiserNames[i], dshape[static_cast<size_t>(i)].size(), &sh);
+            require_shape(kDenoiserNames[i], sh, dshape[static_cast<size_t>(i)]);
+        }
+        const std::vector<std::string> prefixes = block_prefixes(mf);
+        if (prefixes.empty()) throw std::invalid_argument("weight index does not contain any prefixed model blocks");
+        std::vector<const float*> blocks(26 * prefixes.size(), nullptr);
+        int64_t E = 0;
+        for (size_t b = 0; b < prefixes.size(); ++b) {
+            const float** w = blocks.data() + 26 * b;
+            for (int i = 0; i < 26; ++i) {
+                if (!kBlockNames[i]) continue;
+                const std::string name = prefixes[b] + "." + kBlockNames[i];
+                const sana::GgufTensor* t = mf.find(name);
+                if (!t) throw std::invalid_argument("weight name not found in weight index: " + name);
+                w[i] = tensor_f32(mf, name, t->shape.size(), &sh);
+                if (i == 21 && b == 0) E = sh.size() == 4 ? sh[0] : 0;
+                // load_block_weights' checks (transformer.cpp:310-359), with the model's sizes
+                require_shape(name, sh, block_shape(i, C, E));
+            }
+        }
+        if (E <= 0 || E % 2 != 0) throw std::runtime_error("ff point conv input channels must match split GLUMB width");
+        if (C % self_heads != 0)
+            throw std::runtime_error("self attention hidden size must be divisible by self_num_heads");
+        if (C % cross_heads != 0)
+            throw std::runtime_error("cross attention hidden size must be divisible by cross_num_heads");
+        sana::Dims d;
+        d.n_blocks = static_cast<int>(prefixes.size());
+        d.C = static_cast<int>(C);
+        d.Cl = static_cast<int>(Cl);
+        d.Din = static_cast<int>(Din);
+        d.E = static_cast<int>(E);
+        d.Hs = self_heads;
+        d.Hc = cross_heads;
+        engine(ctx).upload(d, model, blocks.data(), sana::kLayoutTorch);
+        if (dims_out) {
+            dims_out->n_blocks = d.n_blocks;
+            dims_out->hidden = d.C;
+            dims_out->latent_channels = d.Cl;
+            dims_out->caption_dim = d.Din;
+            dims_out->ff_expanded = d.E;
+            dims_out->self_heads = d.Hs;
+            dims_out->cross_heads = d.Hc;
+        }
     });
 }
 

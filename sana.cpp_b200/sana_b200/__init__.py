@@ -10,6 +10,7 @@ from .capi import (  # noqa: F401
     SanaCuda,
     SanaError,
     gemm_counts,
+    gguf_index,
     lib_path,
     load_library,
     randn_torch_cpu,

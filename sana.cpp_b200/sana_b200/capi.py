@@ -59,6 +59,15 @@ def load_library():
         lib.sana_cuda_destroy.argtypes = [ctypes.c_void_p]
         lib.sana_cuda_last_launch_count.argtypes = [ctypes.c_void_p]
         lib.sana_randn_torch_cpu.argtypes = [_f32p, ctypes.c_size_t, ctypes.c_uint64]
+        lib.sana_gguf_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p,
+                                       ctypes.c_size_t]
+        lib.sana_gguf_close.argtypes = [ctypes.c_void_p]
+        lib.sana_gguf_tensor_count.argtypes = [ctypes.c_void_p]
+        lib.sana_gguf_find.argtypes = [ctypes.c_void_p, ctypes.c_char_p]
+        lib.sana_gguf_tensor_info.argtypes = [ctypes.c_void_p, _i, ctypes.POINTER(ctypes.c_char_p),
+                                              ctypes.POINTER(_i), ctypes.POINTER(_i),
+                                              ctypes.POINTER(ctypes.c_int64), _i, ctypes.POINTER(ctypes.c_void_p),
+                                              ctypes.POINTER(ctypes.c_uint64)]
         _LIB = lib
     return _LIB
 
@@ -82,6 +91,38 @@ def randn_torch_cpu(n: int, seed: int) -> np.ndarray:
     if rc != 0:
         raise ValueError("randn_torch_cpu needs at least 16 elements")
     return out
+
+
+GGUF_F32, GGUF_F16, GGUF_BF16 = 0, 1, 30
+
+
+def gguf_index(path: str) -> dict:
+    """The library's GGUF reader on one file: {name: (element type, shape, array)} with the
+    shape slowest-first and, for fp32 / fp16 tensors, a copy of the data (None otherwise)."""
+    lib = load_library()
+    h = ctypes.c_void_p()
+    err = ctypes.create_string_buffer(512)
+    rc = lib.sana_gguf_open(os.fsencode(path), ctypes.byref(h), err, 512)
+    if rc != 0:
+        raise SanaError(rc, err.value.decode())
+    try:
+        out = {}
+        for i in range(lib.sana_gguf_tensor_count(h)):
+            name, typ, rank = ctypes.c_char_p(), _i(), _i()
+            shape = (ctypes.c_int64 * 8)()
+            data, nbytes = ctypes.c_void_p(), ctypes.c_uint64()
+            lib.sana_gguf_tensor_info(h, _i(i), ctypes.byref(name), ctypes.byref(typ), ctypes.byref(rank), shape, 8,
+                                      ctypes.byref(data), ctypes.byref(nbytes))
+            shp = tuple(shape[d] for d in range(rank.value))
+            arr = None
+            dt = {GGUF_F32: np.float32, GGUF_F16: np.float16}.get(typ.value)
+            if dt is not None and nbytes.value:
+                buf = (ctypes.c_char * nbytes.value).from_address(data.value)
+                arr = np.frombuffer(bytes(buf), dtype=dt).reshape(shp)
+            out[name.value.decode()] = (typ.value, shp, arr)
+        return out
+    finally:
+        lib.sana_gguf_close(h)
 
 
 def gemm_counts():
@@ -196,6 +237,16 @@ class SanaCuda:
         for i in range(nb):
             blocks += block_tensor_table(tensors[16 + 19 * i: 16 + 19 * (i + 1)])
         self.upload(dims, tensors[:16], blocks, SANA_LAYOUT_TORCH)
+
+    def upload_gguf(self, model_path: str, caption_path: str, denoiser_path: str, self_heads: int = 36,
+                    cross_heads: int = 16):
+        """Uploads the reference's three GGUF weight files straight into the device cache;
+        returns the dims read from them."""
+        d = sana_dims()
+        self._call("sana_cuda_upload_gguf", os.fsencode(model_path), os.fsencode(caption_path),
+                   os.fsencode(denoiser_path), _i(self_heads), _i(cross_heads), ctypes.byref(d))
+        self.dims = d
+        return (d.n_blocks, d.hidden, d.latent_channels, d.caption_dim, d.ff_expanded, d.self_heads, d.cross_heads)
 
     # -- denoiser path (host buffers) ---------------------------------------------------
     def denoise_loop(self, latents, enc, bias, guidance: float = 4.5, num_steps: int = 20, flow_shift: float = 3.0):

@@ -218,3 +218,64 @@ def test_highres_step_is_finite_and_consistent(full_gpu):
     lat2, si, lo, hist = full_gpu.denoise_step(lat, ctx, bias, 4.5, float(ts[0]), sg, 0, 0, [])
     assert si == 1 and lo == 1 and len(hist) == 1
     assert cosine(lat2, one_step) > 0.9999
+
+
+@pytest.mark.parametrize("mode", ["f32", "bf16"])
+def test_gguf_upload_matches_pointer_upload(tmp_path, mode):
+    """The reference's three GGUF weight files, mapped and uploaded straight into the device
+    cache (sana_cuda_upload_gguf), give the same model as the pointer-table upload of the same
+    checkpoint: identical denoising-loop latents and caption projection, in both modes."""
+    from sana_b200 import SANA_MODE_BF16, SANA_MODE_F32, SanaCuda, randn_torch_cpu
+    from sana_b200.gguf_files import write_checkpoint_gguf
+    d = syn.ModelDims(n_blocks=3, hidden=128, latent_channels=8, caption_dim=96, ff_expanded=320, self_heads=4,
+                      cross_heads=2)
+    tensors = syn.generate_model(d, randn_torch_cpu, base_seed=11, bias_std=0.02)
+    paths = write_checkpoint_gguf(tensors, d.n_blocks, str(tmp_path))
+    m = SANA_MODE_F32 if mode == "f32" else SANA_MODE_BF16
+    a, b = SanaCuda(0, m), SanaCuda(0, m)
+    a.upload_checkpoint(d.as_args(), tensors)
+    dims = b.upload_gguf(paths["model"], paths["caption"], paths["denoiser"], d.self_heads, d.cross_heads)
+    assert dims == tuple(d.as_args())
+    enc = syn.encoder_states(randn_torch_cpu, 2, 20, d.caption_dim, 3)
+    bias = syn.attention_bias([5, 12], 20)
+    lat = syn.latents(randn_torch_cpu, 1, d.latent_channels, 8, 8, 4)
+    assert np.array_equal(a.denoise_loop(lat, enc, bias, 4.5, 4), b.denoise_loop(lat, enc, bias, 4.5, 4))
+    assert np.array_equal(a.project_caption_model(enc), b.project_caption_model(enc))
+
+
+def test_gguf_upload_errors_follow_the_loaders(tmp_path):
+    """A missing tensor is the loaders' invalid_argument (ValueError here); a non-fp32 tensor
+    or a wrong shape is a runtime error (SanaError), as weights_io.cpp / transformer.cpp raise."""
+    import gguf
+    from sana_b200 import SanaCuda, SanaError, randn_torch_cpu
+    from sana_b200.gguf_files import write_checkpoint_gguf
+    d = syn.ModelDims(n_blocks=1, hidden=64, latent_channels=4, caption_dim=48, ff_expanded=160, self_heads=2,
+                      cross_heads=2)
+    tensors = syn.generate_model(d, randn_torch_cpu, base_seed=2)
+    paths = write_checkpoint_gguf(tensors, d.n_blocks, str(tmp_path))
+    g = SanaCuda(0)
+
+    def rewrite(path, fn):
+        r = gguf.GGUFReader(path)
+        items = [(t.name, np.array(t.data).reshape(tuple(int(x) for x in reversed(t.shape)))) for t in r.tensors]
+        del r
+        w = gguf.GGUFWriter(path, arch="sana")
+        for name, arr in fn(items):
+            w.add_tensor(name, arr)
+        w.write_header_to_file()
+        w.write_kv_data_to_file()
+        w.write_tensors_to_file()
+        w.close()
+
+    rewrite(paths["denoiser"], lambda items: [x for x in items if x[0] != "proj_out.bias"])
+    with pytest.raises(ValueError, match="weight name not found"):
+        g.upload_gguf(paths["model"], paths["caption"], paths["denoiser"], 2, 2)
+    write_checkpoint_gguf(tensors, d.n_blocks, str(tmp_path))
+    rewrite(paths["caption"], lambda items: [(n, a.astype(np.float16) if n.endswith("linear_2.weight") else a)
+                                             for n, a in items])
+    with pytest.raises(SanaError, match="only float32"):
+        g.upload_gguf(paths["model"], paths["caption"], paths["denoiser"], 2, 2)
+    write_checkpoint_gguf(tensors, d.n_blocks, str(tmp_path))
+    rewrite(paths["model"], lambda items: [(n, a[:, :32] if n.endswith("attn1.to_q.weight") else a) for n, a in items])
+    with pytest.raises(SanaError, match="has shape"):
+        g.upload_gguf(paths["model"], paths["caption"], paths["denoiser"], 2, 2)
