@@ -132,6 +132,14 @@ __device__ __forceinline__ void cp_async_wait_all() {
 __device__ __forceinline__ void ldmatrix_x2_trans(uint32_t addr, uint32_t& r0, uint32_t& r1) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
 __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t (&r)[4]) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -241,11 +249,19 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
             sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = -INFINITY;
             if (nt < ntmax) {
                 float acc[4] = {0.f, 0.f, 0.f, 0.f};
+                // K fragments by ldmatrix: 8 key rows x (two k-steps of 16) per x4 load
+                const uint32_t krow = kbase + static_cast<uint32_t>((nt * 8 + (lane & 7)) * KSTR + (lane >> 3) * 8) * 2u;
 #pragma unroll
-                for (int kk = 0; kk < KS; ++kk) {
-                    const bf16* kr = Ks + (nt * 8 + g) * KSTR + kk * 16 + tig * 2;
-                    mma_bf16_16816(acc, qa[kk], *reinterpret_cast<const uint32_t*>(kr),
-                                   *reinterpret_cast<const uint32_t*>(kr + 8));
+                for (int kk = 0; kk + 1 < KS; kk += 2) {
+                    uint32_t b[4];
+                    ldmatrix_x4(krow + static_cast<uint32_t>(kk * 16) * 2u, b);
+                    mma_bf16_16816(acc, qa[kk], b[0], b[1]);
+                    mma_bf16_16816(acc, qa[kk + 1], b[2], b[3]);
+                }
+                if constexpr (KS % 2 == 1) {
+                    uint32_t b0, b1;
+                    ldmatrix_x2(krow + static_cast<uint32_t>((KS - 1) * 16) * 2u, b0, b1);
+                    mma_bf16_16816(acc, qa[KS - 1], b0, b1);
                 }
                 const int key = nt * 8 + tig * 2;
                 const float2 b2 = *reinterpret_cast<const float2*>(bsh + key);
@@ -304,11 +320,19 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
                                     pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]),
                                     pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3])};
             const uint32_t vrow = vbase + static_cast<uint32_t>((kk * 16 + (lane & 15)) * VSTR) * 2u;
+            // V fragments of two 8-column output tiles per x4 load (lanes 16-31 address the second)
+            const uint32_t vrow4 = vrow + static_cast<uint32_t>((lane >> 4) * 8) * 2u;
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
+            for (int nt = 0; nt + 1 < NT; nt += 2) {
+                uint32_t b[4];
+                ldmatrix_x4_trans(vrow4 + static_cast<uint32_t>(nt * 16), b);
+                mma_bf16_16816(o[nt], pa, b[0], b[1]);
+                mma_bf16_16816(o[nt + 1], pa, b[2], b[3]);
+            }
+            if constexpr (NT % 2 == 1) {
                 uint32_t b0, b1;
-                ldmatrix_x2_trans(vrow + static_cast<uint32_t>(nt * 16), b0, b1);
-                mma_bf16_16816(o[nt], pa, b0, b1);
+                ldmatrix_x2_trans(vrow + static_cast<uint32_t>((NT - 1) * 16), b0, b1);
+                mma_bf16_16816(o[NT - 1], pa, b0, b1);
             }
         }
     }
