@@ -330,6 +330,36 @@ int sana_scheduler_step(sana_cuda_ctx *ctx, const float *sigmas, int n_sigmas, i
  * generator seeded with `seed`, bit-identical to the reference's restatement. Host only. */
 int sana_randn_torch_cpu(float *out, size_t n, uint64_t seed);
 
+/* --- the text-encoder output contract ----------------------------------------------------- */
+
+/* select_rows_first_and_last (gemma_encoder.h:45-48, gemma_encoder.cpp:51-77): row 0 of
+ * in [rows, cols], then its last keep-1 rows, into out [keep, cols]. Host only;
+ * SANA_ERR_INVALID with the reference's message in err when keep is not in (0, rows]. */
+int sana_select_rows_first_and_last(const float *in, size_t rows, size_t cols, size_t keep, float *out, char *err,
+                                    size_t err_len);
+
+/* The host tail of encode_prompt_pair (gemma_encoder.h:50-55, gemma_encoder.cpp:188-244),
+ * after the encoder produced its hidden states: negative [max_seq, hidden] (the negative
+ * prompt padded straight to max_seq, negative_real real tokens) and positive
+ * [positive_rows, hidden] (instruction prefix + prompt padded to positive_rows,
+ * positive_real real tokens) -> embeddings [2, max_seq, hidden] negative first, the positive
+ * branch sliced to row 0 plus its last max_seq-1 rows, and bias [2, 1, max_seq] =
+ * (1 - mask) * -10000 over the real tokens kept. Host only; the reference's
+ * std::invalid_argument cases return SANA_ERR_INVALID with its message in err. */
+int sana_prompt_pair_assemble(const float *negative, size_t negative_rows, size_t negative_real,
+                              const float *positive, size_t positive_rows, size_t positive_real, size_t hidden,
+                              size_t max_sequence_length, float *embeddings, float *bias, char *err,
+                              size_t err_len);
+
+/* The same for `pairs` (1..64) prompt pairs on the device, one launch on the handle's stream:
+ * negative [pairs, L, hidden] and positive [pairs, positive_rows, hidden] fp32 device
+ * buffers, real-token counts in host arrays negative_real[pairs] / positive_real[pairs] ->
+ * enc [2 * pairs, L, hidden] (all negative branches first, the denoiser's batch order) and
+ * bias [2 * pairs, 1, L], ready for sana_cuda_denoise_loop_device. */
+int sana_cuda_prompt_pairs_device(sana_cuda_ctx *ctx, int pairs, const float *negative, const int *negative_real,
+                                  const float *positive, int positive_rows, const int *positive_real, int hidden,
+                                  int L, float *enc, float *bias);
+
 #ifdef __cplusplus
 }
 #endif

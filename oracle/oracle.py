@@ -306,6 +306,25 @@ class _CpuModel:
 
 
 class Oracle(_Cpu):
+    # -- text-encoder output contract (gemma_encoder.cpp:51-77,177-244) -----------------
+    def select_rows_first_and_last(self, x, keep):
+        x = _f32(x)
+        rows, cols = x.shape
+        out = np.empty((keep, cols), np.float32)
+        self._call("select_rows_first_and_last", _ptr(x), _sz(rows), _sz(cols), _sz(keep), _ptr(out))
+        return out
+
+    def prompt_pair_assemble(self, negative, negative_real, positive, positive_real, max_sequence_length=300):
+        negative, positive = _f32(negative), _f32(positive)
+        L = max_sequence_length
+        hidden = positive.shape[1]
+        emb = np.empty((2, L, hidden), np.float32)
+        bias = np.empty((2, 1, L), np.float32)
+        self._call("prompt_pair_assemble", _ptr(negative), _sz(negative.shape[0]), _sz(negative_real), _ptr(positive),
+                   _sz(positive.shape[0]), _sz(positive_real), _sz(hidden), _sz(L), _ptr(emb), _ptr(bias))
+        return emb, bias
+
+
     prefix = "orc_"
     path = ORACLE_LIB
 

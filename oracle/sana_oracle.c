@@ -1097,3 +1097,49 @@ int orc_scheduler_step(const float *sigmas, size_t n_sigmas, size_t step_index, 
     free(conv);
     return rc;
 }
+
+/* ------------------------------------------------------------------------------------
+ * Text-encoder output contract (gemma_encoder.cpp), the conditioning the denoiser reads.
+ * ---------------------------------------------------------------------------------- */
+
+/* select_rows_first_and_last (gemma_encoder.cpp:51-77): row 0, then the last keep-1 rows. */
+int orc_select_rows_first_and_last(const float *in, size_t rows, size_t cols, size_t keep, float *out) {
+    if (keep == 0 || keep > rows) ORC_INVALID("select_rows_first_and_last: keep must be in (0, rows]");
+    memcpy(out, in, cols * sizeof(float));
+    const size_t tail = keep - 1;
+    memcpy(out + cols, in + (rows - tail) * cols, tail * cols * sizeof(float));
+    return 0;
+}
+
+/* write_attention_bias (gemma_encoder.cpp:177-184): 0 on real tokens, (1 - 0) * -10000 after. */
+static void orc_attention_bias_row(float *row, size_t real, size_t n) {
+    for (size_t t = 0; t < n; ++t) {
+        const float mask = t < real ? 1.0f : 0.0f;
+        row[t] = (1.0f - mask) * -10000.0f;
+    }
+}
+
+/* The tail of encode_prompt_pair (gemma_encoder.cpp:188-244), after the encoder ran:
+ * negative [max_seq, hidden] padded straight to max_seq with negative_real real tokens;
+ * positive [positive_rows, hidden] (instruction prefix + prompt, padded to positive_rows
+ * with positive_real real tokens) sliced to row 0 plus its last max_seq-1 rows. Output:
+ * embeddings [2, max_seq, hidden] negative first, bias [2, 1, max_seq]. The real-token
+ * count after the slice counts row 0 and every kept tail row below positive_real
+ * (gemma_encoder.cpp:205-215). */
+int orc_prompt_pair_assemble(const float *negative, size_t negative_rows, size_t negative_real,
+                             const float *positive, size_t positive_rows, size_t positive_real,
+                             size_t hidden, size_t max_sequence_length, float *embeddings, float *bias) {
+    const size_t L = max_sequence_length;
+    if (negative_rows != L) ORC_INVALID("negative branch must be padded to max_sequence_length");
+    if (negative_real > negative_rows || positive_real > positive_rows)
+        ORC_INVALID("tokenized text exceeds padded_length; truncation not implemented");
+    memcpy(embeddings, negative, L * hidden * sizeof(float));
+    const int rc = orc_select_rows_first_and_last(positive, positive_rows, hidden, L, embeddings + L * hidden);
+    if (rc) return rc;
+    size_t kept_real = positive_real > 0 ? 1 : 0;
+    for (size_t pos = positive_rows - (L - 1); pos < positive_rows; ++pos)
+        if (pos < positive_real) ++kept_real;
+    orc_attention_bias_row(bias, negative_real, L);
+    orc_attention_bias_row(bias + L, kept_real, L);
+    return 0;
+}

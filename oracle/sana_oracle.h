@@ -103,6 +103,12 @@ int orc_denoise(void *m, const float *latents, size_t B, size_t H, size_t W, con
                 size_t L, size_t Din, const float *bias, float guidance, size_t num_steps,
                 size_t run_steps, float *out, size_t *step_index_out);
 
+/* Text-encoder output contract (gemma_encoder.cpp). */
+int orc_select_rows_first_and_last(const float *in, size_t rows, size_t cols, size_t keep, float *out);
+int orc_prompt_pair_assemble(const float *negative, size_t negative_rows, size_t negative_real,
+                             const float *positive, size_t positive_rows, size_t positive_real,
+                             size_t hidden, size_t max_sequence_length, float *embeddings, float *bias);
+
 #ifdef __cplusplus
 }
 #endif

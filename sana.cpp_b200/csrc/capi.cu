@@ -1339,4 +1339,93 @@ int sana_randn_torch_cpu(float* out, size_t n, uint64_t seed) {
     return SANA_OK;
 }
 
+/* --- the text-encoder output contract (gemma_encoder.cpp:51-77,177-244) ---------------- */
+
+namespace {
+
+void write_err(char* err, size_t err_len, const char* msg) {
+    if (err && err_len) std::snprintf(err, err_len, "%s", msg);
+}
+
+// Real tokens the positive branch keeps after the row-0 + tail slice: row 0 when the branch
+// has any real token, plus every kept tail row below the real count (gemma_encoder.cpp:205-215).
+size_t kept_real_tokens(size_t positive_rows, size_t positive_real, size_t L) {
+    size_t kept = positive_real > 0 ? 1 : 0;
+    for (size_t pos = positive_rows - (L - 1); pos < positive_rows; ++pos)
+        if (pos < positive_real) ++kept;
+    return kept;
+}
+
+void check_prompt_pair(size_t negative_rows, size_t negative_real, size_t positive_rows, size_t positive_real,
+                       size_t hidden, size_t L) {
+    if (L == 0 || hidden == 0) throw std::invalid_argument("max_sequence_length and hidden must be positive");
+    if (negative_rows != L) throw std::invalid_argument("negative branch must be padded to max_sequence_length");
+    if (negative_real > negative_rows || positive_real > positive_rows)
+        throw std::invalid_argument("tokenized text exceeds padded_length; truncation not implemented");
+    if (L > positive_rows) throw std::invalid_argument("select_rows_first_and_last: keep must be in (0, rows]");
+}
+
+void attention_bias_row(float* row, size_t real, size_t L) {
+    for (size_t t = 0; t < L; ++t) {
+        const float mask = t < real ? 1.0f : 0.0f;
+        row[t] = (1.0f - mask) * -10000.0f;
+    }
+}
+
+}  // namespace
+
+int sana_select_rows_first_and_last(const float* in, size_t rows, size_t cols, size_t keep, float* out, char* err,
+                                    size_t err_len) {
+    if (!in || !out) return SANA_ERR_INVALID;
+    if (keep == 0 || keep > rows) {
+        write_err(err, err_len, "select_rows_first_and_last: keep must be in (0, rows]");
+        return SANA_ERR_INVALID;
+    }
+    std::memcpy(out, in, cols * sizeof(float));
+    std::memcpy(out + cols, in + (rows - (keep - 1)) * cols, (keep - 1) * cols * sizeof(float));
+    return SANA_OK;
+}
+
+int sana_prompt_pair_assemble(const float* negative, size_t negative_rows, size_t negative_real,
+                              const float* positive, size_t positive_rows, size_t positive_real, size_t hidden,
+                              size_t max_sequence_length, float* embeddings, float* bias, char* err,
+                              size_t err_len) {
+    if (!negative || !positive || !embeddings || !bias) return SANA_ERR_INVALID;
+    const size_t L = max_sequence_length;
+    try {
+        check_prompt_pair(negative_rows, negative_real, positive_rows, positive_real, hidden, L);
+    } catch (const std::invalid_argument& e) {
+        write_err(err, err_len, e.what());
+        return SANA_ERR_INVALID;
+    }
+    std::memcpy(embeddings, negative, L * hidden * sizeof(float));
+    sana_select_rows_first_and_last(positive, positive_rows, hidden, L, embeddings + L * hidden, nullptr, 0);
+    attention_bias_row(bias, negative_real, L);
+    attention_bias_row(bias + L, kept_real_tokens(positive_rows, positive_real, L), L);
+    return SANA_OK;
+}
+
+int sana_cuda_prompt_pairs_device(sana_cuda_ctx* ctx, int pairs, const float* negative, const int* negative_real,
+                                  const float* positive, int positive_rows, const int* positive_real, int hidden,
+                                  int L, float* enc, float* bias) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(negative && positive && negative_real && positive_real && enc && bias, "invalid arguments");
+        SANA_REQUIRE(pairs >= 1 && pairs <= sana::kMaxPromptPairs, "prompt pair count must be in [1, 64]");
+        SANA_REQUIRE(positive_rows >= 0 && hidden >= 0 && L >= 0, "invalid arguments");
+        sana::PromptPairCounts counts{};
+        for (int p = 0; p < pairs; ++p) {
+            SANA_REQUIRE(negative_real[p] >= 0 && positive_real[p] >= 0, "invalid arguments");
+            check_prompt_pair(static_cast<size_t>(L), static_cast<size_t>(negative_real[p]),
+                              static_cast<size_t>(positive_rows), static_cast<size_t>(positive_real[p]),
+                              static_cast<size_t>(hidden), static_cast<size_t>(L));
+            counts.real[p] = negative_real[p];
+            counts.real[pairs + p] = static_cast<int>(
+                kept_real_tokens(static_cast<size_t>(positive_rows), static_cast<size_t>(positive_real[p]),
+                                 static_cast<size_t>(L)));
+        }
+        sana::Engine& eng = engine(ctx);
+        sana::prompt_pairs(negative, positive, pairs, positive_rows, hidden, L, counts, enc, bias, eng.stream());
+    });
+}
+
 }  // extern "C"

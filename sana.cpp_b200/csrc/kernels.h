@@ -58,6 +58,17 @@ void softmax_rows(const float* in, long long rows, int n, float* out, cudaStream
 // reference does). Keys past it carry <= -1000 and contribute exactly 0 in fp32.
 void caption_kv_len(const float* bias, int S, int L, int* kv_len, cudaStream_t st);
 
+// Real-token count of each output sequence of prompt_pairs (negatives first).
+constexpr int kMaxPromptPairs = 64;
+struct PromptPairCounts {
+    int real[2 * kMaxPromptPairs];
+};
+// Text-encoder output contract (conditioning.cu): negative [pairs, L, hidden] and positive
+// [pairs, positive_rows, hidden] fp32 hidden states -> enc [2 * pairs, L, hidden] (negatives
+// first, positives sliced to row 0 + last L-1 rows) and bias [2 * pairs, 1, L].
+void prompt_pairs(const float* negative, const float* positive, int pairs, int positive_rows, int hidden, int L,
+                  const PromptPairCounts& counts, float* enc, float* bias, cudaStream_t st);
+
 // One fused classifier-free-guidance + DPM-Solver++ update (apply_classifier_free_guidance,
 // transformer.cpp:570-602; step_sana_scheduler, scheduler.cpp:272-318) on NCHW latents:
 //   guided = u + g (c - u) from token-major noise rows (uncond sequences first)

@@ -13,6 +13,8 @@ from .capi import (  # noqa: F401
     gguf_index,
     lib_path,
     load_library,
+    prompt_pair_assemble,
     randn_torch_cpu,
     scheduler_schedule,
+    select_rows_first_and_last,
 )

@@ -125,6 +125,46 @@ def gguf_index(path: str) -> dict:
         lib.sana_gguf_close(h)
 
 
+def _host_status(rc: int, err) -> None:
+    if rc == 1:
+        raise ValueError(err.value.decode())
+    if rc != 0:
+        raise SanaError(rc, err.value.decode())
+
+
+def select_rows_first_and_last(x, keep: int) -> np.ndarray:
+    """gemma_encoder.cpp:51-77 through the library: row 0 of x [rows, cols], then its last
+    keep-1 rows."""
+    x = _f32(x)
+    if x.ndim != 2:
+        raise ValueError("select_rows_first_and_last expects a rank-2 tensor")
+    rows, cols = x.shape
+    out = np.empty((max(int(keep), 0), cols), np.float32)
+    err = ctypes.create_string_buffer(256)
+    _host_status(load_library().sana_select_rows_first_and_last(
+        _ptr(x), ctypes.c_size_t(rows), ctypes.c_size_t(cols), ctypes.c_size_t(max(int(keep), 0)),
+        _ptr(out), err, 256), err)
+    return out
+
+
+def prompt_pair_assemble(negative, negative_real: int, positive, positive_real: int, max_sequence_length: int = 300):
+    """The tail of encode_prompt_pair (gemma_encoder.cpp:188-244) through the library:
+    (embeddings [2, L, hidden] negative first, bias [2, 1, L])."""
+    negative, positive = _f32(negative), _f32(positive)
+    L = int(max_sequence_length)
+    hidden = positive.shape[1]
+    if negative.ndim != 2 or positive.ndim != 2 or negative.shape[1] != hidden:
+        raise ValueError("negative and positive hidden states must be [rows, hidden] with the same hidden size")
+    emb = np.empty((2, L, hidden), np.float32)
+    bias = np.empty((2, 1, L), np.float32)
+    err = ctypes.create_string_buffer(256)
+    _host_status(load_library().sana_prompt_pair_assemble(
+        _ptr(negative), ctypes.c_size_t(negative.shape[0]), ctypes.c_size_t(negative_real), _ptr(positive),
+        ctypes.c_size_t(positive.shape[0]), ctypes.c_size_t(positive_real), ctypes.c_size_t(hidden),
+        ctypes.c_size_t(L), _ptr(emb), _ptr(bias), err, 256), err)
+    return emb, bias
+
+
 def gemm_counts():
     """(tensor-core GEMM launches, CUDA-core GEMM launches) in this process."""
     a, b = ctypes.c_longlong(0), ctypes.c_longlong(0)
@@ -237,6 +277,21 @@ class SanaCuda:
         for i in range(nb):
             blocks += block_tensor_table(tensors[16 + 19 * i: 16 + 19 * (i + 1)])
         self.upload(dims, tensors[:16], blocks, SANA_LAYOUT_TORCH)
+
+    def prompt_pairs_device(self, negative, negative_real, positive, positive_real, L: int = 300):
+        """sana_cuda_prompt_pairs_device on torch CUDA tensors: negative [pairs, L, hidden],
+        positive [pairs, positive_rows, hidden] fp32 -> (enc [2 * pairs, L, hidden],
+        bias [2 * pairs, 1, L]) on the device, negatives first."""
+        import torch
+        pairs, rows, hidden = positive.shape
+        nr = (_i * pairs)(*[int(v) for v in negative_real])
+        pr = (_i * pairs)(*[int(v) for v in positive_real])
+        enc = torch.empty((2 * pairs, L, hidden), dtype=torch.float32, device=positive.device)
+        bias = torch.empty((2 * pairs, 1, L), dtype=torch.float32, device=positive.device)
+        self._call("sana_cuda_prompt_pairs_device", _i(pairs), ctypes.c_void_p(negative.data_ptr()), nr,
+                   ctypes.c_void_p(positive.data_ptr()), _i(rows), pr, _i(hidden), _i(L),
+                   ctypes.c_void_p(enc.data_ptr()), ctypes.c_void_p(bias.data_ptr()))
+        return enc, bias
 
     def upload_gguf(self, model_path: str, caption_path: str, denoiser_path: str, self_heads: int = 36,
                     cross_heads: int = 16):

@@ -220,6 +220,31 @@ ALL_KATS = [kat_layer_norm, kat_rms_norm, kat_modulate, kat_conv1x1, kat_depthwi
             kat_cross_attention_block, kat_block_forward, kat_scheduler]
 
 
+def kat_select_rows_first_and_last(impl):
+    # test_gemma_encoder.cpp:10-33: a 10x2 ramp; keep 4 -> rows 0, 7, 8, 9; keep 10 -> all; keep 1 -> row 0
+    x = np.arange(20, dtype=F).reshape(10, 2)
+    return [("keep4", impl.select_rows_first_and_last(x, 4), _a([[0, 1], [14, 15], [16, 17], [18, 19]]), 0.0),
+            ("keep10", impl.select_rows_first_and_last(x, 10), x, 0.0),
+            ("keep1", impl.select_rows_first_and_last(x, 1), _a([[0, 1]]), 0.0)]
+
+
+def kat_prompt_pair(impl):
+    # gemma_encoder.cpp:188-244 on a ramp: negative padded to L=4 with 2 real tokens; positive
+    # padded to 7 rows with 5 real tokens -> rows 0, 4, 5, 6; real after the slice: row 0 and
+    # row 4 -> bias (1 - mask) * -10000, -0.0 on real tokens
+    neg = np.arange(8, dtype=F).reshape(4, 2)
+    pos = 100 + np.arange(14, dtype=F).reshape(7, 2)
+    emb, bias = impl.prompt_pair_assemble(neg, 2, pos, 5, 4)
+    want = np.stack([neg, pos[[0, 4, 5, 6]]])
+    wb = _a([[[-0.0, -0.0, -10000, -10000]], [[-0.0, -0.0, -10000, -10000]]])
+    return [("embeddings", emb, want, 0.0), ("bias", bias, wb, 0.0),
+            ("bias_sign", np.signbit(bias).astype(F), np.ones_like(wb), 0.0)]
+
+
+# Host-side contract cases: the oracle and the library's host functions run them.
+ENCODER_KATS = [kat_select_rows_first_and_last, kat_prompt_pair]
+
+
 def check(results):
     """Asserts every (label, got, expected, tol) triple; tol 0 means bit-equal values."""
     for label, got, exp, tol in results:

@@ -5,6 +5,7 @@ launches a kernel."""
 import ctypes
 import os
 import re
+import types
 
 import numpy as np
 import pytest
@@ -88,3 +89,54 @@ def test_handle_errors_are_reported_without_a_device(lib):
     with pytest.raises(SanaError):
         SanaCuda(0)
     assert lib.sana_cuda_synchronize(None) == 1
+
+
+# --- the text-encoder output contract (host functions; gemma_encoder.cpp:51-77,177-244) ----
+
+@pytest.mark.parametrize("case", ["kat_select_rows_first_and_last", "kat_prompt_pair"])
+def test_encoder_contract_kats(case):
+    import kat_cases as K
+    import sana_b200
+    K.check(getattr(K, case)(sana_b200))
+
+
+@pytest.mark.parametrize("neg_real,pos_rows,pos_real,L", [
+    (8, 324, 40, 300),     # the encoder's shapes: 26-token instruction prefix + 300 - 2
+    (0, 300, 0, 300),      # empty prompts: no real token at all
+    (300, 300, 300, 300),  # every row real, no slice
+    (1, 9, 9, 3),          # tail fully real
+    (2, 12, 7, 5),         # real tokens end before the kept tail
+])
+def test_prompt_pair_matches_oracle(oracle, neg_real, pos_rows, pos_real, L):
+    from sana_b200 import prompt_pair_assemble
+    rng = np.random.default_rng(pos_rows * 7 + L)
+    hidden = 24
+    neg = rng.standard_normal((L, hidden)).astype(np.float32)
+    pos = rng.standard_normal((pos_rows, hidden)).astype(np.float32)
+    e1, b1 = prompt_pair_assemble(neg, neg_real, pos, pos_real, L)
+    e2, b2 = oracle.prompt_pair_assemble(neg, neg_real, pos, pos_real, L)
+    assert np.array_equal(e1.view(np.uint32), e2.view(np.uint32))
+    assert np.array_equal(b1.view(np.uint32), b2.view(np.uint32))
+    assert np.array_equal(e1[0], neg) and np.array_equal(e1[1, 0], pos[0])
+    assert np.array_equal(e1[1, 1:], pos[pos_rows - (L - 1):])
+
+
+@pytest.mark.parametrize("bad", ["keep0", "keep_gt_rows", "neg_rows", "neg_real", "pos_real", "pos_short"])
+def test_encoder_contract_errors(oracle, bad):
+    from sana_b200 import prompt_pair_assemble, select_rows_first_and_last
+    x = np.zeros((10, 2), np.float32)
+    neg, pos = np.zeros((4, 2), np.float32), np.zeros((7, 2), np.float32)
+    calls = {
+        "keep0": (lambda m: m.select_rows_first_and_last(x, 0), "keep must be in"),
+        "keep_gt_rows": (lambda m: m.select_rows_first_and_last(x, 11), "keep must be in"),
+        "neg_rows": (lambda m: m.prompt_pair_assemble(np.zeros((5, 2), np.float32), 1, pos, 1, 4), "padded"),
+        "neg_real": (lambda m: m.prompt_pair_assemble(neg, 5, pos, 1, 4), "exceeds padded_length"),
+        "pos_real": (lambda m: m.prompt_pair_assemble(neg, 1, pos, 8, 4), "exceeds padded_length"),
+        "pos_short": (lambda m: m.prompt_pair_assemble(neg, 1, pos[:3], 1, 4), "keep must be in"),
+    }
+    fn, msg = calls[bad]
+    lib = types.SimpleNamespace(select_rows_first_and_last=select_rows_first_and_last,
+                                prompt_pair_assemble=prompt_pair_assemble)
+    for impl in (lib, oracle):
+        with pytest.raises(ValueError, match=msg):
+            fn(impl)

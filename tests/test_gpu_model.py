@@ -203,6 +203,57 @@ def test_batched_loop_images_are_independent(full_gpu):
         assert cosine(batch[i], one[0]) > 0.9999
 
 
+@pytest.mark.parametrize("pairs,hidden,pos_rows,L", [(3, 2304, 324, 300), (2, 30, 12, 5), (1, 2304, 300, 300)])
+def test_prompt_pairs_device_matches_oracle(oracle, pairs, hidden, pos_rows, L):
+    """The encoder output contract assembled on the device equals the reference's host tail
+    (restated in the oracle) pair by pair, bit for bit, mask signs included."""
+    import torch
+    from sana_b200 import SANA_MODE_BF16, SanaCuda
+    g = SanaCuda(0, SANA_MODE_BF16)
+    rng = np.random.default_rng(pairs * 131 + hidden)
+    neg = rng.standard_normal((pairs, L, hidden)).astype(np.float32)
+    pos = rng.standard_normal((pairs, pos_rows, hidden)).astype(np.float32)
+    neg_real = [int(v) for v in rng.integers(0, L + 1, pairs)]
+    pos_real = [int(v) for v in rng.integers(0, pos_rows + 1, pairs)]
+    pos_real[0] = pos_rows
+    enc, bias = g.prompt_pairs_device(torch.from_numpy(neg).cuda(), neg_real, torch.from_numpy(pos).cuda(), pos_real, L)
+    torch.cuda.synchronize()
+    enc, bias = enc.cpu().numpy(), bias.cpu().numpy()
+    for p in range(pairs):
+        e, b = oracle.prompt_pair_assemble(neg[p], neg_real[p], pos[p], pos_real[p], L)
+        for half, row in ((0, p), (1, pairs + p)):
+            assert np.array_equal(enc[row].view(np.uint32), e[half].view(np.uint32))
+            assert np.array_equal(bias[row].view(np.uint32), b[half].view(np.uint32))
+    with pytest.raises(ValueError, match="exceeds padded_length"):
+        g.prompt_pairs_device(torch.from_numpy(neg).cuda(), [L + 1] * pairs, torch.from_numpy(pos).cuda(), pos_real, L)
+
+
+def test_loop_from_device_assembled_prompts(full_gpu, oracle):
+    """Two prompt pairs assembled on the device feed the device loop directly; the result
+    equals the host loop on the host-assembled conditioning (negatives first)."""
+    import torch
+    from sana_b200 import randn_torch_cpu
+    B, L, D, rows = 2, 300, 2304, 324
+    neg = randn_torch_cpu(B * L * D, 71).reshape(B, L, D)
+    pos = randn_torch_cpu(B * rows * D, 72).reshape(B, rows, D)
+    neg_real, pos_real = [9, 17], [60, 324]
+    lat = syn.latents(randn_torch_cpu, B, 32, 32, 32, 73)
+    enc_h = np.empty((2 * B, L, D), np.float32)
+    bias_h = np.empty((2 * B, 1, L), np.float32)
+    for p in range(B):
+        e, b = oracle.prompt_pair_assemble(neg[p], neg_real[p], pos[p], pos_real[p], L)
+        enc_h[p], enc_h[B + p], bias_h[p], bias_h[B + p] = e[0], e[1], b[0], b[1]
+    host = full_gpu.denoise_loop(lat, enc_h, bias_h, 4.5, 3)
+    enc_d, bias_d = full_gpu.prompt_pairs_device(torch.from_numpy(neg).cuda(), neg_real, torch.from_numpy(pos).cuda(),
+                                                 pos_real, L)
+    lat_d = torch.from_numpy(lat).cuda()
+    out_d = torch.empty_like(lat_d)
+    full_gpu.denoise_loop_device(lat_d.data_ptr(), B, 32, 32, enc_d.data_ptr(), L, D, bias_d.data_ptr(),
+                                 out_d.data_ptr(), 4.5, 3)
+    torch.cuda.synchronize()
+    assert np.array_equal(out_d.cpu().numpy(), host)
+
+
 def test_highres_step_is_finite_and_consistent(full_gpu):
     """Config 3 (64 x 64 latent, 4096 tokens): one step through the loop API and through
     the single-step API agree."""
