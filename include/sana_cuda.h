@@ -360,6 +360,44 @@ int sana_cuda_prompt_pairs_device(sana_cuda_ctx *ctx, int pairs, const float *ne
                                   const float *positive, int positive_rows, const int *positive_real, int hidden,
                                   int L, float *enc, float *bias);
 
+/* --- the VAE decoder (vae.h:11-92, vae.cpp:243-325, vae_ops.cpp) ---------------------------- */
+
+/* The decoder's structure, mirroring SanaVaeWeights (vae.h:43-73): up block i has `channels`
+ * outputs, an optional nearest-2x upsample conv from block i+1's channels (every block but
+ * the innermost), then `layers` ResBlocks (is_res_block) or attention + GLUMBConv layers.
+ * head_dim is the attention head size (32, run_vae_decode's value, vae.cpp:292); ms_kernel
+ * the multiscale depthwise size (proj_in's 3 or 5); scaling_factor divides the latents first
+ * (0.41407 for Sana, infer_main.cpp:369-374). */
+typedef struct sana_vae_block {
+    int channels, has_upsample, is_res_block, layers;
+} sana_vae_block;
+typedef struct sana_vae_dims {
+    int latent_channels, out_channels, n_blocks, head_dim, ms_kernel;
+    float scaling_factor;
+    sana_vae_block blocks[8];
+} sana_vae_dims;
+
+/* load_vae_weights (vae.cpp:147-170) from host fp32 tensors in PyTorch layouts, in order:
+ *   conv_in.w [C_{n-1}, latent, 3, 3], conv_in.b, norm_out.w [C_0], norm_out.b,
+ *   conv_out.w [out, C_0, 3, 3], conv_out.b; then per up block i = 0..n-1:
+ *   [upsample conv.w [C_i, C_{i+1}, 3, 3], conv.b] when it has one;
+ *   per ResBlock: conv1.w [C, C, 3, 3], conv1.b, conv2.w, norm.w, norm.b;
+ *   per attention layer: to_q.w [C, C], to_k.w, to_v.w, proj_in.w [3C, 1, k, k],
+ *   proj_out.w [3C, head_dim, 1, 1], to_out.w [C, 2C], norm_out.w, norm_out.b,
+ *   conv_inverted.w [8C, C, 1, 1], conv_inverted.b, conv_depth.w [8C, 1, 3, 3],
+ *   conv_depth.b, conv_point.w [C, 4C, 1, 1], norm.w, norm.b.
+ * Shape errors of validate_vae_weights (vae.cpp:172-208) are SANA_ERR_INVALID. */
+int sana_cuda_vae_upload(sana_cuda_ctx *ctx, const sana_vae_dims *dims, const float *const *tensors);
+
+/* run_vae_decode (vae.cpp:243-325): latents [B, latent, h, w] fp32 NCHW (host) -> image
+ * [B, out, h * 2^u, w * 2^u] fp32 NCHW (host), u = the number of upsampling blocks (5 for
+ * DC-AE f32c32: 32x32 latents give a 1024x1024 image). */
+int sana_cuda_vae_decode(sana_cuda_ctx *ctx, const float *latents, int B, int h, int w, float *out);
+/* The same with device pointers, asynchronous on the handle's stream. */
+int sana_cuda_vae_decode_device(sana_cuda_ctx *ctx, const float *latents, int B, int h, int w, float *out);
+/* Kernel and GEMM launches of the last decode on this handle. */
+int sana_cuda_vae_last_launch_count(const sana_cuda_ctx *ctx);
+
 #ifdef __cplusplus
 }
 #endif

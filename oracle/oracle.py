@@ -62,6 +62,20 @@ class _Cpu:
                 raise ValueError(msg)
             raise CheckerError(msg)
 
+    # -- VAE decoder (vae.cpp:243 run_vae_decode) ---------------------------------------
+    def vae_decode(self, dims, tensors, latents):
+        """dims: sana_b200.synthetic_vae.VaeDims; tensors in its upload order."""
+        from sana_b200.synthetic_vae import dims_struct
+        lat = _f32(latents)
+        B, _, h, w = lat.shape
+        ds = dims_struct(dims)
+        arrs = [_f32(t) for t in tensors]
+        table = (ctypes.c_void_p * len(arrs))(*[a.ctypes.data for a in arrs])
+        up = dims.upscale()
+        out = np.empty((B, dims.out_channels, h * up, w * up), np.float32)
+        self._call("vae_decode", ctypes.byref(ds), table, _ptr(lat), _sz(B), _sz(h), _sz(w), _ptr(out))
+        return out
+
     # -- primitives -------------------------------------------------------------------
     def randn(self, n: int, seed: int) -> np.ndarray:
         out = np.empty(n, np.float32)

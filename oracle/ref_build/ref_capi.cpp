@@ -13,6 +13,8 @@
 #include "torch_rng.h"
 #include "transformer.h"
 #include "transformer_ops.h"
+#include "vae.h"
+#include "vae_ops.h"
 
 #include <algorithm>
 #include <cmath>
@@ -518,6 +520,72 @@ int ref_scheduler_step(const float * sigmas, size_t n_sigmas, size_t step_index,
         }
         *n_hist_out = st.previous_model_outputs.size();
         *lower_out = st.lower_order_step_count;
+    });
+}
+
+// vae.cpp:243 run_vae_decode on SanaVaeWeights built from a pointer table: the same
+// dims struct and tensor order as the oracle's orc_vae_decode (PyTorch layouts; the
+// attention projections go through linear_weight_to_conv1x1 as load_vae_attention_weights
+// does, vae.cpp:26-41).
+struct ref_vae_block {
+    int channels, has_upsample, is_res_block, layers;
+};
+struct ref_vae_dims {
+    int latent_channels, out_channels, n_blocks, head_dim, ms_kernel;
+    float scaling_factor;
+    ref_vae_block blocks[8];
+};
+
+int ref_vae_decode(const ref_vae_dims * d, const float * const * t, const float * latents, size_t B, size_t h,
+                   size_t w, float * out) {
+    return guarded([&] {
+        const size_t n = static_cast<size_t>(d->n_blocks);
+        auto C = [&](size_t i) { return static_cast<size_t>(d->blocks[i].channels); };
+        const size_t Cl = static_cast<size_t>(d->latent_channels), Co = static_cast<size_t>(d->out_channels);
+        const size_t k = static_cast<size_t>(d->ms_kernel), hd = static_cast<size_t>(d->head_dim);
+        size_t j = 0;
+        SanaVaeDecoderWeights dec{
+            from_ptr(t[0], {C(n - 1), Cl, 3, 3}), from_ptr(t[1], {C(n - 1)}),
+            from_ptr(t[2], {C(0)}), from_ptr(t[3], {C(0)}),
+            from_ptr(t[4], {Co, C(0), 3, 3}), from_ptr(t[5], {Co}), {}};
+        j = 6;
+        for (size_t i = 0; i < n; ++i) {
+            const ref_vae_block & b = d->blocks[i];
+            const size_t c = C(i);
+            SanaVaeUpBlockWeights ub;
+            if (b.has_upsample) {
+                ub.upsample_conv_weight = from_ptr(t[j], {c, C(i + 1), 3, 3});
+                ub.upsample_conv_bias = from_ptr(t[j + 1], {c});
+                j += 2;
+            }
+            ub.is_res_block = b.is_res_block != 0;
+            for (int l = 0; l < b.layers; ++l) {
+                if (b.is_res_block) {
+                    ub.res_blocks.push_back(SanaVaeResBlockWeights{
+                        from_ptr(t[j], {c, c, 3, 3}), from_ptr(t[j + 1], {c}), from_ptr(t[j + 2], {c, c, 3, 3}),
+                        from_ptr(t[j + 3], {c}), from_ptr(t[j + 4], {c})});
+                    j += 5;
+                } else {
+                    SanaVaeAttentionWeights a{
+                        linear_weight_to_conv1x1(from_ptr(t[j], {c, c})),
+                        linear_weight_to_conv1x1(from_ptr(t[j + 1], {c, c})),
+                        linear_weight_to_conv1x1(from_ptr(t[j + 2], {c, c})),
+                        from_ptr(t[j + 3], {3 * c, 1, k, k}),
+                        from_ptr(t[j + 4], {3 * c, hd, 1, 1}),
+                        linear_weight_to_conv1x1(from_ptr(t[j + 5], {c, 2 * c})),
+                        from_ptr(t[j + 6], {c}), from_ptr(t[j + 7], {c})};
+                    SanaVaeGlumbConvWeights g{
+                        from_ptr(t[j + 8], {8 * c, c, 1, 1}), from_ptr(t[j + 9], {8 * c}),
+                        from_ptr(t[j + 10], {8 * c, 1, 3, 3}), from_ptr(t[j + 11], {8 * c}),
+                        from_ptr(t[j + 12], {c, 4 * c, 1, 1}), from_ptr(t[j + 13], {c}), from_ptr(t[j + 14], {c})};
+                    ub.attn_glumb_layers.push_back(SanaVaeAttnGlumbLayerWeights{std::move(a), std::move(g)});
+                    j += 15;
+                }
+            }
+            dec.up_blocks.push_back(std::move(ub));
+        }
+        SanaVaeWeights vw{std::move(dec), d->scaling_factor, 32};
+        to_ptr(run_vae_decode(from_ptr(latents, {B, Cl, h, w}), vw), out);
     });
 }
 

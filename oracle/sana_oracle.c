@@ -1143,3 +1143,286 @@ int orc_prompt_pair_assemble(const float *negative, size_t negative_rows, size_t
     orc_attention_bias_row(bias + L, kept_real, L);
     return 0;
 }
+
+/* ------------------------------------------------------------------------------------
+ * VAE decoder (vae.cpp, vae_ops.cpp), NCHW fp32.
+ * ---------------------------------------------------------------------------------- */
+
+/* conv2d_same for odd k (vae_ops.cpp:203-231, :18-75): zero padding k/2,
+ * out[b,o,y,x] = bias[o] + sum_{c,ky,kx} w[o,c,ky,kx] x[b,c,y+ky-k/2,x+kx-k/2]. */
+static void vae_conv_same(const float *x, size_t B, size_t Cin, size_t H, size_t W, const float *w, size_t Cout,
+                          size_t k, const float *bias, float *out) {
+    const size_t S = H * W;
+    const long r = (long)k / 2;
+    const long long BO = (long long)(B * Cout);
+#pragma omp parallel for schedule(dynamic, 1) if (BO * (long long)(Cin * S * k * k) > 65536)
+    for (long long bo = 0; bo < BO; ++bo) {
+        const size_t b = (size_t)bo / Cout, oc = (size_t)bo % Cout;
+        float *o = out + (b * Cout + oc) * S;
+        for (size_t s = 0; s < S; ++s) o[s] = bias ? bias[oc] : 0.0f;
+        for (size_t c = 0; c < Cin; ++c) {
+            const float *xi = x + (b * Cin + c) * S;
+            for (size_t ky = 0; ky < k; ++ky) {
+                for (size_t kx = 0; kx < k; ++kx) {
+                    const float wv = w[((oc * Cin + c) * k + ky) * k + kx];
+                    const long dy = (long)ky - r, dx = (long)kx - r;
+                    for (size_t y = 0; y < H; ++y) {
+                        const long iy = (long)y + dy;
+                        if (iy < 0 || iy >= (long)H) continue;
+                        const long x0 = dx < 0 ? -dx : 0, x1 = dx > 0 ? (long)W - dx : (long)W;
+                        float *orow = o + y * W;
+                        const float *irow = xi + (size_t)iy * W;
+                        for (long xx = x0; xx < x1; ++xx) orow[xx] += wv * irow[xx + dx];
+                    }
+                }
+            }
+        }
+    }
+}
+
+/* depthwise_conv2d_same (vae_ops.cpp:233-258, common_ops.cpp:484-505,658-731): taps summed
+ * ky-major then kx, bias last. */
+static void vae_depthwise(const float *x, size_t B, size_t C, size_t H, size_t W, const float *w, size_t k,
+                          const float *bias, float *out) {
+    const long r = (long)k / 2;
+    const long long P = (long long)(B * C);
+#pragma omp parallel for schedule(static) if (P * (long long)(H * W * k * k) > 65536)
+    for (long long p = 0; p < P; ++p) {
+        const size_t c = (size_t)p % C;
+        const float *xi = x + (size_t)p * H * W;
+        float *o = out + (size_t)p * H * W;
+        for (size_t y = 0; y < H; ++y) {
+            for (size_t xx = 0; xx < W; ++xx) {
+                float sum = 0.0f;
+                for (size_t ky = 0; ky < k; ++ky) {
+                    for (size_t kx = 0; kx < k; ++kx) {
+                        const long iy = (long)y + (long)ky - r, ix = (long)xx + (long)kx - r;
+                        if (iy >= 0 && iy < (long)H && ix >= 0 && ix < (long)W)
+                            sum += xi[(size_t)iy * W + (size_t)ix] * w[(c * k + ky) * k + kx];
+                    }
+                }
+                if (bias) sum += bias[c];
+                o[y * W + xx] = sum;
+            }
+        }
+    }
+}
+
+/* grouped_conv2d_1x1 (vae_ops.cpp:267-326): group g maps its in_per_group input channels to
+ * its out_per_group output channels. */
+static void vae_grouped_1x1(const float *x, size_t B, size_t Cin, size_t S, const float *w, size_t Cout,
+                            size_t groups, float *out) {
+    const size_t ipg = Cin / groups, opg = Cout / groups;
+    const long long BO = (long long)(B * Cout);
+#pragma omp parallel for schedule(static) if (BO * (long long)(ipg * S) > 65536)
+    for (long long bo = 0; bo < BO; ++bo) {
+        const size_t b = (size_t)bo / Cout, oc = (size_t)bo % Cout, g = oc / opg;
+        float *o = out + (b * Cout + oc) * S;
+        for (size_t s = 0; s < S; ++s) o[s] = 0.0f;
+        for (size_t i = 0; i < ipg; ++i) {
+            const float wv = w[oc * ipg + i];
+            const float *xi = x + (b * Cin + g * ipg + i) * S;
+            for (size_t s = 0; s < S; ++s) o[s] += wv * xi[s];
+        }
+    }
+}
+
+/* rms_norm_4d_channelwise (vae_ops.cpp:495-575): per pixel over channels, fma-accumulated
+ * squares in channel order, inv = 1 / sqrt(mean + eps), out = x * inv * w (+ b). */
+static void vae_rms_channelwise(const float *x, size_t B, size_t C, size_t S, const float *w, const float *bias,
+                                float eps, float *out) {
+    float *inv = (float *)malloc(S * sizeof(float));
+    for (size_t b = 0; b < B; ++b) {
+        const float *xb = x + b * C * S;
+        float *ob = out + b * C * S;
+        for (size_t s = 0; s < S; ++s) inv[s] = 0.0f;
+        for (size_t c = 0; c < C; ++c)
+            for (size_t s = 0; s < S; ++s) inv[s] = fmaf(xb[c * S + s], xb[c * S + s], inv[s]);
+        const float inv_c = 1.0f / (float)C;
+        for (size_t s = 0; s < S; ++s) inv[s] = 1.0f / sqrtf(inv[s] * inv_c + eps);
+        for (size_t c = 0; c < C; ++c) {
+            for (size_t s = 0; s < S; ++s) {
+                float v = xb[c * S + s] * inv[s] * w[c];
+                if (bias) v += bias[c];
+                ob[c * S + s] = v;
+            }
+        }
+    }
+    free(inv);
+}
+
+/* run_vae_res_block (vae_ops.cpp:587-603). */
+static void vae_res_block(float *x, size_t B, size_t C, size_t H, size_t W, const float *const *t) {
+    const size_t n = B * C * H * W;
+    float *h = (float *)malloc(n * sizeof(float));
+    float *g = (float *)malloc(n * sizeof(float));
+    vae_conv_same(x, B, C, H, W, t[0], C, 3, t[1], h);
+    silu_inplace(h, n);
+    vae_conv_same(h, B, C, H, W, t[2], C, 3, NULL, g);
+    vae_rms_channelwise(g, B, C, H * W, t[3], t[4], 1e-5f, h);
+    for (size_t i = 0; i < n; ++i) x[i] = h[i] + x[i];
+    free(h);
+    free(g);
+}
+
+/* run_vae_multiscale_attention (vae_ops.cpp:630-808), head dim d: q, k, v 1x1 projections
+ * concatenated [q | k | v] per image, a depthwise k x k and grouped 1x1 multiscale branch,
+ * then per merged head g (the first 3*inner/(3d) from qkv, the rest from the branch) the
+ * channels [g*3d, g*3d + 3d) of its source read as q, k, v: ReLU linear attention
+ * out = (V [K;1]^T)-weighted q / (z . q + 1e-15), to_out 1x1, RMSNorm(+bias), residual. */
+static void vae_attention(float *x, size_t B, size_t C, size_t H, size_t W, size_t d, size_t kms,
+                          const float *const *t) {
+    const size_t S = H * W, inner = C, heads = inner / d, C3 = 3 * inner;
+    float *qkv = (float *)malloc(B * C3 * S * sizeof(float));
+    float *tmp = (float *)malloc(B * C3 * S * sizeof(float));
+    float *ms = (float *)malloc(B * C3 * S * sizeof(float));
+    float *merged = (float *)malloc(B * 2 * inner * S * sizeof(float));
+    for (size_t b = 0; b < B; ++b) {
+        for (int j = 0; j < 3; ++j)
+            orc_conv1x1(x + b * C * S, 1, C, H, W, t[j], NULL, inner, qkv + (b * C3 + (size_t)j * inner) * S);
+    }
+    vae_depthwise(qkv, B, C3, H, W, t[3], kms, NULL, tmp);
+    vae_grouped_1x1(tmp, B, C3, S, t[4], C3, 3 * heads, ms);
+    const long long BG = (long long)(B * 2 * heads);
+#pragma omp parallel for schedule(dynamic, 1)
+    for (long long bg = 0; bg < BG; ++bg) {
+        const size_t b = (size_t)bg / (2 * heads), g = (size_t)bg % (2 * heads);
+        const float *src = (g < heads ? qkv : ms) + b * C3 * S + (g % heads) * 3 * d * S;
+        const float *q = src, *k = src + d * S, *v = src + 2 * d * S;
+        float *sc = (float *)malloc((d + 1) * d * sizeof(float));
+        for (size_t i = 0; i <= d; ++i) {
+            for (size_t j = 0; j < d; ++j) {
+                float acc = 0.0f;
+                for (size_t s = 0; s < S; ++s) {
+                    const float kv = k[j * S + s] > 0.0f ? k[j * S + s] : 0.0f;
+                    acc += (i < d ? v[i * S + s] : 1.0f) * kv;
+                }
+                sc[i * d + j] = acc;
+            }
+        }
+        float *o = merged + (b * 2 * heads + g) * d * S;
+        for (size_t s = 0; s < S; ++s) {
+            float den = 0.0f;
+            for (size_t j = 0; j < d; ++j) den += sc[d * d + j] * (q[j * S + s] > 0.0f ? q[j * S + s] : 0.0f);
+            den += 1e-15f;
+            for (size_t i = 0; i < d; ++i) {
+                float acc = 0.0f;
+                for (size_t j = 0; j < d; ++j) acc += sc[i * d + j] * (q[j * S + s] > 0.0f ? q[j * S + s] : 0.0f);
+                o[i * S + s] = acc / den;
+            }
+        }
+        free(sc);
+    }
+    float *h = tmp;
+    orc_conv1x1(merged, B, 2 * inner, H, W, t[5], NULL, C, h);
+    vae_rms_channelwise(h, B, C, S, t[6], t[7], 1e-5f, ms);
+    for (size_t i = 0; i < B * C * S; ++i) x[i] = ms[i] + x[i];
+    free(qkv);
+    free(tmp);
+    free(ms);
+    free(merged);
+}
+
+/* run_vae_glumb_conv (vae_ops.cpp:605-628): glumb_conv, RMSNorm(+bias), residual. */
+static void vae_glumb(float *x, size_t B, size_t C, size_t H, size_t W, const float *const *t) {
+    const size_t n = B * C * H * W;
+    float *h = (float *)malloc(n * sizeof(float));
+    float *g = (float *)malloc(n * sizeof(float));
+    orc_glumb_conv(x, B, C, H, W, t[0], t[1], 8 * C, t[2], t[3], t[4], C, h);
+    vae_rms_channelwise(h, B, C, H * W, t[5], t[6], 1e-5f, g);
+    for (size_t i = 0; i < n; ++i) x[i] = g[i] + x[i];
+    free(h);
+    free(g);
+}
+
+/* run_vae_upsample_block with shortcut (vae_ops.cpp:810-821, :338-453): nearest 2x, conv,
+ * then up[b,oc,2y+i,2x+j] += x[b, (4 oc + 2i + j) / repeats, y, x], repeats = 4 Cout / Cin. */
+static float *vae_upsample(const float *x, size_t B, size_t Cin, size_t H, size_t W, const float *w,
+                           const float *bias, size_t Cout) {
+    const size_t H2 = 2 * H, W2 = 2 * W;
+    float *up = (float *)malloc(B * Cin * H2 * W2 * sizeof(float));
+    for (size_t p = 0; p < B * Cin; ++p)
+        for (size_t y = 0; y < H2; ++y)
+            for (size_t xx = 0; xx < W2; ++xx) up[(p * H2 + y) * W2 + xx] = x[(p * H + y / 2) * W + xx / 2];
+    float *out = (float *)malloc(B * Cout * H2 * W2 * sizeof(float));
+    vae_conv_same(up, B, Cin, H2, W2, w, Cout, 3, bias, out);
+    free(up);
+    const size_t rep = 4 * Cout / Cin;
+    for (size_t b = 0; b < B; ++b)
+        for (size_t oc = 0; oc < Cout; ++oc)
+            for (size_t y = 0; y < H; ++y)
+                for (size_t xx = 0; xx < W; ++xx)
+                    for (size_t ij = 0; ij < 4; ++ij) {
+                        const size_t ic = (oc * 4 + ij) / rep;
+                        out[((b * Cout + oc) * H2 + 2 * y + ij / 2) * W2 + 2 * xx + ij % 2] +=
+                            x[((b * Cin + ic) * H + y) * W + xx];
+                    }
+    return out;
+}
+
+static size_t vae_block_tensors(const orc_vae_block *b) {
+    return (b->has_upsample ? 2u : 0u) + (size_t)b->layers * (b->is_res_block ? 5u : 15u);
+}
+
+size_t orc_vae_tensor_count(const orc_vae_dims *d) {
+    size_t n = 6;
+    for (int i = 0; i < d->n_blocks; ++i) n += vae_block_tensors(&d->blocks[i]);
+    return n;
+}
+
+int orc_vae_decode(const orc_vae_dims *d, const float *const *t, const float *latents, size_t B, size_t h,
+                   size_t w, float *out) {
+    if (d->n_blocks < 1 || d->n_blocks > 8) ORC_INVALID("vae decoder must contain at least one up block");
+    if (!(d->scaling_factor > 0.0f)) ORC_INVALID("vae scaling_factor must be positive");
+    const int n = d->n_blocks;
+    size_t first[9];
+    first[0] = 6;
+    for (int i = 0; i < n; ++i) first[i + 1] = first[i] + vae_block_tensors(&d->blocks[i]);
+    const size_t Cl = (size_t)d->latent_channels;
+    size_t C = (size_t)d->blocks[n - 1].channels, H = h, W = w;
+    if (C % Cl != 0) ORC_INVALID("vae decoder conv_in output channels must be divisible by latent channels");
+    /* conv_in on latents / scaling_factor, plus the repeated-channel shortcut (vae.cpp:210-241) */
+    const size_t nl = B * Cl * H * W;
+    float *scaled = (float *)malloc(nl * sizeof(float));
+    const float inv_sf = 1.0f / d->scaling_factor;
+    for (size_t i = 0; i < nl; ++i) scaled[i] = latents[i] * inv_sf;
+    float *x = (float *)malloc(B * C * H * W * sizeof(float));
+    vae_conv_same(scaled, B, Cl, H, W, t[0], C, 3, t[1], x);
+    const size_t rep = C / Cl;
+    for (size_t b = 0; b < B; ++b)
+        for (size_t c = 0; c < C; ++c)
+            for (size_t s = 0; s < H * W; ++s) x[(b * C + c) * H * W + s] += scaled[(b * Cl + c / rep) * H * W + s];
+    free(scaled);
+    for (int i = n - 1; i >= 0; --i) {
+        const orc_vae_block *blk = &d->blocks[i];
+        const float *const *bt = t + first[i];
+        if (blk->has_upsample) {
+            float *up = vae_upsample(x, B, C, H, W, bt[0], bt[1], (size_t)blk->channels);
+            free(x);
+            x = up;
+            C = (size_t)blk->channels;
+            H *= 2;
+            W *= 2;
+            bt += 2;
+        }
+        if (C != (size_t)blk->channels) ORC_INVALID("vae up block channels must match its input");
+        for (int l = 0; l < blk->layers; ++l) {
+            if (blk->is_res_block) {
+                vae_res_block(x, B, C, H, W, bt);
+                bt += 5;
+            } else {
+                vae_attention(x, B, C, H, W, (size_t)d->head_dim, (size_t)d->ms_kernel, bt);
+                vae_glumb(x, B, C, H, W, bt + 8);
+                bt += 15;
+            }
+        }
+    }
+    /* norm_out (+bias), ReLU, conv_out (vae.cpp:313-324) */
+    float *y = (float *)malloc(B * C * H * W * sizeof(float));
+    vae_rms_channelwise(x, B, C, H * W, t[2], t[3], 1e-5f, y);
+    for (size_t i = 0; i < B * C * H * W; ++i) y[i] = y[i] > 0.0f ? y[i] : 0.0f;
+    vae_conv_same(y, B, C, H, W, t[4], (size_t)d->out_channels, 3, t[5], out);
+    free(x);
+    free(y);
+    return 0;
+}

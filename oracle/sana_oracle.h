@@ -109,6 +109,32 @@ int orc_prompt_pair_assemble(const float *negative, size_t negative_rows, size_t
                              const float *positive, size_t positive_rows, size_t positive_real,
                              size_t hidden, size_t max_sequence_length, float *embeddings, float *bias);
 
+/* VAE decoder (vae.h, vae.cpp, vae_ops.cpp): the DC-AE decoder the reference runs after the
+ * denoiser. Up block i has `channels` output channels, an optional nearest-2x upsample conv
+ * (from the channels of block i+1; the innermost block has none), then `layers` ResBlocks
+ * or attention + GLUMBConv layers. Tensor table order (PyTorch layouts):
+ *   conv_in.w [C_{n-1}, latent, 3, 3], conv_in.b, norm_out.w [C_0], norm_out.b,
+ *   conv_out.w [out, C_0, 3, 3], conv_out.b; then per block i = 0..n-1:
+ *   [upsample conv.w [C_i, C_{i+1}, 3, 3], conv.b] if has_upsample;
+ *   per ResBlock: conv1.w, conv1.b, conv2.w, norm.w, norm.b;
+ *   per attention layer: to_q [C, C], to_k, to_v, proj_in [3C, 1, k, k], proj_out
+ *   [3C, head_dim, 1, 1], to_out [C, 2C], norm_out.w, norm_out.b, conv_inverted.w [8C, C, 1, 1],
+ *   conv_inverted.b, conv_depth.w [8C, 1, 3, 3], conv_depth.b, conv_point.w [C, 4C, 1, 1],
+ *   norm.w, norm.b. */
+typedef struct orc_vae_block {
+    int channels, has_upsample, is_res_block, layers;
+} orc_vae_block;
+typedef struct orc_vae_dims {
+    int latent_channels, out_channels, n_blocks, head_dim, ms_kernel;
+    float scaling_factor;
+    orc_vae_block blocks[8];
+} orc_vae_dims;
+size_t orc_vae_tensor_count(const orc_vae_dims *d);
+/* run_vae_decode (vae.cpp:243-325): latents [B, latent, h, w] -> out [B, out, h*2^u, w*2^u]
+ * with u the number of upsampling blocks. */
+int orc_vae_decode(const orc_vae_dims *d, const float *const *tensors, const float *latents, size_t B,
+                   size_t h, size_t w, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,10 +15,12 @@
 #include "engine.h"
 #include "gguf.h"
 #include "sana_cuda.h"
+#include "vae.h"
 
 struct sana_cuda_ctx {
     std::unique_ptr<sana::Engine> eng;
     std::string err;
+    std::unique_ptr<sana::VaeDecoder> vae;  // after eng: destroyed first
 };
 
 namespace {
@@ -1426,6 +1428,61 @@ int sana_cuda_prompt_pairs_device(sana_cuda_ctx* ctx, int pairs, const float* ne
         sana::Engine& eng = engine(ctx);
         sana::prompt_pairs(negative, positive, pairs, positive_rows, hidden, L, counts, enc, bias, eng.stream());
     });
+}
+
+/* --- the VAE decoder (vae.h, vae.cpp:243-325) ------------------------------------------- */
+
+namespace {
+
+sana::VaeDecoder& vae_of(sana_cuda_ctx* ctx) {
+    sana::Engine& eng = engine(ctx);
+    if (!ctx->vae) ctx->vae = std::make_unique<sana::VaeDecoder>(eng);
+    return *ctx->vae;
+}
+
+sana::VaeDims vae_dims_from(const sana_vae_dims* d) {
+    sana::VaeDims v;
+    v.latent_channels = d->latent_channels;
+    v.out_channels = d->out_channels;
+    v.n_blocks = d->n_blocks;
+    v.head_dim = d->head_dim;
+    v.ms_kernel = d->ms_kernel;
+    v.scaling_factor = d->scaling_factor;
+    SANA_REQUIRE(d->n_blocks >= 1 && d->n_blocks <= 8, "vae decoder must contain at least one up block");
+    for (int i = 0; i < d->n_blocks; ++i) {
+        v.blocks[i].channels = d->blocks[i].channels;
+        v.blocks[i].has_upsample = d->blocks[i].has_upsample;
+        v.blocks[i].is_res_block = d->blocks[i].is_res_block;
+        v.blocks[i].layers = d->blocks[i].layers;
+    }
+    return v;
+}
+
+}  // namespace
+
+int sana_cuda_vae_upload(sana_cuda_ctx* ctx, const sana_vae_dims* dims, const float* const* tensors) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(dims && tensors, "invalid arguments");
+        vae_of(ctx).upload(vae_dims_from(dims), tensors);
+    });
+}
+
+int sana_cuda_vae_decode(sana_cuda_ctx* ctx, const float* latents, int B, int h, int w, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(latents && out, "invalid arguments");
+        vae_of(ctx).decode_host(latents, B, h, w, out);
+    });
+}
+
+int sana_cuda_vae_decode_device(sana_cuda_ctx* ctx, const float* latents, int B, int h, int w, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(latents && out, "invalid arguments");
+        vae_of(ctx).decode(latents, B, h, w, out);
+    });
+}
+
+int sana_cuda_vae_last_launch_count(const sana_cuda_ctx* ctx) {
+    return (ctx && ctx->vae) ? ctx->vae->last_launches() : 0;
 }
 
 }  // extern "C"

@@ -1,0 +1,580 @@
+// The DC-AE VAE decoder on the device (vae.cpp:243-325, vae_ops.cpp). Activations are NHWC
+// rows [pixels, channels] in the engine's activation type (bf16, or fp32 in check mode).
+//
+//   conv_in (3x3 over latents / scaling_factor, + the repeated-channel shortcut)
+//   for each up block, innermost first:
+//     [nearest-2x upsample conv 3x3 + the pixel-shuffled channel shortcut]
+//     ResBlock:  x + RMSNorm(conv3x3(silu(conv3x3(x) + b)))
+//     or EfficientViT layer:
+//       x + RMSNorm(to_out(linear attention over qkv heads and the multiscale heads))
+//       x + RMSNorm(conv_point(dw3x3 GLU(silu(conv_inverted(x) + b))))
+//   RMSNorm(+bias), ReLU, conv_out 3x3 -> NCHW fp32
+//
+// 3x3 convolutions run as GEMMs over tap-major patches [pixels, 9 * Cin] (the upsample is
+// folded into the patch gather); weights are reordered to [Cout, 9, Cin] at upload. The
+// q/k/v projection rows are permuted at upload in groups of head_dim channels so that the
+// reference's reading of the concatenated [q | k | v] (head g takes channels
+// [3 g d, 3 g d + 3 d) as its q, k, v; vae_ops.cpp:686-714) becomes the plain
+// [q heads | k heads | v heads] layout of the linear-attention kernel; the multiscale
+// depthwise and grouped weights move with their channels.
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <type_traits>
+
+#include "vae.h"
+
+namespace sana {
+
+namespace {
+
+inline int blocks_for(long long n, int threads = 256) { return static_cast<int>((n + threads - 1) / threads); }
+
+// conv_in: 3x3 "same" over latents * inv_sf (NCHW fp32), + bias, + the repeated-channel
+// shortcut out[c] += scaled[c / (C / Cl)] (vae.cpp:210-241, vae_ops.cpp:455-493).
+// w: [C, 9, Cl] fp32. out: NHWC [B*H*W, C].
+template <class T>
+__global__ void vae_conv_in_kernel(const float* __restrict__ lat, int B, int Cl, int H, int W,
+                                   const float* __restrict__ w, const float* __restrict__ bias, float inv_sf, int C,
+                                   T* __restrict__ out) {
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const long long n = static_cast<long long>(B) * H * W * C;
+    if (i >= n) return;
+    const int oc = static_cast<int>(i % C);
+    const long long p = i / C;
+    const int x = static_cast<int>(p % W);
+    const int y = static_cast<int>((p / W) % H);
+    const int b = static_cast<int>(p / (static_cast<long long>(W) * H));
+    const float* lb = lat + static_cast<long long>(b) * Cl * H * W;
+    const float* wo = w + static_cast<long long>(oc) * 9 * Cl;
+    float acc = bias[oc];
+    for (int tap = 0; tap < 9; ++tap) {
+        const int iy = y + tap / 3 - 1, ix = x + tap % 3 - 1;
+        if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;
+        for (int c = 0; c < Cl; ++c)
+            acc = fmaf(wo[tap * Cl + c], lb[(static_cast<long long>(c) * H + iy) * W + ix] * inv_sf, acc);
+    }
+    acc += lb[(static_cast<long long>(oc / (C / Cl)) * H + y) * W + x] * inv_sf;
+    out[i] = from_f<T>(acc);
+}
+
+// Tap-major 3x3 patches of an NHWC image for a "same" convolution at output size
+// (H << up) x (W << up): col[p, tap, c] = in at output pixel p shifted by the tap, read
+// through the nearest-2x upsample when up = 1, zero outside. V channels per thread.
+template <class T, int V>
+__global__ void im2col3x3_kernel(const T* __restrict__ in, int B, int H, int W, int C, int up,
+                                 T* __restrict__ col) {
+    const int Ho = H << up, Wo = W << up, CV = C / V;
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const long long n = static_cast<long long>(B) * Ho * Wo * 9 * CV;
+    if (i >= n) return;
+    const int cv = static_cast<int>(i % CV);
+    const long long r = i / CV;
+    const int tap = static_cast<int>(r % 9);
+    const long long p = r / 9;
+    const int x = static_cast<int>(p % Wo);
+    const int y = static_cast<int>((p / Wo) % Ho);
+    const int b = static_cast<int>(p / (static_cast<long long>(Wo) * Ho));
+    const int yy = y + tap / 3 - 1, xx = x + tap % 3 - 1;
+    using Vec = typename std::conditional<V * sizeof(T) == 16, uint4, T>::type;
+    Vec v;
+    if (yy < 0 || yy >= Ho || xx < 0 || xx >= Wo) {
+        if constexpr (V * sizeof(T) == 16) v = make_uint4(0u, 0u, 0u, 0u);
+        else v = from_f<T>(0.0f);
+    } else {
+        const long long src = ((static_cast<long long>(b) * H + (yy >> up)) * W + (xx >> up)) * C + cv * V;
+        v = *reinterpret_cast<const Vec*>(in + src);
+    }
+    *reinterpret_cast<Vec*>(col + i * V) = v;
+}
+
+// The upsample shortcut (vae_ops.cpp:392-453): out[b, 2y+i, 2x+j, oc] +=
+// in[b, y, x, (4 oc + 2 i + j) / (4 Cout / Cin)].
+template <class T>
+__global__ void up_shortcut_kernel(T* __restrict__ out, const T* __restrict__ in, int B, int H, int W, int Cin,
+                                   int Cout) {
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int Ho = 2 * H, Wo = 2 * W;
+    const long long n = static_cast<long long>(B) * Ho * Wo * Cout;
+    if (i >= n) return;
+    const int oc = static_cast<int>(i % Cout);
+    const long long p = i / Cout;
+    const int xo = static_cast<int>(p % Wo);
+    const int yo = static_cast<int>((p / Wo) % Ho);
+    const int b = static_cast<int>(p / (static_cast<long long>(Wo) * Ho));
+    const int rep = 4 * Cout / Cin;
+    const int ic = (4 * oc + 2 * (yo & 1) + (xo & 1)) / rep;
+    const float s = to_f(in[((static_cast<long long>(b) * H + (yo >> 1)) * W + (xo >> 1)) * Cin + ic]);
+    out[i] = from_f<T>(to_f(out[i]) + s);
+}
+
+// rms_norm_4d_channelwise (vae_ops.cpp:495-575) over each pixel row, then the residual
+// add (add_inplace) or ReLU (vae.cpp:313-319): out = x / sqrt(mean(x^2) + eps) * w + b
+// (+ resid | relu). One warp per row.
+template <class T>
+__global__ void rms_rows_kernel(const T* __restrict__ x, long long rows, int C, const float* __restrict__ w,
+                                const float* __restrict__ b, float eps, const T* __restrict__ resid, int relu,
+                                T* __restrict__ out) {
+    const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const T* xr = x + row * C;
+    float ss = 0.f;
+    for (int c = lane; c < C; c += 32) {
+        const float v = to_f(xr[c]);
+        ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.0f / sqrtf(ss * (1.0f / static_cast<float>(C)) + eps);
+    T* orow = out + row * C;
+    const T* rr = resid ? resid + row * C : nullptr;
+    for (int c = lane; c < C; c += 32) {
+        float v = to_f(xr[c]) * inv * w[c] + b[c];
+        if (rr) v += to_f(rr[c]);
+        if (relu) v = fmaxf(v, 0.0f);
+        orow[c] = from_f<T>(v);
+    }
+}
+
+// The multiscale branch (vae_ops.cpp:681-682): depthwise K x K (no bias) then the grouped
+// 1x1 over groups of 32 channels, fused per (8 x 8 pixel tile, group). qkv / out:
+// [pixels, C3] rows; dw [C3, K*K] and gw [C3, 32] fp32 (rows in the same permuted group
+// order as the qkv columns).
+constexpr int kMsTile = 8;
+template <class T, int K>
+__global__ void __launch_bounds__(256) ms_branch_kernel(const T* __restrict__ qkv, int B, int H, int W, int C3,
+                                                        const float* __restrict__ dw, const float* __restrict__ gw,
+                                                        T* __restrict__ out) {
+    constexpr int R = K / 2, HALO = kMsTile + K - 1;
+    __shared__ float s_in[HALO * HALO][33];
+    __shared__ float s_dw[kMsTile * kMsTile][33];
+    __shared__ float s_w[32][K * K];
+    __shared__ float s_g[32][33];
+    const int tiles_x = (W + kMsTile - 1) / kMsTile;
+    const int tx0 = (blockIdx.x % tiles_x) * kMsTile, ty0 = (blockIdx.x / tiles_x) * kMsTile;
+    const int g = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+    const long long img = static_cast<long long>(b) * H * W;
+    for (int i = tid; i < HALO * HALO * 32; i += blockDim.x) {
+        const int c = i & 31, pix = i >> 5, y = ty0 - R + pix / HALO, x = tx0 - R + pix % HALO;
+        float v = 0.f;
+        if (y >= 0 && y < H && x >= 0 && x < W) v = to_f(qkv[(img + static_cast<long long>(y) * W + x) * C3 + g * 32 + c]);
+        s_in[pix][c] = v;
+    }
+    for (int i = tid; i < 32 * K * K; i += blockDim.x) s_w[i / (K * K)][i % (K * K)] = dw[static_cast<long long>(g) * 32 * K * K + i];
+    for (int i = tid; i < 32 * 32; i += blockDim.x) s_g[i >> 5][i & 31] = gw[static_cast<long long>(g) * 32 * 32 + i];
+    __syncthreads();
+    for (int i = tid; i < kMsTile * kMsTile * 32; i += blockDim.x) {
+        const int c = i & 31, p = i >> 5, py = p / kMsTile, px = p % kMsTile;
+        float sum = 0.f;
+#pragma unroll
+        for (int ky = 0; ky < K; ++ky)
+#pragma unroll
+            for (int kx = 0; kx < K; ++kx) sum += s_in[(py + ky) * HALO + px + kx][c] * s_w[c][ky * K + kx];
+        s_dw[p][c] = sum;
+    }
+    __syncthreads();
+    for (int i = tid; i < kMsTile * kMsTile * 32; i += blockDim.x) {
+        const int o = i & 31, p = i >> 5, y = ty0 + p / kMsTile, x = tx0 + p % kMsTile;
+        if (y >= H || x >= W) continue;
+        float acc = 0.f;
+#pragma unroll 8
+        for (int k = 0; k < 32; ++k) acc += s_g[o][k] * s_dw[p][k];
+        out[(img + static_cast<long long>(y) * W + x) * C3 + g * 32 + o] = from_f<T>(acc);
+    }
+}
+
+// conv_out (vae.cpp:320-324): 3x3 "same" from NHWC rows [pixels, C] to NCHW fp32 with few
+// output channels (Co <= 4); one warp per output pixel. w: [Co, 9, C] fp32.
+template <class T>
+__global__ void vae_conv_out_kernel(const T* __restrict__ in, int B, int H, int W, int C,
+                                    const float* __restrict__ w, const float* __restrict__ bias, int Co,
+                                    float* __restrict__ out) {
+    const long long p = static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    const long long P = static_cast<long long>(B) * H * W;
+    if (p >= P) return;
+    const int x = static_cast<int>(p % W), y = static_cast<int>((p / W) % H);
+    const int b = static_cast<int>(p / (static_cast<long long>(W) * H));
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int tap = 0; tap < 9; ++tap) {
+        const int iy = y + tap / 3 - 1, ix = x + tap % 3 - 1;
+        if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;
+        const T* src = in + ((static_cast<long long>(b) * H + iy) * W + ix) * C;
+        for (int c = lane; c < C; c += 32) {
+            const float v = to_f(src[c]);
+#pragma unroll
+            for (int o = 0; o < 4; ++o)
+                if (o < Co) acc[o] = fmaf(w[(static_cast<long long>(o) * 9 + tap) * C + c], v, acc[o]);
+        }
+    }
+#pragma unroll
+    for (int o = 0; o < 4; ++o)
+#pragma unroll
+        for (int s = 16; s > 0; s >>= 1) acc[o] += __shfl_xor_sync(0xffffffffu, acc[o], s);
+    if (lane < Co) {
+        float v = acc[0];
+#pragma unroll
+        for (int o = 1; o < 4; ++o)
+            if (lane == o) v = acc[o];
+        out[((static_cast<long long>(b) * Co + lane) * H + y) * W + x] = v + bias[lane];
+    }
+}
+
+// --- host-side weight preparation -------------------------------------------------------
+
+uint16_t bf16_bits(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return static_cast<uint16_t>((u >> 16) | 0x40u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return static_cast<uint16_t>(u >> 16);
+}
+
+template <class T>
+void put(DevBuf& dst, const std::vector<float>& src) {
+    dst.ensure(src.size() * sizeof(T));
+    if (sizeof(T) == 4) {
+        SANA_CUDA(cudaMemcpy(dst.get(), src.data(), src.size() * 4, cudaMemcpyHostToDevice));
+    } else {
+        std::vector<uint16_t> h(src.size());
+        for (size_t i = 0; i < src.size(); ++i) h[i] = bf16_bits(src[i]);
+        SANA_CUDA(cudaMemcpy(dst.get(), h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+    }
+}
+
+std::vector<float> copy_of(const float* p, size_t n) { return std::vector<float>(p, p + n); }
+
+// [Cout, Cin, 3, 3] -> [Cout, 9, Cin]
+std::vector<float> tap_major(const float* w, int Cout, int Cin) {
+    std::vector<float> r(static_cast<size_t>(Cout) * 9 * Cin);
+    for (int o = 0; o < Cout; ++o)
+        for (int c = 0; c < Cin; ++c)
+            for (int t = 0; t < 9; ++t) r[(static_cast<size_t>(o) * 9 + t) * Cin + c] = w[(static_cast<size_t>(o) * Cin + c) * 9 + t];
+    return r;
+}
+
+// Row groups of the concatenated [q | k | v] (3 * heads groups of d rows) in the order
+// q-parts of every head, k-parts, v-parts: new group j takes old group 3 (j % heads) + j / heads.
+std::vector<float> permute_groups(const std::vector<float>& rows, int heads, int d, size_t row_len) {
+    std::vector<float> r(rows.size());
+    for (int j = 0; j < 3 * heads; ++j) {
+        const int old = 3 * (j % heads) + j / heads;
+        std::memcpy(&r[static_cast<size_t>(j) * d * row_len], &rows[static_cast<size_t>(old) * d * row_len],
+                    static_cast<size_t>(d) * row_len * sizeof(float));
+    }
+    return r;
+}
+
+template <class T>
+void launch_im2col(const T* in, int B, int H, int W, int C, int up, T* col, cudaStream_t st) {
+    constexpr int V = 16 / static_cast<int>(sizeof(T));
+    const long long pix = static_cast<long long>(B) * (H << up) * (W << up);
+    if (C % V == 0) {
+        im2col3x3_kernel<T, V><<<blocks_for(pix * 9 * (C / V)), 256, 0, st>>>(in, B, H, W, C, up, col);
+    } else {
+        im2col3x3_kernel<T, 1><<<blocks_for(pix * 9 * C), 256, 0, st>>>(in, B, H, W, C, up, col);
+    }
+    SANA_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+
+size_t vae_tensor_count(const VaeDims& d) {
+    size_t n = 6;
+    for (int i = 0; i < d.n_blocks; ++i) {
+        const VaeBlockDims& b = d.blocks[i];
+        n += (b.has_upsample ? 2 : 0) + static_cast<size_t>(b.layers) * (b.is_res_block ? 5 : 15);
+    }
+    return n;
+}
+
+void vae_validate(const VaeDims& d) {
+    if (d.n_blocks < 1 || d.n_blocks > 8) throw InvalidArg("vae decoder must contain at least one up block");
+    if (!(d.scaling_factor > 0.0f)) throw InvalidArg("vae scaling_factor must be positive");
+    if (d.latent_channels < 1 || d.out_channels < 1 || d.out_channels > 4)
+        throw InvalidArg("vae decoder latent channels must be positive and output channels in [1, 4]");
+    if (d.head_dim != 32) throw InvalidArg("vae attention head dim must be 32");
+    if (d.ms_kernel != 3 && d.ms_kernel != 5)
+        throw InvalidArg("depthwise_conv2d_same only supports 3x3 or 5x5 kernels");
+    const int Cin = d.blocks[d.n_blocks - 1].channels;
+    if (Cin % d.latent_channels != 0)
+        throw InvalidArg("vae decoder conv_in output channels must be divisible by latent channels");
+    for (int i = 0; i < d.n_blocks; ++i) {
+        const VaeBlockDims& b = d.blocks[i];
+        if (b.channels < 8 || b.channels % 8 != 0 || b.layers < 0)
+            throw InvalidArg("vae up block channels must be a positive multiple of 8");
+        if (b.has_upsample && i == d.n_blocks - 1) throw InvalidArg("the innermost vae up block has no upsample");
+        if (!b.has_upsample && i < d.n_blocks - 1)
+            throw InvalidArg("every vae up block but the innermost starts with an upsample");
+        if (b.has_upsample && (4 * b.channels) % d.blocks[i + 1].channels != 0)
+            throw InvalidArg("VAE upsample shortcut channel ratio is invalid");
+        if (!b.is_res_block && b.layers > 0 && b.channels % d.head_dim != 0)
+            throw InvalidArg("VAE attention inner_dim must be divisible by attention_head_dim");
+    }
+}
+
+void VaeDecoder::upload(const VaeDims& d, const float* const* tensors) {
+    vae_validate(d);
+    for (size_t i = 0; i < vae_tensor_count(d); ++i)
+        if (!tensors[i]) throw InvalidArg("vae weight table has a missing tensor");
+    d_ = d;
+    have_ = false;
+    if (eng_.mode() == kModeBf16) upload_impl<bf16>(tensors);
+    else upload_impl<float>(tensors);
+    SANA_CUDA(cudaDeviceSynchronize());
+    ws_key_ = -1;
+    have_ = true;
+}
+
+template <class T>
+void VaeDecoder::upload_impl(const float* const* t) {
+    const VaeDims& d = d_;
+    const int n = d.n_blocks, Cl = d.latent_channels, C0 = d.blocks[0].channels, Cn = d.blocks[n - 1].channels;
+    const int k = d.ms_kernel, hd = d.head_dim;
+    put<float>(cin_w_, tap_major(t[0], Cn, Cl));
+    put<float>(cin_b_, copy_of(t[1], Cn));
+    put<float>(nout_w_, copy_of(t[2], C0));
+    put<float>(nout_b_, copy_of(t[3], C0));
+    put<float>(cout_w_, tap_major(t[4], d.out_channels, C0));
+    put<float>(cout_b_, copy_of(t[5], d.out_channels));
+    blocks_.clear();
+    blocks_.resize(n);
+    size_t j = 6;
+    for (int i = 0; i < n; ++i) {
+        const VaeBlockDims& bd = d.blocks[i];
+        Block& blk = blocks_[i];
+        const int C = bd.channels;
+        const size_t CC = static_cast<size_t>(C);
+        if (bd.has_upsample) {
+            put<T>(blk.upw, tap_major(t[j], C, d.blocks[i + 1].channels));
+            put<float>(blk.upb, copy_of(t[j + 1], CC));
+            j += 2;
+        }
+        blk.layers.resize(bd.layers);
+        for (int l = 0; l < bd.layers; ++l) {
+            Layer& L = blk.layers[l];
+            if (bd.is_res_block) {
+                put<T>(L.c1w, tap_major(t[j], C, C));
+                put<float>(L.c1b, copy_of(t[j + 1], CC));
+                put<T>(L.c2w, tap_major(t[j + 2], C, C));
+                put<float>(L.n1w, copy_of(t[j + 3], CC));
+                put<float>(L.n1b, copy_of(t[j + 4], CC));
+                j += 5;
+            } else {
+                const int heads = C / hd;
+                std::vector<float> qkv(3 * CC * CC);
+                for (int m = 0; m < 3; ++m) std::memcpy(&qkv[m * CC * CC], t[j + m], CC * CC * sizeof(float));
+                put<T>(L.wqkv, permute_groups(qkv, heads, hd, CC));
+                put<float>(L.msdw, permute_groups(copy_of(t[j + 3], 3 * CC * k * k), heads, hd, static_cast<size_t>(k * k)));
+                put<float>(L.msgw, permute_groups(copy_of(t[j + 4], 3 * CC * hd), heads, hd, static_cast<size_t>(hd)));
+                put<T>(L.wout, copy_of(t[j + 5], CC * 2 * CC));
+                put<float>(L.n1w, copy_of(t[j + 6], CC));
+                put<float>(L.n1b, copy_of(t[j + 7], CC));
+                put<T>(L.winv, copy_of(t[j + 8], 8 * CC * CC));
+                put<float>(L.binv, copy_of(t[j + 9], 8 * CC));
+                put<float>(L.wdw, copy_of(t[j + 10], 8 * CC * 9));
+                put<float>(L.bdw, copy_of(t[j + 11], 8 * CC));
+                put<T>(L.wpt, copy_of(t[j + 12], CC * 4 * CC));
+                put<float>(L.n2w, copy_of(t[j + 13], CC));
+                put<float>(L.n2b, copy_of(t[j + 14], CC));
+                j += 15;
+            }
+        }
+    }
+}
+
+void VaeDecoder::ensure_workspace(int B, int h, int w) {
+    const long long key = (static_cast<long long>(B) << 40) ^ (static_cast<long long>(h) << 20) ^ w;
+    if (key == ws_key_) return;
+    const size_t as = eng_.mode() == kModeBf16 ? 2 : 4;
+    size_t x = 0, col = 0, qkv = 0, merged = 0, inv = 0, glu = 0, partial = 0;
+    long long H = h, W = w;
+    const int n = d_.n_blocks;
+    x = static_cast<size_t>(B) * H * W * d_.blocks[n - 1].channels;
+    for (int i = n - 1; i >= 0; --i) {
+        const VaeBlockDims& bd = d_.blocks[i];
+        const size_t C = static_cast<size_t>(bd.channels);
+        if (bd.has_upsample) {
+            H *= 2;
+            W *= 2;
+            col = std::max(col, static_cast<size_t>(B * H * W) * 9 * d_.blocks[i + 1].channels);
+        }
+        const size_t P = static_cast<size_t>(B * H * W);
+        x = std::max(x, P * C);
+        if (bd.layers == 0) continue;
+        if (bd.is_res_block) {
+            col = std::max(col, P * 9 * C);
+        } else {
+            qkv = std::max(qkv, P * 3 * C);
+            merged = std::max(merged, P * 2 * C);
+            inv = std::max(inv, P * 8 * C);
+            glu = std::max(glu, P * 4 * C);
+            const int heads = static_cast<int>(C) / d_.head_dim;
+            partial = std::max(partial, static_cast<size_t>(B) * heads * (linattn_chunks(static_cast<int>(H * W)) + 1) *
+                                            (d_.head_dim + 1) * d_.head_dim);
+        }
+    }
+    x_.ensure(x * as);
+    y_.ensure(x * as);
+    g_.ensure(x * as);
+    if (col) col_.ensure(col * as);
+    if (qkv) {
+        qkv_.ensure(qkv * as);
+        ms_.ensure(qkv * as);
+        merged_.ensure(merged * as);
+        inv_.ensure(inv * as);
+        glu_.ensure(glu * as);
+        partial_.ensure(partial * 4);
+    }
+    ws_key_ = key;
+}
+
+void VaeDecoder::decode(const float* lat_d, int B, int h, int w, float* out_d) {
+    if (!have_) throw std::runtime_error("vae weights not uploaded");
+    if (B < 1 || h < 1 || w < 1) throw InvalidArg("vae decode latents must be rank 4");
+    ensure_workspace(B, h, w);
+    launches_ = 0;
+    if (eng_.mode() == kModeBf16) decode_impl<bf16>(lat_d, B, h, w, out_d);
+    else decode_impl<float>(lat_d, B, h, w, out_d);
+}
+
+void VaeDecoder::decode_host(const float* lat, int B, int h, int w, float* out) {
+    if (!have_) throw std::runtime_error("vae weights not uploaded");
+    if (B < 1 || h < 1 || w < 1) throw InvalidArg("vae decode latents must be rank 4");
+    const int up = 1 << (d_.n_blocks - 1);
+    const size_t nin = static_cast<size_t>(B) * d_.latent_channels * h * w;
+    const size_t nout = static_cast<size_t>(B) * d_.out_channels * (h * up) * (w * up);
+    lat_in_.ensure(nin * 4);
+    img_out_.ensure(nout * 4);
+    const cudaStream_t st = eng_.stream();
+    SANA_CUDA(cudaMemcpyAsync(lat_in_.get(), lat, nin * 4, cudaMemcpyHostToDevice, st));
+    decode(lat_in_.as<float>(), B, h, w, img_out_.as<float>());
+    SANA_CUDA(cudaMemcpyAsync(out, img_out_.get(), nout * 4, cudaMemcpyDeviceToHost, st));
+    SANA_CUDA(cudaStreamSynchronize(st));
+    eng_.check_device_error();
+}
+
+template <class T>
+void VaeDecoder::gemm_rows(const T* A, long long M, int K, const DevBuf& w, const float* bias, int N, int act, T* out) {
+    GemmProblem p;
+    p.A = A;
+    p.lda = K;
+    p.B = w.get();
+    p.ldb = K;
+    p.M = static_cast<int>(M);
+    p.N = N;
+    p.K = K;
+    p.a_bf16 = p.b_bf16 = sizeof(T) == 2 ? 1 : 0;
+    p.ep.bias = bias;
+    p.ep.act = act;
+    p.ep.out = out;
+    p.ep.out_bf16 = sizeof(T) == 2 ? 1 : 0;
+    p.ep.ldo = N;
+    gemm(p, eng_.err(), eng_.stream(), eng_.num_sms());
+    ++launches_;
+}
+
+template <class T>
+void VaeDecoder::conv3x3(const T* in, int B, int H, int W, int Cin, bool upsample, const DevBuf& w, const float* bias,
+                         int Cout, int act, T* out) {
+    const int up = upsample ? 1 : 0;
+    T* col = col_.as<T>();
+    launch_im2col<T>(in, B, H, W, Cin, up, col, eng_.stream());
+    ++launches_;
+    const long long P = static_cast<long long>(B) * (H << up) * (W << up);
+    gemm_rows<T>(col, P, 9 * Cin, w, bias, Cout, act, out);
+}
+
+template <class T>
+void VaeDecoder::decode_impl(const float* lat_d, int B, int h, int w, float* out_d) {
+    const VaeDims& d = d_;
+    const cudaStream_t st = eng_.stream();
+    const int n = d.n_blocks;
+    int C = d.blocks[n - 1].channels, H = h, W = w;
+    T* x = x_.as<T>();
+    T* y = y_.as<T>();
+    T* g = g_.as<T>();
+    auto rms = [&](const T* src, long long rows, int Cc, const DevBuf& nw, const DevBuf& nb, const T* resid, int relu,
+                   T* dst) {
+        rms_rows_kernel<T><<<blocks_for(rows * 32, 256), 256, 0, st>>>(src, rows, Cc, nw.as<float>(), nb.as<float>(),
+                                                                       1e-5f, resid, relu, dst);
+        SANA_CUDA(cudaGetLastError());
+        ++launches_;
+    };
+    {
+        const long long nout = static_cast<long long>(B) * H * W * C;
+        vae_conv_in_kernel<T><<<blocks_for(nout), 256, 0, st>>>(lat_d, B, d.latent_channels, H, W, cin_w_.as<float>(),
+                                                               cin_b_.as<float>(), 1.0f / d.scaling_factor, C, x);
+        SANA_CUDA(cudaGetLastError());
+        ++launches_;
+    }
+    for (int i = n - 1; i >= 0; --i) {
+        const VaeBlockDims& bd = d.blocks[i];
+        Block& blk = blocks_[i];
+        if (bd.has_upsample) {
+            const int Cin = C;
+            C = bd.channels;
+            conv3x3<T>(x, B, H, W, Cin, true, blk.upw, blk.upb.as<float>(), C, kActNone, y);
+            const long long nout = static_cast<long long>(B) * (2 * H) * (2 * W) * C;
+            up_shortcut_kernel<T><<<blocks_for(nout), 256, 0, st>>>(y, x, B, H, W, Cin, C);
+            SANA_CUDA(cudaGetLastError());
+            ++launches_;
+            H *= 2;
+            W *= 2;
+            std::swap(x, y);
+        }
+        const long long P = static_cast<long long>(B) * H * W;
+        for (Layer& L : blk.layers) {
+            if (bd.is_res_block) {
+                conv3x3<T>(x, B, H, W, C, false, L.c1w, L.c1b.as<float>(), C, kActSilu, g);
+                conv3x3<T>(g, B, H, W, C, false, L.c2w, nullptr, C, kActNone, y);
+                rms(y, P, C, L.n1w, L.n1b, x, 0, g);
+                std::swap(x, g);
+            } else {
+                const int heads = C / d.head_dim;
+                T* qkv = qkv_.as<T>();
+                T* ms = ms_.as<T>();
+                T* merged = merged_.as<T>();
+                gemm_rows<T>(x, P, C, L.wqkv, nullptr, 3 * C, kActNone, qkv);
+                const dim3 grid(ceil_div(W, kMsTile) * ceil_div(H, kMsTile), 3 * heads, B);
+                if (d.ms_kernel == 5)
+                    ms_branch_kernel<T, 5><<<grid, 256, 0, st>>>(qkv, B, H, W, 3 * C, L.msdw.as<float>(),
+                                                                L.msgw.as<float>(), ms);
+                else
+                    ms_branch_kernel<T, 3><<<grid, 256, 0, st>>>(qkv, B, H, W, 3 * C, L.msdw.as<float>(),
+                                                                L.msgw.as<float>(), ms);
+                SANA_CUDA(cudaGetLastError());
+                ++launches_;
+                const int T_ = H * W;
+                linear_attention<T>(qkv, 3 * C, 0, qkv, 3 * C, C, 2 * C, B, T_, T_, heads, d.head_dim,
+                                    partial_.as<float>(), merged, 2 * C, st);
+                linear_attention<T>(ms, 3 * C, 0, ms, 3 * C, C, 2 * C, B, T_, T_, heads, d.head_dim,
+                                    partial_.as<float>(), merged + C, 2 * C, st);
+                launches_ += 4;
+                gemm_rows<T>(merged, P, 2 * C, L.wout, nullptr, C, kActNone, y);
+                rms(y, P, C, L.n1w, L.n1b, x, 0, g);
+                std::swap(x, g);
+                // GLUMBConv
+                T* inv = inv_.as<T>();
+                T* glu = glu_.as<T>();
+                gemm_rows<T>(x, P, C, L.winv, L.binv.as<float>(), 8 * C, kActSilu, inv);
+                depthwise_glu<T>(inv, 8 * C, B, H, W, 8 * C, L.wdw.as<float>(), L.bdw.as<float>(), glu, 4 * C,
+                                 eng_.err(), st);
+                ++launches_;
+                gemm_rows<T>(glu, P, 4 * C, L.wpt, nullptr, C, kActNone, y);
+                rms(y, P, C, L.n2w, L.n2b, x, 0, g);
+                std::swap(x, g);
+            }
+        }
+    }
+    const long long P = static_cast<long long>(B) * H * W;
+    rms(x, P, C, nout_w_, nout_b_, nullptr, 1, y);
+    vae_conv_out_kernel<T><<<blocks_for(P * 32, 256), 256, 0, st>>>(y, B, H, W, C, cout_w_.as<float>(),
+                                                                   cout_b_.as<float>(), d.out_channels, out_d);
+    SANA_CUDA(cudaGetLastError());
+    ++launches_;
+    // x/y/g rotate through three buffers; keep the members pointing at distinct storage
+}
+
+}  // namespace sana

@@ -58,6 +58,7 @@ def load_library():
         lib.sana_cuda_stream.argtypes = [ctypes.c_void_p]
         lib.sana_cuda_destroy.argtypes = [ctypes.c_void_p]
         lib.sana_cuda_last_launch_count.argtypes = [ctypes.c_void_p]
+        lib.sana_cuda_vae_last_launch_count.argtypes = [ctypes.c_void_p]
         lib.sana_randn_torch_cpu.argtypes = [_f32p, ctypes.c_size_t, ctypes.c_uint64]
         lib.sana_gguf_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p,
                                        ctypes.c_size_t]
@@ -292,6 +293,31 @@ class SanaCuda:
                    ctypes.c_void_p(positive.data_ptr()), _i(rows), pr, _i(hidden), _i(L),
                    ctypes.c_void_p(enc.data_ptr()), ctypes.c_void_p(bias.data_ptr()))
         return enc, bias
+
+    # -- VAE decoder (vae.cpp:243-325) --------------------------------------------------
+    def vae_upload(self, dims, tensors):
+        """dims: synthetic_vae.VaeDims; tensors: fp32 arrays in its upload order."""
+        from .synthetic_vae import dims_struct
+        ds = dims_struct(dims)
+        arrs = [_f32(t) for t in tensors]
+        table = (ctypes.c_void_p * len(arrs))(*[a.ctypes.data for a in arrs])
+        self._call("sana_cuda_vae_upload", ctypes.byref(ds), table)
+        self.vae_dims = dims
+
+    def vae_decode(self, latents):
+        lat = _f32(latents)
+        B, _, h, w = lat.shape
+        up = self.vae_dims.upscale()
+        out = np.empty((B, self.vae_dims.out_channels, h * up, w * up), np.float32)
+        self._call("sana_cuda_vae_decode", _ptr(lat), _i(B), _i(h), _i(w), _ptr(out))
+        return out
+
+    def vae_decode_device(self, lat_ptr: int, B: int, h: int, w: int, out_ptr: int):
+        self._call("sana_cuda_vae_decode_device", ctypes.c_void_p(lat_ptr), _i(B), _i(h), _i(w),
+                   ctypes.c_void_p(out_ptr))
+
+    def vae_last_launches(self) -> int:
+        return self.lib.sana_cuda_vae_last_launch_count(self.h)
 
     def upload_gguf(self, model_path: str, caption_path: str, denoiser_path: str, self_heads: int = 36,
                     cross_heads: int = 16):

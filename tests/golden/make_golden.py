@@ -12,6 +12,7 @@ Usage (from the repo root, after ``make -C oracle``):
     python tests/golden/make_golden.py block      # one full-size block (~10 s)
     python tests/golden/make_golden.py forward    # config 0: one CFG-batch forward (~4 min)
     python tests/golden/make_golden.py loop       # config 1: 20-step loop (~80 min)
+    python tests/golden/make_golden.py vae        # VAE decoder: small dims, DC-AE dims at 2x2 (~1 min)
 """
 from __future__ import annotations
 
@@ -162,7 +163,29 @@ def loop(ref: Reference):
     np.savez_compressed(os.path.join(HERE, "loop20_full.npz"), latents=out, seconds=time.time() - t0)
 
 
+VAE_SMALL_SEED, VAE_FULL_SEED = 31, 32
+
+
+def vae(ref: Reference):
+    """run_vae_decode (vae.cpp:243) on the small test structure (two images of 4 x 6
+    latents) and on DC-AE f32c32's structure at 2 x 2 latents (a 64 x 64 image)."""
+    from sana_b200 import synthetic_vae as sv
+    rnd = ref.randn
+    t0 = time.time()
+    small_out = ref.vae_decode(sv.SMALL, sv.generate_vae(sv.SMALL, rnd, VAE_SMALL_SEED),
+                               sv_latents(rnd, 2, sv.SMALL.latent_channels, 4, 6, VAE_SMALL_SEED))
+    full = sv.VaeDims()
+    full_out = ref.vae_decode(full, sv.generate_vae(full, rnd, VAE_FULL_SEED),
+                              sv_latents(rnd, 1, full.latent_channels, 2, 2, VAE_FULL_SEED))
+    print(f"vae {time.time() - t0:.1f}s", flush=True)
+    np.savez_compressed(os.path.join(HERE, "vae.npz"), small=small_out, full_2x2=full_out)
+
+
+def sv_latents(rnd, B, C, h, w, seed):
+    return syn.latents(rnd, B, C, h, w, 1000 + seed)
+
+
 if __name__ == "__main__":
     ref = Reference()
     for what in sys.argv[1:] or ["small"]:
-        {"small": small, "block": block, "forward": forward, "loop": loop}[what](ref)
+        {"small": small, "block": block, "forward": forward, "loop": loop, "vae": vae}[what](ref)

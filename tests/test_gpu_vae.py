@@ -1,0 +1,142 @@
+"""The VAE decoder on the GPU (vae.cpp:243-325 run_vae_decode, vae_ops.cpp) through the C ABI,
+against the reference build's golden outputs (tests/golden/vae.npz) and the oracle.
+
+Tolerances: fp32 check mode follows the reference to rounding (rel-L2 <= 1e-4); the bf16
+product path keeps activations in bf16 between ops with fp32 accumulation (rel-L2 <= 2e-2,
+cosine >= 0.999)."""
+import importlib.util
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+_spec = importlib.util.spec_from_file_location("make_golden", os.path.join(GOLDEN, "make_golden.py"))
+MG = importlib.util.module_from_spec(_spec)
+_spec.loader.exec_module(MG)
+
+TOL = {"f32": 1e-4, "bf16": 2e-2}
+
+
+def rel_err(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def cosine(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def decoder(mode, dims, seed):
+    from sana_b200 import SANA_MODE_BF16, SANA_MODE_F32, SanaCuda, randn_torch_cpu
+    from sana_b200 import synthetic_vae as sv
+    g = SanaCuda(0, SANA_MODE_F32 if mode == "f32" else SANA_MODE_BF16)
+    g.vae_upload(dims, sv.generate_vae(dims, randn_torch_cpu, seed))
+    return g
+
+
+def latents(dims, B, h, w, seed):
+    from sana_b200 import randn_torch_cpu
+    return MG.sv_latents(randn_torch_cpu, B, dims.latent_channels, h, w, seed)
+
+
+@pytest.mark.parametrize("mode", ["f32", "bf16"])
+def test_vae_small_matches_reference_golden(mode):
+    from sana_b200 import synthetic_vae as sv
+    g = decoder(mode, sv.SMALL, MG.VAE_SMALL_SEED)
+    out = g.vae_decode(latents(sv.SMALL, 2, 4, 6, MG.VAE_SMALL_SEED))
+    gold = np.load(os.path.join(GOLDEN, "vae.npz"))["small"]
+    e = rel_err(out, gold)
+    print(f"vae small {mode}: rel-L2 {e:.3e}")
+    assert e < TOL[mode]
+    assert g.vae_last_launches() > 10
+
+
+@pytest.mark.parametrize("mode", ["f32", "bf16"])
+def test_vae_dcae_dims_match_reference_golden(mode):
+    """DC-AE f32c32's structure (1024-channel attention levels down to 128-channel ResBlocks)
+    at 2 x 2 latents: a 64 x 64 image."""
+    from sana_b200 import synthetic_vae as sv
+    dims = sv.VaeDims()
+    g = decoder(mode, dims, MG.VAE_FULL_SEED)
+    out = g.vae_decode(latents(dims, 1, 2, 2, MG.VAE_FULL_SEED))
+    gold = np.load(os.path.join(GOLDEN, "vae.npz"))["full_2x2"]
+    e, c = rel_err(out, gold), cosine(out, gold)
+    print(f"vae dc-ae 2x2 {mode}: rel-L2 {e:.3e} cosine {c:.6f}")
+    assert e < TOL[mode] and c > 0.999
+
+
+@pytest.mark.parametrize("mode", ["f32", "bf16"])
+def test_vae_fresh_structures_match_oracle(mode, oracle):
+    """A 3x3 multiscale kernel, attention between ResBlock levels, odd latent sizes."""
+    from sana_b200 import randn_torch_cpu
+    from sana_b200 import synthetic_vae as sv
+    dims = sv.VaeDims(latent_channels=4, out_channels=3, channels=(16, 64, 32), res_blocks=(True, False, True),
+                      layers=(2, 1, 1), head_dim=32, ms_kernel=3, scaling_factor=0.7)
+    g = decoder(mode, dims, 41)
+    lat = latents(dims, 1, 3, 5, 41)
+    out = g.vae_decode(lat)
+    want = oracle.vae_decode(dims, sv.generate_vae(dims, randn_torch_cpu, 41), lat)
+    e = rel_err(out, want)
+    print(f"vae fresh {mode}: rel-L2 {e:.3e}")
+    assert e < TOL[mode]
+
+
+def test_vae_dcae_8x8_matches_oracle(oracle):
+    """bf16 product path at 8 x 8 latents (a 256 x 256 image), every level wide enough for
+    the tensor-core GEMM tiles."""
+    from sana_b200 import randn_torch_cpu
+    from sana_b200 import synthetic_vae as sv
+    dims = sv.VaeDims()
+    g = decoder("bf16", dims, 7)
+    lat = latents(dims, 1, 8, 8, 7)
+    out = g.vae_decode(lat)
+    want = oracle.vae_decode(dims, sv.generate_vae(dims, randn_torch_cpu, 7), lat)
+    e, c = rel_err(out, want), cosine(out, want)
+    print(f"vae dc-ae 8x8 bf16: rel-L2 {e:.3e} cosine {c:.6f}")
+    assert e < TOL["bf16"] and c > 0.999
+
+
+def test_vae_batch_images_are_independent():
+    from sana_b200 import synthetic_vae as sv
+    g = decoder("bf16", sv.SMALL, 5)
+    lat = latents(sv.SMALL, 3, 4, 4, 5)
+    both = g.vae_decode(lat)
+    for i in range(3):
+        one = g.vae_decode(lat[i:i + 1])
+        assert cosine(both[i], one[0]) > 0.99999
+
+
+def test_vae_1024_image_is_deterministic_and_finite():
+    """Sana's image size: 32 x 32 latents through DC-AE f32c32 -> 1024 x 1024 RGB."""
+    from sana_b200 import synthetic_vae as sv
+    dims = sv.VaeDims()
+    g = decoder("bf16", dims, 3)
+    lat = latents(dims, 1, 32, 32, 3)
+    a = g.vae_decode(lat)
+    b = g.vae_decode(lat)
+    assert a.shape == (1, 3, 1024, 1024)
+    assert np.isfinite(a).all() and float(np.std(a)) > 1e-3
+    assert np.array_equal(a, b)
+
+
+def test_vae_argument_errors():
+    from sana_b200 import SANA_MODE_BF16, SanaCuda, SanaError, randn_torch_cpu
+    from sana_b200 import synthetic_vae as sv
+    g = SanaCuda(0, SANA_MODE_BF16)
+    with pytest.raises(SanaError):
+        g.vae_dims = sv.SMALL
+        g.vae_decode(latents(sv.SMALL, 1, 2, 2, 1))  # no weights uploaded
+    bad = sv.VaeDims(latent_channels=8, channels=(16, 32, 64), res_blocks=(True, True, False), layers=(1, 1, 1),
+                     head_dim=16)
+    with pytest.raises(ValueError, match="head dim"):
+        g.vae_upload(bad, sv.generate_vae(bad, randn_torch_cpu, 1))
+    bad = sv.VaeDims(latent_channels=6, channels=(16, 32, 64), res_blocks=(True, True, False), layers=(1, 1, 1))
+    with pytest.raises(ValueError, match="divisible by latent channels"):
+        g.vae_upload(bad, sv.generate_vae(bad, randn_torch_cpu, 1))

@@ -145,3 +145,26 @@ def test_full_block_signature(oracle):
         assert rel_err(sig["head"], g[f"{name}_head"]) < 1e-5
         assert rel_err(sig["row_sq"], g[f"{name}_row_sq"]) < 1e-5
         assert rel_err(sig["row_sum"], g[f"{name}_row_sum"]) < 1e-4
+
+
+def _vae_case(impl, dims, seed, B, h, w):
+    from sana_b200 import synthetic_vae as sv
+    return impl.vae_decode(dims, sv.generate_vae(dims, impl.randn, seed),
+                           MG.sv_latents(impl.randn, B, dims.latent_channels, h, w, seed))
+
+
+def test_vae_matches_golden(oracle):
+    """The oracle's VAE decoder reproduces the reference build's run_vae_decode outputs."""
+    from sana_b200 import synthetic_vae as sv
+    g = np.load(os.path.join(GOLDEN, "vae.npz"))
+    assert rel_err(_vae_case(oracle, sv.SMALL, MG.VAE_SMALL_SEED, 2, 4, 6), g["small"]) < 1e-5
+    assert rel_err(_vae_case(oracle, sv.VaeDims(), MG.VAE_FULL_SEED, 1, 2, 2), g["full_2x2"]) < 1e-5
+
+
+def test_vae_oracle_agrees_with_reference(oracle, reference):
+    """Fresh structures: odd latent sizes, a 3x3 multiscale kernel, attention in the middle."""
+    from sana_b200 import synthetic_vae as sv
+    dims = sv.VaeDims(latent_channels=4, out_channels=3, channels=(16, 64, 32), res_blocks=(True, False, True),
+                      layers=(2, 1, 1), head_dim=32, ms_kernel=3, scaling_factor=0.7)
+    assert rel_err(_vae_case(oracle, dims, 41, 1, 3, 5), _vae_case(reference, dims, 41, 1, 3, 5)) < 1e-5
+    assert rel_err(_vae_case(oracle, sv.SMALL, 42, 1, 5, 3), _vae_case(reference, sv.SMALL, 42, 1, 5, 3)) < 1e-5
