@@ -270,7 +270,7 @@ def gemm_roofline(g, torch, stream, M, peak_tflops):
 
 MICRO_OPS = ("qkv_gemm", "linear_attention_16x72", "linear_attention_36x32", "depthwise_glu", "cross_attention",
              "ff_inverted_config2", "linear_attention_config2", "depthwise_glu_config2", "cross_attention_config2",
-             "out_proj_config2", "ff_point_config2", "ln_modulate_config2")
+             "out_proj_config2", "ff_point_config2", "ln_modulate_config2", "vae_decode_1024")
 
 
 def run_microbench(args):
@@ -331,6 +331,18 @@ def run_microbench(args):
               flush=True)
 
     for name in ops:
+        if name == "vae_decode_1024":
+            # the DC-AE f32c32 decoder after the loop (vae.cpp:243): 32 x 32 latents -> 1024 x 1024
+            from sana_b200 import randn_torch_cpu
+            from sana_b200 import synthetic_vae as sv
+            vd = sv.VaeDims()
+            g.vae_upload(vd, sv.generate_vae(vd, randn_torch_cpu, 3))
+            lat = torch.randn(1, vd.latent_channels, 32, 32, generator=gen).cuda()
+            img = torch.empty(1, vd.out_channels, 1024, 1024, device="cuda")
+            ms = timed(lambda: g.vae_decode_device(lat.data_ptr(), 1, 32, 32, img.data_ptr()))
+            report(name, "DC-AE f32c32 decode, latents [1,32,32,32] -> image [1,3,1024,1024], bf16 activations "
+                         f"({g.vae_last_launches()} launches)", ms, sv.vae_flops(vd, 32, 32), "tensor")
+            continue
         S, T = (32, 1024) if name.endswith("config2") else (2, 4096)
         side = int(round(T ** 0.5))
         if name.startswith("linear_attention"):

@@ -37,6 +37,17 @@ struct Epilogue {
     int act2 = kActNone;
 };
 
+// Implicit convolution as the A operand (tensor-core pair kernel only): A is an NHWC bf16
+// image batch [M / (H * W), H, W, C] and row m of the product is pixel m. K = kh * kw * C with
+// k = t * C + c, tap t = ty * kw + tx reading the pixel at offset (oy + ty, ox + tx), zero
+// outside the image. A 3x3 "same" convolution is kh = kw = 3, oy = ox = -1. The weight B is
+// [N, kh * kw * C] in the same tap-major order. Needs C % 64 == 0 and 128-row tiles that
+// are rectangles of whole image rows: W % 128 == 0, or 128 % W == 0 with (H * W) % 128 == 0.
+struct ConvA {
+    int H = 0, W = 0, C = 0;
+    int kh = 3, kw = 3, oy = -1, ox = -1;
+};
+
 struct GemmProblem {
     const void* A = nullptr;
     int a_bf16 = 1;
@@ -46,10 +57,13 @@ struct GemmProblem {
     long long ldb = 0;
     int M = 0, N = 0, K = 0;
     Epilogue ep;
+    ConvA conv;  // conv.H == 0: A is a plain row-major matrix
 };
 
 // True when the tcgen05 kernel can run the problem (bf16 operands, TMA-legal strides).
 bool gemm_tc_supported(const GemmProblem& p);
+// The same for an implicit-convolution problem (p.conv set).
+bool gemm_conv_supported(const GemmProblem& p);
 // tcgen05 / TMEM / TMA tensor-core path (gemm_tc.cu). err: device error word.
 void gemm_tc(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms);
 // Generic CUDA-core path for any shape or operand type (gemm_simt.cu): fp32 check mode,

@@ -199,6 +199,21 @@ __device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_
         : "memory");
 }
 
+// The same for a 4-D box (implicit-convolution A tiles: channels, x, y, image).
+__device__ __forceinline__ void tma_load_4d_pair(const CUtensorMap* map, uint32_t dst, uint32_t bar_cluster, int c0,
+                                                 int c1, int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4, %5, %6}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+// Geometry of an implicit-convolution A operand (ConvA) as the producer uses it.
+struct ConvGeom {
+    int H = 0, W = 0, cchunks = 0, kw = 1, oy = 0, ox = 0;
+};
+
 // --- epilogue -------------------------------------------------------------------------
 __device__ __forceinline__ void store_val(void* out, int is_bf16, long long idx, float v) {
     if (is_bf16) {
@@ -852,11 +867,12 @@ struct Cfg2 : Layout<kResid ? (kDeep ? (BN == 128 ? 7 : 5) : (BN == 128 ? 5 : 4)
     static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
 };
 
-template <int BN, bool kResid, bool kDeep>
+template <int BN, bool kResid, bool kDeep, bool kConv = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmO,
-                    const __grid_constant__ CUtensorMap tmO2, int M, int N, int K, Epilogue ep, int vec, int* err) {
+                    const __grid_constant__ CUtensorMap tmO2, int M, int N, int K, Epilogue ep, int vec, int* err,
+                    ConvGeom cg) {
     using C = Cfg2<BN, kResid, kDeep>;
     constexpr int S = C::kStages;
     constexpr int BM2 = 2 * BM;
@@ -923,6 +939,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             for (int tile = pair; ok && tile < num_tiles; tile += npairs) {
                 const int m_blk = tile / num_n;
                 const int n_blk = tile % num_n;
+                // implicit convolution: this CTA's 128 rows are whole image rows from (img, y0, x0)
+                int img = 0, y0 = 0, x0 = 0;
+                if constexpr (kConv) {
+                    const int m0 = m_blk * BM2 + static_cast<int>(rank) * BM;
+                    const int hw = cg.H * cg.W;
+                    img = m0 / hw;
+                    const int rem = m0 - img * hw;
+                    y0 = rem / cg.W;
+                    x0 = rem - y0 * cg.W;
+                }
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(empty(stage), phase ^ 1u, err, kTimeout)) {
                         ok = false;
@@ -930,8 +956,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                     if (leader) mbar_arrive_expect_tx(full(stage), 2 * C::kStageBytes);
                     const uint32_t fb = full_leader + 8u * stage;
-                    tma_load_2d_pair(&tmA, a_smem + stage * C::kABytes, fb, kb * BK,
-                                     m_blk * BM2 + static_cast<int>(rank) * BM);
+                    if constexpr (kConv) {
+                        const int tap = kb / cg.cchunks;
+                        const int cc = kb - tap * cg.cchunks;
+                        const int ty = tap / cg.kw;
+                        tma_load_4d_pair(&tmA, a_smem + stage * C::kABytes, fb, cc * BK, x0 + cg.ox + (tap - ty * cg.kw),
+                                         y0 + cg.oy + ty, img);
+                    } else {
+                        tma_load_2d_pair(&tmA, a_smem + stage * C::kABytes, fb, kb * BK,
+                                         m_blk * BM2 + static_cast<int>(rank) * BM);
+                    }
                     tma_load_2d_pair(&tmB, b_smem + stage * C::kBBytes, fb, kb * BK,
                                      n_blk * BN + static_cast<int>(rank) * C::kBH);
                     ++issued;
@@ -1105,16 +1139,43 @@ static void launch(const GemmProblem& p, int* err, cudaStream_t stream, int num_
     SANA_CUDA(cudaGetLastError());
 }
 
-template <int BN, bool kResid, bool kDeep = false>
+// 4-D bf16 tensor map over an NHWC image batch [images, H, W, C] for implicit-convolution
+// A tiles: box = 64 channels x (128 pixels of whole rows), 128-byte swizzle (the same shared
+// layout as make_map's 128-row box); out-of-image pixels read as zero.
+static CUtensorMap conv_map(const GemmProblem& p) {
+    const ConvA& c = p.conv;
+    const int images = (p.M + c.H * c.W - 1) / (c.H * c.W);
+    const int bx = c.W >= BM ? BM : c.W;
+    CUtensorMap m;
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(c.C), static_cast<cuuint64_t>(c.W),
+                                static_cast<cuuint64_t>(c.H), static_cast<cuuint64_t>(images)};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(c.C) * 2, static_cast<cuuint64_t>(c.W) * c.C * 2,
+                                   static_cast<cuuint64_t>(c.H) * c.W * c.C * 2};
+    const cuuint32_t box[4] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(bx),
+                               static_cast<cuuint32_t>(BM / bx), 1};
+    tma_encode_tiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, p.A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    return m;
+}
+
+template <int BN, bool kResid, bool kDeep = false, bool kConv = false>
 static void launch2(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
     using C = Cfg2<BN, kResid, kDeep>;
     static bool attr_done = false;
     if (!attr_done) {
-        SANA_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<BN, kResid, kDeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       C::kSmemBytes));
+        SANA_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<BN, kResid, kDeep, kConv>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
         attr_done = true;
     }
-    const CUtensorMap ma = make_map(p.A, p.M, p.K, p.lda, BM);
+    const CUtensorMap ma = kConv ? conv_map(p) : make_map(p.A, p.M, p.K, p.lda, BM);
+    ConvGeom cg;
+    if (kConv) {
+        cg.H = p.conv.H;
+        cg.W = p.conv.W;
+        cg.cchunks = p.conv.C / BK;
+        cg.kw = p.conv.kw;
+        cg.oy = p.conv.oy;
+        cg.ox = p.conv.ox;
+    }
     const CUtensorMap mb = make_map(p.B, p.N, p.K, p.ldb, C::kBH);
     const CUtensorMap mr = kResid ? resid_map(p) : ma;
     const Epilogue& e = p.ep;
@@ -1129,8 +1190,8 @@ static void launch2(const GemmProblem& p, int* err, cudaStream_t stream, int num
     const CUtensorMap mo2 = kResid && vec && e.out2 ? out_map(e.out2, e.out2_bf16, e.ldo2, p.M, p.N) : ma;
     const int tiles = ((p.M + 2 * BM - 1) / (2 * BM)) * ((p.N + BN - 1) / BN);
     const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
-    gemm_tc2_kernel<BN, kResid, kDeep><<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(ma, mb, mr, mo, mo2, p.M, p.N,
-                                                                                        p.K, e, vec ? 1 : 0, err);
+    gemm_tc2_kernel<BN, kResid, kDeep, kConv><<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(
+        ma, mb, mr, mo, mo2, p.M, p.N, p.K, e, vec ? 1 : 0, err, cg);
     SANA_CUDA(cudaGetLastError());
 }
 
@@ -1147,7 +1208,19 @@ static bool use_pair(const GemmProblem& p, int num_sms) {
 
 }  // namespace tc
 
+bool gemm_conv_supported(const GemmProblem& p) {
+    const ConvA& c = p.conv;
+    auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    if (c.H <= 0 || c.W <= 0 || c.C <= 0 || c.kh < 1 || c.kw < 1) return false;
+    constexpr int BM = tc::BM, BK = tc::BK;
+    const bool rows_ok = (c.W % BM == 0) || (BM % c.W == 0 && (static_cast<long long>(c.H) * c.W) % BM == 0);
+    return p.a_bf16 && p.b_bf16 && c.C % BK == 0 && rows_ok && p.K == c.kh * c.kw * c.C && p.N >= 16 &&
+           (p.ldb % 8 == 0) && a16(p.A) && a16(p.B) && !p.ep.resid && p.M % (c.H * c.W) == 0 &&
+           c.kh * c.kw <= 64;
+}
+
 bool gemm_tc_supported(const GemmProblem& p) {
+    if (p.conv.H > 0) return gemm_conv_supported(p);
     auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     // the residual epilogue reads its fp32 residual with TMA: 16-byte aligned base and rows
     const bool resid_ok = !p.ep.resid || (a16(p.ep.resid) && p.ep.ldr % 4 == 0);
@@ -1160,6 +1233,12 @@ void gemm_tc(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
     // The MMA costs the same issue time for any N up to 256, so tiles are 256 wide whenever
     // N allows (the last one ragged: its out-of-range B rows read as zero and its columns
     // are masked in the epilogue); narrow problems use 128 columns.
+    if (p.conv.H > 0) {
+        // implicit convolution: CTA-pair kernel at any M (its producer builds the 4-D tiles)
+        if (p.N >= 256) tc::launch2<256, false, false, true>(p, err, stream, num_sms);
+        else tc::launch2<128, false, false, true>(p, err, stream, num_sms);
+        return;
+    }
     const bool pair = tc::use_pair(p, num_sms);
     const bool resid = p.ep.resid != nullptr;
     // long reductions keep the MMA fed with deeper operand pipelines (their epilogue has slack)
@@ -1179,6 +1258,8 @@ static std::atomic<long long> g_tc_launches{0}, g_simt_launches{0};
 
 void gemm(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms, bool allow_tc) {
     if (p.M == 0 || p.N == 0) return;
+    SANA_REQUIRE(p.conv.H == 0 || (allow_tc && gemm_conv_supported(p)),
+                 "implicit convolution needs the tensor-core path and a supported shape");
     if (allow_tc && gemm_tc_supported(p)) {
         gemm_tc(p, err, stream, num_sms);
         ++g_tc_launches;

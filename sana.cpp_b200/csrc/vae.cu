@@ -10,13 +10,20 @@
 //       x + RMSNorm(conv_point(dw3x3 GLU(silu(conv_inverted(x) + b))))
 //   RMSNorm(+bias), ReLU, conv_out 3x3 -> NCHW fp32
 //
-// 3x3 convolutions run as GEMMs over tap-major patches [pixels, 9 * Cin] (the upsample is
-// folded into the patch gather); weights are reordered to [Cout, 9, Cin] at upload. The
+// 3x3 convolutions are implicit GEMMs on the tensor-core kernel: its producer loads each
+// tap's shifted pixel tile straight from the NHWC image with 4-D TMA boxes (zero fill at
+// the borders), weights reordered to [Cout, 9, Cin] at upload. A nearest-2x upsample
+// followed by a 3x3 conv is computed as four 2x2 convolutions on the low-resolution image,
+// one per output parity (the 3x3 taps that land on the same source pixel summed at
+// upload), and a shuffle kernel interleaves them and adds the channel shortcut: 4/9 of the
+// FLOPs, no upsampled copy. Shapes the implicit path cannot tile (and the fp32 check mode)
+// gather tap-major patches [pixels, 9 * Cin] for a plain GEMM instead. The
 // q/k/v projection rows are permuted at upload in groups of head_dim channels so that the
 // reference's reading of the concatenated [q | k | v] (head g takes channels
 // [3 g d, 3 g d + 3 d) as its q, k, v; vae_ops.cpp:686-714) becomes the plain
 // [q heads | k heads | v heads] layout of the linear-attention kernel; the multiscale
 // depthwise and grouped weights move with their channels.
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -32,7 +39,7 @@ inline int blocks_for(long long n, int threads = 256) { return static_cast<int>(
 
 // conv_in: 3x3 "same" over latents * inv_sf (NCHW fp32), + bias, + the repeated-channel
 // shortcut out[c] += scaled[c / (C / Cl)] (vae.cpp:210-241, vae_ops.cpp:455-493).
-// w: [C, 9, Cl] fp32. out: NHWC [B*H*W, C].
+// w: [9, Cl, C] fp32 (consecutive output channels read consecutive weights). out: NHWC [B*H*W, C].
 template <class T>
 __global__ void vae_conv_in_kernel(const float* __restrict__ lat, int B, int Cl, int H, int W,
                                    const float* __restrict__ w, const float* __restrict__ bias, float inv_sf, int C,
@@ -46,13 +53,13 @@ __global__ void vae_conv_in_kernel(const float* __restrict__ lat, int B, int Cl,
     const int y = static_cast<int>((p / W) % H);
     const int b = static_cast<int>(p / (static_cast<long long>(W) * H));
     const float* lb = lat + static_cast<long long>(b) * Cl * H * W;
-    const float* wo = w + static_cast<long long>(oc) * 9 * Cl;
     float acc = bias[oc];
     for (int tap = 0; tap < 9; ++tap) {
         const int iy = y + tap / 3 - 1, ix = x + tap % 3 - 1;
         if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;
+        const float* wt = w + static_cast<long long>(tap) * Cl * C + oc;
         for (int c = 0; c < Cl; ++c)
-            acc = fmaf(wo[tap * Cl + c], lb[(static_cast<long long>(c) * H + iy) * W + ix] * inv_sf, acc);
+            acc = fmaf(wt[static_cast<long long>(c) * C], lb[(static_cast<long long>(c) * H + iy) * W + ix] * inv_sf, acc);
     }
     acc += lb[(static_cast<long long>(oc / (C / Cl)) * H + y) * W + x] * inv_sf;
     out[i] = from_f<T>(acc);
@@ -106,6 +113,32 @@ __global__ void up_shortcut_kernel(T* __restrict__ out, const T* __restrict__ in
     const int ic = (4 * oc + 2 * (yo & 1) + (xo & 1)) / rep;
     const float s = to_f(in[((static_cast<long long>(b) * H + (yo >> 1)) * W + (xo >> 1)) * Cin + ic]);
     out[i] = from_f<T>(to_f(out[i]) + s);
+}
+
+// Interleaves the four parity outputs par[ij] ([B*H*W, Cout] each, ij = 2 i + j) of a
+// sub-pixel upsample conv into out[b, 2y+i, 2x+j, :] and adds the upsample shortcut of
+// up_shortcut_kernel. 8 channels per thread.
+template <class T>
+__global__ void shuffle_shortcut_kernel(const T* __restrict__ par, const T* __restrict__ in, int B, int H, int W,
+                                        int Cin, int Cout, T* __restrict__ out) {
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int CV = Cout / 8, Ho = 2 * H, Wo = 2 * W;
+    const long long n = static_cast<long long>(B) * Ho * Wo * CV;
+    if (i >= n) return;
+    const int oc0 = static_cast<int>(i % CV) * 8;
+    const long long p = i / CV;
+    const int xo = static_cast<int>(p % Wo);
+    const int yo = static_cast<int>((p / Wo) % Ho);
+    const int b = static_cast<int>(p / (static_cast<long long>(Wo) * Ho));
+    const int ij = 2 * (yo & 1) + (xo & 1);
+    const long long lo = (static_cast<long long>(b) * H + (yo >> 1)) * W + (xo >> 1);
+    const long long plane = static_cast<long long>(B) * H * W * Cout;
+    const T* src = par + ij * plane + lo * Cout + oc0;
+    const T* sc = in + lo * Cin;
+    const int rep = 4 * Cout / Cin;
+    T* dst = out + p * Cout + oc0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) dst[k] = from_f<T>(to_f(src[k]) + to_f(sc[(4 * (oc0 + k) + ij) / rep]));
 }
 
 // rms_norm_4d_channelwise (vae_ops.cpp:495-575) over each pixel row, then the residual
@@ -185,13 +218,19 @@ __global__ void __launch_bounds__(256) ms_branch_kernel(const T* __restrict__ qk
 }
 
 // conv_out (vae.cpp:320-324): 3x3 "same" from NHWC rows [pixels, C] to NCHW fp32 with few
-// output channels (Co <= 4); one warp per output pixel. w: [Co, 9, C] fp32.
+// output channels (Co <= 4); one thread per output pixel, the weights [4, 9, C] fp32 (zero
+// rows past Co) staged in shared memory. C <= kConvOutMaxC.
+constexpr int kConvOutMaxC = 256;
 template <class T>
-__global__ void vae_conv_out_kernel(const T* __restrict__ in, int B, int H, int W, int C,
-                                    const float* __restrict__ w, const float* __restrict__ bias, int Co,
-                                    float* __restrict__ out) {
-    const long long p = static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
-    const int lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(128) vae_conv_out_kernel(const T* __restrict__ in, int B, int H, int W, int C,
+                                                           const float* __restrict__ w, const float* __restrict__ bias,
+                                                           int Co, float* __restrict__ out) {
+    __shared__ float s_w[9 * kConvOutMaxC][4];
+    for (int i = threadIdx.x; i < 9 * C; i += blockDim.x)
+#pragma unroll
+        for (int o = 0; o < 4; ++o) s_w[i][o] = o < Co ? w[static_cast<long long>(o) * 9 * C + i] : 0.f;
+    __syncthreads();
+    const long long p = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     const long long P = static_cast<long long>(B) * H * W;
     if (p >= P) return;
     const int x = static_cast<int>(p % W), y = static_cast<int>((p / W) % H);
@@ -201,24 +240,14 @@ __global__ void vae_conv_out_kernel(const T* __restrict__ in, int B, int H, int 
         const int iy = y + tap / 3 - 1, ix = x + tap % 3 - 1;
         if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;
         const T* src = in + ((static_cast<long long>(b) * H + iy) * W + ix) * C;
-        for (int c = lane; c < C; c += 32) {
+        const float(*wt)[4] = s_w + tap * C;
+        for (int c = 0; c < C; ++c) {
             const float v = to_f(src[c]);
 #pragma unroll
-            for (int o = 0; o < 4; ++o)
-                if (o < Co) acc[o] = fmaf(w[(static_cast<long long>(o) * 9 + tap) * C + c], v, acc[o]);
+            for (int o = 0; o < 4; ++o) acc[o] = fmaf(wt[c][o], v, acc[o]);
         }
     }
-#pragma unroll
-    for (int o = 0; o < 4; ++o)
-#pragma unroll
-        for (int s = 16; s > 0; s >>= 1) acc[o] += __shfl_xor_sync(0xffffffffu, acc[o], s);
-    if (lane < Co) {
-        float v = acc[0];
-#pragma unroll
-        for (int o = 1; o < 4; ++o)
-            if (lane == o) v = acc[o];
-        out[((static_cast<long long>(b) * Co + lane) * H + y) * W + x] = v + bias[lane];
-    }
+    for (int o = 0; o < Co; ++o) out[((static_cast<long long>(b) * Co + o) * H + y) * W + x] = acc[o] + bias[o];
 }
 
 // --- host-side weight preparation -------------------------------------------------------
@@ -251,6 +280,37 @@ std::vector<float> tap_major(const float* w, int Cout, int Cin) {
     for (int o = 0; o < Cout; ++o)
         for (int c = 0; c < Cin; ++c)
             for (int t = 0; t < 9; ++t) r[(static_cast<size_t>(o) * 9 + t) * Cin + c] = w[(static_cast<size_t>(o) * Cin + c) * 9 + t];
+    return r;
+}
+
+// [Cout, Cin, 3, 3] -> four [Cout, 4, Cin] weights of the sub-pixel upsample conv: parity
+// (i, j) reads low-resolution rows y + i - 1 + a and columns x + j - 1 + c (a, c in {0, 1});
+// its weight sums the 3x3 taps that fall on that source pixel after the nearest-2x
+// upsample (rows: i = 0 -> {0}, {1, 2}; i = 1 -> {0, 1}, {2}; columns likewise).
+std::vector<float> parity_weights(const float* w, int Cout, int Cin) {
+    static const int lo[2][2] = {{0, 1}, {0, 2}}, hi[2][2] = {{0, 2}, {1, 2}};  // [parity][a] -> tap range
+    std::vector<float> r(static_cast<size_t>(4) * Cout * 4 * Cin, 0.f);
+    for (int i = 0; i < 2; ++i)
+        for (int j = 0; j < 2; ++j)
+            for (int o = 0; o < Cout; ++o)
+                for (int a = 0; a < 2; ++a)
+                    for (int c2 = 0; c2 < 2; ++c2)
+                        for (int c = 0; c < Cin; ++c) {
+                            float sum = 0.f;
+                            for (int ky = lo[i][a]; ky <= hi[i][a]; ++ky)
+                                for (int kx = lo[j][c2]; kx <= hi[j][c2]; ++kx)
+                                    sum += w[((static_cast<size_t>(o) * Cin + c) * 3 + ky) * 3 + kx];
+                            r[((static_cast<size_t>(2 * i + j) * Cout + o) * 4 + (2 * a + c2)) * Cin + c] = sum;
+                        }
+    return r;
+}
+
+// [C, Cl, 3, 3] -> [9, Cl, C]
+std::vector<float> conv_in_layout(const float* w, int C, int Cl) {
+    std::vector<float> r(static_cast<size_t>(9) * Cl * C);
+    for (int o = 0; o < C; ++o)
+        for (int c = 0; c < Cl; ++c)
+            for (int t = 0; t < 9; ++t) r[(static_cast<size_t>(t) * Cl + c) * C + o] = w[(static_cast<size_t>(o) * Cl + c) * 9 + t];
     return r;
 }
 
@@ -297,6 +357,7 @@ void vae_validate(const VaeDims& d) {
     if (d.head_dim != 32) throw InvalidArg("vae attention head dim must be 32");
     if (d.ms_kernel != 3 && d.ms_kernel != 5)
         throw InvalidArg("depthwise_conv2d_same only supports 3x3 or 5x5 kernels");
+    if (d.blocks[0].channels > 256) throw InvalidArg("vae decoder conv_out supports at most 256 input channels");
     const int Cin = d.blocks[d.n_blocks - 1].channels;
     if (Cin % d.latent_channels != 0)
         throw InvalidArg("vae decoder conv_in output channels must be divisible by latent channels");
@@ -332,7 +393,7 @@ void VaeDecoder::upload_impl(const float* const* t) {
     const VaeDims& d = d_;
     const int n = d.n_blocks, Cl = d.latent_channels, C0 = d.blocks[0].channels, Cn = d.blocks[n - 1].channels;
     const int k = d.ms_kernel, hd = d.head_dim;
-    put<float>(cin_w_, tap_major(t[0], Cn, Cl));
+    put<float>(cin_w_, conv_in_layout(t[0], Cn, Cl));
     put<float>(cin_b_, copy_of(t[1], Cn));
     put<float>(nout_w_, copy_of(t[2], C0));
     put<float>(nout_b_, copy_of(t[3], C0));
@@ -348,6 +409,7 @@ void VaeDecoder::upload_impl(const float* const* t) {
         const size_t CC = static_cast<size_t>(C);
         if (bd.has_upsample) {
             put<T>(blk.upw, tap_major(t[j], C, d.blocks[i + 1].channels));
+            if (sizeof(T) == 2) put<T>(blk.upw4, parity_weights(t[j], C, d.blocks[i + 1].channels));
             put<float>(blk.upb, copy_of(t[j + 1], CC));
             j += 2;
         }
@@ -418,6 +480,7 @@ void VaeDecoder::ensure_workspace(int B, int h, int w) {
     x_.ensure(x * as);
     y_.ensure(x * as);
     g_.ensure(x * as);
+    if (eng_.mode() == kModeBf16) par_.ensure(x * as);
     if (col) col_.ensure(col * as);
     if (qkv) {
         qkv_.ensure(qkv * as);
@@ -475,9 +538,80 @@ void VaeDecoder::gemm_rows(const T* A, long long M, int K, const DevBuf& w, cons
     ++launches_;
 }
 
+bool VaeDecoder::implicit_ok(int H, int W, int Cin) const {
+    if (eng_.mode() != kModeBf16) return false;
+    // SANA_VAE_CONV=im2col selects the patch-gather path for every shape (a cross-check)
+    const char* v = std::getenv("SANA_VAE_CONV");
+    if (v && std::string(v) == "im2col") return false;
+    GemmProblem p;
+    p.conv.H = H;
+    p.conv.W = W;
+    p.conv.C = Cin;
+    p.M = H * W;
+    p.N = 16;
+    p.K = 9 * Cin;
+    p.ldb = p.K;
+    p.A = p.B = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+    return gemm_conv_supported(p);
+}
+
+template <class T>
+void VaeDecoder::conv_gemm(const T* in, int B, int H, int W, int Cin, int kh, int kw, int oy, int ox, const void* w,
+                           const float* bias, int Cout, int act, T* out) {
+    GemmProblem p;
+    p.A = in;
+    p.lda = Cin;
+    p.B = w;
+    p.ldb = static_cast<long long>(kh) * kw * Cin;
+    p.M = B * H * W;
+    p.N = Cout;
+    p.K = kh * kw * Cin;
+    p.a_bf16 = p.b_bf16 = 1;
+    p.conv.H = H;
+    p.conv.W = W;
+    p.conv.C = Cin;
+    p.conv.kh = kh;
+    p.conv.kw = kw;
+    p.conv.oy = oy;
+    p.conv.ox = ox;
+    p.ep.bias = bias;
+    p.ep.act = act;
+    p.ep.out = out;
+    p.ep.out_bf16 = 1;
+    p.ep.ldo = Cout;
+    gemm(p, eng_.err(), eng_.stream(), eng_.num_sms());
+    ++launches_;
+}
+
+template <class T>
+void VaeDecoder::upsample_conv(const T* in, int B, int H, int W, int Cin, const Block& blk, int Cout, T* out) {
+    const cudaStream_t st = eng_.stream();
+    if (sizeof(T) == 2 && implicit_ok(H, W, Cin) && Cout % 8 == 0) {
+        // four 2x2 convolutions on the low-resolution image, one per output parity
+        T* par = par_.as<T>();
+        const long long plane = static_cast<long long>(B) * H * W * Cout;
+        for (int ij = 0; ij < 4; ++ij)
+            conv_gemm<T>(in, B, H, W, Cin, 2, 2, (ij >> 1) - 1, (ij & 1) - 1,
+                         blk.upw4.as<T>() + static_cast<long long>(ij) * Cout * 4 * Cin, blk.upb.as<float>(), Cout,
+                         kActNone, par + ij * plane);
+        const long long n = 4 * plane / 8;
+        shuffle_shortcut_kernel<T><<<blocks_for(n), 256, 0, st>>>(par, in, B, H, W, Cin, Cout, out);
+    } else {
+        conv3x3<T>(in, B, H, W, Cin, true, blk.upw, blk.upb.as<float>(), Cout, kActNone, out);
+        const long long nout = static_cast<long long>(B) * (2 * H) * (2 * W) * Cout;
+        up_shortcut_kernel<T><<<blocks_for(nout), 256, 0, st>>>(out, in, B, H, W, Cin, Cout);
+    }
+    SANA_CUDA(cudaGetLastError());
+    ++launches_;
+}
+
 template <class T>
 void VaeDecoder::conv3x3(const T* in, int B, int H, int W, int Cin, bool upsample, const DevBuf& w, const float* bias,
                          int Cout, int act, T* out) {
+    if (!upsample && sizeof(T) == 2 && implicit_ok(H, W, Cin)) {
+        conv_gemm<T>(in, B, H, W, Cin, 3, 3, -1, -1, w.get(), bias, Cout, act, out);
+        return;
+    }
     const int up = upsample ? 1 : 0;
     T* col = col_.as<T>();
     launch_im2col<T>(in, B, H, W, Cin, up, col, eng_.stream());
@@ -515,11 +649,7 @@ void VaeDecoder::decode_impl(const float* lat_d, int B, int h, int w, float* out
         if (bd.has_upsample) {
             const int Cin = C;
             C = bd.channels;
-            conv3x3<T>(x, B, H, W, Cin, true, blk.upw, blk.upb.as<float>(), C, kActNone, y);
-            const long long nout = static_cast<long long>(B) * (2 * H) * (2 * W) * C;
-            up_shortcut_kernel<T><<<blocks_for(nout), 256, 0, st>>>(y, x, B, H, W, Cin, C);
-            SANA_CUDA(cudaGetLastError());
-            ++launches_;
+            upsample_conv<T>(x, B, H, W, Cin, blk, C, y);
             H *= 2;
             W *= 2;
             std::swap(x, y);
@@ -570,8 +700,8 @@ void VaeDecoder::decode_impl(const float* lat_d, int B, int h, int w, float* out
     }
     const long long P = static_cast<long long>(B) * H * W;
     rms(x, P, C, nout_w_, nout_b_, nullptr, 1, y);
-    vae_conv_out_kernel<T><<<blocks_for(P * 32, 256), 256, 0, st>>>(y, B, H, W, C, cout_w_.as<float>(),
-                                                                   cout_b_.as<float>(), d.out_channels, out_d);
+    vae_conv_out_kernel<T><<<blocks_for(P, 128), 128, 0, st>>>(y, B, H, W, C, cout_w_.as<float>(),
+                                                              cout_b_.as<float>(), d.out_channels, out_d);
     SANA_CUDA(cudaGetLastError());
     ++launches_;
     // x/y/g rotate through three buffers; keep the members pointing at distinct storage

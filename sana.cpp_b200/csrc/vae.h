@@ -56,6 +56,7 @@ class VaeDecoder {
     };
     struct Block {
         DevBuf upw, upb;  // [C, 9, C_next] (act type), [C]
+        DevBuf upw4;      // bf16: the four sub-pixel parity weights [4, C, 4, C_next]
         std::vector<Layer> layers;
     };
 
@@ -64,6 +65,13 @@ class VaeDecoder {
     template <class T>
     void conv3x3(const T* in, int B, int H, int W, int Cin, bool upsample, const DevBuf& w, const float* bias,
                  int Cout, int act, T* out);
+    template <class T>
+    void upsample_conv(const T* in, int B, int H, int W, int Cin, const Block& blk, int Cout, T* out);
+    // implicit convolution on the tensor cores when the shape tiles (bf16 only)
+    bool implicit_ok(int H, int W, int Cin) const;
+    template <class T>
+    void conv_gemm(const T* in, int B, int H, int W, int Cin, int kh, int kw, int oy, int ox, const void* w,
+                   const float* bias, int Cout, int act, T* out);
     template <class T>
     void gemm_rows(const T* A, long long M, int K, const DevBuf& w, const float* bias, int N, int act, T* out);
     void ensure_workspace(int B, int h, int w);
@@ -75,7 +83,7 @@ class VaeDecoder {
     DevBuf cin_w_, cin_b_, nout_w_, nout_b_, cout_w_, cout_b_;
     std::vector<Block> blocks_;
     // workspace (grown on demand): residual stream ping-pong, conv patches, branch buffers
-    DevBuf x_, y_, g_, col_, qkv_, ms_, merged_, inv_, glu_, partial_;
+    DevBuf x_, y_, g_, col_, qkv_, ms_, merged_, inv_, glu_, partial_, par_;
     long long ws_key_ = -1;
     DevBuf lat_in_, img_out_;  // host-path staging
 };

@@ -103,6 +103,27 @@ def test_vae_dcae_8x8_matches_oracle(oracle):
     assert e < TOL["bf16"] and c > 0.999
 
 
+def test_vae_implicit_convolutions_match_patch_gemm(oracle, monkeypatch):
+    """The tensor-core implicit 3x3 convolutions and the sub-pixel upsample convs give the
+    same decode as the patch-gather path, and both follow the oracle. 8 x 8 latents through
+    64/64/128-channel levels: implicit tiles of 16- and 32-pixel rows, one low-resolution
+    grid too small for them (patch path)."""
+    from sana_b200 import randn_torch_cpu
+    from sana_b200 import synthetic_vae as sv
+    dims = sv.VaeDims(latent_channels=8, out_channels=3, channels=(64, 64, 128), res_blocks=(True, True, False),
+                      layers=(2, 1, 1), head_dim=32, ms_kernel=5, scaling_factor=0.5)
+    g = decoder("bf16", dims, 11)
+    lat = latents(dims, 2, 8, 8, 11)
+    implicit = g.vae_decode(lat)
+    monkeypatch.setenv("SANA_VAE_CONV", "im2col")
+    patch = g.vae_decode(lat)
+    monkeypatch.delenv("SANA_VAE_CONV")
+    want = oracle.vae_decode(dims, sv.generate_vae(dims, randn_torch_cpu, 11), lat)
+    e1, e2, c = rel_err(implicit, want), rel_err(patch, want), cosine(implicit, patch)
+    print(f"vae implicit vs oracle {e1:.3e}, patch vs oracle {e2:.3e}, implicit vs patch cosine {c:.7f}")
+    assert e1 < TOL["bf16"] and e2 < TOL["bf16"] and c > 0.9999
+
+
 def test_vae_batch_images_are_independent():
     from sana_b200 import synthetic_vae as sv
     g = decoder("bf16", sv.SMALL, 5)
@@ -124,6 +145,21 @@ def test_vae_1024_image_is_deterministic_and_finite():
     assert a.shape == (1, 3, 1024, 1024)
     assert np.isfinite(a).all() and float(np.std(a)) > 1e-3
     assert np.array_equal(a, b)
+
+
+def test_vae_1024_implicit_matches_patch_gemm(monkeypatch):
+    """At Sana's size every 3x3 and upsample conv takes the implicit tensor-core path; the
+    patch-gather path computes the same image."""
+    from sana_b200 import synthetic_vae as sv
+    dims = sv.VaeDims()
+    g = decoder("bf16", dims, 3)
+    lat = latents(dims, 1, 32, 32, 3)
+    a = g.vae_decode(lat)
+    monkeypatch.setenv("SANA_VAE_CONV", "im2col")
+    b = g.vae_decode(lat)
+    c = cosine(a, b)
+    print(f"vae 1024 implicit vs patch: cosine {c:.7f} rel-L2 {rel_err(a, b):.3e}")
+    assert c > 0.9999
 
 
 def test_vae_argument_errors():
