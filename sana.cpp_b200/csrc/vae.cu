@@ -117,28 +117,30 @@ __global__ void up_shortcut_kernel(T* __restrict__ out, const T* __restrict__ in
 
 // Interleaves the four parity outputs par[ij] ([B*H*W, Cout] each, ij = 2 i + j) of a
 // sub-pixel upsample conv into out[b, 2y+i, 2x+j, :] and adds the upsample shortcut of
-// up_shortcut_kernel. 8 channels per thread.
-template <class T>
-__global__ void shuffle_shortcut_kernel(const T* __restrict__ par, const T* __restrict__ in, int B, int H, int W,
-                                        int Cin, int Cout, T* __restrict__ out) {
-    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const int CV = Cout / 8, Ho = 2 * H, Wo = 2 * W;
-    const long long n = static_cast<long long>(B) * Ho * Wo * CV;
-    if (i >= n) return;
-    const int oc0 = static_cast<int>(i % CV) * 8;
-    const long long p = i / CV;
-    const int xo = static_cast<int>(p % Wo);
-    const int yo = static_cast<int>((p / Wo) % Ho);
-    const int b = static_cast<int>(p / (static_cast<long long>(Wo) * Ho));
+// up_shortcut_kernel. 8 channels per thread (16-byte parity loads and output stores);
+// blockIdx.y is the image.
+__global__ void shuffle_shortcut_kernel(const bf16* __restrict__ par, const bf16* __restrict__ in, int B, int H,
+                                        int W, int Cin, int Cout, bf16* __restrict__ out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int CV = Cout / 8, Wo = 2 * W;
+    if (i >= 4 * H * W * CV) return;
+    const int b = blockIdx.y;
+    const int oc0 = (i % CV) * 8;
+    const int p = i / CV;
+    const int xo = p % Wo, yo = p / Wo;
     const int ij = 2 * (yo & 1) + (xo & 1);
-    const long long lo = (static_cast<long long>(b) * H + (yo >> 1)) * W + (xo >> 1);
+    const long long lo = static_cast<long long>(b) * H * W + (yo >> 1) * W + (xo >> 1);
     const long long plane = static_cast<long long>(B) * H * W * Cout;
-    const T* src = par + ij * plane + lo * Cout + oc0;
-    const T* sc = in + lo * Cin;
+    const uint4 raw = *reinterpret_cast<const uint4*>(par + ij * plane + lo * Cout + oc0);
+    const bf16* e = reinterpret_cast<const bf16*>(&raw);
+    const bf16* sc = in + lo * Cin;
     const int rep = 4 * Cout / Cin;
-    T* dst = out + p * Cout + oc0;
+    uint4 o;
+    bf16* oe = reinterpret_cast<bf16*>(&o);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) dst[k] = from_f<T>(to_f(src[k]) + to_f(sc[(4 * (oc0 + k) + ij) / rep]));
+    for (int k = 0; k < 8; ++k)
+        oe[k] = __float2bfloat16_rn(__bfloat162float(e[k]) + __bfloat162float(sc[(4 * (oc0 + k) + ij) / rep]));
+    *reinterpret_cast<uint4*>(out + (static_cast<long long>(b) * 4 * H * W + p) * Cout + oc0) = o;
 }
 
 // rms_norm_4d_channelwise (vae_ops.cpp:495-575) over each pixel row, then the residual
@@ -170,84 +172,198 @@ __global__ void rms_rows_kernel(const T* __restrict__ x, long long rows, int C, 
     }
 }
 
+// The same with each lane holding ITER chunks of VPL consecutive channels of RPW rows in
+// registers (C == 32 * VPL * ITER; bf16 rows), all loads of a warp's rows issued before
+// the reductions.
+template <int VPL, int ITER, int RPW>
+__global__ void rms_rows_vec_kernel(const bf16* __restrict__ x, long long rows, int C, const float* __restrict__ w,
+                                    const float* __restrict__ b, float eps, const bf16* __restrict__ resid, int relu,
+                                    bf16* __restrict__ out) {
+    using Vec = typename std::conditional<VPL == 8, uint4, uint2>::type;
+    const long long row0 = (static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32) * RPW;
+    const int lane = threadIdx.x & 31;
+    if (row0 >= rows) return;
+    Vec xv[RPW][ITER], rv[RPW][ITER];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+        for (int it = 0; it < ITER; ++it) {
+            const long long row = row0 + r < rows ? row0 + r : rows - 1;
+            const int c0 = (it * 32 + lane) * VPL;
+            xv[r][it] = *reinterpret_cast<const Vec*>(x + row * C + c0);
+            if (resid) rv[r][it] = *reinterpret_cast<const Vec*>(resid + row * C + c0);
+        }
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+        if (row0 + r >= rows) break;
+        float ss = 0.f;
+#pragma unroll
+        for (int it = 0; it < ITER; ++it) {
+            const bf16* e = reinterpret_cast<const bf16*>(&xv[r][it]);
+#pragma unroll
+            for (int k = 0; k < VPL; ++k) {
+                const float v = __bfloat162float(e[k]);
+                ss = fmaf(v, v, ss);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / sqrtf(ss * (1.0f / static_cast<float>(C)) + eps);
+#pragma unroll
+        for (int it = 0; it < ITER; ++it) {
+            const int c0 = (it * 32 + lane) * VPL;
+            const bf16* e = reinterpret_cast<const bf16*>(&xv[r][it]);
+            const bf16* re = reinterpret_cast<const bf16*>(&rv[r][it]);
+            Vec o;
+            bf16* oe = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+            for (int k = 0; k < VPL; ++k) {
+                float y = __bfloat162float(e[k]) * inv * w[c0 + k] + b[c0 + k];
+                if (resid) y += __bfloat162float(re[k]);
+                if (relu) y = fmaxf(y, 0.0f);
+                oe[k] = __float2bfloat16_rn(y);
+            }
+            *reinterpret_cast<Vec*>(out + (row0 + r) * C + c0) = o;
+        }
+    }
+}
+
 // The multiscale branch (vae_ops.cpp:681-682): depthwise K x K (no bias) then the grouped
-// 1x1 over groups of 32 channels, fused per (8 x 8 pixel tile, group). qkv / out:
-// [pixels, C3] rows; dw [C3, K*K] and gw [C3, 32] fp32 (rows in the same permuted group
-// order as the qkv columns).
-constexpr int kMsTile = 8;
+// 1x1 over groups of 32 channels, fused per (16 x 8 pixel tile, group). qkv / out:
+// [pixels, C3] rows (C3 % 8 == 0, 16-byte aligned); weights fp32 per group of 32 channels
+// (in the permuted group order of the qkv columns), channel-fastest so a warp's loads are
+// coalesced: dw [C3 / 32, K*K, 32], gw [C3 / 32, 32 inputs, 32 outputs]. Depthwise: thread (channel c,
+// column pair) slides down its two columns, each input row read once for the 8 outputs
+// it feeds; grouped: thread (output channel o) over 16 pixels with 16-byte broadcast reads.
+constexpr int kMsTileX = 16, kMsTileY = 8, kMsPix = kMsTileX * kMsTileY;
 template <class T, int K>
 __global__ void __launch_bounds__(256) ms_branch_kernel(const T* __restrict__ qkv, int B, int H, int W, int C3,
                                                         const float* __restrict__ dw, const float* __restrict__ gw,
                                                         T* __restrict__ out) {
-    constexpr int R = K / 2, HALO = kMsTile + K - 1;
-    __shared__ float s_in[HALO * HALO][33];
-    __shared__ float s_dw[kMsTile * kMsTile][33];
-    __shared__ float s_w[32][K * K];
-    __shared__ float s_g[32][33];
-    const int tiles_x = (W + kMsTile - 1) / kMsTile;
-    const int tx0 = (blockIdx.x % tiles_x) * kMsTile, ty0 = (blockIdx.x / tiles_x) * kMsTile;
+    constexpr int R = K / 2, HX = kMsTileX + K - 1, HY = kMsTileY + K - 1;
+    constexpr int kVec = 16 / sizeof(T);  // channels per 16-byte load
+    __shared__ float s_in[HX * HY][33];
+    __shared__ __align__(16) float s_d[kMsPix][32];
+    const int tiles_x = (W + kMsTileX - 1) / kMsTileX;
+    const int tx0 = (blockIdx.x % tiles_x) * kMsTileX, ty0 = (blockIdx.x / tiles_x) * kMsTileY;
     const int g = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+    const int c = tid & 31, col = tid >> 5;
     const long long img = static_cast<long long>(b) * H * W;
-    for (int i = tid; i < HALO * HALO * 32; i += blockDim.x) {
-        const int c = i & 31, pix = i >> 5, y = ty0 - R + pix / HALO, x = tx0 - R + pix % HALO;
-        float v = 0.f;
-        if (y >= 0 && y < H && x >= 0 && x < W) v = to_f(qkv[(img + static_cast<long long>(y) * W + x) * C3 + g * 32 + c]);
-        s_in[pix][c] = v;
-    }
-    for (int i = tid; i < 32 * K * K; i += blockDim.x) s_w[i / (K * K)][i % (K * K)] = dw[static_cast<long long>(g) * 32 * K * K + i];
-    for (int i = tid; i < 32 * 32; i += blockDim.x) s_g[i >> 5][i & 31] = gw[static_cast<long long>(g) * 32 * 32 + i];
-    __syncthreads();
-    for (int i = tid; i < kMsTile * kMsTile * 32; i += blockDim.x) {
-        const int c = i & 31, p = i >> 5, py = p / kMsTile, px = p % kMsTile;
-        float sum = 0.f;
+    for (int i = tid; i < HX * HY * (32 / kVec); i += blockDim.x) {
+        const int cv = i % (32 / kVec), pix = i / (32 / kVec);
+        const int y = ty0 - R + pix / HX, x = tx0 - R + pix % HX;
+        float* dst = &s_in[pix][cv * kVec];
+        if (y >= 0 && y < H && x >= 0 && x < W) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(qkv + (img + static_cast<long long>(y) * W + x) * C3 +
+                                                              g * 32 + cv * kVec);
+            const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-        for (int ky = 0; ky < K; ++ky)
+            for (int k = 0; k < kVec; ++k) dst[k] = to_f(e[k]);
+        } else {
 #pragma unroll
-            for (int kx = 0; kx < K; ++kx) sum += s_in[(py + ky) * HALO + px + kx][c] * s_w[c][ky * K + kx];
-        s_dw[p][c] = sum;
+            for (int k = 0; k < kVec; ++k) dst[k] = 0.f;
+        }
     }
+    float wk[K * K];
+#pragma unroll
+    for (int k = 0; k < K * K; ++k) wk[k] = dw[(static_cast<long long>(g) * K * K + k) * 32 + c];
     __syncthreads();
-    for (int i = tid; i < kMsTile * kMsTile * 32; i += blockDim.x) {
-        const int o = i & 31, p = i >> 5, y = ty0 + p / kMsTile, x = tx0 + p % kMsTile;
-        if (y >= H || x >= W) continue;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        const int px = col + 8 * half;
+        float acc[kMsTileY];
+#pragma unroll
+        for (int py = 0; py < kMsTileY; ++py) acc[py] = 0.f;
+#pragma unroll
+        for (int r = 0; r < HY; ++r) {
+            float v[K];
+#pragma unroll
+            for (int kx = 0; kx < K; ++kx) v[kx] = s_in[r * HX + px + kx][c];
+#pragma unroll
+            for (int py = 0; py < kMsTileY; ++py) {
+                const int ky = r - py;
+                if (ky >= 0 && ky < K) {
+#pragma unroll
+                    for (int kx = 0; kx < K; ++kx) acc[py] = fmaf(v[kx], wk[ky * K + kx], acc[py]);
+                }
+            }
+        }
+#pragma unroll
+        for (int py = 0; py < kMsTileY; ++py) s_d[py * kMsTileX + px][c] = acc[py];
+    }
+    float gk[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) gk[k] = gw[(static_cast<long long>(g) * 32 + k) * 32 + c];
+    __syncthreads();
+#pragma unroll 2
+    for (int j = 0; j < kMsPix / 8; ++j) {
+        const int p = j * 8 + col, y = ty0 + p / kMsTileX, x = tx0 + p % kMsTileX;
+        const float4* dp = reinterpret_cast<const float4*>(s_d[p]);
         float acc = 0.f;
-#pragma unroll 8
-        for (int k = 0; k < 32; ++k) acc += s_g[o][k] * s_dw[p][k];
-        out[(img + static_cast<long long>(y) * W + x) * C3 + g * 32 + o] = from_f<T>(acc);
+#pragma unroll
+        for (int k4 = 0; k4 < 8; ++k4) {
+            const float4 d4 = dp[k4];
+            acc = fmaf(gk[4 * k4], d4.x, acc);
+            acc = fmaf(gk[4 * k4 + 1], d4.y, acc);
+            acc = fmaf(gk[4 * k4 + 2], d4.z, acc);
+            acc = fmaf(gk[4 * k4 + 3], d4.w, acc);
+        }
+        if (y < H && x < W) out[(img + static_cast<long long>(y) * W + x) * C3 + g * 32 + c] = from_f<T>(acc);
     }
 }
 
 // conv_out (vae.cpp:320-324): 3x3 "same" from NHWC rows [pixels, C] to NCHW fp32 with few
-// output channels (Co <= 4); one thread per output pixel, the weights [4, 9, C] fp32 (zero
-// rows past Co) staged in shared memory. C <= kConvOutMaxC.
-constexpr int kConvOutMaxC = 256;
-template <class T>
-__global__ void __launch_bounds__(128) vae_conv_out_kernel(const T* __restrict__ in, int B, int H, int W, int C,
+// output channels (Co <= 4). A warp walks kConvOutPix consecutive pixels; lane l holds
+// channels [l * CPL, l * CPL + CPL) (those below C; C <= 32 * CPL), so each tap's row is one coalesced
+// load; the four output sums are reduced across the warp per pixel. Weights are staged in
+// shared memory as [9][4][CPL][32 lanes] fp32 (zero past Co or C), so a lane's reads are
+// consecutive words across the warp (no bank conflicts).
+constexpr int kConvOutPix = 8;
+template <class T, int CPL>
+__global__ void __launch_bounds__(256) vae_conv_out_kernel(const T* __restrict__ in, int B, int H, int W, int C,
                                                            const float* __restrict__ w, const float* __restrict__ bias,
                                                            int Co, float* __restrict__ out) {
-    __shared__ float s_w[9 * kConvOutMaxC][4];
-    for (int i = threadIdx.x; i < 9 * C; i += blockDim.x)
-#pragma unroll
-        for (int o = 0; o < 4; ++o) s_w[i][o] = o < Co ? w[static_cast<long long>(o) * 9 * C + i] : 0.f;
+    extern __shared__ float s_w[];  // [9][4][CPL][32]
+    for (int i = threadIdx.x; i < 9 * 4 * CPL * 32; i += blockDim.x) {
+        const int l = i & 31, j = (i >> 5) % CPL, o = (i / (32 * CPL)) % 4, tap = i / (128 * CPL);
+        const int c = l * CPL + j;
+        s_w[i] = (o < Co && c < C) ? w[(static_cast<long long>(o) * 9 + tap) * C + c] : 0.f;
+    }
     __syncthreads();
-    const long long p = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const long long P = static_cast<long long>(B) * H * W;
-    if (p >= P) return;
-    const int x = static_cast<int>(p % W), y = static_cast<int>((p / W) % H);
-    const int b = static_cast<int>(p / (static_cast<long long>(W) * H));
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int tap = 0; tap < 9; ++tap) {
-        const int iy = y + tap / 3 - 1, ix = x + tap % 3 - 1;
-        if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;
-        const T* src = in + ((static_cast<long long>(b) * H + iy) * W + ix) * C;
-        const float(*wt)[4] = s_w + tap * C;
-        for (int c = 0; c < C; ++c) {
-            const float v = to_f(src[c]);
+    const int lane = threadIdx.x & 31;
+    const int P = H * W, b = blockIdx.y;
+    const int p0 = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * kConvOutPix;
+    for (int k = 0; k < kConvOutPix; ++k) {
+        const int p = p0 + k;
+        if (p >= P) break;
+        const int x = p % W, y = p / W;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int tap = 0; tap < 9; ++tap) {
+            const int iy = y + tap / 3 - 1, ix = x + tap % 3 - 1;
+            if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;
+            const T* src = in + ((static_cast<long long>(b) * H + iy) * W + ix) * C + lane * CPL;
+            if (lane * CPL >= C) continue;
+            float v[CPL];
 #pragma unroll
-            for (int o = 0; o < 4; ++o) acc[o] = fmaf(wt[c][o], v, acc[o]);
+            for (int j = 0; j < CPL; ++j) v[j] = to_f(src[j]);
+            const float* wt = s_w + tap * 128 * CPL + lane;
+#pragma unroll
+            for (int o = 0; o < 4; ++o)
+#pragma unroll
+                for (int j = 0; j < CPL; ++j) acc[o] = fmaf(wt[(o * CPL + j) * 32], v[j], acc[o]);
+        }
+#pragma unroll
+        for (int o = 0; o < 4; ++o)
+#pragma unroll
+            for (int sh = 16; sh > 0; sh >>= 1) acc[o] += __shfl_xor_sync(0xffffffffu, acc[o], sh);
+        if (lane < Co) {
+            float r = acc[0];
+#pragma unroll
+            for (int o = 1; o < 4; ++o)
+                if (lane == o) r = acc[o];
+            out[((static_cast<long long>(b) * Co + lane) * H + y) * W + x] = r + bias[lane];
         }
     }
-    for (int o = 0; o < Co; ++o) out[((static_cast<long long>(b) * Co + o) * H + y) * W + x] = acc[o] + bias[o];
 }
 
 // --- host-side weight preparation -------------------------------------------------------
@@ -302,6 +418,16 @@ std::vector<float> parity_weights(const float* w, int Cout, int Cin) {
                                     sum += w[((static_cast<size_t>(o) * Cin + c) * 3 + ky) * 3 + kx];
                             r[((static_cast<size_t>(2 * i + j) * Cout + o) * 4 + (2 * a + c2)) * Cin + c] = sum;
                         }
+    return r;
+}
+
+// Per group of 32 rows of `rows` ([groups * 32, n]): the [32, n] block transposed to [n, 32].
+std::vector<float> group_transpose(const std::vector<float>& rows, size_t n) {
+    std::vector<float> r(rows.size());
+    const size_t groups = rows.size() / (32 * n);
+    for (size_t g = 0; g < groups; ++g)
+        for (size_t c = 0; c < 32; ++c)
+            for (size_t k = 0; k < n; ++k) r[(g * n + k) * 32 + c] = rows[(g * 32 + c) * n + k];
     return r;
 }
 
@@ -428,8 +554,12 @@ void VaeDecoder::upload_impl(const float* const* t) {
                 std::vector<float> qkv(3 * CC * CC);
                 for (int m = 0; m < 3; ++m) std::memcpy(&qkv[m * CC * CC], t[j + m], CC * CC * sizeof(float));
                 put<T>(L.wqkv, permute_groups(qkv, heads, hd, CC));
-                put<float>(L.msdw, permute_groups(copy_of(t[j + 3], 3 * CC * k * k), heads, hd, static_cast<size_t>(k * k)));
-                put<float>(L.msgw, permute_groups(copy_of(t[j + 4], 3 * CC * hd), heads, hd, static_cast<size_t>(hd)));
+                put<float>(L.msdw, group_transpose(permute_groups(copy_of(t[j + 3], 3 * CC * k * k), heads, hd,
+                                                                  static_cast<size_t>(k * k)),
+                                                   static_cast<size_t>(k * k)));
+                put<float>(L.msgw, group_transpose(permute_groups(copy_of(t[j + 4], 3 * CC * hd), heads, hd,
+                                                                  static_cast<size_t>(hd)),
+                                                   static_cast<size_t>(hd)));
                 put<T>(L.wout, copy_of(t[j + 5], CC * 2 * CC));
                 put<float>(L.n1w, copy_of(t[j + 6], CC));
                 put<float>(L.n1b, copy_of(t[j + 7], CC));
@@ -447,7 +577,9 @@ void VaeDecoder::upload_impl(const float* const* t) {
 }
 
 void VaeDecoder::ensure_workspace(int B, int h, int w) {
-    const long long key = (static_cast<long long>(B) << 40) ^ (static_cast<long long>(h) << 20) ^ w;
+    // the patch buffer's size depends on which shapes take the implicit path
+    const long long key = (static_cast<long long>(B) << 40) ^ (static_cast<long long>(h) << 20) ^ w ^
+                          (static_cast<long long>(implicit_ok(128, 128, 64)) << 62);
     if (key == ws_key_) return;
     const size_t as = eng_.mode() == kModeBf16 ? 2 : 4;
     size_t x = 0, col = 0, qkv = 0, merged = 0, inv = 0, glu = 0, partial = 0;
@@ -458,15 +590,17 @@ void VaeDecoder::ensure_workspace(int B, int h, int w) {
         const VaeBlockDims& bd = d_.blocks[i];
         const size_t C = static_cast<size_t>(bd.channels);
         if (bd.has_upsample) {
+            const int Cin = d_.blocks[i + 1].channels;
+            if (!implicit_ok(static_cast<int>(H), static_cast<int>(W), Cin) || bd.channels % 8 != 0)
+                col = std::max(col, static_cast<size_t>(B * H * W) * 4 * 9 * Cin);
             H *= 2;
             W *= 2;
-            col = std::max(col, static_cast<size_t>(B * H * W) * 9 * d_.blocks[i + 1].channels);
         }
         const size_t P = static_cast<size_t>(B * H * W);
         x = std::max(x, P * C);
         if (bd.layers == 0) continue;
         if (bd.is_res_block) {
-            col = std::max(col, P * 9 * C);
+            if (!implicit_ok(static_cast<int>(H), static_cast<int>(W), static_cast<int>(C))) col = std::max(col, P * 9 * C);
         } else {
             qkv = std::max(qkv, P * 3 * C);
             merged = std::max(merged, P * 2 * C);
@@ -586,17 +720,23 @@ void VaeDecoder::conv_gemm(const T* in, int B, int H, int W, int Cin, int kh, in
 template <class T>
 void VaeDecoder::upsample_conv(const T* in, int B, int H, int W, int Cin, const Block& blk, int Cout, T* out) {
     const cudaStream_t st = eng_.stream();
-    if (sizeof(T) == 2 && implicit_ok(H, W, Cin) && Cout % 8 == 0) {
-        // four 2x2 convolutions on the low-resolution image, one per output parity
-        T* par = par_.as<T>();
-        const long long plane = static_cast<long long>(B) * H * W * Cout;
-        for (int ij = 0; ij < 4; ++ij)
-            conv_gemm<T>(in, B, H, W, Cin, 2, 2, (ij >> 1) - 1, (ij & 1) - 1,
-                         blk.upw4.as<T>() + static_cast<long long>(ij) * Cout * 4 * Cin, blk.upb.as<float>(), Cout,
-                         kActNone, par + ij * plane);
-        const long long n = 4 * plane / 8;
-        shuffle_shortcut_kernel<T><<<blocks_for(n), 256, 0, st>>>(par, in, B, H, W, Cin, Cout, out);
-    } else {
+    if constexpr (sizeof(T) == 2) {
+        if (implicit_ok(H, W, Cin) && Cout % 8 == 0) {
+            // four 2x2 convolutions on the low-resolution image, one per output parity
+            T* par = par_.as<T>();
+            const long long plane = static_cast<long long>(B) * H * W * Cout;
+            for (int ij = 0; ij < 4; ++ij)
+                conv_gemm<T>(in, B, H, W, Cin, 2, 2, (ij >> 1) - 1, (ij & 1) - 1,
+                             blk.upw4.as<T>() + static_cast<long long>(ij) * Cout * 4 * Cin, blk.upb.as<float>(), Cout,
+                             kActNone, par + ij * plane);
+            const dim3 grid(blocks_for(4LL * H * W * (Cout / 8)), B);
+            shuffle_shortcut_kernel<<<grid, 256, 0, st>>>(par, in, B, H, W, Cin, Cout, out);
+            SANA_CUDA(cudaGetLastError());
+            ++launches_;
+            return;
+        }
+    }
+    {
         conv3x3<T>(in, B, H, W, Cin, true, blk.upw, blk.upb.as<float>(), Cout, kActNone, out);
         const long long nout = static_cast<long long>(B) * (2 * H) * (2 * W) * Cout;
         up_shortcut_kernel<T><<<blocks_for(nout), 256, 0, st>>>(out, in, B, H, W, Cin, Cout);
@@ -614,6 +754,8 @@ void VaeDecoder::conv3x3(const T* in, int B, int H, int W, int Cin, bool upsampl
     }
     const int up = upsample ? 1 : 0;
     T* col = col_.as<T>();
+    const size_t need = static_cast<size_t>(B) * (H << up) * (W << up) * 9 * Cin * sizeof(T);
+    if (col_.bytes() < need) throw std::runtime_error("vae patch buffer smaller than the convolution needs");
     launch_im2col<T>(in, B, H, W, Cin, up, col, eng_.stream());
     ++launches_;
     const long long P = static_cast<long long>(B) * (H << up) * (W << up);
@@ -631,8 +773,26 @@ void VaeDecoder::decode_impl(const float* lat_d, int B, int h, int w, float* out
     T* g = g_.as<T>();
     auto rms = [&](const T* src, long long rows, int Cc, const DevBuf& nw, const DevBuf& nb, const T* resid, int relu,
                    T* dst) {
-        rms_rows_kernel<T><<<blocks_for(rows * 32, 256), 256, 0, st>>>(src, rows, Cc, nw.as<float>(), nb.as<float>(),
-                                                                       1e-5f, resid, relu, dst);
+        const int grid = blocks_for(rows * 32, 256);
+        const float* wn = nw.as<float>();
+        const float* bn = nb.as<float>();
+        // rows per warp: enough loads in flight per warp for the narrow rows
+        auto vgrid = [&](int rpw) { return blocks_for(rows, 8 * rpw); };
+        if constexpr (sizeof(T) == 2) {
+            if (Cc == 128) {
+                rms_rows_vec_kernel<4, 1, 4><<<vgrid(4), 256, 0, st>>>(src, rows, Cc, wn, bn, 1e-5f, resid, relu, dst);
+            } else if (Cc == 256) {
+                rms_rows_vec_kernel<8, 1, 4><<<vgrid(4), 256, 0, st>>>(src, rows, Cc, wn, bn, 1e-5f, resid, relu, dst);
+            } else if (Cc == 512) {
+                rms_rows_vec_kernel<8, 2, 2><<<vgrid(2), 256, 0, st>>>(src, rows, Cc, wn, bn, 1e-5f, resid, relu, dst);
+            } else if (Cc == 1024) {
+                rms_rows_vec_kernel<8, 4, 1><<<vgrid(1), 256, 0, st>>>(src, rows, Cc, wn, bn, 1e-5f, resid, relu, dst);
+            } else {
+                rms_rows_kernel<T><<<grid, 256, 0, st>>>(src, rows, Cc, wn, bn, 1e-5f, resid, relu, dst);
+            }
+        } else {
+            rms_rows_kernel<T><<<grid, 256, 0, st>>>(src, rows, Cc, wn, bn, 1e-5f, resid, relu, dst);
+        }
         SANA_CUDA(cudaGetLastError());
         ++launches_;
     };
@@ -667,7 +827,7 @@ void VaeDecoder::decode_impl(const float* lat_d, int B, int h, int w, float* out
                 T* ms = ms_.as<T>();
                 T* merged = merged_.as<T>();
                 gemm_rows<T>(x, P, C, L.wqkv, nullptr, 3 * C, kActNone, qkv);
-                const dim3 grid(ceil_div(W, kMsTile) * ceil_div(H, kMsTile), 3 * heads, B);
+                const dim3 grid(ceil_div(W, kMsTileX) * ceil_div(H, kMsTileY), 3 * heads, B);
                 if (d.ms_kernel == 5)
                     ms_branch_kernel<T, 5><<<grid, 256, 0, st>>>(qkv, B, H, W, 3 * C, L.msdw.as<float>(),
                                                                 L.msgw.as<float>(), ms);
@@ -700,8 +860,20 @@ void VaeDecoder::decode_impl(const float* lat_d, int B, int h, int w, float* out
     }
     const long long P = static_cast<long long>(B) * H * W;
     rms(x, P, C, nout_w_, nout_b_, nullptr, 1, y);
-    vae_conv_out_kernel<T><<<blocks_for(P, 128), 128, 0, st>>>(y, B, H, W, C, cout_w_.as<float>(),
-                                                              cout_b_.as<float>(), d.out_channels, out_d);
+    {
+        const dim3 grid(blocks_for(static_cast<long long>(H) * W, 8 * kConvOutPix), B);
+        auto go = [&](auto kern, int cpl) {
+            const size_t smem = static_cast<size_t>(9) * 4 * cpl * 32 * sizeof(float);
+            kern<<<grid, 256, smem, st>>>(y, B, H, W, C, cout_w_.as<float>(), cout_b_.as<float>(), d.out_channels,
+                                          out_d);
+        };
+        // channels per lane: C / 32 rounded up to 1, 2, 4 or 8 (C is a multiple of 8, so a
+        // lane's chunk is either wholly below C or wholly past it)
+        if (C <= 32) go(vae_conv_out_kernel<T, 1>, 1);
+        else if (C <= 64) go(vae_conv_out_kernel<T, 2>, 2);
+        else if (C <= 128) go(vae_conv_out_kernel<T, 4>, 4);
+        else go(vae_conv_out_kernel<T, 8>, 8);
+    }
     SANA_CUDA(cudaGetLastError());
     ++launches_;
     // x/y/g rotate through three buffers; keep the members pointing at distinct storage

@@ -50,7 +50,7 @@ class VaeDecoder {
    private:
     struct Layer {
         DevBuf c1w, c1b, c2w;                    // ResBlock: conv weights [C, 9, C] (act type)
-        DevBuf wqkv, msdw, msgw, wout;           // attention: [3C, C], [3C, k*k] f32, [3C, hd] f32, [C, 2C]
+        DevBuf wqkv, msdw, msgw, wout;           // attention: [3C, C], [3C/32, k*k, 32] f32, [3C/32, 32, 32] f32, [C, 2C]
         DevBuf winv, binv, wdw, bdw, wpt;        // GLUMBConv: [8C, C], [8C], [8C, 9] f32, [8C], [C, 4C]
         DevBuf n1w, n1b, n2w, n2b;               // RMSNorm weight / bias (ResBlock: n1 only)
     };

@@ -11,8 +11,9 @@ namespace sana_cuda_shim {
 void configure(int device, int mode);
 
 // The entry points keep one device copy of the last SanaDenoiserWeights (or SanaBlockWeights)
-// they were given, recognised by the addresses and sizes of its tensors. A caller that
-// overwrites weight values in place calls this so that the next call uploads them again.
+// and of the last SanaVaeWeights they were given, recognised by the addresses and sizes of
+// their tensors. A caller that overwrites weight values in place calls this so that the next
+// call uploads them again.
 void invalidate_weights();
 
 }  // namespace sana_cuda_shim

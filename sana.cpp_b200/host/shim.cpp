@@ -26,6 +26,7 @@ struct Key {
     bool operator==(const Key& o) const { return kind == o.kind && t == o.t; }
 };
 Key g_key;
+unsigned g_epoch = 1;  // bumped whenever cached device weights may be stale (new handle, invalidate)
 
 int env_int(const char* name, int def) {
     const char* v = std::getenv(name);
@@ -88,6 +89,7 @@ sana_cuda_ctx* handle() {
         g_ctx = c;
         g_mode = m;
         g_key = Key();
+        ++g_epoch;
     }
     return g_ctx;
 }
@@ -95,6 +97,11 @@ sana_cuda_ctx* handle() {
 int mode() {
     handle();
     return g_mode;
+}
+
+unsigned weights_epoch() {
+    std::lock_guard<std::mutex> lock(g_mu);
+    return g_epoch;
 }
 
 void check(int rc) {
@@ -210,11 +217,13 @@ void configure(int device, int mode) {
     sana_shim::g_device = device;
     sana_shim::g_mode = mode;
     sana_shim::g_key = sana_shim::Key();
+    ++sana_shim::g_epoch;
 }
 
 void invalidate_weights() {
     std::lock_guard<std::mutex> lock(sana_shim::g_mu);
     sana_shim::g_key = sana_shim::Key();
+    ++sana_shim::g_epoch;
 }
 
 }  // namespace sana_cuda_shim

@@ -17,6 +17,9 @@ namespace sana_shim {
 
 sana_cuda_ctx* handle();
 int mode();
+// Changes whenever device copies of weights may no longer match the caller's tensors (a new
+// handle, configure(), invalidate_weights()); caches compare it with the value they saw.
+unsigned weights_epoch();
 void check(int rc);
 // Data pointer of a tensor, nullptr when it holds no elements.
 const float* ptr(const Tensor& t);

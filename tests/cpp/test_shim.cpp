@@ -23,6 +23,7 @@
 #include "scheduler.h"
 #include "transformer.h"
 #include "transformer_ops.h"
+#include "vae.h"
 
 namespace {
 
@@ -313,6 +314,115 @@ void bf16_consistency() {
     expect(e_half < 2e-2 && half.step_index == 4, "loop resumes a started state");
 }
 
+// run_vae_decode through the reference's SanaVaeWeights structure: the same image as the C
+// ABI given the documented tensor table, the validators' std::invalid_argument contracts,
+// and a fresh upload after invalidate_weights().
+void vae_decode_entry_point() {
+    std::mt19937 g{77};
+    std::normal_distribution<float> nd(0.0f, 1.0f);
+    auto rnd = [&](std::vector<size_t> shape, float scale, float offset = 0.0f) {
+        Tensor t(std::move(shape));
+        for (float& v : t.data()) v = offset + scale * nd(g);
+        return t;
+    };
+    const size_t Cl = 8, ch[3] = {16, 32, 64};
+    SanaVaeWeights w{SanaVaeDecoderWeights{rnd({ch[2], Cl, 3, 3}, 0.02f), rnd({ch[2]}, 0.02f), rnd({ch[0]}, 0.1f, 1.0f),
+                                           rnd({ch[0]}, 0.1f), rnd({3, ch[0], 3, 3}, 0.02f), rnd({3}, 0.02f), {}},
+                     0.5f, 32};
+    SanaVaeDecoderWeights& d = w.decoder;
+    for (int i = 0; i < 3; ++i) {
+        const size_t c = ch[i];
+        SanaVaeUpBlockWeights b;
+        if (i < 2) {
+            b.upsample_conv_weight = rnd({c, ch[i + 1], 3, 3}, 0.02f);
+            b.upsample_conv_bias = rnd({c}, 0.02f);
+            b.is_res_block = true;
+            for (int l = 0; l < 1 + i; ++l)
+                b.res_blocks.push_back({rnd({c, c, 3, 3}, 0.02f), rnd({c}, 0.02f), rnd({c, c, 3, 3}, 0.02f),
+                                        rnd({c}, 0.1f, 1.0f), rnd({c}, 0.1f)});
+        } else {
+            for (int l = 0; l < 2; ++l) {
+                SanaVaeAttnGlumbLayerWeights layer{
+                    {rnd({c, c, 1, 1}, 0.02f), rnd({c, c, 1, 1}, 0.02f), rnd({c, c, 1, 1}, 0.02f),
+                     rnd({3 * c, 1, 5, 5}, 0.02f), rnd({3 * c, 32, 1, 1}, 0.02f), rnd({c, 2 * c, 1, 1}, 0.02f),
+                     rnd({c}, 0.1f, 1.0f), rnd({c}, 0.1f)},
+                    {rnd({8 * c, c, 1, 1}, 0.02f), rnd({8 * c}, 0.02f), rnd({8 * c, 1, 3, 3}, 0.02f),
+                     rnd({8 * c}, 0.02f), rnd({c, 4 * c, 1, 1}, 0.02f), rnd({c}, 0.1f, 1.0f), rnd({c}, 0.1f)}};
+                b.attn_glumb_layers.push_back(std::move(layer));
+            }
+        }
+        d.up_blocks.push_back(std::move(b));
+    }
+    const Tensor lat = rnd({2, Cl, 4, 6}, 1.0f);
+    const Tensor img = run_vae_decode(lat, w);
+    expect(img.rank() == 4 && img.dim_size(0) == 2 && img.dim_size(1) == 3 && img.dim_size(2) == 16 &&
+               img.dim_size(3) == 24,
+           "run_vae_decode output shape [2, 3, 16, 24]");
+
+    // the C ABI on its own handle, tensors in include/sana_cuda.h's documented order
+    std::vector<const float*> table;
+    auto add = [&](const Tensor& t) { table.push_back(t.data().data()); };
+    for (const Tensor* t : {&d.conv_in_weight, &d.conv_in_bias, &d.norm_out_weight, &d.norm_out_bias,
+                            &d.conv_out_weight, &d.conv_out_bias})
+        add(*t);
+    sana_vae_dims dims{};
+    dims.latent_channels = static_cast<int>(Cl);
+    dims.out_channels = 3;
+    dims.n_blocks = 3;
+    dims.head_dim = 32;
+    dims.ms_kernel = 5;
+    dims.scaling_factor = 0.5f;
+    for (int i = 0; i < 3; ++i) {
+        const SanaVaeUpBlockWeights& b = d.up_blocks[i];
+        dims.blocks[i] = {static_cast<int>(ch[i]), i < 2 ? 1 : 0, i < 2 ? 1 : 0,
+                          static_cast<int>(i < 2 ? b.res_blocks.size() : b.attn_glumb_layers.size())};
+        if (i < 2) {
+            add(*b.upsample_conv_weight);
+            add(*b.upsample_conv_bias);
+            for (const SanaVaeResBlockWeights& r : b.res_blocks)
+                for (const Tensor* t : {&r.conv1_weight, &r.conv1_bias, &r.conv2_weight, &r.norm_weight, &r.norm_bias})
+                    add(*t);
+        } else {
+            for (const SanaVaeAttnGlumbLayerWeights& l : b.attn_glumb_layers)
+                for (const Tensor* t : {&l.attention.to_q_weight_conv1x1, &l.attention.to_k_weight_conv1x1,
+                                        &l.attention.to_v_weight_conv1x1, &l.attention.proj_in_weight,
+                                        &l.attention.proj_out_weight, &l.attention.to_out_weight_conv1x1,
+                                        &l.attention.norm_out_weight, &l.attention.norm_out_bias,
+                                        &l.glumb.conv_inverted_weight, &l.glumb.conv_inverted_bias,
+                                        &l.glumb.conv_depth_weight, &l.glumb.conv_depth_bias,
+                                        &l.glumb.conv_point_weight, &l.glumb.norm_weight, &l.glumb.norm_bias})
+                    add(*t);
+        }
+    }
+    sana_cuda_ctx* h = nullptr;
+    bool ok = sana_cuda_create(0, SANA_MODE_F32, &h) == SANA_OK;
+    ok = ok && sana_cuda_vae_upload(h, &dims, table.data()) == SANA_OK;
+    Tensor direct({2, 3, 16, 24});
+    ok = ok && sana_cuda_vae_decode(h, lat.data().data(), 2, 4, 6, direct.data().data()) == SANA_OK;
+    if (h) sana_cuda_destroy(h);
+    expect(ok && direct.data() == img.data(), "run_vae_decode equals the C ABI on the documented table");
+
+    // the validators and shape contracts (vae.cpp:172-208, 247-254)
+    throws<std::invalid_argument>([&] { run_vae_decode(Tensor({2, Cl, 4}), w); }, "vae latents of rank 3");
+    throws<std::invalid_argument>([&] { run_vae_decode(Tensor({1, Cl + 1, 2, 2}), w); }, "vae latent channels");
+    SanaVaeWeights bad = w;
+    bad.decoder.conv_in_bias = Tensor({ch[2] + 1});
+    throws<std::invalid_argument>([&] { validate_vae_weights(bad); }, "vae conv_in bias shape");
+    bad = w;
+    bad.scaling_factor = 0.0f;
+    throws<std::invalid_argument>([&] { run_vae_decode(lat, bad); }, "vae scaling factor");
+
+    // weights changed in place: the cached upload is refreshed after invalidate_weights()
+    SanaVaeWeights w2 = w;
+    const Tensor before = run_vae_decode(lat, w2);
+    for (float& v : w2.decoder.conv_out_bias.data()) v += 1.0f;
+    sana_cuda_shim::invalidate_weights();
+    const Tensor after = run_vae_decode(lat, w2);
+    double shift = 0.0;
+    for (size_t i = 0; i < after.numel(); ++i) shift += after.data()[i] - before.data()[i];
+    expect(std::fabs(shift / static_cast<double>(after.numel()) - 1.0) < 1e-4, "vae upload refreshed after invalidate");
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -331,6 +441,7 @@ int main(int argc, char** argv) {
         kat_block_forward();
         kat_scheduler();
         errors();
+        vae_decode_entry_point();
         sana_cuda_shim::configure(0, SANA_MODE_BF16);
         bf16_consistency();
     }
