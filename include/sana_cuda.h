@@ -1,7 +1,8 @@
 /*
  * sana_cuda.h — C ABI of the B200 (sm_100a) implementation of the Sana-0.6B denoiser path
  * of cconthekeyboard/sana.cpp: the linear-attention DiT blocks, their step and the
- * DPM-Solver++ classifier-free-guidance loop.
+ * DPM-Solver++ classifier-free-guidance loop; and the steps on either side of it: the text
+ * encoder's output contract (the conditioning the loop reads) and the DC-AE VAE decoder.
  *
  * Plain C: opaque handle, raw pointers and sizes, int status codes. Every call that takes
  * host buffers copies them to the device, runs, copies results back and synchronises; the
@@ -388,6 +389,15 @@ typedef struct sana_vae_dims {
  *   conv_depth.b, conv_point.w [C, 4C, 1, 1], norm.w, norm.b.
  * Shape errors of validate_vae_weights (vae.cpp:172-208) are SANA_ERR_INVALID. */
 int sana_cuda_vae_upload(sana_cuda_ctx *ctx, const sana_vae_dims *dims, const float *const *tensors);
+
+/* load_vae_weights (vae.cpp:147-170) from the reference's vae_decoder_weights.gguf: up blocks
+ * found by their "decoder.up_blocks.<n>" prefixes in numeric order, an upsample conv at
+ * layer 0 when "<prefix>.0.conv.weight" exists, ResBlocks when the first layer after it has
+ * conv1, else attention + GLUMBConv layers; three layers per block; fp32 tensors under their
+ * diffusers names uploaded straight from the mapping. Fills *dims_out if not NULL. A missing
+ * tensor is SANA_ERR_INVALID ("weight name not found in weight index"); an unreadable file, a
+ * non-fp32 tensor or a shape mismatch SANA_ERR_STATE. */
+int sana_cuda_vae_upload_gguf(sana_cuda_ctx *ctx, const char *path, float scaling_factor, sana_vae_dims *dims_out);
 
 /* run_vae_decode (vae.cpp:243-325): latents [B, latent, h, w] fp32 NCHW (host) -> image
  * [B, out, h * 2^u, w * 2^u] fp32 NCHW (host), u = the number of upsampling blocks (5 for

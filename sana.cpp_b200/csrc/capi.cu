@@ -1467,6 +1467,129 @@ int sana_cuda_vae_upload(sana_cuda_ctx* ctx, const sana_vae_dims* dims, const fl
     });
 }
 
+namespace {
+
+// Up block prefixes "decoder.up_blocks.<n>" of the file in numeric order
+// (find_vae_decoder_up_block_prefixes, vae.cpp:103-145).
+std::vector<std::string> vae_block_prefixes(const sana::GgufFile& f) {
+    static const std::string head = "decoder.up_blocks.";
+    std::set<std::pair<size_t, std::string>> ordered;
+    for (const sana::GgufTensor& t : f.tensors()) {
+        if (t.name.compare(0, head.size(), head) != 0) continue;
+        const size_t dot = t.name.find('.', head.size());
+        if (dot == std::string::npos || dot == head.size()) continue;
+        const std::string num = t.name.substr(head.size(), dot - head.size());
+        if (num.find_first_not_of("0123456789") != std::string::npos) continue;
+        ordered.insert({static_cast<size_t>(std::stoull(num)), head + num});
+    }
+    std::vector<std::string> v;
+    for (const auto& e : ordered) v.push_back(e.second);
+    return v;
+}
+
+}  // namespace
+
+int sana_cuda_vae_upload_gguf(sana_cuda_ctx* ctx, const char* path, float scaling_factor, sana_vae_dims* dims_out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(path, "invalid arguments");
+        const sana::GgufFile f(path);
+        std::vector<int64_t> sh;
+        std::vector<const float*> table;
+        auto take = [&](const std::string& name, const std::vector<int64_t>& want) {
+            table.push_back(tensor_f32(f, name, want.size(), &sh));
+            require_shape(name, sh, want);
+        };
+        auto shape_of = [&](const std::string& name, size_t rank) {
+            tensor_f32(f, name, rank, &sh);
+            return sh;
+        };
+        const std::vector<std::string> prefixes = vae_block_prefixes(f);
+        if (prefixes.empty()) throw std::invalid_argument("vae decoder must contain at least one up block");
+        if (prefixes.size() > 8) throw std::invalid_argument("vae decoder has more than 8 up blocks");
+        // load_vae_up_block_weights (vae.cpp:64-99): an upsample conv at layer 0 when present,
+        // ResBlocks only after one, three layers
+        sana::VaeDims d;
+        d.n_blocks = static_cast<int>(prefixes.size());
+        d.head_dim = 32;
+        d.ms_kernel = 5;
+        d.scaling_factor = scaling_factor;
+        std::vector<int> base(prefixes.size());
+        for (size_t i = 0; i < prefixes.size(); ++i) {
+            const std::string& pre = prefixes[i];
+            sana::VaeBlockDims& b = d.blocks[i];
+            b.has_upsample = f.find(pre + ".0.conv.weight") ? 1 : 0;
+            base[i] = b.has_upsample;
+            b.is_res_block = (b.has_upsample && f.find(pre + "." + std::to_string(base[i]) + ".conv1.weight")) ? 1 : 0;
+            b.layers = 3;
+            const std::string l0 = pre + "." + std::to_string(base[i]);
+            b.channels = static_cast<int>(
+                b.has_upsample ? shape_of(pre + ".0.conv.weight", 4)[0]
+                               : (b.is_res_block ? shape_of(l0 + ".conv1.weight", 4)[0] : shape_of(l0 + ".attn.to_q.weight", 2)[0]));
+            if (!b.is_res_block) d.ms_kernel = static_cast<int>(shape_of(l0 + ".attn.to_qkv_multiscale.0.proj_in.weight", 4)[2]);
+        }
+        const std::vector<int64_t> cin = shape_of("decoder.conv_in.weight", 4);
+        const std::vector<int64_t> cout = shape_of("decoder.conv_out.weight", 4);
+        d.latent_channels = static_cast<int>(cin[1]);
+        d.out_channels = static_cast<int>(cout[0]);
+        const int64_t n = d.n_blocks, Cn = d.blocks[n - 1].channels, C0 = d.blocks[0].channels;
+        const int64_t k = d.ms_kernel;
+        take("decoder.conv_in.weight", {Cn, cin[1], 3, 3});
+        take("decoder.conv_in.bias", {Cn});
+        take("decoder.norm_out.weight", {C0});
+        take("decoder.norm_out.bias", {C0});
+        take("decoder.conv_out.weight", {cout[0], C0, 3, 3});
+        take("decoder.conv_out.bias", {cout[0]});
+        for (int64_t i = 0; i < n; ++i) {
+            const sana::VaeBlockDims& b = d.blocks[i];
+            const std::string& pre = prefixes[static_cast<size_t>(i)];
+            const int64_t C = b.channels;
+            if (b.has_upsample) {
+                if (i + 1 >= n) throw std::invalid_argument("the innermost vae up block has no upsample");
+                take(pre + ".0.conv.weight", {C, d.blocks[i + 1].channels, 3, 3});
+                take(pre + ".0.conv.bias", {C});
+            }
+            for (int l = 0; l < b.layers; ++l) {
+                const std::string lp = pre + "." + std::to_string(base[static_cast<size_t>(i)] + l);
+                if (b.is_res_block) {
+                    take(lp + ".conv1.weight", {C, C, 3, 3});
+                    take(lp + ".conv1.bias", {C});
+                    take(lp + ".conv2.weight", {C, C, 3, 3});
+                    take(lp + ".norm.weight", {C});
+                    take(lp + ".norm.bias", {C});
+                } else {
+                    take(lp + ".attn.to_q.weight", {C, C});
+                    take(lp + ".attn.to_k.weight", {C, C});
+                    take(lp + ".attn.to_v.weight", {C, C});
+                    take(lp + ".attn.to_qkv_multiscale.0.proj_in.weight", {3 * C, 1, k, k});
+                    take(lp + ".attn.to_qkv_multiscale.0.proj_out.weight", {3 * C, 32, 1, 1});
+                    take(lp + ".attn.to_out.weight", {C, 2 * C});
+                    take(lp + ".attn.norm_out.weight", {C});
+                    take(lp + ".attn.norm_out.bias", {C});
+                    take(lp + ".conv_out.conv_inverted.weight", {8 * C, C, 1, 1});
+                    take(lp + ".conv_out.conv_inverted.bias", {8 * C});
+                    take(lp + ".conv_out.conv_depth.weight", {8 * C, 1, 3, 3});
+                    take(lp + ".conv_out.conv_depth.bias", {8 * C});
+                    take(lp + ".conv_out.conv_point.weight", {C, 4 * C, 1, 1});
+                    take(lp + ".conv_out.norm.weight", {C});
+                    take(lp + ".conv_out.norm.bias", {C});
+                }
+            }
+        }
+        vae_of(ctx).upload(d, table.data());
+        if (dims_out) {
+            dims_out->latent_channels = d.latent_channels;
+            dims_out->out_channels = d.out_channels;
+            dims_out->n_blocks = d.n_blocks;
+            dims_out->head_dim = d.head_dim;
+            dims_out->ms_kernel = d.ms_kernel;
+            dims_out->scaling_factor = d.scaling_factor;
+            for (int i = 0; i < d.n_blocks; ++i)
+                dims_out->blocks[i] = {d.blocks[i].channels, d.blocks[i].has_upsample, d.blocks[i].is_res_block,
+                                       d.blocks[i].layers};
+        }
+    });
+}
+
 int sana_cuda_vae_decode(sana_cuda_ctx* ctx, const float* latents, int B, int h, int w, float* out) {
     return guard(ctx, [&] {
         SANA_REQUIRE(latents && out, "invalid arguments");

@@ -304,6 +304,20 @@ class SanaCuda:
         self._call("sana_cuda_vae_upload", ctypes.byref(ds), table)
         self.vae_dims = dims
 
+    def vae_upload_gguf(self, path: str, scaling_factor: float = 0.41407):
+        """sana_cuda_vae_upload_gguf: the reference's vae_decoder_weights.gguf; returns the
+        VaeDims read from it."""
+        from .synthetic_vae import VaeDims, VaeDimsStruct
+        ds = VaeDimsStruct()
+        self._call("sana_cuda_vae_upload_gguf", os.fsencode(path), _f(scaling_factor), ctypes.byref(ds))
+        n = ds.n_blocks
+        self.vae_dims = VaeDims(latent_channels=ds.latent_channels, out_channels=ds.out_channels,
+                                channels=tuple(ds.blocks[i].channels for i in range(n)),
+                                res_blocks=tuple(bool(ds.blocks[i].is_res_block) for i in range(n)),
+                                layers=tuple(ds.blocks[i].layers for i in range(n)), head_dim=ds.head_dim,
+                                ms_kernel=ds.ms_kernel, scaling_factor=ds.scaling_factor)
+        return self.vae_dims
+
     def vae_decode(self, latents):
         lat = _f32(latents)
         B, _, h, w = lat.shape

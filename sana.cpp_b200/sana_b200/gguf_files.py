@@ -45,3 +45,12 @@ def write_checkpoint_gguf(tensors: Sequence[np.ndarray], n_blocks: int, director
             blocks.append((f"{block_prefix}.{b}.{suffix}", tensors[16 + 19 * b + j]))
     _write(paths["model"], blocks)
     return paths
+
+
+def write_vae_gguf(dims, tensors: Sequence[np.ndarray], path: str) -> str:
+    """The reference's vae_decoder_weights.gguf from VAE tensors in
+    ``sana_b200.synthetic_vae`` upload order (their diffusers names, fp32, PyTorch layouts)."""
+    from .synthetic_vae import vae_tensor_specs
+    specs = vae_tensor_specs(dims)
+    _write(path, [(name, t) for (name, _, _), t in zip(specs, tensors)])
+    return path

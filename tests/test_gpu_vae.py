@@ -176,3 +176,43 @@ def test_vae_argument_errors():
     bad = sv.VaeDims(latent_channels=6, channels=(16, 32, 64), res_blocks=(True, True, False), layers=(1, 1, 1))
     with pytest.raises(ValueError, match="divisible by latent channels"):
         g.vae_upload(bad, sv.generate_vae(bad, randn_torch_cpu, 1))
+
+
+def test_vae_gguf_upload_matches_pointer_upload(tmp_path):
+    """vae_decoder_weights.gguf written under the reference's names loads into the same decoder
+    as the pointer table (load_vae_weights' structure discovery, vae.cpp:64-170)."""
+    from sana_b200 import SANA_MODE_BF16, SanaCuda, randn_torch_cpu
+    from sana_b200 import synthetic_vae as sv
+    from sana_b200.gguf_files import write_vae_gguf
+    dims = sv.VaeDims(latent_channels=8, out_channels=3, channels=(16, 32, 64), res_blocks=(True, True, False),
+                      layers=(3, 3, 3), head_dim=32, ms_kernel=5, scaling_factor=0.41407)
+    tensors = sv.generate_vae(dims, randn_torch_cpu, 13)
+    path = write_vae_gguf(dims, tensors, str(tmp_path / "vae_decoder_weights.gguf"))
+    lat = latents(dims, 1, 4, 4, 13)
+    a = SanaCuda(0, SANA_MODE_BF16)
+    a.vae_upload(dims, tensors)
+    b = SanaCuda(0, SANA_MODE_BF16)
+    got = b.vae_upload_gguf(path, 0.41407)
+    import dataclasses
+    assert abs(got.scaling_factor - dims.scaling_factor) < 1e-7
+    assert dataclasses.replace(got, scaling_factor=dims.scaling_factor) == dims
+    assert np.array_equal(a.vae_decode(lat), b.vae_decode(lat))
+
+
+def test_vae_gguf_errors_follow_the_loader(tmp_path):
+    from sana_b200 import SANA_MODE_BF16, SanaCuda, SanaError, randn_torch_cpu
+    from sana_b200 import synthetic_vae as sv
+    from sana_b200.gguf_files import _write
+    dims = sv.VaeDims(latent_channels=8, out_channels=3, channels=(16, 32, 64), res_blocks=(True, True, False),
+                      layers=(3, 3, 3))
+    specs = sv.vae_tensor_specs(dims)
+    tensors = sv.generate_vae(dims, randn_torch_cpu, 2)
+    g = SanaCuda(0, SANA_MODE_BF16)
+    missing = str(tmp_path / "missing.gguf")
+    _write(missing, [(n, t) for (n, _, _), t in zip(specs, tensors) if n != "decoder.conv_out.bias"])
+    with pytest.raises(ValueError, match="weight name not found"):
+        g.vae_upload_gguf(missing)
+    bad = str(tmp_path / "bad.gguf")
+    _write(bad, [(n, t if n != "decoder.conv_in.bias" else t[:-1]) for (n, _, _), t in zip(specs, tensors)])
+    with pytest.raises(SanaError, match="shape"):
+        g.vae_upload_gguf(bad)
