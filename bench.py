@@ -167,6 +167,29 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
 
 
+def vae_cpu_sample(vd, threads=None):
+    """The reference's run_vae_decode (oracle/_ref; the oracle port without it) on this host:
+    one decode of 4 x 4 latents (a 128 x 128 image) per thread, all threads at once, scaled
+    to the 1024 x 1024 decode by algorithmic FLOPs (the decoder's work is linear in pixels)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Oracle, Reference
+    from sana_b200 import randn_torch_cpu
+    from sana_b200 import synthetic_vae as sv
+    impl, kind = (Reference(), "reference") if Reference.available() else (Oracle(), "port")
+    threads = 1 if kind == "port" else (threads or min(64, len(os.sched_getaffinity(0))))
+    tensors = sv.generate_vae(vd, randn_torch_cpu, 3)
+    lats = [randn_torch_cpu(vd.latent_channels * 16, 900 + i).reshape(1, vd.latent_channels, 4, 4)
+            for i in range(threads)]
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(lambda x: impl.vae_decode(vd, tensors, x), lats))
+    dt = time.perf_counter() - t0
+    scale = sv.vae_flops(vd, 32, 32) / sv.vae_flops(vd, 4, 4)
+    ms_per_image = dt * 1000.0 * scale / threads
+    return {"value": round(ms_per_image, 1), "unit": "ms per 1024x1024 image (throughput)", "cores": threads,
+            "kind": kind, "sample": f"{threads} decodes of 4x4 latents in {dt:.1f} s, scaled by FLOPs x{scale:.0f}"}
+
+
 # ------------------------------------------------------------------------------------------
 # CPU baseline (the reference's own code) — a bounded sample on this host's cores
 # ------------------------------------------------------------------------------------------
@@ -319,7 +342,7 @@ def run_microbench(args):
                 times.append(e0.elapsed_time(e1))
         return statistics.median(times)
 
-    def report(name, what, ms, work, bound):
+    def report(name, what, ms, work, bound, extra=None):
         if bound == "hbm":
             ach, peak, unit = work / ms / 1e6, pk["hbm_gbs"], "GB/s"
         else:
@@ -327,7 +350,8 @@ def run_microbench(args):
         print(json.dumps({"microbench": name, "workload": what, "ms": round(ms, 4), "bound": bound,
                           "algorithmic": work, "achieved": round(ach, 1), "peak": peak, "unit": unit,
                           "frac": round(ach / peak, 3), "peak_source": f"{pk_kind} (burst: op timed alone)",
-                          "steps": args.steps, "warmup": args.warmup, "l2": "flushed before every launch"}),
+                          "steps": args.steps, "warmup": args.warmup, "l2": "flushed before every launch",
+                          **(extra or {})}),
               flush=True)
 
     for name in ops:
@@ -341,7 +365,8 @@ def run_microbench(args):
             img = torch.empty(1, vd.out_channels, 1024, 1024, device="cuda")
             ms = timed(lambda: g.vae_decode_device(lat.data_ptr(), 1, 32, 32, img.data_ptr()))
             report(name, "DC-AE f32c32 decode, latents [1,32,32,32] -> image [1,3,1024,1024], bf16 activations "
-                         f"({g.vae_last_launches()} launches)", ms, sv.vae_flops(vd, 32, 32), "tensor")
+                         f"({g.vae_last_launches()} launches)", ms, sv.vae_flops(vd, 32, 32), "tensor",
+                   extra=None if args.no_cpu_baseline else {"cpu_baseline": vae_cpu_sample(vd)})
             continue
         S, T = (32, 1024) if name.endswith("config2") else (2, 4096)
         side = int(round(T ** 0.5))
