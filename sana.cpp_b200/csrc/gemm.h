@@ -43,9 +43,16 @@ struct Epilogue {
 // outside the image. A 3x3 "same" convolution is kh = kw = 3, oy = ox = -1. The weight B is
 // [N, kh * kw * C] in the same tap-major order. Needs C % 64 == 0 and 128-row tiles that
 // are rectangles of whole image rows: W % 128 == 0, or 128 % W == 0 with (H * W) % 128 == 0.
+//
+// pair = 1 makes each product row a pair of horizontally adjacent pixels (2x, 2x + 1), so an
+// N = 128-channel convolution becomes an N = 256 product: W and C then describe the image
+// as super-pixels of two pixels (W = pixel width / 2, C = 2 * channels), K = kh * kw * (C / 2)
+// with tap column e = ox + tx relative to the row's first pixel reading pixel 2x + e, and
+// the weight rows [0, N/2) / [N/2, N) are the even / odd pixel's outputs.
 struct ConvA {
     int H = 0, W = 0, C = 0;
     int kh = 3, kw = 3, oy = -1, ox = -1;
+    int pair = 0;
 };
 
 struct GemmProblem {

@@ -212,6 +212,7 @@ __device__ __forceinline__ void tma_load_4d_pair(const CUtensorMap* map, uint32_
 // Geometry of an implicit-convolution A operand (ConvA) as the producer uses it.
 struct ConvGeom {
     int H = 0, W = 0, cchunks = 0, kw = 1, oy = 0, ox = 0;
+    int pair = 0, cin = 0;  // pixel-pair rows: tap column e reads super-pixel floor(e/2), channels (e & 1) * cin
 };
 
 // --- epilogue -------------------------------------------------------------------------
@@ -960,8 +961,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         const int tap = kb / cg.cchunks;
                         const int cc = kb - tap * cg.cchunks;
                         const int ty = tap / cg.kw;
-                        tma_load_4d_pair(&tmA, a_smem + stage * C::kABytes, fb, cc * BK, x0 + cg.ox + (tap - ty * cg.kw),
-                                         y0 + cg.oy + ty, img);
+                        const int e = cg.ox + (tap - ty * cg.kw);  // tap column relative to the row's (first) pixel
+                        int xc = x0 + e, ch = cc * BK;
+                        if (cg.pair) {  // e >= -2: super-pixel floor(e / 2), its (e & 1)-th half
+                            xc = x0 + (e + 2) / 2 - 1;
+                            ch += (e & 1) * cg.cin;
+                        }
+                        tma_load_4d_pair(&tmA, a_smem + stage * C::kABytes, fb, ch, xc, y0 + cg.oy + ty, img);
                     } else {
                         tma_load_2d_pair(&tmA, a_smem + stage * C::kABytes, fb, kb * BK,
                                          m_blk * BM2 + static_cast<int>(rank) * BM);
@@ -1171,7 +1177,9 @@ static void launch2(const GemmProblem& p, int* err, cudaStream_t stream, int num
     if (kConv) {
         cg.H = p.conv.H;
         cg.W = p.conv.W;
-        cg.cchunks = p.conv.C / BK;
+        cg.pair = p.conv.pair ? 1 : 0;
+        cg.cin = p.conv.pair ? p.conv.C / 2 : p.conv.C;
+        cg.cchunks = cg.cin / BK;
         cg.kw = p.conv.kw;
         cg.oy = p.conv.oy;
         cg.ox = p.conv.ox;
@@ -1214,7 +1222,9 @@ bool gemm_conv_supported(const GemmProblem& p) {
     if (c.H <= 0 || c.W <= 0 || c.C <= 0 || c.kh < 1 || c.kw < 1) return false;
     constexpr int BM = tc::BM, BK = tc::BK;
     const bool rows_ok = (c.W % BM == 0) || (BM % c.W == 0 && (static_cast<long long>(c.H) * c.W) % BM == 0);
-    return p.a_bf16 && p.b_bf16 && c.C % BK == 0 && rows_ok && p.K == c.kh * c.kw * c.C && p.N >= 16 &&
+    const int cin = c.pair ? c.C / 2 : c.C;
+    const bool pair_ok = !c.pair || (c.C % 2 == 0 && c.ox >= -2);
+    return p.a_bf16 && p.b_bf16 && cin % BK == 0 && pair_ok && rows_ok && p.K == c.kh * c.kw * cin && p.N >= 16 &&
            (p.ldb % 8 == 0) && a16(p.A) && a16(p.B) && !p.ep.resid && p.M % (c.H * c.W) == 0 &&
            c.kh * c.kw <= 64;
 }

@@ -23,6 +23,7 @@
 // [3 g d, 3 g d + 3 d) as its q, k, v; vae_ops.cpp:686-714) becomes the plain
 // [q heads | k heads | v heads] layout of the linear-attention kernel; the multiscale
 // depthwise and grouped weights move with their channels.
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <stdexcept>
@@ -312,6 +313,79 @@ __global__ void __launch_bounds__(256) ms_branch_kernel(const T* __restrict__ qk
     }
 }
 
+// conv_out, bf16 rows, C % 8 == 0: a block computes an 8 x 128-pixel tile (thread: one row,
+// pixels x0 + lane + 32 k, k < 4), staging the tile's halo 8 channels at a time in shared
+// memory ([10 rows][130 px] x 16 bytes: a warp's reads are consecutive pixels, no bank
+// conflicts); the four output channels' weights of each (tap, channel) are one float4 in
+// shared memory, read once per (tap, channel) for all four pixels. blockIdx.z is the image.
+constexpr int kCoTileX = 128, kCoTileY = 8, kCoHaloX = kCoTileX + 2, kCoHaloY = kCoTileY + 2;
+__global__ void __launch_bounds__(256) vae_conv_out_bf16_kernel(const bf16* __restrict__ in, int H, int W, int C,
+                                                                const float* __restrict__ w,
+                                                                const float* __restrict__ bias, int Co,
+                                                                float* __restrict__ out) {
+    extern __shared__ float4 s_w4[];                        // [9][C]
+    __shared__ uint4 s_in[kCoHaloY * kCoHaloX];            // 8 channels per pixel
+    for (int i = threadIdx.x; i < 9 * C; i += blockDim.x) {
+        const int tap = i / C, c = i % C;
+        float v[4];
+#pragma unroll
+        for (int o = 0; o < 4; ++o) v[o] = o < Co ? w[(static_cast<long long>(o) * 9 + tap) * C + c] : 0.f;
+        s_w4[i] = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    const int x0 = blockIdx.x * kCoTileX, y0 = blockIdx.y * kCoTileY, b = blockIdx.z;
+    const int lane = threadIdx.x & 31, row = threadIdx.x >> 5;
+    const bf16* img = in + static_cast<long long>(b) * H * W * C;
+    float4 acc[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c0 = 0; c0 < C; c0 += 8) {
+        __syncthreads();  // the previous chunk's reads are done (and the weights are staged)
+        for (int i = threadIdx.x; i < kCoHaloY * kCoHaloX; i += blockDim.x) {
+            const int y = y0 - 1 + i / kCoHaloX, x = x0 - 1 + i % kCoHaloX;
+            s_in[i] = (y >= 0 && y < H && x >= 0 && x < W)
+                          ? *reinterpret_cast<const uint4*>(img + (static_cast<long long>(y) * W + x) * C + c0)
+                          : make_uint4(0u, 0u, 0u, 0u);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int tap = 0; tap < 9; ++tap) {
+            const int dy = tap / 3, dx = tap % 3;
+            float v[4][8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint4 raw = s_in[(row + dy) * kCoHaloX + lane + 32 * k + dx];
+                const bf16* e = reinterpret_cast<const bf16*>(&raw);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[k][j] = __bfloat162float(e[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 wv = s_w4[tap * C + c0 + j];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    acc[k].x = fmaf(wv.x, v[k][j], acc[k].x);
+                    acc[k].y = fmaf(wv.y, v[k][j], acc[k].y);
+                    acc[k].z = fmaf(wv.z, v[k][j], acc[k].z);
+                    acc[k].w = fmaf(wv.w, v[k][j], acc[k].w);
+                }
+            }
+        }
+    }
+    const int y = y0 + row;
+    if (y >= H) return;
+    const long long plane = static_cast<long long>(H) * W;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int x = x0 + lane + 32 * k;
+        if (x >= W) continue;
+        float* o0 = out + static_cast<long long>(b) * Co * plane + static_cast<long long>(y) * W + x;
+        o0[0] = acc[k].x + bias[0];
+        if (Co > 1) o0[plane] = acc[k].y + bias[1];
+        if (Co > 2) o0[2 * plane] = acc[k].z + bias[2];
+        if (Co > 3) o0[3 * plane] = acc[k].w + bias[3];
+    }
+}
+
 // conv_out (vae.cpp:320-324): 3x3 "same" from NHWC rows [pixels, C] to NCHW fp32 with few
 // output channels (Co <= 4). A warp walks kConvOutPix consecutive pixels; lane l holds
 // channels [l * CPL, l * CPL + CPL) (those below C; C <= 32 * CPL), so each tap's row is one coalesced
@@ -431,6 +505,52 @@ std::vector<float> group_transpose(const std::vector<float>& rows, size_t n) {
     return r;
 }
 
+// Pixel-pair weights of a 3x3 "same" conv ([Cout, Cin, 3, 3] -> [2 Cout, 3, 4, Cin]): rows
+// [0, Cout) the even pixel's outputs, [Cout, 2 Cout) the odd one's; tap column tx reads the
+// pixel at offset tx - 1 from the even pixel, i.e. kernel column tx for the even pixel and
+// tx - 1 for the odd one (zero where the column falls outside the kernel).
+std::vector<float> pair_conv3x3(const float* w, int Cout, int Cin) {
+    std::vector<float> r(static_cast<size_t>(2) * Cout * 12 * Cin, 0.f);
+    for (int n = 0; n < 2 * Cout; ++n) {
+        const int o = n % Cout, shift = n / Cout;
+        for (int ty = 0; ty < 3; ++ty)
+            for (int tx = 0; tx < 4; ++tx) {
+                const int kx = tx - shift;
+                if (kx < 0 || kx > 2) continue;
+                for (int c = 0; c < Cin; ++c)
+                    r[((static_cast<size_t>(n) * 3 + ty) * 4 + tx) * Cin + c] =
+                        w[((static_cast<size_t>(o) * Cin + c) * 3 + ty) * 3 + kx];
+            }
+    }
+    return r;
+}
+
+// Pixel-pair form of the four sub-pixel weights ([4, Cout, 4, Cin] -> [4, 2 Cout, 2, 3, Cin]):
+// tap column tx is the even pixel's column tx and the odd pixel's tx - 1.
+std::vector<float> pair_parity(const std::vector<float>& w4, int Cout, int Cin) {
+    std::vector<float> r(static_cast<size_t>(4) * 2 * Cout * 6 * Cin, 0.f);
+    for (int ij = 0; ij < 4; ++ij)
+        for (int n = 0; n < 2 * Cout; ++n) {
+            const int o = n % Cout, shift = n / Cout;
+            for (int ty = 0; ty < 2; ++ty)
+                for (int tx = 0; tx < 3; ++tx) {
+                    const int kx = tx - shift;
+                    if (kx < 0 || kx > 1) continue;
+                    for (int c = 0; c < Cin; ++c)
+                        r[(((static_cast<size_t>(ij) * 2 * Cout + n) * 2 + ty) * 3 + tx) * Cin + c] =
+                            w4[((static_cast<size_t>(ij) * Cout + o) * 4 + ty * 2 + kx) * Cin + c];
+                }
+        }
+    return r;
+}
+
+std::vector<float> twice(const float* b, size_t n) {
+    std::vector<float> r(2 * n);
+    std::copy(b, b + n, r.begin());
+    std::copy(b, b + n, r.begin() + static_cast<long>(n));
+    return r;
+}
+
 // [C, Cl, 3, 3] -> [9, Cl, C]
 std::vector<float> conv_in_layout(const float* w, int C, int Cl) {
     std::vector<float> r(static_cast<size_t>(9) * Cl * C);
@@ -535,7 +655,15 @@ void VaeDecoder::upload_impl(const float* const* t) {
         const size_t CC = static_cast<size_t>(C);
         if (bd.has_upsample) {
             put<T>(blk.upw, tap_major(t[j], C, d.blocks[i + 1].channels));
-            if (sizeof(T) == 2) put<T>(blk.upw4, parity_weights(t[j], C, d.blocks[i + 1].channels));
+            if (sizeof(T) == 2) {
+                const int Cin = d.blocks[i + 1].channels;
+                const std::vector<float> w4 = parity_weights(t[j], C, Cin);
+                put<T>(blk.upw4, w4);
+                if (C <= 128) {
+                    put<T>(blk.upw4p, pair_parity(w4, C, Cin));
+                    put<float>(blk.upb2, twice(t[j + 1], CC));
+                }
+            }
             put<float>(blk.upb, copy_of(t[j + 1], CC));
             j += 2;
         }
@@ -546,6 +674,11 @@ void VaeDecoder::upload_impl(const float* const* t) {
                 put<T>(L.c1w, tap_major(t[j], C, C));
                 put<float>(L.c1b, copy_of(t[j + 1], CC));
                 put<T>(L.c2w, tap_major(t[j + 2], C, C));
+                if (sizeof(T) == 2 && C <= 128) {
+                    put<T>(L.c1w2, pair_conv3x3(t[j], C, C));
+                    put<float>(L.c1b2, twice(t[j + 1], CC));
+                    put<T>(L.c2w2, pair_conv3x3(t[j + 2], C, C));
+                }
                 put<float>(L.n1w, copy_of(t[j + 3], CC));
                 put<float>(L.n1b, copy_of(t[j + 4], CC));
                 j += 5;
@@ -689,21 +822,41 @@ bool VaeDecoder::implicit_ok(int H, int W, int Cin) const {
     return gemm_conv_supported(p);
 }
 
+bool VaeDecoder::pair_ok(int H, int W, int Cin, int Cout) const {
+    if (!implicit_ok(H, W, Cin) || Cout > 128 || Cout % 8 != 0 || W % 2 != 0) return false;
+    // SANA_VAE_PAIR=0 keeps one pixel per product row everywhere (a cross-check)
+    const char* v = std::getenv("SANA_VAE_PAIR");
+    if (v && std::string(v) == "0") return false;
+    GemmProblem p;
+    p.conv.H = H;
+    p.conv.W = W / 2;
+    p.conv.C = 2 * Cin;
+    p.conv.kw = 4;
+    p.conv.pair = 1;
+    p.M = H * W / 2;
+    p.N = 2 * Cout;
+    p.K = 12 * Cin;
+    p.ldb = p.K;
+    p.A = p.B = reinterpret_cast<const void*>(static_cast<uintptr_t>(256));
+    return gemm_conv_supported(p);
+}
+
 template <class T>
 void VaeDecoder::conv_gemm(const T* in, int B, int H, int W, int Cin, int kh, int kw, int oy, int ox, const void* w,
-                           const float* bias, int Cout, int act, T* out) {
+                           const float* bias, int Cout, int act, T* out, bool pair) {
     GemmProblem p;
     p.A = in;
     p.lda = Cin;
     p.B = w;
     p.ldb = static_cast<long long>(kh) * kw * Cin;
-    p.M = B * H * W;
-    p.N = Cout;
+    p.M = B * H * W / (pair ? 2 : 1);
+    p.N = Cout * (pair ? 2 : 1);
     p.K = kh * kw * Cin;
     p.a_bf16 = p.b_bf16 = 1;
     p.conv.H = H;
-    p.conv.W = W;
-    p.conv.C = Cin;
+    p.conv.W = pair ? W / 2 : W;
+    p.conv.C = pair ? 2 * Cin : Cin;
+    p.conv.pair = pair ? 1 : 0;
     p.conv.kh = kh;
     p.conv.kw = kw;
     p.conv.oy = oy;
@@ -712,7 +865,7 @@ void VaeDecoder::conv_gemm(const T* in, int B, int H, int W, int Cin, int kh, in
     p.ep.act = act;
     p.ep.out = out;
     p.ep.out_bf16 = 1;
-    p.ep.ldo = Cout;
+    p.ep.ldo = p.N;
     gemm(p, eng_.err(), eng_.stream(), eng_.num_sms());
     ++launches_;
 }
@@ -725,10 +878,17 @@ void VaeDecoder::upsample_conv(const T* in, int B, int H, int W, int Cin, const 
             // four 2x2 convolutions on the low-resolution image, one per output parity
             T* par = par_.as<T>();
             const long long plane = static_cast<long long>(B) * H * W * Cout;
-            for (int ij = 0; ij < 4; ++ij)
-                conv_gemm<T>(in, B, H, W, Cin, 2, 2, (ij >> 1) - 1, (ij & 1) - 1,
-                             blk.upw4.as<T>() + static_cast<long long>(ij) * Cout * 4 * Cin, blk.upb.as<float>(), Cout,
-                             kActNone, par + ij * plane);
+            const bool pair = pair_ok(H, W, Cin, Cout) && blk.upw4p.get();
+            for (int ij = 0; ij < 4; ++ij) {
+                if (pair)  // pixel pairs: 2x3 tap columns, 2 Cout outputs per row
+                    conv_gemm<T>(in, B, H, W, Cin, 2, 3, (ij >> 1) - 1, (ij & 1) - 1,
+                                 blk.upw4p.as<T>() + static_cast<long long>(ij) * 2 * Cout * 6 * Cin,
+                                 blk.upb2.as<float>(), Cout, kActNone, par + ij * plane, true);
+                else
+                    conv_gemm<T>(in, B, H, W, Cin, 2, 2, (ij >> 1) - 1, (ij & 1) - 1,
+                                 blk.upw4.as<T>() + static_cast<long long>(ij) * Cout * 4 * Cin, blk.upb.as<float>(),
+                                 Cout, kActNone, par + ij * plane);
+            }
             const dim3 grid(blocks_for(4LL * H * W * (Cout / 8)), B);
             shuffle_shortcut_kernel<<<grid, 256, 0, st>>>(par, in, B, H, W, Cin, Cout, out);
             SANA_CUDA(cudaGetLastError());
@@ -817,8 +977,14 @@ void VaeDecoder::decode_impl(const float* lat_d, int B, int h, int w, float* out
         const long long P = static_cast<long long>(B) * H * W;
         for (Layer& L : blk.layers) {
             if (bd.is_res_block) {
-                conv3x3<T>(x, B, H, W, C, false, L.c1w, L.c1b.as<float>(), C, kActSilu, g);
-                conv3x3<T>(g, B, H, W, C, false, L.c2w, nullptr, C, kActNone, y);
+                if (sizeof(T) == 2 && L.c1w2.get() && pair_ok(H, W, C, C)) {
+                    // 128-channel levels: pixel-pair rows make the product 256 wide
+                    conv_gemm<T>(x, B, H, W, C, 3, 4, -1, -1, L.c1w2.get(), L.c1b2.as<float>(), C, kActSilu, g, true);
+                    conv_gemm<T>(g, B, H, W, C, 3, 4, -1, -1, L.c2w2.get(), nullptr, C, kActNone, y, true);
+                } else {
+                    conv3x3<T>(x, B, H, W, C, false, L.c1w, L.c1b.as<float>(), C, kActSilu, g);
+                    conv3x3<T>(g, B, H, W, C, false, L.c2w, nullptr, C, kActNone, y);
+                }
                 rms(y, P, C, L.n1w, L.n1b, x, 0, g);
                 std::swap(x, g);
             } else {
@@ -860,7 +1026,17 @@ void VaeDecoder::decode_impl(const float* lat_d, int B, int h, int w, float* out
     }
     const long long P = static_cast<long long>(B) * H * W;
     rms(x, P, C, nout_w_, nout_b_, nullptr, 1, y);
-    {
+    if constexpr (sizeof(T) == 2) {
+        static bool attr = false;
+        if (!attr) {  // weights of up to 256 channels: 36 KB dynamic + the 20 KB halo
+            SANA_CUDA(cudaFuncSetAttribute(vae_conv_out_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           9 * 256 * static_cast<int>(sizeof(float4))));
+            attr = true;
+        }
+        const dim3 grid(ceil_div(W, kCoTileX), ceil_div(H, kCoTileY), B);
+        vae_conv_out_bf16_kernel<<<grid, 256, static_cast<size_t>(9) * C * sizeof(float4), st>>>(
+            y, H, W, C, cout_w_.as<float>(), cout_b_.as<float>(), d.out_channels, out_d);
+    } else {
         const dim3 grid(blocks_for(static_cast<long long>(H) * W, 8 * kConvOutPix), B);
         auto go = [&](auto kern, int cpl) {
             const size_t smem = static_cast<size_t>(9) * 4 * cpl * 32 * sizeof(float);

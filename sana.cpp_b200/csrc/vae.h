@@ -50,6 +50,7 @@ class VaeDecoder {
    private:
     struct Layer {
         DevBuf c1w, c1b, c2w;                    // ResBlock: conv weights [C, 9, C] (act type)
+        DevBuf c1w2, c1b2, c2w2;                 // bf16, C <= 128: pixel-pair forms [2C, 12, C], [2C]
         DevBuf wqkv, msdw, msgw, wout;           // attention: [3C, C], [3C/32, k*k, 32] f32, [3C/32, 32, 32] f32, [C, 2C]
         DevBuf winv, binv, wdw, bdw, wpt;        // GLUMBConv: [8C, C], [8C], [8C, 9] f32, [8C], [C, 4C]
         DevBuf n1w, n1b, n2w, n2b;               // RMSNorm weight / bias (ResBlock: n1 only)
@@ -57,6 +58,7 @@ class VaeDecoder {
     struct Block {
         DevBuf upw, upb;  // [C, 9, C_next] (act type), [C]
         DevBuf upw4;      // bf16: the four sub-pixel parity weights [4, C, 4, C_next]
+        DevBuf upw4p, upb2;  // bf16, C <= 128: their pixel-pair forms [4, 2C, 6, C_next], bias [2C]
         std::vector<Layer> layers;
     };
 
@@ -69,9 +71,12 @@ class VaeDecoder {
     void upsample_conv(const T* in, int B, int H, int W, int Cin, const Block& blk, int Cout, T* out);
     // implicit convolution on the tensor cores when the shape tiles (bf16 only)
     bool implicit_ok(int H, int W, int Cin) const;
+    // pair: two horizontally adjacent pixels per product row (ConvA::pair); w then holds the
+    // pair weights and bias the doubled bias
     template <class T>
     void conv_gemm(const T* in, int B, int H, int W, int Cin, int kh, int kw, int oy, int ox, const void* w,
-                   const float* bias, int Cout, int act, T* out);
+                   const float* bias, int Cout, int act, T* out, bool pair = false);
+    bool pair_ok(int H, int W, int Cin, int Cout) const;
     template <class T>
     void gemm_rows(const T* A, long long M, int K, const DevBuf& w, const float* bias, int N, int act, T* out);
     void ensure_workspace(int B, int h, int w);

@@ -124,6 +124,23 @@ def test_vae_implicit_convolutions_match_patch_gemm(oracle, monkeypatch):
     assert e1 < TOL["bf16"] and e2 < TOL["bf16"] and c > 0.9999
 
 
+def test_vae_pixel_pair_convolutions_match_single_pixel_rows(monkeypatch):
+    """The 64- and 128-channel levels run their 3x3 and sub-pixel convolutions with two pixels
+    per product row (zero taps padding each pixel's kernel); the single-pixel rows give the
+    same decode."""
+    from sana_b200 import synthetic_vae as sv
+    dims = sv.VaeDims(latent_channels=8, out_channels=3, channels=(64, 64, 128), res_blocks=(True, True, False),
+                      layers=(2, 1, 1), head_dim=32, ms_kernel=5, scaling_factor=0.5)
+    g = decoder("bf16", dims, 12)
+    lat = latents(dims, 2, 8, 8, 12)
+    pairs = g.vae_decode(lat)
+    monkeypatch.setenv("SANA_VAE_PAIR", "0")
+    single = g.vae_decode(lat)
+    c = cosine(pairs, single)
+    print(f"vae pixel pairs vs single rows: cosine {c:.8f}, identical {np.array_equal(pairs, single)}")
+    assert c > 0.99999
+
+
 def test_vae_batch_images_are_independent():
     from sana_b200 import synthetic_vae as sv
     g = decoder("bf16", sv.SMALL, 5)
