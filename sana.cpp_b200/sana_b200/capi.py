@@ -58,7 +58,8 @@ def load_library():
         lib.sana_cuda_stream.argtypes = [ctypes.c_void_p]
         lib.sana_cuda_destroy.argtypes = [ctypes.c_void_p]
         lib.sana_cuda_last_launch_count.argtypes = [ctypes.c_void_p]
-        lib.sana_cuda_vae_last_launch_count.argtypes = [ctypes.c_void_p]
+        if hasattr(lib, "sana_cuda_vae_last_launch_count"):
+            lib.sana_cuda_vae_last_launch_count.argtypes = [ctypes.c_void_p]
         lib.sana_randn_torch_cpu.argtypes = [_f32p, ctypes.c_size_t, ctypes.c_uint64]
         lib.sana_gguf_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p,
                                        ctypes.c_size_t]
