@@ -41,29 +41,61 @@ inline int blocks_for(long long n, int threads = 256) { return static_cast<int>(
 // conv_in: 3x3 "same" over latents * inv_sf (NCHW fp32), + bias, + the repeated-channel
 // shortcut out[c] += scaled[c / (C / Cl)] (vae.cpp:210-241, vae_ops.cpp:455-493).
 // w: [9, Cl, C] fp32 (consecutive output channels read consecutive weights). out: NHWC [B*H*W, C].
+// A block computes kCinPix consecutive pixels for every output channel: their scaled 3x3
+// neighbourhoods ([9 * Cl][kCinPix], zero outside the image) sit in shared memory and each
+// weight is read once for all of them. Cl <= 64, C <= 1024.
+constexpr int kCinPix = 8;
 template <class T>
-__global__ void vae_conv_in_kernel(const float* __restrict__ lat, int B, int Cl, int H, int W,
-                                   const float* __restrict__ w, const float* __restrict__ bias, float inv_sf, int C,
-                                   T* __restrict__ out) {
-    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const long long n = static_cast<long long>(B) * H * W * C;
-    if (i >= n) return;
-    const int oc = static_cast<int>(i % C);
-    const long long p = i / C;
-    const int x = static_cast<int>(p % W);
-    const int y = static_cast<int>((p / W) % H);
-    const int b = static_cast<int>(p / (static_cast<long long>(W) * H));
-    const float* lb = lat + static_cast<long long>(b) * Cl * H * W;
-    float acc = bias[oc];
-    for (int tap = 0; tap < 9; ++tap) {
-        const int iy = y + tap / 3 - 1, ix = x + tap % 3 - 1;
-        if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;
-        const float* wt = w + static_cast<long long>(tap) * Cl * C + oc;
-        for (int c = 0; c < Cl; ++c)
-            acc = fmaf(wt[static_cast<long long>(c) * C], lb[(static_cast<long long>(c) * H + iy) * W + ix] * inv_sf, acc);
+__global__ void __launch_bounds__(256) vae_conv_in_kernel(const float* __restrict__ lat, int B, int Cl, int H, int W,
+                                                          const float* __restrict__ w, const float* __restrict__ bias,
+                                                          float inv_sf, int C, T* __restrict__ out) {
+    __shared__ __align__(16) float s_lat[9 * 64][kCinPix];
+    const long long P = static_cast<long long>(B) * H * W;
+    const long long p0 = static_cast<long long>(blockIdx.x) * kCinPix;
+    const int K = 9 * Cl;
+    for (int i = threadIdx.x; i < K * kCinPix; i += blockDim.x) {
+        const int k = i % kCinPix, t = i / kCinPix;
+        const int tap = t / Cl, c = t % Cl;
+        const long long p = p0 + k;
+        float v = 0.f;
+        if (p < P) {
+            const int x = static_cast<int>(p % W), y = static_cast<int>((p / W) % H);
+            const int b = static_cast<int>(p / (static_cast<long long>(W) * H));
+            const int iy = y + tap / 3 - 1, ix = x + tap % 3 - 1;
+            if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+                v = lat[((static_cast<long long>(b) * Cl + c) * H + iy) * W + ix] * inv_sf;
+        }
+        s_lat[t][k] = v;
     }
-    acc += lb[(static_cast<long long>(oc / (C / Cl)) * H + y) * W + x] * inv_sf;
-    out[i] = from_f<T>(acc);
+    __syncthreads();
+    const int rep = C / Cl;
+    for (int oc = threadIdx.x; oc < C; oc += blockDim.x) {
+        float acc[kCinPix];
+#pragma unroll
+        for (int k = 0; k < kCinPix; ++k) acc[k] = bias[oc];
+        for (int t = 0; t < K; ++t) {
+            const float wv = w[static_cast<long long>(t) * C + oc];
+            const float4 a = *reinterpret_cast<const float4*>(&s_lat[t][0]);
+            const float4 b4 = *reinterpret_cast<const float4*>(&s_lat[t][4]);
+            acc[0] = fmaf(wv, a.x, acc[0]);
+            acc[1] = fmaf(wv, a.y, acc[1]);
+            acc[2] = fmaf(wv, a.z, acc[2]);
+            acc[3] = fmaf(wv, a.w, acc[3]);
+            acc[4] = fmaf(wv, b4.x, acc[4]);
+            acc[5] = fmaf(wv, b4.y, acc[5]);
+            acc[6] = fmaf(wv, b4.z, acc[6]);
+            acc[7] = fmaf(wv, b4.w, acc[7]);
+        }
+#pragma unroll
+        for (int k = 0; k < kCinPix; ++k) {
+            const long long p = p0 + k;
+            if (p >= P) break;
+            const int x = static_cast<int>(p % W), y = static_cast<int>((p / W) % H);
+            const int b = static_cast<int>(p / (static_cast<long long>(W) * H));
+            const float sc = lat[((static_cast<long long>(b) * Cl + oc / rep) * H + y) * W + x] * inv_sf;
+            out[p * C + oc] = from_f<T>(acc[k] + sc);
+        }
+    }
 }
 
 // Tap-major 3x3 patches of an NHWC image for a "same" convolution at output size
@@ -138,9 +170,27 @@ __global__ void shuffle_shortcut_kernel(const bf16* __restrict__ par, const bf16
     const int rep = 4 * Cout / Cin;
     uint4 o;
     bf16* oe = reinterpret_cast<bf16*>(&o);
+    if (rep == 4) {  // Cin == Cout: the shortcut channel is oc itself
+        const uint4 sraw = *reinterpret_cast<const uint4*>(sc + oc0);
+        const bf16* se = reinterpret_cast<const bf16*>(&sraw);
 #pragma unroll
-    for (int k = 0; k < 8; ++k)
-        oe[k] = __float2bfloat16_rn(__bfloat162float(e[k]) + __bfloat162float(sc[(4 * (oc0 + k) + ij) / rep]));
+        for (int k = 0; k < 8; ++k) oe[k] = __float2bfloat16_rn(__bfloat162float(e[k]) + __bfloat162float(se[k]));
+    } else if (rep == 2) {  // Cin == 2 Cout: channel 2 oc + (ij >> 1), every other one of 16
+        const uint4 s0 = *reinterpret_cast<const uint4*>(sc + 2 * oc0);
+        const uint4 s1 = *reinterpret_cast<const uint4*>(sc + 2 * oc0 + 8);
+        const bf16* se0 = reinterpret_cast<const bf16*>(&s0);
+        const bf16* se1 = reinterpret_cast<const bf16*>(&s1);
+        const int odd = ij >> 1;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const bf16 v = k < 4 ? se0[2 * k + odd] : se1[2 * (k - 4) + odd];
+            oe[k] = __float2bfloat16_rn(__bfloat162float(e[k]) + __bfloat162float(v));
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            oe[k] = __float2bfloat16_rn(__bfloat162float(e[k]) + __bfloat162float(sc[(4 * (oc0 + k) + ij) / rep]));
+    }
     *reinterpret_cast<uint4*>(out + (static_cast<long long>(b) * 4 * H * W + p) * Cout + oc0) = o;
 }
 
@@ -598,8 +648,8 @@ size_t vae_tensor_count(const VaeDims& d) {
 void vae_validate(const VaeDims& d) {
     if (d.n_blocks < 1 || d.n_blocks > 8) throw InvalidArg("vae decoder must contain at least one up block");
     if (!(d.scaling_factor > 0.0f)) throw InvalidArg("vae scaling_factor must be positive");
-    if (d.latent_channels < 1 || d.out_channels < 1 || d.out_channels > 4)
-        throw InvalidArg("vae decoder latent channels must be positive and output channels in [1, 4]");
+    if (d.latent_channels < 1 || d.latent_channels > 64 || d.out_channels < 1 || d.out_channels > 4)
+        throw InvalidArg("vae decoder latent channels must be in [1, 64] and output channels in [1, 4]");
     if (d.head_dim != 32) throw InvalidArg("vae attention head dim must be 32");
     if (d.ms_kernel != 3 && d.ms_kernel != 5)
         throw InvalidArg("depthwise_conv2d_same only supports 3x3 or 5x5 kernels");
@@ -957,9 +1007,10 @@ void VaeDecoder::decode_impl(const float* lat_d, int B, int h, int w, float* out
         ++launches_;
     };
     {
-        const long long nout = static_cast<long long>(B) * H * W * C;
-        vae_conv_in_kernel<T><<<blocks_for(nout), 256, 0, st>>>(lat_d, B, d.latent_channels, H, W, cin_w_.as<float>(),
-                                                               cin_b_.as<float>(), 1.0f / d.scaling_factor, C, x);
+        const long long pix = static_cast<long long>(B) * H * W;
+        vae_conv_in_kernel<T><<<blocks_for(pix, kCinPix), 256, 0, st>>>(lat_d, B, d.latent_channels, H, W,
+                                                                       cin_w_.as<float>(), cin_b_.as<float>(),
+                                                                       1.0f / d.scaling_factor, C, x);
         SANA_CUDA(cudaGetLastError());
         ++launches_;
     }
