@@ -125,9 +125,11 @@ PipelineRunResult run_pipeline_once(const Dims& d, const Tensor& negative_states
     Tensor embeddings({2, d.L, d.Din});
     Tensor attention_bias({2, 1, d.L});
     char err[256] = {0};
-    if (sana_prompt_pair_assemble(negative_states.data().data(), d.L, 8, positive_states.data().data(), d.pos_rows,
-                                  40, d.Din, d.L, embeddings.data().data(), attention_bias.data().data(), err,
-                                  sizeof(err)) != SANA_OK)
+    // real tokens: 8 in the negative prompt, 40 in the instruction-prefixed positive one
+    const size_t neg_real = d.L < 8 ? d.L : 8, pos_real = d.pos_rows < 40 ? d.pos_rows : 40;
+    if (sana_prompt_pair_assemble(negative_states.data().data(), d.L, neg_real, positive_states.data().data(),
+                                  d.pos_rows, pos_real, d.Din, d.L, embeddings.data().data(),
+                                  attention_bias.data().data(), err, sizeof(err)) != SANA_OK)
         throw std::invalid_argument(err);
     const auto encoder_end = Clock::now();
 
