@@ -226,6 +226,11 @@ def test_prompt_pairs_device_matches_oracle(oracle, pairs, hidden, pos_rows, L):
             assert np.array_equal(bias[row].view(np.uint32), b[half].view(np.uint32))
     with pytest.raises(ValueError, match="exceeds padded_length"):
         g.prompt_pairs_device(torch.from_numpy(neg).cuda(), [L + 1] * pairs, torch.from_numpy(pos).cuda(), pos_real, L)
+    if pairs == 1:  # more pairs than one launch takes
+        many = torch.zeros((65, L, hidden), dtype=torch.float32, device="cuda")
+        many_pos = torch.zeros((65, pos_rows, hidden), dtype=torch.float32, device="cuda")
+        with pytest.raises(ValueError, match="prompt pair count"):
+            g.prompt_pairs_device(many, [1] * 65, many_pos, [1] * 65, L)
 
 
 def test_loop_from_device_assembled_prompts(full_gpu, oracle):

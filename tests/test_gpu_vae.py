@@ -233,3 +233,27 @@ def test_vae_gguf_errors_follow_the_loader(tmp_path):
     _write(bad, [(n, t if n != "decoder.conv_in.bias" else t[:-1]) for (n, _, _), t in zip(specs, tensors)])
     with pytest.raises(SanaError, match="shape"):
         g.vae_upload_gguf(bad)
+
+
+def test_vae_device_entry_and_batch_on_the_implicit_path():
+    """Two images of 16 x 16 latents through DC-AE f32c32 (every level from 128 x 128 up takes
+    the implicit tensor-core convolutions and pixel pairs): the device-pointer entry point gives
+    the host entry point's image, and each image of the batch is the one it gets alone."""
+    import torch
+    from sana_b200 import synthetic_vae as sv
+    dims = sv.VaeDims()
+    g = decoder("bf16", dims, 17)
+    lat = latents(dims, 2, 16, 16, 17)
+    host = g.vae_decode(lat)
+    d_lat = torch.from_numpy(lat).cuda()
+    d_out = torch.empty((2, 3, 512, 512), dtype=torch.float32, device="cuda")
+    g.vae_decode_device(d_lat.data_ptr(), 2, 16, 16, d_out.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(d_out.cpu().numpy(), host)
+    # alone, an image's linear attention splits its token sums differently (the split depends on
+    # the batch), so bf16 roundings differ slightly: the denoiser's batch criterion applies
+    for i in range(2):
+        one = g.vae_decode(lat[i:i + 1])
+        c, e = cosine(host[i], one[0]), rel_err(host[i], one[0])
+        print(f"vae batch image {i}: cosine {c:.7f} rel-L2 {e:.2e}")
+        assert c > 0.9999 and e < 1e-2, (i, c, e)
