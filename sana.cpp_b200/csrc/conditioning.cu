@@ -16,7 +16,7 @@ namespace {
 
 __global__ void prompt_pairs_kernel(const float* __restrict__ negative, const float* __restrict__ positive,
                                     int pairs, int positive_rows, int hidden, int L, PromptPairCounts counts,
-                                    float* __restrict__ enc, float* __restrict__ bias) {
+                                    int vec, float* __restrict__ enc, float* __restrict__ bias) {
     const int row = blockIdx.x;  // output row in [0, 2 * pairs * L)
     const int seq = row / L, t = row - seq * L;
     const bool pos = seq >= pairs;
@@ -30,7 +30,7 @@ __global__ void prompt_pairs_kernel(const float* __restrict__ negative, const fl
     }
     const float* src = (pos ? positive : negative) + src_row * hidden;
     float* dst = enc + static_cast<long long>(row) * hidden;
-    if ((hidden & 3) == 0) {
+    if (vec) {  // rows of 16-byte vectors (hidden % 4 == 0, 16-byte aligned buffers)
         const float4* s4 = reinterpret_cast<const float4*>(src);
         float4* d4 = reinterpret_cast<float4*>(dst);
         for (int i = threadIdx.x; i < hidden / 4; i += blockDim.x) d4[i] = s4[i];
@@ -49,11 +49,9 @@ void prompt_pairs(const float* negative, const float* positive, int pairs, int p
                   const PromptPairCounts& counts, float* enc, float* bias, cudaStream_t st) {
     const bool vec = (hidden & 3) == 0 && (reinterpret_cast<uintptr_t>(negative) & 15) == 0 &&
                      (reinterpret_cast<uintptr_t>(positive) & 15) == 0 && (reinterpret_cast<uintptr_t>(enc) & 15) == 0;
-    if (!vec && (hidden & 3) == 0)
-        throw std::invalid_argument("prompt pair buffers must be 16-byte aligned when hidden is a multiple of 4");
     const int threads = hidden >= 512 ? 256 : 128;
     prompt_pairs_kernel<<<2 * pairs * L, threads, 0, st>>>(negative, positive, pairs, positive_rows, hidden, L, counts,
-                                                           enc, bias);
+                                                           vec ? 1 : 0, enc, bias);
     SANA_CUDA(cudaGetLastError());
 }
 

@@ -226,6 +226,14 @@ def test_prompt_pairs_device_matches_oracle(oracle, pairs, hidden, pos_rows, L):
             assert np.array_equal(bias[row].view(np.uint32), b[half].view(np.uint32))
     with pytest.raises(ValueError, match="exceeds padded_length"):
         g.prompt_pairs_device(torch.from_numpy(neg).cuda(), [L + 1] * pairs, torch.from_numpy(pos).cuda(), pos_real, L)
+    if pairs == 3:  # buffers offset by one float (not 16-byte aligned): the scalar copy, same result
+        nb = torch.zeros(neg.size + 1, dtype=torch.float32, device="cuda")
+        pb = torch.zeros(pos.size + 1, dtype=torch.float32, device="cuda")
+        nb[1:] = torch.from_numpy(neg.ravel()).cuda()
+        pb[1:] = torch.from_numpy(pos.ravel()).cuda()
+        enc2, bias2 = g.prompt_pairs_device(nb[1:].view(neg.shape), neg_real, pb[1:].view(pos.shape), pos_real, L)
+        torch.cuda.synchronize()
+        assert np.array_equal(enc2.cpu().numpy(), enc) and np.array_equal(bias2.cpu().numpy(), bias)
     if pairs == 1:  # more pairs than one launch takes
         many = torch.zeros((65, L, hidden), dtype=torch.float32, device="cuda")
         many_pos = torch.zeros((65, pos_rows, hidden), dtype=torch.float32, device="cuda")
