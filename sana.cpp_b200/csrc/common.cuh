@@ -215,4 +215,22 @@ __device__ __forceinline__ void fence_barrier_init() {
 
 inline int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 
+// Kernel attributes (cudaFuncSetAttribute) belong to a device's context, so a launch site sets
+// them once per device: `static PerDeviceOnce attr; if (attr.pending()) { set...; attr.mark(); }`.
+struct PerDeviceOnce {
+    bool done[64] = {};
+    static int current() {
+        int d = 0;
+        return cudaGetDevice(&d) == cudaSuccess && d >= 0 && d < 64 ? d : -1;
+    }
+    bool pending() const {
+        const int d = current();
+        return d < 0 || !done[d];
+    }
+    void mark() {
+        const int d = current();
+        if (d >= 0) done[d] = true;
+    }
+};
+
 }  // namespace sana

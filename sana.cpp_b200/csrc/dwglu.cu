@@ -363,13 +363,13 @@ void depthwise_glu(const T* in, long long ldi, int S, int H, int W, int E, const
                (reinterpret_cast<uintptr_t>(in) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 3) == 0;
     if (vec) {
         static int device_sms[64] = {0};
-        static bool attr = false;
+        static PerDeviceOnce attr;
         int dev = 0;
         SANA_CUDA(cudaGetDevice(&dev));
-        if (!attr) {
+        if (attr.pending()) {
             SANA_CUDA(cudaFuncSetAttribute(dwglu_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(dwglu_stream_smem())));
-            attr = true;
+            attr.mark();
         }
         int& sms = device_sms[dev & 63];
         if (sms == 0) SANA_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));

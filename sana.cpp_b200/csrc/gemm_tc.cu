@@ -1118,11 +1118,11 @@ static CUtensorMap out_map(void* ptr, int is_bf16, long long ld, int M, int N) {
 template <int BN, bool kResid>
 static void launch(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
     using C = Cfg<BN, kResid>;
-    static bool attr_done = false;
-    if (!attr_done) {
+    static PerDeviceOnce attr_done;
+    if (attr_done.pending()) {
         SANA_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, kResid>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::kSmemBytes));
-        attr_done = true;
+        attr_done.mark();
     }
     const CUtensorMap ma = make_map(p.A, p.M, p.K, p.lda, BM);
     const CUtensorMap mb = make_map(p.B, p.N, p.K, p.ldb, BN);
@@ -1166,11 +1166,11 @@ static CUtensorMap conv_map(const GemmProblem& p) {
 template <int BN, bool kResid, bool kDeep = false, bool kConv = false>
 static void launch2(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
     using C = Cfg2<BN, kResid, kDeep>;
-    static bool attr_done = false;
-    if (!attr_done) {
+    static PerDeviceOnce attr_done;
+    if (attr_done.pending()) {
         SANA_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<BN, kResid, kDeep, kConv>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
-        attr_done = true;
+        attr_done.mark();
     }
     const CUtensorMap ma = kConv ? conv_map(p) : make_map(p.A, p.M, p.K, p.lda, BM);
     ConvGeom cg;

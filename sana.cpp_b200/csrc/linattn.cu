@@ -230,11 +230,11 @@ template <class T, int D>
 void launch_apply_reg(const T* q, long long ldq, int q_off, int Tq, int heads, int S, const float* state, T* out,
                       long long ldo, cudaStream_t st) {
     const size_t smem = (static_cast<size_t>(D + 1) * D + static_cast<size_t>(kTile) * (D + 1)) * sizeof(float);
-    static bool attr = false;
-    if (!attr) {
+    static PerDeviceOnce attr;
+    if (attr.pending()) {
         SANA_CUDA(cudaFuncSetAttribute(linattn_apply_reg_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem)));
-        attr = true;
+        attr.mark();
     }
     linattn_apply_reg_kernel<T, D><<<dim3(ceil_div(Tq, kTile), heads, S), kTile, smem, st>>>(q, ldq, q_off, Tq, heads,
                                                                                           state, out, ldo);
@@ -419,11 +419,11 @@ bool linattn_bf16_path<bf16>(const bf16* q, long long ldq, int q_off, const bf16
     int splits = 1;
     while (splits * 2 * nblk <= 256 && splits < 8) splits *= 2;
     const size_t sm = static_cast<size_t>(2) * kChunk * D * 2 + static_cast<size_t>(splits) * width * 4;
-    static bool attr = false;
-    if (!attr) {
+    static PerDeviceOnce attr;
+    if (attr.pending()) {
         SANA_CUDA(cudaFuncSetAttribute(linattn_state_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        227 * 1024));
-        attr = true;
+        attr.mark();
     }
     linattn_state_bf16_kernel<<<dim3(chunks, heads, S), 256, sm, st>>>(kv, ldkv, k_off, v_off, Tk, heads, D, chunks,
                                                                        partial);
@@ -458,13 +458,13 @@ void linear_attention(const T* q, long long ldq, int q_off, const T* kv, long lo
     const size_t sm1 = static_cast<size_t>(2) * kChunk * D * sizeof(float);
     const size_t sm3 = (static_cast<size_t>(width) + static_cast<size_t>(D) * kTile +
                         static_cast<size_t>(kTile) * (D + 1)) * sizeof(float);
-    static bool attr = false;
-    if (!attr) {
+    static PerDeviceOnce attr;
+    if (attr.pending()) {
         SANA_CUDA(cudaFuncSetAttribute(linattn_state_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        2 * kChunk * 128 * 4));
         SANA_CUDA(cudaFuncSetAttribute(linattn_apply_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (129 * 128 + 128 * kTile + kTile * 129) * 4));
-        attr = true;
+        attr.mark();
     }
     if (Tk > 0) {
         if (D % 4 == 0) {
@@ -472,11 +472,11 @@ void linear_attention(const T* q, long long ldq, int q_off, const T* kv, long lo
             int splits = 1;
             while (splits * 2 * nblk <= 256 && splits < 8) splits *= 2;
             const size_t sm4 = (static_cast<size_t>(2) * kChunk * D + static_cast<size_t>(splits) * width) * 4;
-            static bool attr4 = false;
-            if (!attr4) {
+            static PerDeviceOnce attr4;
+            if (attr4.pending()) {
                 SANA_CUDA(cudaFuncSetAttribute(linattn_state4_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                227 * 1024));
-                attr4 = true;
+                attr4.mark();
             }
             linattn_state4_kernel<T><<<dim3(chunks, heads, S), 256, sm4, st>>>(kv, ldkv, k_off, v_off, Tk, heads, D,
                                                                                chunks, partial);

@@ -320,14 +320,14 @@ int token_splits(int units, int T, int min_tokens, int* per) {
 template <int D, int TS, int CH>
 void launch(const bf16* q, long long ldq, int q_off, const bf16* kv, long long ldkv, int k_off, int v_off, int S,
             int Tq, int Tk, int heads, float* partial, bf16* out, long long ldo, cudaStream_t st) {
-    static bool attr = false;
+    static PerDeviceOnce attr;
     const size_t sm1 = state_smem<D, TS, CH>(), sm2 = apply_smem<D>();
-    if (!attr) {
+    if (attr.pending()) {
         SANA_CUDA(cudaFuncSetAttribute(la_state_kernel<D, TS, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(sm1)));
         SANA_CUDA(cudaFuncSetAttribute(la_apply_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(sm2)));
-        attr = true;
+        attr.mark();
     }
     // at least 128 tokens per state split: the partial-state buffer holds ceil(Tk / 128)
     // states per (sequence, head)

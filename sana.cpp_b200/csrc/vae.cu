@@ -1078,11 +1078,11 @@ void VaeDecoder::decode_impl(const float* lat_d, int B, int h, int w, float* out
     const long long P = static_cast<long long>(B) * H * W;
     rms(x, P, C, nout_w_, nout_b_, nullptr, 1, y);
     if constexpr (sizeof(T) == 2) {
-        static bool attr = false;
-        if (!attr) {  // weights of up to 256 channels: 36 KB dynamic + the 20 KB halo
+        static PerDeviceOnce attr;
+        if (attr.pending()) {  // weights of up to 256 channels: 36 KB dynamic + the 20 KB halo
             SANA_CUDA(cudaFuncSetAttribute(vae_conv_out_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            9 * 256 * static_cast<int>(sizeof(float4))));
-            attr = true;
+            attr.mark();
         }
         const dim3 grid(ceil_div(W, kCoTileX), ceil_div(H, kCoTileY), B);
         vae_conv_out_bf16_kernel<<<grid, 256, static_cast<size_t>(9) * C * sizeof(float4), st>>>(

@@ -84,11 +84,11 @@ void launch(const T* q, long long ldq, const T* kv, long long ldkv, int k_off, i
             const int* kv_len, int S, int Tq, int L, int heads, int D, float scale, T* out, long long ldo,
             cudaStream_t st) {
     const size_t smem = 2 * static_cast<size_t>(L) * D * sizeof(T) + static_cast<size_t>(L) * 4 + 8;
-    static bool attr = false;
-    if (!attr) {
+    static PerDeviceOnce attr;
+    if (attr.pending()) {
         SANA_CUDA(cudaFuncSetAttribute(xattn_kernel<T, DMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        227 * 1024));
-        attr = true;
+        attr.mark();
     }
     xattn_kernel<T, DMAX><<<dim3(ceil_div(Tq, kQ), heads, S), kQ, smem, st>>>(q, ldq, kv, ldkv, k_off, v_off, bias,
                                                                              kv_len, Tq, L, D, scale, out, ldo);
@@ -364,11 +364,11 @@ bool launch_mma(const bf16* q, long long ldq, const bf16* kv, long long ldkv, in
                 const int* kv_len, int S, int Tq, int L, int heads, float scale, bf16* out, long long ldo,
                 cudaStream_t st) {
     constexpr size_t smem = XattnTiles<D>::kBytes;
-    static bool attr = false;
-    if (!attr) {
+    static PerDeviceOnce attr;
+    if (attr.pending()) {
         SANA_CUDA(cudaFuncSetAttribute(xattn_mma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem)));
-        attr = true;
+        attr.mark();
     }
     xattn_mma_kernel<D><<<dim3(ceil_div(Tq, 16 * kMmaWarps), heads, S), 32 * kMmaWarps, smem, st>>>(
         q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, Tq, L, scale, out, ldo);
