@@ -7,6 +7,7 @@
   (fp32 check mode: relative L2 <= 1e-5; bf16 mode: <= 2e-2);
 * edge cases of the reference's op contracts against the oracle.
 """
+import ctypes
 import importlib.util
 import os
 
@@ -236,6 +237,40 @@ def test_gemm_repeatable(gpu_bf16):
     a = gpu_bf16.linear_3d(x, w)
     b = gpu_bf16.linear_3d(x, w)
     assert np.array_equal(a, b)
+
+
+def test_handles_on_two_devices_in_one_process():
+    """Handles on two GPUs of one process: the tensor-core GEMM and the depthwise stream kernel
+    (both above the default shared-memory limit, set up per device) give the same bits on
+    each device. Needs two visible GPUs."""
+    import torch
+    from sana_b200 import SANA_MODE_BF16, SanaCuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    gen = torch.Generator(device="cpu").manual_seed(3)
+    A = torch.randn(4096, 1152, generator=gen).to(torch.bfloat16)
+    B = (torch.randn(1152, 1152, generator=gen) * 0.02).to(torch.bfloat16)
+    H = torch.randn(2 * 32 * 32, 640, generator=gen).to(torch.bfloat16)
+    w = torch.randn(640 * 9, generator=gen) * 0.1
+    b = torch.randn(640, generator=gen) * 0.1
+    outs = []
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            g = SanaCuda(dev, SANA_MODE_BF16)
+            a, bb, h = A.cuda(dev), B.cuda(dev), H.cuda(dev)
+            wd, bd = w.cuda(dev), b.cuda(dev)
+            out = torch.empty(4096, 1152, dtype=torch.bfloat16, device=f"cuda:{dev}")
+            glu = torch.empty(2 * 32 * 32, 320, dtype=torch.bfloat16, device=f"cuda:{dev}")
+            g.gemm_device(a.data_ptr(), bb.data_ptr(), 4096, 1152, 1152, out.data_ptr())
+            g._call("sana_op_depthwise_glu_device", ctypes.c_void_p(h.data_ptr()), ctypes.c_int(2), ctypes.c_int(32),
+                    ctypes.c_int(32), ctypes.c_int(640), ctypes.c_void_p(wd.data_ptr()), ctypes.c_void_p(bd.data_ptr()),
+                    ctypes.c_void_p(glu.data_ptr()))
+            torch.cuda.synchronize(dev)
+            outs.append((out.cpu(), glu.cpu()))
+            g.close()
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    ref = (A.float() @ B.float().T)
+    assert float((outs[0][0].float() - ref).norm() / ref.norm()) < 1e-2
 
 
 # --- the reference's known-answer tests ------------------------------------------------------
