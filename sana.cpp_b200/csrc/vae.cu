@@ -44,7 +44,7 @@ inline int blocks_for(long long n, int threads = 256) { return static_cast<int>(
 // A block computes kCinPix consecutive pixels for every output channel: their scaled 3x3
 // neighbourhoods ([9 * Cl][kCinPix], zero outside the image) sit in shared memory and each
 // weight is read once for all of them. Cl <= 64, C <= 1024.
-constexpr int kCinPix = 8;
+constexpr int kCinPix = 4;
 template <class T>
 __global__ void __launch_bounds__(256) vae_conv_in_kernel(const float* __restrict__ lat, int B, int Cl, int H, int W,
                                                           const float* __restrict__ w, const float* __restrict__ bias,
@@ -73,18 +73,17 @@ __global__ void __launch_bounds__(256) vae_conv_in_kernel(const float* __restric
         float acc[kCinPix];
 #pragma unroll
         for (int k = 0; k < kCinPix; ++k) acc[k] = bias[oc];
+#pragma unroll 8  // several weight loads in flight per thread
         for (int t = 0; t < K; ++t) {
             const float wv = w[static_cast<long long>(t) * C + oc];
-            const float4 a = *reinterpret_cast<const float4*>(&s_lat[t][0]);
-            const float4 b4 = *reinterpret_cast<const float4*>(&s_lat[t][4]);
-            acc[0] = fmaf(wv, a.x, acc[0]);
-            acc[1] = fmaf(wv, a.y, acc[1]);
-            acc[2] = fmaf(wv, a.z, acc[2]);
-            acc[3] = fmaf(wv, a.w, acc[3]);
-            acc[4] = fmaf(wv, b4.x, acc[4]);
-            acc[5] = fmaf(wv, b4.y, acc[5]);
-            acc[6] = fmaf(wv, b4.z, acc[6]);
-            acc[7] = fmaf(wv, b4.w, acc[7]);
+#pragma unroll
+            for (int k4 = 0; k4 < kCinPix; k4 += 4) {
+                const float4 a = *reinterpret_cast<const float4*>(&s_lat[t][k4]);
+                acc[k4] = fmaf(wv, a.x, acc[k4]);
+                acc[k4 + 1] = fmaf(wv, a.y, acc[k4 + 1]);
+                acc[k4 + 2] = fmaf(wv, a.z, acc[k4 + 2]);
+                acc[k4 + 3] = fmaf(wv, a.w, acc[k4 + 3]);
+            }
         }
 #pragma unroll
         for (int k = 0; k < kCinPix; ++k) {
