@@ -368,6 +368,7 @@ __global__ void __launch_bounds__(256) ms_branch_kernel(const T* __restrict__ qk
 // conflicts); the four output channels' weights of each (tap, channel) are one float4 in
 // shared memory, read once per (tap, channel) for all four pixels. blockIdx.z is the image.
 constexpr int kCoTileX = 128, kCoTileY = 8, kCoHaloX = kCoTileX + 2, kCoHaloY = kCoTileY + 2;
+template <bool kFourth>  // a fourth output channel (Co == 4); RGB skips its FMAs
 __global__ void __launch_bounds__(256) vae_conv_out_bf16_kernel(const bf16* __restrict__ in, int H, int W, int C,
                                                                 const float* __restrict__ w,
                                                                 const float* __restrict__ bias, int Co,
@@ -415,7 +416,7 @@ __global__ void __launch_bounds__(256) vae_conv_out_bf16_kernel(const bf16* __re
                     acc[k].x = fmaf(wv.x, v[k][j], acc[k].x);
                     acc[k].y = fmaf(wv.y, v[k][j], acc[k].y);
                     acc[k].z = fmaf(wv.z, v[k][j], acc[k].z);
-                    acc[k].w = fmaf(wv.w, v[k][j], acc[k].w);
+                    if constexpr (kFourth) acc[k].w = fmaf(wv.w, v[k][j], acc[k].w);
                 }
             }
         }
@@ -1079,13 +1080,21 @@ void VaeDecoder::decode_impl(const float* lat_d, int B, int h, int w, float* out
     if constexpr (sizeof(T) == 2) {
         static PerDeviceOnce attr;
         if (attr.pending()) {  // weights of up to 256 channels: 36 KB dynamic + the 20 KB halo
-            SANA_CUDA(cudaFuncSetAttribute(vae_conv_out_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           9 * 256 * static_cast<int>(sizeof(float4))));
+            const int smem_max = 9 * 256 * static_cast<int>(sizeof(float4));
+            SANA_CUDA(cudaFuncSetAttribute(vae_conv_out_bf16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           smem_max));
+            SANA_CUDA(cudaFuncSetAttribute(vae_conv_out_bf16_kernel<false>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
             attr.mark();
         }
         const dim3 grid(ceil_div(W, kCoTileX), ceil_div(H, kCoTileY), B);
-        vae_conv_out_bf16_kernel<<<grid, 256, static_cast<size_t>(9) * C * sizeof(float4), st>>>(
-            y, H, W, C, cout_w_.as<float>(), cout_b_.as<float>(), d.out_channels, out_d);
+        const size_t smem = static_cast<size_t>(9) * C * sizeof(float4);
+        if (d.out_channels == 4)
+            vae_conv_out_bf16_kernel<true><<<grid, 256, smem, st>>>(y, H, W, C, cout_w_.as<float>(), cout_b_.as<float>(),
+                                                                    d.out_channels, out_d);
+        else
+            vae_conv_out_bf16_kernel<false><<<grid, 256, smem, st>>>(y, H, W, C, cout_w_.as<float>(),
+                                                                     cout_b_.as<float>(), d.out_channels, out_d);
     } else {
         const dim3 grid(blocks_for(static_cast<long long>(H) * W, 8 * kConvOutPix), B);
         auto go = [&](auto kern, int cpl) {
