@@ -48,9 +48,12 @@ NUM_STEPS = 20
 GUIDANCE = 4.5
 CAPTION_LEN = 300
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes (read + write) of one FF-inverted projection launch at the default workload,
-# from the ncu capture summarised in profiles/gemm_tc2_ff_inverted_config2.md.
-FF_INVERTED_TRAFFIC_BYTES = 88_987_904 + 329_661_952
+# dram__bytes_read.sum + dram__bytes_write.sum of one FF-inverted projection launch at the
+# default workload (M=32768, K=1152, N=5760), copied from an ncu capture of that kernel; the
+# JSON line names the capture it came from. Not measured by this script.
+FF_INVERTED_TRAFFIC = {"bytes": 88_987_904 + 329_661_952,
+                       "source": "ncu --set full capture of gemm_tc2_kernel<256,0,0,0> at M=32768 K=1152 N=5760 "
+                                 "(profiles/gemm_tc2_ff_inverted_config2.md)"}
 
 
 def log(*a):
@@ -68,13 +71,17 @@ def peaks():
 # ------------------------------------------------------------------------------------------
 # Synthetic workload
 # ------------------------------------------------------------------------------------------
-def make_weights(dims, seed=0):
-    from sana_b200 import randn_torch_cpu
+def make_weights(dims, seed=0, randn=None):
+    """The synthetic checkpoint, drawn with `randn` (the product's torch-compatible generator by
+    default; the CPU arms pass their own checker's, so that their process maps no product
+    library)."""
     from sana_b200 import synthetic as syn
+    if randn is None:
+        from sana_b200 import randn_torch_cpu as randn
     specs = syn.model_tensor_specs(dims)
     workers = min(32, len(os.sched_getaffinity(0)))
     with cf.ThreadPoolExecutor(max_workers=workers) as ex:
-        return list(ex.map(lambda j: syn.generate_tensor(specs[j], j, dims, randn_torch_cpu, seed), range(len(specs))))
+        return list(ex.map(lambda j: syn.generate_tensor(specs[j], j, dims, randn, seed), range(len(specs))))
 
 
 def make_inputs(first, count):
@@ -173,12 +180,11 @@ def vae_cpu_sample(vd, threads=None):
     to the 1024 x 1024 decode by algorithmic FLOPs (the decoder's work is linear in pixels)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     from oracle import Oracle, Reference
-    from sana_b200 import randn_torch_cpu
     from sana_b200 import synthetic_vae as sv
     impl, kind = (Reference(), "reference") if Reference.available() else (Oracle(), "port")
     threads = 1 if kind == "port" else (threads or min(64, len(os.sched_getaffinity(0))))
-    tensors = sv.generate_vae(vd, randn_torch_cpu, 3)
-    lats = [randn_torch_cpu(vd.latent_channels * 16, 900 + i).reshape(1, vd.latent_channels, 4, 4)
+    tensors = sv.generate_vae(vd, impl.randn, 3)
+    lats = [impl.randn(vd.latent_channels * 16, 900 + i).reshape(1, vd.latent_channels, 4, 4)
             for i in range(threads)]
     t0 = time.perf_counter()
     with cf.ThreadPoolExecutor(max_workers=threads) as ex:
@@ -195,14 +201,15 @@ def vae_cpu_sample(vd, threads=None):
 # ------------------------------------------------------------------------------------------
 def cpu_sample(threads=None):
     """One reference block_forward of one 1024-token sequence per thread, all threads at
-    once; returns (images_per_s, seconds, threads, kind)."""
+    once; returns (images_per_s, seconds, threads, kind). Weights and inputs come from the
+    checker's own torch-compatible generator (the same draws as the product's)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     from oracle import Oracle, Reference
-    from sana_b200 import randn_torch_cpu
     from sana_b200 import synthetic as syn
     impl, kind = (Reference(), "reference") if Reference.available() else (Oracle(), "port")
+    randn_torch_cpu = impl.randn
     d1 = syn.ModelDims(n_blocks=1)
-    tensors = make_weights(d1)
+    tensors = make_weights(d1, randn=randn_torch_cpu)
     model = impl.model(tensors, *d1.as_args())
     del tensors
     threads = threads or min(64, len(os.sched_getaffinity(0)))
@@ -556,9 +563,12 @@ def run_cuda(args):
     d2h = h_out.numel() * 4
 
     # ---- roofline of the dominant kernel, measured live: one eager loop with CUDA events ----
+    from sana_b200 import gemm_counts
+    tc0, simt0 = gemm_counts()
     prof = g.profile_loop_device(d_lat.data_ptr(), B, 32, 32, d_enc.data_ptr(), CAPTION_LEN, 2304,
                                  d_bias.data_ptr(), d_out.data_ptr(), GUIDANCE, NUM_STEPS)
     torch.cuda.synchronize()
+    tc1, simt1 = gemm_counts()
     classes = kernel_classes(B, lens)
     gemm_names = [k for k, v in classes.items() if v[0] == "flop"]
     gemm_ms = sum(prof[k][1] for k in gemm_names if k in prof)
@@ -609,14 +619,14 @@ def run_cuda(args):
                          "algorithmic_per_launch": ff_flops, "launches": ff_n, "avg_launch_ms": ff_ms_launch,
                          "peak_source": f"{pk_kind} bf16_tflops_sustained (kernel timed inside the loop)",
                          "measured": "CUDA events around every launch of one eager loop on the launch stream",
-                         # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel at this
-                         # workload (M=32768, K=1152, N=5760) from the ncu capture summarised in
-                         # profiles/gemm_tc2_ff_inverted_config2.md (algorithmic bytes: 466 MB)
-                         "traffic": FF_INVERTED_TRAFFIC_BYTES if B == 16 else None, "traffic_unit": "bytes",
+                         "traffic": FF_INVERTED_TRAFFIC["bytes"] if B == 16 else None, "traffic_unit": "bytes",
+                         "traffic_source": (FF_INVERTED_TRAFFIC["source"] + ", copied, not measured in this run")
+                         if B == 16 else "no capture at this per-GPU batch",
                          "all_block_gemms": {"achieved": achieved, "unit": "TFLOP/s",
                                              "frac": achieved / pk["bf16_tflops_sustained"]},
                          "isolated_per_shape": per_shape},
             "kernels": breakdown,
+            "gemm_dispatch_per_loop": {"tensor_core": tc1 - tc0, "cuda_core": simt1 - simt0},
             "model_flops": {"per_loop_tflop": flops / 1e12, "achieved_tflops": flops / (ms_per_step / 1e3) / 1e12,
                             "frac_of_sustained_peak": flops / (ms_per_step / 1e3) / 1e12 / pk["bf16_tflops_sustained"],
                             "gemm_share_of_flops": gemm_flops / flops},

@@ -284,7 +284,11 @@ size_t sana_op_linear_attention_workspace(int S, int T, int heads, int D);
  *    launch nothing.
  *  - First call on each device: it looks up the scratch's device address, with the handle's
  *    device made current for the call, and the CUDA runtime may load this library's device
- *    code there at that moment. Make that first call before any stream capture begins.
+ *    code there at that moment. Make that first call before any stream capture begins. The
+ *    address is remembered per device together with the id of the CUDA context it belongs
+ *    to; if that context has been replaced (cudaDeviceReset re-creates the primary context),
+ *    the next call looks the address up again, so the first call after a reset is another
+ *    set-up call with the same rule.
  *  - Nothing in the scratch has to start at zero: every call writes each scratch word
  *    before reading it.
  *  - All handles, streams and host threads on one device share the one scratch. Two calls
@@ -307,6 +311,53 @@ int sana_op_cross_attention_device(sana_cuda_ctx *ctx, const void *q, const void
                                    int *kv_len, int S, int T, int L, int heads, int D, void *out);
 
 /* --- scheduler (scheduler.h:34-65) ----------------------------------------------------- */
+
+/* SanaSchedulerConfig (scheduler.h:9-20) as plain fields. The string-valued fields map to
+ * flags: use_flow_sigmas, final_sigmas_zero (final_sigmas_type == "zero"), solver_heun
+ * (solver_type "heun" rather than "midpoint"); timestep_spacing "linspace",
+ * prediction_type "flow_prediction" and algorithm_type "dpmsolver++" are the only values
+ * the reference accepts and are not carried. sana_scheduler_config_default fills the
+ * reference's defaults (make_sana_scheduler_config, scheduler.cpp:85-87). Every entry
+ * point below that takes a config checks it as validate_scheduler_config does
+ * (scheduler.cpp:8-24): solver_order 1 or 2, else SANA_ERR_INVALID. */
+typedef struct sana_scheduler_config {
+    int num_train_timesteps;
+    float flow_shift;
+    int use_flow_sigmas;
+    int solver_order;
+    int lower_order_final;
+    int final_sigmas_zero;
+    int solver_heun;
+} sana_scheduler_config;
+void sana_scheduler_config_default(sana_scheduler_config *config);
+
+/* build_sana_scheduler_timesteps (scheduler.cpp:89-141) for any config: timesteps[n],
+ * sigmas[n + 1]; SANA_ERR_INVALID where the reference throws (flow sigmas, zero final
+ * sigma and num_train_timesteps > 0 required). Host only. */
+int sana_scheduler_schedule_config(const sana_scheduler_config *config, int n, float *timesteps, float *sigmas);
+/* sana_scheduler_update with a config: flow or variance-preserving sigmas
+ * (sigma_to_alpha_sigma_t, scheduler.cpp:71-77), midpoint or heun second order
+ * (scheduler.cpp:250-269). */
+int sana_scheduler_update_config(sana_cuda_ctx *ctx, const sana_scheduler_config *config, int order,
+                                 const float *sigmas, int n_sigmas, int step_index, const float *m0, const float *m1,
+                                 const float *sample, int numel, float *out);
+/* sana_scheduler_step with a config: the order chosen as step_sana_scheduler chooses it
+ * (solver_order, lower_order_final, final_sigmas_type; scheduler.cpp:291-311), the history
+ * kept to solver_order outputs. */
+int sana_scheduler_step_config(sana_cuda_ctx *ctx, const sana_scheduler_config *config, const float *sigmas,
+                               int n_sigmas, int *step_index, int *lower_order_count, float *history, int *n_history,
+                               const float *model_output, const float *sample, int numel, float *out);
+/* sana_cuda_denoise_step with a config (run_full_denoising_step_with_cfg passes its
+ * SanaSchedulerConfig to step_sana_scheduler, transformer.cpp:683-689). */
+int sana_cuda_denoise_step_config(sana_cuda_ctx *ctx, const sana_scheduler_config *config, float *latents, int B,
+                                  int H, int W, const float *context, int L, const float *bias, float guidance,
+                                  float timestep, const float *sigmas, int n_sigmas, int *step_index,
+                                  int *lower_order_count, float *history, int *n_history);
+/* sana_cuda_denoise_loop with a config: a fresh state built from `config`
+ * (init_sana_scheduler_state) run to its last step, as one CUDA graph from the second call. */
+int sana_cuda_denoise_loop_config(sana_cuda_ctx *ctx, const sana_scheduler_config *config, const float *latents,
+                                  int B, int H, int W, const float *enc, int L, int enc_dim, const float *bias,
+                                  float guidance, int num_steps, float *out);
 
 /* build_sana_scheduler_timesteps (scheduler.cpp:89-141), default config with flow_shift;
  * host only: timesteps[n], sigmas[n + 1]. */

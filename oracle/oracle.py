@@ -43,6 +43,18 @@ class CheckerError(RuntimeError):
     pass
 
 
+class SchedConfig(ctypes.Structure):
+    """SanaSchedulerConfig (scheduler.h:9-20) as plain fields (orc_sched_config / RefSchedConfig)."""
+    _fields_ = [("num_train_timesteps", ctypes.c_int), ("flow_shift", ctypes.c_float),
+                ("use_flow_sigmas", ctypes.c_int), ("solver_order", ctypes.c_int),
+                ("lower_order_final", ctypes.c_int), ("final_sigmas_zero", ctypes.c_int),
+                ("solver_heun", ctypes.c_int)]
+
+
+SCHED_DEFAULTS = dict(num_train_timesteps=1000, flow_shift=3.0, use_flow_sigmas=1, solver_order=2,
+                      lower_order_final=1, final_sigmas_zero=1, solver_heun=0)
+
+
 class _Cpu:
     prefix = ""
     path = ""
@@ -181,6 +193,23 @@ class _Cpu:
         out = np.empty((n, x.size), np.float32)
         self._call("scheduler_run", _sz(n), ctypes.c_float(flow_shift), _ptr(mo), _ptr(x), _sz(x.size), _ptr(out))
         return out
+
+    def scheduler_run_config(self, config: dict, model_outputs, sample, sigmas=None):
+        """init_sana_scheduler_state + step_sana_scheduler over all model outputs with a
+        config (the fields of the C ABI's sana_scheduler_config; missing fields take the
+        reference's defaults). `sigmas` [n + 1] replaces the built schedule. Returns
+        (timesteps, sigmas, samples after every step)."""
+        c = SchedConfig(**{**SCHED_DEFAULTS, **config})
+        mo = _f32(model_outputs)
+        x = _f32(sample).reshape(-1)
+        n = mo.shape[0]
+        sg_in = None if sigmas is None else _f32(sigmas)
+        ts = np.empty(n, np.float32)
+        sg = np.empty(n + 1, np.float32)
+        out = np.empty((n, x.size), np.float32)
+        self._call("scheduler_run_config", ctypes.byref(c), _sz(n), _ptr(sg_in), _ptr(mo), _ptr(x), _sz(x.size),
+                   _ptr(ts), _ptr(sg), _ptr(out))
+        return ts, sg, out
 
     def attention_block(self, x, wq, bq, wk, bk, wv, bv, wo, bo, heads):
         x, wq, bq, wk, bk, wv, bv, wo, bo = map(_f32, (x, wq, bq, wk, bk, wv, bv, wo, bo))

@@ -407,6 +407,48 @@ int ref_scheduler_run(size_t n_steps, float flow_shift, const float * model_outp
     });
 }
 
+// The C ABI's scheduler config as plain fields (same layout as orc_sched_config).
+struct RefSchedConfig {
+    int num_train_timesteps;
+    float flow_shift;
+    int use_flow_sigmas;
+    int solver_order;
+    int lower_order_final;
+    int final_sigmas_zero;
+    int solver_heun;
+};
+
+// init_sana_scheduler_state + step_sana_scheduler n_steps times with any config; sigmas_in
+// [n_steps + 1] (or null) replaces the built schedule, for configs the builder refuses.
+int ref_scheduler_run_config(const RefSchedConfig * c, size_t n_steps, const float * sigmas_in,
+                             const float * model_outputs, const float * sample, size_t numel,
+                             float * timesteps_out, float * sigmas_out, float * samples_out) {
+    return guarded([&] {
+        SanaSchedulerConfig cfg = make_sana_scheduler_config();
+        cfg.num_train_timesteps = static_cast<size_t>(c->num_train_timesteps);
+        cfg.flow_shift = c->flow_shift;
+        cfg.use_flow_sigmas = c->use_flow_sigmas != 0;
+        cfg.solver_order = static_cast<size_t>(c->solver_order);
+        cfg.lower_order_final = c->lower_order_final != 0;
+        cfg.final_sigmas_type = c->final_sigmas_zero ? "zero" : "sigma_min";
+        cfg.solver_type = c->solver_heun ? "heun" : "midpoint";
+        SanaSchedulerState state;
+        if (sigmas_in) {
+            state.schedule.timesteps.assign(n_steps, 0.0f);
+            state.schedule.sigmas.assign(sigmas_in, sigmas_in + n_steps + 1);
+        } else {
+            state = init_sana_scheduler_state(n_steps, cfg);
+        }
+        std::copy(state.schedule.timesteps.begin(), state.schedule.timesteps.end(), timesteps_out);
+        std::copy(state.schedule.sigmas.begin(), state.schedule.sigmas.end(), sigmas_out);
+        Tensor x = from_ptr(sample, {numel});
+        for (size_t s = 0; s < n_steps; ++s) {
+            x = step_sana_scheduler(from_ptr(model_outputs + s * numel, {numel}), x, state, cfg);
+            to_ptr(x, samples_out + s * numel);
+        }
+    });
+}
+
 // transformer.cpp:570 apply_classifier_free_guidance; noise [2B, Cl, H, W]
 int ref_cfg(const float * noise, size_t B, size_t Cl, size_t Hh, size_t Ww, float g, float * out) {
     return guarded([&] {

@@ -1028,6 +1028,100 @@ int orc_cross_attention_block(const float *x, size_t B, size_t T, size_t C, cons
     return 0;
 }
 
+/* sigma_to_alpha_sigma_t (scheduler.cpp:71-77) and compute_lambda (:79-81). */
+static void alpha_sigma_of(const orc_sched_config *c, float sigma, float *alpha, float *sig) {
+    if (c->use_flow_sigmas) {
+        *alpha = 1.0f - sigma;
+        *sig = sigma;
+    } else {
+        *alpha = 1.0f / sqrtf(sigma * sigma + 1.0f);
+        *sig = sigma * *alpha;
+    }
+}
+
+/* init_sana_scheduler_state (scheduler.cpp:143-153, built by :89-141 with the config's
+ * num_train_timesteps), then step_sana_scheduler (:272-318) n_steps times: convert (:155-173),
+ * history push capped at solver_order, order 1 when solver_order is 1, before the first
+ * completed step or at the final step with lower_order_final / zero final sigma, else the
+ * second-order update (:207-270, midpoint or heun coefficient). */
+int orc_scheduler_run_config(const orc_sched_config *c, size_t n_steps, const float *sigmas_in,
+                             const float *model_outputs, const float *sample, size_t numel,
+                             float *timesteps_out, float *sigmas_out, float *samples_out) {
+    if (c->solver_order <= 0) ORC_INVALID("solver_order must be positive");
+    if (c->solver_order > 2) ORC_INVALID("only solver_order <= 2 is supported");
+    if (n_steps == 0) ORC_INVALID("num_inference_steps must be positive");
+    float *sg = sigmas_out;
+    if (sigmas_in) {
+        memcpy(sg, sigmas_in, (n_steps + 1) * sizeof(float));
+        for (size_t i = 0; i < n_steps; ++i) timesteps_out[i] = 0.0f;
+    } else {
+        if (!c->use_flow_sigmas) ORC_INVALID("only use_flow_sigmas=true is supported");
+        if (!c->final_sigmas_zero) ORC_INVALID("only zero final_sigmas_type is supported");
+        if (c->num_train_timesteps <= 0) ORC_INVALID("num_train_timesteps must be positive");
+        const float denom = (float)c->num_train_timesteps;
+        for (size_t i = 0; i <= n_steps; ++i) {
+            const float alpha = 1.0f + (1.0f / denom - 1.0f) * ((float)i / (float)n_steps);
+            const float sigma = 1.0f - alpha;
+            const float shifted = c->flow_shift * sigma / (1.0f + (c->flow_shift - 1.0f) * sigma);
+            if (i > 0) {
+                sg[n_steps - i] = shifted;
+                timesteps_out[n_steps - i] = (float)(int)(shifted * denom);
+            }
+        }
+        sg[n_steps] = 0.0f;
+    }
+    float *x = (float *)malloc(numel * sizeof(float));
+    float *m0 = (float *)malloc(numel * sizeof(float));
+    float *m1 = (float *)malloc(numel * sizeof(float));
+    memcpy(x, sample, numel * sizeof(float));
+    size_t hist = 0, lower = 0;
+    int rc = 0;
+    for (size_t s = 0; s < n_steps; ++s) {
+        const float *v = model_outputs + s * numel;
+        float *tmp = m1;
+        m1 = m0;
+        m0 = tmp;
+        for (size_t i = 0; i < numel; ++i) m0[i] = x[i] - sg[s] * v[i];
+        hist = hist + 1 < (size_t)c->solver_order ? hist + 1 : (size_t)c->solver_order;
+        const int lower_final = (s == n_steps - 1) && (c->lower_order_final || c->final_sigmas_zero);
+        float at, st, a0, s0;
+        alpha_sigma_of(c, sg[s + 1], &at, &st);
+        alpha_sigma_of(c, sg[s], &a0, &s0);
+        const float lt = logf(at) - logf(st), l0 = logf(a0) - logf(s0);
+        const float h = lt - l0;
+        const float a = st / s0;
+        const float bcoef = -at * (expf(-h) - 1.0f);
+        if (c->solver_order == 1 || lower < 1 || lower_final) {
+            for (size_t i = 0; i < numel; ++i) x[i] = a * x[i] + bcoef * m0[i];
+        } else {
+            if (s == 0) {
+                rc = fail(1, "second-order update requires at least one previous step");
+                break;
+            }
+            if (hist < 2) {
+                rc = fail(1, "second-order update requires two model outputs");
+                break;
+            }
+            float a1, s1;
+            alpha_sigma_of(c, sg[s - 1], &a1, &s1);
+            const float h0 = l0 - (logf(a1) - logf(s1));
+            const float r0 = h0 / h;
+            const float ccoef = c->solver_heun ? at * ((expf(-h) - 1.0f) / h + 1.0f)
+                                               : -0.5f * at * (expf(-h) - 1.0f);
+            for (size_t i = 0; i < numel; ++i) {
+                const float d1 = (1.0f / r0) * (m0[i] - m1[i]);
+                x[i] = a * x[i] + bcoef * m0[i] + ccoef * d1;
+            }
+        }
+        if (lower < (size_t)c->solver_order) lower++;
+        memcpy(samples_out + s * numel, x, numel * sizeof(float));
+    }
+    free(x);
+    free(m0);
+    free(m1);
+    return rc;
+}
+
 /* convert_sana_scheduler_model_output (scheduler.cpp:155-173): x0 = sample - sigma_s v. */
 int orc_scheduler_convert(const float *sigmas, size_t n_sigmas, size_t step_index,
                           const float *model_output, const float *sample, size_t numel,

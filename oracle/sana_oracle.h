@@ -57,6 +57,25 @@ int orc_scheduler_schedule(size_t n, float flow_shift, float *timesteps, float *
 int orc_scheduler_run(size_t n_steps, float flow_shift, const float *model_outputs,
                       const float *sample, size_t numel, float *samples_out);
 
+/* SanaSchedulerConfig (scheduler.h:9-20) as plain fields (the C ABI's sana_scheduler_config). */
+typedef struct orc_sched_config {
+    int num_train_timesteps;
+    float flow_shift;
+    int use_flow_sigmas;
+    int solver_order;
+    int lower_order_final;
+    int final_sigmas_zero;
+    int solver_heun;
+} orc_sched_config;
+/* init_sana_scheduler_state + n_steps x step_sana_scheduler (scheduler.cpp:89-153,272-318) for
+ * any config. sigmas_in [n_steps + 1] replaces the built schedule when not NULL (the step
+ * functions accept schedules the builder refuses, e.g. without flow sigmas); timesteps_out
+ * [n_steps] and sigmas_out [n_steps + 1] receive the schedule used, samples_out
+ * [n_steps, numel] the sample after every step. */
+int orc_scheduler_run_config(const orc_sched_config *c, size_t n_steps, const float *sigmas_in,
+                             const float *model_outputs, const float *sample, size_t numel,
+                             float *timesteps_out, float *sigmas_out, float *samples_out);
+
 int orc_attention_block(const float *x, size_t B, size_t T, size_t C, const float *wq,
                         const float *bq, const float *wk, const float *bk, const float *wv,
                         const float *bv, const float *wo, const float *bo, size_t heads,

@@ -12,6 +12,8 @@
 #include <set>
 #include <stdexcept>
 
+#include <cuda.h>
+
 #include "engine.h"
 #include "gguf.h"
 #include "sana_cuda.h"
@@ -54,6 +56,30 @@ int guard(sana_cuda_ctx* ctx, F&& f) {
         ctx->err = e.what();
         return SANA_ERR_STATE;
     }
+}
+
+// The reference's default scheduler config with `flow_shift`.
+sana::SchedConfig default_sched(float flow_shift) {
+    sana::SchedConfig c;
+    c.flow_shift = flow_shift;
+    return c;
+}
+
+// A C-ABI scheduler config (NULL = the defaults), checked as validate_scheduler_config
+// checks its numeric fields (scheduler.cpp:8-24).
+sana::SchedConfig sched_of(const sana_scheduler_config* p) {
+    sana::SchedConfig c;
+    if (p) {
+        c.num_train_timesteps = p->num_train_timesteps;
+        c.flow_shift = p->flow_shift;
+        c.flow_sigmas = p->use_flow_sigmas != 0;
+        c.solver_order = p->solver_order;
+        c.lower_order_final = p->lower_order_final != 0;
+        c.final_sigmas_zero = p->final_sigmas_zero != 0;
+        c.heun = p->solver_heun != 0;
+    }
+    sana::scheduler_validate(c);
+    return c;
 }
 
 // --- host-side layout / precision helpers for the single-op entry points ----------------
@@ -218,16 +244,47 @@ namespace {
 constexpr int kScratchMaxDevices = 64;
 std::mutex g_scratch_mu;
 float* g_scratch_addr[kScratchMaxDevices] = {};
+unsigned long long g_scratch_ctx[kScratchMaxDevices] = {};  // context id the address belongs to
+
+// The unique id of the calling thread's current CUDA context (cuCtxGetId: never reused within
+// a process, so a context re-created by cudaDeviceReset gets a new one).
+unsigned long long current_context_id() {
+    using GetCurrent = CUresult (*)(CUcontext*);
+    using GetId = CUresult (*)(CUcontext, unsigned long long*);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(p);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(p);
+    });
+    if (!get_current || !get_id) throw sana::CudaError("cuCtxGetCurrent / cuCtxGetId are not available");
+    CUcontext c = nullptr;
+    unsigned long long id = 0;
+    if (get_current(&c) != CUDA_SUCCESS || !c || get_id(c, &id) != CUDA_SUCCESS)
+        throw sana::CudaError("no current CUDA context for the fixed scratch");
+    return id;
+}
 
 // The device address of g_linattn_scratch on `device`, which the caller has made current.
-// Looked up on the first call per device and remembered.
+// Looked up with cudaGetSymbolAddress on the first call per device and remembered together
+// with the id of the context it belongs to; a call in a different context of that device
+// (the primary context re-created after cudaDeviceReset) looks it up again.
 float* linattn_scratch(int device) {
     SANA_REQUIRE(device >= 0 && device < kScratchMaxDevices, "device ordinal out of range for the fixed scratch");
+    const unsigned long long ctx = current_context_id();
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_addr[device]) {
+    if (!g_scratch_addr[device] || g_scratch_ctx[device] != ctx) {
         void* p = nullptr;
         SANA_CUDA(cudaGetSymbolAddress(&p, g_linattn_scratch));
         g_scratch_addr[device] = static_cast<float*>(p);
+        g_scratch_ctx[device] = ctx;
     }
     return g_scratch_addr[device];
 }
@@ -503,7 +560,18 @@ int sana_cuda_denoise_loop(sana_cuda_ctx* ctx, const float* latents, int B, int 
                            float* out) {
     return guard(ctx, [&] {
         SANA_REQUIRE(latents && enc && out, "latents, encoder states and output must not be null");
-        engine(ctx).denoise_loop(latents, B, H, W, enc, L, enc_dim, bias, guidance, num_steps, flow_shift, out);
+        engine(ctx).denoise_loop(latents, B, H, W, enc, L, enc_dim, bias, guidance, num_steps,
+                                 default_sched(flow_shift), out);
+    });
+}
+
+int sana_cuda_denoise_loop_config(sana_cuda_ctx* ctx, const sana_scheduler_config* config, const float* latents,
+                                  int B, int H, int W, const float* enc, int L, int enc_dim, const float* bias,
+                                  float guidance, int num_steps, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(latents && enc && out, "latents, encoder states and output must not be null");
+        engine(ctx).denoise_loop(latents, B, H, W, enc, L, enc_dim, bias, guidance, num_steps, sched_of(config),
+                                 out);
     });
 }
 
@@ -512,17 +580,26 @@ int sana_cuda_denoise_loop_device(sana_cuda_ctx* ctx, const float* latents, int 
                                   float flow_shift, float* out) {
     return guard(ctx, [&] {
         SANA_REQUIRE(latents && enc && out, "latents, encoder states and output must not be null");
-        engine(ctx).denoise_loop_device(latents, B, H, W, enc, L, enc_dim, bias, guidance, num_steps, flow_shift,
-                                        out);
+        engine(ctx).denoise_loop_device(latents, B, H, W, enc, L, enc_dim, bias, guidance, num_steps,
+                                        default_sched(flow_shift), out);
     });
 }
 
 int sana_cuda_denoise_step(sana_cuda_ctx* ctx, float* latents, int B, int H, int W, const float* context, int L,
                            const float* bias, float guidance, float timestep, const float* sigmas, int n_sigmas,
                            int* step_index, int* lower_order_count, float* history, int* n_history) {
+    return sana_cuda_denoise_step_config(ctx, nullptr, latents, B, H, W, context, L, bias, guidance, timestep, sigmas,
+                                         n_sigmas, step_index, lower_order_count, history, n_history);
+}
+
+int sana_cuda_denoise_step_config(sana_cuda_ctx* ctx, const sana_scheduler_config* config, float* latents, int B,
+                                  int H, int W, const float* context, int L, const float* bias, float guidance,
+                                  float timestep, const float* sigmas, int n_sigmas, int* step_index,
+                                  int* lower_order_count, float* history, int* n_history) {
     return guard(ctx, [&] {
         SANA_REQUIRE(latents && context && sigmas && step_index && lower_order_count && n_history,
                      "null argument to denoise_step");
+        const sana::SchedConfig sc = sched_of(config);
         SANA_REQUIRE(*n_history >= 0 && *n_history <= 2, "history holds at most two converted outputs");
         SANA_REQUIRE(*n_history == 0 || history, "history buffer missing");
         sana::Engine& eng = engine(ctx);
@@ -532,7 +609,7 @@ int sana_cuda_denoise_step(sana_cuda_ctx* ctx, float* latents, int B, int H, int
         st.step_index = *step_index;
         st.lower_order_count = *lower_order_count;
         for (int i = 0; i < *n_history; ++i) st.history.emplace_back(history + i * numel, history + (i + 1) * numel);
-        eng.denoise_step(latents, B, H, W, context, L, bias, guidance, st, timestep);
+        eng.denoise_step(latents, B, H, W, context, L, bias, guidance, st, timestep, sc);
         *step_index = st.step_index;
         *lower_order_count = st.lower_order_count;
         *n_history = static_cast<int>(st.history.size());
@@ -579,7 +656,8 @@ int sana_cuda_profile_loop(sana_cuda_ctx* ctx, const float* latents, int B, int 
     return guard(ctx, [&] {
         SANA_REQUIRE(latents && enc && out && report && report_len > 0, "null argument to profile_loop");
         sana::Engine& eng = engine(ctx);
-        eng.profile_loop_device(latents, B, H, W, enc, L, enc_dim, bias, guidance, num_steps, flow_shift, out);
+        eng.profile_loop_device(latents, B, H, W, enc, L, enc_dim, bias, guidance, num_steps,
+                                default_sched(flow_shift), out);
         const std::string r = eng.profile_report();
         eng.profile_enable(false);
         std::snprintf(report, report_len, "%s", r.c_str());
@@ -1222,17 +1300,36 @@ int sana_op_cross_attention_device(sana_cuda_ctx* ctx, const void* q, const void
 
 // --- scheduler -------------------------------------------------------------------------------
 
-int sana_scheduler_schedule(int n, float flow_shift, float* timesteps, float* sigmas) {
-    if (n <= 0 || !timesteps || !sigmas) return SANA_ERR_INVALID;
+void sana_scheduler_config_default(sana_scheduler_config* c) {
+    if (!c) return;
+    const sana::SchedConfig d;
+    c->num_train_timesteps = d.num_train_timesteps;
+    c->flow_shift = d.flow_shift;
+    c->use_flow_sigmas = d.flow_sigmas ? 1 : 0;
+    c->solver_order = d.solver_order;
+    c->lower_order_final = d.lower_order_final ? 1 : 0;
+    c->final_sigmas_zero = d.final_sigmas_zero ? 1 : 0;
+    c->solver_heun = d.heun ? 1 : 0;
+}
+
+int sana_scheduler_schedule_config(const sana_scheduler_config* config, int n, float* timesteps, float* sigmas) {
+    if (!timesteps || !sigmas) return SANA_ERR_INVALID;
     try {
         std::vector<float> ts, sg;
-        sana::scheduler_schedule(n, flow_shift, ts, sg);
+        sana::scheduler_schedule(n, sched_of(config), ts, sg);
         std::memcpy(timesteps, ts.data(), ts.size() * 4);
         std::memcpy(sigmas, sg.data(), sg.size() * 4);
         return SANA_OK;
     } catch (...) {
         return SANA_ERR_INVALID;
     }
+}
+
+int sana_scheduler_schedule(int n, float flow_shift, float* timesteps, float* sigmas) {
+    sana_scheduler_config c;
+    sana_scheduler_config_default(&c);
+    c.flow_shift = flow_shift;
+    return sana_scheduler_schedule_config(&c, n, timesteps, sigmas);
 }
 
 int sana_scheduler_convert(sana_cuda_ctx* ctx, const float* sigmas, int n_sigmas, int step_index,
@@ -1260,13 +1357,21 @@ int sana_scheduler_convert(sana_cuda_ctx* ctx, const float* sigmas, int n_sigmas
 
 int sana_scheduler_update(sana_cuda_ctx* ctx, int order, const float* sigmas, int n_sigmas, int step_index,
                           const float* m0, const float* m1, const float* sample, int numel, float* out) {
+    return sana_scheduler_update_config(ctx, nullptr, order, sigmas, n_sigmas, step_index, m0, m1, sample, numel,
+                                        out);
+}
+
+int sana_scheduler_update_config(sana_cuda_ctx* ctx, const sana_scheduler_config* config, int order,
+                                 const float* sigmas, int n_sigmas, int step_index, const float* m0, const float* m1,
+                                 const float* sample, int numel, float* out) {
     return guard(ctx, [&] {
         SANA_REQUIRE(sigmas && m0 && sample && out && numel >= 1, "invalid update arguments");
         SANA_REQUIRE(order == 1 || order == 2, "order must be 1 or 2");
         SANA_REQUIRE(order == 1 || m1, "second-order update requires two model outputs");
+        const sana::SchedConfig sc = sched_of(config);
         sana::Engine& eng = engine(ctx);
         std::vector<float> sg(sigmas, sigmas + n_sigmas);
-        const sana::SchedCoef k = sana::scheduler_coefficients_order(sg, step_index, order, 1.0f);
+        const sana::SchedCoef k = sana::scheduler_coefficients_order(sg, step_index, order, 1.0f, sc);
         DevBuf a = f32_upload(m0, numel), b = f32_upload(m1 ? m1 : m0, numel), x = f32_upload(sample, numel), o;
         o.ensure(numel * 4);
         sana::scheduler_update(a.as<float>(), b.as<float>(), x.as<float>(), numel, k, o.as<float>(), eng.stream());
@@ -1278,17 +1383,28 @@ int sana_scheduler_update(sana_cuda_ctx* ctx, int order, const float* sigmas, in
 int sana_scheduler_step(sana_cuda_ctx* ctx, const float* sigmas, int n_sigmas, int* step_index,
                         int* lower_order_count, float* history, int* n_history, const float* model_output,
                         const float* sample, int numel, float* out) {
+    return sana_scheduler_step_config(ctx, nullptr, sigmas, n_sigmas, step_index, lower_order_count, history,
+                                      n_history, model_output, sample, numel, out);
+}
+
+int sana_scheduler_step_config(sana_cuda_ctx* ctx, const sana_scheduler_config* config, const float* sigmas,
+                               int n_sigmas, int* step_index, int* lower_order_count, float* history, int* n_history,
+                               const float* model_output, const float* sample, int numel, float* out) {
     return guard(ctx, [&] {
         SANA_REQUIRE(sigmas && step_index && lower_order_count && n_history && model_output && sample && out &&
                          numel >= 1,
                      "invalid step arguments");
         SANA_REQUIRE(*n_history >= 0 && *n_history <= 2 && (*n_history == 0 || history), "invalid history");
         SANA_REQUIRE(history != nullptr, "history buffer (2 x numel) required");
+        const sana::SchedConfig sc = sched_of(config);
         sana::Engine& eng = engine(ctx);
         std::vector<float> sg(sigmas, sigmas + n_sigmas);
-        const sana::SchedCoef k = sana::scheduler_coefficients(sg, *step_index, *lower_order_count, 1.0f);
+        const sana::SchedCoef k = sana::scheduler_coefficients(sg, *step_index, *lower_order_count, 1.0f, sc);
+        // the history after this step's push, capped at solver_order (step_sana_scheduler,
+        // scheduler.cpp:286-289), must hold two outputs for the second-order update
+        const int kept = std::min(*n_history + 1, sc.solver_order);
         if (k.second_order) {
-            SANA_REQUIRE(*n_history >= 1, "second-order update requires two model outputs");
+            SANA_REQUIRE(kept >= 2, "second-order update requires two model outputs");
         }
         std::vector<float> rows(2 * static_cast<size_t>(numel));
         std::memcpy(rows.data(), model_output, numel * 4);
@@ -1303,11 +1419,14 @@ int sana_scheduler_step(sana_cuda_ctx* ctx, const float* sigmas, int n_sigmas, i
         d2h(out, lat.get(), numel * 4);
         std::vector<float> conv(numel);
         d2h(conv.data(), h0.get(), numel * 4);
-        if (*n_history == 2) std::memmove(history, history + numel, static_cast<size_t>(numel) * 4);
-        const int slot = *n_history == 2 ? 1 : *n_history;
-        std::memcpy(history + static_cast<size_t>(slot) * numel, conv.data(), numel * 4);
-        *n_history = slot + 1;
-        if (*lower_order_count < 2) ++*lower_order_count;
+        // push, then keep the newest `kept` outputs, oldest first
+        const int drop = *n_history + 1 - kept;
+        if (drop > 0 && *n_history > drop)
+            std::memmove(history, history + static_cast<size_t>(drop) * numel,
+                         static_cast<size_t>(*n_history - drop) * numel * 4);
+        std::memcpy(history + static_cast<size_t>(kept - 1) * numel, conv.data(), numel * 4);
+        *n_history = kept;
+        if (*lower_order_count < sc.solver_order) ++*lower_order_count;
         ++*step_index;
     });
 }

@@ -34,9 +34,19 @@ void DevBuf::release() {
 // ---------------------------------------------------------------------------------------
 // Host-side scheduler and timestep arithmetic (the reference's fp32 expressions)
 // ---------------------------------------------------------------------------------------
-void scheduler_schedule(int n, float flow_shift, std::vector<float>& timesteps, std::vector<float>& sigmas) {
+void scheduler_validate(const SchedConfig& c) {
+    SANA_REQUIRE(c.solver_order >= 1, "solver_order must be positive");
+    SANA_REQUIRE(c.solver_order <= 2, "only solver_order <= 2 is supported");
+}
+
+void scheduler_schedule(int n, const SchedConfig& c, std::vector<float>& timesteps, std::vector<float>& sigmas) {
+    scheduler_validate(c);
     SANA_REQUIRE(n > 0, "num_inference_steps must be positive");
-    const float denom = 1000.0f;
+    SANA_REQUIRE(c.flow_sigmas, "only use_flow_sigmas=true is supported");
+    SANA_REQUIRE(c.final_sigmas_zero, "only zero final_sigmas_type is supported");
+    SANA_REQUIRE(c.num_train_timesteps > 0, "num_train_timesteps must be positive");
+    const float denom = static_cast<float>(c.num_train_timesteps);
+    const float flow_shift = c.flow_shift;
     std::vector<float> shifted(static_cast<size_t>(n) + 1);
     // alpha = 1 + (1/denom - 1) * i/n; sigma = 1 - alpha; shifted = shift*sigma / (1 + (shift-1)*sigma)
     // (scheduler.cpp:124-131). The reference as compiled (g++ -O3 with FMA available)
@@ -57,47 +67,82 @@ void scheduler_schedule(int n, float flow_shift, std::vector<float>& timesteps, 
     sigmas.push_back(0.0f);
 }
 
-static float flow_lambda(float sigma) {
-    const float alpha = 1.0f - sigma;
-    return std::log(alpha) - std::log(sigma);
+void scheduler_schedule(int n, float flow_shift, std::vector<float>& timesteps, std::vector<float>& sigmas) {
+    SchedConfig c;
+    c.flow_shift = flow_shift;
+    scheduler_schedule(n, c, timesteps, sigmas);
 }
 
-SchedCoef scheduler_coefficients(const std::vector<float>& sg, int i, int lower, float guidance) {
+// sigma_to_alpha_sigma_t (scheduler.cpp:71-77): flow sigmas give (1 - sigma, sigma), the
+// variance-preserving form (1 / sqrt(sigma^2 + 1), sigma / sqrt(sigma^2 + 1)); the square
+// term is a fused multiply-add as in the reference build.
+static void alpha_sigma(float sigma, const SchedConfig& c, float& alpha, float& sig) {
+    if (c.flow_sigmas) {
+        alpha = 1.0f - sigma;
+        sig = sigma;
+    } else {
+        alpha = 1.0f / std::sqrt(std::fma(sigma, sigma, 1.0f));
+        sig = sigma * alpha;
+    }
+}
+
+// compute_lambda (scheduler.cpp:79-81).
+static float lambda_of(float alpha, float sigma) { return std::log(alpha) - std::log(sigma); }
+
+int scheduler_step_order(const SchedConfig& c, int n, int i, int lower) {
+    const bool lower_final = (i == n - 1) && (c.lower_order_final || c.final_sigmas_zero);
+    return (c.solver_order == 1 || lower < 1 || lower_final) ? 1 : 2;
+}
+
+SchedCoef scheduler_coefficients(const std::vector<float>& sg, int i, int lower, float guidance,
+                                 const SchedConfig& c) {
     SANA_REQUIRE(sg.size() >= 2 && i >= 0 && i < static_cast<int>(sg.size()) - 1,
                  "scheduler step_index is out of range");
     const int n = static_cast<int>(sg.size()) - 1;
-    // lower_order_final at the last step, first order until one step has run
-    // (step_sana_scheduler, scheduler.cpp:291-311 with solver_order 2)
-    return scheduler_coefficients_order(sg, i, (lower < 1 || i == n - 1) ? 1 : 2, guidance);
+    return scheduler_coefficients_order(sg, i, scheduler_step_order(c, n, i, lower), guidance, c);
 }
 
-SchedCoef scheduler_coefficients_order(const std::vector<float>& sg, int i, int order, float guidance) {
+SchedCoef scheduler_coefficients_order(const std::vector<float>& sg, int i, int order, float guidance,
+                                       const SchedConfig& c) {
     SANA_REQUIRE(sg.size() >= 2 && i >= 0 && i < static_cast<int>(sg.size()) - 1,
                  "scheduler step_index is out of range");
     SANA_REQUIRE(order == 1 || i >= 1, "second-order update requires at least one previous step");
     SchedCoef k{};
     k.guidance = guidance;
-    k.sigma_s = sg[i];
-    const float sigma_t = sg[i + 1];
-    const float alpha_t = 1.0f - sg[i + 1];
-    if (order == 1) {
-        const float h = flow_lambda(sigma_t) - flow_lambda(sg[i]);
-        k.a = sigma_t / sg[i];
-        k.b = -alpha_t * (std::exp(-h) - 1.0f);
+    k.sigma_s = sg[i];  // convert_sana_scheduler_model_output uses the schedule's sigma as is
+    float alpha_t, sigma_t, alpha_s0, sigma_s0;
+    alpha_sigma(sg[i + 1], c, alpha_t, sigma_t);
+    alpha_sigma(sg[i], c, alpha_s0, sigma_s0);
+    const float lambda_t = lambda_of(alpha_t, sigma_t), lambda_s0 = lambda_of(alpha_s0, sigma_s0);
+    const float h = lambda_t - lambda_s0;
+    k.a = sigma_t / sigma_s0;
+    k.b = -alpha_t * (std::exp(-h) - 1.0f);
+    if (order == 1) {  // sana_scheduler_first_order_update (scheduler.cpp:175-205)
         k.c = 0.0f;
         k.inv_r0 = 0.0f;
         k.second_order = 0;
-    } else {
-        const float lt = flow_lambda(sigma_t), l0 = flow_lambda(sg[i]), l1 = flow_lambda(sg[i - 1]);
-        const float h = lt - l0, h0 = l0 - l1;
+    } else {  // sana_scheduler_second_order_update (scheduler.cpp:207-270)
+        float alpha_s1, sigma_s1;
+        alpha_sigma(sg[i - 1], c, alpha_s1, sigma_s1);
+        const float h0 = lambda_s0 - lambda_of(alpha_s1, sigma_s1);
         const float r0 = h0 / h;
-        k.a = sigma_t / sg[i];
-        k.b = -alpha_t * (std::exp(-h) - 1.0f);
-        k.c = -0.5f * alpha_t * (std::exp(-h) - 1.0f);
+        k.c = c.heun ? alpha_t * ((std::exp(-h) - 1.0f) / h + 1.0f) : -0.5f * alpha_t * (std::exp(-h) - 1.0f);
         k.inv_r0 = 1.0f / r0;
         k.second_order = 1;
     }
     return k;
+}
+
+std::vector<SchedCoef> scheduler_loop_coefficients(const SchedConfig& c, const std::vector<float>& sg, float guidance) {
+    scheduler_validate(c);
+    const int n = static_cast<int>(sg.size()) - 1;
+    std::vector<SchedCoef> coefs;
+    int lower = 0;
+    for (int i = 0; i < n; ++i) {
+        coefs.push_back(scheduler_coefficients(sg, i, lower, guidance, c));
+        if (lower < c.solver_order) ++lower;
+    }
+    return coefs;
 }
 
 void timestep_features(float t, float* out) {
@@ -157,6 +202,7 @@ void Engine::gemm_act(const void* A, long long lda, const void* Bw, long long ld
     p.a_bf16 = (!f32_operands && mode_ == kModeBf16) ? 1 : 0;
     p.b_bf16 = p.a_bf16;
     p.ep = ep;
+    p.require_tc = 1;
     gemm(p, err(), st_, num_sms_);
 }
 
@@ -590,24 +636,21 @@ void Engine::loop_body(const float* lat_in, int B, int H, int W, const float* en
 // Loop driver with graph capture
 // ---------------------------------------------------------------------------------------
 void Engine::run_loop(const float* lat_d, int B, int H, int W, const float* enc_d, int L, int Din,
-                      const float* bias_d, float guidance, int num_steps, float flow_shift, float* out_d,
+                      const float* bias_d, float guidance, int num_steps, const SchedConfig& sc, float* out_d,
                       const std::string& key_extra) {
     SANA_REQUIRE(num_steps >= 1 && num_steps <= 1024, "num_inference_steps must be in 1..1024");
     std::vector<float> ts, sg;
-    scheduler_schedule(num_steps, flow_shift, ts, sg);
-    std::vector<SchedCoef> coefs;
-    int lower = 0;
-    for (int i = 0; i < num_steps; ++i) {
-        coefs.push_back(scheduler_coefficients(sg, i, lower, guidance));
-        if (lower < 2) ++lower;
-    }
+    scheduler_schedule(num_steps, sc, ts, sg);
+    const std::vector<SchedCoef> coefs = scheduler_loop_coefficients(sc, sg, guidance);
     std::vector<float> table(static_cast<size_t>(num_steps) * 256);
     for (int i = 0; i < num_steps; ++i) timestep_features(ts[i], table.data() + static_cast<size_t>(i) * 256);
     SANA_CUDA(cudaMemcpyAsync(tproj_table_.get(), table.data(), table.size() * 4, cudaMemcpyHostToDevice, st_));
 
     std::ostringstream key;
     key << B << ',' << H << ',' << W << ',' << L << ',' << Din << ',' << num_steps << ',' << guidance << ','
-        << flow_shift << ',' << lat_d << ',' << enc_d << ',' << bias_d << ',' << out_d << ',' << key_extra;
+        << sc.flow_shift << ',' << sc.num_train_timesteps << ',' << sc.flow_sigmas << sc.solver_order
+        << sc.lower_order_final << sc.final_sigmas_zero << sc.heun << ',' << lat_d << ',' << enc_d << ',' << bias_d
+        << ',' << out_d << ',' << key_extra;
     GraphEntry& g = graphs_[key.str()];
     auto body = [&] {
         if (mode_ == kModeBf16) loop_body<bf16>(lat_d, B, H, W, enc_d, L, Din, bias_d, coefs, out_d);
@@ -647,16 +690,16 @@ void Engine::run_loop(const float* lat_d, int B, int H, int W, const float* enc_
 }
 
 void Engine::denoise_loop_device(const float* lat, int B, int H, int W, const float* enc, int L, int Din,
-                                 const float* bias, float guidance, int num_steps, float flow_shift, float* out) {
+                                 const float* bias, float guidance, int num_steps, const SchedConfig& sc, float* out) {
     SANA_REQUIRE(have_w_, "weights have not been uploaded");
     SANA_REQUIRE(B >= 1 && H >= 1 && W >= 1 && L >= 1, "invalid loop shapes");
     SANA_REQUIRE(Din == d_.Din, "encoder hidden size must match caption projection input");
     ensure_workspace(2 * B, H * W, L);
-    run_loop(lat, B, H, W, enc, L, Din, bias, guidance, num_steps, flow_shift, out, "dev");
+    run_loop(lat, B, H, W, enc, L, Din, bias, guidance, num_steps, sc, out, "dev");
 }
 
 void Engine::denoise_loop(const float* lat, int B, int H, int W, const float* enc, int L, int Din, const float* bias,
-                          float guidance, int num_steps, float flow_shift, float* out) {
+                          float guidance, int num_steps, const SchedConfig& sc, float* out) {
     SANA_REQUIRE(have_w_, "weights have not been uploaded");
     SANA_REQUIRE(B >= 1 && H >= 1 && W >= 1 && L >= 1, "invalid loop shapes");
     SANA_REQUIRE(Din == d_.Din, "encoder hidden size must match caption projection input");
@@ -669,7 +712,7 @@ void Engine::denoise_loop(const float* lat, int B, int H, int W, const float* en
         SANA_CUDA(cudaMemcpyAsync(in_bias_.get(), bias, static_cast<size_t>(S) * L * 4, cudaMemcpyHostToDevice, st_));
     }
     run_loop(in_lat_.as<float>(), B, H, W, in_enc_.as<float>(), L, Din, bias ? in_bias_.as<float>() : nullptr,
-             guidance, num_steps, flow_shift, out_buf_.as<float>(), "host");
+             guidance, num_steps, sc, out_buf_.as<float>(), "host");
     SANA_CUDA(cudaMemcpyAsync(out, out_buf_.get(), n_lat * 4, cudaMemcpyDeviceToHost, st_));
     SANA_CUDA(cudaStreamSynchronize(st_));
     check_device_error();
@@ -813,7 +856,8 @@ void Engine::forward_nocfg(const float* lat, int S, int H, int W, float t, const
 }
 
 void Engine::denoise_step(float* lat, int B, int H, int W, const float* ctx, int L, const float* bias, float guidance,
-                          SchedulerHostState& state, float timestep) {
+                          SchedulerHostState& state, float timestep, const SchedConfig& sc) {
+    scheduler_validate(sc);
     SANA_REQUIRE(have_w_, "weights have not been uploaded");
     SANA_REQUIRE(state.sigmas.size() >= 2, "scheduler sigmas must have one extra final entry");
     SANA_REQUIRE(state.step_index >= 0 && state.step_index < static_cast<int>(state.sigmas.size()) - 1,
@@ -821,8 +865,9 @@ void Engine::denoise_step(float* lat, int B, int H, int W, const float* ctx, int
     const int S = 2 * B, Tn = H * W, C = d_.C, Cl = d_.Cl;
     ensure_workspace(S, Tn, L);
     const size_t n_lat = static_cast<size_t>(B) * Cl * Tn;
-    const SchedCoef k = scheduler_coefficients(state.sigmas, state.step_index, state.lower_order_count, guidance);
+    const SchedCoef k = scheduler_coefficients(state.sigmas, state.step_index, state.lower_order_count, guidance, sc);
     if (k.second_order) {
+        // the converted output of this step joins the history, capped at solver_order (2)
         SANA_REQUIRE(!state.history.empty() && state.history.back().size() == n_lat,
                      "second-order update requires two model outputs");
     }
@@ -865,8 +910,8 @@ void Engine::denoise_step(float* lat, int B, int H, int W, const float* ctx, int
     SANA_CUDA(cudaStreamSynchronize(st_));
     check_device_error();
     state.history.push_back(std::move(x0));
-    if (state.history.size() > 2) state.history.erase(state.history.begin());
-    if (state.lower_order_count < 2) ++state.lower_order_count;
+    while (state.history.size() > static_cast<size_t>(sc.solver_order)) state.history.erase(state.history.begin());
+    if (state.lower_order_count < sc.solver_order) ++state.lower_order_count;
     ++state.step_index;
 }
 
@@ -925,17 +970,12 @@ std::string Engine::profile_report() {
 }
 
 void Engine::profile_loop_device(const float* lat, int B, int H, int W, const float* enc, int L, int Din,
-                                 const float* bias, float guidance, int num_steps, float flow_shift, float* out) {
+                                 const float* bias, float guidance, int num_steps, const SchedConfig& sc, float* out) {
     SANA_REQUIRE(have_w_, "weights have not been uploaded");
     ensure_workspace(2 * B, H * W, L);
     std::vector<float> ts, sg;
-    scheduler_schedule(num_steps, flow_shift, ts, sg);
-    std::vector<SchedCoef> coefs;
-    int lower = 0;
-    for (int i = 0; i < num_steps; ++i) {
-        coefs.push_back(scheduler_coefficients(sg, i, lower, guidance));
-        if (lower < 2) ++lower;
-    }
+    scheduler_schedule(num_steps, sc, ts, sg);
+    const std::vector<SchedCoef> coefs = scheduler_loop_coefficients(sc, sg, guidance);
     std::vector<float> table(static_cast<size_t>(num_steps) * 256);
     for (int i = 0; i < num_steps; ++i) timestep_features(ts[i], table.data() + static_cast<size_t>(i) * 256);
     SANA_CUDA(cudaMemcpyAsync(tproj_table_.get(), table.data(), table.size() * 4, cudaMemcpyHostToDevice, st_));

@@ -73,13 +73,35 @@ struct SchedulerHostState {
     std::vector<std::vector<float>> history;  // oldest first, <= 2
 };
 
+// SanaSchedulerConfig (scheduler.h:9-20) as the device path uses it: the string-valued
+// fields the reference only compares against one accepted value (timestep_spacing,
+// prediction_type, algorithm_type) are checked by the callers.
+struct SchedConfig {
+    int num_train_timesteps = 1000;
+    float flow_shift = 3.0f;
+    bool flow_sigmas = true;        // use_flow_sigmas
+    int solver_order = 2;           // 1 or 2
+    bool lower_order_final = true;
+    bool final_sigmas_zero = true;  // final_sigmas_type == "zero"
+    bool heun = false;              // solver_type: midpoint (false) or heun (true)
+};
+// validate_scheduler_config (scheduler.cpp:8-24) for the numeric fields.
+void scheduler_validate(const SchedConfig& c);
+// The order step_sana_scheduler takes at step i of n with lower_order_step_count `lower`
+// (scheduler.cpp:291-311): 1 or 2.
+int scheduler_step_order(const SchedConfig& c, int n_steps, int step_index, int lower_order_count);
 // Host-side DPM-Solver++ coefficients of one step, computed with the reference's fp32
-// arithmetic (scheduler.cpp:175-270, 291-311).
+// arithmetic (scheduler.cpp:71-81, 175-270, 291-311).
 SchedCoef scheduler_coefficients(const std::vector<float>& sigmas, int step_index, int lower_order_count,
-                                 float guidance);
+                                 float guidance, const SchedConfig& c = SchedConfig());
 // The same for an explicit order (1 or 2).
-SchedCoef scheduler_coefficients_order(const std::vector<float>& sigmas, int step_index, int order, float guidance);
+SchedCoef scheduler_coefficients_order(const std::vector<float>& sigmas, int step_index, int order, float guidance,
+                                       const SchedConfig& c = SchedConfig());
+// The coefficients of every step of a fresh state (init_sana_scheduler_state) run to the end.
+std::vector<SchedCoef> scheduler_loop_coefficients(const SchedConfig& c, const std::vector<float>& sigmas,
+                                                   float guidance);
 // build_sana_scheduler_timesteps (scheduler.cpp:89-141).
+void scheduler_schedule(int n, const SchedConfig& c, std::vector<float>& timesteps, std::vector<float>& sigmas);
 void scheduler_schedule(int n, float flow_shift, std::vector<float>& timesteps, std::vector<float>& sigmas);
 // timestep_embedding_2d for one timestep (transformer.cpp:77-122): [cos | sin], 256 wide.
 void timestep_features(float t, float* out256);
@@ -108,12 +130,12 @@ class Engine {
     void forward_nocfg(const float* lat, int S, int H, int W, float t, const float* ctx, int L, const float* bias,
                        float* noise);
     void denoise_step(float* lat, int B, int H, int W, const float* ctx, int L, const float* bias, float guidance,
-                      SchedulerHostState& state, float timestep);
+                      SchedulerHostState& state, float timestep, const SchedConfig& sc = SchedConfig());
     void denoise_loop(const float* lat, int B, int H, int W, const float* enc, int L, int Din, const float* bias,
-                      float guidance, int num_steps, float flow_shift, float* out);
+                      float guidance, int num_steps, const SchedConfig& sc, float* out);
     // Device-pointer variant of denoise_loop (inputs already in HBM, fp32).
     void denoise_loop_device(const float* lat, int B, int H, int W, const float* enc, int L, int Din,
-                             const float* bias, float guidance, int num_steps, float flow_shift, float* out);
+                             const float* bias, float guidance, int num_steps, const SchedConfig& sc, float* out);
 
     // Per-kernel profiling of eager (uncaptured) work: CUDA events around every launch of the
     // loop, summed per kernel class. enable() clears previous records.
@@ -121,7 +143,7 @@ class Engine {
     std::string profile_report();  // JSON: {"kernel": [launches, total_ms], ...}
     // Runs the denoising loop once eagerly with profiling on (device pointers).
     void profile_loop_device(const float* lat, int B, int H, int W, const float* enc, int L, int Din,
-                             const float* bias, float guidance, int num_steps, float flow_shift, float* out);
+                             const float* bias, float guidance, int num_steps, const SchedConfig& sc, float* out);
 
     // Read-back of a named workspace buffer (diagnostics): a, qkv, ao, cq, xb, ffh, glu,
     // x, x1, x2, x3, mods, tmod, emb, ckv1, ctx, kvlen, noise, lat. Returns its size.
@@ -152,7 +174,7 @@ class Engine {
     void gemm_act(const void* A, long long lda, const void* Bw, long long ldb, int M, int N, int K,
                   const Epilogue& ep, bool b_is_f32 = false);
     void run_loop(const float* lat_d, int B, int H, int W, const float* enc_d, int L, int Din, const float* bias_d,
-                  float guidance, int num_steps, float flow_shift, float* out_d, const std::string& key_extra);
+                  float guidance, int num_steps, const SchedConfig& sc, float* out_d, const std::string& key_extra);
     size_t act_size() const { return mode_ == kModeBf16 ? 2 : 4; }
 
     int device_ = 0, mode_ = 0, num_sms_ = 148;

@@ -65,10 +65,16 @@ struct GemmProblem {
     int M = 0, N = 0, K = 0;
     Epilogue ep;
     ConvA conv;  // conv.H == 0: A is a plain row-major matrix
+    // Set by the denoiser and VAE paths: bf16 operands must take the tensor-core kernel
+    // unless the shape itself rules it out (K % 8 != 0 or N < 16, tiny test models); a
+    // problem refused only for its pointers or strides is an error, not a slow fallback.
+    int require_tc = 0;
 };
 
 // True when the tcgen05 kernel can run the problem (bf16 operands, TMA-legal strides).
 bool gemm_tc_supported(const GemmProblem& p);
+// True when the problem's shape alone (K % 8 == 0, N >= 16) allows the tensor-core kernel.
+bool gemm_tc_shape_ok(const GemmProblem& p);
 // The same for an implicit-convolution problem (p.conv set).
 bool gemm_conv_supported(const GemmProblem& p);
 // tcgen05 / TMEM / TMA tensor-core path (gemm_tc.cu). err: device error word.

@@ -1266,10 +1266,17 @@ void gemm_tc(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
 
 static std::atomic<long long> g_tc_launches{0}, g_simt_launches{0};
 
+bool gemm_tc_shape_ok(const GemmProblem& p) { return p.K % 8 == 0 && p.N >= 16; }
+
 void gemm(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms, bool allow_tc) {
     if (p.M == 0 || p.N == 0) return;
     SANA_REQUIRE(p.conv.H == 0 || (allow_tc && gemm_conv_supported(p)),
                  "implicit convolution needs the tensor-core path and a supported shape");
+    if (p.require_tc && allow_tc && p.a_bf16 && p.b_bf16 && gemm_tc_shape_ok(p) && !gemm_tc_supported(p))
+        throw std::logic_error("gemm: a bf16 projection of shape M=" + std::to_string(p.M) + " N=" +
+                               std::to_string(p.N) + " K=" + std::to_string(p.K) +
+                               " has operands the tensor-core kernel cannot load (pointer or row stride "
+                               "not 16-byte aligned); refusing the CUDA-core fallback");
     if (allow_tc && gemm_tc_supported(p)) {
         gemm_tc(p, err, stream, num_sms);
         ++g_tc_launches;

@@ -851,6 +851,7 @@ void VaeDecoder::gemm_rows(const T* A, long long M, int K, const DevBuf& w, cons
     p.ep.out = out;
     p.ep.out_bf16 = sizeof(T) == 2 ? 1 : 0;
     p.ep.ldo = N;
+    p.require_tc = 1;
     gemm(p, eng_.err(), eng_.stream(), eng_.num_sms());
     ++launches_;
 }

@@ -38,14 +38,20 @@ int sigma_count(const SanaSchedulerState& s) { return as_int(s.schedule.sigmas.s
 }  // namespace
 
 namespace sana_shim {
-void check_scheduler_config(const SanaSchedulerConfig& c) {
+sana_scheduler_config c_config(const SanaSchedulerConfig& c) {
     validate_config(c);
-    if (c.solver_type != "midpoint")
-        throw std::invalid_argument("the CUDA scheduler update implements solver_type midpoint only");
-    if (!c.use_flow_sigmas) throw std::invalid_argument("the CUDA scheduler update implements flow sigmas only");
-    if (c.solver_order != 2 || !c.lower_order_final || c.final_sigmas_type != "zero")
-        throw std::invalid_argument(
-            "the CUDA scheduler step implements solver_order 2 with lower_order_final and zero final sigma");
+    sana_scheduler_config r;
+    sana_scheduler_config_default(&r);
+    if (c.num_train_timesteps > static_cast<size_t>(2147483647))
+        throw std::invalid_argument("num_train_timesteps does not fit the C ABI's int");
+    r.num_train_timesteps = static_cast<int>(c.num_train_timesteps);
+    r.flow_shift = c.flow_shift;
+    r.use_flow_sigmas = c.use_flow_sigmas ? 1 : 0;
+    r.solver_order = static_cast<int>(c.solver_order);
+    r.lower_order_final = c.lower_order_final ? 1 : 0;
+    r.final_sigmas_zero = c.final_sigmas_type == "zero" ? 1 : 0;
+    r.solver_heun = c.solver_type == "heun" ? 1 : 0;
+    return r;
 }
 }  // namespace sana_shim
 
@@ -58,13 +64,12 @@ SanaSchedulerTimesteps build_sana_scheduler_timesteps(size_t num_inference_steps
     if (config.timestep_spacing != "linspace") throw std::invalid_argument("only linspace timestep_spacing is supported");
     if (config.final_sigmas_type != "zero") throw std::invalid_argument("only zero final_sigmas_type is supported");
     if (config.num_train_timesteps == 0) throw std::invalid_argument("num_train_timesteps must be positive");
-    if (config.num_train_timesteps != 1000)
-        throw std::invalid_argument("the CUDA host layer builds schedules for num_train_timesteps = 1000 only");
+    const sana_scheduler_config cc = sana_shim::c_config(config);
     SanaSchedulerTimesteps s;
     s.timesteps.resize(num_inference_steps);
     s.sigmas.resize(num_inference_steps + 1);
-    check(sana_scheduler_schedule(as_int(num_inference_steps, "num_inference_steps"), config.flow_shift,
-                                  s.timesteps.data(), s.sigmas.data()));
+    check(sana_scheduler_schedule_config(&cc, as_int(num_inference_steps, "num_inference_steps"), s.timesteps.data(),
+                                         s.sigmas.data()));
     return s;
 }
 
@@ -95,12 +100,12 @@ Tensor sana_scheduler_first_order_update(const Tensor& converted_model_output, c
     validate_config(config);
     validate_state(state);
     require(converted_model_output.same_shape(sample), "converted_model_output and sample must have the same shape");
-    if (!config.use_flow_sigmas) throw std::invalid_argument("the CUDA scheduler update implements flow sigmas only");
+    const sana_scheduler_config cc = sana_shim::c_config(config);
     Tensor out(sample.shape());
     if (out.numel() == 0) return out;
-    check(sana_scheduler_update(handle(), 1, state.schedule.sigmas.data(), sigma_count(state),
-                                as_int(state.step_index, "step index"), ptr(converted_model_output), nullptr,
-                                ptr(sample), as_int(sample.numel(), "numel"), out.data().data()));
+    check(sana_scheduler_update_config(handle(), &cc, 1, state.schedule.sigmas.data(), sigma_count(state),
+                                       as_int(state.step_index, "step index"), ptr(converted_model_output), nullptr,
+                                       ptr(sample), as_int(sample.numel(), "numel"), out.data().data()));
     return out;
 }
 
@@ -115,14 +120,12 @@ Tensor sana_scheduler_second_order_update(const Tensor& sample, const SanaSchedu
     const Tensor& m0 = state.previous_model_outputs.back();
     const Tensor& m1 = state.previous_model_outputs[state.previous_model_outputs.size() - 2];
     require(m0.same_shape(sample) && m1.same_shape(sample), "stored model outputs must match sample shape");
-    if (config.solver_type != "midpoint")
-        throw std::invalid_argument("the CUDA scheduler update implements solver_type midpoint only");
-    if (!config.use_flow_sigmas) throw std::invalid_argument("the CUDA scheduler update implements flow sigmas only");
+    const sana_scheduler_config cc = sana_shim::c_config(config);
     Tensor out(sample.shape());
     if (out.numel() == 0) return out;
-    check(sana_scheduler_update(handle(), 2, state.schedule.sigmas.data(), sigma_count(state),
-                                as_int(state.step_index, "step index"), ptr(m0), ptr(m1), ptr(sample),
-                                as_int(sample.numel(), "numel"), out.data().data()));
+    check(sana_scheduler_update_config(handle(), &cc, 2, state.schedule.sigmas.data(), sigma_count(state),
+                                       as_int(state.step_index, "step index"), ptr(m0), ptr(m1), ptr(sample),
+                                       as_int(sample.numel(), "numel"), out.data().data()));
     return out;
 }
 
@@ -131,11 +134,11 @@ Tensor step_sana_scheduler(const Tensor& model_output, const Tensor& sample, San
     validate_config(config);
     validate_state(state);
     require(model_output.same_shape(sample), "model_output and sample must have the same shape");
-    sana_shim::check_scheduler_config(config);
+    const sana_scheduler_config cc = sana_shim::c_config(config);
     const size_t numel = sample.numel();
     for (const Tensor& h : state.previous_model_outputs)
         require(h.same_shape(sample), "stored model outputs must match sample shape");
-    // the device step keeps the last solver_order (= 2) converted outputs, oldest first
+    // the device step takes at most the last two converted outputs, oldest first
     std::vector<float> history(2 * numel);
     const size_t keep = state.previous_model_outputs.size() > 2 ? 2 : state.previous_model_outputs.size();
     const size_t first = state.previous_model_outputs.size() - keep;
@@ -146,9 +149,9 @@ Tensor step_sana_scheduler(const Tensor& model_output, const Tensor& sample, San
     int step = as_int(state.step_index, "step index");
     int lower = as_int(state.lower_order_step_count, "lower order count");
     Tensor out(sample.shape());
-    check(sana_scheduler_step(handle(), state.schedule.sigmas.data(), sigma_count(state), &step, &lower,
-                              history.data(), &n_history, ptr(model_output), ptr(sample), as_int(numel, "numel"),
-                              out.data().data()));
+    check(sana_scheduler_step_config(handle(), &cc, state.schedule.sigmas.data(), sigma_count(state), &step, &lower,
+                                     history.data(), &n_history, ptr(model_output), ptr(sample),
+                                     as_int(numel, "numel"), out.data().data()));
     state.step_index = static_cast<size_t>(step);
     state.lower_order_step_count = static_cast<size_t>(lower);
     state.previous_model_outputs.clear();

@@ -33,8 +33,8 @@ void require(bool ok, const char* message);
 void ensure_weights(const SanaDenoiserWeights& w);
 void ensure_block(const SanaBlockWeights& b);
 
-// validate_scheduler_config (scheduler.cpp:8-24) plus the limits of the device update
-// (DPM-Solver++ midpoint on flow sigmas); std::invalid_argument otherwise.
-void check_scheduler_config(const SanaSchedulerConfig& c);
+// The config as the C ABI's struct, after validate_scheduler_config's checks
+// (scheduler.cpp:8-24; std::invalid_argument otherwise).
+sana_scheduler_config c_config(const SanaSchedulerConfig& c);
 
 }  // namespace sana_shim

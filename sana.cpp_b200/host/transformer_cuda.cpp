@@ -27,11 +27,12 @@ Tensor slab(const std::vector<float>& all, size_t B, size_t C, size_t k) {
     return t;
 }
 
-bool default_schedule(const SanaSchedulerState& s, const SanaSchedulerConfig& c) {
+// True when the state's schedule is the one build_sana_scheduler_timesteps gives `c`.
+bool built_schedule(const SanaSchedulerState& s, const sana_scheduler_config& c) {
     const size_t n = s.schedule.timesteps.size();
-    if (n == 0 || s.schedule.sigmas.size() != n + 1 || c.num_train_timesteps != 1000) return false;
+    if (n == 0 || n > 1024 || s.schedule.sigmas.size() != n + 1) return false;
     std::vector<float> ts(n), sg(n + 1);
-    if (sana_scheduler_schedule(static_cast<int>(n), c.flow_shift, ts.data(), sg.data()) != SANA_OK) return false;
+    if (sana_scheduler_schedule_config(&c, static_cast<int>(n), ts.data(), sg.data()) != SANA_OK) return false;
     return ts == s.schedule.timesteps && sg == s.schedule.sigmas;
 }
 
@@ -121,7 +122,7 @@ Tensor run_full_denoising_step_with_cfg(const Tensor& latents, const Tensor& con
                 "encoder_attention_bias batch size must equal 2 * latent batch size for CFG");
     require(scheduler_state.schedule.sigmas.size() == scheduler_state.schedule.timesteps.size() + 1,
             "scheduler sigmas must have one extra final entry");
-    sana_shim::check_scheduler_config(scheduler_config);
+    const sana_scheduler_config cc = sana_shim::c_config(scheduler_config);
     sana_shim::ensure_weights(denoiser_weights);
     const size_t B = latents.dim_size(0), numel = latents.numel();
     for (const Tensor& h : scheduler_state.previous_model_outputs)
@@ -135,13 +136,12 @@ Tensor run_full_denoising_step_with_cfg(const Tensor& latents, const Tensor& con
     Tensor out = latents;
     int step = as_int(scheduler_state.step_index, "step index");
     int lower = as_int(scheduler_state.lower_order_step_count, "lower order count");
-    check(sana_cuda_denoise_step(handle(), out.data().data(), as_int(B, "batch"), as_int(latents.dim_size(2), "height"),
-                                 as_int(latents.dim_size(3), "width"), ptr(context),
-                                 as_int(context.dim_size(1), "context tokens"), opt(encoder_attention_bias),
-                                 guidance_scale, scheduler_state.schedule.timesteps[scheduler_state.step_index],
-                                 scheduler_state.schedule.sigmas.data(),
-                                 as_int(scheduler_state.schedule.sigmas.size(), "sigmas"), &step, &lower,
-                                 history.data(), &n_history));
+    check(sana_cuda_denoise_step_config(
+        handle(), &cc, out.data().data(), as_int(B, "batch"), as_int(latents.dim_size(2), "height"),
+        as_int(latents.dim_size(3), "width"), ptr(context), as_int(context.dim_size(1), "context tokens"),
+        opt(encoder_attention_bias), guidance_scale, scheduler_state.schedule.timesteps[scheduler_state.step_index],
+        scheduler_state.schedule.sigmas.data(), as_int(scheduler_state.schedule.sigmas.size(), "sigmas"), &step,
+        &lower, history.data(), &n_history));
     scheduler_state.step_index = static_cast<size_t>(step);
     scheduler_state.lower_order_step_count = static_cast<size_t>(lower);
     scheduler_state.previous_model_outputs.clear();
@@ -165,21 +165,22 @@ Tensor run_full_denoising_loop_with_cfg(const Tensor& initial_latents, const Ten
     if (encoder_attention_bias)
         require(encoder_attention_bias->dim_size(0) == initial_latents.dim_size(0) * 2,
                 "encoder_attention_bias batch size must equal 2 * latent batch size for CFG");
-    sana_shim::check_scheduler_config(scheduler_config);
+    const sana_scheduler_config cc = sana_shim::c_config(scheduler_config);
     sana_shim::ensure_weights(denoiser_weights);
     const size_t n = scheduler_state.schedule.timesteps.size();
     const size_t L = encoder_hidden_states.dim_size(1), Din = encoder_hidden_states.dim_size(2);
     if (scheduler_state.step_index == 0 && scheduler_state.previous_model_outputs.empty() &&
-        scheduler_state.lower_order_step_count == 0 && default_schedule(scheduler_state, scheduler_config)) {
-        // A fresh state on the default schedule: the whole loop runs on the device (one CUDA
-        // graph from the second call with the same shapes).
+        scheduler_state.lower_order_step_count == 0 && built_schedule(scheduler_state, cc)) {
+        // A fresh state on the config's own schedule: the whole loop runs on the device (one
+        // CUDA graph from the second call with the same shapes).
         Tensor out(initial_latents.shape());
-        check(sana_cuda_denoise_loop(handle(), ptr(initial_latents), as_int(initial_latents.dim_size(0), "batch"),
-                                     as_int(initial_latents.dim_size(2), "height"),
-                                     as_int(initial_latents.dim_size(3), "width"), ptr(encoder_hidden_states),
-                                     as_int(L, "context tokens"), as_int(Din, "caption dim"),
-                                     opt(encoder_attention_bias), guidance_scale, as_int(n, "steps"),
-                                     scheduler_config.flow_shift, out.data().data()));
+        check(sana_cuda_denoise_loop_config(handle(), &cc, ptr(initial_latents),
+                                            as_int(initial_latents.dim_size(0), "batch"),
+                                            as_int(initial_latents.dim_size(2), "height"),
+                                            as_int(initial_latents.dim_size(3), "width"), ptr(encoder_hidden_states),
+                                            as_int(L, "context tokens"), as_int(Din, "caption dim"),
+                                            opt(encoder_attention_bias), guidance_scale, as_int(n, "steps"),
+                                            out.data().data()));
         scheduler_state.step_index = n;
         scheduler_state.lower_order_step_count = std::min(n, scheduler_config.solver_order);
         return out;

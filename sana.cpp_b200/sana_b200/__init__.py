@@ -15,6 +15,8 @@ from .capi import (  # noqa: F401
     load_library,
     prompt_pair_assemble,
     randn_torch_cpu,
+    scheduler_config,
     scheduler_schedule,
+    scheduler_schedule_config,
     select_rows_first_and_last,
 )

@@ -183,6 +183,34 @@ def scheduler_schedule(n: int, flow_shift: float = 3.0):
     return ts, sg
 
 
+class sana_scheduler_config(ctypes.Structure):
+    """SanaSchedulerConfig (scheduler.h:9-20) as the C ABI carries it."""
+    _fields_ = [("num_train_timesteps", _i), ("flow_shift", _f), ("use_flow_sigmas", _i), ("solver_order", _i),
+                ("lower_order_final", _i), ("final_sigmas_zero", _i), ("solver_heun", _i)]
+
+
+SCHEDULER_DEFAULTS = dict(num_train_timesteps=1000, flow_shift=3.0, use_flow_sigmas=1, solver_order=2,
+                          lower_order_final=1, final_sigmas_zero=1, solver_heun=0)
+
+
+def scheduler_config(**kw) -> sana_scheduler_config:
+    """A config with the reference's defaults (make_sana_scheduler_config) except `kw`."""
+    bad = set(kw) - set(SCHEDULER_DEFAULTS)
+    if bad:
+        raise TypeError(f"unknown scheduler config fields {sorted(bad)}")
+    return sana_scheduler_config(**{**SCHEDULER_DEFAULTS, **kw})
+
+
+def scheduler_schedule_config(n: int, **kw):
+    ts = np.empty(max(n, 0), np.float32)
+    sg = np.empty(max(n, 0) + 1, np.float32)
+    c = scheduler_config(**kw)
+    rc = load_library().sana_scheduler_schedule_config(ctypes.byref(c), _i(n), _ptr(ts), _ptr(sg))
+    if rc != 0:
+        raise ValueError("build_sana_scheduler_timesteps rejects this config")
+    return ts, sg
+
+
 def block_tensor_table(block19: Sequence[np.ndarray]) -> List[Optional[np.ndarray]]:
     """Maps the 19 checkpoint tensors of a block (sana_b200.synthetic.BLOCK_TENSORS order)
     to the 26 SanaBlockWeights fields, with the loader's defaults (NULL = zero bias /
@@ -554,6 +582,58 @@ class SanaCuda:
         self._call("sana_scheduler_step", _ptr(sg), _i(sg.size), ctypes.byref(si), ctypes.byref(lo), _ptr(h),
                    ctypes.byref(nh), _ptr(mo), _ptr(x), _i(n), _ptr(out))
         return out, [h[i].copy() for i in range(nh.value)], lo.value
+
+    def scheduler_step_config(self, config: dict, sigmas, step_index, lower, hist, model_output, sample):
+        """step_sana_scheduler with a config (dict of sana_scheduler_config fields):
+        returns (new_sample, new_history [oldest first], new_lower_count, new_step_index)."""
+        c = scheduler_config(**config)
+        sg, mo, x = _f32(sigmas), _f32(model_output).reshape(-1), _f32(sample).reshape(-1)
+        n = x.size
+        h = np.zeros((2, n), np.float32)
+        for i, a in enumerate(hist):
+            h[i] = np.asarray(a, np.float32).reshape(-1)
+        si, lo, nh = _i(step_index), _i(lower), _i(len(hist))
+        out = np.empty_like(x)
+        self._call("sana_scheduler_step_config", ctypes.byref(c), _ptr(sg), _i(sg.size), ctypes.byref(si),
+                   ctypes.byref(lo), _ptr(h), ctypes.byref(nh), _ptr(mo), _ptr(x), _i(n), _ptr(out))
+        return out, [h[i].copy() for i in range(nh.value)], lo.value, si.value
+
+    def scheduler_update_config(self, config: dict, order, sigmas, step_index, m0, m1, sample):
+        c = scheduler_config(**config)
+        sg, x = _f32(sigmas), _f32(sample).reshape(-1)
+        m0 = _f32(m0).reshape(-1)
+        m1 = _f32(m1).reshape(-1) if m1 is not None else None
+        out = np.empty_like(x)
+        self._call("sana_scheduler_update_config", ctypes.byref(c), _i(order), _ptr(sg), _i(sg.size), _i(step_index),
+                   _ptr(m0), _ptr(m1), _ptr(x), _i(x.size), _ptr(out))
+        return out
+
+    def denoise_loop_config(self, config: dict, latents, enc, bias, guidance: float = 4.5, num_steps: int = 20):
+        c = scheduler_config(**config)
+        lat, enc, bias = _f32(latents), _f32(enc), _f32(bias)
+        B, Cl, H, W = lat.shape
+        L, Din = enc.shape[1], enc.shape[2]
+        out = np.empty_like(lat)
+        self._call("sana_cuda_denoise_loop_config", ctypes.byref(c), _ptr(lat), _i(B), _i(H), _i(W), _ptr(enc),
+                   _i(L), _i(Din), _ptr(bias), _f(guidance), _i(num_steps), _ptr(out))
+        return out
+
+    def denoise_step_config(self, config: dict, latents, context, bias, guidance, timestep, sigmas, step_index,
+                            lower, history):
+        """Returns (latents, step_index, lower, history list)."""
+        c = scheduler_config(**config)
+        lat = _f32(latents).copy()
+        ctx, bias, sg = _f32(context), _f32(bias), _f32(sigmas)
+        B, Cl, H, W = lat.shape
+        n = lat.size
+        hist = np.zeros((2, n), np.float32)
+        for i, h in enumerate(history):
+            hist[i] = np.asarray(h, np.float32).reshape(-1)
+        si, lo, nh = _i(step_index), _i(lower), _i(len(history))
+        self._call("sana_cuda_denoise_step_config", ctypes.byref(c), _ptr(lat), _i(B), _i(H), _i(W), _ptr(ctx),
+                   _i(ctx.shape[1]), _ptr(bias), _f(guidance), _f(timestep), _ptr(sg), _i(sg.size), ctypes.byref(si),
+                   ctypes.byref(lo), _ptr(hist), ctypes.byref(nh))
+        return lat, si.value, lo.value, [hist[i].copy() for i in range(nh.value)]
 
     # -- model handle compatible with the checkers' model() ------------------------------
     def model(self, tensors, n_blocks, C, Cl, Din, E, self_heads, cross_heads):

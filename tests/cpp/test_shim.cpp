@@ -206,6 +206,77 @@ void kat_scheduler() {
            "step_sana_scheduler second step state");
 }
 
+// Scheduler configurations other than the default (scheduler.cpp:71-81,207-318): heun and
+// midpoint second order, solver_order 1, lower_order_final off, variance-preserving sigmas,
+// other num_train_timesteps. Expected values: the reference build's step_sana_scheduler on
+// the same inputs (tests/golden/make_golden.py scheduler -> scheduler_configs.inc).
+#include "scheduler_configs.inc"
+
+SanaSchedulerConfig sched_case_config(int i) {
+    const int* c = kSchedCfg + 9 * i;
+    SanaSchedulerConfig cfg = make_sana_scheduler_config();
+    cfg.num_train_timesteps = static_cast<size_t>(c[0]);
+    cfg.flow_shift = static_cast<float>(c[1]) / 1000.0f;
+    cfg.use_flow_sigmas = c[2] != 0;
+    cfg.solver_order = static_cast<size_t>(c[3]);
+    cfg.lower_order_final = c[4] != 0;
+    cfg.final_sigmas_type = c[5] ? "zero" : "sigma_min";
+    cfg.solver_type = c[6] ? "heun" : "midpoint";
+    return cfg;
+}
+
+// Host only: the schedules build_sana_scheduler_timesteps makes for every buildable case.
+void scheduler_config_schedules() {
+    for (int i = 0; i < kSchedCases; ++i) {
+        const int* c = kSchedCfg + 9 * i;
+        if (c[8]) continue;
+        const size_t n = static_cast<size_t>(c[7]);
+        const SanaSchedulerTimesteps s = build_sana_scheduler_timesteps(n, sched_case_config(i));
+        const float* want = kSchedSchedule + kSchedSgOff[i];
+        bool same = s.timesteps.size() == n && s.sigmas.size() == n + 1;
+        for (size_t j = 0; same && j < n; ++j) same = s.timesteps[j] == want[j];
+        for (size_t j = 0; same && j <= n; ++j) same = s.sigmas[j] == want[n + j];
+        expect(same, "build_sana_scheduler_timesteps config case " + std::to_string(i));
+    }
+    SanaSchedulerConfig vp = make_sana_scheduler_config();
+    vp.use_flow_sigmas = false;
+    throws<std::invalid_argument>([&] { build_sana_scheduler_timesteps(4, vp); }, "schedule without flow sigmas");
+    SanaSchedulerConfig zero_train = make_sana_scheduler_config();
+    zero_train.num_train_timesteps = 0;
+    throws<std::invalid_argument>([&] { build_sana_scheduler_timesteps(4, zero_train); }, "num_train_timesteps 0");
+}
+
+// On the device: every case stepped through step_sana_scheduler, each step's sample within
+// 1e-6 of the reference's (relative to the sample's largest magnitude).
+void scheduler_config_steps() {
+    for (int i = 0; i < kSchedCases; ++i) {
+        const int* c = kSchedCfg + 9 * i;
+        const size_t n = static_cast<size_t>(c[7]), numel = static_cast<size_t>(kSchedNumel);
+        const SanaSchedulerConfig cfg = sched_case_config(i);
+        SanaSchedulerState st;
+        st.schedule.timesteps.assign(kSchedSchedule + kSchedSgOff[i], kSchedSchedule + kSchedSgOff[i] + n);
+        st.schedule.sigmas.assign(kSchedSchedule + kSchedSgOff[i] + n, kSchedSchedule + kSchedSgOff[i] + 2 * n + 1);
+        Tensor x = T({numel}, std::vector<float>(kSchedSample0 + i * numel, kSchedSample0 + (i + 1) * numel));
+        const float* mo = kSchedModelOut + kSchedMoOff[i];
+        const float* want_all = kSchedSamples + kSchedMoOff[i];
+        double worst = 0.0;
+        for (size_t s = 0; s < n; ++s) {
+            x = step_sana_scheduler(T({numel}, std::vector<float>(mo + s * numel, mo + (s + 1) * numel)), x, st, cfg);
+            double scale = 1e-30, diff = 0.0;
+            for (size_t j = 0; j < numel; ++j) {
+                scale = std::max(scale, static_cast<double>(std::fabs(want_all[s * numel + j])));
+                diff = std::max(diff, static_cast<double>(std::fabs(x.data()[j] - want_all[s * numel + j])));
+            }
+            worst = std::max(worst, diff / scale);
+        }
+        const bool ok = worst <= 1e-6 && st.step_index == n &&
+                        st.previous_model_outputs.size() == std::min<size_t>(n, cfg.solver_order) &&
+                        st.lower_order_step_count == std::min<size_t>(n, cfg.solver_order);
+        if (!ok) std::printf("  scheduler config case %d: worst relative diff %g\n", i, worst);
+        expect(ok, "step_sana_scheduler config case " + std::to_string(i));
+    }
+}
+
 void errors() {
     // the reference's std::invalid_argument contracts (test_transformer.cpp:511-619)
     throws<std::invalid_argument>([] { split_heads_3d(Tensor({1, 2, 6}), 4); }, "split_heads_3d bad heads");
@@ -434,12 +505,15 @@ int main(int argc, char** argv) {
                                    "call without a CUDA device");
         // shape errors are found before any device work
         throws<std::invalid_argument>([] { split_heads_3d(Tensor({1, 2, 6}), 4); }, "split_heads_3d bad heads");
+        scheduler_config_schedules();
     } else {
         sana_cuda_shim::configure(0, SANA_MODE_F32);
         kat_tensor_ops();
         kat_transformer_ops();
         kat_block_forward();
         kat_scheduler();
+        scheduler_config_schedules();
+        scheduler_config_steps();
         errors();
         vae_decode_entry_point();
         sana_cuda_shim::configure(0, SANA_MODE_BF16);

@@ -13,6 +13,7 @@ Usage (from the repo root, after ``make -C oracle``):
     python tests/golden/make_golden.py forward    # config 0: one CFG-batch forward (~4 min)
     python tests/golden/make_golden.py loop       # config 1: 20-step loop (~80 min)
     python tests/golden/make_golden.py vae        # VAE decoder: small dims, DC-AE dims at 2x2 (~1 min)
+    python tests/golden/make_golden.py scheduler  # scheduler configurations (+ tests/cpp/scheduler_configs.inc)
 """
 from __future__ import annotations
 
@@ -105,6 +106,87 @@ def small(ref: Reference):
                         samples=ref.scheduler_run(mo, x0, 3.0))
 
 
+# Scheduler configurations beyond the default 2M midpoint (step_sana_scheduler,
+# scheduler.cpp:272-318): (num_train_timesteps, flow_shift, use_flow_sigmas, solver_order,
+# lower_order_final, final_sigmas_zero, solver_heun, steps, explicit schedule). An explicit
+# schedule (the configs the builder refuses: variance-preserving sigmas, a nonzero final
+# sigma) is the flow schedule of the same length with its final sigma set to 0.02.
+SCHEDULER_CASES = [
+    (1000, 3.0, 1, 2, 1, 1, 0, 20, 0),
+    (1000, 3.0, 1, 2, 1, 1, 1, 20, 0),
+    (1000, 3.0, 1, 1, 1, 1, 0, 20, 0),
+    (1000, 3.0, 1, 1, 0, 0, 0, 8, 1),
+    (1000, 3.0, 1, 2, 0, 0, 0, 8, 1),
+    (1000, 3.0, 1, 2, 0, 0, 1, 8, 1),
+    (1000, 3.0, 1, 2, 0, 1, 1, 10, 0),
+    (500, 3.0, 1, 2, 1, 1, 0, 20, 0),
+    (37, 2.5, 1, 2, 1, 1, 1, 7, 0),
+    (1000, 1.0, 1, 2, 1, 1, 0, 5, 0),
+    (1000, 3.0, 0, 2, 1, 1, 0, 12, 1),
+    (1000, 3.0, 0, 2, 0, 0, 1, 12, 1),
+    (1000, 3.0, 0, 1, 1, 1, 0, 12, 1),
+    (1000, 3.0, 1, 2, 1, 1, 0, 1, 0),
+    (1000, 3.0, 1, 2, 1, 1, 1, 2, 0),
+]
+SCHED_KEYS = ("num_train_timesteps", "flow_shift", "use_flow_sigmas", "solver_order", "lower_order_final",
+              "final_sigmas_zero", "solver_heun")
+SCHED_NUMEL = 16
+
+
+def scheduler_configs(ref: Reference):
+    """step_sana_scheduler run over every SCHEDULER_CASES entry on the reference build:
+    tests/golden/scheduler_configs.npz and, for the C++ host-layer test, the same values as
+    C arrays in tests/cpp/scheduler_configs.inc."""
+    rnd = ref.randn
+    out = {"cases": np.array(SCHEDULER_CASES, np.float64)}
+    inc = ["// Generated by tests/golden/make_golden.py scheduler from the reference build", "// (step_sana_scheduler, scheduler.cpp:272-318); do not edit.",
+           f"static const int kSchedCases = {len(SCHEDULER_CASES)};",
+           f"static const int kSchedNumel = {SCHED_NUMEL};"]
+    cfg_rows, offs_mo, offs_out, offs_sg = [], [], [], []
+    all_mo, all_x0, all_out, all_sg = [], [], [], []
+    for i, case in enumerate(SCHEDULER_CASES):
+        cfg = dict(zip(SCHED_KEYS, case[:7]))
+        n = case[7]
+        mo = syn._draw(rnd, max(16, n * SCHED_NUMEL), 600 + 2 * i)[:n * SCHED_NUMEL].reshape(n, SCHED_NUMEL)
+        x0 = syn._draw(rnd, SCHED_NUMEL, 601 + 2 * i)
+        sig = None
+        if case[8]:
+            _, sig, _ = ref.scheduler_run_config({"num_train_timesteps": case[0], "flow_shift": case[1]}, mo, x0)
+            sig = sig.copy()
+            sig[-1] = np.float32(0.02)
+        ts, sg, samples = ref.scheduler_run_config(cfg, mo, x0, sig)
+        out[f"mo_{i}"], out[f"x0_{i}"], out[f"ts_{i}"], out[f"sg_{i}"], out[f"samples_{i}"] = mo, x0, ts, sg, samples
+        cfg_rows.append(case)
+        offs_mo.append(sum(len(a) for a in all_mo))
+        offs_sg.append(sum(len(a) for a in all_sg))
+        all_mo.append(mo.reshape(-1))
+        all_x0.append(x0)
+        all_sg.append(np.concatenate([ts, sg]))
+        all_out.append(samples.reshape(-1))
+    np.savez_compressed(os.path.join(HERE, "scheduler_configs.npz"), **out)
+
+    def lit(v):  # shortest text that reads back as the same float32, as a C float literal
+        t = format(float(v), ".9g")
+        return (t if any(ch in t for ch in ".e") else t + ".0") + "f"
+
+    def arr(name, ctype, vals):
+        body = ", ".join(lit(v) if ctype == "float" else str(int(v)) for v in vals)
+        return f"static const {ctype} {name}[] = {{{body}}};"
+    inc.append("// per case: num_train_timesteps, flow_shift x 1000, use_flow_sigmas, solver_order,")
+    inc.append("// lower_order_final, final_sigmas_zero, solver_heun, steps, explicit schedule")
+    inc.append(arr("kSchedCfg", "int", [int(round(v * 1000)) if j == 1 else v for c in cfg_rows for j, v in enumerate(c)]))
+    inc.append(arr("kSchedMoOff", "int", offs_mo))
+    inc.append(arr("kSchedSgOff", "int", offs_sg))
+    inc.append(arr("kSchedModelOut", "float", np.concatenate(all_mo).view(np.float32)))
+    inc.append(arr("kSchedSample0", "float", np.concatenate(all_x0)))
+    inc.append("// per case: timesteps[steps] then sigmas[steps + 1]")
+    inc.append(arr("kSchedSchedule", "float", np.concatenate(all_sg)))
+    inc.append("// per case: the sample after every step [steps, numel]")
+    inc.append(arr("kSchedSamples", "float", np.concatenate(all_out)))
+    with open(os.path.join(ROOT, "tests", "cpp", "scheduler_configs.inc"), "w") as f:
+        f.write("\n".join(inc) + "\n")
+
+
 def _signature(a: np.ndarray) -> dict:
     """A few hundred KB stand-in for a large activation: its first 4096 values, per-row
     sums and per-row sums of squares (rows = last axis), all in float64."""
@@ -188,4 +270,5 @@ def sv_latents(rnd, B, C, h, w, seed):
 if __name__ == "__main__":
     ref = Reference()
     for what in sys.argv[1:] or ["small"]:
-        {"small": small, "block": block, "forward": forward, "loop": loop, "vae": vae}[what](ref)
+        {"small": small, "block": block, "forward": forward, "loop": loop, "vae": vae,
+         "scheduler": scheduler_configs}[what](ref)

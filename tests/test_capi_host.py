@@ -46,6 +46,27 @@ def test_randn_matches_oracle_and_golden(oracle):
         randn_torch_cpu(15, 0)
 
 
+def test_schedule_configs_match_reference_build():
+    """build_sana_scheduler_timesteps for other configs (num_train_timesteps, flow_shift,
+    solver settings) bit for bit against the reference's schedules, and its refusals."""
+    from sana_b200 import scheduler_schedule_config
+    from test_oracle_pin import scheduler_cases
+    n_checked = 0
+    for cfg, _, _, explicit, want in scheduler_cases():
+        if explicit is not None:
+            continue
+        ts, sg = scheduler_schedule_config(len(want["ts"]), **cfg)
+        assert np.array_equal(ts, want["ts"]) and np.array_equal(sg.view(np.uint32), want["sg"].view(np.uint32)), cfg
+        n_checked += 1
+    assert n_checked >= 8
+    for bad in ({"solver_order": 0}, {"solver_order": 3}, {"use_flow_sigmas": 0}, {"final_sigmas_zero": 0},
+                {"num_train_timesteps": 0}):
+        with pytest.raises(ValueError):
+            scheduler_schedule_config(4, **bad)
+    with pytest.raises(ValueError):
+        scheduler_schedule_config(0)
+
+
 def test_schedule_matches_golden():
     from sana_b200 import scheduler_schedule
     g = np.load(os.path.join(GOLDEN, "scheduler_20.npz"))

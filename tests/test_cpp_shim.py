@@ -32,7 +32,7 @@ def shim_binary(tmp_path_factory):
     out = str(tmp_path_factory.mktemp("shim") / "test_shim")
     cmd = ["g++", "-std=c++17", "-O1", "-Wall", "-Wextra", "-I", os.path.join(ROOT, "include"),
            "-I", os.path.join(PKG, "host", "include"), "-I", os.path.join(PKG, "host"),
-           os.path.join(ROOT, "tests", "cpp", "test_shim.cpp"), os.path.join(PKG, "host", "tensor.cpp"),
+           "-I", os.path.join(ROOT, "tests", "cpp"), os.path.join(ROOT, "tests", "cpp", "test_shim.cpp"), os.path.join(PKG, "host", "tensor.cpp"),
            "-L", LIB, "-lsana_shim", "-lsana_cuda", f"-Wl,-rpath,{LIB}", "-o", out]
     r = subprocess.run(cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr

@@ -343,3 +343,34 @@ def test_gguf_upload_errors_follow_the_loaders(tmp_path):
     rewrite(paths["model"], lambda items: [(n, a[:, :32] if n.endswith("attn1.to_q.weight") else a) for n, a in items])
     with pytest.raises(SanaError, match="has shape"):
         g.upload_gguf(paths["model"], paths["caption"], paths["denoiser"], 2, 2)
+
+
+@pytest.mark.parametrize("cfg", [dict(solver_heun=1), dict(solver_order=1),
+                                 dict(num_train_timesteps=500, flow_shift=2.0, solver_heun=1)])
+def test_loop_with_scheduler_config_equals_stepped_loop(cfg):
+    """run_full_denoising_loop_with_cfg with a non-default SanaSchedulerConfig: the captured
+    device loop (sana_cuda_denoise_loop_config) equals the loop run step by step through
+    run_full_denoising_step_with_cfg (sana_cuda_denoise_step_config), whose scheduler
+    arithmetic the scheduler-config tests hold against the reference. The graph replay of the
+    second call equals the eager first call."""
+    from sana_b200 import SANA_MODE_F32, SanaCuda, randn_torch_cpu, scheduler_schedule_config
+    g = SanaCuda(0, SANA_MODE_F32)
+    tensors = syn.generate_model(MG.SMALL, randn_torch_cpu, base_seed=5, bias_std=0.02)
+    g.upload_checkpoint(MG.SMALL.as_args(), tensors)
+    d = MG.SMALL
+    enc = syn.encoder_states(randn_torch_cpu, 2, 12, d.caption_dim, 3)
+    bias = syn.attention_bias([5, 12], 12)
+    lat = syn.latents(randn_torch_cpu, 1, d.latent_channels, 4, 4, 4)
+    n = 5
+    loop = g.denoise_loop_config(cfg, lat, enc, bias, 4.5, n)
+    assert np.array_equal(g.denoise_loop_config(cfg, lat, enc, bias, 4.5, n), loop)  # graph replay
+    ts, sg = scheduler_schedule_config(n, **cfg)
+    ctx = g.project_caption_model(enc)
+    x, step, lower, hist = lat, 0, 0, []
+    for _ in range(n):
+        x, step, lower, hist = g.denoise_step_config(cfg, x, ctx, bias, 4.5, float(ts[step]), sg, step, lower, hist)
+    order = cfg.get("solver_order", 2)
+    assert step == n and lower == min(n, order) and len(hist) == min(n, order)
+    assert rel_err(x, loop) < 1e-6
+    # the default config differs from these (the configs change the trajectory)
+    assert rel_err(g.denoise_loop(lat, enc, bias, 4.5, n), loop) > 1e-5

@@ -383,6 +383,27 @@ def test_scheduler_trajectory_matches_golden(gpu_f32, oracle):
         assert rel_err(x, g["samples"][s]) < 1e-6, s
 
 
+def test_scheduler_configs_match_reference(gpu_f32):
+    """step_sana_scheduler for every configuration the reference accepts (heun / midpoint,
+    solver_order 1, lower_order_final off, variance-preserving sigmas, other
+    num_train_timesteps), through the device update, against the reference's trajectories."""
+    from test_oracle_pin import scheduler_cases
+    for cfg, mo, x0, _, want in scheduler_cases():
+        sg = want["sg"]
+        x, hist, lower, step = x0, [], 0, 0
+        for s in range(len(mo)):
+            x, hist, lower, step = gpu_f32.scheduler_step_config(cfg, sg, step, lower, hist, mo[s], x)
+            assert rel_err(x, want["samples"][s]) < 1e-6, (cfg, s)
+        n = len(mo)
+        assert step == n and lower == min(n, cfg["solver_order"]) and len(hist) == min(n, cfg["solver_order"])
+    heun = dict(solver_heun=1)
+    with pytest.raises(ValueError):
+        gpu_f32.scheduler_step_config(dict(solver_order=3), want["sg"], 0, 0, [], mo[0], x0)
+    # second order at step 0 is refused as the reference refuses it
+    with pytest.raises(ValueError):
+        gpu_f32.scheduler_update_config(heun, 2, want["sg"], 0, mo[0], mo[0], x0)
+
+
 @pytest.mark.parametrize("D,Tq,L,lens", [(72, 1024, 300, (8, 24)), (72, 100, 300, (300, 1)), (32, 77, 70, (70, 65)),
                                         (64, 130, 129, (64, 129)), (128, 40, 20, (20, 3))])
 def test_cross_attention_tensor_core_shapes(gpu_bf16, oracle, D, Tq, L, lens):

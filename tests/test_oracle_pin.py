@@ -82,6 +82,56 @@ def test_scheduler_matches_golden(oracle):
     assert rel_err(oracle.scheduler_run(mo, x0, 3.0), g["samples"]) < 1e-6
 
 
+SCHED_KEYS = ("num_train_timesteps", "flow_shift", "use_flow_sigmas", "solver_order", "lower_order_final",
+              "final_sigmas_zero", "solver_heun")
+
+
+def scheduler_cases():
+    """(config dict, model outputs, sample, explicit sigmas or None, golden) per case of
+    tests/golden/scheduler_configs.npz (made by the reference build)."""
+    g = np.load(os.path.join(GOLDEN, "scheduler_configs.npz"))
+    out = []
+    for i, row in enumerate(g["cases"]):
+        cfg = {k: (float(v) if k == "flow_shift" else int(v)) for k, v in zip(SCHED_KEYS, row[:7])}
+        explicit = g[f"sg_{i}"] if row[8] else None
+        out.append((cfg, g[f"mo_{i}"], g[f"x0_{i}"], explicit,
+                    {"ts": g[f"ts_{i}"], "sg": g[f"sg_{i}"], "samples": g[f"samples_{i}"]}))
+    return out
+
+
+def test_scheduler_configs_match_golden(oracle):
+    """Every scheduler configuration the reference accepts (heun / midpoint, solver_order 1,
+    lower_order_final off, variance-preserving sigmas, other num_train_timesteps): the
+    oracle's restatement against the reference's own trajectories."""
+    cases = scheduler_cases()
+    assert len(cases) >= 10
+    for cfg, mo, x0, explicit, want in cases:
+        ts, sg, samples = oracle.scheduler_run_config(cfg, mo, x0, explicit)
+        assert np.array_equal(ts, want["ts"]) and np.array_equal(sg.view(np.uint32), want["sg"].view(np.uint32)), cfg
+        for s in range(len(samples)):
+            assert rel_err(samples[s], want["samples"][s]) < 1e-6, (cfg, s)
+
+
+def test_scheduler_config_rejections(oracle):
+    mo, x = np.ones((3, 4), np.float32), np.ones(4, np.float32)
+    for bad in ({"solver_order": 0}, {"solver_order": 3}, {"use_flow_sigmas": 0}, {"final_sigmas_zero": 0},
+                {"num_train_timesteps": 0}):
+        with pytest.raises(ValueError):
+            oracle.scheduler_run_config(bad, mo, x)
+
+
+def test_scheduler_configs_oracle_agrees_with_reference(oracle, reference):
+    rng = np.random.default_rng(5)
+    for cfg, _, _, explicit, _ in scheduler_cases():
+        n = len(explicit) - 1 if explicit is not None else 6
+        mo = rng.standard_normal((n, 33)).astype(np.float32)
+        x = rng.standard_normal(33).astype(np.float32)
+        a = oracle.scheduler_run_config(cfg, mo, x, explicit)
+        b = reference.scheduler_run_config(cfg, mo, x, explicit)
+        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+        assert rel_err(a[2], b[2]) < 1e-6, cfg
+
+
 def test_scheduler_step_state_machine(oracle):
     """The explicit-state step reproduces the whole-run trajectory: first order at step 0
     and at the last step, second order between, a history of two."""
