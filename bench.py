@@ -313,20 +313,32 @@ def run_microbench(args):
     N=5760 with bias and SiLU, linear attention 36 x 32 and depthwise+GLU on 32 x 32 images.
     L2 is flushed (256 MiB write, untimed) before every timed launch; the median of --steps
     launches is reported. One JSON line per op."""
-    import ctypes
     import torch
     from sana_b200 import SANA_MODE_BF16, SanaCuda
-    pk, pk_kind = peaks()
     ops = MICRO_OPS if not args.op else tuple(args.op.split(","))
     bad = [o for o in ops if o not in MICRO_OPS]
     if bad:
         raise SystemExit(f"unknown --op {bad}; choose from {MICRO_OPS}")
     torch.cuda.set_device(0)
     g = SanaCuda(0, SANA_MODE_BF16)
-    g.lib.sana_op_linear_attention_workspace.restype = ctypes.c_size_t
     st = torch.cuda.Stream()
     g.set_stream(st.cuda_stream)
+    for line in microbench_lines(g, st, ops, args.steps, args.warmup, args.no_cpu_baseline):
+        print(json.dumps(line), flush=True)
+    g.close()
+
+
+CONFIG4_OPS = ("linear_attention_16x72", "linear_attention_36x32", "depthwise_glu", "qkv_gemm", "cross_attention")
+
+
+def microbench_lines(g, st, ops, steps, warmup, no_cpu_baseline=True):
+    """The microbenchmark of each op in `ops` on handle g (stream st): a list of dicts."""
+    import ctypes
+    import torch
+    pk, pk_kind = peaks()
+    g.lib.sana_op_linear_attention_workspace.restype = ctypes.c_size_t
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    lines = []
     vp, I = ctypes.c_void_p, ctypes.c_int
     S, T, C, E, L = 2, 4096, 1152, 5760, CAPTION_LEN
     gen = torch.Generator(device="cpu").manual_seed(4)
@@ -337,9 +349,9 @@ def run_microbench(args):
     def timed(fn):
         times = []
         with torch.cuda.stream(st):
-            for _ in range(args.warmup):
+            for _ in range(warmup):
                 fn()
-            for _ in range(args.steps):
+            for _ in range(steps):
                 flush.zero_()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(st)
@@ -354,12 +366,10 @@ def run_microbench(args):
             ach, peak, unit = work / ms / 1e6, pk["hbm_gbs"], "GB/s"
         else:
             ach, peak, unit = work / ms / 1e9, pk["bf16_tflops"], "TFLOP/s"
-        print(json.dumps({"microbench": name, "workload": what, "ms": round(ms, 4), "bound": bound,
-                          "algorithmic": work, "achieved": round(ach, 1), "peak": peak, "unit": unit,
-                          "frac": round(ach / peak, 3), "peak_source": f"{pk_kind} (burst: op timed alone)",
-                          "steps": args.steps, "warmup": args.warmup, "l2": "flushed before every launch",
-                          **(extra or {})}),
-              flush=True)
+        lines.append({"microbench": name, "workload": what, "ms": round(ms, 4), "bound": bound,
+                      "algorithmic": work, "achieved": round(ach, 1), "peak": peak, "unit": unit,
+                      "frac": round(ach / peak, 3), "peak_source": f"{pk_kind} (burst: op timed alone)",
+                      "steps": steps, "warmup": warmup, "l2": "flushed before every launch", **(extra or {})})
 
     for name in ops:
         if name == "vae_decode_1024":
@@ -373,7 +383,7 @@ def run_microbench(args):
             ms = timed(lambda: g.vae_decode_device(lat.data_ptr(), 1, 32, 32, img.data_ptr()))
             report(name, "DC-AE f32c32 decode, latents [1,32,32,32] -> image [1,3,1024,1024], bf16 activations "
                          f"({g.vae_last_launches()} launches)", ms, sv.vae_flops(vd, 32, 32), "tensor",
-                   extra=None if args.no_cpu_baseline else {"cpu_baseline": vae_cpu_sample(vd)})
+                   extra=None if no_cpu_baseline else {"cpu_baseline": vae_cpu_sample(vd)})
             continue
         S, T = (32, 1024) if name.endswith("config2") else (2, 4096)
         side = int(round(T ** 0.5))
@@ -453,7 +463,8 @@ def run_microbench(args):
                                        vp(bias.data_ptr()) if bias is not None else None, vp(kvl.data_ptr()), I(S),
                                        I(T), I(L), I(heads), I(D), vp(out.data_ptr())))
             report(name, what, ms, 4.0 * T * C * sum(lens), "tensor")
-    g.close()
+    del flush
+    return lines
 
 
 def run_cuda(args):
@@ -594,6 +605,12 @@ def run_cuda(args):
         breakdown[k] = e
     _, per_shape = gemm_roofline(g, torch, stream, 2 * B * 1024, pk["bf16_tflops"])
 
+    # BASELINE configs[4], the op-level microbenchmark, at one GPU (after the timed region)
+    micro = None
+    if world == 1 and not args.no_microbench:
+        micro = [{k: v for k, v in m.items() if k not in ("steps", "warmup", "l2", "peak_source")}
+                 for m in microbench_lines(g, stream, CONFIG4_OPS, 5, 3)]
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, dt, threads, kind = cpu_sample()
@@ -627,6 +644,9 @@ def run_cuda(args):
                          "isolated_per_shape": per_shape},
             "kernels": breakdown,
             "gemm_dispatch_per_loop": {"tensor_core": tc1 - tc0, "cuda_core": simt1 - simt0},
+            "microbench_config4": None if micro is None else {
+                "ops": micro, "timing": "median of 5 launches after 3 warm-up, L2 flushed before each, "
+                                        "peaks are the burst figures (ops timed alone)"},
             "model_flops": {"per_loop_tflop": flops / 1e12, "achieved_tflops": flops / (ms_per_step / 1e3) / 1e12,
                             "frac_of_sustained_peak": flops / (ms_per_step / 1e3) / 1e12 / pk["bf16_tflops_sustained"],
                             "gemm_share_of_flops": gemm_flops / flops},
@@ -650,6 +670,7 @@ def main():
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--images", type=int, default=16, help="images (x2 CFG sequences) in the batch, over all GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-microbench", action="store_true", help="skip the config-4 op lines of the 1-GPU run")
     ap.add_argument("--microbench", action="store_true",
                     help="op-level microbenchmark (BASELINE configs[4]) instead of the loop; one GPU")
     ap.add_argument("--op", default="", help="with --microbench: comma-separated subset of " + ",".join(MICRO_OPS))

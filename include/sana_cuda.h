@@ -253,6 +253,11 @@ int sana_op_block_modulation(sana_cuda_ctx *ctx, const float *tmod, const float 
  * linear_3d_lastdim / conv2d_1x1 (common_ops.cpp:177, :322). act: 0 none, 1 SiLU, 2 GELU-tanh. */
 int sana_op_gemm_device(sana_cuda_ctx *ctx, const void *A, const void *B, int M, int N, int K, const float *bias,
                         int act, void *out);
+/* The same product with an fp32 output out[M, N] (the projections that write the fp32
+ * residual stream and the noise prediction do), e.g. to read the epilogue's activations at
+ * full precision. */
+int sana_op_gemm_f32out_device(sana_cuda_ctx *ctx, const void *A, const void *B, int M, int N, int K,
+                               const float *bias, int act, float *out);
 /* The residual projection of a block stage (the attention / cross-attention output and the
  * Mix-FFN point projection, transformer.cpp:740-777): out[M, N] (fp32) =
  * resid + gate[row / rows_per_gate] * (A . B^T + bias), gate NULL = 1, bias NULL = 0; out

@@ -1197,6 +1197,24 @@ int sana_op_gemm_device(sana_cuda_ctx* ctx, const void* A, const void* B, int M,
     });
 }
 
+int sana_op_gemm_f32out_device(sana_cuda_ctx* ctx, const void* A, const void* B, int M, int N, int K,
+                               const float* bias, int act, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(A && B && out && M >= 1 && N >= 1 && K >= 1, "invalid gemm arguments");
+        sana::Engine& eng = engine(ctx);
+        sana::GemmProblem p;
+        p.A = A;
+        p.lda = K;
+        p.B = B;
+        p.ldb = K;
+        p.M = M;
+        p.N = N;
+        p.K = K;
+        p.ep = epi(out, false, N, bias, act);
+        sana::gemm(p, eng.err(), eng.stream(), eng.num_sms());
+    });
+}
+
 int sana_op_gemm_residual_device(sana_cuda_ctx* ctx, const void* A, const void* B, int M, int N, int K,
                                  const float* bias, const float* resid, const float* gate, int rows_per_gate,
                                  float* out, void* out_bf16) {

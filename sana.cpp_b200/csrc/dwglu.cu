@@ -361,6 +361,11 @@ void depthwise_glu(const T* in, long long ldi, int S, int H, int W, int E, const
     if (pixels == 0 || half == 0) return;
     bool vec = sizeof(T) == 2 && half % 8 == 0 && ldi % 8 == 0 && ldo % 2 == 0 &&
                (reinterpret_cast<uintptr_t>(in) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 3) == 0;
+    // bf16 channel counts the stream kernel tiles (half % 8 == 0) must take it: a refusal for
+    // pointers or row strides alone is an error, not a slow fallback. The scalar kernel is
+    // the fp32 check mode's path and that of odd channel counts (small test models).
+    SANA_REQUIRE(vec || sizeof(T) != 2 || half % 8 != 0,
+                 "depthwise_glu: bf16 rows must be 16-byte aligned (input) and 4-byte aligned (output)");
     if (vec) {
         static int device_sms[64] = {0};
         static PerDeviceOnce attr;

@@ -242,165 +242,6 @@ void launch_apply_reg(const T* q, long long ldq, int q_off, int Tq, int heads, i
 }
 
 
-// ---------------------------------------------------------------------------------------
-// bf16 fast path (head_dim % 8 == 0, 16-byte aligned rows): 16-byte asynchronous copies
-// and vector register traffic instead of scalar loads.
-// ---------------------------------------------------------------------------------------
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
-__device__ __forceinline__ void bf4(const uint2& u, float (&f)[4]) {
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-    const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
-    f[0] = a.x;
-    f[1] = a.y;
-    f[2] = b.x;
-    f[3] = b.y;
-}
-
-// State: K and V of a 128-token chunk land in shared memory (raw bf16) by cp.async; each
-// thread accumulates 4 x 4 tiles of relu(K)^T V with 8-byte shared loads; token splits are
-// summed in a fixed order.
-__global__ void __launch_bounds__(256) linattn_state_bf16_kernel(const bf16* __restrict__ kv, long long ld, int k_off,
-                                                                 int v_off, int Tk, int heads, int D, int chunks,
-                                                                 float* __restrict__ partial) {
-    extern __shared__ __align__(16) unsigned char smb[];
-    bf16* Ks = reinterpret_cast<bf16*>(smb);               // [kChunk][D]
-    bf16* Vs = Ks + kChunk * D;                             // [kChunk][D]
-    float* red = reinterpret_cast<float*>(Vs + kChunk * D); // [splits][(D+1) * D]
-    const int s = blockIdx.z, h = blockIdx.y, c = blockIdx.x;
-    const int t0 = c * kChunk;
-    const int n = min(Tk - t0, kChunk);
-    const int cpr = D / 8;  // 16-byte chunks per row
-    const uint32_t kb = smem_u32(Ks), vb = smem_u32(Vs);
-    for (int i = threadIdx.x; i < n * cpr * 2; i += blockDim.x) {
-        const int which = i / (n * cpr), j = i % (n * cpr);
-        const int t = j / cpr, ck = j % cpr;
-        const long long row = static_cast<long long>(s) * Tk + t0 + t;
-        const bf16* src = kv + row * ld + (which ? v_off : k_off) + h * D + ck * 8;
-        cp_async16((which ? vb : kb) + static_cast<uint32_t>(t * D + ck * 8) * 2u, src);
-    }
-    cp_async_wait_all();
-    __syncthreads();
-    const int nb = D / 4, nblk = nb * nb;
-    int splits = 1;
-    while (splits * 2 * nblk <= static_cast<int>(blockDim.x) && splits < 8) splits *= 2;
-    const int per = blockDim.x / splits;
-    const int split = threadIdx.x / per;
-    const int ta = (n * split) / splits, tb = (n * (split + 1)) / splits;
-    const int width = (D + 1) * D;
-    for (int blk = threadIdx.x % per; blk < nblk; blk += per) {
-        const int r0 = (blk / nb) * 4, d0 = (blk % nb) * 4;
-        float acc[4][4] = {};
-        float z[4] = {};
-        for (int t = ta; t < tb; ++t) {
-            float vv[4], kk[4];
-            bf4(*reinterpret_cast<const uint2*>(Vs + t * D + r0), vv);
-            bf4(*reinterpret_cast<const uint2*>(Ks + t * D + d0), kk);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) kk[j] = kk[j] > 0.f ? kk[j] : 0.f;
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(vv[i], kk[j], acc[i][j]);
-            if (r0 == 0) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) z[j] += kk[j];
-            }
-        }
-        float* rd = red + split * width;
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) rd[(r0 + i) * D + d0 + j] = acc[i][j];
-        if (r0 == 0) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) rd[D * D + d0 + j] = z[j];
-        }
-    }
-    __syncthreads();
-    float* out = partial + ((static_cast<long long>(s) * heads + h) * chunks + c) * width;
-    for (int e = threadIdx.x; e < width; e += blockDim.x) {
-        float a = 0.f;
-        for (int sp = 0; sp < splits; ++sp) a += red[sp * width + e];
-        out[e] = a;
-    }
-}
-
-// Apply: each thread owns one token; its q row is read with 16-byte loads straight into
-// registers, the (D+1) x D state is read from shared memory as 16-byte broadcasts, and the
-// output row is written with 16-byte stores.
-template <int D>
-__global__ void __launch_bounds__(kTile) linattn_apply_bf16_kernel(const bf16* __restrict__ q, long long ld, int q_off,
-                                                                   int Tq, int heads,
-                                                                   const float* __restrict__ state,
-                                                                   bf16* __restrict__ out, long long ldo) {
-    __shared__ __align__(16) float Ss[(D + 1) * D];
-    const int s = blockIdx.z, h = blockIdx.y;
-    const float* st = state + (static_cast<long long>(s) * heads + h) * (D + 1) * D;
-    for (int e = threadIdx.x * 4; e < (D + 1) * D; e += blockDim.x * 4)
-        *reinterpret_cast<float4*>(Ss + e) = *reinterpret_cast<const float4*>(st + e);
-    const int t = blockIdx.x * kTile + threadIdx.x;
-    float qv[D];
-    if (t < Tq) {
-        const uint4* src = reinterpret_cast<const uint4*>(q + (static_cast<long long>(s) * Tq + t) * ld + q_off + h * D);
-#pragma unroll
-        for (int c = 0; c < D / 8; ++c) {
-            const uint4 u = src[c];
-            float a[4], b[4];
-            bf4(make_uint2(u.x, u.y), a);
-            bf4(make_uint2(u.z, u.w), b);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                qv[c * 8 + j] = a[j] > 0.f ? a[j] : 0.f;
-                qv[c * 8 + 4 + j] = b[j] > 0.f ? b[j] : 0.f;
-            }
-        }
-    }
-    __syncthreads();
-    if (t >= Tq) return;
-    float den = 0.f;
-#pragma unroll
-    for (int d = 0; d < D; d += 4) {
-        const float4 zz = *reinterpret_cast<const float4*>(Ss + D * D + d);
-        den = fmaf(zz.x, qv[d], den);
-        den = fmaf(zz.y, qv[d + 1], den);
-        den = fmaf(zz.z, qv[d + 2], den);
-        den = fmaf(zz.w, qv[d + 3], den);
-    }
-    den += 1e-15f;
-    uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<long long>(s) * Tq + t) * ldo + h * D);
-#pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
-        float o[8];
-#pragma unroll
-        for (int rr = 0; rr < 8; ++rr) {
-            const float* srow = Ss + (c * 8 + rr) * D;
-            float num = 0.f;
-#pragma unroll
-            for (int d = 0; d < D; d += 4) {
-                const float4 w4 = *reinterpret_cast<const float4*>(srow + d);
-                num = fmaf(w4.x, qv[d], num);
-                num = fmaf(w4.y, qv[d + 1], num);
-                num = fmaf(w4.z, qv[d + 2], num);
-                num = fmaf(w4.w, qv[d + 3], num);
-            }
-            o[rr] = num / den;
-        }
-        uint4 pk;
-        __nv_bfloat162 h0 = __floats2bfloat162_rn(o[0], o[1]), h1 = __floats2bfloat162_rn(o[2], o[3]);
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(o[4], o[5]), h3 = __floats2bfloat162_rn(o[6], o[7]);
-        pk.x = *reinterpret_cast<uint32_t*>(&h0);
-        pk.y = *reinterpret_cast<uint32_t*>(&h1);
-        pk.z = *reinterpret_cast<uint32_t*>(&h2);
-        pk.w = *reinterpret_cast<uint32_t*>(&h3);
-        dst[c] = pk;
-    }
-}
-
 template <class T>
 bool linattn_bf16_path(const T*, long long, int, const T*, long long, int, int, int, int, int, int, int, float*, T*,
                        long long, int, int, cudaStream_t) {
@@ -409,34 +250,14 @@ bool linattn_bf16_path(const T*, long long, int, const T*, long long, int, int, 
 template <>
 bool linattn_bf16_path<bf16>(const bf16* q, long long ldq, int q_off, const bf16* kv, long long ldkv, int k_off,
                              int v_off, int S, int Tq, int Tk, int heads, int D, float* partial, bf16* out,
-                             long long ldo, int chunks, int width, cudaStream_t st) {
+                             long long ldo, int, int, cudaStream_t st) {
     if (linattn_mma(q, ldq, q_off, kv, ldkv, k_off, v_off, S, Tq, Tk, heads, D, partial, out, ldo, st)) return true;
-    auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-    if (D % 8 != 0 || (D != 32 && D != 64 && D != 72) || ldq % 8 || ldkv % 8 || ldo % 8 || q_off % 8 || k_off % 8 ||
-        v_off % 8 || !a16(q) || !a16(kv) || !a16(out) || Tk <= 0)
-        return false;
-    const int nblk = (D / 4) * (D / 4);
-    int splits = 1;
-    while (splits * 2 * nblk <= 256 && splits < 8) splits *= 2;
-    const size_t sm = static_cast<size_t>(2) * kChunk * D * 2 + static_cast<size_t>(splits) * width * 4;
-    static PerDeviceOnce attr;
-    if (attr.pending()) {
-        SANA_CUDA(cudaFuncSetAttribute(linattn_state_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       227 * 1024));
-        attr.mark();
-    }
-    linattn_state_bf16_kernel<<<dim3(chunks, heads, S), 256, sm, st>>>(kv, ldkv, k_off, v_off, Tk, heads, D, chunks,
-                                                                       partial);
-    SANA_CUDA(cudaGetLastError());
-    float* state = partial + static_cast<long long>(S) * heads * chunks * width;
-    linattn_reduce_kernel<<<dim3(ceil_div(width, 256), S * heads), 256, 0, st>>>(partial, chunks, width, state);
-    SANA_CUDA(cudaGetLastError());
-    const dim3 grid(ceil_div(Tq, kTile), heads, S);
-    if (D == 32) linattn_apply_bf16_kernel<32><<<grid, kTile, 0, st>>>(q, ldq, q_off, Tq, heads, state, out, ldo);
-    else if (D == 64) linattn_apply_bf16_kernel<64><<<grid, kTile, 0, st>>>(q, ldq, q_off, Tq, heads, state, out, ldo);
-    else linattn_apply_bf16_kernel<72><<<grid, kTile, 0, st>>>(q, ldq, q_off, Tq, heads, state, out, ldo);
-    SANA_CUDA(cudaGetLastError());
-    return true;
+    // The tensor-core kernels take head dims 32, 64 and 72 with 16-byte aligned rows; such a
+    // problem refused only for its pointers or strides is an error, not a slow fallback.
+    // Other head dims (small test models) take the generic kernels below.
+    SANA_REQUIRE(!(D == 32 || D == 64 || D == 72) || Tk <= 0,
+                 "linear attention: bf16 q/k/v/out rows must be 16-byte aligned for the tensor-core kernels");
+    return false;
 }
 
 }  // namespace

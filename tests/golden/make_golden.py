@@ -10,6 +10,7 @@ tests show is bit-identical across the reference, the oracle and the product.
 Usage (from the repo root, after ``make -C oracle``):
     python tests/golden/make_golden.py small      # ops, small model, scheduler (seconds)
     python tests/golden/make_golden.py block      # one full-size block (~10 s)
+    python tests/golden/make_golden.py blocks     # block 0 at 4096 tokens and at mixed masks (~1 min)
     python tests/golden/make_golden.py forward    # config 0: one CFG-batch forward (~4 min)
     python tests/golden/make_golden.py loop       # config 1: 20-step loop (~80 min)
     python tests/golden/make_golden.py vae        # VAE decoder: small dims, DC-AE dims at 2x2 (~1 min)
@@ -226,6 +227,44 @@ def block(ref: Reference):
     np.savez_compressed(os.path.join(HERE, "block0_full.npz"), **out)
 
 
+# Further full-size block_forward cases: config 3's 64 x 64 latent grid (4096 tokens per
+# sequence, its linear-attention token split and depthwise halo) and config 2's mixed caption
+# masks (four sequences with valid lengths drawn from 8..120). (name, sequences, grid side,
+# valid lengths, timestep, input seed)
+BLOCK_CASES = {
+    "block0_4096": (2, 64, (8, 24), 999.0, 402),
+    "block0_mixed": (4, 32, (17, 120, 64, 9), 500.0, 403),
+}
+
+
+def block_case_inputs(m, rnd, name):
+    """(x, ctx, tmod, bias) of a BLOCK_CASES entry for model `m` (one block, FULL dims)."""
+    S, side, lens, t, seed = BLOCK_CASES[name]
+    enc = syn.encoder_states(rnd, S, 300, FULL.caption_dim, 7 + seed)
+    bias = syn.attention_bias(list(lens), 300)
+    ctx = m.project_caption(enc)
+    _, tmod = m.time_embed([t] * S)
+    x = syn._draw(rnd, S * side * side * FULL.hidden, seed).reshape(S, side * side, FULL.hidden)
+    return x, ctx, tmod, bias
+
+
+def blocks_more(ref: Reference):
+    t0 = time.time()
+    d1 = syn.ModelDims(n_blocks=1)
+    m = ref.model(syn.generate_model(d1, ref.randn, base_seed=0), *d1.as_args())
+    for name in BLOCK_CASES:
+        x, ctx, tmod, bias = block_case_inputs(m, ref.randn, name)
+        t1 = time.time()
+        st = m.block_forward(0, x, ctx, tmod, bias)
+        print(f"{name}: block_forward {time.time() - t1:.1f}s", flush=True)
+        out = {}
+        for stage, a in zip(("after_self", "after_cross", "after_ff"), st):
+            for k, v in _signature(a).items():
+                out[f"{stage}_{k}"] = v
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+    print(f"blocks {time.time() - t0:.1f}s", flush=True)
+
+
 def forward(ref: Reference):
     m = full_model(ref)
     lat, enc, bias = full_inputs(ref, 2)
@@ -271,4 +310,4 @@ if __name__ == "__main__":
     ref = Reference()
     for what in sys.argv[1:] or ["small"]:
         {"small": small, "block": block, "forward": forward, "loop": loop, "vae": vae,
-         "scheduler": scheduler_configs}[what](ref)
+         "scheduler": scheduler_configs, "blocks": blocks_more}[what](ref)

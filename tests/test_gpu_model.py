@@ -5,6 +5,9 @@
 * full-size Sana-0.6B block 0 at config-0 shapes ([2, 1024, 1152], 36x32 and 16x72 self
   heads) against the oracle: per-stage relative L2 <= 1e-2 in bf16 mode, <= 1e-4 in the
   fp32 check mode;
+* full-size block 0 at config 3's 4096 tokens ([2, 4096, 1152]) and at config 2's mixed
+  caption masks, against the oracle (same bars), the oracle pinned on the reference's stage
+  outputs;
 * the config-1 20-step image against the reference's golden latents (cosine >= 0.999), and
   properties at config-3 size (4096 tokens).
 """
@@ -142,6 +145,48 @@ def test_full_block_baseline_heads(oracle):
     got = g.block_forward(0, x, ctx, tmod, bias)
     for a, b in zip(got, ref):
         assert rel_err(a, b) < BLOCK_BF16
+
+
+@pytest.fixture(scope="module", params=sorted(MG.BLOCK_CASES))
+def block_case(request, oracle):
+    """Block 0 of the full-size model on a BLOCK_CASES input of make_golden.py: config 3's
+    4096-token grid ([2, 4096, 1152]) or four 1024-token sequences with mixed caption masks
+    (valid lengths 17, 120, 64, 9), with the oracle's stage outputs."""
+    from sana_b200 import randn_torch_cpu
+    d1 = syn.ModelDims(n_blocks=1)
+    tensors = product_model(d1, base_seed=0)
+    m = oracle.model(tensors, *d1.as_args())
+    x, ctx, tmod, bias = MG.block_case_inputs(m, randn_torch_cpu, request.param)
+    return request.param, d1, tensors, x, ctx, tmod, bias, m.block_forward(0, x, ctx, tmod, bias)
+
+
+def test_block_case_oracle_matches_reference_signature(block_case):
+    """The oracle's stage outputs against the reference build's (tests/golden/<case>.npz)."""
+    name, *_, ref = block_case
+    g = np.load(os.path.join(GOLDEN, f"{name}.npz"))
+    for stage, a in zip(("after_self", "after_cross", "after_ff"), ref):
+        sig = MG._signature(a)
+        assert rel_err(sig["head"], g[f"{stage}_head"]) < 1e-5, (name, stage)
+        assert rel_err(sig["row_sum"], g[f"{stage}_row_sum"]) < 1e-4, (name, stage)
+        assert rel_err(sig["row_sq"], g[f"{stage}_row_sq"]) < 1e-5, (name, stage)
+
+
+@pytest.mark.parametrize("mode", ["bf16", "f32"])
+def test_block_case_parity(block_case, mode):
+    """Per-stage parity at config 3's 4096 tokens and at config 2's mixed masks: relative L2
+    <= 1e-2 in bf16 mode and <= 1e-4 in the fp32 check mode, as for the 1024-token block."""
+    from sana_b200 import SANA_MODE_BF16, SANA_MODE_F32, SanaCuda
+    name, d1, tensors, x, ctx, tmod, bias, ref = block_case
+    g = SanaCuda(0, SANA_MODE_BF16 if mode == "bf16" else SANA_MODE_F32)
+    g.upload_checkpoint(d1.as_args(), tensors)
+    got = g.block_forward(0, x, ctx, tmod, bias)
+    tol = BLOCK_BF16 if mode == "bf16" else BLOCK_F32
+    for stage, a, b in zip(("after_self", "after_cross", "after_ff"), got, ref):
+        e = rel_err(a, b)
+        assert e < tol, (name, mode, stage, e)
+    e_branch = rel_err(got[2] - x, ref[2] - x)
+    assert e_branch < (5 * tol if mode == "bf16" else 10 * tol), (name, e_branch)
+    g.close()
 
 
 @pytest.fixture(scope="module")

@@ -115,6 +115,36 @@ def test_gemm_activation_epilogue(gpu_bf16, act):
     assert (err <= bound).all(), float((err / bound).max())
 
 
+def test_silu_epilogue_fp32_accuracy(gpu_bf16):
+    """The tensor-core SiLU epilogue at full precision: pre-activations x in [-80, 80] (bf16
+    values, passed through an exact product), fp32 output against float64 x / (1 + e^-x).
+    Its reciprocal (bit-pattern estimate + two Newton steps, <= 6.7e-6; host-checked in
+    test_numerics_host.py) and the fast exponential (whose argument rounding grows with |x|)
+    keep the relative error below 1.5e-5 over the whole range the epilogue clamps to."""
+    import ctypes
+    import torch
+    M, K, N = 2048, 16, 16
+    x = bf16_round(np.linspace(-80.0, 80.0, M).astype(np.float32))
+    a = np.zeros((M, K), np.float32)
+    a[:, 0] = x
+    w = np.zeros((N, K), np.float32)
+    w[:, 0] = 1.0
+    A = torch.from_numpy(a).to("cuda", torch.bfloat16)
+    B = torch.from_numpy(w).to("cuda", torch.bfloat16)
+    out = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    torch.cuda.synchronize()
+    vp = ctypes.c_void_p
+    gpu_bf16._call("sana_op_gemm_f32out_device", vp(A.data_ptr()), vp(B.data_ptr()), ctypes.c_int(M),
+                   ctypes.c_int(N), ctypes.c_int(K), None, ctypes.c_int(1), vp(out.data_ptr()))
+    gpu_bf16.synchronize()
+    got = out.cpu().numpy().astype(np.float64)
+    xd = x.astype(np.float64)[:, None]
+    ref = xd / (1.0 + np.exp(-xd))
+    rel = np.abs(got - ref) / np.maximum(np.abs(ref), 1e-300)
+    assert np.isfinite(got).all()
+    assert rel.max() <= 1.5e-5, float(rel.max())
+
+
 def _dwglu_f64(x, w, b):
     """Depthwise 3x3 (zero padding) + bias over [S, H, W, E] tokens, split into the value and
     gate halves (common_ops.cpp:484-505 and 745-758), in float64."""
