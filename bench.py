@@ -28,7 +28,6 @@ from __future__ import annotations
 
 import argparse
 import concurrent.futures as cf
-import datetime
 import json
 import os
 import statistics
@@ -473,13 +472,12 @@ def run_cuda(args):
     from sana_b200 import SANA_MODE_BF16, SanaCuda
     from sana_b200 import synthetic as syn
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
+    from sana_b200.watchdog import init_ranks
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+    # a bounded process-group timeout and host heartbeats: a rank that never joins or stops
+    # ends the others with an error instead of a wait for good
+    rank, world, watch = init_ranks("nccl", timeout_s=300.0, device_id=torch.device("cuda", local))
     dims = syn.ModelDims()
     t0 = time.time()
     tensors = make_weights(dims)
@@ -510,8 +508,12 @@ def run_cuda(args):
         if world > 1:
             gather_images(d_out, total, world)
 
-    for _ in range(args.warmup):
+    for i in range(args.warmup):
         step()
+        if watch:
+            torch.cuda.synchronize()
+            watch.beat(i + 1)
+            watch.check()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -538,6 +540,9 @@ def run_cuda(args):
         wall = time.perf_counter() - wall0
     ms = sum(a.elapsed_time(b) for a, b in events)
     launches = g.last_launch_count()
+    if watch:
+        watch.beat(args.warmup + args.steps)
+        watch.check()
     if world > 1:
         t = torch.tensor([ms], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -69,6 +69,18 @@ void *sana_cuda_stream(sana_cuda_ctx *ctx);
 int sana_cuda_set_stream(sana_cuda_ctx *ctx, void *stream);
 /* Waits for the handle's stream and reports device-side timeouts. */
 int sana_cuda_synchronize(sana_cuda_ctx *ctx);
+/* Failure detection (no reference counterpart; the reference has no device waits). Every
+ * spin in this library's kernels (mbarrier waits of the TMA / tensor-core pipelines, flag
+ * waits) gives up after the handle's wait limit, records the
+ * timeout in the handle's device error word and unwinds; the call then returns
+ * SANA_ERR_TIMEOUT and the handle stays usable. sana_cuda_set_wait_limit sets that limit in
+ * nanoseconds (>= 1000; default 2 s), sana_cuda_wait_limit reads it. */
+int sana_cuda_set_wait_limit(sana_cuda_ctx *ctx, unsigned long long ns);
+unsigned long long sana_cuda_wait_limit(const sana_cuda_ctx *ctx);
+/* Self-test of that path: one device thread waits, with the handle's limit, for the int at
+ * device address `flag` to equal `expect`. SANA_OK once it does, SANA_ERR_TIMEOUT when the
+ * limit runs out first. */
+int sana_cuda_selftest_wait(sana_cuda_ctx *ctx, const int *flag, int expect);
 /* Kernel launches in the last captured denoising loop replay (0 before the first replay). */
 int sana_cuda_last_launch_count(const sana_cuda_ctx *ctx);
 /* Process-wide number of dense projections dispatched to the tcgen05 tensor-core kernel

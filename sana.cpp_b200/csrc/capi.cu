@@ -333,6 +333,23 @@ int sana_cuda_set_stream(sana_cuda_ctx* ctx, void* stream) {
 
 int sana_cuda_synchronize(sana_cuda_ctx* ctx) { return guard(ctx, [&] { finish(engine(ctx)); }); }
 
+int sana_cuda_set_wait_limit(sana_cuda_ctx* ctx, unsigned long long ns) {
+    return guard(ctx, [&] { engine(ctx).set_wait_limit_ns(ns); });
+}
+
+unsigned long long sana_cuda_wait_limit(const sana_cuda_ctx* ctx) {
+    return (ctx && ctx->eng) ? ctx->eng->wait_limit_ns() : 0;
+}
+
+int sana_cuda_selftest_wait(sana_cuda_ctx* ctx, const int* flag, int expect) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(flag != nullptr, "flag must be a device address");
+        sana::Engine& eng = engine(ctx);
+        sana::wait_flag(flag, expect, eng.err(), eng.stream());
+        finish(eng);
+    });
+}
+
 int sana_cuda_last_launch_count(const sana_cuda_ctx* ctx) {
     return (ctx && ctx->eng) ? ctx->eng->last_launches() : 0;
 }

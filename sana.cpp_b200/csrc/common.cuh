@@ -149,8 +149,17 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 // Bounded waits. Every spin in this library has a time limit: on expiry the waiter
 // records `code` in the context's device error word and returns false, and the kernel
 // unwinds. Waiters also give up early once any thread has recorded an error.
+//
+// A handle's device error word is 16 bytes: int [0] is the error code (0 = none), and the
+// 64-bit value at byte 8 is the handle's wait limit in nanoseconds (sana_cuda_set_wait_limit;
+// kWaitLimitNs by default). Waiters read the limit once they have spun a while.
 // ---------------------------------------------------------------------------------------
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr int kErrWordBytes = 16;
+
+__device__ __forceinline__ uint64_t wait_limit_ns(const int* err) {
+    return *reinterpret_cast<const volatile unsigned long long*>(err + 2);
+}
 
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
@@ -175,11 +184,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
         if (mbar_try_wait(bar, parity)) return true;
     }
     const uint64_t t0 = global_ns();
+    const uint64_t limit = wait_limit_ns(err);
     for (uint32_t n = 0;; ++n) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((n & 255u) == 0) {
             if (*(volatile int*)err != 0) return false;
-            if (global_ns() - t0 > kWaitLimitNs) {
+            if (global_ns() - t0 > limit) {
                 atomicCAS(err, 0, code);
                 return false;
             }

@@ -165,11 +165,22 @@ Engine::Engine(int device, int mode) : device_(device), mode_(mode) {
     SANA_CUDA(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device));
     SANA_CUDA(cudaStreamCreateWithFlags(&own_st_, cudaStreamNonBlocking));
     st_ = own_st_;
-    err_.ensure(sizeof(int));
-    SANA_CUDA(cudaMemsetAsync(err_.get(), 0, sizeof(int), st_));
+    err_.ensure(kErrWordBytes);
+    SANA_CUDA(cudaMemsetAsync(err_.get(), 0, kErrWordBytes, st_));
+    set_wait_limit_ns(kWaitLimitNs);
     SANA_CUDA(cudaStreamSynchronize(st_));
     tproj_table_.ensure(static_cast<size_t>(1024) * 256 * sizeof(float));
 }
+
+void Engine::set_wait_limit_ns(unsigned long long ns) {
+    SANA_REQUIRE(ns >= 1000, "the wait limit must be at least 1 microsecond");
+    wait_limit_host_ = ns;
+    SANA_CUDA(cudaMemcpyAsync(static_cast<char*>(err_.get()) + 8, &wait_limit_host_, sizeof(wait_limit_host_),
+                              cudaMemcpyHostToDevice, st_));
+    SANA_CUDA(cudaStreamSynchronize(st_));
+}
+
+
 
 Engine::~Engine() {
     cudaSetDevice(device_);

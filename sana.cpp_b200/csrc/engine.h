@@ -152,6 +152,9 @@ class Engine {
     // Device-side error word (timeouts); checked and cleared after every host API call.
     void check_device_error();
     int* err() const { return err_.as<int>(); }
+    // Time limit of every bounded device-side wait of this handle (common.cuh).
+    void set_wait_limit_ns(unsigned long long ns);
+    unsigned long long wait_limit_ns() const { return wait_limit_host_; }
     int num_sms() const { return num_sms_; }
     int device() const { return device_; }
 
@@ -183,6 +186,7 @@ class Engine {
     bool have_w_ = false;
     int last_launches_ = 0;
     DevBuf err_;
+    unsigned long long wait_limit_host_ = 0;  // host copy of the limit in err_ (pinned by value)
 
     // weights
     DevBuf cap_w1_, cap_b1_, cap_w2_, cap_b2_, cap_norm_;

@@ -82,6 +82,10 @@ struct SchedCoef {
     float inv_r0;
     int second_order;
 };
+// One thread waits (bounded by the handle's wait limit) for *flag == expect; on expiry the
+// error word records kTimeout (the failure-detection self-test).
+void wait_flag(const int* flag, int expect, int* err, cudaStream_t st);
+
 void cfg_scheduler_step(const float* noise, int images, int Cl, int HW, float* lat, float* hist_cur,
                         const float* hist_prev, SchedCoef k, cudaStream_t st);
 

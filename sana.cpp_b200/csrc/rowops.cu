@@ -492,6 +492,23 @@ void caption_kv_len(const float* bias, int S, int L, int* kv_len, cudaStream_t s
     SANA_CUDA(cudaGetLastError());
 }
 
+__global__ void wait_flag_kernel(const int* flag, int expect, int* err) {
+    const uint64_t t0 = global_ns();
+    const uint64_t limit = wait_limit_ns(err);
+    for (uint32_t n = 0;; ++n) {
+        if (*reinterpret_cast<const volatile int*>(flag) == expect) return;
+        if ((n & 63u) == 0 && global_ns() - t0 > limit) {
+            atomicCAS(err, 0, kTimeout);
+            return;
+        }
+    }
+}
+
+void wait_flag(const int* flag, int expect, int* err, cudaStream_t st) {
+    wait_flag_kernel<<<1, 1, 0, st>>>(flag, expect, err);
+    SANA_CUDA(cudaGetLastError());
+}
+
 void cfg_scheduler_step(const float* noise, int images, int Cl, int HW, float* lat, float* hist_cur,
                         const float* hist_prev, SchedCoef k, cudaStream_t st) {
     const long long n = static_cast<long long>(images) * Cl * HW;

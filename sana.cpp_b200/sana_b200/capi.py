@@ -262,6 +262,19 @@ class SanaCuda:
     def synchronize(self):
         self._call("sana_cuda_synchronize")
 
+    def set_wait_limit(self, ns: int):
+        """Time limit of the handle's bounded device-side waits (sana_cuda_set_wait_limit)."""
+        self._call("sana_cuda_set_wait_limit", ctypes.c_ulonglong(ns))
+
+    def wait_limit(self) -> int:
+        self.lib.sana_cuda_wait_limit.restype = ctypes.c_ulonglong
+        self.lib.sana_cuda_wait_limit.argtypes = [ctypes.c_void_p]
+        return int(self.lib.sana_cuda_wait_limit(self.h))
+
+    def selftest_wait(self, flag_ptr: int, expect: int):
+        """One device thread waits for the int at flag_ptr to equal `expect` (bounded)."""
+        self._call("sana_cuda_selftest_wait", ctypes.c_void_p(flag_ptr), _i(expect))
+
     def set_stream(self, stream_ptr: int):
         """Runs later work on the given cudaStream_t (0 restores the handle's own stream)."""
         self._call("sana_cuda_set_stream", ctypes.c_void_p(stream_ptr or None))

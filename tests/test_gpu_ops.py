@@ -260,6 +260,73 @@ def test_gemm_residual_epilogue(gpu_bf16, M, N, K, rpg, copy):
         assert (np.abs(got2 - got) <= 2.0 ** -8 * np.abs(got) + 1e-30).all()
 
 
+@pytest.mark.parametrize("M,N,K", [(4096, 1152, 1152), (4096, 3456, 1152), (2048, 5760, 1152), (2304, 1152, 2880),
+                                   (4096, 1152, 128), (8192, 3456, 1152)])
+def test_gemm_short_m_shapes(gpu_bf16, M, N, K):
+    """The projections at the per-GPU batch of 4 and 8 GPUs (2048 and 4096 rows), with K up to
+    the FF point projection's 2880, and config 4's QKV: fp32 output against float64 of the same
+    bf16 operands, bit-identical across calls."""
+    import ctypes
+    import torch
+    rng = np.random.default_rng(M + 3 * N + 7 * K)
+    a = bf16_round(rng.standard_normal((M, K)).astype(np.float32))
+    w = bf16_round((rng.standard_normal((N, K)) * 0.05).astype(np.float32))
+    b = rng.standard_normal(N).astype(np.float32)
+    ref = a.astype(np.float64) @ w.astype(np.float64).T + b
+    A, B = torch.from_numpy(a).to("cuda", torch.bfloat16), torch.from_numpy(w).to("cuda", torch.bfloat16)
+    bt = torch.from_numpy(b).cuda()
+    outs = []
+    vp = ctypes.c_void_p
+    for _ in range(2):
+        out = torch.full((M, N), float("nan"), device="cuda")
+        torch.cuda.synchronize()
+        gpu_bf16._call("sana_op_gemm_f32out_device", vp(A.data_ptr()), vp(B.data_ptr()), ctypes.c_int(M),
+                       ctypes.c_int(N), ctypes.c_int(K), vp(bt.data_ptr()), ctypes.c_int(0), vp(out.data_ptr()))
+        gpu_bf16.synchronize()
+        outs.append(out.cpu().numpy())
+    assert np.array_equal(outs[0], outs[1])
+    got = outs[0].astype(np.float64)
+    scale = np.abs(a).astype(np.float64) @ np.abs(w).astype(np.float64).T + np.abs(b)
+    assert (np.abs(got - ref) <= 1e-5 * scale + 1e-6).all(), float((np.abs(got - ref) / (scale + 1e-6)).max())
+
+
+def test_bounded_wait_times_out_and_handle_recovers():
+    """Failure detection without a fault: a device wait on a flag that nothing sets gives up
+    after the handle's wait limit (1 ms here), the call returns SANA_ERR_TIMEOUT, and the same
+    handle then runs a tensor-core GEMM correctly and passes the wait once the flag is set."""
+    import time
+
+    import torch
+    from sana_b200 import SANA_MODE_BF16, SanaCuda, SanaError
+    g = SanaCuda(0, SANA_MODE_BF16)
+    assert g.wait_limit() == 2_000_000_000
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    g.set_wait_limit(1_000_000)
+    t0 = time.perf_counter()
+    with pytest.raises(SanaError) as e:
+        g.selftest_wait(flag.data_ptr(), 1)
+    assert e.value.code == 3, e.value  # SANA_ERR_TIMEOUT
+    assert time.perf_counter() - t0 < 1.0
+    with pytest.raises(ValueError):
+        g.set_wait_limit(10)
+    g.set_wait_limit(2_000_000_000)
+    rng = np.random.default_rng(9)
+    a = bf16_round(rng.standard_normal((2048, 256)).astype(np.float32))
+    w = bf16_round((rng.standard_normal((512, 256)) * 0.05).astype(np.float32))
+    A, B = torch.from_numpy(a).to("cuda", torch.bfloat16), torch.from_numpy(w).to("cuda", torch.bfloat16)
+    out = torch.empty(2048, 512, device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    g.gemm_device(A.data_ptr(), B.data_ptr(), 2048, 512, 256, out.data_ptr())
+    g.synchronize()
+    ref = a.astype(np.float64) @ w.astype(np.float64).T
+    assert rel_err(out.float().cpu().numpy(), ref) < 5e-3
+    flag.fill_(1)
+    torch.cuda.synchronize()
+    g.selftest_wait(flag.data_ptr(), 1)
+    g.close()
+
+
 def test_gemm_repeatable(gpu_bf16):
     rng = np.random.default_rng(5)
     x = rng.standard_normal((1024, 1152)).astype(np.float32)
