@@ -146,6 +146,15 @@ int sana_gguf_tensor_info(const sana_gguf *file, int i, const char **name, int *
 int sana_cuda_upload_gguf(sana_cuda_ctx *ctx, const char *model_path, const char *caption_path,
                           const char *denoiser_path, int self_heads, int cross_heads, sana_dims *dims_out);
 
+/* Optional RMSNorm of the cross-attention query and key projections over each token's
+ * hidden channels (q = RMSNorm(x Wq + bq) * q_weight, k = RMSNorm(ctx Wk + bk) * k_weight, eps
+ * inside the root), as later Sana checkpoints normalise q / k. No counterpart in the reference:
+ * its block (transformer_ops.cpp:572-608) has no such norm, and the option is off by default
+ * and after every weight upload. q_weights / k_weights: n_blocks pointers to [hidden] fp32
+ * (a NULL array or entry = ones); enable = 0 switches it off. Applies to every later call. */
+int sana_cuda_set_cross_qk_norm(sana_cuda_ctx *ctx, int enable, const float *const *q_weights,
+                                const float *const *k_weights, float eps);
+
 /* --- the denoiser path (host buffers) --------------------------------------------------- */
 
 /* run_full_denoising_loop_with_cfg (transformer.h:140-148, transformer.cpp:692-724) with a

@@ -287,6 +287,15 @@ class _CpuModel:
     def _call(self, name, *args):
         self.cpu._call(name, ctypes.c_void_p(self.h), *args)
 
+    def set_cross_qk_norm(self, block, enable, q_weight=None, k_weight=None, eps=1e-6):
+        """The optional RMSNorm of the cross-attention q and k projections (off = the
+        reference's block)."""
+        qw, kw = _f32(q_weight), _f32(k_weight)
+        self._keep_norm = getattr(self, "_keep_norm", {})
+        self._keep_norm[block] = (qw, kw)
+        self._call("model_set_cross_qk_norm", _sz(block), ctypes.c_int(1 if enable else 0), _ptr(qw), _ptr(kw),
+                   ctypes.c_float(eps))
+
     def set_block_extras(self, block, **kw):
         names = ["q_bias", "k_bias", "v_bias", "attn_gamma", "attn_beta", "mlp_gamma", "mlp_beta"]
         vals = [_f32(kw.get(n)) for n in names]

@@ -534,6 +534,10 @@ typedef struct {
     float *w_inv, *b_inv;            /* [E, C], [E] */
     float *w_dw, *b_dw;              /* [E, 9], [E] */
     float *w_pt;                     /* [C, E/2] */
+    /* optional RMSNorm of the cross-attention q and k projections (not in the reference) */
+    int cqk_norm;                    /* 0 = off (the reference) */
+    float cqk_eps;
+    float *cq_norm, *ck_norm;        /* [C] weights, NULL = ones */
 } orc_block;
 
 typedef struct {
@@ -639,7 +643,7 @@ void orc_model_destroy(void *mp) {
         float *bf[] = {k->table, k->attn_gamma, k->attn_beta, k->wq, k->wk, k->wv, k->wo,
                        k->bq, k->bk, k->bv, k->bo, k->cwq, k->cwk, k->cwv, k->cwo, k->cbq,
                        k->cbk, k->cbv, k->cbo, k->mlp_gamma, k->mlp_beta, k->w_inv, k->b_inv,
-                       k->w_dw, k->b_dw, k->w_pt};
+                       k->w_dw, k->b_dw, k->w_pt, k->cq_norm, k->ck_norm};
         for (size_t j = 0; j < sizeof bf / sizeof bf[0]; ++j) free(bf[j]);
     }
     free(m->blocks);
@@ -661,6 +665,31 @@ int orc_model_set_block_extras(void *mp, size_t block, const float *q_bias, cons
     if (attn_beta) memcpy(k->attn_beta, attn_beta, C * sizeof(float));
     if (mlp_gamma) memcpy(k->mlp_gamma, mlp_gamma, C * sizeof(float));
     if (mlp_beta) memcpy(k->mlp_beta, mlp_beta, C * sizeof(float));
+    return 0;
+}
+
+/* Optional RMSNorm of the cross-attention query and key projections over all C channels of a
+ * token (the form of rms_norm_3d_lastdim, tensor.cpp:276-316, with eps and weight given):
+ * enable = 0 switches it off (the reference's block, the default). Weights NULL = ones. */
+int orc_model_set_cross_qk_norm(void *mp, size_t block, int enable, const float *q_weight,
+                                const float *k_weight, float eps) {
+    orc_model *m = (orc_model *)mp;
+    if (!m || block >= m->n_blocks) ORC_INVALID("block index out of range");
+    orc_block *k = &m->blocks[block];
+    const size_t C = m->C;
+    free(k->cq_norm);
+    free(k->ck_norm);
+    k->cq_norm = k->ck_norm = NULL;
+    k->cqk_norm = enable != 0;
+    k->cqk_eps = eps;
+    if (enable && q_weight) {
+        k->cq_norm = (float *)malloc(C * sizeof(float));
+        memcpy(k->cq_norm, q_weight, C * sizeof(float));
+    }
+    if (enable && k_weight) {
+        k->ck_norm = (float *)malloc(C * sizeof(float));
+        memcpy(k->ck_norm, k_weight, C * sizeof(float));
+    }
     return 0;
 }
 
@@ -749,6 +778,10 @@ int orc_block_forward(void *mp, size_t block, const float *x, size_t S, size_t T
         gemm(res, k->cwq, k->cbq, qp, M, C, C, 0);
         gemm(ctx, k->cwk, k->cbk, ck, S * L, C, C, 0);
         gemm(ctx, k->cwv, k->cbv, cv, S * L, C, C, 0);
+        if (k->cqk_norm) {
+            orc_rms_norm(qp, 1, M, C, k->cqk_eps, k->cq_norm, qp);
+            orc_rms_norm(ck, 1, S * L, C, k->cqk_eps, k->ck_norm, ck);
+        }
         split_heads(qp, S, T, Hc, Dc, qh);
         split_heads(ck, S, L, Hc, Dc, ckh);
         split_heads(cv, S, L, Hc, Dc, cvh);

@@ -103,6 +103,8 @@ void *orc_model_create(const float *const *tensors, size_t n_blocks, size_t C, s
 void orc_model_destroy(void *m);
 /* Overrides the loader defaults of one block (zero q/k/v bias, identity norms); any
  * pointer may be NULL to keep the default. Vectors of length C. */
+int orc_model_set_cross_qk_norm(void *m, size_t block, int enable, const float *q_weight,
+                                const float *k_weight, float eps);
 int orc_model_set_block_extras(void *m, size_t block, const float *q_bias, const float *k_bias,
                                const float *v_bias, const float *attn_gamma,
                                const float *attn_beta, const float *mlp_gamma,

@@ -572,6 +572,11 @@ int sana_cuda_upload_gguf(sana_cuda_ctx* ctx, const char* model_path, const char
     });
 }
 
+int sana_cuda_set_cross_qk_norm(sana_cuda_ctx* ctx, int enable, const float* const* q_weights,
+                                const float* const* k_weights, float eps) {
+    return guard(ctx, [&] { engine(ctx).set_cross_qk_norm(enable != 0, q_weights, k_weights, eps); });
+}
+
 int sana_cuda_denoise_loop(sana_cuda_ctx* ctx, const float* latents, int B, int H, int W, const float* enc, int L,
                            int enc_dim, const float* bias, float guidance, int num_steps, float flow_shift,
                            float* out) {
@@ -828,11 +833,11 @@ int sana_op_attention(sana_cuda_ctx* ctx, const float* q, const float* k, const 
         if (bf) {
             sana::cross_attention<bf16>(static_cast<const bf16*>(Q.get()), HD, static_cast<const bf16*>(KV.get()),
                                         2LL * HD, 0, HD, bd.as<float>(), kl.as<int>(), B, Tq, Tk, H, D, scale,
-                                        static_cast<bf16*>(O.get()), HD, eng.stream());
+                                        static_cast<bf16*>(O.get()), HD, eng.err(), eng.stream());
         } else {
             sana::cross_attention<float>(static_cast<const float*>(Q.get()), HD, static_cast<const float*>(KV.get()),
                                          2LL * HD, 0, HD, bd.as<float>(), kl.as<int>(), B, Tq, Tk, H, D, scale,
-                                         static_cast<float*>(O.get()), HD, eng.stream());
+                                         static_cast<float*>(O.get()), HD, eng.err(), eng.stream());
         }
         finish(eng);
         std::vector<float> ot(qt.size());
@@ -1031,11 +1036,11 @@ int sana_op_cross_attention_block(sana_cuda_ctx* ctx, const float* x, int B, int
         if (bf) {
             sana::cross_attention<bf16>(static_cast<const bf16*>(Q.get()), C, static_cast<const bf16*>(KV.get()), 2LL * C,
                                         0, C, bd.as<float>(), kl.as<int>(), B, T, L, heads, D, scale,
-                                        static_cast<bf16*>(AO.get()), C, eng.stream());
+                                        static_cast<bf16*>(AO.get()), C, eng.err(), eng.stream());
         } else {
             sana::cross_attention<float>(static_cast<const float*>(Q.get()), C, static_cast<const float*>(KV.get()),
                                          2LL * C, 0, C, bd.as<float>(), kl.as<int>(), B, T, L, heads, D, scale,
-                                         static_cast<float*>(AO.get()), C, eng.stream());
+                                         static_cast<float*>(AO.get()), C, eng.err(), eng.stream());
         }
         run_gemm(eng, AO, C, Wo, C, M, C, C, epi(o.get(), false, C, bod.as<float>()));
         finish(eng);
@@ -1329,7 +1334,7 @@ int sana_op_cross_attention_device(sana_cuda_ctx* ctx, const void* q, const void
         const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)));
         sana::cross_attention<bf16>(static_cast<const bf16*>(q), C, static_cast<const bf16*>(kv), 2LL * C, 0, C, bias,
                                     bias ? kv_len : nullptr, S, T, L, heads, D, scale, static_cast<bf16*>(out), C,
-                                    eng.stream());
+                                    eng.err(), eng.stream());
     });
 }
 

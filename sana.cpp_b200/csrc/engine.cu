@@ -252,6 +252,7 @@ void Engine::upload(const Dims& d, const float* const* model, const float* const
     graphs_.clear();
     d_ = d;
     ws_S_ = ws_T_ = ws_L_ = 0;
+    cross_qk_norm_ = false;  // new weights: the option's weights are gone with the old ones
     if (mode_ == kModeBf16) upload_impl<bf16>(model, blocks, layout);
     else upload_impl<float>(model, blocks, layout);
     SANA_CUDA(cudaStreamSynchronize(st_));
@@ -459,6 +460,34 @@ void Engine::kv_impl(int b, int S, int L, void* dst) {
     const long long rows = static_cast<long long>(S) * L;
     gemm_act(ctx_.get(), C, blk_[b].wckv.get(), C, static_cast<int>(rows), 2 * C, C,
              epi_out(dst, mode_ == kModeBf16, 2 * C, blk_[b].bckv.as<float>()));
+    if (cross_qk_norm_)  // the K half of each [k | v] row
+        rms_norm_rows<T>(static_cast<T*>(dst), rows, C, 2LL * C, cross_qk_eps_, blk_[b].ckn.as<float>(), st_);
+}
+
+void Engine::set_cross_qk_norm(bool enable, const float* const* q_w, const float* const* k_w, float eps) {
+    SANA_REQUIRE(have_w_, "weights have not been uploaded");
+    SANA_REQUIRE(!enable || eps >= 0.f, "eps must not be negative");
+    for (int b = 0; b < d_.n_blocks; ++b) {
+        BlockWeights& w = blk_[b];
+        w.cqn.release();
+        w.ckn.release();
+        if (!enable) continue;
+        const size_t bytes = static_cast<size_t>(d_.C) * 4;
+        if (q_w && q_w[b]) {
+            w.cqn.ensure(bytes);
+            SANA_CUDA(cudaMemcpyAsync(w.cqn.get(), q_w[b], bytes, cudaMemcpyHostToDevice, st_));
+        }
+        if (k_w && k_w[b]) {
+            w.ckn.ensure(bytes);
+            SANA_CUDA(cudaMemcpyAsync(w.ckn.get(), k_w[b], bytes, cudaMemcpyHostToDevice, st_));
+        }
+    }
+    SANA_CUDA(cudaStreamSynchronize(st_));
+    cross_qk_norm_ = enable;
+    cross_qk_eps_ = eps;
+    for (auto& g : graphs_)  // captured loops hold the old choice
+        if (g.second.exec) cudaGraphExecDestroy(g.second.exec);
+    graphs_.clear();
 }
 
 template <class T>
@@ -517,12 +546,16 @@ void Engine::block_impl(int b, const float* x_in, float* x_self, float* x_cross,
         ProfScope p(this, "gemm_cross_q");
         gemm_act(xq, C, w.wcq.get(), C, M, C, C, epi_out(cq_.get(), bf, C, w.bcq.as<float>()));
     }
+    if (cross_qk_norm_) {
+        ProfScope p(this, "cross_q_norm");
+        rms_norm_rows<T>(cq_.as<T>(), M, C, C, cross_qk_eps_, w.cqn.as<float>(), st_);
+    }
     const int Dc = C / d_.Hc;
     const float scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(Dc)));
     {
         ProfScope p(this, "cross_attention");
         cross_attention<T>(cq_.as<T>(), C, static_cast<const T*>(ckv_b), 2LL * C, 0, C, bias_d, kvlen_d, S, Tn, L,
-                           d_.Hc, Dc, scale, ao, C, st_);
+                           d_.Hc, Dc, scale, ao, C, err(), st_);
     }
     {
         Epilogue e = epi_out(x_cross, false, C, w.bco.as<float>());

@@ -53,6 +53,7 @@ class DevBuf {
 };
 
 struct BlockWeights {
+    DevBuf cqn, ckn;            // optional cross-attention q / k RMSNorm weights [C] f32 (empty = ones)
     DevBuf wqkv, bqkv;          // [3C, C] act type, [3C] f32
     DevBuf wo, bo;              // [C, C], [C]
     DevBuf wcq, bcq;            // [C, C], [C]
@@ -152,6 +153,10 @@ class Engine {
     // Device-side error word (timeouts); checked and cleared after every host API call.
     void check_device_error();
     int* err() const { return err_.as<int>(); }
+    // Optional RMSNorm of the cross-attention q and k projections over each token's C channels,
+    // not part of the reference's block (off by default). q_w / k_w: n_blocks pointers to [C]
+    // weights (NULL array or entries = ones).
+    void set_cross_qk_norm(bool enable, const float* const* q_w, const float* const* k_w, float eps);
     // Time limit of every bounded device-side wait of this handle (common.cuh).
     void set_wait_limit_ns(unsigned long long ns);
     unsigned long long wait_limit_ns() const { return wait_limit_host_; }
@@ -187,6 +192,8 @@ class Engine {
     int last_launches_ = 0;
     DevBuf err_;
     unsigned long long wait_limit_host_ = 0;  // host copy of the limit in err_ (pinned by value)
+    bool cross_qk_norm_ = false;
+    float cross_qk_eps_ = 1e-6f;
 
     // weights
     DevBuf cap_w1_, cap_b1_, cap_w2_, cap_b2_, cap_norm_;

@@ -175,6 +175,27 @@ __global__ void rms_norm_kernel(const float* __restrict__ x, long long rows, int
     }
 }
 
+// In-place RMSNorm of rows of width C (row stride ld), fp32 math: one warp per row.
+template <class T>
+__global__ void rms_norm_rows_kernel(T* __restrict__ x, long long rows, int C, long long ld, float eps,
+                                     const float* __restrict__ w) {
+    const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    T* xr = x + row * ld;
+    float s = 0.f;
+    for (int c = lane; c < C; c += 32) {
+        const float v = to_f(xr[c]);
+        s += v * v;
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(s) / static_cast<float>(C) + eps);
+    for (int c = lane; c < C; c += 32) {
+        float v = to_f(xr[c]) * inv;
+        if (w) v *= w[c];
+        xr[c] = from_f<T>(v);
+    }
+}
+
 __global__ void block_modulation_kernel(const float* __restrict__ tmod, int S, int width,
                                         const float* __restrict__ tables, int n_blocks, float* __restrict__ mod) {
     const long long total = static_cast<long long>(n_blocks) * S * width;
@@ -432,6 +453,17 @@ void ln_modulate(const float* x, long long rows, int C, int rows_per_seq, const 
                                                         scale_idx, eps, out);
     SANA_CUDA(cudaGetLastError());
 }
+
+template <class T>
+void rms_norm_rows(T* x, long long rows, int C, long long ld, float eps, const float* w, cudaStream_t st) {
+    if (rows == 0) return;
+    constexpr int warps = 8;
+    rms_norm_rows_kernel<T><<<static_cast<unsigned>((rows + warps - 1) / warps), warps * 32, 0, st>>>(x, rows, C, ld,
+                                                                                                      eps, w);
+    SANA_CUDA(cudaGetLastError());
+}
+template void rms_norm_rows<float>(float*, long long, int, long long, float, const float*, cudaStream_t);
+template void rms_norm_rows<bf16>(bf16*, long long, int, long long, float, const float*, cudaStream_t);
 
 template <class TO>
 void rms_norm(const float* x, long long rows, int C, float eps, const float* w, TO* out, cudaStream_t st) {

@@ -8,6 +8,8 @@
 //
 // Keys at index >= kv_len[s] are skipped: their bias is <= -1000 (caption_kv_len), so
 // exp(score - max) underflows to exactly 0 in fp32 and the reference's sum is unchanged.
+#include <cstdlib>
+
 #include "kernels.h"
 
 namespace sana {
@@ -400,17 +402,33 @@ bool try_mma<bf16>(const bf16* q, long long ldq, const bf16* kv, long long ldkv,
     }
 }
 
+// SANA_XATTN_TC=1 in the environment selects the tcgen05 kernel for bf16 cross-attention
+// (xattn_tc.cu); the mma.sync kernel below is the default while it is the faster one.
+bool tc_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("SANA_XATTN_TC");
+        return v && v[0] == '1';
+    }();
+    return on;
+}
+
 }  // namespace
 
 template <class T>
 void cross_attention(const T* q, long long ldq, const T* kv, long long ldkv, int k_off, int v_off,
                      const float* bias, const int* kv_len, int S, int Tq, int L, int heads, int D, float scale,
-                     T* out, long long ldo, cudaStream_t st) {
+                     T* out, long long ldo, int* err, cudaStream_t st) {
     SANA_REQUIRE(D >= 1 && D <= 128, "cross attention supports head_dim 1..128");
     SANA_REQUIRE(L >= 1, "cross attention needs at least one key");
     const size_t smem = 2 * static_cast<size_t>(L) * D * sizeof(T) + static_cast<size_t>(L) * 4 + 8;
     SANA_REQUIRE(smem <= 227 * 1024, "caption too long for the shared-memory key/value tile");
     if (S == 0 || Tq == 0) return;
+    if constexpr (sizeof(T) == 2) {
+        if (tc_enabled() &&
+            cross_attention_tc(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, D, scale, out, ldo, err,
+                               st))
+            return;
+    }
     if (try_mma<T>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, D, scale, out, ldo, st)) return;
     if (D <= 8) launch<T, 8>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, D, scale, out, ldo, st);
     else if (D <= 32) launch<T, 32>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, D, scale, out, ldo, st);
@@ -419,8 +437,9 @@ void cross_attention(const T* q, long long ldq, const T* kv, long long ldkv, int
 }
 
 template void cross_attention<float>(const float*, long long, const float*, long long, int, int, const float*,
-                                     const int*, int, int, int, int, int, float, float*, long long, cudaStream_t);
+                                     const int*, int, int, int, int, int, float, float*, long long, int*,
+                                     cudaStream_t);
 template void cross_attention<bf16>(const bf16*, long long, const bf16*, long long, int, int, const float*,
-                                    const int*, int, int, int, int, int, float, bf16*, long long, cudaStream_t);
+                                    const int*, int, int, int, int, int, float, bf16*, long long, int*, cudaStream_t);
 
 }  // namespace sana

@@ -262,6 +262,19 @@ class SanaCuda:
     def synchronize(self):
         self._call("sana_cuda_synchronize")
 
+    def set_cross_qk_norm(self, enable: bool, q_weights=None, k_weights=None, eps: float = 1e-6):
+        """Optional RMSNorm of the cross-attention q / k projections (off by default; not in the
+        reference). q_weights / k_weights: per-block [hidden] arrays, or None for ones."""
+        n = self.dims.n_blocks if self.dims is not None else 0
+
+        def table(ws):
+            if ws is None:
+                return None
+            keep = [_f32(w) for w in ws]
+            self._keep_qk = getattr(self, "_keep_qk", []) + keep
+            return (_f32p * n)(*[_ptr(w) for w in keep])
+        self._call("sana_cuda_set_cross_qk_norm", _i(1 if enable else 0), table(q_weights), table(k_weights), _f(eps))
+
     def set_wait_limit(self, ns: int):
         """Time limit of the handle's bounded device-side waits (sana_cuda_set_wait_limit)."""
         self._call("sana_cuda_set_wait_limit", ctypes.c_ulonglong(ns))

@@ -501,6 +501,24 @@ def test_scheduler_configs_match_reference(gpu_f32):
         gpu_f32.scheduler_update_config(heun, 2, want["sg"], 0, mo[0], mo[0], x0)
 
 
+@pytest.mark.parametrize("D", [72, 64, 32])
+def test_cross_attention_tcgen05_key_chunks(gpu_bf16, oracle, D):
+    """The tcgen05 cross-attention (TMEM scores, online softmax over 128-key chunks) at valid
+    lengths of 1, 17, 128, 129, 255 and 300 keys (one to three chunks, a chunk of one live
+    key), a query count that leaves a partial 128-query tile, and six sequences."""
+    from sana_b200 import synthetic as syn
+    rng = np.random.default_rng(D)
+    lens = (1, 17, 128, 129, 255, 300)
+    S, H, Tq, L = len(lens), 3, 1024 + 64, 300
+    q = rng.standard_normal((S, H, Tq, D)).astype(np.float32)
+    k, v = (rng.standard_normal((S, H, L, D)).astype(np.float32) for _ in range(2))
+    bias = syn.attention_bias(lens, L)
+    ref = oracle.attention(q, k, v, bias)
+    got = gpu_bf16.attention(q, k, v, bias)
+    for s in range(S):
+        assert rel_err(got[s], ref[s]) < BF16_TOL, (D, lens[s], rel_err(got[s], ref[s]))
+
+
 @pytest.mark.parametrize("D,Tq,L,lens", [(72, 1024, 300, (8, 24)), (72, 100, 300, (300, 1)), (32, 77, 70, (70, 65)),
                                         (64, 130, 129, (64, 129)), (128, 40, 20, (20, 3))])
 def test_cross_attention_tensor_core_shapes(gpu_bf16, oracle, D, Tq, L, lens):
