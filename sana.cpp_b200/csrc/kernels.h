@@ -134,18 +134,13 @@ void linear_attention(const T* q, long long ldq, int q_off, const T* kv, long lo
 // Masked softmax cross-attention (attention_4d, transformer_ops.cpp:348-392): per head,
 // softmax(q k^T * scale + bias) v over the first kv_len[s] keys. q rows s*Tq.. at column
 // h*D (stride ldq); k/v rows s*L.. at columns k_off + h*D / v_off + h*D (stride ldkv);
-// bias fp32 [S, L] or null; out rows at column h*D (stride ldo). bf16 with head dims 32 / 64 / 72,
-// 16-byte aligned rows and captions of at most 304 keys run the tcgen05 kernel (xattn_tc.cu);
-// other bf16 shapes the mma.sync kernel, fp32 the CUDA-core kernel (xattn.cu). err: the
-// handle's device error word (bounded waits).
+// bias fp32 [S, L] or null; out rows at column h*D (stride ldo). bf16 runs on tensor cores
+// (mma.sync) for head dims 32 / 64 / 72 / 128 with 16-byte aligned rows, fp32 on CUDA cores.
+// err: the handle's device error word.
 template <class T>
 void cross_attention(const T* q, long long ldq, const T* kv, long long ldkv, int k_off, int v_off,
                      const float* bias, const int* kv_len, int S, int Tq, int L, int heads, int D, float scale,
                      T* out, long long ldo, int* err, cudaStream_t st);
-// The tcgen05 kernel alone; false (nothing launched) when the shape is not one it takes.
-bool cross_attention_tc(const bf16* q, long long ldq, const bf16* kv, long long ldkv, int k_off, int v_off,
-                        const float* bias, const int* kv_len, int S, int Tq, int L, int heads, int D, float scale,
-                        bf16* out, long long ldo, int* err, cudaStream_t st);
 
 // --- dwglu.cu -----------------------------------------------------------------------------
 

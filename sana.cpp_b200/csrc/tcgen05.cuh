@@ -1,5 +1,5 @@
-// Single-CTA tcgen05 / TMEM primitives and shared-memory matrix descriptors (sm_100a), shared
-// by the tensor-core GEMM (gemm_tc.cu) and the tensor-core cross-attention (xattn_tc.cu).
+// Single-CTA tcgen05 / TMEM primitives and shared-memory matrix descriptors (sm_100a) of the
+// tensor-core GEMM (gemm_tc.cu).
 #pragma once
 #include <cuda.h>
 
@@ -49,7 +49,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint32_t dst, uint32_t bar, int c0, int c1) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
@@ -77,19 +76,6 @@ __device__ __forceinline__ uint64_t kmajor_sw128_desc(uint32_t smem_addr) {
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
            (static_cast<uint32_t>(m >> 4) << 24);
-}
-
-// Shared-memory matrix descriptor of a K-major operand in the canonical layout without
-// swizzling: 8-row x 16-byte core matrices (rows 16 bytes apart, 128 contiguous bytes), the
-// next 8 rows `sbo` bytes on, the next 16-byte (8-element) slice of K `lbo` bytes on;
-// descriptor version 1 (sm_100), base offset 0, layout type 0 = no swizzle.
-__device__ __forceinline__ uint64_t kmajor_nosw_desc(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
-    uint64_t d = 0;
-    d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
-    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
-    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
-    d |= static_cast<uint64_t>(1u) << 46;
-    return d;
 }
 
 }  // namespace tc

@@ -8,8 +8,6 @@
 //
 // Keys at index >= kv_len[s] are skipped: their bias is <= -1000 (caption_kv_len), so
 // exp(score - max) underflows to exactly 0 in fp32 and the reference's sum is unchanged.
-#include <cstdlib>
-
 #include "kernels.h"
 
 namespace sana {
@@ -402,16 +400,6 @@ bool try_mma<bf16>(const bf16* q, long long ldq, const bf16* kv, long long ldkv,
     }
 }
 
-// SANA_XATTN_TC=1 in the environment selects the tcgen05 kernel for bf16 cross-attention
-// (xattn_tc.cu); the mma.sync kernel below is the default while it is the faster one.
-bool tc_enabled() {
-    static const bool on = [] {
-        const char* v = std::getenv("SANA_XATTN_TC");
-        return v && v[0] == '1';
-    }();
-    return on;
-}
-
 }  // namespace
 
 template <class T>
@@ -423,12 +411,7 @@ void cross_attention(const T* q, long long ldq, const T* kv, long long ldkv, int
     const size_t smem = 2 * static_cast<size_t>(L) * D * sizeof(T) + static_cast<size_t>(L) * 4 + 8;
     SANA_REQUIRE(smem <= 227 * 1024, "caption too long for the shared-memory key/value tile");
     if (S == 0 || Tq == 0) return;
-    if constexpr (sizeof(T) == 2) {
-        if (tc_enabled() &&
-            cross_attention_tc(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, D, scale, out, ldo, err,
-                               st))
-            return;
-    }
+    (void)err;
     if (try_mma<T>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, D, scale, out, ldo, st)) return;
     if (D <= 8) launch<T, 8>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, D, scale, out, ldo, st);
     else if (D <= 32) launch<T, 32>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, D, scale, out, ldo, st);

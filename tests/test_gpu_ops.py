@@ -502,10 +502,10 @@ def test_scheduler_configs_match_reference(gpu_f32):
 
 
 @pytest.mark.parametrize("D", [72, 64, 32])
-def test_cross_attention_tcgen05_key_chunks(gpu_bf16, oracle, D):
-    """The tcgen05 cross-attention (TMEM scores, online softmax over 128-key chunks) at valid
-    lengths of 1, 17, 128, 129, 255 and 300 keys (one to three chunks, a chunk of one live
-    key), a query count that leaves a partial 128-query tile, and six sequences."""
+def test_cross_attention_key_counts(gpu_bf16, oracle, D):
+    """The tensor-core cross-attention at valid lengths of 1, 17, 128, 129, 255 and 300 keys
+    (64-key chunks full, partial and single-key), a query count that leaves a partial
+    128-query tile, and six sequences."""
     from sana_b200 import synthetic as syn
     rng = np.random.default_rng(D)
     lens = (1, 17, 128, 129, 255, 300)
