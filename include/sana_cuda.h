@@ -143,6 +143,9 @@ int sana_gguf_find(const sana_gguf *file, const char *name);
  * mapping (valid until sana_gguf_close) and their count (0 for types other than those three). */
 int sana_gguf_tensor_info(const sana_gguf *file, int i, const char **name, int *type, int *rank, int64_t *shape,
                           int max_rank, const void **data, uint64_t *nbytes);
+/* byte offset of tensor i's data from the start of the file (SavedWeightInfo::offset of
+ * weights_io.h:19-25, gguf_get_data_offset + gguf_get_tensor_offset in weights_io.cpp:156) */
+int sana_gguf_tensor_offset(const sana_gguf *file, int i, uint64_t *offset);
 int sana_cuda_upload_gguf(sana_cuda_ctx *ctx, const char *model_path, const char *caption_path,
                           const char *denoiser_path, int self_heads, int cross_heads, sana_dims *dims_out);
 

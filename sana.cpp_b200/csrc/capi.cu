@@ -502,6 +502,12 @@ int sana_gguf_tensor_info(const sana_gguf* f, int i, const char** name, int* typ
     return SANA_OK;
 }
 
+int sana_gguf_tensor_offset(const sana_gguf* f, int i, uint64_t* offset) {
+    if (!f || !offset || i < 0 || i >= static_cast<int>(f->file->tensors().size())) return SANA_ERR_INVALID;
+    *offset = f->file->tensors()[static_cast<size_t>(i)].file_offset;
+    return SANA_OK;
+}
+
 int sana_cuda_upload_gguf(sana_cuda_ctx* ctx, const char* model_path, const char* caption_path,
                           const char* denoiser_path, int self_heads, int cross_heads, sana_dims* dims_out) {
     return guard(ctx, [&] {

@@ -145,6 +145,7 @@ GgufFile::GgufFile(const std::string& path) : path_(path) {
             if (r.offset > size_ - data_start || t.nbytes > size_ - data_start - r.offset)
                 c.fail("tensor data past the end of the file: " + r.name);
             t.data = static_cast<const uint8_t*>(map_) + data_start + r.offset;
+            t.file_offset = data_start + r.offset;
             if (!by_name_.emplace(t.name, tensors_.size()).second) c.fail("duplicate tensor name " + t.name);
             tensors_.push_back(std::move(t));
         }

@@ -23,6 +23,7 @@ struct GgufTensor {
     uint32_t type = 0;
     std::vector<int64_t> shape;  // slowest-varying first (numpy / PyTorch order: extents reversed)
     const uint8_t* data = nullptr;
+    uint64_t file_offset = 0;    // of the first data byte from the start of the file
     uint64_t nbytes = 0;         // 0 for element types without a fixed size here
     int64_t elements() const;
 };

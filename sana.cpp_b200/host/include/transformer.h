@@ -1,15 +1,16 @@
 // The reference's denoiser API (cconthekeyboard/sana.cpp src/transformer.h:11-155): the weight
 // structs and the hot-path entry points, implemented by host/transformer_cuda.cpp over the C
-// ABI of include/sana_cuda.h. The reference header also declares the safetensors/GGUF loaders
-// (load_*_weights, find_block_prefixes, validate_*), which stay the reference's own code and
-// are not declared here.
+// ABI of include/sana_cuda.h, and the weight loaders and validators (load_*_weights,
+// find_block_prefixes, validate_*), implemented by host/loaders.cpp on top of weights_io.h.
 #pragma once
 
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "scheduler.h"
 #include "tensor.h"
+#include "weights_io.h"
 
 struct SanaBlockModulation {
     Tensor shift_msa;
@@ -80,6 +81,29 @@ struct SanaDenoiserWeights {
     Tensor proj_out_weight;
     Tensor proj_out_bias;
 };
+
+// Loaders (transformer.cpp:166-488): tensors by their diffusers names, linear weights
+// transposed to [in, out]; blocks found by "<prefix>.scale_shift_table" and ordered by their
+// trailing index. Errors are the reference's (std::invalid_argument / std::runtime_error).
+SanaCaptionWeights load_caption_weights(const std::string& weights_dir,
+                                        const std::unordered_map<std::string, SavedWeightInfo>& index);
+SanaBlockWeights load_block_weights(const std::string& weights_dir,
+                                    const std::unordered_map<std::string, SavedWeightInfo>& index,
+                                    const std::string& block_prefix, size_t self_num_heads, size_t cross_num_heads);
+std::vector<std::string> find_block_prefixes(const std::unordered_map<std::string, SavedWeightInfo>& index);
+std::vector<SanaBlockWeights> load_model_block_weights(const std::string& weights_dir,
+                                                       const std::unordered_map<std::string, SavedWeightInfo>& index,
+                                                       size_t self_num_heads, size_t cross_num_heads);
+SanaDenoiserWeights load_denoiser_weights(const std::string& block_weights_dir,
+                                          const std::unordered_map<std::string, SavedWeightInfo>& block_index,
+                                          const std::string& caption_weights_dir,
+                                          const std::unordered_map<std::string, SavedWeightInfo>& caption_index,
+                                          const std::string& denoiser_weights_dir,
+                                          const std::unordered_map<std::string, SavedWeightInfo>& denoiser_index,
+                                          size_t self_num_heads, size_t cross_num_heads);
+// transformer.cpp:780-881: std::invalid_argument with the reference's messages.
+void validate_denoiser_weights(const SanaDenoiserWeights& weights);
+void validate_model_block_sequence(const std::vector<SanaBlockWeights>& blocks);
 
 SanaBlockModulation compute_sana_block_modulation(const Tensor& timestep, const Tensor& scale_shift_table);
 Tensor run_model_blocks(const Tensor& input, const Tensor& context, const Tensor& timestep,

@@ -1,15 +1,18 @@
 // The reference's VAE decoder API (cconthekeyboard/sana.cpp src/vae.h:11-92): the weight
 // structs, with the same members in the same order so that weights built by the reference's
 // own load_vae_weights pass straight through, and the decode entry points, implemented by
-// host/vae_cuda.cpp over the C ABI of include/sana_cuda.h. The GGUF index helpers
-// (find_vae_decoder_up_block_prefixes, load_vae_weights) stay the reference's own code and
-// are not declared here.
+// host/vae_cuda.cpp over the C ABI of include/sana_cuda.h, and the loaders
+// (find_vae_decoder_up_block_prefixes, load_vae_weights), implemented by host/loaders.cpp on
+// top of weights_io.h.
 #pragma once
 
 #include <optional>
+#include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "tensor.h"
+#include "weights_io.h"
 
 struct SanaVaeResBlockWeights {
     Tensor conv1_weight;
@@ -68,6 +71,17 @@ struct SanaVaeWeights {
     float scaling_factor = 1.0f;
     size_t spatial_compression_ratio = 32;
 };
+
+// "decoder.up_blocks.<i>" prefixes ordered by i (vae.cpp:88-136).
+std::vector<std::string> find_vae_decoder_up_block_prefixes(
+    const std::unordered_map<std::string, SavedWeightInfo>& index);
+// vae.cpp:12-86, 138-160: an up block has an upsample conv when "<prefix>.0.conv.weight"
+// exists, then three layers; it holds ResBlocks only when it has the upsample conv and its
+// first layer has conv1 (otherwise attention + GLUMBConv layers); attention linear weights
+// become [out, in, 1, 1].
+SanaVaeWeights load_vae_weights(const std::string& weights_dir,
+                                const std::unordered_map<std::string, SavedWeightInfo>& index, float scaling_factor,
+                                size_t spatial_compression_ratio);
 
 // validate_vae_decoder_weights / validate_vae_weights (vae.cpp:172-208): std::invalid_argument
 // with the reference's messages.
