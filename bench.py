@@ -12,6 +12,7 @@ own index; the final latents are NCCL-gathered into the full batch on every rank
 loop (the path's only collective). Total work is fixed as N grows ("strong" scaling).
 
     python bench.py --microbench [--op NAME,...]     (one GPU)
+    torchrun --nproc-per-node 2 bench.py --gpus 2 --cfg-pair   (latency mode, configs[1])
 
 One bench step = one full denoising loop over the rank's batch (caption projection,
 cross-K/V for all blocks, 20 denoiser steps, CFG + scheduler), replayed from a CUDA graph.
@@ -667,6 +668,152 @@ def run_cuda(args):
         dist.destroy_process_group()
 
 
+def run_cfg_pair(args):
+    """--cfg-pair: the latency mode. Ranks 2p / 2p+1 run the unconditional / conditional
+    branch of the same images (configs[1]: one image per pair by default) and meet once per
+    step inside the guidance kernel over NVLink peer memory (sana_b200.cfgpair). `value` is
+    images/s over all pairs; `latency_ms` is one image's 20-step loop. Rank 0 also times the
+    one-GPU loop of the same images and reports how far the paired result is from it."""
+    import torch
+    import torch.distributed as dist
+    from sana_b200 import SANA_MODE_BF16, SanaCuda
+    from sana_b200 import synthetic as syn
+    from sana_b200.cfgpair import connect_engine, pair_of
+    from sana_b200.watchdog import init_ranks
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    rank, world, watch = init_ranks("nccl", timeout_s=300.0, device_id=torch.device("cuda", local))
+    pair, branch, _ = pair_of(rank, world)
+    pairs = world // 2
+    B = args.images if args.images else 1
+    dims = syn.ModelDims()
+    tensors = make_weights(dims)
+    g = SanaCuda(local, SANA_MODE_BF16)
+    g.upload_checkpoint(dims.as_args(), tensors)
+    del tensors
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    g.set_stream(stream.cuda_stream)
+    lat, enc, bias, lens = make_inputs(pair * B, B)
+    assert connect_engine(g, lat.size) == branch
+    d_lat = torch.from_numpy(lat).cuda()
+    d_enc = torch.from_numpy(np.ascontiguousarray(enc[branch * B:(branch + 1) * B])).cuda()
+    d_bias = torch.from_numpy(np.ascontiguousarray(bias[branch * B:(branch + 1) * B])).cuda()
+    d_out = torch.empty_like(d_lat)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def step():
+        g.denoise_loop_pair_device(d_lat.data_ptr(), B, 32, 32, d_enc.data_ptr(), CAPTION_LEN, 2304,
+                                   d_bias.data_ptr(), d_out.data_ptr(), GUIDANCE, NUM_STEPS)
+
+    for i in range(args.warmup):
+        step()
+        g.synchronize()
+        if watch:
+            watch.beat(i + 1)
+            watch.check()
+    dist.barrier()
+    gpu_index = os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local] if os.environ.get(
+        "CUDA_VISIBLE_DEVICES") else str(local)
+    events = []
+    with ClockSampler(gpu_index) as clk:
+        torch.cuda.synchronize()
+        dist.barrier()
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+            events.append((e0, e1))
+        g.synchronize()
+        dist.barrier()
+    ms = sum(a.elapsed_time(b) for a, b in events) / args.steps
+    launches = g.last_launch_count()
+    t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    paired = d_out.cpu().numpy()
+
+    # e2e through the Python API: pinned host inputs in, result out, every step
+    h_lat = torch.from_numpy(lat).pin_memory()
+    h_enc = torch.from_numpy(np.ascontiguousarray(enc[branch * B:(branch + 1) * B])).pin_memory()
+    h_bias = torch.from_numpy(np.ascontiguousarray(bias[branch * B:(branch + 1) * B])).pin_memory()
+    h_out = torch.empty_like(h_lat).pin_memory()
+
+    def e2e_step():
+        d_lat.copy_(h_lat, non_blocking=True)
+        d_enc.copy_(h_enc, non_blocking=True)
+        d_bias.copy_(h_bias, non_blocking=True)
+        step()
+        h_out.copy_(d_out, non_blocking=True)
+        stream.synchronize()
+
+    e2e_step()
+    dist.barrier()
+    t1 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t1) / args.steps
+    t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_s = float(t.item())
+    g.synchronize()
+    g.cfg_pair_close()
+    dist.barrier()
+
+    single = None
+    if rank == 0:
+        # the same images on one GPU, both branches in one batch
+        s_enc, s_bias = torch.from_numpy(enc).cuda(), torch.from_numpy(bias).cuda()
+        s_out = torch.empty_like(d_lat)
+
+        def one_gpu():
+            g.denoise_loop_device(d_lat.data_ptr(), B, 32, 32, s_enc.data_ptr(), CAPTION_LEN, 2304,
+                                  s_bias.data_ptr(), s_out.data_ptr(), GUIDANCE, NUM_STEPS)
+        d_lat.copy_(torch.from_numpy(lat))
+        for _ in range(args.warmup):
+            one_gpu()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            flush.zero_()
+            one_gpu()
+        e1.record(stream)
+        e1.synchronize()
+        ref = s_out.cpu().numpy().astype(np.float64).ravel()
+        a = paired.astype(np.float64).ravel()
+        single = {"ms": e0.elapsed_time(e1) / args.steps,
+                  "cosine": float(a @ ref / (np.linalg.norm(a) * np.linalg.norm(ref))),
+                  "rel_l2": float(np.linalg.norm(a - ref) / np.linalg.norm(ref))}
+        out = {
+            "metric": METRIC, "mode": "cfg_pair (latency)", "value": pairs * B / (ms / 1e3), "unit": "images/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "latency_ms": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded random-init Sana-0.6B weights, N(0,1) latents and caption states",
+            "config": {"workload": f"config1: {B} image(s) per GPU pair, unconditional branch on one GPU and "
+                                   f"conditional on the other, {NUM_STEPS}-step DPM-Solver++ loop, guidance "
+                                   f"{GUIDANCE}; one {B * 32 * 1024 * 4 // 1024} KB noise exchange per step and "
+                                   "direction over NVLink inside the guidance kernel",
+                       "global_batch": pairs * B, "seq_len": 1024, "caption_tokens": CAPTION_LEN,
+                       "parallelism": f"{pairs} pair(s) x 2 CFG branches",
+                       "l2": "flushed between timed iterations (256 MiB write, untimed)"},
+            "one_gpu_same_images": {"ms": single["ms"], "speedup": single["ms"] / ms,
+                                    "paired_vs_one_gpu_cosine": single["cosine"],
+                                    "paired_vs_one_gpu_rel_l2": single["rel_l2"]},
+            "e2e": {"value": pairs * B / e2e_s, "unit": "images/s",
+                    "h2d_bytes_per_step": 2 * (h_lat.numel() + h_enc.numel() + h_bias.numel()) * 4,
+                    "d2h_bytes_per_step": 2 * h_out.numel() * 4,
+                    "note": "Python API (torch copies from pinned host memory + the paired loop), both ranks"},
+            "gpu_launches": launches * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(out), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -679,8 +826,15 @@ def main():
     ap.add_argument("--microbench", action="store_true",
                     help="op-level microbenchmark (BASELINE configs[4]) instead of the loop; one GPU")
     ap.add_argument("--op", default="", help="with --microbench: comma-separated subset of " + ",".join(MICRO_OPS))
+    ap.add_argument("--cfg-pair", action="store_true",
+                    help="latency mode: each pair of ranks splits one batch's CFG branches (--images per pair, "
+                         "default 1)")
     args = ap.parse_args()
-    if args.microbench:
+    if args.cfg_pair and args.impl == "cuda":
+        if args.images == 16 and "--images" not in sys.argv:
+            args.images = 1
+        run_cfg_pair(args)
+    elif args.microbench:
         run_microbench(args)
     elif args.impl == "reference":
         run_reference(args)

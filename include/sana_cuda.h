@@ -81,6 +81,25 @@ unsigned long long sana_cuda_wait_limit(const sana_cuda_ctx *ctx);
  * device address `flag` to equal `expect`. SANA_OK once it does, SANA_ERR_TIMEOUT when the
  * limit runs out first. */
 int sana_cuda_selftest_wait(sana_cuda_ctx *ctx, const int *flag, int expect);
+/* --- classifier-free guidance across two GPUs (latency mode) ----------------------------------
+ * One process and handle per GPU. The two noise predictions of a step meet once, inside the
+ * guidance + scheduler kernel, over NVLink peer memory (apply_classifier_free_guidance,
+ * transformer.cpp:570-602; step_sana_scheduler, scheduler.cpp:272-318): each GPU pushes its
+ * prediction into the other's receive buffer and waits (bounded by the wait limit) for the
+ * other's. Setup: both export, swap the 64-byte handles (any host channel), both connect; GPU 0
+ * takes branch 0 (unconditional), GPU 1 branch 1 (conditional). Both then call
+ * sana_cuda_denoise_loop_pair_device with the same latents, shapes and schedule, each with its
+ * own branch's B encoder sequences [B, L, enc_dim] and bias [B, 1, L], and both receive the
+ * same guided latents. A timeout (SANA_ERR_TIMEOUT) leaves the exchange out of step: export and
+ * connect again. */
+#define SANA_PAIR_HANDLE_BYTES 64
+int sana_cuda_cfg_pair_export(sana_cuda_ctx *ctx, size_t max_latent_elems, void *handle);
+int sana_cuda_cfg_pair_connect(sana_cuda_ctx *ctx, int branch, const void *peer_handle);
+int sana_cuda_cfg_pair_close(sana_cuda_ctx *ctx);
+int sana_cuda_denoise_loop_pair_device(sana_cuda_ctx *ctx, const float *latents, int B, int H, int W,
+                                       const float *enc, int L, int enc_dim, const float *bias, float guidance,
+                                       int num_steps, float flow_shift, float *out);
+
 /* Kernel launches in the last captured denoising loop replay (0 before the first replay). */
 int sana_cuda_last_launch_count(const sana_cuda_ctx *ctx);
 /* Process-wide number of dense projections dispatched to the tcgen05 tensor-core kernel

@@ -613,6 +613,34 @@ int sana_cuda_denoise_loop_device(sana_cuda_ctx* ctx, const float* latents, int 
     });
 }
 
+int sana_cuda_cfg_pair_export(sana_cuda_ctx* ctx, size_t max_latent_elems, void* handle) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(handle, "handle must not be null");
+        engine(ctx).pair_export(max_latent_elems, handle);
+    });
+}
+
+int sana_cuda_cfg_pair_connect(sana_cuda_ctx* ctx, int branch, const void* peer_handle) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(peer_handle, "peer handle must not be null");
+        engine(ctx).pair_connect(branch, peer_handle);
+    });
+}
+
+int sana_cuda_cfg_pair_close(sana_cuda_ctx* ctx) {
+    return guard(ctx, [&] { engine(ctx).pair_close(); });
+}
+
+int sana_cuda_denoise_loop_pair_device(sana_cuda_ctx* ctx, const float* latents, int B, int H, int W,
+                                       const float* enc, int L, int enc_dim, const float* bias, float guidance,
+                                       int num_steps, float flow_shift, float* out) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(latents && enc && out, "latents, encoder states and output must not be null");
+        engine(ctx).denoise_loop_pair_device(latents, B, H, W, enc, L, enc_dim, bias, guidance, num_steps,
+                                             default_sched(flow_shift), out);
+    });
+}
+
 int sana_cuda_denoise_step(sana_cuda_ctx* ctx, float* latents, int B, int H, int W, const float* context, int L,
                            const float* bias, float guidance, float timestep, const float* sigmas, int n_sigmas,
                            int* step_index, int* lower_order_count, float* history, int* n_history) {

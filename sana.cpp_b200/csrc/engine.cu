@@ -186,7 +186,100 @@ Engine::~Engine() {
     cudaSetDevice(device_);
     for (auto& g : graphs_)
         if (g.second.exec) cudaGraphExecDestroy(g.second.exec);
+    if (pair_peer_) cudaIpcCloseMemHandle(pair_peer_);
+    if (pair_region_) cudaFree(pair_region_);
     if (own_st_) cudaStreamDestroy(own_st_);
+}
+
+// Region layout: kPairBlocks flags, kPairBlocks exchange counts and the buffer capacity
+// (a 1 KB header), then two receive buffers of pair_cap_ floats.
+constexpr size_t kPairHeader = 1024;
+constexpr size_t kPairCapOffset = 2 * kPairBlocks * sizeof(int);
+
+PairLink Engine::pair_link() const {
+    PairLink l;
+    l.flags = static_cast<int*>(pair_region_);
+    l.count = l.flags + kPairBlocks;
+    l.recv = reinterpret_cast<float*>(static_cast<char*>(pair_region_) + kPairHeader);
+    l.peer_flags = static_cast<int*>(pair_peer_);
+    l.peer_recv = reinterpret_cast<float*>(static_cast<char*>(pair_peer_) + kPairHeader);
+    l.capacity = pair_cap_;
+    return l;
+}
+
+void Engine::pair_close() {
+    SANA_CUDA(cudaSetDevice(device_));
+    SANA_CUDA(cudaStreamSynchronize(st_));
+    // recorded loops hold the peer's addresses
+    for (auto it = graphs_.begin(); it != graphs_.end();) {
+        if (it->first.find(",pair") != std::string::npos) {
+            if (it->second.exec) cudaGraphExecDestroy(it->second.exec);
+            it = graphs_.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    if (pair_peer_) SANA_CUDA(cudaIpcCloseMemHandle(pair_peer_));
+    pair_peer_ = nullptr;
+    pair_branch_ = -1;
+}
+
+void Engine::pair_export(size_t capacity, void* handle) {
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+    SANA_REQUIRE(capacity >= 4 && capacity <= (1ull << 32), "exchange capacity must be 4 .. 2^32 latent elements");
+    static_assert(kPairCapOffset + sizeof(long long) <= kPairHeader, "pair header too small");
+    pair_close();
+    if (pair_region_) SANA_CUDA(cudaFree(pair_region_));
+    pair_region_ = nullptr;
+    pair_cap_ = static_cast<long long>((capacity + 3) / 4 * 4);
+    const size_t bytes = kPairHeader + 2 * static_cast<size_t>(pair_cap_) * sizeof(float);
+    SANA_CUDA(cudaMalloc(&pair_region_, bytes));
+    SANA_CUDA(cudaMemsetAsync(pair_region_, 0, bytes, st_));
+    SANA_CUDA(cudaMemcpyAsync(static_cast<char*>(pair_region_) + kPairCapOffset, &pair_cap_, sizeof pair_cap_,
+                              cudaMemcpyHostToDevice, st_));
+    SANA_CUDA(cudaStreamSynchronize(st_));
+    cudaIpcMemHandle_t h;
+    SANA_CUDA(cudaIpcGetMemHandle(&h, pair_region_));
+    std::memcpy(handle, &h, sizeof h);
+}
+
+void Engine::pair_connect(int branch, const void* peer_handle) {
+    SANA_REQUIRE(pair_region_, "export this GPU's exchange region before connecting");
+    SANA_REQUIRE(branch == 0 || branch == 1, "branch must be 0 (unconditional) or 1 (conditional)");
+    pair_close();
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, peer_handle, sizeof h);
+    SANA_CUDA(cudaIpcOpenMemHandle(&pair_peer_, h, cudaIpcMemLazyEnablePeerAccess));
+    // the kernel addresses the peer's buffers with this GPU's capacity: they must agree
+    long long peer_cap = 0;
+    SANA_CUDA(cudaMemcpy(&peer_cap, static_cast<char*>(pair_peer_) + kPairCapOffset, sizeof peer_cap,
+                         cudaMemcpyDeviceToHost));
+    if (peer_cap != pair_cap_) {
+        cudaIpcCloseMemHandle(pair_peer_);
+        pair_peer_ = nullptr;
+        throw std::invalid_argument("the peer exported a different exchange capacity");
+    }
+    pair_branch_ = branch;
+}
+
+void Engine::denoise_loop_pair_device(const float* lat, int B, int H, int W, const float* enc, int L, int Din,
+                                      const float* bias, float guidance, int num_steps, const SchedConfig& sc,
+                                      float* out) {
+    SANA_REQUIRE(have_w_, "weights have not been uploaded");
+    SANA_REQUIRE(pair_peer_, "connect to the peer GPU before running a two-GPU loop");
+    SANA_REQUIRE(B >= 1 && H >= 1 && W >= 1 && L >= 1, "invalid loop shapes");
+    SANA_REQUIRE(Din == d_.Din, "encoder hidden size must match caption projection input");
+    SANA_REQUIRE(static_cast<long long>(B) * d_.Cl * H * W <= pair_cap_, "latents exceed the exchange capacity");
+    ensure_workspace(B, H * W, L);
+    pair_run_ = true;
+    try {
+        run_loop(lat, B, H, W, enc, L, Din, bias, guidance, num_steps, sc, out,
+                 "dev,pair" + std::to_string(pair_branch_));
+    } catch (...) {
+        pair_run_ = false;
+        throw;
+    }
+    pair_run_ = false;
 }
 
 void Engine::check_device_error() {
@@ -635,7 +728,8 @@ template <class T>
 void Engine::loop_body(const float* lat_in, int B, int H, int W, const float* enc_d, int L, int Din,
                        const float* bias_d, const std::vector<SchedCoef>& coefs, float* out_d) {
     (void)Din;
-    const int S = 2 * B, Tn = H * W, C = d_.C, Cl = d_.Cl, nb = d_.n_blocks;
+    // both branches (uncond then cond sequences), or this GPU's branch of a two-GPU pair
+    const int S = pair_run_ ? B : 2 * B, Tn = H * W, C = d_.C, Cl = d_.Cl, nb = d_.n_blocks;
     const size_t n_lat = static_cast<size_t>(B) * Cl * Tn;
     {
         ProfScope p(this, "caption_projection");
@@ -671,7 +765,11 @@ void Engine::loop_body(const float* lat_in, int B, int H, int W, const float* en
         float* cur = hist_.as<float>() + (step % 2) * n_lat;
         const float* prev = hist_.as<float>() + ((step + 1) % 2) * n_lat;
         ProfScope p(this, "cfg_scheduler");
-        cfg_scheduler_step(noise_.as<float>(), B, Cl, Tn, lat_.as<float>(), cur, prev, coefs[step], st_);
+        if (pair_run_)
+            cfg_pair_step(noise_.as<float>(), pair_link(), B, Cl, Tn, lat_.as<float>(), cur, prev, coefs[step],
+                          pair_branch_, err(), st_);
+        else
+            cfg_scheduler_step(noise_.as<float>(), B, Cl, Tn, lat_.as<float>(), cur, prev, coefs[step], st_);
     }
     SANA_CUDA(cudaMemcpyAsync(out_d, lat_.get(), n_lat * 4, cudaMemcpyDeviceToDevice, st_));
 }

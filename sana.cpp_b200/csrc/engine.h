@@ -163,6 +163,19 @@ class Engine {
     int num_sms() const { return num_sms_; }
     int device() const { return device_; }
 
+    // Guidance split across two GPUs (cfgpair.cu), one process and handle per GPU:
+    // pair_export allocates this GPU's exchange region for up to `capacity` latent elements and
+    // writes its CUDA IPC handle (64 bytes) to `handle`; pair_connect maps the peer's region and
+    // takes branch 0 (unconditional) or 1 (conditional); denoise_loop_pair_device runs the loop
+    // of that branch (enc / bias hold its B sequences), meeting the peer once per step. Both
+    // GPUs must run the same loops in the same order; after a timeout both export again.
+    void pair_export(size_t capacity, void* handle);
+    void pair_connect(int branch, const void* peer_handle);
+    void pair_close();
+    void denoise_loop_pair_device(const float* lat, int B, int H, int W, const float* enc, int L, int Din,
+                                  const float* bias, float guidance, int num_steps, const SchedConfig& sc,
+                                  float* out);
+
    private:
     template <class T> void upload_impl(const float* const* model, const float* const* blocks, int layout);
     template <class T> void caption_impl(const float* enc_d, int S, int L);
@@ -194,6 +207,15 @@ class Engine {
     unsigned long long wait_limit_host_ = 0;  // host copy of the limit in err_ (pinned by value)
     bool cross_qk_norm_ = false;
     float cross_qk_eps_ = 1e-6f;
+
+    // two-GPU guidance: this GPU's region [flags | counts | 2 receive buffers], the peer's
+    // mapping, the branch, and whether the loop being recorded runs one branch
+    void* pair_region_ = nullptr;
+    long long pair_cap_ = 0;
+    void* pair_peer_ = nullptr;
+    int pair_branch_ = -1;
+    bool pair_run_ = false;
+    PairLink pair_link() const;
 
     // weights
     DevBuf cap_w1_, cap_b1_, cap_w2_, cap_b2_, cap_norm_;

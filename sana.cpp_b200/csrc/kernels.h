@@ -93,6 +93,27 @@ void wait_flag(const int* flag, int expect, int* err, cudaStream_t st);
 void cfg_scheduler_step(const float* noise, int images, int Cl, int HW, float* lat, float* hist_cur,
                         const float* hist_prev, SchedCoef k, cudaStream_t st);
 
+// --- cfgpair.cu: guidance across two GPUs ------------------------------------------------------
+
+// One GPU's view of the exchange: its own receive buffers (2 x capacity floats, written by the
+// peer), flags (incremented by the peer) and per-slot exchange counts, and the peer's receive
+// buffers and flags mapped through CUDA IPC.
+constexpr int kPairBlocks = 64;
+struct PairLink {
+    float* recv;
+    float* peer_recv;
+    int* flags;
+    int* peer_flags;
+    int* count;
+    long long capacity;  // floats per receive buffer, a multiple of 4
+};
+// CFG + scheduler update of this GPU's branch (0 unconditional, 1 conditional) against the
+// peer's: pushes own_noise (token-major [images * HW, Cl]) to the peer, waits for the peer's
+// (bounded; kTimeout in err on expiry, the latents then left unchanged) and updates lat /
+// hist_cur as cfg_scheduler_step does.
+void cfg_pair_step(const float* own_noise, const PairLink& link, int images, int Cl, int HW, float* lat,
+                   float* hist_cur, const float* hist_prev, SchedCoef k, int branch, int* err, cudaStream_t st);
+
 // The update alone on already-converted outputs: out = a x + b m0 [+ c (m0 - m1) / r0]
 // (sana_scheduler_first_order_update / _second_order_update, scheduler.cpp:175-270).
 void scheduler_update(const float* m0, const float* m1, const float* x, long long n, SchedCoef k, float* out,

@@ -415,6 +415,32 @@ class SanaCuda:
         self._call("sana_cuda_denoise_loop_device", vp(lat_ptr), _i(B), _i(H), _i(W), vp(enc_ptr), _i(L), _i(Din),
                    vp(bias_ptr) if bias_ptr else None, _f(guidance), _i(num_steps), _f(flow_shift), vp(out_ptr))
 
+    # --- guidance across two GPUs (sana_cuda_cfg_pair_*) --------------------------------------
+
+    def cfg_pair_export(self, max_latent_elems: int) -> bytes:
+        """Allocates this GPU's exchange region; returns its 64-byte CUDA IPC handle."""
+        buf = ctypes.create_string_buffer(64)
+        self._call("sana_cuda_cfg_pair_export", ctypes.c_size_t(max_latent_elems), buf)
+        return buf.raw
+
+    def cfg_pair_connect(self, branch: int, peer_handle: bytes):
+        """Maps the peer's region; branch 0 runs the unconditional sequences, 1 the conditional."""
+        if len(peer_handle) != 64:
+            raise ValueError("a peer handle is 64 bytes")
+        self._call("sana_cuda_cfg_pair_connect", _i(branch), ctypes.create_string_buffer(peer_handle, 64))
+
+    def cfg_pair_close(self):
+        self._call("sana_cuda_cfg_pair_close")
+
+    def denoise_loop_pair_device(self, lat_ptr: int, B: int, H: int, W: int, enc_ptr: int, L: int, Din: int,
+                                 bias_ptr: Optional[int], out_ptr: int, guidance: float = 4.5, num_steps: int = 20,
+                                 flow_shift: float = 3.0):
+        """The loop of this GPU's branch: enc [B, L, Din] / bias [B, 1, L] of that branch."""
+        vp = ctypes.c_void_p
+        self._call("sana_cuda_denoise_loop_pair_device", vp(lat_ptr), _i(B), _i(H), _i(W), vp(enc_ptr), _i(L),
+                   _i(Din), vp(bias_ptr) if bias_ptr else None, _f(guidance), _i(num_steps), _f(flow_shift),
+                   vp(out_ptr))
+
     def profile_loop_device(self, lat_ptr: int, B: int, H: int, W: int, enc_ptr: int, L: int, Din: int,
                             bias_ptr: Optional[int], out_ptr: int, guidance: float = 4.5, num_steps: int = 20,
                             flow_shift: float = 3.0) -> dict:
