@@ -93,6 +93,14 @@ def _inputs(d):
 
 
 def _pair_rank(rank, port, q, partner_runs):
+    try:
+        _pair_rank_body(rank, port, q, partner_runs)
+    except BaseException as e:  # report instead of leaving the parent waiting on the queue
+        q.put((rank, f"raised {type(e).__name__}: {e}", None))
+        raise
+
+
+def _pair_rank_body(rank, port, q, partner_runs):
     _env(rank, 2, port)
     import datetime
 
@@ -154,6 +162,8 @@ def _run_pair(partner_runs):
         p.start()
     n = 2 if partner_runs else 1
     out = sorted((q.get(timeout=600) for _ in range(n)), key=lambda t: t[0])
+    for _, what, _ in out:
+        assert not (isinstance(what, str) and what.startswith("raised")), what
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
