@@ -126,9 +126,6 @@ constexpr int kChunkKeys = 64;
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
 __device__ __forceinline__ void ldmatrix_x2_trans(uint32_t addr, uint32_t& r0, uint32_t& r1) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
@@ -159,8 +156,9 @@ struct XattnTiles {
     static constexpr int KSTR = conflict_free_stride(DP);  // Q and K tile row stride
     static constexpr int VSTR = conflict_free_stride(D);   // V tile row stride
     static constexpr int kQRows = 16 * kMmaWarps;
-    static constexpr size_t kBytes = (static_cast<size_t>(kQRows) * KSTR + kChunkKeys * KSTR + kChunkKeys * VSTR) * 2 +
-                                     kChunkKeys * 4;
+    // the query tile, then two buffers of one key / value / bias chunk each
+    static constexpr size_t kChunkBytes = static_cast<size_t>(kChunkKeys) * (KSTR + VSTR) * 2 + kChunkKeys * 4;
+    static constexpr size_t kBytes = static_cast<size_t>(kQRows) * KSTR * 2 + 2 * kChunkBytes;
 };
 
 template <int D>
@@ -178,9 +176,10 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
     static_assert((KSTR / 2) % 8 == 4 && (VSTR / 2) % 8 == 4 && KSTR % 8 == 0 && VSTR % 8 == 0, "strides");
     extern __shared__ __align__(16) unsigned char xsm[];
     bf16* Qs = reinterpret_cast<bf16*>(xsm);            // [128][KSTR], later the output rows
-    bf16* Ks = Qs + X::kQRows * KSTR;                    // [64][KSTR]
-    bf16* Vs = Ks + kChunkKeys * KSTR;                   // [64][VSTR]
-    float* bsh = reinterpret_cast<float*>(Vs + kChunkKeys * VSTR);
+    unsigned char* chunk0 = xsm + X::kQRows * KSTR * 2;   // two buffers of [K 64][KSTR], [V 64][VSTR], bias [64]
+    auto Kbuf = [&](int b) { return reinterpret_cast<bf16*>(chunk0 + b * X::kChunkBytes); };
+    auto Vbuf = [&](int b) { return Kbuf(b) + kChunkKeys * KSTR; };
+    auto Bbuf = [&](int b) { return reinterpret_cast<float*>(Vbuf(b) + kChunkKeys * VSTR); };
 
     const int s = blockIdx.z, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -189,9 +188,20 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
     const int q0 = qb + warp * 16;
     const int n_kv = kv_len ? kv_len[s] : L;
     const bool active = q0 < Tq;
-    const uint32_t qbase = smem_u32(Qs), kbase = smem_u32(Ks), vbase = smem_u32(Vs);
+    const uint32_t qbase = smem_u32(Qs);
 
-    // query tile (rows past Tq and the head-dim padding read as zeros)
+    // Head-dim padding of the query tile and of both key buffers: zero once (copies write D
+    // columns). Stores here and in load_chunk are ordered before any read by the barrier that
+    // follows the first wait.
+    if constexpr (DP > D) {
+        for (int i = threadIdx.x; i < X::kQRows * (DP - D); i += blockDim.x)
+            Qs[(i / (DP - D)) * KSTR + D + i % (DP - D)] = __float2bfloat16_rn(0.f);
+        for (int i = threadIdx.x; i < 2 * kChunkKeys * (DP - D); i += blockDim.x) {
+            const int b = i / (kChunkKeys * (DP - D)), r = i % (kChunkKeys * (DP - D));
+            Kbuf(b)[(r / (DP - D)) * KSTR + D + r % (DP - D)] = __float2bfloat16_rn(0.f);
+        }
+    }
+    // query tile (rows past Tq read as zeros)
     for (int i = threadIdx.x; i < X::kQRows * RC; i += blockDim.x) {
         const int r = i / RC, ck = i % RC;
         if (qb + r < Tq)
@@ -200,141 +210,158 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
         else
             *reinterpret_cast<uint4*>(Qs + r * KSTR + ck * 8) = make_uint4(0u, 0u, 0u, 0u);
     }
-    if constexpr (DP > D) {
-        for (int i = threadIdx.x; i < X::kQRows * (DP - D); i += blockDim.x)
-            Qs[(i / (DP - D)) * KSTR + D + i % (DP - D)] = __float2bfloat16_rn(0.f);
-        for (int i = threadIdx.x; i < kChunkKeys * (DP - D); i += blockDim.x)
-            Ks[(i / (DP - D)) * KSTR + D + i % (DP - D)] = __float2bfloat16_rn(0.f);
-    }
-    cp_async_wait_all();
-    __syncthreads();
-    uint32_t qa[KS][4];
-#pragma unroll
-    for (int kk = 0; kk < KS; ++kk)
-        ldmatrix_x4(qbase + static_cast<uint32_t>((warp * 16 + (lane & 15)) * KSTR + kk * 16 + (lane >> 4) * 8) * 2u,
-                    qa[kk]);
-
-    float o[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-
-    for (int c0 = 0; c0 < n_kv; c0 += kChunkKeys) {
-        const int nk = min(kChunkKeys, n_kv - c0);
-        __syncthreads();
+    // keys and values of chunk c into buffer b; keys past the chunk end are zeros (their scores
+    // are masked to -inf)
+    auto load_chunk = [&](int c, int b) {
+        const int c0 = c * kChunkKeys, nk = min(kChunkKeys, n_kv - c0);
+        bf16* Kb = Kbuf(b);
+        bf16* Vb = Vbuf(b);
+        const uint32_t kb = smem_u32(Kb), vb = smem_u32(Vb);
         for (int i = threadIdx.x; i < kChunkKeys * RC * 2; i += blockDim.x) {
             const int which = i / (kChunkKeys * RC), rem = i % (kChunkKeys * RC);
             const int j = rem / RC, ck = rem % RC;
             if (j < nk) {
                 const bf16* src = kv + (static_cast<long long>(s) * L + c0 + j) * ldkv + (which ? v_off : k_off) + h * D +
                                   ck * 8;
-                cp_async16((which ? vbase + static_cast<uint32_t>(j * VSTR + ck * 8) * 2u
-                                  : kbase + static_cast<uint32_t>(j * KSTR + ck * 8) * 2u),
+                cp_async16(which ? vb + static_cast<uint32_t>(j * VSTR + ck * 8) * 2u
+                                 : kb + static_cast<uint32_t>(j * KSTR + ck * 8) * 2u,
                            src);
-            } else {  // keys past the chunk end: zeros (their scores are masked to -inf)
-                bf16* dst = which ? Vs + j * VSTR + ck * 8 : Ks + j * KSTR + ck * 8;
+            } else {
+                bf16* dst = which ? Vb + j * VSTR + ck * 8 : Kb + j * KSTR + ck * 8;
                 *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
             }
         }
+        float* bb = Bbuf(b);
         for (int j = threadIdx.x; j < kChunkKeys; j += blockDim.x)
-            bsh[j] = (j < nk && bias) ? bias[static_cast<long long>(s) * L + c0 + j] : 0.f;
-        cp_async_wait_all();
-        __syncthreads();
-        if (!active) continue;
+            bb[j] = (j < nk && bias) ? bias[static_cast<long long>(s) * L + c0 + j] : 0.f;
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // the query tile and the first chunk arrive together; later chunks load one ahead
+    const int nchunks = (n_kv + kChunkKeys - 1) / kChunkKeys;
+    load_chunk(0, 0);
 
-        const int ntmax = (nk + 7) / 8;  // 8-key column tiles holding live keys
-        float sc[kChunkKeys / 8][4];
+    uint32_t qa[KS][4];
+    float o[NT][4];
 #pragma unroll
-        for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
-            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = -INFINITY;
-            if (nt < ntmax) {
-                float acc[4] = {0.f, 0.f, 0.f, 0.f};
-                // K fragments by ldmatrix: 8 key rows x (two k-steps of 16) per x4 load
-                const uint32_t krow = kbase + static_cast<uint32_t>((nt * 8 + (lane & 7)) * KSTR + (lane >> 3) * 8) * 2u;
+    for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+    for (int c = 0; c < nchunks; ++c) {
+        const int buf = c & 1;
+        if (c + 1 < nchunks) {
+            load_chunk(c + 1, buf ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const int c0 = c * kChunkKeys;
+        const int nk = min(kChunkKeys, n_kv - c0);
+        const uint32_t kbase = smem_u32(Kbuf(buf)), vbase = smem_u32(Vbuf(buf));
+        const float* bsh = Bbuf(buf);
+        if (active) {
+            if (c == 0) {
 #pragma unroll
-                for (int kk = 0; kk + 1 < KS; kk += 2) {
+                for (int kk = 0; kk < KS; ++kk)
+                    ldmatrix_x4(qbase + static_cast<uint32_t>((warp * 16 + (lane & 15)) * KSTR + kk * 16 + (lane >> 4) * 8) *
+                                            2u,
+                                qa[kk]);
+            }
+            const int ntmax = (nk + 7) / 8;  // 8-key column tiles holding live keys
+            float sc[kChunkKeys / 8][4];
+#pragma unroll
+            for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
+                sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = -INFINITY;
+                if (nt < ntmax) {
+                    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+                    // K fragments by ldmatrix: 8 key rows x (two k-steps of 16) per x4 load
+                    const uint32_t krow = kbase + static_cast<uint32_t>((nt * 8 + (lane & 7)) * KSTR + (lane >> 3) * 8) * 2u;
+#pragma unroll
+                    for (int kk = 0; kk + 1 < KS; kk += 2) {
+                        uint32_t b[4];
+                        ldmatrix_x4(krow + static_cast<uint32_t>(kk * 16) * 2u, b);
+                        mma_bf16_16816(acc, qa[kk], b[0], b[1]);
+                        mma_bf16_16816(acc, qa[kk + 1], b[2], b[3]);
+                    }
+                    if constexpr (KS % 2 == 1) {
+                        uint32_t b0, b1;
+                        ldmatrix_x2(krow + static_cast<uint32_t>((KS - 1) * 16) * 2u, b0, b1);
+                        mma_bf16_16816(acc, qa[KS - 1], b0, b1);
+                    }
+                    const int key = nt * 8 + tig * 2;
+                    const float2 b2 = *reinterpret_cast<const float2*>(bsh + key);
+                    if (key < nk) {
+                        sc[nt][0] = __fadd_rn(__fmul_rn(acc[0], scale), b2.x);
+                        sc[nt][2] = __fadd_rn(__fmul_rn(acc[2], scale), b2.x);
+                    }
+                    if (key + 1 < nk) {
+                        sc[nt][1] = __fadd_rn(__fmul_rn(acc[1], scale), b2.y);
+                        sc[nt][3] = __fadd_rn(__fmul_rn(acc[3], scale), b2.y);
+                    }
+                }
+            }
+            float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+            for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
+                mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
+                mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
+            }
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+            const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+            const float corr0 = __expf(m0 - mn0), corr1 = __expf(m1 - mn1);  // m = -inf on the first chunk: 0
+            m0 = mn0;
+            m1 = mn1;
+            float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+            for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
+                if (nt < ntmax) {
+                    sc[nt][0] = __expf(sc[nt][0] - mn0);
+                    sc[nt][1] = __expf(sc[nt][1] - mn0);
+                    sc[nt][2] = __expf(sc[nt][2] - mn1);
+                    sc[nt][3] = __expf(sc[nt][3] - mn1);
+                    sum0 += sc[nt][0] + sc[nt][1];
+                    sum1 += sc[nt][2] + sc[nt][3];
+                } else {
+                    sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+                }
+            }
+            l0 = l0 * corr0 + sum0;
+            l1 = l1 * corr1 + sum1;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                o[nt][0] *= corr0;
+                o[nt][1] *= corr0;
+                o[nt][2] *= corr1;
+                o[nt][3] *= corr1;
+            }
+            const int kmax = (nk + 15) / 16;  // k-steps holding live keys
+#pragma unroll
+            for (int kk = 0; kk < kChunkKeys / 16; ++kk) {
+                if (kk >= kmax) break;
+                const uint32_t pa[4] = {pack_bf16(sc[2 * kk][0], sc[2 * kk][1]), pack_bf16(sc[2 * kk][2], sc[2 * kk][3]),
+                                        pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]),
+                                        pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3])};
+                const uint32_t vrow = vbase + static_cast<uint32_t>((kk * 16 + (lane & 15)) * VSTR) * 2u;
+                // V fragments of two 8-column output tiles per x4 load (lanes 16-31 address the second)
+                const uint32_t vrow4 = vrow + static_cast<uint32_t>((lane >> 4) * 8) * 2u;
+#pragma unroll
+                for (int nt = 0; nt + 1 < NT; nt += 2) {
                     uint32_t b[4];
-                    ldmatrix_x4(krow + static_cast<uint32_t>(kk * 16) * 2u, b);
-                    mma_bf16_16816(acc, qa[kk], b[0], b[1]);
-                    mma_bf16_16816(acc, qa[kk + 1], b[2], b[3]);
+                    ldmatrix_x4_trans(vrow4 + static_cast<uint32_t>(nt * 16), b);
+                    mma_bf16_16816(o[nt], pa, b[0], b[1]);
+                    mma_bf16_16816(o[nt + 1], pa, b[2], b[3]);
                 }
-                if constexpr (KS % 2 == 1) {
+                if constexpr (NT % 2 == 1) {
                     uint32_t b0, b1;
-                    ldmatrix_x2(krow + static_cast<uint32_t>((KS - 1) * 16) * 2u, b0, b1);
-                    mma_bf16_16816(acc, qa[KS - 1], b0, b1);
-                }
-                const int key = nt * 8 + tig * 2;
-                const float2 b2 = *reinterpret_cast<const float2*>(bsh + key);
-                if (key < nk) {
-                    sc[nt][0] = __fadd_rn(__fmul_rn(acc[0], scale), b2.x);
-                    sc[nt][2] = __fadd_rn(__fmul_rn(acc[2], scale), b2.x);
-                }
-                if (key + 1 < nk) {
-                    sc[nt][1] = __fadd_rn(__fmul_rn(acc[1], scale), b2.y);
-                    sc[nt][3] = __fadd_rn(__fmul_rn(acc[3], scale), b2.y);
+                    ldmatrix_x2_trans(vrow + static_cast<uint32_t>((NT - 1) * 16), b0, b1);
+                    mma_bf16_16816(o[NT - 1], pa, b0, b1);
                 }
             }
         }
-        float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-        for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
-            mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
-            mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
-        }
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-        const float corr0 = __expf(m0 - mn0), corr1 = __expf(m1 - mn1);  // m = -inf on the first chunk: 0
-        m0 = mn0;
-        m1 = mn1;
-        float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-        for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
-            if (nt < ntmax) {
-                sc[nt][0] = __expf(sc[nt][0] - mn0);
-                sc[nt][1] = __expf(sc[nt][1] - mn0);
-                sc[nt][2] = __expf(sc[nt][2] - mn1);
-                sc[nt][3] = __expf(sc[nt][3] - mn1);
-                sum0 += sc[nt][0] + sc[nt][1];
-                sum1 += sc[nt][2] + sc[nt][3];
-            } else {
-                sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-            }
-        }
-        l0 = l0 * corr0 + sum0;
-        l1 = l1 * corr1 + sum1;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            o[nt][0] *= corr0;
-            o[nt][1] *= corr0;
-            o[nt][2] *= corr1;
-            o[nt][3] *= corr1;
-        }
-        const int kmax = (nk + 15) / 16;  // k-steps holding live keys
-#pragma unroll
-        for (int kk = 0; kk < kChunkKeys / 16; ++kk) {
-            if (kk >= kmax) break;
-            const uint32_t pa[4] = {pack_bf16(sc[2 * kk][0], sc[2 * kk][1]), pack_bf16(sc[2 * kk][2], sc[2 * kk][3]),
-                                    pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]),
-                                    pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3])};
-            const uint32_t vrow = vbase + static_cast<uint32_t>((kk * 16 + (lane & 15)) * VSTR) * 2u;
-            // V fragments of two 8-column output tiles per x4 load (lanes 16-31 address the second)
-            const uint32_t vrow4 = vrow + static_cast<uint32_t>((lane >> 4) * 8) * 2u;
-#pragma unroll
-            for (int nt = 0; nt + 1 < NT; nt += 2) {
-                uint32_t b[4];
-                ldmatrix_x4_trans(vrow4 + static_cast<uint32_t>(nt * 16), b);
-                mma_bf16_16816(o[nt], pa, b[0], b[1]);
-                mma_bf16_16816(o[nt + 1], pa, b[2], b[3]);
-            }
-            if constexpr (NT % 2 == 1) {
-                uint32_t b0, b1;
-                ldmatrix_x2_trans(vrow + static_cast<uint32_t>((NT - 1) * 16), b0, b1);
-                mma_bf16_16816(o[NT - 1], pa, b0, b1);
-            }
-        }
+        __syncthreads();  // buffer `buf` is free for chunk c + 2
     }
     if (!active) return;
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
