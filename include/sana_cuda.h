@@ -204,6 +204,13 @@ int sana_cuda_denoise_step(sana_cuda_ctx *ctx, float *latents, int B, int H, int
                            const float *bias, float guidance, float timestep, const float *sigmas, int n_sigmas,
                            int *step_index, int *lower_order_count, float *history, int *n_history);
 
+/* The timestep embedding (sinusoidal features, timestep_embedder MLP with SiLU; emb, which the
+ * final layer's modulation reads) and t_block (SiLU then the 6C projection) for S sequences at
+ * timesteps t[S] (transformer.cpp:77-122, 638-656): emb [S, hidden] and tmod [S, 6 * hidden] to
+ * host buffers (either may be NULL). In bf16 mode the three projections run on the tensor cores
+ * as inside the loop. */
+int sana_cuda_time_embed(sana_cuda_ctx *ctx, const float *timesteps, int S, float *emb, float *tmod);
+
 /* One denoiser forward without CFG or scheduler for S independent sequences at timestep t:
  * patch embed, time embedding, all blocks, final layer (transformer.cpp:631-681).
  *   latents [S, Cl, H, W]; context [S, L, hidden] (projected); bias [S, 1, L] or NULL;

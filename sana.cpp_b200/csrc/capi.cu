@@ -641,6 +641,15 @@ int sana_cuda_denoise_loop_pair_device(sana_cuda_ctx* ctx, const float* latents,
     });
 }
 
+int sana_cuda_time_embed(sana_cuda_ctx* ctx, const float* timesteps, int S, float* emb, float* tmod) {
+    return guard(ctx, [&] {
+        SANA_REQUIRE(timesteps, "timesteps must not be null");
+        sana::Engine& eng = engine(ctx);
+        eng.time_embed(timesteps, S, emb, tmod);
+        eng.check_device_error();
+    });
+}
+
 int sana_cuda_denoise_step(sana_cuda_ctx* ctx, float* latents, int B, int H, int W, const float* context, int L,
                            const float* bias, float guidance, float timestep, const float* sigmas, int n_sigmas,
                            int* step_index, int* lower_order_count, float* history, int* n_history) {

@@ -863,6 +863,28 @@ void Engine::denoise_loop(const float* lat, int B, int H, int W, const float* en
 // ---------------------------------------------------------------------------------------
 // Finer host-buffer entry points
 // ---------------------------------------------------------------------------------------
+void Engine::time_embed(const float* t, int S, float* emb, float* tmod) {
+    SANA_REQUIRE(have_w_, "weights have not been uploaded");
+    SANA_REQUIRE(S >= 1 && S <= 1024, "time_embed takes 1..1024 timesteps");
+    ensure_workspace(S, 1, 1);
+    std::vector<float> feats(static_cast<size_t>(S) * 256);
+    for (int s = 0; s < S; ++s) timestep_features(t[s], feats.data() + static_cast<size_t>(s) * 256);
+    SANA_CUDA(cudaMemcpyAsync(tproj_table_.get(), feats.data(), feats.size() * 4, cudaMemcpyHostToDevice, st_));
+    const int C = d_.C;
+    if (mode_ == kModeBf16) {
+        convert<bf16>(tproj_table_.as<float>(), static_cast<long long>(S) * 256, tproj_.as<bf16>(), st_);
+        time_embed_impl<bf16>(tproj_.get(), S);
+    } else {
+        convert<float>(tproj_table_.as<float>(), static_cast<long long>(S) * 256, tproj_.as<float>(), st_);
+        time_embed_impl<float>(tproj_.get(), S);
+    }
+    if (emb)
+        SANA_CUDA(cudaMemcpyAsync(emb, emb_.get(), static_cast<size_t>(S) * C * 4, cudaMemcpyDeviceToHost, st_));
+    if (tmod)
+        SANA_CUDA(cudaMemcpyAsync(tmod, tmod_.get(), static_cast<size_t>(S) * 6 * C * 4, cudaMemcpyDeviceToHost, st_));
+    SANA_CUDA(cudaStreamSynchronize(st_));
+}
+
 void Engine::project_caption(const float* enc, int S, int L, int Din, float* out) {
     SANA_REQUIRE(have_w_, "weights have not been uploaded");
     SANA_REQUIRE(Din == d_.Din, "encoder hidden size must match caption projection input");

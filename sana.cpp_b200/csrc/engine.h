@@ -124,6 +124,9 @@ class Engine {
 
     // --- host-buffer entry points (the reference-facing API) ---------------------------
     void project_caption(const float* enc, int S, int L, int Din, float* out);
+    // Timestep embedding and t_block for S sequences at host timesteps t[S]: emb [S, C] (the
+    // final layer's modulation input) and tmod [S, 6C] to host buffers (either may be null).
+    void time_embed(const float* t, int S, float* emb, float* tmod);
     void block_forward(int b, const float* x, int S, int T, const float* ctx, int L, const float* tmod,
                        const float* bias, float* after_self, float* after_cross, float* after_ff);
     void run_blocks(const float* x, int S, int T, const float* ctx, int L, const float* tmod, const float* bias,

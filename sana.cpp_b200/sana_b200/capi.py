@@ -468,6 +468,16 @@ class SanaCuda:
                    _ptr(hist), ctypes.byref(nh))
         return lat, si.value, lo.value, [hist[i].copy() for i in range(nh.value)]
 
+    def time_embed(self, tvals):
+        """Timestep embedding + t_block on the device: (emb [S, C], tmod [S, 6C])."""
+        t = np.ascontiguousarray(np.asarray(tvals, np.float32).ravel())
+        S = t.size
+        C = self.dims.hidden
+        emb = np.empty((S, C), np.float32)
+        tmod = np.empty((S, 6 * C), np.float32)
+        self._call("sana_cuda_time_embed", _ptr(t), _i(S), _ptr(emb), _ptr(tmod))
+        return emb, tmod
+
     def forward(self, latents, t, context, bias=None):
         lat, ctx, bias = _f32(latents), _f32(context), _f32(bias)
         S, Cl, H, W = lat.shape
@@ -707,6 +717,9 @@ class _GpuModel:
 
     def project_caption(self, enc):
         return self.g.project_caption_model(enc)
+
+    def time_embed(self, tvals):
+        return self.g.time_embed(tvals)
 
     def forward_nocfg(self, latents, t, ctx, bias=None):
         return self.g.forward(latents, t, ctx, bias)
