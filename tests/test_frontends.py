@@ -20,7 +20,7 @@ import sys
 import numpy as np
 import pytest
 
-from conftest import ROOT
+from conftest import ROOT, reference_root
 
 PKG = os.path.join(ROOT, "sana.cpp_b200")
 LIB = os.path.join(PKG, "lib")
@@ -67,8 +67,8 @@ def frontends():
     exes = {name: os.path.join(LIB, name) for name in b.REFERENCE_FRONTENDS.values()}
     if all(os.path.exists(e) for e in exes.values()):
         return exes
-    ref = os.environ.get("SANA_REFERENCE_ROOT", "/root/reference")
-    if not os.path.isdir(os.path.join(ref, "src")):
+    ref = reference_root()
+    if not ref or not os.path.isdir(os.path.join(ref, "src")):
         pytest.skip("reference front ends not built and the reference tree is absent")
     built = b.build_reference_frontends(ref)
     return {b.REFERENCE_FRONTENDS[k]: v for k, v in built.items()}
