@@ -159,30 +159,46 @@ struct Side16 {
     float g[16];
 };
 
+// v = resid + gate * v on 16 columns, as fused multiply-adds on pairs.
+__device__ __forceinline__ void resid16(float (&v)[16], const float (&rv)[16], const float (&gv)[16]) {
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+        const float2 y = f2_split(fma2(f2_make(gv[j], gv[j + 1]), f2_make(v[j], v[j + 1]), f2_make(rv[j], rv[j + 1])));
+        v[j] = y.x;
+        v[j + 1] = y.y;
+    }
+}
+
 // Bias, activation and gated residual on 16 consecutive columns [n0, n0+16) of one row,
 // all of them in range (the fast path); the stores are the caller's.
 template <bool kResid>
 __device__ __forceinline__ void compute16(const Epilogue& ep, const float (&bv)[16], float (&v)[16],
                                           const float (&rv)[16], const float (&gv)[16]) {
-    if (ep.bias) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] += bv[j];
-    }
-    if (ep.act == kActSilu) {
+    if (ep.act == kActSilu) {  // bias and SiLU on pairs
 #pragma unroll
         for (int j = 0; j < 16; j += 2) {
-            const float2 y = f2_split(silu2(f2_make(v[j], v[j + 1])));
+            uint64_t x = f2_make(v[j], v[j + 1]);
+            if (ep.bias) x = add2(x, f2_make(bv[j], bv[j + 1]));
+            const float2 y = f2_split(silu2(x));
             v[j] = y.x;
             v[j + 1] = y.y;
         }
-    } else if (ep.act == kActGelu) {
+        if (kResid) resid16(v, rv, gv);
+        return;
+    }
+    if (ep.bias) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+            const float2 y = f2_split(add2(f2_make(v[j], v[j + 1]), f2_make(bv[j], bv[j + 1])));
+            v[j] = y.x;
+            v[j + 1] = y.y;
+        }
+    }
+    if (ep.act == kActGelu) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = gelu_tanh(v[j]);
     }
-    if (kResid) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = rv[j] + gv[j] * v[j];
-    }
+    if (kResid) resid16(v, rv, gv);
 }
 
 // --- coalesced stores through a per-warp staging block ----------------------------------
