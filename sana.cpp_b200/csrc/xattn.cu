@@ -122,6 +122,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 constexpr int kMmaWarps = 8;   // 128 queries per block
 constexpr int kChunkKeys = 64;
+static_assert(kChunkKeys == 64, "a chunk is two groups of four 8-key column tiles");
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
@@ -270,33 +271,48 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
             const int ntmax = (nk + 7) / 8;  // 8-key column tiles holding live keys
             float sc[kChunkKeys / 8][4];
 #pragma unroll
-            for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
-                sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = -INFINITY;
-                if (nt < ntmax) {
-                    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-                    // K fragments by ldmatrix: 8 key rows x (two k-steps of 16) per x4 load
-                    const uint32_t krow = kbase + static_cast<uint32_t>((nt * 8 + (lane & 7)) * KSTR + (lane >> 3) * 8) * 2u;
+            for (int nt = 0; nt < kChunkKeys / 8; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = -INFINITY;
+            // Four 8-key column tiles at a time, k-steps outermost: four independent accumulator
+            // chains per k-step instead of one. The second group runs only when it holds live
+            // keys; tiles past the live ones read zero rows and stay masked.
 #pragma unroll
-                    for (int kk = 0; kk + 1 < KS; kk += 2) {
+            for (int grp = 0; grp < 2; ++grp) {
+                if (grp == 1 && ntmax <= 4) break;
+                float acc[4][4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+                // K fragments by ldmatrix: 8 key rows x (two k-steps of 16) per x4 load
+                const uint32_t krow = kbase + static_cast<uint32_t>((grp * 32 + (lane & 7)) * KSTR + (lane >> 3) * 8) * 2u;
+#pragma unroll
+                for (int kk = 0; kk + 1 < KS; kk += 2) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
                         uint32_t b[4];
-                        ldmatrix_x4(krow + static_cast<uint32_t>(kk * 16) * 2u, b);
-                        mma_bf16_16816(acc, qa[kk], b[0], b[1]);
-                        mma_bf16_16816(acc, qa[kk + 1], b[2], b[3]);
+                        ldmatrix_x4(krow + static_cast<uint32_t>(j * 8 * KSTR + kk * 16) * 2u, b);
+                        mma_bf16_16816(acc[j], qa[kk], b[0], b[1]);
+                        mma_bf16_16816(acc[j], qa[kk + 1], b[2], b[3]);
                     }
-                    if constexpr (KS % 2 == 1) {
+                }
+                if constexpr (KS % 2 == 1) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
                         uint32_t b0, b1;
-                        ldmatrix_x2(krow + static_cast<uint32_t>((KS - 1) * 16) * 2u, b0, b1);
-                        mma_bf16_16816(acc, qa[KS - 1], b0, b1);
+                        ldmatrix_x2(krow + static_cast<uint32_t>(j * 8 * KSTR + (KS - 1) * 16) * 2u, b0, b1);
+                        mma_bf16_16816(acc[j], qa[KS - 1], b0, b1);
                     }
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int nt = grp * 4 + j;
                     const int key = nt * 8 + tig * 2;
                     const float2 b2 = *reinterpret_cast<const float2*>(bsh + key);
                     if (key < nk) {
-                        sc[nt][0] = __fadd_rn(__fmul_rn(acc[0], scale), b2.x);
-                        sc[nt][2] = __fadd_rn(__fmul_rn(acc[2], scale), b2.x);
+                        sc[nt][0] = __fadd_rn(__fmul_rn(acc[j][0], scale), b2.x);
+                        sc[nt][2] = __fadd_rn(__fmul_rn(acc[j][2], scale), b2.x);
                     }
                     if (key + 1 < nk) {
-                        sc[nt][1] = __fadd_rn(__fmul_rn(acc[1], scale), b2.y);
-                        sc[nt][3] = __fadd_rn(__fmul_rn(acc[3], scale), b2.y);
+                        sc[nt][1] = __fadd_rn(__fmul_rn(acc[j][1], scale), b2.y);
+                        sc[nt][3] = __fadd_rn(__fmul_rn(acc[j][3], scale), b2.y);
                     }
                 }
             }
