@@ -301,18 +301,22 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
                         mma_bf16_16816(acc[j], qa[KS - 1], b0, b1);
                     }
                 }
+                // scores: scale, then bias, each rounded, two keys per packed operation
+                const uint64_t scale2 = f2_make(scale, scale);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int nt = grp * 4 + j;
                     const int key = nt * 8 + tig * 2;
-                    const float2 b2 = *reinterpret_cast<const float2*>(bsh + key);
+                    const uint64_t b2 = *reinterpret_cast<const uint64_t*>(bsh + key);
+                    const float2 r0 = f2_split(add2(mul2(f2_make(acc[j][0], acc[j][1]), scale2), b2));
+                    const float2 r1 = f2_split(add2(mul2(f2_make(acc[j][2], acc[j][3]), scale2), b2));
                     if (key < nk) {
-                        sc[nt][0] = __fadd_rn(__fmul_rn(acc[j][0], scale), b2.x);
-                        sc[nt][2] = __fadd_rn(__fmul_rn(acc[j][2], scale), b2.x);
+                        sc[nt][0] = r0.x;
+                        sc[nt][2] = r1.x;
                     }
                     if (key + 1 < nk) {
-                        sc[nt][1] = __fadd_rn(__fmul_rn(acc[j][1], scale), b2.y);
-                        sc[nt][3] = __fadd_rn(__fmul_rn(acc[j][3], scale), b2.y);
+                        sc[nt][1] = r0.y;
+                        sc[nt][3] = r1.y;
                     }
                 }
             }
@@ -327,7 +331,7 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
             mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
             mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
             const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-            const float corr0 = __expf(m0 - mn0), corr1 = __expf(m1 - mn1);  // m = -inf on the first chunk: 0
+            const float mp0 = m0, mp1 = m1;
             m0 = mn0;
             m1 = mn1;
             float sum0 = 0.f, sum1 = 0.f;
@@ -344,14 +348,23 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
                     sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
                 }
             }
-            l0 = l0 * corr0 + sum0;
-            l1 = l1 * corr1 + sum1;
+            if (c == 0) {  // nothing accumulated yet (the rescale would multiply zeros by exp(-inf) = 0)
+                l0 = sum0;
+                l1 = sum1;
+            } else {
+                const float corr0 = __expf(mp0 - mn0), corr1 = __expf(mp1 - mn1);
+                l0 = l0 * corr0 + sum0;
+                l1 = l1 * corr1 + sum1;
+                const uint64_t c0 = f2_make(corr0, corr0), c1 = f2_make(corr1, corr1);
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                o[nt][0] *= corr0;
-                o[nt][1] *= corr0;
-                o[nt][2] *= corr1;
-                o[nt][3] *= corr1;
+                for (int nt = 0; nt < NT; ++nt) {
+                    const float2 a = f2_split(mul2(f2_make(o[nt][0], o[nt][1]), c0));
+                    const float2 b = f2_split(mul2(f2_make(o[nt][2], o[nt][3]), c1));
+                    o[nt][0] = a.x;
+                    o[nt][1] = a.y;
+                    o[nt][2] = b.x;
+                    o[nt][3] = b.y;
+                }
             }
             const int kmax = (nk + 15) / 16;  // k-steps holding live keys
 #pragma unroll
@@ -387,11 +400,13 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
     const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
     // the warp's 16 output rows through its own rows of the query tile, then 16-byte stores
     bf16* orows = Qs + warp * 16 * KSTR;
+    const uint64_t i0 = f2_make(inv0, inv0), i1 = f2_make(inv1, inv1);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-        *reinterpret_cast<uint32_t*>(orows + g * KSTR + nt * 8 + tig * 2) = pack_bf16(o[nt][0] * inv0, o[nt][1] * inv0);
-        *reinterpret_cast<uint32_t*>(orows + (g + 8) * KSTR + nt * 8 + tig * 2) =
-            pack_bf16(o[nt][2] * inv1, o[nt][3] * inv1);
+        const float2 a = f2_split(mul2(f2_make(o[nt][0], o[nt][1]), i0));
+        const float2 b = f2_split(mul2(f2_make(o[nt][2], o[nt][3]), i1));
+        *reinterpret_cast<uint32_t*>(orows + g * KSTR + nt * 8 + tig * 2) = pack_bf16(a.x, a.y);
+        *reinterpret_cast<uint32_t*>(orows + (g + 8) * KSTR + nt * 8 + tig * 2) = pack_bf16(b.x, b.y);
     }
     __syncwarp();
     for (int i = lane; i < 16 * RC; i += 32) {
