@@ -335,13 +335,20 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
             m0 = mn0;
             m1 = mn1;
             float sum0 = 0.f, sum1 = 0.f;
+            constexpr float kLog2e = 1.4426950408889634f;  // log2(e)
+            const uint64_t l2e = f2_make(kLog2e, kLog2e);
+            const uint64_t nb0 = f2_make(-mn0 * kLog2e, -mn0 * kLog2e), nb1 = f2_make(-mn1 * kLog2e, -mn1 * kLog2e);
 #pragma unroll
             for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
                 if (nt < ntmax) {
-                    sc[nt][0] = __expf(sc[nt][0] - mn0);
-                    sc[nt][1] = __expf(sc[nt][1] - mn0);
-                    sc[nt][2] = __expf(sc[nt][2] - mn1);
-                    sc[nt][3] = __expf(sc[nt][3] - mn1);
+                    // exp(s - max) = 2^(s log2 e - max log2 e): one packed FMA per two keys and the
+                    // hardware base-2 exponential (a few ulp; P is rounded to bf16 below)
+                    const float2 e0 = f2_split(fma2(f2_make(sc[nt][0], sc[nt][1]), l2e, nb0));
+                    const float2 e1 = f2_split(fma2(f2_make(sc[nt][2], sc[nt][3]), l2e, nb1));
+                    sc[nt][0] = ex2_approx(e0.x);
+                    sc[nt][1] = ex2_approx(e0.y);
+                    sc[nt][2] = ex2_approx(e1.x);
+                    sc[nt][3] = ex2_approx(e1.y);
                     sum0 += sc[nt][0] + sc[nt][1];
                     sum1 += sc[nt][2] + sc[nt][3];
                 } else {
