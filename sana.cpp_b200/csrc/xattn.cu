@@ -115,6 +115,13 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void mma_bf16_1688(float (&c)[4], const uint32_t (&a)[2], uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(b0));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -135,6 +142,9 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t (&r)[4
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                  : "r"(addr));
 }
+__device__ __forceinline__ void ldmatrix_x1(uint32_t addr, uint32_t& r0) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x1.shared.b16 {%0}, [%1];" : "=r"(r0) : "r"(addr));
+}
 __device__ __forceinline__ void ldmatrix_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
@@ -152,9 +162,9 @@ __host__ __device__ constexpr int conflict_free_stride(int min_elems) {
 
 template <int D>
 struct XattnTiles {
-    static constexpr int KS = (D + 15) / 16;               // k-steps over the head dim
-    static constexpr int DP = KS * 16;                     // padded head dim
-    static constexpr int KSTR = conflict_free_stride(DP);  // Q and K tile row stride
+    static constexpr int KS = D / 16;                      // k-steps of 16 over the head dim
+    static constexpr bool KT = D % 16 != 0;                // and one of 8 (D = 72)
+    static constexpr int KSTR = conflict_free_stride(D);   // Q and K tile row stride
     static constexpr int VSTR = conflict_free_stride(D);   // V tile row stride
     static constexpr int kQRows = 16 * kMmaWarps;
     // the query tile, then two buffers of one key / value / bias chunk each
@@ -171,7 +181,9 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
                                                                    float scale, bf16* __restrict__ out,
                                                                    long long ldo) {
     using X = XattnTiles<D>;
-    constexpr int KS = X::KS, DP = X::DP, KSTR = X::KSTR, VSTR = X::VSTR;
+    constexpr int KS = X::KS, KSTR = X::KSTR, VSTR = X::VSTR;
+    constexpr bool KT = X::KT;
+    static_assert(D % 8 == 0, "head dim in 8-column fragments");
     constexpr int NT = D / 8;  // 8-wide output tiles
     constexpr int RC = D / 8;  // 16-byte pieces of a row
     static_assert((KSTR / 2) % 8 == 4 && (VSTR / 2) % 8 == 4 && KSTR % 8 == 0 && VSTR % 8 == 0, "strides");
@@ -191,17 +203,6 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
     const bool active = q0 < Tq;
     const uint32_t qbase = smem_u32(Qs);
 
-    // Head-dim padding of the query tile and of both key buffers: zero once (copies write D
-    // columns). Stores here and in load_chunk are ordered before any read by the barrier that
-    // follows the first wait.
-    if constexpr (DP > D) {
-        for (int i = threadIdx.x; i < X::kQRows * (DP - D); i += blockDim.x)
-            Qs[(i / (DP - D)) * KSTR + D + i % (DP - D)] = __float2bfloat16_rn(0.f);
-        for (int i = threadIdx.x; i < 2 * kChunkKeys * (DP - D); i += blockDim.x) {
-            const int b = i / (kChunkKeys * (DP - D)), r = i % (kChunkKeys * (DP - D));
-            Kbuf(b)[(r / (DP - D)) * KSTR + D + r % (DP - D)] = __float2bfloat16_rn(0.f);
-        }
-    }
     // query tile (rows past Tq read as zeros)
     for (int i = threadIdx.x; i < X::kQRows * RC; i += blockDim.x) {
         const int r = i / RC, ck = i % RC;
@@ -241,7 +242,7 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
     const int nchunks = (n_kv + kChunkKeys - 1) / kChunkKeys;
     load_chunk(0, 0);
 
-    uint32_t qa[KS][4];
+    uint32_t qa[KS][4], qt[2];
     float o[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
@@ -267,6 +268,8 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
                     ldmatrix_x4(qbase + static_cast<uint32_t>((warp * 16 + (lane & 15)) * KSTR + kk * 16 + (lane >> 4) * 8) *
                                             2u,
                                 qa[kk]);
+                if constexpr (KT)
+                    ldmatrix_x2(qbase + static_cast<uint32_t>((warp * 16 + (lane & 15)) * KSTR + KS * 16) * 2u, qt[0], qt[1]);
             }
             const int ntmax = (nk + 7) / 8;  // 8-key column tiles holding live keys
             float sc[kChunkKeys / 8][4];
@@ -299,6 +302,14 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
                         uint32_t b0, b1;
                         ldmatrix_x2(krow + static_cast<uint32_t>(j * 8 * KSTR + (KS - 1) * 16) * 2u, b0, b1);
                         mma_bf16_16816(acc[j], qa[KS - 1], b0, b1);
+                    }
+                }
+                if constexpr (KT) {  // the last 8 head-dim columns: one m16n8k8 per tile
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t b0;
+                        ldmatrix_x1(krow + static_cast<uint32_t>(j * 8 * KSTR + KS * 16) * 2u, b0);
+                        mma_bf16_1688(acc[j], qt, b0);
                     }
                 }
                 // scores: scale, then bias, each rounded, two keys per packed operation
