@@ -351,7 +351,8 @@ size_t sana_op_linear_attention_workspace(int S, int T, int heads, int D);
  *    them) race on it and give wrong results: keep such calls on one stream, or order them
  *    with events. */
 int sana_op_linear_attention_noalloc(sana_cuda_ctx *ctx, const void *qkv, int S, int T, int heads, int D, void *out);
-/* depthwise_conv2d_3x3 + GLU gate on NHWC rows [S*H*W, E] -> [S*H*W, E/2]; w [E, 9], b [E] fp32. */
+/* depthwise_conv2d_3x3 + GLU gate on NHWC rows [S*H*W, E] -> [S*H*W, E/2]; w [E, 9], b [E] fp32,
+ * both 16-byte aligned (the kernel bulk-copies them into shared memory). */
 int sana_op_depthwise_glu_device(sana_cuda_ctx *ctx, const void *in, int S, int H, int W, int E, const float *w,
                                  const float *b, void *out);
 /* layer_norm (no affine) followed by modulate_3d_lastdim (tensor.cpp:243-265, 323-376) on

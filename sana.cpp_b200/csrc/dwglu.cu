@@ -43,6 +43,21 @@ constexpr int kSlotRows = DW_SLOT_ROWS;               // input rows per ring slo
 constexpr int kSlotBytes = kSlotRows * kRowBytes;
 constexpr int kDwRing = DW_RING;                      // slots
 constexpr int kDwThreads = 32 * (kDwWarps + 1);
+// Beside each ring slot: the taps and biases of the item whose first rows the slot holds
+// ([64 value channels][9], [64 gate channels][9], then 64 + 64 biases, fp32), copied in with
+// those rows, so a consumer reads its item's weights from shared memory once the first slot
+// has landed instead of waiting on 72 global loads at every item.
+constexpr int kWTapBytes = kSliceCh * 9 * 4;           // 2304
+constexpr int kWBiasOffset = 2 * kWTapBytes;           // 4608
+constexpr int kWAreaBytes = kWBiasOffset + 2 * kSliceCh * 4;  // 5120
+
+// Untiled bulk copy global -> this CTA's shared memory, completing on `bar` (16-byte aligned
+// addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
 
 __device__ __forceinline__ float tanh_approx(float x) {
     float y;
@@ -185,6 +200,7 @@ __global__ void __launch_bounds__(kDwThreads, 1)
     extern __shared__ __align__(128) unsigned char dyn[];
     __shared__ __align__(8) uint64_t full_bar[kDwRing], empty_bar[kDwRing];
     unsigned char* ring = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(dyn) + 127) & ~uintptr_t(127));
+    unsigned char* wts = ring + kDwRing * kSlotBytes;  // [kDwRing][kWAreaBytes]
     const int slices = (half + kSliceCh - 1) / kSliceCh;
     const int items = S * bands * stripes * slices;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -211,7 +227,17 @@ __global__ void __launch_bounds__(kDwThreads, 1)
                     break;
                 }
                 const uint32_t fb = smem_u32(&full_bar[slot]);
-                mbar_arrive_expect_tx(fb, kSlotBytes);
+                if (k == 0) {  // the item's taps and biases come with its first rows
+                    const uint32_t nch = static_cast<uint32_t>(min(kSliceCh, half - d.c0));
+                    const uint32_t wa = smem_u32(wts + slot * kWAreaBytes);
+                    mbar_arrive_expect_tx(fb, kSlotBytes + nch * (2 * 9 * 4 + 2 * 4));
+                    bulk_load(wa, w + static_cast<long long>(d.c0) * 9, nch * 36, fb);
+                    bulk_load(wa + kWTapBytes, w + static_cast<long long>(half + d.c0) * 9, nch * 36, fb);
+                    bulk_load(wa + kWBiasOffset, b + d.c0, nch * 4, fb);
+                    bulk_load(wa + kWBiasOffset + kSliceCh * 4, b + half + d.c0, nch * 4, fb);
+                } else {
+                    mbar_arrive_expect_tx(fb, kSlotBytes);
+                }
                 tma_load_5d(&map, smem_u32(ring + slot * kSlotBytes), fb, d.c0, 0, d.x0 - 1,
                             d.y0 - 1 + k * kSlotRows, d.s);
             }
@@ -239,18 +265,32 @@ __global__ void __launch_bounds__(kDwThreads, 1)
         const DwItem d = dw_item(it, H, band_rows, bands, stripes, slices);
         const int ch = d.c0 + 2 * p;
         st.pok = ch < half;  // half is a multiple of 8: both channels of the pair exist
+        // the item's first rows, and with them its taps and biases (read before the slot is released)
+        DwRaw raw;
+        dw_fetch(st, 0, raw);
         uint64_t wv[9], wg[9], bv = 0, bg = 0;
+        {
+            const unsigned char* wa = wts + (st.slot0 % kDwRing) * kWAreaBytes;
+            const float2* tv = reinterpret_cast<const float2*>(wa + 72 * p);  // taps of channels 2p, 2p + 1
+            const float2* tg = reinterpret_cast<const float2*>(wa + kWTapBytes + 72 * p);
+            float a[18], g[18];
 #pragma unroll
-        for (int t = 0; t < 9; ++t) {
-            wv[t] = st.pok ? f2_make(w[static_cast<long long>(ch) * 9 + t], w[static_cast<long long>(ch + 1) * 9 + t])
-                           : 0;
-            wg[t] = st.pok ? f2_make(0.5f * w[static_cast<long long>(half + ch) * 9 + t],
-                                     0.5f * w[static_cast<long long>(half + ch + 1) * 9 + t])
-                           : 0;
-        }
-        if (st.pok) {
-            bv = f2_make(b[ch], b[ch + 1]);
-            bg = f2_make(0.5f * b[half + ch], 0.5f * b[half + ch + 1]);
+            for (int j = 0; j < 9; ++j) {
+                const float2 x = tv[j], y = tg[j];
+                a[2 * j] = x.x, a[2 * j + 1] = x.y;
+                g[2 * j] = y.x, g[2 * j + 1] = y.y;
+            }
+#pragma unroll
+            for (int t = 0; t < 9; ++t) {
+                wv[t] = st.pok ? f2_make(a[t], a[9 + t]) : 0;
+                wg[t] = st.pok ? f2_make(0.5f * g[t], 0.5f * g[9 + t]) : 0;
+            }
+            if (st.pok) {
+                const float2 x = *reinterpret_cast<const float2*>(wa + kWBiasOffset + 8 * p);
+                const float2 y = *reinterpret_cast<const float2*>(wa + kWBiasOffset + kSliceCh * 4 + 8 * p);
+                bv = f2_make(x.x, x.y);
+                bg = f2_make(0.5f * y.x, 0.5f * y.y);
+            }
         }
         const int xw = d.x0 + kCols * warp;  // first column of this thread
         st.ncols = min(kCols, W - xw);
@@ -267,8 +307,6 @@ __global__ void __launch_bounds__(kDwThreads, 1)
             }
         // step i passes (output i, output i - 1, output i - 2) =
         // (acc[i % 3], acc[(i + 2) % 3], acc[(i + 1) % 3])
-        DwRaw raw;
-        dw_fetch(st, 0, raw);
         dw_step<false>(st, 0, acc[0], acc[2], acc[1], raw, wv, wg, bv, bg);
         dw_step<false>(st, 1, acc[1], acc[0], acc[2], raw, wv, wg, bv, bg);
         int i = 2;
@@ -287,7 +325,7 @@ __global__ void __launch_bounds__(kDwThreads, 1)
     }
 }
 
-size_t dwglu_stream_smem() { return static_cast<size_t>(kDwRing) * kSlotBytes + 128; }
+size_t dwglu_stream_smem() { return static_cast<size_t>(kDwRing) * (kSlotBytes + kWAreaBytes) + 128; }
 
 // Any type / channel count: one output channel per thread.
 template <class T>
@@ -369,6 +407,9 @@ void depthwise_glu(const T* in, long long ldi, int S, int H, int W, int E, const
     SANA_REQUIRE(vec || sizeof(T) != 2 || half % 8 != 0,
                  "depthwise_glu: bf16 rows must be 16-byte aligned (input) and 4-byte aligned (output)");
     if (vec) {
+        // the kernel copies each work item's taps and biases with bulk copies from 16-byte boundaries
+        SANA_REQUIRE((reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(b) & 15) == 0,
+                     "depthwise_glu: the bf16 path needs 16-byte aligned tap and bias arrays");
         static int device_sms[64] = {0};
         static PerDeviceOnce attr;
         int dev = 0;
