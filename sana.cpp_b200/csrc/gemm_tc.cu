@@ -620,6 +620,11 @@ __device__ __forceinline__ void epilogue_span(const Epilogue& ep, int row0, int 
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 
+// TMEM columns between the two accumulators: BN, or 256 for 192-column tiles (each
+// accumulator then starts on a 256-column boundary).
+template <int BN>
+constexpr int kAccCols = BN <= 128 ? BN : 256;
+
 template <int BN, bool kResid>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -721,7 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * BN);
+                const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * kAccCols<BN>);
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(full(stage), phase, err, kTimeout)) {
                         ok = false;
@@ -773,7 +778,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n_blk = tile % num_n;
             const int col0 = chalf * (BN / 2);
             const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
-                                   static_cast<uint32_t>(acc * BN + col0);
+                                   static_cast<uint32_t>(acc * kAccCols<BN> + col0);
             epilogue_span<BN / 2, kResid, C::kStoreBufs>(ep, m_blk * BM + q * 32, M, n_blk * BN + col0, N,
                                                          vec != 0, t_row, stg, &ring, &ts, &tmO, &tmO2, side);
             tc_fence_before();
@@ -953,7 +958,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * BN);
+                const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * kAccCols<BN>);
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait(full(stage), phase, err, kTimeout)) {
                         ok = false;
@@ -1003,7 +1008,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int n_blk = tile % num_n;
             const int col0 = chalf * (BN / 2);
             const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) +
-                                   static_cast<uint32_t>(acc * BN + col0);
+                                   static_cast<uint32_t>(acc * kAccCols<BN> + col0);
             epilogue_span<BN / 2, kResid, C::kStoreBufs>(ep, m_blk * BM2 + static_cast<int>(rank) * BM + q * 32, M,
                                                          n_blk * BN + col0, N, vec != 0, t_row, stg, &ring, &ts,
                                                          &tmO, &tmO2, side);
@@ -1198,6 +1203,14 @@ void gemm_tc(const GemmProblem& p, int* err, cudaStream_t stream, int num_sms) {
     const bool resid = p.ep.resid != nullptr;
     // long reductions keep the MMA fed with deeper operand pipelines (their epilogue has slack)
     const bool deep = p.K >= 2048;
+    // Short per-GPU batches (M <= 8192, the multi-GPU runs' shards) leave few 256 x 256 tiles per
+    // CTA pair: the model's width 1152 then takes six 192-column tiles instead of four and a half
+    // 256-column ones (measured 4-7 % faster at M = 4096 and 8192, slower at larger M or N).
+    if (pair && p.M <= 8192 && p.N % 192 == 0 && p.N <= 1536) {
+        if (resid && deep) tc::launch2<192, true, true>(p, err, stream, num_sms);
+        else resid ? tc::launch2<192, true>(p, err, stream, num_sms) : tc::launch2<192, false>(p, err, stream, num_sms);
+        return;
+    }
     if (p.N >= 256) {
         if (pair && resid && deep) tc::launch2<256, true, true>(p, err, stream, num_sms);
         else if (pair) resid ? tc::launch2<256, true>(p, err, stream, num_sms) : tc::launch2<256, false>(p, err, stream, num_sms);
