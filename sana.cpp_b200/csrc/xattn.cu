@@ -127,8 +127,20 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-constexpr int kMmaWarps = 8;   // 128 queries per block
+constexpr int kMmaWarps = 8;   // 16 query rows per warp, 128 per query tile
 constexpr int kChunkKeys = 64;
+
+// SMs of the current device (cached per device).
+int xattn_sms() {
+    static int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int n = 0;
+        cached[dev] = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0 ? n : 148;
+    }
+    return cached[dev];
+}
 static_assert(kChunkKeys == 64, "a chunk is two groups of four 8-key column tiles");
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
@@ -160,7 +172,7 @@ __host__ __device__ constexpr int conflict_free_stride(int min_elems) {
     return ((min_elems / 2) % 8 == 4) ? min_elems : ((min_elems + 7) / 8 * 8 + ((((min_elems + 7) / 8 * 8) / 2) % 8 == 4 ? 0 : 8));
 }
 
-template <int D>
+template <int D, int kXTiles>
 struct XattnTiles {
     static constexpr int KS = D / 16;                      // k-steps of 16 over the head dim
     static constexpr bool KT = D % 16 != 0;                // and one of 8 (D = 72)
@@ -169,10 +181,11 @@ struct XattnTiles {
     static constexpr int kQRows = 16 * kMmaWarps;
     // the query tile, then two buffers of one key / value / bias chunk each
     static constexpr size_t kChunkBytes = static_cast<size_t>(kChunkKeys) * (KSTR + VSTR) * 2 + kChunkKeys * 4;
-    static constexpr size_t kBytes = static_cast<size_t>(kQRows) * KSTR * 2 + 2 * kChunkBytes;
+    static constexpr size_t kBytes = static_cast<size_t>(kXTiles) * kQRows * KSTR * 2 + 2 * kChunkBytes;
 };
 
-template <int D>
+// kXTiles query tiles of 128 per block (one or two, chosen by the launch).
+template <int D, int kXTiles>
 __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* __restrict__ q, long long ldq,
                                                                    const bf16* __restrict__ kv, long long ldkv,
                                                                    int k_off, int v_off,
@@ -180,7 +193,7 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
                                                                    const int* __restrict__ kv_len, int Tq, int L,
                                                                    float scale, bf16* __restrict__ out,
                                                                    long long ldo) {
-    using X = XattnTiles<D>;
+    using X = XattnTiles<D, kXTiles>;
     constexpr int KS = X::KS, KSTR = X::KSTR, VSTR = X::VSTR;
     constexpr bool KT = X::KT;
     static_assert(D % 8 == 0, "head dim in 8-column fragments");
@@ -188,8 +201,8 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
     constexpr int RC = D / 8;  // 16-byte pieces of a row
     static_assert((KSTR / 2) % 8 == 4 && (VSTR / 2) % 8 == 4 && KSTR % 8 == 0 && VSTR % 8 == 0, "strides");
     extern __shared__ __align__(16) unsigned char xsm[];
-    bf16* Qs = reinterpret_cast<bf16*>(xsm);            // [128][KSTR], later the output rows
-    unsigned char* chunk0 = xsm + X::kQRows * KSTR * 2;   // two buffers of [K 64][KSTR], [V 64][VSTR], bias [64]
+    bf16* Qs = reinterpret_cast<bf16*>(xsm);  // kXTiles x [128][KSTR], later the output rows
+    unsigned char* chunk0 = xsm + kXTiles * X::kQRows * KSTR * 2;  // two buffers of [K 64][KSTR], [V 64][VSTR], bias [64]
     auto Kbuf = [&](int b) { return reinterpret_cast<bf16*>(chunk0 + b * X::kChunkBytes); };
     auto Vbuf = [&](int b) { return Kbuf(b) + kChunkKeys * KSTR; };
     auto Bbuf = [&](int b) { return reinterpret_cast<float*>(Vbuf(b) + kChunkKeys * VSTR); };
@@ -197,21 +210,29 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
     const int s = blockIdx.z, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, tig = lane & 3;
-    const int qb = blockIdx.x * X::kQRows;
-    const int q0 = qb + warp * 16;
     const int n_kv = kv_len ? kv_len[s] : L;
-    const bool active = q0 < Tq;
-    const uint32_t qbase = smem_u32(Qs);
+    const int nchunks = (n_kv + kChunkKeys - 1) / kChunkKeys;
+    // Both query tiles of the block share the key / value chunks: with at most two chunks (the
+    // captions' live keys fit in 128) they stay resident and load once; longer captions stream
+    // them again for the second tile.
+    const bool resident = nchunks <= 2;
+    const int ntiles = min(kXTiles, (Tq - static_cast<int>(blockIdx.x) * kXTiles * X::kQRows + X::kQRows - 1) / X::kQRows);
 
-    // query tile (rows past Tq read as zeros)
-    for (int i = threadIdx.x; i < X::kQRows * RC; i += blockDim.x) {
-        const int r = i / RC, ck = i % RC;
-        if (qb + r < Tq)
-            cp_async16(qbase + static_cast<uint32_t>(r * KSTR + ck * 8) * 2u,
-                       q + (static_cast<long long>(s) * Tq + qb + r) * ldq + h * D + ck * 8);
-        else
-            *reinterpret_cast<uint4*>(Qs + r * KSTR + ck * 8) = make_uint4(0u, 0u, 0u, 0u);
-    }
+    auto Qtile = [&](int t) { return Qs + t * X::kQRows * KSTR; };
+    // query tile t (rows past Tq read as zeros); the caller commits the copies
+    auto load_q = [&](int t) {
+        const int qb = (blockIdx.x * kXTiles + t) * X::kQRows;
+        bf16* Qt = Qtile(t);
+        const uint32_t qt_s = smem_u32(Qt);
+        for (int i = threadIdx.x; i < X::kQRows * RC; i += blockDim.x) {
+            const int r = i / RC, ck = i % RC;
+            if (qb + r < Tq)
+                cp_async16(qt_s + static_cast<uint32_t>(r * KSTR + ck * 8) * 2u,
+                           q + (static_cast<long long>(s) * Tq + qb + r) * ldq + h * D + ck * 8);
+            else
+                *reinterpret_cast<uint4*>(Qt + r * KSTR + ck * 8) = make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
     // keys and values of chunk c into buffer b; keys past the chunk end are zeros (their scores
     // are masked to -inf)
     auto load_chunk = [&](int c, int b) {
@@ -236,219 +257,261 @@ __global__ void __launch_bounds__(32 * kMmaWarps) xattn_mma_kernel(const bf16* _
         float* bb = Bbuf(b);
         for (int j = threadIdx.x; j < kChunkKeys; j += blockDim.x)
             bb[j] = (j < nk && bias) ? bias[static_cast<long long>(s) * L + c0 + j] : 0.f;
-        asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    // the query tile and the first chunk arrive together; later chunks load one ahead
-    const int nchunks = (n_kv + kChunkKeys - 1) / kChunkKeys;
+    auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
+
+    // the first query tile with the first chunk (and, when resident, the second chunk); the
+    // second query tile after them, landing while the first computes
+    load_q(0);
     load_chunk(0, 0);
+    if (resident && nchunks == 2) load_chunk(1, 1);
+    commit();
+    if (resident && ntiles > 1) {
+        load_q(1);
+        commit();
+    }
 
-    uint32_t qa[KS][4], qt[2];
-    float o[NT][4];
+    for (int t = 0; t < ntiles; ++t) {
+        const int q0 = (blockIdx.x * kXTiles + t) * X::kQRows + warp * 16;
+        const bool active = q0 < Tq;
+        const uint32_t qbase = smem_u32(Qtile(t));
+        uint32_t qa[KS][4], qt[2];
+        float o[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+        for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+        float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
-    for (int c = 0; c < nchunks; ++c) {
-        const int buf = c & 1;
-        if (c + 1 < nchunks) {
-            load_chunk(c + 1, buf ^ 1);
-            asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        if (!resident && t > 0) {  // chunk buffers are free: the last chunk loop ended with a barrier
+            load_q(t);
+            load_chunk(0, 0);
+            commit();
         }
-        __syncthreads();
-        const int c0 = c * kChunkKeys;
-        const int nk = min(kChunkKeys, n_kv - c0);
-        const uint32_t kbase = smem_u32(Kbuf(buf)), vbase = smem_u32(Vbuf(buf));
-        const float* bsh = Bbuf(buf);
-        if (active) {
-            if (c == 0) {
-#pragma unroll
-                for (int kk = 0; kk < KS; ++kk)
-                    ldmatrix_x4(qbase + static_cast<uint32_t>((warp * 16 + (lane & 15)) * KSTR + kk * 16 + (lane >> 4) * 8) *
-                                            2u,
-                                qa[kk]);
-                if constexpr (KT)
-                    ldmatrix_x2(qbase + static_cast<uint32_t>((warp * 16 + (lane & 15)) * KSTR + KS * 16) * 2u, qt[0], qt[1]);
-            }
-            const int ntmax = (nk + 7) / 8;  // 8-key column tiles holding live keys
-            float sc[kChunkKeys / 8][4];
-#pragma unroll
-            for (int nt = 0; nt < kChunkKeys / 8; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = -INFINITY;
-            // Four 8-key column tiles at a time, k-steps outermost: four independent accumulator
-            // chains per k-step instead of one. The second group runs only when it holds live
-            // keys; tiles past the live ones read zero rows and stay masked.
-#pragma unroll
-            for (int grp = 0; grp < 2; ++grp) {
-                if (grp == 1 && ntmax <= 4) break;
-                float acc[4][4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-                // K fragments by ldmatrix: 8 key rows x (two k-steps of 16) per x4 load
-                const uint32_t krow = kbase + static_cast<uint32_t>((grp * 32 + (lane & 7)) * KSTR + (lane >> 3) * 8) * 2u;
-#pragma unroll
-                for (int kk = 0; kk + 1 < KS; kk += 2) {
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t b[4];
-                        ldmatrix_x4(krow + static_cast<uint32_t>(j * 8 * KSTR + kk * 16) * 2u, b);
-                        mma_bf16_16816(acc[j], qa[kk], b[0], b[1]);
-                        mma_bf16_16816(acc[j], qa[kk + 1], b[2], b[3]);
-                    }
+        for (int c = 0; c < nchunks; ++c) {
+            const int buf = c & 1;
+            if (resident) {
+                if (c == 0) {
+                    if (t == 0 && ntiles > 1) asm volatile("cp.async.wait_group 1;" ::: "memory");
+                    else asm volatile("cp.async.wait_group 0;" ::: "memory");
+                    __syncthreads();
                 }
-                if constexpr (KS % 2 == 1) {
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t b0, b1;
-                        ldmatrix_x2(krow + static_cast<uint32_t>(j * 8 * KSTR + (KS - 1) * 16) * 2u, b0, b1);
-                        mma_bf16_16816(acc[j], qa[KS - 1], b0, b1);
-                    }
-                }
-                if constexpr (KT) {  // the last 8 head-dim columns: one m16n8k8 per tile
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t b0;
-                        ldmatrix_x1(krow + static_cast<uint32_t>(j * 8 * KSTR + KS * 16) * 2u, b0);
-                        mma_bf16_1688(acc[j], qt, b0);
-                    }
-                }
-                // scores: scale, then bias, each rounded, two keys per packed operation
-                const uint64_t scale2 = f2_make(scale, scale);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int nt = grp * 4 + j;
-                    const int key = nt * 8 + tig * 2;
-                    const uint64_t b2 = *reinterpret_cast<const uint64_t*>(bsh + key);
-                    const float2 r0 = f2_split(add2(mul2(f2_make(acc[j][0], acc[j][1]), scale2), b2));
-                    const float2 r1 = f2_split(add2(mul2(f2_make(acc[j][2], acc[j][3]), scale2), b2));
-                    if (key < nk) {
-                        sc[nt][0] = r0.x;
-                        sc[nt][2] = r1.x;
-                    }
-                    if (key + 1 < nk) {
-                        sc[nt][1] = r0.y;
-                        sc[nt][3] = r1.y;
-                    }
-                }
-            }
-            float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-            for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
-                mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
-                mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
-            }
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-            const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-            const float mp0 = m0, mp1 = m1;
-            m0 = mn0;
-            m1 = mn1;
-            float sum0 = 0.f, sum1 = 0.f;
-            constexpr float kLog2e = 1.4426950408889634f;  // log2(e)
-            const uint64_t l2e = f2_make(kLog2e, kLog2e);
-            const uint64_t nb0 = f2_make(-mn0 * kLog2e, -mn0 * kLog2e), nb1 = f2_make(-mn1 * kLog2e, -mn1 * kLog2e);
-#pragma unroll
-            for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
-                if (nt < ntmax) {
-                    // exp(s - max) = 2^(s log2 e - max log2 e): one packed FMA per two keys and the
-                    // hardware base-2 exponential (a few ulp; P is rounded to bf16 below)
-                    const float2 e0 = f2_split(fma2(f2_make(sc[nt][0], sc[nt][1]), l2e, nb0));
-                    const float2 e1 = f2_split(fma2(f2_make(sc[nt][2], sc[nt][3]), l2e, nb1));
-                    sc[nt][0] = ex2_approx(e0.x);
-                    sc[nt][1] = ex2_approx(e0.y);
-                    sc[nt][2] = ex2_approx(e1.x);
-                    sc[nt][3] = ex2_approx(e1.y);
-                    sum0 += sc[nt][0] + sc[nt][1];
-                    sum1 += sc[nt][2] + sc[nt][3];
-                } else {
-                    sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-                }
-            }
-            if (c == 0) {  // nothing accumulated yet (the rescale would multiply zeros by exp(-inf) = 0)
-                l0 = sum0;
-                l1 = sum1;
             } else {
-                const float corr0 = __expf(mp0 - mn0), corr1 = __expf(mp1 - mn1);
-                l0 = l0 * corr0 + sum0;
-                l1 = l1 * corr1 + sum1;
-                const uint64_t c0 = f2_make(corr0, corr0), c1 = f2_make(corr1, corr1);
+                if (c + 1 < nchunks) {
+                    load_chunk(c + 1, buf ^ 1);
+                    commit();
+                    asm volatile("cp.async.wait_group 1;" ::: "memory");
+                } else {
+                    asm volatile("cp.async.wait_group 0;" ::: "memory");
+                }
+                __syncthreads();
+            }
+            const int c0 = c * kChunkKeys;
+            const int nk = min(kChunkKeys, n_kv - c0);
+            const uint32_t kbase = smem_u32(Kbuf(buf)), vbase = smem_u32(Vbuf(buf));
+            const float* bsh = Bbuf(buf);
+            if (active) {
+                if (c == 0) {
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    const float2 a = f2_split(mul2(f2_make(o[nt][0], o[nt][1]), c0));
-                    const float2 b = f2_split(mul2(f2_make(o[nt][2], o[nt][3]), c1));
-                    o[nt][0] = a.x;
-                    o[nt][1] = a.y;
-                    o[nt][2] = b.x;
-                    o[nt][3] = b.y;
+                    for (int kk = 0; kk < KS; ++kk)
+                        ldmatrix_x4(qbase + static_cast<uint32_t>((warp * 16 + (lane & 15)) * KSTR + kk * 16 + (lane >> 4) * 8) *
+                                                2u,
+                                    qa[kk]);
+                    if constexpr (KT)
+                        ldmatrix_x2(qbase + static_cast<uint32_t>((warp * 16 + (lane & 15)) * KSTR + KS * 16) * 2u, qt[0], qt[1]);
+                }
+                const int ntmax = (nk + 7) / 8;  // 8-key column tiles holding live keys
+                float sc[kChunkKeys / 8][4];
+#pragma unroll
+                for (int nt = 0; nt < kChunkKeys / 8; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = -INFINITY;
+                // Four 8-key column tiles at a time, k-steps outermost: four independent accumulator
+                // chains per k-step instead of one. The second group runs only when it holds live
+                // keys; tiles past the live ones read zero rows and stay masked.
+#pragma unroll
+                for (int grp = 0; grp < 2; ++grp) {
+                    if (grp == 1 && ntmax <= 4) break;
+                    float acc[4][4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+                    // K fragments by ldmatrix: 8 key rows x (two k-steps of 16) per x4 load
+                    const uint32_t krow = kbase + static_cast<uint32_t>((grp * 32 + (lane & 7)) * KSTR + (lane >> 3) * 8) * 2u;
+#pragma unroll
+                    for (int kk = 0; kk + 1 < KS; kk += 2) {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            uint32_t b[4];
+                            ldmatrix_x4(krow + static_cast<uint32_t>(j * 8 * KSTR + kk * 16) * 2u, b);
+                            mma_bf16_16816(acc[j], qa[kk], b[0], b[1]);
+                            mma_bf16_16816(acc[j], qa[kk + 1], b[2], b[3]);
+                        }
+                    }
+                    if constexpr (KS % 2 == 1) {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            uint32_t b0, b1;
+                            ldmatrix_x2(krow + static_cast<uint32_t>(j * 8 * KSTR + (KS - 1) * 16) * 2u, b0, b1);
+                            mma_bf16_16816(acc[j], qa[KS - 1], b0, b1);
+                        }
+                    }
+                    if constexpr (KT) {  // the last 8 head-dim columns: one m16n8k8 per tile
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            uint32_t b0;
+                            ldmatrix_x1(krow + static_cast<uint32_t>(j * 8 * KSTR + KS * 16) * 2u, b0);
+                            mma_bf16_1688(acc[j], qt, b0);
+                        }
+                    }
+                    // scores: scale, then bias, each rounded, two keys per packed operation
+                    const uint64_t scale2 = f2_make(scale, scale);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int nt = grp * 4 + j;
+                        const int key = nt * 8 + tig * 2;
+                        const uint64_t b2 = *reinterpret_cast<const uint64_t*>(bsh + key);
+                        const float2 r0 = f2_split(add2(mul2(f2_make(acc[j][0], acc[j][1]), scale2), b2));
+                        const float2 r1 = f2_split(add2(mul2(f2_make(acc[j][2], acc[j][3]), scale2), b2));
+                        if (key < nk) {
+                            sc[nt][0] = r0.x;
+                            sc[nt][2] = r1.x;
+                        }
+                        if (key + 1 < nk) {
+                            sc[nt][1] = r0.y;
+                            sc[nt][3] = r1.y;
+                        }
+                    }
+                }
+                float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+                for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
+                    mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
+                    mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
+                }
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+                const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+                const float mp0 = m0, mp1 = m1;
+                m0 = mn0;
+                m1 = mn1;
+                float sum0 = 0.f, sum1 = 0.f;
+                constexpr float kLog2e = 1.4426950408889634f;  // log2(e)
+                const uint64_t l2e = f2_make(kLog2e, kLog2e);
+                const uint64_t nb0 = f2_make(-mn0 * kLog2e, -mn0 * kLog2e), nb1 = f2_make(-mn1 * kLog2e, -mn1 * kLog2e);
+#pragma unroll
+                for (int nt = 0; nt < kChunkKeys / 8; ++nt) {
+                    if (nt < ntmax) {
+                        // exp(s - max) = 2^(s log2 e - max log2 e): one packed FMA per two keys and the
+                        // hardware base-2 exponential (a few ulp; P is rounded to bf16 below)
+                        const float2 e0 = f2_split(fma2(f2_make(sc[nt][0], sc[nt][1]), l2e, nb0));
+                        const float2 e1 = f2_split(fma2(f2_make(sc[nt][2], sc[nt][3]), l2e, nb1));
+                        sc[nt][0] = ex2_approx(e0.x);
+                        sc[nt][1] = ex2_approx(e0.y);
+                        sc[nt][2] = ex2_approx(e1.x);
+                        sc[nt][3] = ex2_approx(e1.y);
+                        sum0 += sc[nt][0] + sc[nt][1];
+                        sum1 += sc[nt][2] + sc[nt][3];
+                    } else {
+                        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+                    }
+                }
+                if (c == 0) {  // nothing accumulated yet (the rescale would multiply zeros by exp(-inf) = 0)
+                    l0 = sum0;
+                    l1 = sum1;
+                } else {
+                    const float corr0 = __expf(mp0 - mn0), corr1 = __expf(mp1 - mn1);
+                    l0 = l0 * corr0 + sum0;
+                    l1 = l1 * corr1 + sum1;
+                    const uint64_t c0 = f2_make(corr0, corr0), c1 = f2_make(corr1, corr1);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        const float2 a = f2_split(mul2(f2_make(o[nt][0], o[nt][1]), c0));
+                        const float2 b = f2_split(mul2(f2_make(o[nt][2], o[nt][3]), c1));
+                        o[nt][0] = a.x;
+                        o[nt][1] = a.y;
+                        o[nt][2] = b.x;
+                        o[nt][3] = b.y;
+                    }
+                }
+                const int kmax = (nk + 15) / 16;  // k-steps holding live keys
+#pragma unroll
+                for (int kk = 0; kk < kChunkKeys / 16; ++kk) {
+                    if (kk >= kmax) break;
+                    const uint32_t pa[4] = {pack_bf16(sc[2 * kk][0], sc[2 * kk][1]), pack_bf16(sc[2 * kk][2], sc[2 * kk][3]),
+                                            pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]),
+                                            pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3])};
+                    const uint32_t vrow = vbase + static_cast<uint32_t>((kk * 16 + (lane & 15)) * VSTR) * 2u;
+                    // V fragments of two 8-column output tiles per x4 load (lanes 16-31 address the second)
+                    const uint32_t vrow4 = vrow + static_cast<uint32_t>((lane >> 4) * 8) * 2u;
+#pragma unroll
+                    for (int nt = 0; nt + 1 < NT; nt += 2) {
+                        uint32_t b[4];
+                        ldmatrix_x4_trans(vrow4 + static_cast<uint32_t>(nt * 16), b);
+                        mma_bf16_16816(o[nt], pa, b[0], b[1]);
+                        mma_bf16_16816(o[nt + 1], pa, b[2], b[3]);
+                    }
+                    if constexpr (NT % 2 == 1) {
+                        uint32_t b0, b1;
+                        ldmatrix_x2_trans(vrow + static_cast<uint32_t>((NT - 1) * 16), b0, b1);
+                        mma_bf16_16816(o[NT - 1], pa, b0, b1);
+                    }
                 }
             }
-            const int kmax = (nk + 15) / 16;  // k-steps holding live keys
+            if (!resident) __syncthreads();  // buffer `buf` is free for chunk c + 2
+        }
+        if (active) {
+            l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+            l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+            const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
+            // the warp's 16 output rows through its own rows of the query tile, then 16-byte stores
+            bf16* orows = Qtile(t) + warp * 16 * KSTR;
+            const uint64_t i0 = f2_make(inv0, inv0), i1 = f2_make(inv1, inv1);
 #pragma unroll
-            for (int kk = 0; kk < kChunkKeys / 16; ++kk) {
-                if (kk >= kmax) break;
-                const uint32_t pa[4] = {pack_bf16(sc[2 * kk][0], sc[2 * kk][1]), pack_bf16(sc[2 * kk][2], sc[2 * kk][3]),
-                                        pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]),
-                                        pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3])};
-                const uint32_t vrow = vbase + static_cast<uint32_t>((kk * 16 + (lane & 15)) * VSTR) * 2u;
-                // V fragments of two 8-column output tiles per x4 load (lanes 16-31 address the second)
-                const uint32_t vrow4 = vrow + static_cast<uint32_t>((lane >> 4) * 8) * 2u;
-#pragma unroll
-                for (int nt = 0; nt + 1 < NT; nt += 2) {
-                    uint32_t b[4];
-                    ldmatrix_x4_trans(vrow4 + static_cast<uint32_t>(nt * 16), b);
-                    mma_bf16_16816(o[nt], pa, b[0], b[1]);
-                    mma_bf16_16816(o[nt + 1], pa, b[2], b[3]);
-                }
-                if constexpr (NT % 2 == 1) {
-                    uint32_t b0, b1;
-                    ldmatrix_x2_trans(vrow + static_cast<uint32_t>((NT - 1) * 16), b0, b1);
-                    mma_bf16_16816(o[NT - 1], pa, b0, b1);
-                }
+            for (int nt = 0; nt < NT; ++nt) {
+                const float2 a = f2_split(mul2(f2_make(o[nt][0], o[nt][1]), i0));
+                const float2 b = f2_split(mul2(f2_make(o[nt][2], o[nt][3]), i1));
+                *reinterpret_cast<uint32_t*>(orows + g * KSTR + nt * 8 + tig * 2) = pack_bf16(a.x, a.y);
+                *reinterpret_cast<uint32_t*>(orows + (g + 8) * KSTR + nt * 8 + tig * 2) = pack_bf16(b.x, b.y);
+            }
+            __syncwarp();
+            for (int i = lane; i < 16 * RC; i += 32) {
+                const int r = i / RC, ck = i % RC;
+                if (q0 + r < Tq)
+                    *reinterpret_cast<uint4*>(out + (static_cast<long long>(s) * Tq + q0 + r) * ldo + h * D + ck * 8) =
+                        *reinterpret_cast<const uint4*>(orows + r * KSTR + ck * 8);
             }
         }
-        __syncthreads();  // buffer `buf` is free for chunk c + 2
-    }
-    if (!active) return;
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
-    // the warp's 16 output rows through its own rows of the query tile, then 16-byte stores
-    bf16* orows = Qs + warp * 16 * KSTR;
-    const uint64_t i0 = f2_make(inv0, inv0), i1 = f2_make(inv1, inv1);
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        const float2 a = f2_split(mul2(f2_make(o[nt][0], o[nt][1]), i0));
-        const float2 b = f2_split(mul2(f2_make(o[nt][2], o[nt][3]), i1));
-        *reinterpret_cast<uint32_t*>(orows + g * KSTR + nt * 8 + tig * 2) = pack_bf16(a.x, a.y);
-        *reinterpret_cast<uint32_t*>(orows + (g + 8) * KSTR + nt * 8 + tig * 2) = pack_bf16(b.x, b.y);
-    }
-    __syncwarp();
-    for (int i = lane; i < 16 * RC; i += 32) {
-        const int r = i / RC, ck = i % RC;
-        if (q0 + r < Tq)
-            *reinterpret_cast<uint4*>(out + (static_cast<long long>(s) * Tq + q0 + r) * ldo + h * D + ck * 8) =
-                *reinterpret_cast<const uint4*>(orows + r * KSTR + ck * 8);
     }
 }
 
+template <int D, int kXTiles>
+void launch_mma_tiles(const bf16* q, long long ldq, const bf16* kv, long long ldkv, int k_off, int v_off,
+                      const float* bias, const int* kv_len, int S, int Tq, int L, int heads, float scale, bf16* out,
+                      long long ldo, cudaStream_t st) {
+    constexpr size_t smem = XattnTiles<D, kXTiles>::kBytes;
+    static PerDeviceOnce attr;
+    if (attr.pending()) {
+        SANA_CUDA(cudaFuncSetAttribute(xattn_mma_kernel<D, kXTiles>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem)));
+        attr.mark();
+    }
+    xattn_mma_kernel<D, kXTiles><<<dim3(ceil_div(Tq, kXTiles * 16 * kMmaWarps), heads, S), 32 * kMmaWarps, smem, st>>>(
+        q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, Tq, L, scale, out, ldo);
+    SANA_CUDA(cudaGetLastError());
+}
+
+// Two query tiles per block share one load of the keys and values (measured 6 % faster at
+// config 2's short captions) when that still leaves at least four waves of blocks (two blocks
+// per SM); otherwise one tile per block keeps the grid wide enough to fill the GPU.
 template <int D>
 bool launch_mma(const bf16* q, long long ldq, const bf16* kv, long long ldkv, int k_off, int v_off, const float* bias,
                 const int* kv_len, int S, int Tq, int L, int heads, float scale, bf16* out, long long ldo,
                 cudaStream_t st) {
-    constexpr size_t smem = XattnTiles<D>::kBytes;
-    static PerDeviceOnce attr;
-    if (attr.pending()) {
-        SANA_CUDA(cudaFuncSetAttribute(xattn_mma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem)));
-        attr.mark();
-    }
-    xattn_mma_kernel<D><<<dim3(ceil_div(Tq, 16 * kMmaWarps), heads, S), 32 * kMmaWarps, smem, st>>>(
-        q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, Tq, L, scale, out, ldo);
-    SANA_CUDA(cudaGetLastError());
+    const long long blocks2 = static_cast<long long>(ceil_div(Tq, 2 * 16 * kMmaWarps)) * heads * S;
+    if (blocks2 >= 4LL * 2 * xattn_sms())
+        launch_mma_tiles<D, 2>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, scale, out, ldo, st);
+    else
+        launch_mma_tiles<D, 1>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, scale, out, ldo, st);
     return true;
 }
 
