@@ -519,6 +519,31 @@ def test_cross_attention_key_counts(gpu_bf16, oracle, D):
         assert rel_err(got[s], ref[s]) < BF16_TOL, (D, lens[s], rel_err(got[s], ref[s]))
 
 
+def test_cross_attention_two_tile_blocks(gpu_bf16):
+    """Config 2's cross-attention grid (32 sequences x 16 heads x 1024 queries, 300 caption
+    tokens), where each block takes two query tiles that share the keys and values: valid
+    lengths on both sides of the two-chunk limit (kept in shared memory up to 128 live keys,
+    streamed again beyond), against float64 softmax over the live keys of the same bf16
+    operands (masked keys carry exactly zero weight, transformer_ops.cpp:357-388)."""
+    from sana_b200 import synthetic as syn
+    rng = np.random.default_rng(11)
+    S, H, Tq, L, D = 32, 16, 1024, 300, 72
+    lens = [(8, 24, 64, 65, 120, 128, 129, 200, 300, 1)[i % 10] for i in range(S)]
+    q = bf16_round(rng.standard_normal((S, H, Tq, D)).astype(np.float32))
+    k = bf16_round(rng.standard_normal((S, H, L, D)).astype(np.float32))
+    v = bf16_round(rng.standard_normal((S, H, L, D)).astype(np.float32))
+    got = gpu_bf16.attention(q, k, v, syn.attention_bias(lens, L))
+    scale = 1.0 / np.sqrt(D)
+    for s in range(S):
+        n = lens[s]
+        sc = np.einsum("htd,hkd->htk", q[s].astype(np.float64), k[s, :, :n].astype(np.float64)) * scale
+        sc -= sc.max(axis=-1, keepdims=True)
+        p_ = np.exp(sc)
+        p_ /= p_.sum(axis=-1, keepdims=True)
+        ref = np.einsum("htk,hkd->htd", p_, v[s, :, :n].astype(np.float64))
+        assert rel_err(got[s], ref) < BF16_TOL, (s, n, rel_err(got[s], ref))
+
+
 @pytest.mark.parametrize("D,Tq,L,lens", [(72, 1024, 300, (8, 24)), (72, 100, 300, (300, 1)), (32, 77, 70, (70, 65)),
                                         (64, 130, 129, (64, 129)), (128, 40, 20, (20, 3))])
 def test_cross_attention_tensor_core_shapes(gpu_bf16, oracle, D, Tq, L, lens):
