@@ -500,15 +500,17 @@ void launch_mma_tiles(const bf16* q, long long ldq, const bf16* kv, long long ld
     SANA_CUDA(cudaGetLastError());
 }
 
-// Two query tiles per block share one load of the keys and values (measured 6 % faster at
-// config 2's short captions) when that still leaves at least four waves of blocks (two blocks
-// per SM); otherwise one tile per block keeps the grid wide enough to fill the GPU.
+// Two query tiles per block share one load of the keys and values: measured 6 % faster at
+// config 2 (32 sequences of 1024 queries) and 1-5 % faster in the loop at 4-16 sequences, but
+// 12 % slower on 4096-query sequences with 300 live keys (the keys stream again for each tile).
+// So: two tiles for grids of at least four waves (two blocks per SM), and for sequences of up to
+// 2048 queries whenever the two-tile grid still gives every SM a block; one tile otherwise.
 template <int D>
 bool launch_mma(const bf16* q, long long ldq, const bf16* kv, long long ldkv, int k_off, int v_off, const float* bias,
                 const int* kv_len, int S, int Tq, int L, int heads, float scale, bf16* out, long long ldo,
                 cudaStream_t st) {
     const long long blocks2 = static_cast<long long>(ceil_div(Tq, 2 * 16 * kMmaWarps)) * heads * S;
-    if (blocks2 >= 4LL * 2 * xattn_sms())
+    if (blocks2 >= 4LL * 2 * xattn_sms() || (Tq <= 2048 && blocks2 >= xattn_sms()))
         launch_mma_tiles<D, 2>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, scale, out, ldo, st);
     else
         launch_mma_tiles<D, 1>(q, ldq, kv, ldkv, k_off, v_off, bias, kv_len, S, Tq, L, heads, scale, out, ldo, st);
